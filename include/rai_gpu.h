@@ -1,0 +1,153 @@
+/* rai_gpu.h - C ABI of the B200-native prompt-lookup decode path.
+ *
+ * Drop-in boundary for rai-infer's prompt-lookup speculative decode step
+ * (rai-infer/src/lookup.rs LookupDecoder, rai-infer/src/model.rs RaiModel,
+ * rai-infer/src/kv_cache.rs KVCache). The host keeps the .raimodel loader,
+ * tokenizer and sampling loop; this library uploads the model once and runs
+ * draft lookup, the (k+1)-row verify forward, greedy acceptance and KV
+ * rollback on the GPU with no host round-trip inside a step.
+ *
+ * Conventions: every function returns an int status (RAI_OK = 0, negative on
+ * error) and never aborts or unwinds; rai_gpu_last_error() returns the
+ * message of the calling thread's last failure. A model is shared read-only
+ * by any number of decoders on its device; a decoder owns one CUDA stream, its
+ * KV cache and scratch, and must not be used from two threads at once.
+ * Token ids are uint32; positions and lengths are size_t.
+ */
+#ifndef RAI_GPU_H
+#define RAI_GPU_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define RAI_API __attribute__((visibility("default")))
+#else
+#define RAI_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum {
+  RAI_OK = 0,
+  RAI_ERR_INVALID = -1,     /* bad argument / misuse (ensure! in the reference) */
+  RAI_ERR_OOM = -2,         /* device or pinned-host allocation failed */
+  RAI_ERR_DEVICE = -3,      /* CUDA error */
+  RAI_ERR_TIMEOUT = -4,     /* a bounded device-side wait gave up */
+  RAI_ERR_UNSUPPORTED = -5, /* valid model, capability this build does not run */
+  RAI_ERR_FORMAT = -6       /* malformed .raimodel (format.rs validation) */
+};
+
+typedef struct rai_model rai_model;
+typedef struct rai_dec rai_dec;
+
+/* LookupConfig (rai-infer/src/lookup.rs:63-93) plus the SamplerConfig fields
+ * the reference validates (lookup.rs:457-475). temperature == 0 selects
+ * greedy acceptance, the t -> 0 limit of the reference's exact rule (accept a
+ * drafted token iff it is the target argmax; correction and bonus are
+ * argmaxes). top_k must be 0, top_p 1 and repetition_penalty 1, as in the
+ * reference. */
+typedef struct {
+  uint32_t max_draft;   /* K: tokens copied per step, >= 1 */
+  uint32_t max_ngram;   /* longest suffix n-gram tried first */
+  uint32_t min_ngram;   /* shortest suffix n-gram, >= 1 */
+  float temperature;    /* 0 = greedy */
+  uint32_t top_k;       /* must be 0 */
+  float top_p;          /* must be 1 */
+  float repetition_penalty; /* must be 1 */
+} rai_lookup_cfg;
+
+/* LookupMetrics (rai-infer/src/lookup.rs:111-119). matched_ngram = 0 when no
+ * n-gram matched (the reference's None). */
+typedef struct {
+  uint32_t accepted;
+  uint32_t drafted;
+  uint32_t produced;
+  uint32_t matched_ngram;
+  float accept_rate;
+} rai_lookup_metrics;
+
+/* ModelConfig fields the host loop needs (rai-infer/src/format.rs:162-265). */
+typedef struct {
+  uint32_t hidden_size, num_layers, num_heads, num_kv_heads, head_dim;
+  uint32_t intermediate_size, vocab_size, max_context;
+  uint32_t group_size, embed_group_size, num_experts, experts_per_token;
+  uint32_t tied_embeddings, version;
+  uint64_t device_bytes; /* HBM held by the uploaded model */
+} rai_model_info;
+
+/* RaiModel::load (rai-infer/src/model.rs:97-181) from an in-memory .raimodel:
+ * validates like RaiModelFile::open (format.rs:557-637), uploads the blob to
+ * HBM once and repacks the weights into the device layout. */
+RAI_API int rai_gpu_model_create(const uint8_t* blob, size_t len, int device, rai_model** out);
+RAI_API int rai_gpu_model_destroy(rai_model* model);
+RAI_API int rai_gpu_model_info(const rai_model* model, rai_model_info* info);
+
+/* LookupDecoder::new (rai-infer/src/lookup.rs:192-209): context window =
+ * min(max_ctx, model max_context); allocates the KV cache on the device. */
+RAI_API int rai_gpu_decoder_create(rai_model* model, size_t max_ctx, rai_dec** out);
+RAI_API int rai_gpu_decoder_destroy(rai_dec* dec);
+
+/* LookupDecoder::prefill (rai-infer/src/lookup.rs:219-247): runs every prompt
+ * token but the last through the model; *pos_out = n - 1. */
+RAI_API int rai_gpu_prefill(rai_dec* dec, const uint32_t* ids, size_t n, size_t* pos_out);
+
+/* LookupDecoder::step (rai-infer/src/lookup.rs:260-425). `ctx` is the whole
+ * token sequence; its last element lives at `pos`. Writes produced tokens to
+ * out_tokens (capacity out_cap >= max_draft + 1), their count to *n_out, and
+ * the step's metrics. The KV cache is rolled back to pos + produced. */
+RAI_API int rai_gpu_step(rai_dec* dec, size_t pos, const uint32_t* ctx, size_t ctx_len,
+                 const rai_lookup_cfg* cfg, uint32_t* out_tokens, size_t out_cap,
+                 size_t* n_out, rai_lookup_metrics* metrics);
+
+/* One step for each of n decoders sharing one model and device, batched so
+ * their verify rows share every weight read (one forward over
+ * sum(k_i + 1) rows). Same semantics as n calls of rai_gpu_step.
+ * out_tokens is n * out_cap. */
+RAI_API int rai_gpu_step_many(rai_dec* const* decs, size_t n, const size_t* pos,
+                      const uint32_t* const* ctx, const size_t* ctx_len,
+                      const rai_lookup_cfg* cfg, uint32_t* out_tokens, size_t out_cap,
+                      size_t* n_out, rai_lookup_metrics* metrics);
+
+/* KVCache::filled / truncate (rai-infer/src/kv_cache.rs:289-304). */
+RAI_API int rai_gpu_kv_filled(const rai_dec* dec, size_t layer, size_t* filled);
+RAI_API int rai_gpu_kv_truncate(rai_dec* dec, size_t len);
+/* Copy one cached (K, V) row to the host; position must be < filled. */
+RAI_API int rai_gpu_kv_read(const rai_dec* dec, size_t layer, size_t kv_head, size_t pos, float* k,
+                    float* v);
+
+/* RaiModel::forward_batch + hidden_to_logits_batch
+ * (rai-infer/src/model.rs:692-1033) for `batch` tokens at positions
+ * start_pos.., storing their KV; logits (batch * vocab f32, host) may be
+ * NULL. */
+RAI_API int rai_gpu_forward_logits(rai_dec* dec, const uint32_t* ids, size_t start_pos, size_t batch,
+                           float* logits);
+
+/* Wall-clock device time (microseconds) of the decoder's last step /
+ * step_many, measured with CUDA events on its stream. */
+RAI_API int rai_gpu_last_step_us(const rai_dec* dec, float* us);
+
+RAI_API size_t rai_gpu_last_error(char* buf, size_t len);
+
+/* ---- kernel-level entry points (device pointers, caller's stream) ----
+ *
+ * The W4A8 linear of rai-infer/src/gemm.rs (w4a8_matmul, gemm.rs:1774-1919;
+ * w4a8_matvec, gemm.rs:1336-1392): out[t * rows + r] = sum over the row's
+ * groups of the int8-quantized input against 4-bit codes with f16
+ * (scale, zero), bit-identical to the AVX2 kernel. Weights are first packed
+ * once into the device layout; `scratch` holds the quantized activations
+ * (rai_gpu_w4a8_scratch_bytes). group_size must be 64 or 128. */
+RAI_API size_t rai_gpu_w4a8_packed_bytes(size_t rows, size_t cols, size_t group_size);
+RAI_API int rai_gpu_w4a8_pack(const uint8_t* nibbles, const uint8_t* params, size_t rows, size_t cols,
+                      size_t group_size, void* packed, void* stream);
+RAI_API size_t rai_gpu_w4a8_scratch_bytes(size_t tokens, size_t cols, size_t group_size);
+RAI_API int rai_gpu_w4a8_matmul(float* out, const void* packed, const float* input, size_t rows,
+                        size_t cols, size_t tokens, size_t group_size, void* scratch,
+                        size_t scratch_bytes, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* RAI_GPU_H */

@@ -1,0 +1,174 @@
+"""Host-side mirror of rai-infer's prompt-lookup API over the C ABI.
+
+Same names and argument meaning as the reference:
+  RaiModel.load(path)                      rai-infer/src/model.rs:97-181
+  LookupConfig(max_draft, max_ngram, ...)  rai-infer/src/lookup.rs:63-93
+  LookupMetrics                            rai-infer/src/lookup.rs:111-119
+  LookupDecoder(model, max_ctx)            rai-infer/src/lookup.rs:192-209
+    .prefill(prompt) -> pos                lookup.rs:219-247
+    .step(pos, context, config) -> (tokens, metrics)   lookup.rs:260-425
+    .kv_filled(layer) / .truncate(len)     rai-infer/src/kv_cache.rs:289-304
+Errors the reference raises with ensure! surface as RaiError. The reference
+requires temperature > 1e-6 for its exact sampled rule; this build runs the
+greedy (temperature 0) limit of that rule.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import dataclasses
+from typing import Optional, Sequence
+
+import numpy as np
+
+from . import native
+from .native import RaiError, check
+
+
+@dataclasses.dataclass
+class LookupConfig:
+    max_draft: int = 10
+    max_ngram: int = 3
+    min_ngram: int = 1
+    temperature: float = 0.0
+    top_k: int = 0
+    top_p: float = 1.0
+    repetition_penalty: float = 1.0
+
+    def _c(self) -> native.LookupCfg:
+        return native.LookupCfg(self.max_draft, self.max_ngram, self.min_ngram, self.temperature,
+                                self.top_k, self.top_p, self.repetition_penalty)
+
+
+@dataclasses.dataclass
+class LookupMetrics:
+    accepted: int
+    drafted: int
+    produced: int
+    accept_rate: float
+    matched_ngram: Optional[int]
+
+    @classmethod
+    def _from_c(cls, m: native.LookupMetricsC) -> "LookupMetrics":
+        return cls(int(m.accepted), int(m.drafted), int(m.produced), float(m.accept_rate),
+                   int(m.matched_ngram) or None)
+
+
+class RaiModel:
+    """A .raimodel uploaded to one GPU (validated like RaiModelFile::open)."""
+
+    def __init__(self, blob: bytes, device: int = 0):
+        self._blob = np.frombuffer(blob, np.uint8)
+        h = C.c_void_p()
+        check(native.lib().rai_gpu_model_create(self._blob.ctypes.data_as(C.c_void_p), self._blob.size,
+                                                device, C.byref(h)))
+        self._h = h
+        self._blob = None
+        info = native.ModelInfo()
+        check(native.lib().rai_gpu_model_info(h, C.byref(info)))
+        self.config = {f: getattr(info, f) for f, _ in native.ModelInfo._fields_}
+        self.device = device
+
+    @classmethod
+    def load(cls, path: str, device: int = 0) -> "RaiModel":
+        with open(path, "rb") as f:
+            return cls(f.read(), device)
+
+    def close(self) -> None:
+        if getattr(self, "_h", None):
+            native.lib().rai_gpu_model_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        self.close()
+
+
+def _u32(a: Sequence[int]) -> np.ndarray:
+    return np.ascontiguousarray(np.asarray(a, dtype=np.uint32))
+
+
+class LookupDecoder:
+    """Prompt-lookup decoder: n-gram draft, one batched verify, greedy accept,
+    KV rollback -- all on the device."""
+
+    def __init__(self, model: RaiModel, max_ctx: int):
+        self.model = model
+        h = C.c_void_p()
+        check(native.lib().rai_gpu_decoder_create(model._h, max_ctx, C.byref(h)))
+        self._h = h
+        self.max_ctx = min(max_ctx, model.config["max_context"])
+
+    def close(self) -> None:
+        if getattr(self, "_h", None):
+            native.lib().rai_gpu_decoder_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        self.close()
+
+    def prefill(self, prompt_tokens: Sequence[int]) -> int:
+        ids = _u32(prompt_tokens)
+        pos = C.c_size_t()
+        check(native.lib().rai_gpu_prefill(self._h, ids.ctypes.data_as(C.c_void_p), ids.size, C.byref(pos)))
+        return pos.value
+
+    def step(self, pos: int, context: Sequence[int], config: LookupConfig):
+        ctx = _u32(context)
+        cap = max(config.max_draft + 1, 1)
+        out = np.zeros(cap, np.uint32)
+        n = C.c_size_t()
+        met = native.LookupMetricsC()
+        cfg = config._c()
+        check(native.lib().rai_gpu_step(self._h, pos, ctx.ctypes.data_as(C.c_void_p), ctx.size, C.byref(cfg),
+                                        out.ctypes.data_as(C.c_void_p), cap, C.byref(n), C.byref(met)))
+        return [int(t) for t in out[: n.value]], LookupMetrics._from_c(met)
+
+    def forward_logits(self, ids: Sequence[int], start_pos: int) -> np.ndarray:
+        ids = _u32(ids)
+        out = np.zeros((ids.size, self.model.config["vocab_size"]), np.float32)
+        check(native.lib().rai_gpu_forward_logits(self._h, ids.ctypes.data_as(C.c_void_p), start_pos, ids.size,
+                                                  out.ctypes.data_as(C.c_void_p)))
+        return out
+
+    def kv_filled(self, layer: int = 0) -> int:
+        f = C.c_size_t()
+        check(native.lib().rai_gpu_kv_filled(self._h, layer, C.byref(f)))
+        return f.value
+
+    def truncate(self, length: int) -> None:
+        check(native.lib().rai_gpu_kv_truncate(self._h, length))
+
+    def kv_read(self, layer: int, kv_head: int, pos: int):
+        hd = self.model.config["head_dim"]
+        k = np.zeros(hd, np.float32)
+        v = np.zeros(hd, np.float32)
+        check(native.lib().rai_gpu_kv_read(self._h, layer, kv_head, pos, k.ctypes.data_as(C.c_void_p),
+                                           v.ctypes.data_as(C.c_void_p)))
+        return k, v
+
+    def last_step_us(self) -> float:
+        us = C.c_float()
+        check(native.lib().rai_gpu_last_step_us(self._h, C.byref(us)))
+        return us.value
+
+
+def step_many(decoders: Sequence[LookupDecoder], positions: Sequence[int], contexts: Sequence[Sequence[int]],
+              config: LookupConfig):
+    """One step for each decoder (rai_gpu_step_many)."""
+    n = len(decoders)
+    cap = config.max_draft + 1
+    handles = (C.c_void_p * n)(*[d._h.value for d in decoders])
+    pos = (C.c_size_t * n)(*positions)
+    arrs = [_u32(c) for c in contexts]
+    ctxp = (C.c_void_p * n)(*[a.ctypes.data for a in arrs])
+    lens = (C.c_size_t * n)(*[a.size for a in arrs])
+    out = np.zeros((n, cap), np.uint32)
+    nout = (C.c_size_t * n)()
+    mets = (native.LookupMetricsC * n)()
+    cfg = config._c()
+    check(native.lib().rai_gpu_step_many(handles, n, pos, ctxp, lens, C.byref(cfg), out.ctypes.data_as(C.c_void_p),
+                                         cap, nout, mets))
+    return ([[int(t) for t in out[i, : nout[i]]] for i in range(n)],
+            [LookupMetrics._from_c(mets[i]) for i in range(n)])
+
+
+__all__ = ["RaiModel", "LookupDecoder", "LookupConfig", "LookupMetrics", "RaiError", "step_many"]

@@ -1,0 +1,116 @@
+// Shared device helpers for the sm_100a decode kernels.
+//
+// Numerics rule for every kernel in this library: the reference is Rust,
+// which never contracts a*b+c into an FMA, while nvcc does by default. Every
+// parity-critical expression is therefore written with explicit
+// round-to-nearest intrinsics (__fmul_rn, __fadd_rn, __fmaf_rn, __fdiv_rn,
+// __fsqrt_rn) exactly where the reference multiplies, adds, fuses, divides
+// or takes a square root.
+#pragma once
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace rai {
+
+// Device-side error word (per model context): bit 0 = a bounded wait gave up.
+enum : uint32_t { kErrWaitTimeout = 1u, kErrBadInput = 2u };
+
+// A spin on an mbarrier or flag gives up after this many polls (each poll
+// after the first 64 sleeps ~256 ns, so the bound is ~0.5 s) and reports
+// kErrWaitTimeout instead of hanging the GPU.
+constexpr uint32_t kMaxPolls = 1u << 21;
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+}
+
+__device__ __forceinline__ void fence_barrier_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
+               "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+      " selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait: returns false (and sets the error word) if the phase never
+// completes. Callers stop issuing work after a false return.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32_t* err) {
+  for (uint32_t i = 0; i < kMaxPolls; ++i) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if (i > 64) __nanosleep(256);
+  }
+  if (err) atomicOr(err, kErrWaitTimeout);
+  return false;
+}
+
+// TMA bulk copy global -> this CTA's shared memory, completing on `bar`.
+// Both addresses 16-byte aligned, bytes a multiple of 16.
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// Programmatic dependent launch: let the next kernel in the stream start its
+// prologue, and wait for the previous kernel's results before reading them.
+__device__ __forceinline__ void pdl_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void pdl_wait_prior() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
+// Exact IEEE half -> float (F16C _mm_cvtph_ps / half::f16::to_f32).
+__device__ __forceinline__ float f16_bits_to_f32(uint16_t h) {
+  return __half2float(__ushort_as_half(h));
+}
+
+// 8-lane horizontal sum of the reference (hi+lo, movehdup, add, movehl,
+// add_ss): ((a0+a4)+(a1+a5)) + ((a2+a6)+(a3+a7)).
+__device__ __forceinline__ float hsum8(const float a[8]) {
+  float s0 = __fadd_rn(a[0], a[4]), s1 = __fadd_rn(a[1], a[5]);
+  float s2 = __fadd_rn(a[2], a[6]), s3 = __fadd_rn(a[3], a[7]);
+  return __fadd_rn(__fadd_rn(s0, s1), __fadd_rn(s2, s3));
+}
+
+// Schraudolph exp of silu_mul_avx2 / attention_head_avx2
+// (rai-infer/src/layers.rs:862-869, 1330-1337): bits = cvt_rne(clamp(a*x+b)).
+__device__ __forceinline__ float schraudolph(float x) {
+  float t = __fadd_rn(__fmul_rn(12102203.0f, x), 1065353216.0f - 486411.0f);
+  // _mm256_max_ps(_mm256_min_ps(t, hi), lo): NaN t yields hi then hi.
+  t = (t < 2139095040.0f) ? t : 2139095040.0f;
+  t = (t > 0.0f) ? t : 0.0f;
+  return __int_as_float(__float2int_rn(t));
+}
+
+// Rust f32::exp resolves to glibc expf, which is correctly rounded for all
+// but a tiny fraction of inputs; evaluating exp in double and rounding once
+// reproduces it there (the exceptions are covered by the logit tolerance).
+__device__ __forceinline__ float expf_ref(float x) { return (float)exp((double)x); }
+
+}  // namespace rai

@@ -1,0 +1,68 @@
+// Host-side launch API of the sm_100a kernels (internal to librai_gpu.so).
+#pragma once
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+namespace rai {
+
+// ---- W4A8 / W8A8 exact linear (kernels_gemm.cu) ----
+constexpr int kTileRows = 64;          // weight rows per CTA tile
+constexpr int kRowGroupBytes = 64;     // packed bytes per (row, group)
+constexpr int kWeightStageBytes = kTileRows * kRowGroupBytes;      // 4096
+constexpr int kParamStageBytes = kTileRows * 4;                    // 256
+constexpr int kBlockBytes = kWeightStageBytes + kParamStageBytes;  // 4352
+constexpr int kActRowBytes = 128;      // quantized activation bytes per (token, group)
+constexpr int kActTokBytes = kActRowBytes + 8;  // + (scale, sum) f32 pair
+constexpr int kTokChunk = 32;          // tokens per CTA pass
+
+inline size_t ceil_div(size_t a, size_t b) { return (a + b - 1) / b; }
+inline size_t round_up(size_t a, size_t b) { return ceil_div(a, b) * b; }
+
+// A linear repacked for the device kernel.
+struct PackedLinear {
+  const uint8_t* data = nullptr;  // [tile][group] blocks of kBlockBytes
+  int rows = 0, cols = 0, group_size = 0, groups = 0, tiles = 0;
+  int wbits = 4;                   // 4: u4 codes (+ f16 scale/zero), 8: u8 embedding codes
+};
+
+inline size_t packed_linear_bytes(size_t rows, size_t cols, size_t gs) {
+  return ceil_div(rows, kTileRows) * ceil_div(cols, gs) * (size_t)kBlockBytes;
+}
+
+// Quantized-activation staging for one linear input: per group a block of
+// tok_alloc * 128 B codes then tok_alloc (scale, sum) pairs.
+struct ActBuf {
+  uint8_t* data = nullptr;
+  int tok_alloc = 0;   // multiple of 8
+  int groups = 0;
+  size_t group_stride() const { return (size_t)tok_alloc * kActTokBytes; }
+  static size_t bytes(int tok_alloc, int groups) { return (size_t)tok_alloc * kActTokBytes * groups; }
+};
+
+enum EpilogueMode : int { kEpiStore = 0, kEpiBias = 1, kEpiResidual = 2 };
+
+struct GemmEpilogue {
+  int mode = kEpiStore;
+  const float* bias = nullptr;      // per output row
+  const float* residual = nullptr;  // residual[t * ld + r]
+};
+
+// Pack raw reference-layout weights (device pointers) into `out`.
+cudaError_t pack_linear4(const uint8_t* nibbles, const uint8_t* params, int rows, int cols, int gs,
+                         uint8_t* out, cudaStream_t s);
+cudaError_t pack_linear8(const uint8_t* codes, const uint8_t* params, int rows, int cols, int gs,
+                         uint8_t* out, cudaStream_t s);
+
+// Quantize x[M][ldx] (f32) into `act` for a 4-bit linear (wbits = 4: per
+// group of gs, +-127) or the tied 8-bit head (wbits = 8: per group of gs,
+// +-63). Tokens in [M, tok_alloc) are zero-filled. `m_dev`, if non-null,
+// overrides M with a device-resident active row count.
+cudaError_t quantize_act(const float* x, int ldx, int M, const int* m_dev, int K, int gs, int wbits,
+                         ActBuf act, cudaStream_t s);
+
+// out[t * ld_out + r] (= epilogue(dot)) for t < M, r < rows.
+cudaError_t gemm_exact(const PackedLinear& w, const ActBuf& act, int M, float* out, int ld_out,
+                       const GemmEpilogue& epi, uint32_t* err, cudaStream_t s, bool pdl = false);
+
+}  // namespace rai

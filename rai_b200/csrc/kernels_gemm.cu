@@ -1,0 +1,470 @@
+// Exact W4A8 (and tied W8A8 head) linear for sm_100a.
+//
+// Restates the arithmetic of rai-infer/src/gemm.rs bit for bit:
+//   * activations quantized per (token, group): absmax -> scale = absmax/127
+//     (1.0 below 1e-10) -> q = clamp(rne(x * (1/scale)), -128, 127), plus the
+//     f32 group sum accumulated in 8 lanes then the fixed horizontal-sum tree
+//     (quantize_input_split_avx2, gemm.rs:280-374; compute_input_sums_avx2,
+//     gemm.rs:182-212). The tied head uses +-63 and the embedding group
+//     (quantize_hidden_i8_avx2, gemm.rs:976-1047).
+//   * per (token, row, group) the reference keeps 8 int32 lane dots: lane L
+//     holds columns 8L..8L+7 of every 64-column chunk (PMADDUBSW + PMADDWD,
+//     gemm.rs:455-469); each is converted to f32, multiplied by
+//     (w_scale * x_scale) and added into an 8-lane f32 accumulator in group
+//     order; the row result is the horizontal-sum tree plus the sequential
+//     zero correction sum_g(w_zero * x_sum) (gemm.rs:599-673). For the tied
+//     head lane L holds bytes 4L..4L+3 of each 32-byte chunk (gemm.rs:857-872).
+//
+// Device design: one CTA owns 64 weight rows and sweeps every group in order
+// (the f32 lane accumulation is order-sensitive, so K is never split). A
+// producer warp streams (weights + params, activation codes + scales) for
+// each group through a ring of shared-memory stages with cp.async.bulk (TMA)
+// and mbarriers; four consumer warps each own 16 rows. The per-lane int32
+// dots run on the tensor cores: the repacked weight layout puts each
+// reference lane's 16 columns into one K=16 slice, so one
+// mma.m16n8k16.u8.s8 per lane yields exactly the reference's lane dot for
+// 16 rows x 8 tokens. The accumulator is seeded with 0x4B400000 so the
+// int32 result read as f32 is 12582912 + dot exactly; one subtraction gives
+// the dot as f32 without an I2F conversion.
+#include <cuda_runtime.h>
+
+#include "common.cuh"
+#include "kernels.h"
+
+namespace rai {
+
+namespace {
+
+constexpr int kConsumerWarps = 4;
+constexpr int kThreads = (kConsumerWarps + 1) * 32;
+constexpr uint32_t kMagic = 0x4B400000u;  // 12582912.0f
+constexpr float kMagicF = 12582912.0f;
+
+// ---------------------------------------------------------------------------
+// Weight repack
+// ---------------------------------------------------------------------------
+// 4-bit block (tile, group): row r's 64 bytes are 4 slots of 16 bytes. Slot t
+// (chunk c = t >> 1, column parity p = t & 1) word j, byte b holds in its low
+// nibble the code of group column 64c + 8(2j) + 2b + p (reference lane 2j)
+// and in its high nibble column 64c + 8(2j+1) + 2b + p (lane 2j+1). Chunk 1
+// is zero when the group is 64 wide.
+__global__ void pack4_kernel(const uint8_t* __restrict__ nib, const uint8_t* __restrict__ params,
+                             int rows, int cols, int gs, int groups, uint8_t* __restrict__ out,
+                             size_t total) {
+  size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
+  if (i >= total) return;
+  size_t blk = i / kBlockBytes;
+  int within = (int)(i % kBlockBytes);
+  int g = (int)(blk % groups);
+  int tile = (int)(blk / groups);
+  uint8_t v = 0;
+  if (within < kWeightStageBytes) {
+    int r = within / kRowGroupBytes, o = within % kRowGroupBytes;
+    int row = tile * kTileRows + r;
+    int t = o / 16, j = (o % 16) / 4, b = o % 4;
+    int c = t >> 1, p = t & 1;
+    if (row < rows && 64 * c < gs) {
+      size_t rowbase = (size_t)row * (cols / 2) + (size_t)g * gs / 2;
+      int col0 = 64 * c + 8 * (2 * j) + 2 * b;  // even column of the byte
+      uint8_t lo = nib[rowbase + col0 / 2];
+      uint8_t hi = nib[rowbase + (col0 + 8) / 2];
+      uint8_t c0 = p ? (lo >> 4) : (lo & 0xF);
+      uint8_t c1 = p ? (hi >> 4) : (hi & 0xF);
+      v = (uint8_t)(c0 | (c1 << 4));
+    }
+  } else {
+    int q = within - kWeightStageBytes;
+    int r = q / 4, k = q % 4;
+    int row = tile * kTileRows + r;
+    if (row < rows) v = params[((size_t)row * groups + g) * 4 + k];
+  }
+  out[i] = v;
+}
+
+// 8-bit block (tile, group of 64): row r's 64 bytes are the group's codes in
+// their original order (slot 0 = bytes 0..31, slot 1 = bytes 32..63; lane L
+// of a slot = bytes 4L..4L+3).
+__global__ void pack8_kernel(const uint8_t* __restrict__ codes, const uint8_t* __restrict__ params,
+                             int rows, int cols, int gs, int groups, uint8_t* __restrict__ out,
+                             size_t total) {
+  size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
+  if (i >= total) return;
+  size_t blk = i / kBlockBytes;
+  int within = (int)(i % kBlockBytes);
+  int g = (int)(blk % groups);
+  int tile = (int)(blk / groups);
+  uint8_t v = 0;
+  if (within < kWeightStageBytes) {
+    int r = within / kRowGroupBytes, o = within % kRowGroupBytes;
+    int row = tile * kTileRows + r;
+    if (row < rows) v = codes[(size_t)row * cols + (size_t)g * gs + o];
+  } else {
+    int q = within - kWeightStageBytes;
+    int r = q / 4, k = q % 4;
+    int row = tile * kTileRows + r;
+    if (row < rows) v = params[((size_t)row * groups + g) * 4 + k];
+  }
+  out[i] = v;
+}
+
+// ---------------------------------------------------------------------------
+// Activation quantization: one warp per (token, group).
+// ---------------------------------------------------------------------------
+// Logical byte (slot t, lane L, elem b) of a token row is at t*32 + 4L + b;
+// 16-byte unit u = offset/16 is stored at unit u ^ (token & 7) so the GEMM's
+// B-fragment loads are bank-conflict free.
+__global__ void quantize_kernel(const float* __restrict__ x, int ldx, int M, const int* m_dev,
+                                int K, int gs, int wbits, uint8_t* __restrict__ act, int tok_alloc) {
+  __shared__ float sx[8][128];
+  __shared__ uint32_t sqw[8][32];
+  int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  int g = blockIdx.x;
+  int tok = blockIdx.y * 8 + warp;
+  if (tok >= tok_alloc) return;
+  int mact = m_dev ? *m_dev : M;
+  uint8_t* blk = act + (size_t)g * tok_alloc * kActTokBytes;
+  uint32_t* qrow = reinterpret_cast<uint32_t*>(blk + (size_t)tok * kActRowBytes);
+  float2* sc = reinterpret_cast<float2*>(blk + (size_t)tok_alloc * kActRowBytes) + tok;
+  if (tok >= mact) {
+    qrow[lane] = 0;
+    if (lane == 0) *sc = make_float2(0.f, 0.f);
+    return;
+  }
+  const float* xr = x + (size_t)tok * ldx + (size_t)g * gs;
+  int len = min(gs, K - g * gs);
+  float amax = 0.f;
+  for (int i = lane; i < gs; i += 32) {
+    float v = i < len ? xr[i] : 0.f;
+    sx[warp][i] = v;
+    amax = fmaxf(amax, fabsf(v));
+  }
+  for (int o = 16; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+  const float lim = wbits == 4 ? 127.f : 63.f;
+  const float lo = wbits == 4 ? -128.f : -63.f;
+  float scale = amax > 1e-10f ? __fdiv_rn(amax, lim) : 1.0f;
+  float inv = __fdiv_rn(1.0f, scale);
+  uint8_t* sq = reinterpret_cast<uint8_t*>(sqw[warp]);
+  sqw[warp][lane] = 0;
+  __syncwarp();
+  for (int col = lane; col < len; col += 32) {
+    float r = rintf(__fmul_rn(sx[warp][col], inv));
+    r = fminf(r, lim);
+    r = fmaxf(r, lo);
+    int qv = (int)r;
+    int off;
+    if (wbits == 4) {
+      int c = col >> 6, rr = col & 63, L = rr >> 3, b = (rr & 7) >> 1, p = rr & 1;
+      off = (2 * c + p) * 32 + 4 * L + b;
+    } else {
+      int t = col >> 5, rr = col & 31;
+      off = t * 32 + rr;  // lane L = rr / 4, elem b = rr % 4
+    }
+    sq[off] = (uint8_t)(int8_t)qv;
+  }
+  __syncwarp();
+  // Group sum: lane j accumulates columns 8i + j in order, then the tree.
+  float accj = 0.f;
+  if (lane < 8) {
+    int chunks8 = len / 8;
+    for (int i = 0; i < chunks8; ++i) accj = __fadd_rn(accj, sx[warp][8 * i + lane]);
+  }
+  float a[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) a[j] = __shfl_sync(0xffffffffu, accj, j);
+  float sum = hsum8(a);
+  for (int i = (len / 8) * 8; i < len; ++i) sum = __fadd_rn(sum, sx[warp][i]);
+  // Swizzled store: lane writes 4 bytes of logical unit u = lane / 4.
+  int u = lane >> 2;
+  int phys = ((u ^ (tok & 7)) << 2) | (lane & 3);
+  qrow[phys] = sqw[warp][lane];
+  if (lane == 0) *sc = make_float2(scale, sum);
+}
+
+// ---------------------------------------------------------------------------
+// The exact GEMM
+// ---------------------------------------------------------------------------
+struct GemmParams {
+  const uint8_t* w;
+  const uint8_t* act;
+  float* out;
+  const float* bias;
+  const float* residual;
+  uint32_t* err;
+  int rows, groups, M, tok_alloc, ld_out, mode, stages;
+};
+
+__device__ __forceinline__ void mma_u8s8(uint32_t a0, uint32_t a1, uint32_t b, int32_t d[4]) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5}, {%6}, "
+      "{%7,%7,%7,%7};"
+      : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+      : "r"(a0), "r"(a1), "r"(b), "r"(kMagic));
+}
+
+template <int WBITS, int NTILES>
+__global__ void __launch_bounds__(kThreads, NTILES >= 4 ? 1 : 2) gemm_exact_kernel(GemmParams p) {
+  constexpr int NT = 8 * NTILES;  // token slots per pass
+  constexpr int kStageBytes = kBlockBytes + NT * kActTokBytes;
+  extern __shared__ __align__(128) uint8_t smem[];
+  const int S = p.stages;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + (size_t)S * kStageBytes);
+  uint64_t* empty = full + S;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int tile = blockIdx.x;
+  const int t0 = blockIdx.y * kTokChunk;
+  const int G = p.groups;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kConsumerWarps);
+    }
+    fence_barrier_init();
+  }
+  __syncthreads();
+
+  if (warp == kConsumerWarps) {
+    // ---------------- producer ----------------
+    if (lane == 0) {
+      const int nt = min(NT, p.M - t0);
+      const int npad = (nt + 7) & ~7;
+      const uint32_t bytes = kBlockBytes + npad * kActTokBytes;
+      const size_t act_gstride = (size_t)p.tok_alloc * kActTokBytes;
+      auto issue_act = [&](int g, uint8_t* st) {
+        const uint8_t* ab = p.act + (size_t)g * act_gstride;
+        bulk_g2s(st + kBlockBytes, ab + (size_t)t0 * kActRowBytes, npad * kActRowBytes, &full[g % S]);
+        bulk_g2s(st + kBlockBytes + NT * kActRowBytes,
+                 ab + (size_t)p.tok_alloc * kActRowBytes + (size_t)t0 * 8, npad * 8, &full[g % S]);
+      };
+      // Weights do not depend on the previous kernel, so the first ring's
+      // worth is requested before waiting on it (programmatic dependent
+      // launch); activations are requested after.
+      const int pre = min(S, G);
+      for (int g = 0; g < pre; ++g) {
+        mbar_arrive_expect_tx(&full[g], bytes);
+        bulk_g2s(smem + (size_t)g * kStageBytes, p.w + ((size_t)tile * G + g) * kBlockBytes, kBlockBytes,
+                 &full[g]);
+      }
+      pdl_wait_prior();
+      for (int g = 0; g < pre; ++g) issue_act(g, smem + (size_t)g * kStageBytes);
+      int g = pre;
+      for (; g < G; ++g) {
+        const int s = g % S, n = g / S;
+        if (!mbar_wait(&empty[s], (n - 1) & 1, p.err)) break;
+        uint8_t* st = smem + (size_t)s * kStageBytes;
+        mbar_arrive_expect_tx(&full[s], bytes);
+        bulk_g2s(st, p.w + ((size_t)tile * G + g) * kBlockBytes, kBlockBytes, &full[s]);
+        issue_act(g, st);
+      }
+      if (g < G) {
+        // Gave up: wait (bounded) for the copies still in flight, then exit.
+        for (int gg = (g > S ? g - S : 0); gg < g; ++gg) mbar_wait(&full[gg % S], (gg / S) & 1, nullptr);
+      }
+    }
+    return;
+  }
+
+  // ---------------- consumers ----------------
+  pdl_launch_dependents();
+  const int gq = lane >> 2, tq = lane & 3;
+  const int r0 = warp * 16 + gq;  // tile-local rows r0 and r0 + 8
+  float facc[NTILES][8][4];
+  float zc[NTILES][4];
+#pragma unroll
+  for (int n = 0; n < NTILES; ++n) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) zc[n][i] = 0.f;
+#pragma unroll
+    for (int L = 0; L < 8; ++L)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) facc[n][L][i] = 0.f;
+  }
+
+  bool ok = true;
+  for (int g = 0; g < G; ++g) {
+    const int s = g % S;
+    if (!mbar_wait(&full[s], (g / S) & 1, p.err)) { ok = false; break; }
+    const uint8_t* st = smem + (size_t)s * kStageBytes;
+    const uint8_t* W = st;
+    const uint32_t* P = reinterpret_cast<const uint32_t*>(st + kWeightStageBytes);
+    const uint8_t* Q = st + kBlockBytes;
+    const float2* XS = reinterpret_cast<const float2*>(st + kBlockBytes + NT * kActRowBytes);
+
+    uint32_t A0[8], A1[8];
+    if (WBITS == 4) {
+      uint4 wa = *reinterpret_cast<const uint4*>(W + r0 * kRowGroupBytes + tq * 16);
+      uint4 wb = *reinterpret_cast<const uint4*>(W + (r0 + 8) * kRowGroupBytes + tq * 16);
+      const uint32_t wa_[4] = {wa.x, wa.y, wa.z, wa.w}, wb_[4] = {wb.x, wb.y, wb.z, wb.w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        A0[2 * j] = wa_[j] & 0x0F0F0F0Fu;
+        A0[2 * j + 1] = (wa_[j] >> 4) & 0x0F0F0F0Fu;
+        A1[2 * j] = wb_[j] & 0x0F0F0F0Fu;
+        A1[2 * j + 1] = (wb_[j] >> 4) & 0x0F0F0F0Fu;
+      }
+    } else {
+      if (tq < 2) {
+        const uint4* pa = reinterpret_cast<const uint4*>(W + r0 * kRowGroupBytes + tq * 32);
+        const uint4* pb = reinterpret_cast<const uint4*>(W + (r0 + 8) * kRowGroupBytes + tq * 32);
+        uint4 a_lo = pa[0], a_hi = pa[1], b_lo = pb[0], b_hi = pb[1];
+        A0[0] = a_lo.x; A0[1] = a_lo.y; A0[2] = a_lo.z; A0[3] = a_lo.w;
+        A0[4] = a_hi.x; A0[5] = a_hi.y; A0[6] = a_hi.z; A0[7] = a_hi.w;
+        A1[0] = b_lo.x; A1[1] = b_lo.y; A1[2] = b_lo.z; A1[3] = b_lo.w;
+        A1[4] = b_hi.x; A1[5] = b_hi.y; A1[6] = b_hi.z; A1[7] = b_hi.w;
+      } else {
+#pragma unroll
+        for (int L = 0; L < 8; ++L) A0[L] = A1[L] = 0u;
+      }
+    }
+    const uint32_t p0 = P[r0], p1 = P[r0 + 8];
+    const float ws0 = f16_bits_to_f32((uint16_t)(p0 & 0xFFFF)), wz0 = f16_bits_to_f32((uint16_t)(p0 >> 16));
+    const float ws1 = f16_bits_to_f32((uint16_t)(p1 & 0xFFFF)), wz1 = f16_bits_to_f32((uint16_t)(p1 >> 16));
+
+#pragma unroll
+    for (int n = 0; n < NTILES; ++n) {
+      const int tb = n * 8 + gq;  // B-fragment token (column gq of the N tile)
+      const uint8_t* qrow = Q + tb * kActRowBytes;
+      const uint4 u0 = *reinterpret_cast<const uint4*>(qrow + (((2 * tq) ^ (tb & 7)) << 4));
+      const uint4 u1 = *reinterpret_cast<const uint4*>(qrow + (((2 * tq + 1) ^ (tb & 7)) << 4));
+      const uint32_t B[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
+      const float2 xa = XS[n * 8 + 2 * tq], xb = XS[n * 8 + 2 * tq + 1];
+      // combined_scale = w_scale * x_scale (gemm.rs:606, 493)
+      const float c00 = __fmul_rn(ws0, xa.x), c01 = __fmul_rn(ws0, xb.x);
+      const float c10 = __fmul_rn(ws1, xa.x), c11 = __fmul_rn(ws1, xb.x);
+#pragma unroll
+      for (int L = 0; L < 8; ++L) {
+        int32_t d[4];
+        mma_u8s8(A0[L], A1[L], B[L], d);
+        facc[n][L][0] = __fadd_rn(facc[n][L][0], __fmul_rn(__fsub_rn(__int_as_float(d[0]), kMagicF), c00));
+        facc[n][L][1] = __fadd_rn(facc[n][L][1], __fmul_rn(__fsub_rn(__int_as_float(d[1]), kMagicF), c01));
+        facc[n][L][2] = __fadd_rn(facc[n][L][2], __fmul_rn(__fsub_rn(__int_as_float(d[2]), kMagicF), c10));
+        facc[n][L][3] = __fadd_rn(facc[n][L][3], __fmul_rn(__fsub_rn(__int_as_float(d[3]), kMagicF), c11));
+      }
+      // zero correction: sum_g w_zero * x_sum, sequential in g (gemm.rs:666-670)
+      zc[n][0] = __fadd_rn(zc[n][0], __fmul_rn(wz0, xa.y));
+      zc[n][1] = __fadd_rn(zc[n][1], __fmul_rn(wz0, xb.y));
+      zc[n][2] = __fadd_rn(zc[n][2], __fmul_rn(wz1, xa.y));
+      zc[n][3] = __fadd_rn(zc[n][3], __fmul_rn(wz1, xb.y));
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[s]);
+  }
+  if (!ok) return;
+
+  // Epilogue: horizontal-sum tree + zero correction, then bias / residual.
+#pragma unroll
+  for (int n = 0; n < NTILES; ++n) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int row = tile * kTileRows + r0 + ((i & 2) ? 8 : 0);
+      const int tok = t0 + n * 8 + 2 * tq + (i & 1);
+      if (row >= p.rows || tok >= p.M) continue;
+      float a[8];
+#pragma unroll
+      for (int L = 0; L < 8; ++L) a[L] = facc[n][L][i];
+      float v = __fadd_rn(hsum8(a), zc[n][i]);
+      const size_t o = (size_t)tok * p.ld_out + row;
+      if (p.mode == kEpiBias) v = __fadd_rn(v, p.bias[row]);
+      else if (p.mode == kEpiResidual) v = __fadd_rn(p.residual[o], v);
+      p.out[o] = v;
+    }
+  }
+}
+
+template <int WBITS, int NTILES>
+cudaError_t launch_gemm(const GemmParams& gp, int tiles, int chunks, cudaStream_t s, bool pdl) {
+  constexpr int NT = 8 * NTILES;
+  constexpr int kStageBytes = kBlockBytes + NT * kActTokBytes;
+  int stages = (int)(((NTILES >= 4 ? 200 : 100) * 1024) / kStageBytes);
+  if (stages > 24) stages = 24;
+  if (stages > gp.groups) stages = gp.groups < 2 ? 2 : gp.groups;
+  GemmParams p = gp;
+  p.stages = stages;
+  size_t smem = (size_t)stages * kStageBytes + 2 * stages * sizeof(uint64_t);
+  auto kern = gemm_exact_kernel<WBITS, NTILES>;
+  // The attribute is raised once per process (not inside stream capture).
+  static bool attr_set = false;
+  if (!attr_set) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 210 * 1024);
+    if (e != cudaSuccess) return e;
+    attr_set = true;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(tiles, chunks);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kern, p);
+}
+
+}  // namespace
+
+cudaError_t pack_linear4(const uint8_t* nibbles, const uint8_t* params, int rows, int cols, int gs,
+                         uint8_t* out, cudaStream_t s) {
+  int groups = (int)ceil_div(cols, gs);
+  size_t total = packed_linear_bytes(rows, cols, gs);
+  int threads = 256;
+  size_t blocks = ceil_div(total, threads);
+  pack4_kernel<<<(unsigned)blocks, threads, 0, s>>>(nibbles, params, rows, cols, gs, groups, out, total);
+  return cudaGetLastError();
+}
+
+cudaError_t pack_linear8(const uint8_t* codes, const uint8_t* params, int rows, int cols, int gs,
+                         uint8_t* out, cudaStream_t s) {
+  int groups = (int)ceil_div(cols, gs);
+  size_t total = packed_linear_bytes(rows, cols, gs);
+  int threads = 256;
+  size_t blocks = ceil_div(total, threads);
+  pack8_kernel<<<(unsigned)blocks, threads, 0, s>>>(codes, params, rows, cols, gs, groups, out, total);
+  return cudaGetLastError();
+}
+
+cudaError_t quantize_act(const float* x, int ldx, int M, const int* m_dev, int K, int gs, int wbits,
+                         ActBuf act, cudaStream_t s) {
+  dim3 grid((unsigned)act.groups, (unsigned)ceil_div(act.tok_alloc, 8));
+  quantize_kernel<<<grid, 256, 0, s>>>(x, ldx, M, m_dev, K, gs, wbits, act.data, act.tok_alloc);
+  return cudaGetLastError();
+}
+
+cudaError_t gemm_exact(const PackedLinear& w, const ActBuf& act, int M, float* out, int ld_out,
+                       const GemmEpilogue& epi, uint32_t* err, cudaStream_t s, bool pdl) {
+  if (M <= 0) return cudaSuccess;
+  GemmParams gp = {};
+  gp.w = w.data;
+  gp.act = act.data;
+  gp.out = out;
+  gp.bias = epi.bias;
+  gp.residual = epi.residual;
+  gp.err = err;
+  gp.rows = w.rows;
+  gp.groups = w.groups;
+  gp.M = M;
+  gp.tok_alloc = act.tok_alloc;
+  gp.ld_out = ld_out;
+  gp.mode = epi.mode;
+  int per = M < kTokChunk ? M : kTokChunk;
+  int ntiles = (per + 7) / 8;
+  int chunks = (int)ceil_div(M, kTokChunk);
+  if (w.wbits == 4) {
+    switch (ntiles) {
+      case 1: return launch_gemm<4, 1>(gp, w.tiles, chunks, s, pdl);
+      case 2: return launch_gemm<4, 2>(gp, w.tiles, chunks, s, pdl);
+      case 3: return launch_gemm<4, 3>(gp, w.tiles, chunks, s, pdl);
+      default: return launch_gemm<4, 4>(gp, w.tiles, chunks, s, pdl);
+    }
+  }
+  switch (ntiles) {
+    case 1: return launch_gemm<8, 1>(gp, w.tiles, chunks, s, pdl);
+    case 2: return launch_gemm<8, 2>(gp, w.tiles, chunks, s, pdl);
+    case 3: return launch_gemm<8, 3>(gp, w.tiles, chunks, s, pdl);
+    default: return launch_gemm<8, 4>(gp, w.tiles, chunks, s, pdl);
+  }
+}
+
+}  // namespace rai

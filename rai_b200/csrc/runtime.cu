@@ -1,0 +1,761 @@
+// C ABI (include/rai_gpu.h): model upload, decoder state, the forward pass
+// and the CUDA-graph decode step.
+//
+// The step restates LookupDecoder::step (rai-infer/src/lookup.rs:260-425)
+// entirely on the device: ngram_kernel drafts from the device copy of the
+// context, the verify forward runs over a fixed row budget of max_draft + 1
+// with the active row count read from device memory, accept_kernel applies
+// greedy acceptance and rolls the KV watermark back. The host copies the
+// context in, replays one CUDA graph and reads one small struct back.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <memory>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "../../include/rai_gpu.h"
+#include "common.cuh"
+#include "kernels.h"
+#include "layers.h"
+#include "raimodel_format.h"
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int code, const std::string& msg) {
+  g_last_error = msg;
+  return code;
+}
+
+#define RAI_CUDA(call)                                                                        \
+  do {                                                                                        \
+    cudaError_t e_ = (call);                                                                  \
+    if (e_ != cudaSuccess)                                                                    \
+      return fail(e_ == cudaErrorMemoryAllocation ? RAI_ERR_OOM : RAI_ERR_DEVICE,             \
+                  std::string(#call) + ": " + cudaGetErrorString(e_));                        \
+  } while (0)
+
+using raimodel::Config;
+using rai::ActBuf;
+using rai::PackedLinear;
+
+// RoPETable::with_scaling + apply_llama3_scaling (rai-infer/src/layers.rs:
+// 561-633, 760-808), built on the host with the same f32 libm calls the
+// reference makes, then uploaded.
+void build_rope(const Config& c, float theta, std::vector<float>& cs, std::vector<float>& sn) {
+  size_t hd = c.head_dim, half = hd / 2, mc = c.max_context;
+  std::vector<float> inv(half);
+  for (size_t i = 0; i < half; ++i) {
+    float e = 2.0f * (float)i / (float)hd;
+    inv[i] = 1.0f / powf(theta, e);
+  }
+  if (c.rope_type == 1) {
+    float old_ctx = (float)c.rope_orig_max;
+    float low_wl = old_ctx / c.rope_low, high_wl = old_ctx / c.rope_high;
+    const float two_pi = 2.0f * 3.14159265358979323846f;
+    for (size_t i = 0; i < half; ++i) {
+      float v = inv[i];
+      float wl = two_pi / v;
+      float banded = wl > low_wl ? v / c.rope_factor : v;
+      if (wl >= high_wl && wl <= low_wl) {
+        float smooth = (old_ctx / wl - c.rope_low) / (c.rope_high - c.rope_low);
+        float a = (1.0f - smooth) * banded;
+        a = a / c.rope_factor;
+        float b = smooth * banded;
+        inv[i] = a + b;
+      } else {
+        inv[i] = banded;
+      }
+    }
+  }
+  cs.resize(mc * half);
+  sn.resize(mc * half);
+  for (size_t p = 0; p < mc; ++p)
+    for (size_t i = 0; i < half; ++i) {
+      float ang = (float)p * inv[i];
+      cs[p * half + i] = cosf(ang);
+      sn[p * half + i] = sinf(ang);
+    }
+}
+
+}  // namespace
+
+struct LayerDev {
+  PackedLinear qkv, o, gateup, down;
+  float* bias_qkv = nullptr;
+  float* in_norm = nullptr;
+  float* post_norm = nullptr;
+  float* q_norm = nullptr;
+  float* k_norm = nullptr;
+};
+
+struct rai_model {
+  int device = 0;
+  Config cfg;
+  raimodel::Model layout;
+  std::vector<void*> allocs;
+  std::vector<LayerDev> layers;
+  PackedLinear head;
+  uint8_t* embed_codes = nullptr;
+  uint8_t* embed_params = nullptr;
+  float* final_norm = nullptr;
+  float* rope_cos = nullptr;
+  float* rope_sin = nullptr;
+  float scale = 0.f;
+  int qk_mode = 0;  // 0 none, 1 per head, 2 full width
+  size_t device_bytes = 0;
+  uint32_t* err_dev = nullptr;
+
+  template <class T>
+  int alloc(T** p, size_t bytes) {
+    void* q = nullptr;
+    cudaError_t e = cudaMalloc(&q, bytes ? bytes : 16);
+    if (e != cudaSuccess)
+      return fail(RAI_ERR_OOM, "cudaMalloc(" + std::to_string(bytes) + "): " + cudaGetErrorString(e));
+    allocs.push_back(q);
+    device_bytes += bytes;
+    *p = static_cast<T*>(q);
+    return RAI_OK;
+  }
+  ~rai_model() {
+    int prev = 0;
+    cudaGetDevice(&prev);
+    cudaSetDevice(device);
+    for (void* p : allocs) cudaFree(p);
+    cudaSetDevice(prev);
+  }
+};
+
+struct rai_dec {
+  rai_model* m = nullptr;
+  int max_ctx = 0;
+  int mcap = 0;  // rows the scratch buffers hold
+  cudaStream_t stream = nullptr;
+  std::vector<void*> allocs;
+  float* kc = nullptr;  // [layer][kv_head][max_ctx][head_dim]
+  float* vc = nullptr;
+  int* filled_dev = nullptr;
+  std::vector<size_t> filled;
+  float *hidden = nullptr, *resid = nullptr, *normed = nullptr, *qkv = nullptr, *q = nullptr;
+  float *attn = nullptr, *gu = nullptr, *ff = nullptr, *logits = nullptr;
+  ActBuf act_h, act_q, act_ff, act_head;
+  uint32_t* ids_dev = nullptr;
+  uint32_t* ctx_dev = nullptr;
+  uint32_t* ctx_host = nullptr;
+  rai::StepState* st_dev = nullptr;
+  rai::StepState* st_host = nullptr;
+  cudaGraphExec_t graph = nullptr;
+  uint32_t graph_key[3] = {0, 0, 0};
+  cudaEvent_t ev0 = nullptr, ev1 = nullptr;
+  float last_us = 0.f;
+
+  template <class T>
+  int alloc(T** p, size_t bytes) {
+    void* q_ = nullptr;
+    cudaError_t e = cudaMalloc(&q_, bytes ? bytes : 16);
+    if (e != cudaSuccess)
+      return fail(RAI_ERR_OOM, "cudaMalloc(" + std::to_string(bytes) + "): " + cudaGetErrorString(e));
+    allocs.push_back(q_);
+    *p = static_cast<T*>(q_);
+    return RAI_OK;
+  }
+  ~rai_dec() {
+    int prev = 0;
+    cudaGetDevice(&prev);
+    cudaSetDevice(m->device);
+    if (graph) cudaGraphExecDestroy(graph);
+    if (stream) cudaStreamSynchronize(stream);
+    for (void* p : allocs) cudaFree(p);
+    if (ctx_host) cudaFreeHost(ctx_host);
+    if (st_host) cudaFreeHost(st_host);
+    if (ev0) cudaEventDestroy(ev0);
+    if (ev1) cudaEventDestroy(ev1);
+    if (stream) cudaStreamDestroy(stream);
+    cudaSetDevice(prev);
+  }
+};
+
+namespace {
+
+// Scoped device switch for entry points.
+struct DeviceGuard {
+  int prev = -1;
+  explicit DeviceGuard(int dev) {
+    cudaGetDevice(&prev);
+    if (prev != dev) cudaSetDevice(dev);
+  }
+  ~DeviceGuard() {
+    int cur = -1;
+    cudaGetDevice(&cur);
+    if (prev >= 0 && cur != prev) cudaSetDevice(prev);
+  }
+};
+
+int upload(rai_model* M, const void* host, size_t bytes, void** dev) {
+  uint8_t* p = nullptr;
+  int rc = M->alloc(&p, bytes);
+  if (rc) return rc;
+  RAI_CUDA(cudaMemcpy(p, host, bytes, cudaMemcpyHostToDevice));
+  *dev = p;
+  return RAI_OK;
+}
+
+int upload_vec(rai_model* M, const uint8_t* blob, const raimodel::Vec32& v, float** dev) {
+  std::vector<float> h = raimodel::read_vec(blob, v);
+  return upload(M, h.data(), h.size() * 4, reinterpret_cast<void**>(dev));
+}
+
+// Pack one or more raw linears with the same cols into one device linear
+// (rows concatenated in order).
+int pack_concat(rai_model* M, const uint8_t* blob_dev, const std::vector<const raimodel::Linear*>& parts,
+                PackedLinear* out) {
+  size_t cols = parts[0]->cols, gs = parts[0]->group_size, ng = parts[0]->num_groups();
+  size_t rows = 0;
+  for (auto* p : parts) rows += p->rows;
+  uint8_t* packed = nullptr;
+  int rc = M->alloc(&packed, rai::packed_linear_bytes(rows, cols, gs));
+  if (rc) return rc;
+  const uint8_t *nib = nullptr, *par = nullptr;
+  void* tmp = nullptr;
+  if (parts.size() == 1) {
+    nib = blob_dev + parts[0]->nib_off;
+    par = blob_dev + parts[0]->params_off;
+  } else {
+    size_t nb = rows * cols / 2, pb = rows * ng * 4;
+    RAI_CUDA(cudaMalloc(&tmp, nb + pb));
+    uint8_t* t = static_cast<uint8_t*>(tmp);
+    size_t no = 0, po = 0;
+    for (auto* p : parts) {
+      RAI_CUDA(cudaMemcpy(t + no, blob_dev + p->nib_off, p->nib_len, cudaMemcpyDeviceToDevice));
+      RAI_CUDA(cudaMemcpy(t + nb + po, blob_dev + p->params_off, p->params_len, cudaMemcpyDeviceToDevice));
+      no += p->nib_len;
+      po += p->params_len;
+    }
+    nib = t;
+    par = t + nb;
+  }
+  RAI_CUDA(rai::pack_linear4(nib, par, (int)rows, (int)cols, (int)gs, packed, 0));
+  RAI_CUDA(cudaDeviceSynchronize());
+  if (tmp) cudaFree(tmp);
+  out->data = packed;
+  out->rows = (int)rows;
+  out->cols = (int)cols;
+  out->group_size = (int)gs;
+  out->groups = (int)ng;
+  out->tiles = (int)rai::ceil_div(rows, rai::kTileRows);
+  out->wbits = 4;
+  return RAI_OK;
+}
+
+int check_supported(const Config& c, const raimodel::Model& L) {
+  if (c.group_size != 64 && c.group_size != 128)
+    return fail(RAI_ERR_UNSUPPORTED, "group_size " + std::to_string(c.group_size) + " (this build runs 64 or 128)");
+  if (!L.has_lm_head && c.embed_group_size != 64)
+    return fail(RAI_ERR_UNSUPPORTED, "tied head with embed_group_size != 64");
+  if (c.activation != 0) return fail(RAI_ERR_UNSUPPORTED, "GeLU-tanh activation");
+  if (c.has_sandwich_norm || c.post_norm) return fail(RAI_ERR_UNSUPPORTED, "sandwich / post-norm placement");
+  if (c.global_layer_stride) return fail(RAI_ERR_UNSUPPORTED, "per-layer RoPE bases");
+  if (c.final_logit_softcap > 0.f) return fail(RAI_ERR_UNSUPPORTED, "final logit softcap");
+  if (c.num_experts) return fail(RAI_ERR_UNSUPPORTED, "mixture-of-experts layers");
+  if ((c.bias_mask & 7) != 0 && (c.bias_mask & 7) != 7)
+    return fail(RAI_ERR_UNSUPPORTED, "bias on only some of q/k/v");
+  if (c.bias_mask & 0x78) return fail(RAI_ERR_UNSUPPORTED, "bias on o/gate/up/down projections");
+  int hpk = (int)(c.num_heads / c.num_kv_heads);
+  if (hpk > 8) return fail(RAI_ERR_UNSUPPORTED, "more than 8 query heads per KV head");
+  if (c.head_dim != 16 && c.head_dim != 32 && c.head_dim != 64 && c.head_dim != 128)
+    return fail(RAI_ERR_UNSUPPORTED, "head_dim " + std::to_string(c.head_dim));
+  if (hpk * c.head_dim > 1024) return fail(RAI_ERR_UNSUPPORTED, "attention group wider than 1024");
+  return RAI_OK;
+}
+
+// ---------------------------------------------------------------------------
+// Forward over M rows (static), of which *m_dev are active when m_dev is set.
+// Positions are pos + b with pos from pos_dev (device) or pos0 (host).
+int forward(rai_dec* d, int M, const int* m_dev, const int* pos_dev, int pos0, const uint32_t* ids_dev,
+            bool logits) {
+  rai_model* Mo = d->m;
+  const Config& c = Mo->cfg;
+  cudaStream_t s = d->stream;
+  const int h = c.hidden_size, nh = c.num_heads, nkv = c.num_kv_heads, hd = c.head_dim;
+  const int qd = nh * hd, kvd = nkv * hd, ffd = c.intermediate_size;
+  const int gs = c.group_size;
+  const float eps = c.norm_eps;
+  uint32_t* err = Mo->err_dev;
+  RAI_CUDA(rai::launch_embed(ids_dev, m_dev, M, Mo->embed_codes, Mo->embed_params, c.vocab_size, h,
+                             c.embed_group_size, c.embed_scale, d->hidden, err, s));
+  for (size_t li = 0; li < c.num_layers; ++li) {
+    const LayerDev& L = Mo->layers[li];
+    float* kc = d->kc + li * (size_t)nkv * d->max_ctx * hd;
+    float* vc = d->vc + li * (size_t)nkv * d->max_ctx * hd;
+    RAI_CUDA(rai::launch_rmsnorm(d->hidden, L.in_norm, h, eps, d->normed, d->resid, m_dev, M, s));
+    RAI_CUDA(rai::quantize_act(d->normed, h, M, m_dev, h, gs, 4, d->act_h, s));
+    rai::GemmEpilogue e_qkv;
+    if (L.bias_qkv) { e_qkv.mode = rai::kEpiBias; e_qkv.bias = L.bias_qkv; }
+    RAI_CUDA(rai::gemm_exact(L.qkv, d->act_h, M, d->qkv, qd + 2 * kvd, e_qkv, err, s));
+    RAI_CUDA(rai::launch_qkv_post(d->qkv, qd + 2 * kvd, d->q, nh, nkv, hd, L.q_norm, L.k_norm, Mo->qk_mode, eps,
+                                  Mo->rope_cos, Mo->rope_sin, kc, vc, d->max_ctx, pos_dev, pos0, m_dev, M, s));
+    RAI_CUDA(rai::launch_attention(d->q, d->attn, kc, vc, nh, nkv, hd, d->max_ctx, pos_dev, pos0, m_dev, M,
+                                   Mo->scale, c.attn_logit_softcap, d->max_ctx, s));
+    RAI_CUDA(rai::quantize_act(d->attn, qd, M, m_dev, qd, gs, 4, d->act_q, s));
+    rai::GemmEpilogue e_res;
+    e_res.mode = rai::kEpiResidual;
+    e_res.residual = d->resid;
+    RAI_CUDA(rai::gemm_exact(L.o, d->act_q, M, d->hidden, h, e_res, err, s));
+    RAI_CUDA(rai::launch_rmsnorm(d->hidden, L.post_norm, h, eps, d->normed, d->resid, m_dev, M, s));
+    RAI_CUDA(rai::quantize_act(d->normed, h, M, m_dev, h, gs, 4, d->act_h, s));
+    RAI_CUDA(rai::gemm_exact(L.gateup, d->act_h, M, d->gu, 2 * ffd, rai::GemmEpilogue{}, err, s));
+    RAI_CUDA(rai::launch_swiglu(d->gu, ffd, d->ff, m_dev, M, s));
+    RAI_CUDA(rai::quantize_act(d->ff, ffd, M, m_dev, ffd, gs, 4, d->act_ff, s));
+    RAI_CUDA(rai::gemm_exact(L.down, d->act_ff, M, d->hidden, h, e_res, err, s));
+  }
+  if (logits) {
+    RAI_CUDA(rai::launch_rmsnorm(d->hidden, Mo->final_norm, h, eps, d->normed, nullptr, m_dev, M, s));
+    bool tied = Mo->head.wbits == 8;
+    RAI_CUDA(rai::quantize_act(d->normed, h, M, m_dev, h, tied ? c.embed_group_size : gs, tied ? 8 : 4,
+                               d->act_head, s));
+    RAI_CUDA(rai::gemm_exact(Mo->head, d->act_head, M, d->logits, c.vocab_size, rai::GemmEpilogue{}, err, s));
+  }
+  return RAI_OK;
+}
+
+int check_err(rai_dec* d) {
+  uint32_t e = 0;
+  RAI_CUDA(cudaMemcpyAsync(&e, d->m->err_dev, 4, cudaMemcpyDeviceToHost, d->stream));
+  RAI_CUDA(cudaStreamSynchronize(d->stream));
+  if (e) {
+    cudaMemsetAsync(d->m->err_dev, 0, 4, d->stream);
+    if (e & rai::kErrWaitTimeout) return fail(RAI_ERR_TIMEOUT, "a device-side wait timed out");
+    return fail(RAI_ERR_INVALID, "device kernel rejected its input (token id out of range)");
+  }
+  return RAI_OK;
+}
+
+int validate_cfg(const rai_lookup_cfg* cfg) {
+  if (!cfg) return fail(RAI_ERR_INVALID, "null lookup config");
+  // validate_lookup_config (rai-infer/src/lookup.rs:457-475)
+  if (cfg->max_draft == 0) return fail(RAI_ERR_INVALID, "prompt-lookup max_draft must be non-zero");
+  if (!(cfg->min_ngram >= 1 && cfg->min_ngram <= cfg->max_ngram))
+    return fail(RAI_ERR_INVALID, "prompt-lookup requires 1 <= min_ngram <= max_ngram");
+  if (!(std::isfinite(cfg->temperature) && cfg->temperature >= 0.f) || cfg->top_k != 0 || cfg->top_p != 1.0f ||
+      cfg->repetition_penalty != 1.0f)
+    return fail(RAI_ERR_INVALID,
+                "prompt-lookup decoding requires finite temperature, top_k=0, top_p=1, and repetition_penalty=1");
+  if (cfg->temperature != 0.f)
+    return fail(RAI_ERR_UNSUPPORTED, "sampled acceptance (temperature > 0); this build runs greedy (temperature 0)");
+  if (cfg->max_draft + 1 > (uint32_t)rai::kMaxRows)
+    return fail(RAI_ERR_INVALID, "max_draft exceeds 32");
+  return RAI_OK;
+}
+
+int ensure_graph(rai_dec* d, const rai_lookup_cfg* cfg) {
+  uint32_t key[3] = {cfg->max_draft, cfg->max_ngram, cfg->min_ngram};
+  if (d->graph && std::memcmp(key, d->graph_key, sizeof(key)) == 0) return RAI_OK;
+  if (d->graph) {
+    cudaGraphExecDestroy(d->graph);
+    d->graph = nullptr;
+  }
+  const int rows = (int)cfg->max_draft + 1;
+  cudaStream_t s = d->stream;
+  cudaGraph_t g = nullptr;
+  RAI_CUDA(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal));
+  int rc = RAI_OK;
+  do {
+    if (cudaSuccess != rai::launch_ngram(d->ctx_dev, d->st_dev, (int)cfg->max_draft, (int)cfg->max_ngram,
+                                         (int)cfg->min_ngram, d->max_ctx, s)) {
+      rc = fail(RAI_ERR_DEVICE, "ngram launch failed");
+      break;
+    }
+    rc = forward(d, rows, &d->st_dev->n_rows, &d->st_dev->pos, 0, d->st_dev->tokens, true);
+    if (rc) break;
+    if (cudaSuccess != rai::launch_argmax(d->logits, d->m->cfg.vocab_size, &d->st_dev->n_rows, rows,
+                                          d->st_dev->amax, s)) {
+      rc = fail(RAI_ERR_DEVICE, "argmax launch failed");
+      break;
+    }
+    if (cudaSuccess != rai::launch_accept(d->st_dev, d->filled_dev, d->m->cfg.num_layers, s)) {
+      rc = fail(RAI_ERR_DEVICE, "accept launch failed");
+      break;
+    }
+  } while (0);
+  cudaError_t ce = cudaStreamEndCapture(s, &g);
+  if (rc) {
+    if (g) cudaGraphDestroy(g);
+    return rc;
+  }
+  if (ce != cudaSuccess) return fail(RAI_ERR_DEVICE, std::string("graph capture: ") + cudaGetErrorString(ce));
+  cudaError_t ie = cudaGraphInstantiate(&d->graph, g, 0);
+  cudaGraphDestroy(g);
+  if (ie != cudaSuccess) return fail(RAI_ERR_DEVICE, std::string("graph instantiate: ") + cudaGetErrorString(ie));
+  std::memcpy(d->graph_key, key, sizeof(key));
+  return RAI_OK;
+}
+
+int alloc_act(rai_dec* d, ActBuf* a, int tok, int cols, int gs) {
+  a->tok_alloc = (int)rai::round_up(tok, 8);
+  a->groups = (int)rai::ceil_div(cols, gs);
+  return d->alloc(&a->data, ActBuf::bytes(a->tok_alloc, a->groups));
+}
+
+}  // namespace
+
+// ===========================================================================
+extern "C" {
+
+size_t rai_gpu_last_error(char* buf, size_t len) {
+  if (buf && len) {
+    size_t n = std::min(len - 1, g_last_error.size());
+    std::memcpy(buf, g_last_error.data(), n);
+    buf[n] = 0;
+  }
+  return g_last_error.size();
+}
+
+int rai_gpu_model_create(const uint8_t* blob, size_t len, int device, rai_model** out) {
+  if (!blob || !out) return fail(RAI_ERR_INVALID, "null argument");
+  *out = nullptr;
+  // Host-side validation first (RaiModelFile::open), so a malformed file is
+  // reported as such whether or not a device is present.
+  raimodel::Model layout;
+  std::string err;
+  if (!raimodel::open(blob, len, layout, err)) return fail(RAI_ERR_FORMAT, err);
+  if (int rc = check_supported(layout.cfg, layout)) return rc;
+  int ndev = 0;
+  if (cudaGetDeviceCount(&ndev) != cudaSuccess || ndev == 0) return fail(RAI_ERR_DEVICE, "no CUDA device");
+  if (device < 0 || device >= ndev) return fail(RAI_ERR_INVALID, "device index out of range");
+  DeviceGuard guard(device);
+  auto M = std::make_unique<rai_model>();
+  M->device = device;
+  M->layout = std::move(layout);
+  M->cfg = M->layout.cfg;
+  const Config& c = M->cfg;
+  M->scale = c.attention_scale();
+  M->qk_mode = c.has_full_qk_norm ? 2 : (c.has_qk_norm ? 1 : 0);
+  if (int rc = M->alloc(&M->err_dev, 4)) return rc;
+  RAI_CUDA(cudaMemset(M->err_dev, 0, 4));
+
+  // Upload the blob once; pack from the device copy, then release it.
+  uint8_t* blob_dev = nullptr;
+  RAI_CUDA(cudaMalloc(&blob_dev, len));
+  struct Free { uint8_t* p; ~Free() { if (p) cudaFree(p); } } free_blob{blob_dev};
+  RAI_CUDA(cudaMemcpy(blob_dev, blob, len, cudaMemcpyHostToDevice));
+
+  const auto& E = M->layout.embed;
+  size_t ecodes = (size_t)E.vocab * E.hidden, eparams = (size_t)E.vocab * rai::ceil_div(E.hidden, E.group_size) * 4;
+  if (int rc = M->alloc(&M->embed_codes, ecodes)) return rc;
+  if (int rc = M->alloc(&M->embed_params, eparams)) return rc;
+  RAI_CUDA(cudaMemcpy(M->embed_codes, blob_dev + E.data_off, ecodes, cudaMemcpyDeviceToDevice));
+  RAI_CUDA(cudaMemcpy(M->embed_params, blob_dev + E.params_off, eparams, cudaMemcpyDeviceToDevice));
+
+  M->layers.resize(c.num_layers);
+  for (size_t li = 0; li < c.num_layers; ++li) {
+    const raimodel::Layer& L = M->layout.layers[li];
+    LayerDev& D = M->layers[li];
+    if (int rc = pack_concat(M.get(), blob_dev, {&L.proj[0], &L.proj[1], &L.proj[2]}, &D.qkv)) return rc;
+    if (int rc = pack_concat(M.get(), blob_dev, {&L.proj[3]}, &D.o)) return rc;
+    if (int rc = pack_concat(M.get(), blob_dev, {&L.proj[4], &L.proj[5]}, &D.gateup)) return rc;
+    if (int rc = pack_concat(M.get(), blob_dev, {&L.proj[6]}, &D.down)) return rc;
+    if (int rc = upload_vec(M.get(), blob, L.input_norm, &D.in_norm)) return rc;
+    if (int rc = upload_vec(M.get(), blob, L.post_attn_norm, &D.post_norm)) return rc;
+    if ((c.bias_mask & 7) == 7) {
+      std::vector<float> b;
+      for (int p = 0; p < 3; ++p) {
+        auto v = raimodel::read_vec(blob, L.bias[p]);
+        b.insert(b.end(), v.begin(), v.end());
+      }
+      if (int rc = upload(M.get(), b.data(), b.size() * 4, reinterpret_cast<void**>(&D.bias_qkv))) return rc;
+    }
+    if (L.q_norm.present) {
+      if (int rc = upload_vec(M.get(), blob, L.q_norm, &D.q_norm)) return rc;
+      if (int rc = upload_vec(M.get(), blob, L.k_norm, &D.k_norm)) return rc;
+    }
+  }
+  if (int rc = upload_vec(M.get(), blob, M->layout.final_norm, &M->final_norm)) return rc;
+  if (M->layout.has_lm_head) {
+    if (int rc = pack_concat(M.get(), blob_dev, {&M->layout.lm_head}, &M->head)) return rc;
+  } else {
+    uint8_t* packed = nullptr;
+    if (int rc = M->alloc(&packed, rai::packed_linear_bytes(E.vocab, E.hidden, E.group_size))) return rc;
+    RAI_CUDA(rai::pack_linear8(M->embed_codes, M->embed_params, (int)E.vocab, (int)E.hidden, (int)E.group_size,
+                               packed, 0));
+    M->head.data = packed;
+    M->head.rows = (int)E.vocab;
+    M->head.cols = (int)E.hidden;
+    M->head.group_size = (int)E.group_size;
+    M->head.groups = (int)rai::ceil_div(E.hidden, E.group_size);
+    M->head.tiles = (int)rai::ceil_div(E.vocab, rai::kTileRows);
+    M->head.wbits = 8;
+  }
+  std::vector<float> cs, sn;
+  build_rope(c, c.rope_theta, cs, sn);
+  if (int rc = upload(M.get(), cs.data(), cs.size() * 4, reinterpret_cast<void**>(&M->rope_cos))) return rc;
+  if (int rc = upload(M.get(), sn.data(), sn.size() * 4, reinterpret_cast<void**>(&M->rope_sin))) return rc;
+  RAI_CUDA(cudaDeviceSynchronize());
+  *out = M.release();
+  return RAI_OK;
+}
+
+int rai_gpu_model_destroy(rai_model* model) {
+  delete model;
+  return RAI_OK;
+}
+
+int rai_gpu_model_info(const rai_model* m, rai_model_info* info) {
+  if (!m || !info) return fail(RAI_ERR_INVALID, "null argument");
+  const Config& c = m->cfg;
+  info->hidden_size = c.hidden_size;
+  info->num_layers = c.num_layers;
+  info->num_heads = c.num_heads;
+  info->num_kv_heads = c.num_kv_heads;
+  info->head_dim = c.head_dim;
+  info->intermediate_size = c.intermediate_size;
+  info->vocab_size = c.vocab_size;
+  info->max_context = c.max_context;
+  info->group_size = c.group_size;
+  info->embed_group_size = c.embed_group_size;
+  info->num_experts = c.num_experts;
+  info->experts_per_token = c.experts_per_token;
+  info->tied_embeddings = m->layout.has_lm_head ? 0 : 1;
+  info->version = c.version;
+  info->device_bytes = m->device_bytes;
+  return RAI_OK;
+}
+
+int rai_gpu_decoder_create(rai_model* m, size_t max_ctx, rai_dec** out) {
+  if (!m || !out) return fail(RAI_ERR_INVALID, "null argument");
+  *out = nullptr;
+  size_t ctx = std::min<size_t>(max_ctx, m->cfg.max_context);
+  if (ctx == 0) return fail(RAI_ERR_INVALID, "prompt-lookup context must be non-zero");
+  DeviceGuard guard(m->device);
+  const Config& c = m->cfg;
+  auto d = std::make_unique<rai_dec>();
+  d->m = m;
+  d->max_ctx = (int)ctx;
+  d->mcap = (int)std::max<size_t>(rai::kMaxRows, std::min<size_t>(256, ctx));
+  RAI_CUDA(cudaStreamCreateWithFlags(&d->stream, cudaStreamNonBlocking));
+  RAI_CUDA(cudaEventCreate(&d->ev0));
+  RAI_CUDA(cudaEventCreate(&d->ev1));
+  size_t kv = (size_t)c.num_layers * c.num_kv_heads * ctx * c.head_dim * sizeof(float);
+  if (int rc = d->alloc(&d->kc, kv)) return rc;
+  if (int rc = d->alloc(&d->vc, kv)) return rc;
+  RAI_CUDA(cudaMemset(d->kc, 0, kv));
+  RAI_CUDA(cudaMemset(d->vc, 0, kv));
+  if (int rc = d->alloc(&d->filled_dev, c.num_layers * sizeof(int))) return rc;
+  RAI_CUDA(cudaMemset(d->filled_dev, 0, c.num_layers * sizeof(int)));
+  d->filled.assign(c.num_layers, 0);
+  const size_t R = d->mcap, h = c.hidden_size, qd = c.q_dim(), kvd = c.kv_dim(), ff = c.intermediate_size;
+  if (int rc = d->alloc(&d->hidden, R * h * 4)) return rc;
+  if (int rc = d->alloc(&d->resid, R * h * 4)) return rc;
+  if (int rc = d->alloc(&d->normed, R * h * 4)) return rc;
+  if (int rc = d->alloc(&d->qkv, R * (qd + 2 * kvd) * 4)) return rc;
+  if (int rc = d->alloc(&d->q, R * qd * 4)) return rc;
+  if (int rc = d->alloc(&d->attn, R * qd * 4)) return rc;
+  if (int rc = d->alloc(&d->gu, R * 2 * ff * 4)) return rc;
+  if (int rc = d->alloc(&d->ff, R * ff * 4)) return rc;
+  if (int rc = d->alloc(&d->logits, (size_t)rai::kMaxRows * c.vocab_size * 4)) return rc;
+  if (int rc = alloc_act(d.get(), &d->act_h, (int)R, (int)h, c.group_size)) return rc;
+  if (int rc = alloc_act(d.get(), &d->act_q, (int)R, (int)qd, c.group_size)) return rc;
+  if (int rc = alloc_act(d.get(), &d->act_ff, (int)R, (int)ff, c.group_size)) return rc;
+  int hgs = m->head.wbits == 8 ? (int)c.embed_group_size : (int)c.group_size;
+  if (int rc = alloc_act(d.get(), &d->act_head, rai::kMaxRows, (int)h, hgs)) return rc;
+  if (int rc = d->alloc(&d->ids_dev, R * 4)) return rc;
+  if (int rc = d->alloc(&d->ctx_dev, ctx * 4)) return rc;
+  if (int rc = d->alloc(&d->st_dev, sizeof(rai::StepState))) return rc;
+  RAI_CUDA(cudaMemset(d->st_dev, 0, sizeof(rai::StepState)));
+  RAI_CUDA(cudaMallocHost(&d->ctx_host, ctx * 4));
+  RAI_CUDA(cudaMallocHost(&d->st_host, sizeof(rai::StepState)));
+  size_t attn_smem = rai::attention_smem_bytes(c.head_dim, c.num_heads / c.num_kv_heads, (int)ctx);
+  if (attn_smem > 227 * 1024)
+    return fail(RAI_ERR_UNSUPPORTED, "context window too long for the single-pass attention kernel");
+  *out = d.release();
+  return RAI_OK;
+}
+
+int rai_gpu_decoder_destroy(rai_dec* d) {
+  delete d;
+  return RAI_OK;
+}
+
+int rai_gpu_prefill(rai_dec* d, const uint32_t* ids, size_t n, size_t* pos_out) {
+  if (!d || !pos_out || (!ids && n)) return fail(RAI_ERR_INVALID, "null argument");
+  if (n == 0) return fail(RAI_ERR_INVALID, "prompt must contain at least one token");
+  if (n > (size_t)d->max_ctx) return fail(RAI_ERR_INVALID, "prompt exceeds the prompt-lookup context window");
+  const Config& c = d->m->cfg;
+  for (size_t i = 0; i + 1 < n; ++i)
+    if (ids[i] >= c.vocab_size) return fail(RAI_ERR_INVALID, "token id is out of model vocabulary");
+  DeviceGuard guard(d->m->device);
+  size_t m = n - 1;
+  *pos_out = m;
+  if (m == 0) return RAI_OK;
+  for (size_t start = 0; start < m; start += d->mcap) {
+    int rows = (int)std::min<size_t>(d->mcap, m - start);
+    if (start > d->filled[0]) return fail(RAI_ERR_INVALID, "KV store would leave a gap");
+    RAI_CUDA(cudaMemcpyAsync(d->ids_dev, ids + start, rows * 4, cudaMemcpyHostToDevice, d->stream));
+    if (int rc = forward(d, rows, nullptr, nullptr, (int)start, d->ids_dev, false)) return rc;
+    if (int rc = check_err(d)) return rc;
+    for (auto& f : d->filled) f = std::max(f, start + rows);
+  }
+  std::vector<int> fd(d->filled.begin(), d->filled.end());
+  RAI_CUDA(cudaMemcpy(d->filled_dev, fd.data(), fd.size() * 4, cudaMemcpyHostToDevice));
+  return RAI_OK;
+}
+
+int rai_gpu_forward_logits(rai_dec* d, const uint32_t* ids, size_t start_pos, size_t batch, float* logits) {
+  if (!d || !ids || batch == 0) return fail(RAI_ERR_INVALID, "bad argument");
+  const Config& c = d->m->cfg;
+  if (batch > (size_t)rai::kMaxRows) return fail(RAI_ERR_INVALID, "batch exceeds 33 rows");
+  if (start_pos + batch > (size_t)d->max_ctx || start_pos + batch > c.max_context)
+    return fail(RAI_ERR_INVALID, "batch position exceeds model context");
+  if (start_pos > d->filled[0]) return fail(RAI_ERR_INVALID, "KV store would leave a gap");
+  for (size_t i = 0; i < batch; ++i)
+    if (ids[i] >= c.vocab_size) return fail(RAI_ERR_INVALID, "token id is out of model vocabulary");
+  DeviceGuard guard(d->m->device);
+  RAI_CUDA(cudaMemcpyAsync(d->ids_dev, ids, batch * 4, cudaMemcpyHostToDevice, d->stream));
+  if (int rc = forward(d, (int)batch, nullptr, nullptr, (int)start_pos, d->ids_dev, true)) return rc;
+  if (logits)
+    RAI_CUDA(cudaMemcpyAsync(logits, d->logits, batch * c.vocab_size * 4, cudaMemcpyDeviceToHost, d->stream));
+  if (int rc = check_err(d)) return rc;
+  for (auto& f : d->filled) f = std::max(f, start_pos + batch);
+  std::vector<int> fd(d->filled.begin(), d->filled.end());
+  RAI_CUDA(cudaMemcpy(d->filled_dev, fd.data(), fd.size() * 4, cudaMemcpyHostToDevice));
+  return RAI_OK;
+}
+
+int rai_gpu_step(rai_dec* d, size_t pos, const uint32_t* ctx, size_t ctx_len, const rai_lookup_cfg* cfg,
+                 uint32_t* out_tokens, size_t out_cap, size_t* n_out, rai_lookup_metrics* metrics) {
+  if (!d || !ctx || !out_tokens || !n_out) return fail(RAI_ERR_INVALID, "null argument");
+  if (int rc = validate_cfg(cfg)) return rc;
+  if (ctx_len == 0) return fail(RAI_ERR_INVALID, "prompt-lookup step requires a non-empty context");
+  if (pos >= (size_t)d->max_ctx) return fail(RAI_ERR_INVALID, "decode position exceeds the context window");
+  if (ctx_len > (size_t)d->max_ctx) return fail(RAI_ERR_INVALID, "context longer than the window");
+  if (out_cap < cfg->max_draft + 1) return fail(RAI_ERR_INVALID, "out_tokens capacity below max_draft + 1");
+  if (pos > d->filled[0]) return fail(RAI_ERR_INVALID, "KV store would leave a gap");
+  const Config& c = d->m->cfg;
+  for (size_t i = 0; i < ctx_len; ++i)
+    if (ctx[i] >= c.vocab_size) return fail(RAI_ERR_INVALID, "context contains a token outside the model vocabulary");
+  DeviceGuard guard(d->m->device);
+  if (int rc = ensure_graph(d, cfg)) return rc;
+  std::memcpy(d->ctx_host, ctx, ctx_len * 4);
+  d->st_host->pos = (int)pos;
+  d->st_host->ctx_len = (int)ctx_len;
+  cudaStream_t s = d->stream;
+  RAI_CUDA(cudaEventRecord(d->ev0, s));
+  RAI_CUDA(cudaMemcpyAsync(d->ctx_dev, d->ctx_host, ctx_len * 4, cudaMemcpyHostToDevice, s));
+  RAI_CUDA(cudaMemcpyAsync(d->st_dev, d->st_host, 2 * sizeof(int), cudaMemcpyHostToDevice, s));
+  RAI_CUDA(cudaGraphLaunch(d->graph, s));
+  RAI_CUDA(cudaMemcpyAsync(d->st_host, d->st_dev, sizeof(rai::StepState), cudaMemcpyDeviceToHost, s));
+  RAI_CUDA(cudaEventRecord(d->ev1, s));
+  if (int rc = check_err(d)) return rc;
+  cudaEventElapsedTime(&d->last_us, d->ev0, d->ev1);
+  d->last_us *= 1000.f;
+  const rai::StepState& st = *d->st_host;
+  *n_out = (size_t)st.produced;
+  for (int i = 0; i < st.produced; ++i) out_tokens[i] = st.out[i];
+  for (auto& f : d->filled) f = pos + st.produced;
+  if (metrics) {
+    metrics->accepted = st.accepted;
+    metrics->drafted = st.drafted;
+    metrics->produced = st.produced;
+    metrics->matched_ngram = st.ngram;
+    metrics->accept_rate = st.drafted ? (float)st.accepted / (float)st.drafted : 0.f;
+  }
+  return RAI_OK;
+}
+
+int rai_gpu_step_many(rai_dec* const* decs, size_t n, const size_t* pos, const uint32_t* const* ctx,
+                      const size_t* ctx_len, const rai_lookup_cfg* cfg, uint32_t* out_tokens, size_t out_cap,
+                      size_t* n_out, rai_lookup_metrics* metrics) {
+  if (!decs || !pos || !ctx || !ctx_len || !out_tokens || !n_out) return fail(RAI_ERR_INVALID, "null argument");
+  for (size_t i = 0; i < n; ++i) {
+    int rc = rai_gpu_step(decs[i], pos[i], ctx[i], ctx_len[i], cfg, out_tokens + i * out_cap, out_cap, n_out + i,
+                          metrics ? metrics + i : nullptr);
+    if (rc) return rc;
+  }
+  return RAI_OK;
+}
+
+int rai_gpu_kv_filled(const rai_dec* d, size_t layer, size_t* filled) {
+  if (!d || !filled) return fail(RAI_ERR_INVALID, "null argument");
+  if (layer >= d->filled.size()) return fail(RAI_ERR_INVALID, "layer index out of range");
+  *filled = d->filled[layer];
+  return RAI_OK;
+}
+
+int rai_gpu_kv_truncate(rai_dec* d, size_t len) {
+  if (!d) return fail(RAI_ERR_INVALID, "null argument");
+  for (auto& f : d->filled) f = std::min(f, len);
+  std::vector<int> fd(d->filled.begin(), d->filled.end());
+  DeviceGuard guard(d->m->device);
+  RAI_CUDA(cudaMemcpy(d->filled_dev, fd.data(), fd.size() * 4, cudaMemcpyHostToDevice));
+  return RAI_OK;
+}
+
+int rai_gpu_kv_read(const rai_dec* d, size_t layer, size_t kvh, size_t pos, float* k, float* v) {
+  if (!d || !k || !v) return fail(RAI_ERR_INVALID, "null argument");
+  const Config& c = d->m->cfg;
+  if (layer >= c.num_layers || kvh >= c.num_kv_heads) return fail(RAI_ERR_INVALID, "KV cache head is out of range");
+  if (pos >= d->filled[layer]) return fail(RAI_ERR_INVALID, "KV read at unwritten position");
+  DeviceGuard guard(d->m->device);
+  size_t off = ((layer * c.num_kv_heads + kvh) * (size_t)d->max_ctx + pos) * c.head_dim;
+  RAI_CUDA(cudaMemcpy(k, d->kc + off, c.head_dim * 4, cudaMemcpyDeviceToHost));
+  RAI_CUDA(cudaMemcpy(v, d->vc + off, c.head_dim * 4, cudaMemcpyDeviceToHost));
+  return RAI_OK;
+}
+
+int rai_gpu_last_step_us(const rai_dec* d, float* us) {
+  if (!d || !us) return fail(RAI_ERR_INVALID, "null argument");
+  *us = d->last_us;
+  return RAI_OK;
+}
+
+// ---- kernel-level entry points ----
+size_t rai_gpu_w4a8_packed_bytes(size_t rows, size_t cols, size_t gs) {
+  return rai::packed_linear_bytes(rows, cols, gs);
+}
+
+int rai_gpu_w4a8_pack(const uint8_t* nibbles, const uint8_t* params, size_t rows, size_t cols, size_t gs,
+                      void* packed, void* stream) {
+  if (!nibbles || !params || !packed) return fail(RAI_ERR_INVALID, "null argument");
+  if (gs != 64 && gs != 128) return fail(RAI_ERR_UNSUPPORTED, "group_size must be 64 or 128");
+  if (cols % 2 || cols == 0 || rows == 0) return fail(RAI_ERR_INVALID, "rows must be non-zero, cols non-zero and even");
+  if (rai::ceil_div(cols, gs) > raimodel::kMaxGroups) return fail(RAI_ERR_INVALID, "quantization group count exceeds kernel capacity");
+  RAI_CUDA(rai::pack_linear4(nibbles, params, (int)rows, (int)cols, (int)gs, static_cast<uint8_t*>(packed),
+                             static_cast<cudaStream_t>(stream)));
+  return RAI_OK;
+}
+
+size_t rai_gpu_w4a8_scratch_bytes(size_t tokens, size_t cols, size_t gs) {
+  return ActBuf::bytes((int)rai::round_up(tokens, 8), (int)rai::ceil_div(cols, gs));
+}
+
+int rai_gpu_w4a8_matmul(float* out, const void* packed, const float* input, size_t rows, size_t cols, size_t tokens,
+                        size_t gs, void* scratch, size_t scratch_bytes, void* stream) {
+  if (!out || !packed || !input || !scratch) return fail(RAI_ERR_INVALID, "null argument");
+  if (gs != 64 && gs != 128) return fail(RAI_ERR_UNSUPPORTED, "group_size must be 64 or 128");
+  if (tokens == 0 || rows == 0 || cols == 0 || cols % 2) return fail(RAI_ERR_INVALID, "bad dimensions");
+  if (rai::ceil_div(cols, gs) > raimodel::kMaxGroups) return fail(RAI_ERR_INVALID, "quantization group count exceeds kernel capacity");
+  if (scratch_bytes < rai_gpu_w4a8_scratch_bytes(tokens, cols, gs)) return fail(RAI_ERR_INVALID, "scratch buffer is too small");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  ActBuf a;
+  a.data = static_cast<uint8_t*>(scratch);
+  a.tok_alloc = (int)rai::round_up(tokens, 8);
+  a.groups = (int)rai::ceil_div(cols, gs);
+  RAI_CUDA(rai::quantize_act(input, (int)cols, (int)tokens, nullptr, (int)cols, (int)gs, 4, a, s));
+  PackedLinear w;
+  w.data = static_cast<const uint8_t*>(packed);
+  w.rows = (int)rows;
+  w.cols = (int)cols;
+  w.group_size = (int)gs;
+  w.groups = a.groups;
+  w.tiles = (int)rai::ceil_div(rows, rai::kTileRows);
+  w.wbits = 4;
+  RAI_CUDA(rai::gemm_exact(w, a, (int)tokens, out, (int)rows, rai::GemmEpilogue{}, nullptr, s));
+  return RAI_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,38 @@
+"""The C-ABI library loads and exports every symbol include/rai_gpu.h
+declares (no compute without a GPU)."""
+import ctypes
+import os
+import re
+
+from conftest import ROOT
+
+
+def _declared():
+    src = open(os.path.join(ROOT, "include", "rai_gpu.h")).read()
+    return sorted(set(re.findall(r"RAI_API\s+\w+\s+(rai_gpu_\w+)\s*\(", src)))
+
+
+def test_header_declares_the_boundary():
+    names = _declared()
+    for required in ("rai_gpu_model_create", "rai_gpu_decoder_create", "rai_gpu_prefill", "rai_gpu_step",
+                     "rai_gpu_kv_filled", "rai_gpu_decoder_destroy", "rai_gpu_model_destroy",
+                     "rai_gpu_last_error"):
+        assert required in names
+
+
+def test_library_exports_every_declared_symbol():
+    from rai_b200 import native
+    lib = native.lib()
+    for name in _declared():
+        assert hasattr(lib, name), name
+        assert ctypes.cast(getattr(lib, name), ctypes.c_void_p).value
+
+
+def test_errors_are_status_codes_not_aborts():
+    import rai_b200
+    from rai_b200 import native
+    try:
+        rai_b200.RaiModel(b"\x00" * 10)
+        raise AssertionError("expected an error")
+    except rai_b200.RaiError as e:
+        assert e.code == native.RAI_ERR_FORMAT

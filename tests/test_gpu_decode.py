@@ -1,0 +1,131 @@
+"""The device decode path vs the oracle on the same models and prompts.
+
+Bar: logits within max|d| <= 1e-3 * max|logit|; greedy
+tokens and drafted / accepted / produced counts identical; KV watermark ==
+pos after every step. The only non-restated arithmetic is libm expf in the
+attention softmax tail, so logits are usually bit-identical too; the test
+reports how many rows are.
+"""
+import numpy as np
+import pytest
+
+from conftest import periodic_prompt
+
+pytestmark = pytest.mark.gpu
+torch = pytest.importorskip("torch")
+
+MODELS = ["tiny-tied", "tiny-untied", "tiny-llama", "tiny-qwen", "tiny-llama3"]
+
+
+def _open(paths, name, oracle, max_ctx=256):
+    import rai_b200
+    gm = rai_b200.RaiModel.load(paths[name])
+    om = oracle.Model.load(paths[name])
+    return gm, om, rai_b200.LookupDecoder(gm, max_ctx), oracle.Decoder(om, max_ctx)
+
+
+def _tol(want):
+    return 1e-3 * max(float(np.max(np.abs(want))), 1e-30)
+
+
+@pytest.mark.parametrize("name", MODELS)
+def test_forward_logits_match_oracle(tiny_model_paths, oracle, name):
+    gm, om, gd, od = _open(tiny_model_paths, name, oracle)
+    vocab = gm.config["vocab_size"]
+    ids = periodic_prompt(24, vocab, seed=3)
+    want = od.forward_logits(ids, 0)
+    got = gd.forward_logits(ids, 0)
+    assert np.max(np.abs(got - want)) <= _tol(want)
+    assert np.array_equal(np.argmax(got, 1), np.argmax(want, 1))
+    # verify-sized batch at a later position on top of the stored cache
+    ids2 = periodic_prompt(9, vocab, seed=4)
+    want2 = od.forward_logits(ids2, 24)
+    got2 = gd.forward_logits(ids2, 24)
+    assert np.max(np.abs(got2 - want2)) <= _tol(want2)
+    exact = sum(np.array_equal(a, b) for a, b in zip(got2, want2))
+    print(f"{name}: {exact}/{len(ids2)} verify rows bit-identical")
+
+
+@pytest.mark.parametrize("name", MODELS)
+def test_kv_rows_match_oracle(tiny_model_paths, oracle, name):
+    gm, om, gd, od = _open(tiny_model_paths, name, oracle)
+    ids = periodic_prompt(12, gm.config["vocab_size"], seed=5)
+    gd.forward_logits(ids, 0)
+    od.forward_logits(ids, 0)
+    for layer in (0, gm.config["num_layers"] - 1):
+        for pos in (0, 11):
+            gk, gv = gd.kv_read(layer, 0, pos)
+            ok, ov = od.kv_read(layer, 0, pos)
+            assert np.allclose(gk, ok, rtol=1e-5, atol=1e-6) and np.allclose(gv, ov, rtol=1e-5, atol=1e-6)
+
+
+@pytest.mark.parametrize("name", MODELS)
+@pytest.mark.parametrize("k", [1, 4, 8])
+def test_lookup_steps_match_oracle(tiny_model_paths, oracle, name, k):
+    import rai_b200
+    gm, om, gd, od = _open(tiny_model_paths, name, oracle)
+    vocab = gm.config["vocab_size"]
+    prompt = periodic_prompt(40, vocab, seed=k)
+    pos_g = gd.prefill(prompt)
+    pos_o = od.prefill(prompt)
+    assert pos_g == pos_o == len(prompt) - 1
+    ctx = list(prompt)
+    pos = pos_g
+    cfg = rai_b200.LookupConfig(max_draft=k, max_ngram=3, min_ngram=1)
+    for _ in range(14):
+        gt, gmet = gd.step(pos, ctx, cfg)
+        ot, omet = od.step(pos, ctx, k)
+        assert gt == ot, (pos, gt, ot)
+        assert (gmet.accepted, gmet.drafted, gmet.produced) == (omet["accepted"], omet["drafted"], omet["produced"])
+        assert gmet.matched_ngram == omet["matched_ngram"]
+        ctx += gt
+        pos += len(gt)
+        assert gd.kv_filled(0) == pos == od.kv_filled(0)
+
+
+def test_no_draft_step_produces_one_token(tiny_model_paths, oracle):
+    import rai_b200
+    gm, om, gd, od = _open(tiny_model_paths, "tiny-llama", oracle)
+    prompt = list(range(1, 30))  # no repeated n-gram
+    pos = gd.prefill(prompt)
+    od.prefill(prompt)
+    toks, met = gd.step(pos, prompt, rai_b200.LookupConfig(max_draft=4))
+    otoks, omet = od.step(pos, prompt, 4)
+    assert met.drafted == 0 and met.produced == 1 and met.matched_ngram is None
+    assert toks == otoks
+
+
+def test_errors_follow_the_reference(tiny_model_paths, oracle):
+    import rai_b200
+    gm, om, gd, od = _open(tiny_model_paths, "tiny-llama", oracle, max_ctx=64)
+    prompt = periodic_prompt(20, gm.config["vocab_size"], seed=1)
+    pos = gd.prefill(prompt)
+    for bad in (rai_b200.LookupConfig(max_draft=0), rai_b200.LookupConfig(min_ngram=0),
+                rai_b200.LookupConfig(min_ngram=4, max_ngram=3), rai_b200.LookupConfig(top_k=40)):
+        with pytest.raises(rai_b200.RaiError):
+            gd.step(pos, prompt, bad)
+    with pytest.raises(rai_b200.RaiError):
+        gd.step(64, prompt, rai_b200.LookupConfig(max_draft=2))  # beyond the window
+    with pytest.raises(rai_b200.RaiError):
+        gd.prefill([])
+    with pytest.raises(rai_b200.RaiError):
+        gd.step(pos, prompt[:-1] + [10 ** 6], rai_b200.LookupConfig(max_draft=2))
+    # the decoder still works after rejected calls
+    toks, met = gd.step(pos, prompt, rai_b200.LookupConfig(max_draft=2))
+    assert met.produced >= 1
+
+
+def test_window_end_caps_the_draft(tiny_model_paths, oracle):
+    import rai_b200
+    gm, om, gd, od = _open(tiny_model_paths, "tiny-llama", oracle, max_ctx=44)
+    prompt = periodic_prompt(40, gm.config["vocab_size"], seed=9)
+    ctx = list(prompt)
+    pos = gd.prefill(prompt)
+    od.prefill(prompt)
+    while pos < 43:
+        gt, gmet = gd.step(pos, ctx, rai_b200.LookupConfig(max_draft=8))
+        ot, omet = od.step(pos, ctx, 8)
+        assert gt == ot and gmet.drafted == omet["drafted"]
+        assert pos + gmet.produced <= 44
+        ctx += gt
+        pos += len(gt)
