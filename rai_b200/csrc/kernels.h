@@ -48,6 +48,10 @@ struct GemmEpilogue {
   const float* residual = nullptr;  // residual[t * ld + r]
 };
 
+// Raise the dynamic shared-memory limit of every GEMM variant (call once
+// per process before capturing a graph).
+cudaError_t init_gemm_attributes();
+
 // Pack raw reference-layout weights (device pointers) into `out`.
 cudaError_t pack_linear4(const uint8_t* nibbles, const uint8_t* params, int rows, int cols, int gs,
                          uint8_t* out, cudaStream_t s);

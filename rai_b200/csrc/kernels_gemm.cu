@@ -383,13 +383,6 @@ cudaError_t launch_gemm(const GemmParams& gp, int tiles, int chunks, cudaStream_
   p.stages = stages;
   size_t smem = (size_t)stages * kStageBytes + 2 * stages * sizeof(uint64_t);
   auto kern = gemm_exact_kernel<WBITS, NTILES>;
-  // The attribute is raised once per process (not inside stream capture).
-  static bool attr_set = false;
-  if (!attr_set) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 210 * 1024);
-    if (e != cudaSuccess) return e;
-    attr_set = true;
-  }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(tiles, chunks);
   cfg.blockDim = dim3(kThreads);
@@ -404,6 +397,18 @@ cudaError_t launch_gemm(const GemmParams& gp, int tiles, int chunks, cudaStream_
 }
 
 }  // namespace
+
+cudaError_t init_gemm_attributes() {
+  // Raised once per process, before any stream capture.
+  const int bytes = 210 * 1024;
+  cudaError_t e = cudaSuccess;
+  auto set = [&](auto kern) {
+    if (e == cudaSuccess) e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  };
+  set(gemm_exact_kernel<4, 1>); set(gemm_exact_kernel<4, 2>); set(gemm_exact_kernel<4, 3>); set(gemm_exact_kernel<4, 4>);
+  set(gemm_exact_kernel<8, 1>); set(gemm_exact_kernel<8, 2>); set(gemm_exact_kernel<8, 3>); set(gemm_exact_kernel<8, 4>);
+  return e;
+}
 
 cudaError_t pack_linear4(const uint8_t* nibbles, const uint8_t* params, int rows, int cols, int gs,
                          uint8_t* out, cudaStream_t s) {

@@ -481,15 +481,7 @@ cudaError_t launch_attention(const float* q, float* out, const float* kc, const 
   dim3 grid(nkv, M);
   cudaError_t e = cudaSuccess;
 #define RAI_ATTN(HDV)                                                                                  \
-  case HDV: {                                                                                          \
-    static bool attr_set = false;                                                                      \
-    if (!attr_set) {                                                                                   \
-      e = cudaFuncSetAttribute(attention_kernel<HDV>, cudaFuncAttributeMaxDynamicSharedMemorySize,     \
-                               227 * 1024);                                                            \
-      if (e != cudaSuccess) return e;                                                                  \
-      attr_set = true;                                                                                 \
-    }                                                                                                  \
-  }                                                                                                    \
+  case HDV:                                                                                            \
     attention_kernel<HDV><<<grid, 256, smem, s>>>(q, out, kc, vc, nh, nkv, max_ctx, pos_dev, pos0,     \
                                                   m_dev, M, scale, softcap, n_alloc);                  \
     break;
@@ -503,6 +495,15 @@ cudaError_t launch_attention(const float* q, float* out, const float* kc, const 
   }
 #undef RAI_ATTN
   return cudaGetLastError();
+}
+
+cudaError_t init_layer_attributes() {
+  const int bytes = 227 * 1024;
+  cudaError_t e = cudaFuncSetAttribute(attention_kernel<16>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e == cudaSuccess) e = cudaFuncSetAttribute(attention_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e == cudaSuccess) e = cudaFuncSetAttribute(attention_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e == cudaSuccess) e = cudaFuncSetAttribute(attention_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  return e;
 }
 
 cudaError_t launch_swiglu(const float* gu, int ff, float* act, const int* m_dev, int M, cudaStream_t s) {

@@ -24,6 +24,10 @@ struct StepState {
   unsigned long long amax[kMaxRows];
 };
 
+// Raise the dynamic shared-memory limit of the attention kernels (once per
+// process, before any stream capture).
+cudaError_t init_layer_attributes();
+
 cudaError_t launch_embed(const uint32_t* ids, const int* m_dev, int M, const uint8_t* codes,
                          const uint8_t* params, int vocab, int hidden, int gs, float embed_scale,
                          float* out, uint32_t* err, cudaStream_t s);

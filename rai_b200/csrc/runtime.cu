@@ -429,6 +429,8 @@ int rai_gpu_model_create(const uint8_t* blob, size_t len, int device, rai_model*
   if (cudaGetDeviceCount(&ndev) != cudaSuccess || ndev == 0) return fail(RAI_ERR_DEVICE, "no CUDA device");
   if (device < 0 || device >= ndev) return fail(RAI_ERR_INVALID, "device index out of range");
   DeviceGuard guard(device);
+  RAI_CUDA(rai::init_gemm_attributes());
+  RAI_CUDA(rai::init_layer_attributes());
   auto M = std::make_unique<rai_model>();
   M->device = device;
   M->layout = std::move(layout);
@@ -741,6 +743,7 @@ int rai_gpu_w4a8_matmul(float* out, const void* packed, const float* input, size
   if (rai::ceil_div(cols, gs) > raimodel::kMaxGroups) return fail(RAI_ERR_INVALID, "quantization group count exceeds kernel capacity");
   if (scratch_bytes < rai_gpu_w4a8_scratch_bytes(tokens, cols, gs)) return fail(RAI_ERR_INVALID, "scratch buffer is too small");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  RAI_CUDA(rai::init_gemm_attributes());
   ActBuf a;
   a.data = static_cast<uint8_t*>(scratch);
   a.tok_alloc = (int)rai::round_up(tokens, 8);
