@@ -1,0 +1,367 @@
+"""Benchmark: prompt-lookup speculative decode step on B200.
+
+Workload: TinyLlama-1.1B-shaped decoder (22 layers,
+hidden 2048, 32/4 heads x 64, FFN 5632, vocab 32000), seeded synthetic
+weights RTN-quantized to the reference's .raimodel format; 64 independent
+streams with distinct seeds, each a 1024-token prompt of which 40% are spans
+copied from earlier positions; greedy prompt-lookup with k = 8
+(max_ngram 3, min_ngram 1). Streams are sharded data-parallel over the
+ranks (64 / N per GPU, no collective). A step = one lookup step
+(draft + (k+1)-row verify + greedy accept + KV rollback) of every stream on
+the GPU. Weights (550 MB) exceed L2 (126 MB), so no flush is needed.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
+
+Prints one JSON line (rank 0). `value` = tokens produced by all streams per
+second of device time (CUDA events around each step's graph, max over ranks);
+`e2e` = the same through the C ABI with host context/result copies inside
+the timed region (wall clock per step call).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import tempfile
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+MODEL = "tinyllama-1.1b"
+STREAMS = 64
+PROMPT = 1024
+COPY_FRAC = 0.40
+K_DRAFT = 8
+METRIC = "accepted tok/s per stream + verify-step us at k=8; W4A8 GEMM HBM GB/s vs peak"
+
+
+def make_prompt(seed: int, n: int, vocab: int, copy_frac: float) -> list:
+    """Uniform random ids with spans (16..48 tokens) copied verbatim from
+    earlier positions until `copy_frac` of the prompt is copied."""
+    rng = np.random.default_rng(seed)
+    ids = list(rng.integers(0, vocab, size=n))
+    copied = np.zeros(n, bool)
+    target = int(copy_frac * n)
+    while copied.sum() < target:
+        ln = int(rng.integers(16, 49))
+        dst = int(rng.integers(64, n - ln))
+        src = int(rng.integers(0, dst - ln))
+        ids[dst:dst + ln] = ids[src:src + ln]
+        copied[dst:dst + ln] = True
+    return [int(t) for t in ids]
+
+
+def model_path(rank: int, world: int) -> str:
+    from rai_b200 import convert
+    path = os.path.join(tempfile.gettempdir(), f"rai_bench_{MODEL}.raimodel")
+    if rank == 0 and not os.path.exists(path):
+        convert.write_synthetic(path + f".{os.getpid()}", MODEL, seed=0, fast=True)
+        os.replace(path + f".{os.getpid()}", path)
+    return path
+
+
+class ClockSampler:
+    """nvidia-smi clocks/throttle sampling during the timed region."""
+
+    def __init__(self, device: int):
+        self.device = device
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.device), f"--query-gpu={q}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *a):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], 0.0, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = max(mx, float(parts[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": mx or None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+def gemm_traffic_from_profile():
+    """DRAM bytes per launch of the dominant GEMM from the committed ncu
+    summary (profiles/), scaled as that file states; None if absent."""
+    p = os.path.join(ROOT, "profiles", "w4a8_gemm_tinyllama_gateup_m9.md")
+    try:
+        for line in open(p):
+            if line.startswith("dram_bytes_per_launch:"):
+                return float(line.split(":")[1])
+    except OSError:
+        pass
+    return None
+
+
+def measure_gemm_roofline(torch, k_rows: int, iters: int = 50):
+    """Time the exact W4A8 GEMM kernel alone (quantize once, then the GEMM
+    launch on pre-quantized activations) at the fused gate/up shape of the
+    model (N = 2*5632, K = 2048) with k_rows verify rows, rotating through
+    enough weight copies to exceed L2, CUDA events on the launching stream."""
+    from rai_b200 import native
+    L = native.lib()
+    dev = torch.device("cuda")
+    N, K, gs = 2 * 5632, 2048, 128
+    nbytes = L.rai_gpu_w4a8_packed_bytes(N, K, gs)
+    copies = max(2, int(np.ceil(3 * 126e6 / nbytes)))
+    rng = np.random.default_rng(0)
+    nib = torch.from_numpy(rng.integers(0, 256, N * K // 2, dtype=np.uint8)).to(dev)
+    sc = rng.uniform(0.001, 0.02, size=(N, K // gs)).astype(np.float16)
+    par = torch.from_numpy(np.stack([sc, (-8 * sc.astype(np.float32)).astype(np.float16)], -1)
+                           .astype("<f2").view(np.uint8).reshape(-1).copy()).to(dev)
+    s = torch.cuda.current_stream().cuda_stream
+    packs = []
+    for _ in range(copies):
+        p = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+        native.check(L.rai_gpu_w4a8_pack(nib.data_ptr(), par.data_ptr(), N, K, gs, p.data_ptr(), s))
+        packs.append(p)
+    x = torch.randn(k_rows, K, device=dev)
+    sb = L.rai_gpu_w4a8_scratch_bytes(k_rows, K, gs)
+    scratch = torch.empty(sb, dtype=torch.uint8, device=dev)
+    out = torch.empty(k_rows, N, device=dev)
+    native.check(L.rai_gpu_w4a8_quantize(x.data_ptr(), K, k_rows, gs, scratch.data_ptr(), sb, s))
+    for i in range(5):
+        native.check(L.rai_gpu_w4a8_matmul_prequant(out.data_ptr(), packs[i % copies].data_ptr(),
+                                                    scratch.data_ptr(), N, K, k_rows, gs, s))
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(iters):
+        native.check(L.rai_gpu_w4a8_matmul_prequant(out.data_ptr(), packs[i % copies].data_ptr(),
+                                                    scratch.data_ptr(), N, K, k_rows, gs, s))
+    e1.record()
+    torch.cuda.synchronize()
+    us = e0.elapsed_time(e1) * 1e3 / iters
+    alg = N * K // 2 + N * (K // gs) * 4  # gemm_bench.rs:73-76 accounting
+    return {"kernel": "gemm_exact_kernel<4,2> (W4A8 verify GEMM, gate/up 11264x2048, M=%d)" % k_rows,
+            "us_per_launch": us, "alg_bytes": alg, "gbs": alg / us / 1e3}
+
+
+def cpu_baseline_run(steps: int, warmup: int, threads: int | None = None):
+    """The oracle port of the reference's AVX2 path on the host cores: one
+    stream of the same workload, prefill, `warmup` untimed steps, then
+    `steps` timed lookup steps. Returns (tok/s, produced, seconds, sample)."""
+    from oracle import oracle as O
+    O.build()
+    path = model_path(0, 1)
+    m = O.Model.load(path)
+    vocab = m.config["vocab"]
+    prompt = make_prompt(1000, PROMPT, vocab, COPY_FRAC)
+    d = O.Decoder(m, PROMPT + (steps + warmup + 2) * (K_DRAFT + 1) + 16)
+    pos = d.prefill(prompt)
+    ctx = list(prompt)
+    for _ in range(warmup):
+        t, _m = d.step(pos, ctx, K_DRAFT)
+        ctx += t
+        pos += len(t)
+    produced = 0
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        t, _m = d.step(pos, ctx, K_DRAFT)
+        ctx += t
+        pos += len(t)
+        produced += len(t)
+    dt = time.perf_counter() - t0
+    sample = f"1 stream of {MODEL}, {PROMPT}-token prompt, {steps} timed lookup steps (k={K_DRAFT})"
+    return produced / dt, produced, dt, sample
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    from oracle import oracle as O
+    O.build()
+    tps, produced, dt, sample = cpu_baseline_run(args.steps, args.warmup)
+    cores = O.num_threads()
+    line = {
+        "impl": "reference", "metric": METRIC, "value": tps, "unit": "tok/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt * 1e3 / args.steps,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "int8xu4->int32->f32",
+        "data": "synthetic",
+        "config": {"workload": f"{MODEL} prompt-lookup k={K_DRAFT}, {PROMPT}-token prompts, 40% copied spans",
+                   "streams": 1, "sample": sample},
+        "cpu_baseline": {"value": tps, "unit": "tok/s", "cores": cores, "kind": "port", "sample": sample},
+        "e2e": {"value": tps, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=8)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--streams", type=int, default=STREAMS)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        return run_reference(args)
+
+    import torch
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600))
+
+    def barrier():
+        if dist:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    import rai_b200
+    from rai_b200 import convert
+    from rai_b200 import native
+    import ctypes as C
+
+    path = model_path(rank, world)
+    if dist:
+        dist.barrier()
+    model = rai_b200.RaiModel.load(path, device=local)
+    vocab = model.config["vocab_size"]
+    mine = [s for s in range(args.streams) if s % world == rank]
+    max_ctx = PROMPT + (args.steps + args.warmup + 2) * (K_DRAFT + 1) + 16
+    decs, ctxs, poss = [], [], []
+    for s in mine:
+        d = rai_b200.LookupDecoder(model, max_ctx)
+        prompt = make_prompt(1000 + s, PROMPT, vocab, COPY_FRAC)
+        poss.append(d.prefill(prompt))
+        ctxs.append(list(prompt))
+        decs.append(d)
+    cfg = rai_b200.LookupConfig(max_draft=K_DRAFT, max_ngram=3, min_ngram=1)
+
+    def one_step():
+        dev_us, host_s, produced, drafted, accepted, h2d = 0.0, 0.0, 0, 0, 0, 0
+        for i, d in enumerate(decs):
+            t0 = time.perf_counter()
+            toks, met = d.step(poss[i], ctxs[i], cfg)
+            host_s += time.perf_counter() - t0
+            h2d += 4 * len(ctxs[i]) + 8
+            dev_us += d.last_step_us()
+            ctxs[i] += toks
+            poss[i] += len(toks)
+            produced += met.produced
+            drafted += met.drafted
+            accepted += met.accepted
+        return dev_us, host_s, produced, drafted, accepted, h2d
+
+    for _ in range(args.warmup):
+        one_step()
+    barrier()
+    tot = np.zeros(6)
+    with ClockSampler(local) as clk:
+        barrier()
+        for _ in range(args.steps):
+            tot += np.array(one_step())
+        barrier()
+    dev_s = tot[0] / 1e6
+    stats = torch.tensor([dev_s, tot[1], tot[2], tot[3], tot[4], tot[5]], dtype=torch.float64, device="cuda")
+    if dist:
+        t_max = stats[:2].clone()
+        dist.all_reduce(t_max, op=dist.ReduceOp.MAX)
+        sums = stats[2:].clone()
+        dist.all_reduce(sums, op=dist.ReduceOp.SUM)
+        stats = torch.cat([t_max, sums])
+    dev_s, host_s, produced, drafted, accepted, h2d = [float(v) for v in stats.cpu()]
+    nk = C.c_size_t()
+    native.check(native.lib().rai_gpu_step_kernel_count(decs[0]._h, C.byref(nk)))
+    launches = int(nk.value) * len(mine) * args.steps
+
+    if rank == 0:
+        peak, peak_kind = peaks()
+        gem = measure_gemm_roofline(torch, K_DRAFT + 1)
+        traffic = gemm_traffic_from_profile()
+        value = produced / dev_s
+        e2e = produced / host_s
+        total_streams = args.streams
+        steps_per_stream = args.steps
+        line = {
+            "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": dev_s * 1e3 / args.steps, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "int8xu4->int32->f32", "data": "synthetic",
+            "config": {"workload": f"{MODEL} prompt-lookup k={K_DRAFT}: {total_streams} streams, "
+                                   f"{PROMPT}-token prompts (40% copied spans), greedy",
+                       "streams": total_streams, "k": K_DRAFT, "parallelism": f"dp{world} (streams sharded)",
+                       "l2": "weights 550 MB > L2 126 MB; no flush needed"},
+            "per_stream_tok_s": produced / dev_s / total_streams,
+            "verify_step_us": dev_s * 1e6 / (total_streams * steps_per_stream) * world,
+            "tokens_per_step": produced / (total_streams * steps_per_stream),
+            "accept_rate": accepted / drafted if drafted else 0.0,
+            "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": int(h2d / args.steps),
+                    "d2h_bytes_per_step": int(564 * total_streams)},
+            "gpu_launches": launches * world,
+            "roofline": {"bound": "hbm", "achieved": gem["gbs"], "peak": peak, "unit": "GB/s",
+                         "frac": gem["gbs"] / peak, "traffic": traffic, "kernel": gem["kernel"],
+                         "us_per_launch": gem["us_per_launch"], "peak_kind": peak_kind},
+            "clocks": clk.summary(),
+        }
+        if not args.no_cpu_baseline and world == 1:
+            tps, prod, dt, sample = cpu_baseline_run(steps=8, warmup=1)
+            from oracle import oracle as O
+            line["cpu_baseline"] = {"value": tps, "unit": "tok/s", "cores": O.num_threads(), "kind": "port",
+                                    "sample": sample}
+        print(json.dumps(line), flush=True)
+    for d in decs:
+        d.close()
+    model.close()
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

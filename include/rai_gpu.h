@@ -147,6 +147,35 @@ RAI_API int rai_gpu_w4a8_matmul(float* out, const void* packed, const float* inp
                         size_t cols, size_t tokens, size_t group_size, void* scratch,
                         size_t scratch_bytes, void* stream);
 
+/* The two launches of rai_gpu_w4a8_matmul separately: quantize `input`
+ * (tokens x cols f32) into `scratch`, then the GEMM kernel alone on an
+ * already-quantized scratch (e.g. to time it). */
+RAI_API int rai_gpu_w4a8_quantize(const float* input, size_t cols, size_t tokens, size_t group_size,
+                                  void* scratch, size_t scratch_bytes, void* stream);
+RAI_API int rai_gpu_w4a8_matmul_prequant(float* out, const void* packed, const void* scratch, size_t rows,
+                                         size_t cols, size_t tokens, size_t group_size, void* stream);
+
+/* Number of kernels one rai_gpu_step replays (the captured CUDA graph's
+ * kernel nodes for the decoder's current configuration; 0 before the first
+ * step). */
+RAI_API int rai_gpu_step_kernel_count(const rai_dec* dec, size_t* kernels);
+
+/* ---- host-side .raimodel writer utilities (no device needed) ----
+ *
+ * The RTN quantizer of `rai convert` (quantize_row,
+ * rai-infer/src/convert.rs:2551-2639), multi-threaded: per (row, group) f64
+ * min/max, scale = max((max-min)/(2^bits-1), 2^-24) rounded to f16, zero =
+ * f16(min), code = clamp(round_half_even((w-zero)/scale)). 4-bit codes are
+ * packed low nibble = even column. */
+RAI_API int rai_rtn_quantize(const float* w, size_t rows, size_t cols, int bits, size_t group_size,
+                             uint8_t* params, uint8_t* codes, int threads);
+/* n seeded N(0, stddev) values rounded through f16 (the checkpoint cast of
+ * rai-infer/src/safetensors.rs:457-477); deterministic per (seed, stream). */
+RAI_API int rai_synth_normal_f16(uint64_t seed, uint64_t stream, size_t n, float stddev, float* out,
+                                 int threads);
+/* binary64 -> binary16 with round-to-nearest-even. */
+RAI_API int rai_f64_to_f16(const double* in, size_t n, uint16_t* out);
+
 #ifdef __cplusplus
 }
 #endif

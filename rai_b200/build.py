@@ -17,7 +17,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(HERE)
 CSRC = os.path.join(HERE, "csrc")
 LIB = os.path.join(HERE, "librai_gpu.so")
-SOURCES = ["kernels_gemm.cu", "kernels_layers.cu", "runtime.cu"]
+SOURCES = ["kernels_gemm.cu", "kernels_layers.cu", "runtime.cu", "convert_host.cpp"]
 HEADERS = ["common.cuh", "kernels.h", "layers.h", "raimodel_format.h"]
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 FLAGS = [
@@ -41,7 +41,27 @@ def _digest() -> str:
     return h.hexdigest()
 
 
+EXPF_TABLE = os.path.join(HERE, "expf_exceptions.bin")
+
+
+def build_expf_table(force: bool = False) -> str:
+    """Tabulate where the host libm expf differs from correctly rounded exp
+    (csrc/gen_expf_table.c); the library loads the table at model load."""
+    if os.path.exists(EXPF_TABLE) and not force:
+        return EXPF_TABLE
+    bdir = os.path.join(HERE, "_build")
+    os.makedirs(bdir, exist_ok=True)
+    exe = os.path.join(bdir, "gen_expf_table")
+    subprocess.run(["gcc", "-O2", "-fopenmp", os.path.join(CSRC, "gen_expf_table.c"), "-o", exe, "-lm"],
+                   check=True)
+    tmp = EXPF_TABLE + ".tmp"
+    subprocess.run([exe, tmp], check=True, stdout=subprocess.DEVNULL)
+    os.replace(tmp, EXPF_TABLE)
+    return EXPF_TABLE
+
+
 def build(force: bool = False, verbose: bool = False) -> str:
+    build_expf_table()
     stamp = LIB + ".sha256"
     digest = _digest()
     if not force and os.path.exists(LIB) and os.path.exists(stamp):
@@ -52,7 +72,7 @@ def build(force: bool = False, verbose: bool = False) -> str:
     bdir = os.path.join(HERE, "_build")
     os.makedirs(bdir, exist_ok=True)
     for src in SOURCES:
-        obj = os.path.join(bdir, src.replace(".cu", ".o"))
+        obj = os.path.join(bdir, os.path.splitext(src)[0] + ".o")
         cmd = [NVCC, *FLAGS, "-c", os.path.join(CSRC, src), "-o", obj]
         if verbose:
             print(" ".join(cmd), file=sys.stderr)

@@ -155,9 +155,24 @@ def quantize_rtn(w: np.ndarray, bits: int, group_size: int) -> tuple[bytes, byte
     return params.astype("<f2").tobytes(), code_bytes
 
 
-def linear_section(w: np.ndarray, group_size: int) -> bytes:
+def quantize_rtn_native(w: np.ndarray, bits: int, group_size: int) -> tuple[bytes, bytes]:
+    """quantize_rtn through the multi-threaded C++ restatement in
+    librai_gpu.so (byte-identical; no device needed)."""
+    import ctypes as C
+    from . import native
+    w = np.ascontiguousarray(w, np.float32)
     rows, cols = w.shape
-    params, codes = quantize_rtn(w, 4, group_size)
+    ng = -(-cols // group_size)
+    params = np.empty(rows * ng * 4, np.uint8)
+    codes = np.empty(rows * (cols // 2 if bits == 4 else cols), np.uint8)
+    native.check(native.lib().rai_rtn_quantize(w.ctypes.data_as(C.c_void_p), rows, cols, bits, group_size,
+                                               params.ctypes.data_as(C.c_void_p), codes.ctypes.data_as(C.c_void_p), 0))
+    return params.tobytes(), codes.tobytes()
+
+
+def linear_section(w: np.ndarray, group_size: int, quantize=quantize_rtn) -> bytes:
+    rows, cols = w.shape
+    params, codes = quantize(w, 4, group_size)
     return struct.pack("<II", rows, cols) + params + codes
 
 
@@ -204,6 +219,25 @@ class _Rng:
         return f16_round(self.g.standard_normal(size=shape, dtype=np.float32) * np.float32(std))
 
 
+class _NativeRng:
+    """The C++ seeded N(0, std) source (rai_synth_normal_f16): one stream per
+    tensor, so tensors can be drawn in any order and thread count."""
+
+    def __init__(self, seed: int):
+        self.seed = seed
+        self.stream = 0
+
+    def normal(self, shape, std=0.02) -> np.ndarray:
+        import ctypes as C
+        from . import native
+        n = int(np.prod(shape))
+        out = np.empty(n, np.float32)
+        native.check(native.lib().rai_synth_normal_f16(self.seed, self.stream, n, std,
+                                                       out.ctypes.data_as(C.c_void_p), 0))
+        self.stream += 1
+        return out.reshape(shape)
+
+
 def write_model(path: str, s: Shape, sections: Iterable[bytes]) -> int:
     """Write header + section table + sections; returns the file size."""
     secs = list(sections)
@@ -225,11 +259,14 @@ def write_model(path: str, s: Shape, sections: Iterable[bytes]) -> int:
     return off
 
 
-def synthetic_sections(s: Shape, seed: int, progress: Callable[[str], None] | None = None):
-    """Yield the sections of a seeded random model of shape `s`."""
-    rng = _Rng(seed)
+def synthetic_sections(s: Shape, seed: int, progress: Callable[[str], None] | None = None,
+                       fast: bool = False):
+    """Yield the sections of a seeded random model of shape `s`. `fast` uses
+    the C++ weight source and quantizer (same format, different draws)."""
+    rng = _NativeRng(seed) if fast else _Rng(seed)
+    q = quantize_rtn_native if fast else quantize_rtn
     emb = rng.normal((s.vocab, s.hidden))
-    ep, ec = quantize_rtn(emb, 8, s.embed_group_size)
+    ep, ec = q(emb, 8, s.embed_group_size)
     yield ep + ec
     dims = s.projection_dims()
     for li in range(s.layers):
@@ -237,7 +274,7 @@ def synthetic_sections(s: Shape, seed: int, progress: Callable[[str], None] | No
             progress(f"layer {li}")
         sec = bytearray()
         for (r, c) in dims:
-            sec += linear_section(rng.normal((r, c)), s.group_size)
+            sec += linear_section(rng.normal((r, c)), s.group_size, q)
         if s.bias_mask:
             for p in range(7):
                 if s.bias_mask & (1 << p):
@@ -249,20 +286,20 @@ def synthetic_sections(s: Shape, seed: int, progress: Callable[[str], None] | No
             sec += f32_bytes(rng.normal((s.num_experts, s.hidden)))
             for _ in range(1, s.num_experts):
                 for (r, c) in dims[4:]:
-                    sec += linear_section(rng.normal((r, c)), s.group_size)
+                    sec += linear_section(rng.normal((r, c)), s.group_size, q)
         sec += f32_bytes(np.ones(s.hidden, np.float32))
         sec += f32_bytes(np.ones(s.hidden, np.float32))
         yield bytes(sec)
     yield f32_bytes(np.ones(s.hidden, np.float32))
     if not s.tied:
-        yield linear_section(rng.normal((s.vocab, s.hidden)), s.group_size)
+        yield linear_section(rng.normal((s.vocab, s.hidden)), s.group_size, q)
 
 
-def write_synthetic(path: str, s: Shape | str, seed: int = 0, progress=None) -> int:
+def write_synthetic(path: str, s: Shape | str, seed: int = 0, progress=None, fast: bool = False) -> int:
     """Write a seeded synthetic .raimodel of the given shape (or preset name)."""
     if isinstance(s, str):
         s = PRESETS[s]
-    return write_model(path, s, synthetic_sections(s, seed, progress))
+    return write_model(path, s, synthetic_sections(s, seed, progress, fast))
 
 
 def weight_bytes_per_step(s: Shape) -> int:

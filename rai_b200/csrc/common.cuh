@@ -108,9 +108,27 @@ __device__ __forceinline__ float schraudolph(float x) {
   return __int_as_float(__float2int_rn(t));
 }
 
-// Rust f32::exp resolves to glibc expf, which is correctly rounded for all
-// but a tiny fraction of inputs; evaluating exp in double and rounding once
-// reproduces it there (the exceptions are covered by the logit tolerance).
-__device__ __forceinline__ float expf_ref(float x) { return (float)exp((double)x); }
+// Rust f32::exp resolves to the host libm's expf. The device evaluates exp in
+// double and rounds once (correctly rounded), then patches the inputs where
+// the host expf rounds differently, from a table generated at build time by
+// running that expf over every binary32 input (csrc/gen_expf_table.c).
+struct ExpfTable {
+  const uint32_t* keys = nullptr;  // sorted input bit patterns
+  const uint32_t* vals = nullptr;  // host expf result bits
+  int n = 0;
+};
+
+__device__ __forceinline__ float expf_host(float x, const ExpfTable& t) {
+  float r = (float)exp((double)x);
+  uint32_t k = __float_as_uint(x);
+  int lo = 0, hi = t.n - 1;
+  while (lo <= hi) {
+    int mid = (lo + hi) >> 1;
+    uint32_t v = t.keys[mid];
+    if (v == k) return __uint_as_float(t.vals[mid]);
+    if (v < k) lo = mid + 1; else hi = mid - 1;
+  }
+  return r;
+}
 
 }  // namespace rai

@@ -182,7 +182,7 @@ __global__ void __launch_bounds__(256) attention_kernel(const float* __restrict_
                                                         const float* __restrict__ kc, const float* __restrict__ vc,
                                                         int nh, int nkv, int max_ctx, const int* pos_dev, int pos0,
                                                         const int* m_dev, int M, float scale, float softcap,
-                                                        int n_alloc) {
+                                                        int n_alloc, ExpfTable et) {
   constexpr int VT = 32;  // positions per V tile
   extern __shared__ __align__(16) float sm[];
   const int hpk = nh / nkv;
@@ -249,7 +249,7 @@ __global__ void __launch_bounds__(256) attention_kernel(const float* __restrict_
     int h = idx / n, t = idx % n;
     float* p = sc + (size_t)h * n_alloc + t;
     float x = __fsub_rn(*p, s_max[h]);
-    *p = t < n8 ? schraudolph(x) : expf_ref(x);
+    *p = t < n8 ? schraudolph(x) : expf_host(x, et);
   }
   __syncthreads();
   if (tid < hpk * 8) {
@@ -328,7 +328,7 @@ __global__ void __launch_bounds__(256) attention_kernel(const float* __restrict_
 // ---------------------------------------------------------------------------
 // act[b][i] = silu(gate) * up with gate/up rows [gate | up] of width 2*ff.
 __global__ void swiglu_kernel(const float* __restrict__ gu, int ff, float* __restrict__ act,
-                              const int* m_dev, int M) {
+                              const int* m_dev, int M, ExpfTable et) {
   int b = blockIdx.y;
   int mact = m_dev ? *m_dev : M;
   if (b >= mact) return;
@@ -340,7 +340,7 @@ __global__ void swiglu_kernel(const float* __restrict__ gu, int ff, float* __res
     float e = schraudolph(__fmul_rn(x, -1.0f));
     s = __fdiv_rn(x, __fadd_rn(1.0f, e));
   } else {
-    s = __fdiv_rn(x, __fadd_rn(1.0f, expf_ref(-x)));
+    s = __fdiv_rn(x, __fadd_rn(1.0f, expf_host(-x, et)));
   }
   act[(size_t)b * ff + i] = __fmul_rn(s, u);
 }
@@ -469,21 +469,23 @@ cudaError_t launch_qkv_post(float* qkv, int ld, float* q_out, int nh, int nkv, i
   return cudaGetLastError();
 }
 
+// n_alloc must be a multiple of 4 so the V tile behind the scores is 16-byte
+// aligned for cp.async.
 size_t attention_smem_bytes(int hd, int hpk, int n_alloc) {
   return ((size_t)hpk * hd + (size_t)hpk * n_alloc + 2 * 32 * (size_t)hd) * sizeof(float);
 }
 
 cudaError_t launch_attention(const float* q, float* out, const float* kc, const float* vc, int nh, int nkv,
                              int hd, int max_ctx, const int* pos_dev, int pos0, const int* m_dev, int M,
-                             float scale, float softcap, int n_alloc, cudaStream_t s) {
+                             float scale, float softcap, int n_alloc, const ExpfTable& et, cudaStream_t s) {
   int hpk = nh / nkv;
   size_t smem = attention_smem_bytes(hd, hpk, n_alloc);
   dim3 grid(nkv, M);
-  cudaError_t e = cudaSuccess;
+  if (smem > kAttnMaxSmem) return cudaErrorInvalidValue;
 #define RAI_ATTN(HDV)                                                                                  \
   case HDV:                                                                                            \
     attention_kernel<HDV><<<grid, 256, smem, s>>>(q, out, kc, vc, nh, nkv, max_ctx, pos_dev, pos0,     \
-                                                  m_dev, M, scale, softcap, n_alloc);                  \
+                                                  m_dev, M, scale, softcap, n_alloc, et);              \
     break;
   switch (hd) {
     RAI_ATTN(16)
@@ -498,7 +500,7 @@ cudaError_t launch_attention(const float* q, float* out, const float* kc, const 
 }
 
 cudaError_t init_layer_attributes() {
-  const int bytes = 227 * 1024;
+  const int bytes = (int)kAttnMaxSmem;
   cudaError_t e = cudaFuncSetAttribute(attention_kernel<16>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
   if (e == cudaSuccess) e = cudaFuncSetAttribute(attention_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
   if (e == cudaSuccess) e = cudaFuncSetAttribute(attention_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
@@ -506,9 +508,10 @@ cudaError_t init_layer_attributes() {
   return e;
 }
 
-cudaError_t launch_swiglu(const float* gu, int ff, float* act, const int* m_dev, int M, cudaStream_t s) {
+cudaError_t launch_swiglu(const float* gu, int ff, float* act, const int* m_dev, int M, const ExpfTable& et,
+                          cudaStream_t s) {
   dim3 grid((ff + 255) / 256, M);
-  swiglu_kernel<<<grid, 256, 0, s>>>(gu, ff, act, m_dev, M);
+  swiglu_kernel<<<grid, 256, 0, s>>>(gu, ff, act, m_dev, M, et);
   return cudaGetLastError();
 }
 

@@ -3,6 +3,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include "common.cuh"
+
 namespace rai {
 
 constexpr int kMaxRows = 33;  // max_draft <= 32 (rai run's --lookup-k limit) + 1
@@ -24,6 +26,10 @@ struct StepState {
   unsigned long long amax[kMaxRows];
 };
 
+// Dynamic shared memory the attention kernel may use (the opt-in limit of
+// 227 KB less its static shared memory and a margin).
+constexpr size_t kAttnMaxSmem = 224 * 1024;
+
 // Raise the dynamic shared-memory limit of the attention kernels (once per
 // process, before any stream capture).
 cudaError_t init_layer_attributes();
@@ -40,8 +46,9 @@ cudaError_t launch_qkv_post(float* qkv, int ld, float* q_out, int nh, int nkv, i
 size_t attention_smem_bytes(int hd, int hpk, int n_alloc);
 cudaError_t launch_attention(const float* q, float* out, const float* kc, const float* vc, int nh, int nkv,
                              int hd, int max_ctx, const int* pos_dev, int pos0, const int* m_dev, int M,
-                             float scale, float softcap, int n_alloc, cudaStream_t s);
-cudaError_t launch_swiglu(const float* gu, int ff, float* act, const int* m_dev, int M, cudaStream_t s);
+                             float scale, float softcap, int n_alloc, const ExpfTable& et, cudaStream_t s);
+cudaError_t launch_swiglu(const float* gu, int ff, float* act, const int* m_dev, int M, const ExpfTable& et,
+                          cudaStream_t s);
 cudaError_t launch_argmax(const float* logits, int vocab, const int* m_dev, int M, unsigned long long* best,
                           cudaStream_t s);
 cudaError_t launch_ngram(const uint32_t* ctx, StepState* st, int max_draft, int max_ngram, int min_ngram,

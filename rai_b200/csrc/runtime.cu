@@ -8,8 +8,10 @@
 // greedy acceptance and rolls the KV watermark back. The host copies the
 // context in, replays one CUDA graph and reads one small struct back.
 #include <cuda_runtime.h>
+#include <dlfcn.h>
 
 #include <algorithm>
+#include <fstream>
 #include <cmath>
 #include <cstdio>
 #include <cstring>
@@ -33,12 +35,16 @@ int fail(int code, const std::string& msg) {
   return code;
 }
 
+// On failure the runtime's (non-sticky) last-error slot is cleared so the
+// next launch check does not report this error again.
 #define RAI_CUDA(call)                                                                        \
   do {                                                                                        \
     cudaError_t e_ = (call);                                                                  \
-    if (e_ != cudaSuccess)                                                                    \
+    if (e_ != cudaSuccess) {                                                                  \
+      (void)cudaGetLastError();                                                               \
       return fail(e_ == cudaErrorMemoryAllocation ? RAI_ERR_OOM : RAI_ERR_DEVICE,             \
                   std::string(#call) + ": " + cudaGetErrorString(e_));                        \
+    }                                                                                         \
   } while (0)
 
 using raimodel::Config;
@@ -111,6 +117,7 @@ struct rai_model {
   int qk_mode = 0;  // 0 none, 1 per head, 2 full width
   size_t device_bytes = 0;
   uint32_t* err_dev = nullptr;
+  rai::ExpfTable expf;
 
   template <class T>
   int alloc(T** p, size_t bytes) {
@@ -135,6 +142,7 @@ struct rai_model {
 struct rai_dec {
   rai_model* m = nullptr;
   int max_ctx = 0;
+  int n_alloc = 0;  // attention score row stride: max_ctx rounded up to 4
   int mcap = 0;  // rows the scratch buffers hold
   cudaStream_t stream = nullptr;
   std::vector<void*> allocs;
@@ -151,6 +159,7 @@ struct rai_dec {
   rai::StepState* st_dev = nullptr;
   rai::StepState* st_host = nullptr;
   cudaGraphExec_t graph = nullptr;
+  size_t graph_kernels = 0;
   uint32_t graph_key[3] = {0, 0, 0};
   cudaEvent_t ev0 = nullptr, ev1 = nullptr;
   float last_us = 0.f;
@@ -253,6 +262,38 @@ int pack_concat(rai_model* M, const uint8_t* blob_dev, const std::vector<const r
   return RAI_OK;
 }
 
+// The host-libm expf exception table written next to the library at build
+// time (RAI_EXPF_TABLE overrides the path).
+std::string lib_dir() {
+  Dl_info info;
+  if (dladdr(reinterpret_cast<void*>(&lib_dir), &info) && info.dli_fname) {
+    std::string p = info.dli_fname;
+    size_t k = p.rfind('/');
+    return k == std::string::npos ? std::string(".") : p.substr(0, k);
+  }
+  return ".";
+}
+
+int load_expf_table(rai_model* M) {
+  const char* env = std::getenv("RAI_EXPF_TABLE");
+  std::string path = env ? std::string(env) : lib_dir() + "/expf_exceptions.bin";
+  std::ifstream f(path, std::ios::binary);
+  if (!f) return fail(RAI_ERR_INVALID, "missing " + path + " (run rai_b200.build)");
+  uint32_t hdr[2] = {0, 0};
+  f.read(reinterpret_cast<char*>(hdr), 8);
+  if (!f || hdr[0] != 0x46505845u) return fail(RAI_ERR_INVALID, "bad expf table " + path);
+  std::vector<uint32_t> kv(2 * (size_t)hdr[1]);
+  f.read(reinterpret_cast<char*>(kv.data()), kv.size() * 4);
+  if (!f) return fail(RAI_ERR_INVALID, "truncated expf table " + path);
+  uint32_t* dev = nullptr;
+  if (int rc = M->alloc(&dev, kv.size() * 4)) return rc;
+  RAI_CUDA(cudaMemcpy(dev, kv.data(), kv.size() * 4, cudaMemcpyHostToDevice));
+  M->expf.keys = dev;
+  M->expf.vals = dev + hdr[1];
+  M->expf.n = (int)hdr[1];
+  return RAI_OK;
+}
+
 int check_supported(const Config& c, const raimodel::Model& L) {
   if (c.group_size != 64 && c.group_size != 128)
     return fail(RAI_ERR_UNSUPPORTED, "group_size " + std::to_string(c.group_size) + " (this build runs 64 or 128)");
@@ -301,7 +342,7 @@ int forward(rai_dec* d, int M, const int* m_dev, const int* pos_dev, int pos0, c
     RAI_CUDA(rai::launch_qkv_post(d->qkv, qd + 2 * kvd, d->q, nh, nkv, hd, L.q_norm, L.k_norm, Mo->qk_mode, eps,
                                   Mo->rope_cos, Mo->rope_sin, kc, vc, d->max_ctx, pos_dev, pos0, m_dev, M, s));
     RAI_CUDA(rai::launch_attention(d->q, d->attn, kc, vc, nh, nkv, hd, d->max_ctx, pos_dev, pos0, m_dev, M,
-                                   Mo->scale, c.attn_logit_softcap, d->max_ctx, s));
+                                   Mo->scale, c.attn_logit_softcap, d->n_alloc, Mo->expf, s));
     RAI_CUDA(rai::quantize_act(d->attn, qd, M, m_dev, qd, gs, 4, d->act_q, s));
     rai::GemmEpilogue e_res;
     e_res.mode = rai::kEpiResidual;
@@ -310,7 +351,7 @@ int forward(rai_dec* d, int M, const int* m_dev, const int* pos_dev, int pos0, c
     RAI_CUDA(rai::launch_rmsnorm(d->hidden, L.post_norm, h, eps, d->normed, d->resid, m_dev, M, s));
     RAI_CUDA(rai::quantize_act(d->normed, h, M, m_dev, h, gs, 4, d->act_h, s));
     RAI_CUDA(rai::gemm_exact(L.gateup, d->act_h, M, d->gu, 2 * ffd, rai::GemmEpilogue{}, err, s));
-    RAI_CUDA(rai::launch_swiglu(d->gu, ffd, d->ff, m_dev, M, s));
+    RAI_CUDA(rai::launch_swiglu(d->gu, ffd, d->ff, m_dev, M, Mo->expf, s));
     RAI_CUDA(rai::quantize_act(d->ff, ffd, M, m_dev, ffd, gs, 4, d->act_ff, s));
     RAI_CUDA(rai::gemm_exact(L.down, d->act_ff, M, d->hidden, h, e_res, err, s));
   }
@@ -389,6 +430,15 @@ int ensure_graph(rai_dec* d, const rai_lookup_cfg* cfg) {
     return rc;
   }
   if (ce != cudaSuccess) return fail(RAI_ERR_DEVICE, std::string("graph capture: ") + cudaGetErrorString(ce));
+  size_t nnodes = 0;
+  cudaGraphGetNodes(g, nullptr, &nnodes);
+  std::vector<cudaGraphNode_t> nodes(nnodes);
+  cudaGraphGetNodes(g, nodes.data(), &nnodes);
+  d->graph_kernels = 0;
+  for (auto nd : nodes) {
+    cudaGraphNodeType ty;
+    if (cudaGraphNodeGetType(nd, &ty) == cudaSuccess && ty == cudaGraphNodeTypeKernel) ++d->graph_kernels;
+  }
   cudaError_t ie = cudaGraphInstantiate(&d->graph, g, 0);
   cudaGraphDestroy(g);
   if (ie != cudaSuccess) return fail(RAI_ERR_DEVICE, std::string("graph instantiate: ") + cudaGetErrorString(ie));
@@ -440,6 +490,7 @@ int rai_gpu_model_create(const uint8_t* blob, size_t len, int device, rai_model*
   M->qk_mode = c.has_full_qk_norm ? 2 : (c.has_qk_norm ? 1 : 0);
   if (int rc = M->alloc(&M->err_dev, 4)) return rc;
   RAI_CUDA(cudaMemset(M->err_dev, 0, 4));
+  if (int rc = load_expf_table(M.get())) return rc;
 
   // Upload the blob once; pack from the device copy, then release it.
   uint8_t* blob_dev = nullptr;
@@ -538,6 +589,7 @@ int rai_gpu_decoder_create(rai_model* m, size_t max_ctx, rai_dec** out) {
   auto d = std::make_unique<rai_dec>();
   d->m = m;
   d->max_ctx = (int)ctx;
+  d->n_alloc = (int)rai::round_up(ctx, 4);
   d->mcap = (int)std::max<size_t>(rai::kMaxRows, std::min<size_t>(256, ctx));
   RAI_CUDA(cudaStreamCreateWithFlags(&d->stream, cudaStreamNonBlocking));
   RAI_CUDA(cudaEventCreate(&d->ev0));
@@ -571,8 +623,8 @@ int rai_gpu_decoder_create(rai_model* m, size_t max_ctx, rai_dec** out) {
   RAI_CUDA(cudaMemset(d->st_dev, 0, sizeof(rai::StepState)));
   RAI_CUDA(cudaMallocHost(&d->ctx_host, ctx * 4));
   RAI_CUDA(cudaMallocHost(&d->st_host, sizeof(rai::StepState)));
-  size_t attn_smem = rai::attention_smem_bytes(c.head_dim, c.num_heads / c.num_kv_heads, (int)ctx);
-  if (attn_smem > 227 * 1024)
+  size_t attn_smem = rai::attention_smem_bytes(c.head_dim, c.num_heads / c.num_kv_heads, d->n_alloc);
+  if (attn_smem > rai::kAttnMaxSmem)
     return fail(RAI_ERR_UNSUPPORTED, "context window too long for the single-pass attention kernel");
   *out = d.release();
   return RAI_OK;
@@ -709,6 +761,12 @@ int rai_gpu_kv_read(const rai_dec* d, size_t layer, size_t kvh, size_t pos, floa
   return RAI_OK;
 }
 
+int rai_gpu_step_kernel_count(const rai_dec* d, size_t* kernels) {
+  if (!d || !kernels) return fail(RAI_ERR_INVALID, "null argument");
+  *kernels = d->graph ? d->graph_kernels : 0;
+  return RAI_OK;
+}
+
 int rai_gpu_last_step_us(const rai_dec* d, float* us) {
   if (!d || !us) return fail(RAI_ERR_INVALID, "null argument");
   *us = d->last_us;
@@ -758,6 +816,44 @@ int rai_gpu_w4a8_matmul(float* out, const void* packed, const float* input, size
   w.tiles = (int)rai::ceil_div(rows, rai::kTileRows);
   w.wbits = 4;
   RAI_CUDA(rai::gemm_exact(w, a, (int)tokens, out, (int)rows, rai::GemmEpilogue{}, nullptr, s));
+  return RAI_OK;
+}
+
+int rai_gpu_w4a8_quantize(const float* input, size_t cols, size_t tokens, size_t gs, void* scratch,
+                          size_t scratch_bytes, void* stream) {
+  if (!input || !scratch) return fail(RAI_ERR_INVALID, "null argument");
+  if (gs != 64 && gs != 128) return fail(RAI_ERR_UNSUPPORTED, "group_size must be 64 or 128");
+  if (tokens == 0 || cols == 0 || cols % 2) return fail(RAI_ERR_INVALID, "bad dimensions");
+  if (scratch_bytes < rai_gpu_w4a8_scratch_bytes(tokens, cols, gs)) return fail(RAI_ERR_INVALID, "scratch buffer is too small");
+  ActBuf a;
+  a.data = static_cast<uint8_t*>(scratch);
+  a.tok_alloc = (int)rai::round_up(tokens, 8);
+  a.groups = (int)rai::ceil_div(cols, gs);
+  RAI_CUDA(rai::quantize_act(input, (int)cols, (int)tokens, nullptr, (int)cols, (int)gs, 4, a,
+                             static_cast<cudaStream_t>(stream)));
+  return RAI_OK;
+}
+
+int rai_gpu_w4a8_matmul_prequant(float* out, const void* packed, const void* scratch, size_t rows, size_t cols,
+                                 size_t tokens, size_t gs, void* stream) {
+  if (!out || !packed || !scratch) return fail(RAI_ERR_INVALID, "null argument");
+  if (gs != 64 && gs != 128) return fail(RAI_ERR_UNSUPPORTED, "group_size must be 64 or 128");
+  if (tokens == 0 || rows == 0 || cols == 0 || cols % 2) return fail(RAI_ERR_INVALID, "bad dimensions");
+  RAI_CUDA(rai::init_gemm_attributes());
+  ActBuf a;
+  a.data = static_cast<uint8_t*>(const_cast<void*>(scratch));
+  a.tok_alloc = (int)rai::round_up(tokens, 8);
+  a.groups = (int)rai::ceil_div(cols, gs);
+  PackedLinear w;
+  w.data = static_cast<const uint8_t*>(packed);
+  w.rows = (int)rows;
+  w.cols = (int)cols;
+  w.group_size = (int)gs;
+  w.groups = a.groups;
+  w.tiles = (int)rai::ceil_div(rows, rai::kTileRows);
+  w.wbits = 4;
+  RAI_CUDA(rai::gemm_exact(w, a, (int)tokens, out, (int)rows, rai::GemmEpilogue{}, nullptr,
+                           static_cast<cudaStream_t>(stream)));
   return RAI_OK;
 }
 

@@ -63,3 +63,28 @@ def test_weight_bytes_match_the_reference_accounting():
     # BENCHMARKS.md:99-102 quotes 549.5 MB streamed per TinyLlama token.
     mb = convert.weight_bytes_per_step(convert.PRESETS["tinyllama-1.1b"]) / 1e6
     assert abs(mb - 549.5) < 1.0
+
+
+def test_native_quantizer_is_byte_identical_to_numpy():
+    rng = np.random.default_rng(0)
+    for rows, cols, gs, bits in [(37, 256, 128, 4), (5, 192, 64, 4), (11, 96, 64, 8), (3, 130, 64, 4)]:
+        w = convert.f16_round(rng.standard_normal((rows, cols)).astype(np.float32) * np.float32(0.02))
+        w[0, :gs] = 0.0  # degenerate group: scale floors at MIN_F16_SCALE
+        w[1, 3] = 7.0    # outlier group
+        assert convert.quantize_rtn(w, bits, gs) == convert.quantize_rtn_native(w, bits, gs)
+
+
+def test_native_f64_to_f16_rounds_like_numpy():
+    import ctypes as C
+    from rai_b200 import native
+    rng = np.random.default_rng(1)
+    x = np.concatenate([
+        rng.standard_normal(200000) * 10.0 ** rng.integers(-9, 6, 200000),
+        # exact ties between neighbouring f16 values, normal and subnormal
+        (np.arange(1, 4000, dtype=np.float64) + 0.5) * 2.0 ** -24,
+        (np.arange(1024, 2048, dtype=np.float64) + 0.5) * 2.0 ** -10,
+        [0.0, -0.0, 65504.0, 65520.0, 1e9, -1e-30, np.inf, -np.inf],
+    ]).astype(np.float64)
+    out = np.zeros(x.size, np.uint16)
+    native.check(native.lib().rai_f64_to_f16(x.ctypes.data_as(C.c_void_p), x.size, out.ctypes.data_as(C.c_void_p)))
+    assert np.array_equal(out, x.astype(np.float16).view(np.uint16))

@@ -75,12 +75,41 @@ def test_lookup_steps_match_oracle(tiny_model_paths, oracle, name, k):
     for _ in range(14):
         gt, gmet = gd.step(pos, ctx, cfg)
         ot, omet = od.step(pos, ctx, k)
-        assert gt == ot, (pos, gt, ot)
+        if gt != ot:
+            _explain_divergence(tiny_model_paths[name], oracle, ctx, pos, gmet.drafted, k, gt, ot)
+            return
         assert (gmet.accepted, gmet.drafted, gmet.produced) == (omet["accepted"], omet["drafted"], omet["produced"])
         assert gmet.matched_ngram == omet["matched_ngram"]
         ctx += gt
         pos += len(gt)
         assert gd.kv_filled(0) == pos == od.kv_filled(0)
+
+
+def _explain_divergence(path, oracle, ctx, pos, drafted, k, gt, ot):
+    """A token mismatch is allowed only where the oracle's top-2 logit margin
+    is below the logit tolerance (BASELINE north_star parity rule). Replays
+    the step's verify batch on fresh decoders and checks exactly that."""
+    import rai_b200
+    n = oracle.find_ngram_draft(ctx, 1, 3, k)
+    draft = ctx[n[1]:n[1] + n[2]] if n else []
+    rows = [ctx[pos]] + draft
+    om = oracle.Model.load(path)
+    od = oracle.Decoder(om, 256)
+    od.prefill(ctx[:pos + 1])
+    want = od.forward_logits(rows, pos)
+    gm = rai_b200.RaiModel.load(path)
+    gd = rai_b200.LookupDecoder(gm, 256)
+    gd.prefill(ctx[:pos + 1])
+    got = gd.forward_logits(rows, pos)
+    tol = _tol(want)
+    assert np.max(np.abs(got - want)) <= tol, "logits differ beyond tolerance"
+    i = 0
+    while i < min(len(gt), len(ot)) and gt[i] == ot[i]:
+        i += 1
+    top2 = np.sort(want[i])[-2:]
+    margin = float(top2[1] - top2[0])
+    print(f"divergence at pos {pos} row {i}: margin {margin:.3g}, tol {tol:.3g}, max|d| {np.max(np.abs(got - want)):.3g}")
+    assert margin <= tol, f"tokens differ at row {i} with a top-2 margin {margin} above the tolerance {tol}"
 
 
 def test_no_draft_step_produces_one_token(tiny_model_paths, oracle):
