@@ -65,8 +65,10 @@ cudaError_t pack_linear8(const uint8_t* codes, const uint8_t* params, int rows, 
 cudaError_t quantize_act(const float* x, int ldx, int M, const int* m_dev, int K, int gs, int wbits,
                          ActBuf act, cudaStream_t s);
 
-// out[t * ld_out + r] (= epilogue(dot)) for t < M, r < rows.
+// out[t * ld_out + r] (= epilogue(dot)) for t < M, r < rows. With m_dev set,
+// M is the static row budget (grid size) and *m_dev the active row count.
 cudaError_t gemm_exact(const PackedLinear& w, const ActBuf& act, int M, float* out, int ld_out,
-                       const GemmEpilogue& epi, uint32_t* err, cudaStream_t s, bool pdl = false);
+                       const GemmEpilogue& epi, uint32_t* err, cudaStream_t s, bool pdl = false,
+                       const int* m_dev = nullptr);
 
 }  // namespace rai

@@ -190,6 +190,7 @@ struct GemmParams {
   const float* bias;
   const float* residual;
   uint32_t* err;
+  const int* m_dev;  // active token count (device); overrides M when set
   int rows, groups, M, tok_alloc, ld_out, mode, stages;
 };
 
@@ -214,6 +215,13 @@ __global__ void __launch_bounds__(kThreads, NTILES >= 4 ? 1 : 2) gemm_exact_kern
   const int tile = blockIdx.x;
   const int t0 = blockIdx.y * kTokChunk;
   const int G = p.groups;
+  // Token chunks beyond the active row count (produced on the device) exit
+  // before touching any barrier.
+  if (p.m_dev) {
+    const int mact = *p.m_dev;
+    if (t0 >= mact) return;
+    p.M = mact;
+  }
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
@@ -438,9 +446,10 @@ cudaError_t quantize_act(const float* x, int ldx, int M, const int* m_dev, int K
 }
 
 cudaError_t gemm_exact(const PackedLinear& w, const ActBuf& act, int M, float* out, int ld_out,
-                       const GemmEpilogue& epi, uint32_t* err, cudaStream_t s, bool pdl) {
+                       const GemmEpilogue& epi, uint32_t* err, cudaStream_t s, bool pdl, const int* m_dev) {
   if (M <= 0) return cudaSuccess;
   GemmParams gp = {};
+  gp.m_dev = m_dev;
   gp.w = w.data;
   gp.act = act.data;
   gp.out = out;

@@ -1,19 +1,20 @@
 // Per-layer and speculation kernels of the decode step (sm_100a).
 //
 // Each kernel restates one reference routine's floating-point order:
-//   embed_kernel      embed_lookup (rai-infer/src/gemm.rs:1926-1970)
-//   rmsnorm_kernel    rms_norm_avx2 / rms_norm_with_residual_avx2
-//                     (rai-infer/src/layers.rs:325-376, 433-497)
-//   qkv_post_kernel   QkNorm::apply -> rms_norm_heads (layers.rs:201-240,
-//                     308-314), RoPETable::apply_avx2 (layers.rs:689-726) and
-//                     KVCache::store (rai-infer/src/kv_cache.rs:143-172)
-//   attention_kernel  attention_head_avx2 (layers.rs:1266-1380) for every
-//                     (query row, head) of attend_batch (layers.rs:1675-1747)
-//   swiglu_kernel     silu_mul_avx2 (layers.rs:850-883)
-//   argmax_kernel     sampler::argmax (rai-infer/src/sampler.rs:201-208)
-//   ngram_kernel      find_ngram_draft (rai-infer/src/lookup.rs:131-171)
-//   accept_kernel     the greedy limit of LookupDecoder::step's acceptance
-//                     loop and KV truncate (lookup.rs:359-411)
+//   embed_kernel        embed_lookup (rai-infer/src/gemm.rs:1926-1970)
+//   rmsnorm_kernel      rms_norm_avx2 / rms_norm_with_residual_avx2
+//                       (rai-infer/src/layers.rs:325-376, 433-497)
+//   qkv_post_kernel     QkNorm::apply -> rms_norm_heads (layers.rs:201-240,
+//                       308-314), RoPETable::apply_avx2 (layers.rs:689-726),
+//                       KVCache::store (rai-infer/src/kv_cache.rs:143-172)
+//   attn_*_kernel       attention_head_avx2 (layers.rs:1266-1380) for every
+//                       (row, head) of attend_batch (layers.rs:1675-1747):
+//                       scores, then softmax, then the P.V accumulation
+//   swiglu_kernel       silu_mul_avx2 (layers.rs:850-883)
+//   argmax_kernel       sampler::argmax (rai-infer/src/sampler.rs:201-208)
+//   ngram_kernel        find_ngram_draft (rai-infer/src/lookup.rs:131-171)
+//   accept_kernel       the greedy limit of LookupDecoder::step's acceptance
+//                       loop (lookup.rs:359-411)
 #include <cuda_runtime.h>
 
 #include "common.cuh"
@@ -21,14 +22,15 @@
 
 namespace rai {
 
+__device__ __forceinline__ int active_rows(const int* m_dev, int M) { return m_dev ? *m_dev : M; }
+
 // ---------------------------------------------------------------------------
 __global__ void embed_kernel(const uint32_t* __restrict__ ids, const int* m_dev, int M,
                              const uint8_t* __restrict__ codes, const uint8_t* __restrict__ params,
                              int vocab, int hidden, int gs, float embed_scale, float* __restrict__ out,
                              uint32_t* err) {
   int b = blockIdx.x;
-  int mact = m_dev ? *m_dev : M;
-  if (b >= mact) return;
+  if (b >= active_rows(m_dev, M)) return;
   uint32_t tok = ids[b];
   if (tok >= (uint32_t)vocab) {
     if (threadIdx.x == 0) atomicOr(err, kErrBadInput);
@@ -57,8 +59,7 @@ __global__ void rmsnorm_kernel(const float* __restrict__ x, const float* __restr
   __shared__ float lanes[16];
   __shared__ float s_inv;
   int b = blockIdx.x;
-  int mact = m_dev ? *m_dev : M;
-  if (b >= mact) return;
+  if (b >= active_rows(m_dev, M)) return;
   const float* xr = x + (size_t)b * n;
   for (int i = threadIdx.x; i < n; i += blockDim.x) {
     float v = xr[i];
@@ -70,7 +71,16 @@ __global__ void rmsnorm_kernel(const float* __restrict__ x, const float* __restr
   if (threadIdx.x < 16) {
     int j = threadIdx.x & 7, half = threadIdx.x >> 3;
     float acc = 0.f;
-    for (int c = 0; c < chunks16; ++c) {
+    int c = 0;
+    // Loads are independent of the chain: fetch eight strides ahead.
+    for (; c + 8 <= chunks16; c += 8) {
+      float v[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) v[u] = sx[16 * (c + u) + 8 * half + j];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) acc = __fmaf_rn(v[u], v[u], acc);
+    }
+    for (; c < chunks16; ++c) {
       float v = sx[16 * c + 8 * half + j];
       acc = __fmaf_rn(v, v, acc);
     }
@@ -95,11 +105,11 @@ __global__ void rmsnorm_kernel(const float* __restrict__ x, const float* __restr
 }
 
 // ---------------------------------------------------------------------------
-// Sequential scalar RMS over `len` values at x (in place): rms_norm_heads.
-__device__ void rms_inplace_seq(float* x, int len, const float* w, float eps, float* inv_out) {
+// rms_norm_heads: sequential scalar sum of squares over `len` values.
+__device__ float rms_inv_seq(const float* x, int len, float eps) {
   float ss = 0.f;
   for (int i = 0; i < len; ++i) ss = __fadd_rn(ss, __fmul_rn(x[i], x[i]));
-  *inv_out = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)len), eps)));
+  return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)len), eps)));
 }
 
 // RoPE on one head (NeoX half split): FMA form for the first (half/8)*8
@@ -117,38 +127,37 @@ __device__ __forceinline__ void rope_pair(float* h, int i, int half, int chunked
 }
 
 // One CTA per active row: QK norm, RoPE on q and k, then store k, v into the
-// layer's cache at position pos + b. qkv row layout [q | k | v].
-__global__ void qkv_post_kernel(float* __restrict__ qkv, int ld, float* __restrict__ q_out, int nh,
+// row's stream cache at the row's position. qkv row layout [q | k | v].
+__global__ void qkv_post_kernel(const float* __restrict__ qkv, int ld, float* __restrict__ q_out, int nh,
                                 int nkv, int hd, const float* __restrict__ qn, const float* __restrict__ kn,
                                 int qk_mode, float eps, const float* __restrict__ rope_cos,
-                                const float* __restrict__ rope_sin, float* __restrict__ kc,
-                                float* __restrict__ vc, int max_ctx, const int* pos_dev, int pos0,
-                                const int* m_dev, int M) {
+                                const float* __restrict__ rope_sin, const StreamKV* __restrict__ kv, int layer,
+                                const RowInfo* __restrict__ rows, const int* m_dev, int M) {
   extern __shared__ float srow[];  // q | k
   __shared__ float s_inv[2];
   int b = blockIdx.x;
-  int mact = m_dev ? *m_dev : M;
-  if (b >= mact) return;
-  int pos = (pos_dev ? *pos_dev : pos0) + b;
+  if (b >= active_rows(m_dev, M)) return;
+  const RowInfo ri = rows[b];
+  const StreamKV sk_ = kv[ri.stream];
+  const int pos = ri.pos;
   int qd = nh * hd, kvd = nkv * hd, half = hd / 2, chunked = (half / 8) * 8;
-  float* row = qkv + (size_t)b * ld;
+  const float* row = qkv + (size_t)b * ld;
   for (int i = threadIdx.x; i < qd + kvd; i += blockDim.x) srow[i] = row[i];
   __syncthreads();
   float* sq = srow;
   float* sk = srow + qd;
-  if (qk_mode == 2) {  // full-width: one RMS over the whole projection
-    if (threadIdx.x == 0) rms_inplace_seq(sq, qd, qn, eps, &s_inv[0]);
-    if (threadIdx.x == 32) rms_inplace_seq(sk, kvd, kn, eps, &s_inv[1]);
+  if (qk_mode == 2) {  // full width: one RMS over the whole projection
+    if (threadIdx.x == 0) s_inv[0] = rms_inv_seq(sq, qd, eps);
+    if (threadIdx.x == 32) s_inv[1] = rms_inv_seq(sk, kvd, eps);
     __syncthreads();
     for (int i = threadIdx.x; i < qd; i += blockDim.x) sq[i] = __fmul_rn(__fmul_rn(sq[i], s_inv[0]), qn[i]);
     for (int i = threadIdx.x; i < kvd; i += blockDim.x) sk[i] = __fmul_rn(__fmul_rn(sk[i], s_inv[1]), kn[i]);
     __syncthreads();
-  } else if (qk_mode == 1) {  // per head, weight of head_dim shared by heads
+  } else if (qk_mode == 1) {  // per head, one head_dim weight shared by heads
     for (int h = threadIdx.x; h < nh + nkv; h += blockDim.x) {
       float* hp = h < nh ? sq + h * hd : sk + (h - nh) * hd;
       const float* wv = h < nh ? qn : kn;
-      float inv;
-      rms_inplace_seq(hp, hd, wv, eps, &inv);
+      float inv = rms_inv_seq(hp, hd, eps);
       for (int i = 0; i < hd; ++i) hp[i] = __fmul_rn(__fmul_rn(hp[i], inv), wv[i]);
     }
     __syncthreads();
@@ -163,55 +172,46 @@ __global__ void qkv_post_kernel(float* __restrict__ qkv, int ld, float* __restri
   __syncthreads();
   for (int i = threadIdx.x; i < qd; i += blockDim.x) q_out[(size_t)b * qd + i] = sq[i];
   const float* vrow = row + qd + kvd;
+  const size_t lbase = (size_t)layer * nkv * sk_.max_ctx * hd;
   for (int i = threadIdx.x; i < kvd; i += blockDim.x) {
     int h = i / hd, d = i % hd;
-    size_t o = ((size_t)h * max_ctx + pos) * hd + d;
-    kc[o] = sk[i];
-    vc[o] = vrow[i];
+    size_t o = lbase + ((size_t)h * sk_.max_ctx + pos) * hd + d;
+    sk_.k[o] = sk[i];
+    sk_.v[o] = vrow[i];
   }
 }
 
 // ---------------------------------------------------------------------------
-// Exact attention: CTA (kv head, query row). Scores for every cached
-// position (8-lane FMA dot + tree, times scale), max, Schraudolph exp for
-// the first (n/8)*8 scores and libm-accurate exp for the tail, 8-lane
-// ordered sum, normalise, then out[d] = fma(p_t, v_t[d], out[d]) in
-// position order. V is streamed through a double-buffered smem tile.
+// Attention, step 1: scores. CTA (kv head, row, chunk of kScoreChunk
+// positions); thread t owns one cached position, keeps its K row in
+// registers and scores it against the group's query heads: 8-lane FMA dot,
+// horizontal-sum tree, times scale (then softcap).
 template <int HD>
-__global__ void __launch_bounds__(256) attention_kernel(const float* __restrict__ q, float* __restrict__ out,
-                                                        const float* __restrict__ kc, const float* __restrict__ vc,
-                                                        int nh, int nkv, int max_ctx, const int* pos_dev, int pos0,
-                                                        const int* m_dev, int M, float scale, float softcap,
-                                                        int n_alloc, ExpfTable et) {
-  constexpr int VT = 32;  // positions per V tile
-  extern __shared__ __align__(16) float sm[];
+__global__ void __launch_bounds__(kScoreChunk) attn_scores_kernel(
+    const float* __restrict__ q, const StreamKV* __restrict__ kv, int layer, const RowInfo* __restrict__ rows,
+    const int* m_dev, int M, int nh, int nkv, float scale, float softcap, float* __restrict__ scores,
+    float* __restrict__ smax, int n_alloc, int n_chunks) {
+  __shared__ float sq[8 * HD];
+  __shared__ float red[8][kScoreChunk / 32];
+  const int kvh = blockIdx.x, j = blockIdx.y, chunk = blockIdx.z;
+  if (j >= active_rows(m_dev, M)) return;
+  const RowInfo ri = rows[j];
+  const int n = ri.pos + 1;
+  const int t0 = chunk * kScoreChunk;
+  if (t0 >= n) return;
   const int hpk = nh / nkv;
-  float* sq = sm;                          // hpk * HD
-  float* sc = sq + hpk * HD;               // hpk * n_alloc
-  float* vt = sc + (size_t)hpk * n_alloc;  // 2 * VT * HD
-  __shared__ float red[8][8];
-  __shared__ float lane_part[8][8];
-  __shared__ float s_max[8], s_inv[8];
-
-  const int kvh = blockIdx.x, b = blockIdx.y;
-  const int mact = m_dev ? *m_dev : M;
-  if (b >= mact) return;
-  const int pos = (pos_dev ? *pos_dev : pos0) + b;
-  const int n = pos + 1;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int qd = nh * HD;
-  const float* kbase = kc + (size_t)kvh * max_ctx * HD;
-  const float* vbase = vc + (size_t)kvh * max_ctx * HD;
-
-  for (int i = tid; i < hpk * HD; i += blockDim.x) sq[i] = q[(size_t)b * qd + (size_t)kvh * hpk * HD + i];
+  for (int i = tid; i < hpk * HD; i += blockDim.x) sq[i] = q[(size_t)j * nh * HD + (size_t)kvh * hpk * HD + i];
   __syncthreads();
-
-  // Phase A: scores.
+  const StreamKV sk_ = kv[ri.stream];
+  const int t = t0 + tid;
   float tmax[8];
+#pragma unroll
   for (int h = 0; h < 8; ++h) tmax[h] = -INFINITY;
-  for (int t = tid; t < n; t += blockDim.x) {
+  if (t < n) {
+    const float4* kp = reinterpret_cast<const float4*>(
+        sk_.k + (((size_t)layer * nkv + kvh) * sk_.max_ctx + t) * HD);
     float kr[HD];
-    const float4* kp = reinterpret_cast<const float4*>(kbase + (size_t)t * HD);
 #pragma unroll
     for (int i = 0; i < HD / 4; ++i) {
       float4 v = __ldg(kp + i);
@@ -223,14 +223,13 @@ __global__ void __launch_bounds__(256) attention_kernel(const float* __restrict_
 #pragma unroll
       for (int cc = 0; cc < HD / 8; ++cc)
 #pragma unroll
-        for (int j = 0; j < 8; ++j) acc[j] = __fmaf_rn(qh[8 * cc + j], kr[8 * cc + j], acc[j]);
+        for (int jj = 0; jj < 8; ++jj) acc[jj] = __fmaf_rn(qh[8 * cc + jj], kr[8 * cc + jj], acc[jj]);
       float sv = __fmul_rn(hsum8(acc), scale);
       if (softcap > 0.f) sv = __fmul_rn(softcap, tanhf(__fdiv_rn(sv, softcap)));
-      sc[(size_t)h * n_alloc + t] = sv;
-      if (h < 8 && sv > tmax[h]) tmax[h] = sv;
+      scores[((size_t)j * nh + kvh * hpk + h) * n_alloc + t] = sv;
+      tmax[h] = sv;
     }
   }
-  // Block max per head (hpk <= 8).
   for (int h = 0; h < hpk; ++h) {
     float m = tmax[h];
     for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
@@ -239,90 +238,132 @@ __global__ void __launch_bounds__(256) attention_kernel(const float* __restrict_
   __syncthreads();
   if (tid < hpk) {
     float m = red[tid][0];
-    for (int w = 1; w < 8; ++w) m = fmaxf(m, red[tid][w]);
-    s_max[tid] = m;
+    for (int w = 1; w < kScoreChunk / 32; ++w) m = fmaxf(m, red[tid][w]);
+    smax[((size_t)j * nh + kvh * hpk + tid) * n_chunks + chunk] = m;
   }
-  __syncthreads();
-  // Phase B: exponentials.
+}
+
+// Attention, step 2: softmax of one (row, head). Schraudolph exp for the
+// first (n/8)*8 scores, the host-libm expf for the tail; the sum in 8 lanes
+// (lane j adds scores 8i + j in order), the tree, then the tail added in
+// order; stores exp values in place and 1/sum.
+__global__ void __launch_bounds__(256) attn_softmax_kernel(const RowInfo* __restrict__ rows, const int* m_dev,
+                                                           int M, int nh, float* __restrict__ scores,
+                                                           const float* __restrict__ smax, float* __restrict__ inv,
+                                                           int n_alloc, int n_chunks, ExpfTable et) {
+  extern __shared__ float se[];
+  __shared__ float lanes[8];
+  const int j = blockIdx.x, h = blockIdx.y;
+  if (j >= active_rows(m_dev, M)) return;
+  const int n = rows[j].pos + 1;
+  const int nch = (n + kScoreChunk - 1) / kScoreChunk;
+  const float* cm = smax + ((size_t)j * nh + h) * n_chunks;
+  float m = cm[0];
+  for (int c = 1; c < nch; ++c) m = fmaxf(m, cm[c]);
+  float* row = scores + ((size_t)j * nh + h) * n_alloc;
   const int n8 = (n / 8) * 8;
-  for (int idx = tid; idx < hpk * n; idx += blockDim.x) {
-    int h = idx / n, t = idx % n;
-    float* p = sc + (size_t)h * n_alloc + t;
-    float x = __fsub_rn(*p, s_max[h]);
-    *p = t < n8 ? schraudolph(x) : expf_host(x, et);
+  for (int t = threadIdx.x; t < n; t += blockDim.x) {
+    float x = __fsub_rn(row[t], m);
+    float e = t < n8 ? schraudolph(x) : expf_host(x, et);
+    row[t] = e;
+    se[t] = e;
   }
   __syncthreads();
-  if (tid < hpk * 8) {
-    int h = tid >> 3, j = tid & 7;
-    const float* p = sc + (size_t)h * n_alloc;
+  if (threadIdx.x < 8) {
+    const int jj = threadIdx.x, cnt = n8 / 8;
     float acc = 0.f;
-    for (int i = 0; i < n8 / 8; ++i) acc = __fadd_rn(acc, p[8 * i + j]);
-    lane_part[h][j] = acc;
-  }
-  __syncthreads();
-  if (tid < hpk) {
-    const float* p = sc + (size_t)tid * n_alloc;
-    float sum = hsum8(lane_part[tid]);
-    for (int t = n8; t < n; ++t) sum = __fadd_rn(sum, p[t]);
-    s_inv[tid] = __fdiv_rn(1.0f, sum);
-  }
-  __syncthreads();
-  for (int idx = tid; idx < hpk * n; idx += blockDim.x) {
-    int h = idx / n, t = idx % n;
-    float* p = sc + (size_t)h * n_alloc + t;
-    *p = __fmul_rn(*p, s_inv[h]);
-  }
-  // Phase C: V accumulation, chains (h, d) in position order.
-  constexpr int kMaxChains = 4;
-  float acc[kMaxChains];
-  int ch_h[kMaxChains], ch_d[kMaxChains];
-  const int chains = hpk * HD;
+    int i = 0;
+    for (; i + 8 <= cnt; i += 8) {
+      float v[8];
 #pragma unroll
-  for (int k = 0; k < kMaxChains; ++k) {
-    int idx = tid + k * 256;
-    acc[k] = 0.f;
-    ch_h[k] = idx < chains ? idx / HD : 0;
-    ch_d[k] = idx % HD;
+      for (int u = 0; u < 8; ++u) v[u] = se[8 * (i + u) + jj];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) acc = __fadd_rn(acc, v[u]);
+    }
+    for (; i < cnt; ++i) acc = __fadd_rn(acc, se[8 * i + jj]);
+    lanes[jj] = acc;
   }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float sum = hsum8(lanes);
+    for (int t = n8; t < n; ++t) sum = __fadd_rn(sum, se[t]);
+    inv[(size_t)j * nh + h] = __fdiv_rn(1.0f, sum);
+  }
+}
+
+// Attention, step 3: out[h][d] = fma(p_t, v_t[d], out) over t in order, with
+// p_t = e_t * (1/sum). CTA (kv head, row); one thread per (head, dim) chain;
+// V and p tiles staged in shared memory (double-buffered V via cp.async).
+template <int HD>
+__global__ void __launch_bounds__(1024) attn_pv_kernel(const StreamKV* __restrict__ kv, int layer,
+                                                       const RowInfo* __restrict__ rows, const int* m_dev, int M,
+                                                       int nh, int nkv, const float* __restrict__ scores,
+                                                       const float* __restrict__ inv, int n_alloc,
+                                                       float* __restrict__ out) {
+  constexpr int VT = 64;
+  extern __shared__ __align__(16) float sm[];
+  const int hpk = nh / nkv;
+  float* vt = sm;                       // [2][VT][HD]
+  float* pt = sm + 2 * VT * HD;         // [hpk][VT]
+  const int kvh = blockIdx.x, j = blockIdx.y;
+  if (j >= active_rows(m_dev, M)) return;
+  const RowInfo ri = rows[j];
+  const int n = ri.pos + 1;
+  const StreamKV sk_ = kv[ri.stream];
+  const float* vbase = sk_.v + ((size_t)layer * nkv + kvh) * sk_.max_ctx * HD;
+  const int tid = threadIdx.x;
+  const int h = tid / HD, d = tid % HD;
+  const bool chain = tid < hpk * HD;
+  const float* erow0 = scores + ((size_t)j * nh + kvh * hpk) * n_alloc;
+  const float* invr = inv + (size_t)j * nh + kvh * hpk;
   const int ntiles = (n + VT - 1) / VT;
-  auto load_tile = [&](int tile, int buf) {
+  auto load_v = [&](int tile, int buf) {
     int t0 = tile * VT;
     int cnt = min(VT, n - t0) * HD / 4;
     const float4* src = reinterpret_cast<const float4*>(vbase + (size_t)t0 * HD);
     float4* dst = reinterpret_cast<float4*>(vt + (size_t)buf * VT * HD);
     for (int i = tid; i < cnt; i += blockDim.x) {
-      uint32_t d = smem_u32(dst + i);
-      asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(d), "l"(src + i) : "memory");
+      uint32_t a = smem_u32(dst + i);
+      asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(a), "l"(src + i) : "memory");
     }
     asm volatile("cp.async.commit_group;" ::: "memory");
   };
-  load_tile(0, 0);
+  float acc = 0.f;
+  load_v(0, 0);
   for (int tile = 0; tile < ntiles; ++tile) {
+    const int t0 = tile * VT, cnt = min(VT, n - t0);
+    // p tile for this block's heads: p = e * inv (the reference's
+    // `*sp *= inv_sum`).
+    for (int i = tid; i < hpk * VT; i += blockDim.x) {
+      int hh = i / VT, tt = i % VT;
+      pt[i] = tt < cnt ? __fmul_rn(erow0[(size_t)hh * n_alloc + t0 + tt], invr[hh]) : 0.f;
+    }
     if (tile + 1 < ntiles) {
-      load_tile(tile + 1, (tile + 1) & 1);
+      load_v(tile + 1, (tile + 1) & 1);
       asm volatile("cp.async.wait_group 1;" ::: "memory");
     } else {
       asm volatile("cp.async.wait_group 0;" ::: "memory");
     }
     __syncthreads();
-    const float* vb = vt + (size_t)(tile & 1) * VT * HD;
-    const int t0 = tile * VT, cnt = min(VT, n - t0);
+    if (chain) {
+      const float* vb = vt + (size_t)(tile & 1) * VT * HD + d;
+      const float* pb = pt + h * VT;
+      int t = 0;
+      for (; t + 8 <= cnt; t += 8) {
+        float pv[8], vv[8];
 #pragma unroll
-    for (int k = 0; k < kMaxChains; ++k) {
-      if (tid + k * 256 >= chains) break;
-      const float* prow = sc + (size_t)ch_h[k] * n_alloc + t0;
-      float a = acc[k];
-      for (int t = 0; t < cnt; ++t) a = __fmaf_rn(prow[t], vb[t * HD + ch_d[k]], a);
-      acc[k] = a;
+        for (int u = 0; u < 8; ++u) {
+          pv[u] = pb[t + u];
+          vv[u] = vb[(t + u) * HD];
+        }
+#pragma unroll
+        for (int u = 0; u < 8; ++u) acc = __fmaf_rn(pv[u], vv[u], acc);
+      }
+      for (; t < cnt; ++t) acc = __fmaf_rn(pb[t], vb[t * HD], acc);
     }
     __syncthreads();
   }
-#pragma unroll
-  for (int k = 0; k < kMaxChains; ++k) {
-    int idx = tid + k * 256;
-    if (idx < chains)
-      out[(size_t)b * qd + (size_t)(kvh * hpk + ch_h[k]) * HD + ch_d[k]] = acc[k];
-  }
+  if (chain) out[(size_t)j * nh * HD + (size_t)(kvh * hpk + h) * HD + d] = acc;
 }
 
 // ---------------------------------------------------------------------------
@@ -330,8 +371,7 @@ __global__ void __launch_bounds__(256) attention_kernel(const float* __restrict_
 __global__ void swiglu_kernel(const float* __restrict__ gu, int ff, float* __restrict__ act,
                               const int* m_dev, int M, ExpfTable et) {
   int b = blockIdx.y;
-  int mact = m_dev ? *m_dev : M;
-  if (b >= mact) return;
+  if (b >= active_rows(m_dev, M)) return;
   int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= ff) return;
   float x = gu[(size_t)b * 2 * ff + i], u = gu[(size_t)b * 2 * ff + ff + i];
@@ -359,8 +399,7 @@ __device__ __forceinline__ unsigned long long argmax_key(float v, uint32_t idx) 
 __global__ void argmax_kernel(const float* __restrict__ logits, int vocab, const int* m_dev, int M,
                               unsigned long long* __restrict__ best) {
   int b = blockIdx.y;
-  int mact = m_dev ? *m_dev : M;
-  if (b >= mact) return;
+  if (b >= active_rows(m_dev, M)) return;
   unsigned long long k = 0;
   const float* row = logits + (size_t)b * vocab;
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < vocab; i += gridDim.x * blockDim.x) {
@@ -375,12 +414,17 @@ __global__ void argmax_kernel(const float* __restrict__ logits, int vocab, const
 }
 
 // ---------------------------------------------------------------------------
-// Draft search. One CTA: for n from hi down to lo, the largest start s with
-// ctx[s..s+n] == suffix (s <= len-n-1) wins; draft = ctx[s+n .. s+n+dl).
-__global__ void ngram_kernel(const uint32_t* __restrict__ ctx, StepState* st, int max_draft,
-                             int max_ngram, int min_ngram, int max_ctx) {
+// Draft search, one CTA per stream: for n from hi down to lo, the largest
+// start s with ctx[s..s+n] == suffix (s <= len-n-1) wins; draft =
+// ctx[s+n .. s+n+dl) with dl = min(max_draft, budget, len - s - n), budget =
+// max_ctx - pos - 1.
+__global__ void ngram_kernel(const uint32_t* __restrict__ ctx_all, int ctx_cap, StreamStep* st_all,
+                             const StreamKV* __restrict__ kv, int max_draft, int max_ngram, int min_ngram) {
   __shared__ int best;
-  const int len = st->ctx_len, pos = st->pos;
+  const int sidx = blockIdx.x;
+  StreamStep* st = st_all + sidx;
+  const uint32_t* ctx = ctx_all + (size_t)sidx * ctx_cap;
+  const int len = st->ctx_len, pos = st->pos, max_ctx = kv[sidx].max_ctx;
   const int budget = max_ctx > pos + 1 ? max_ctx - pos - 1 : 0;
   const int kcap = min(max_draft, budget);
   int found_n = 0, found_s = -1;
@@ -402,8 +446,7 @@ __global__ void ngram_kernel(const uint32_t* __restrict__ ctx, StepState* st, in
     }
   }
   if (threadIdx.x == 0) {
-    const uint32_t last = ctx[len - 1];
-    st->tokens[0] = last;
+    st->tokens[0] = ctx[len - 1];
     if (found_s >= 0) {
       int ds = found_s + found_n;
       int dl = min(kcap, len - ds);
@@ -416,32 +459,48 @@ __global__ void ngram_kernel(const uint32_t* __restrict__ ctx, StepState* st, in
       st->ngram = 0;
       st->n_rows = 1;
     }
-    for (int r = 0; r < kMaxRows; ++r) st->amax[r] = 0ull;
   }
 }
 
-// Greedy acceptance: accept d_i while argmax_i == d_i; the first mismatch is
-// replaced by argmax_i; if all are accepted the bonus is argmax_k. Then the
-// KV watermark becomes pos + produced.
-__global__ void accept_kernel(StepState* st, int* filled, int num_layers) {
-  if (threadIdx.x != 0) return;
-  const int dl = st->drafted;
-  int produced = 0, accepted = 0;
-  if (dl == 0) {
-    st->out[produced++] = (uint32_t)(st->amax[0] & 0xFFFFFFFFull);
-  } else {
-    for (int i = 0; i < dl; ++i) {
-      uint32_t target = (uint32_t)(st->amax[i] & 0xFFFFFFFFull);
-      st->out[produced++] = target;
-      if (target != st->tokens[1 + i]) break;
-      ++accepted;
+// Compact every stream's verify rows into one row set (prefix sum over the
+// streams), write row metadata and token ids, zero the argmax slots.
+__global__ void plan_kernel(StreamStep* st, int n, RowInfo* rows, uint32_t* ids, int* m_active,
+                            unsigned long long* best, int best_len) {
+  if (threadIdx.x == 0) {
+    int r = 0;
+    for (int i = 0; i < n; ++i) {
+      st[i].row0 = r;
+      r += st[i].n_rows;
     }
-    if (accepted == dl) st->out[produced++] = (uint32_t)(st->amax[dl] & 0xFFFFFFFFull);
+    *m_active = r;
   }
+  __syncthreads();
+  for (int i = threadIdx.x; i < best_len; i += blockDim.x) best[i] = 0ull;
+  for (int i = 0; i < n; ++i) {
+    const int r0 = st[i].row0, nr = st[i].n_rows, p = st[i].pos;
+    for (int b = threadIdx.x; b < nr; b += blockDim.x) {
+      rows[r0 + b] = RowInfo{p + b, i};
+      ids[r0 + b] = st[i].tokens[b];
+    }
+  }
+}
+
+// Greedy acceptance per stream: accept d_i while argmax_i == d_i; the first
+// mismatch is replaced by argmax_i; if all are accepted the bonus is argmax_k.
+__global__ void accept_kernel(StreamStep* st_all, const unsigned long long* __restrict__ best) {
+  if (threadIdx.x != 0) return;
+  StreamStep* st = st_all + blockIdx.x;
+  const int dl = st->drafted, r0 = st->row0;
+  int produced = 0, accepted = 0;
+  for (int i = 0; i < dl; ++i) {
+    uint32_t target = (uint32_t)(best[r0 + i] & 0xFFFFFFFFull);
+    st->out[produced++] = target;
+    if (target != st->tokens[1 + i]) break;
+    ++accepted;
+  }
+  if (accepted == dl) st->out[produced++] = (uint32_t)(best[r0 + dl] & 0xFFFFFFFFull);
   st->accepted = accepted;
   st->produced = produced;
-  // Stores reached pos + n_rows; truncate(pos + produced) leaves exactly this.
-  for (int l = 0; l < num_layers; ++l) filled[l] = st->pos + produced;
 }
 
 // ---------------------------------------------------------------------------
@@ -461,31 +520,36 @@ cudaError_t launch_rmsnorm(const float* x, const float* w, int n, float eps, flo
 
 cudaError_t launch_qkv_post(float* qkv, int ld, float* q_out, int nh, int nkv, int hd, const float* qn,
                             const float* kn, int qk_mode, float eps, const float* rope_cos,
-                            const float* rope_sin, float* kc, float* vc, int max_ctx, const int* pos_dev,
-                            int pos0, const int* m_dev, int M, cudaStream_t s) {
+                            const float* rope_sin, const StreamKV* kv, int layer, const RowInfo* rows,
+                            const int* m_dev, int M, cudaStream_t s) {
   size_t smem = (size_t)(nh + nkv) * hd * sizeof(float);
   qkv_post_kernel<<<M, 256, smem, s>>>(qkv, ld, q_out, nh, nkv, hd, qn, kn, qk_mode, eps, rope_cos, rope_sin,
-                                       kc, vc, max_ctx, pos_dev, pos0, m_dev, M);
+                                       kv, layer, rows, m_dev, M);
   return cudaGetLastError();
 }
 
-// n_alloc must be a multiple of 4 so the V tile behind the scores is 16-byte
-// aligned for cp.async.
-size_t attention_smem_bytes(int hd, int hpk, int n_alloc) {
-  return ((size_t)hpk * hd + (size_t)hpk * n_alloc + 2 * 32 * (size_t)hd) * sizeof(float);
-}
+size_t attention_n_chunks(int n_alloc) { return (size_t)(n_alloc + kScoreChunk - 1) / kScoreChunk; }
 
-cudaError_t launch_attention(const float* q, float* out, const float* kc, const float* vc, int nh, int nkv,
-                             int hd, int max_ctx, const int* pos_dev, int pos0, const int* m_dev, int M,
-                             float scale, float softcap, int n_alloc, const ExpfTable& et, cudaStream_t s) {
-  int hpk = nh / nkv;
-  size_t smem = attention_smem_bytes(hd, hpk, n_alloc);
-  dim3 grid(nkv, M);
-  if (smem > kAttnMaxSmem) return cudaErrorInvalidValue;
-#define RAI_ATTN(HDV)                                                                                  \
-  case HDV:                                                                                            \
-    attention_kernel<HDV><<<grid, 256, smem, s>>>(q, out, kc, vc, nh, nkv, max_ctx, pos_dev, pos0,     \
-                                                  m_dev, M, scale, softcap, n_alloc, et);              \
+static size_t pv_smem_bytes(int hd, int hpk) { return (size_t)(2 * 64 * hd + hpk * 64) * sizeof(float); }
+
+cudaError_t launch_attention(const float* q, float* out, const StreamKV* kv, int layer, const RowInfo* rows,
+                             const int* m_dev, int M, int nh, int nkv, int hd, float scale, float softcap,
+                             float* scores, float* smax, float* inv, int n_alloc, const ExpfTable& et,
+                             cudaStream_t s) {
+  const int hpk = nh / nkv;
+  const int nch = (int)attention_n_chunks(n_alloc);
+  dim3 g1(nkv, M, nch), g2(M, nh), g3(nkv, M);
+  const size_t sm2 = (size_t)n_alloc * sizeof(float);
+  const size_t sm3 = pv_smem_bytes(hd, hpk);
+  const int t3 = (hpk * hd + 31) / 32 * 32;
+  if (sm2 > kAttnMaxSmem || sm3 > kAttnMaxSmem || hpk > 8 || t3 > 1024) return cudaErrorInvalidValue;
+#define RAI_ATTN(HDV)                                                                                   \
+  case HDV:                                                                                             \
+    attn_scores_kernel<HDV><<<g1, kScoreChunk, 0, s>>>(q, kv, layer, rows, m_dev, M, nh, nkv, scale,    \
+                                                       softcap, scores, smax, n_alloc, nch);            \
+    attn_softmax_kernel<<<g2, 256, sm2, s>>>(rows, m_dev, M, nh, scores, smax, inv, n_alloc, nch, et);  \
+    attn_pv_kernel<HDV><<<g3, t3, sm3, s>>>(kv, layer, rows, m_dev, M, nh, nkv, scores, inv, n_alloc,   \
+                                            out);                                                       \
     break;
   switch (hd) {
     RAI_ATTN(16)
@@ -501,10 +565,11 @@ cudaError_t launch_attention(const float* q, float* out, const float* kc, const 
 
 cudaError_t init_layer_attributes() {
   const int bytes = (int)kAttnMaxSmem;
-  cudaError_t e = cudaFuncSetAttribute(attention_kernel<16>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
-  if (e == cudaSuccess) e = cudaFuncSetAttribute(attention_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
-  if (e == cudaSuccess) e = cudaFuncSetAttribute(attention_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
-  if (e == cudaSuccess) e = cudaFuncSetAttribute(attention_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  cudaError_t e = cudaFuncSetAttribute(attn_softmax_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e == cudaSuccess) e = cudaFuncSetAttribute(attn_pv_kernel<16>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e == cudaSuccess) e = cudaFuncSetAttribute(attn_pv_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e == cudaSuccess) e = cudaFuncSetAttribute(attn_pv_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e == cudaSuccess) e = cudaFuncSetAttribute(attn_pv_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
   return e;
 }
 
@@ -524,14 +589,20 @@ cudaError_t launch_argmax(const float* logits, int vocab, const int* m_dev, int 
   return cudaGetLastError();
 }
 
-cudaError_t launch_ngram(const uint32_t* ctx, StepState* st, int max_draft, int max_ngram, int min_ngram,
-                         int max_ctx, cudaStream_t s) {
-  ngram_kernel<<<1, 1024, 0, s>>>(ctx, st, max_draft, max_ngram, min_ngram, max_ctx);
+cudaError_t launch_ngram(const uint32_t* ctx, int ctx_cap, StreamStep* st, const StreamKV* kv, int n,
+                         int max_draft, int max_ngram, int min_ngram, cudaStream_t s) {
+  ngram_kernel<<<n, 1024, 0, s>>>(ctx, ctx_cap, st, kv, max_draft, max_ngram, min_ngram);
   return cudaGetLastError();
 }
 
-cudaError_t launch_accept(StepState* st, int* filled, int num_layers, cudaStream_t s) {
-  accept_kernel<<<1, 32, 0, s>>>(st, filled, num_layers);
+cudaError_t launch_plan(StreamStep* st, int n, RowInfo* rows, uint32_t* ids, int* m_active,
+                        unsigned long long* best, int best_len, cudaStream_t s) {
+  plan_kernel<<<1, 256, 0, s>>>(st, n, rows, ids, m_active, best, best_len);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_accept(StreamStep* st, int n, const unsigned long long* best, cudaStream_t s) {
+  accept_kernel<<<n, 32, 0, s>>>(st, best);
   return cudaGetLastError();
 }
 

@@ -1,4 +1,10 @@
 // Launchers of the per-layer and speculation kernels (internal).
+//
+// Every per-row kernel works on a set of "rows": a row is one token of one
+// stream at one position. Rows are described by a device array of RowInfo;
+// the number of active rows is static (M) or read from device memory (m_dev)
+// when it is produced on the device inside a CUDA graph. Each stream has its
+// own KV cache (StreamKV); many streams can share one forward pass.
 #pragma once
 #include <cuda_runtime.h>
 #include <stdint.h>
@@ -7,27 +13,37 @@
 
 namespace rai {
 
-constexpr int kMaxRows = 33;  // max_draft <= 32 (rai run's --lookup-k limit) + 1
+constexpr int kMaxRowsPerStream = 33;  // max_draft <= 32 (rai run's --lookup-k limit) + 1
+constexpr int kScoreChunk = 256;       // positions per attention-score CTA
 
-// Device-resident state of one decode step. The host writes pos and ctx_len
-// (and the context) before the step; the kernels fill the rest; the host
-// reads it back once at the end of the step.
-struct StepState {
-  int pos;
-  int ctx_len;
-  int n_rows;    // verify rows this step: drafted + 1
-  int drafted;
-  int ngram;     // matched n-gram length, 0 = none
-  int accepted;
-  int produced;
-  uint32_t err;
-  uint32_t tokens[kMaxRows];  // [last, draft_0 .. draft_{k-1}]
-  uint32_t out[kMaxRows];     // produced tokens
-  unsigned long long amax[kMaxRows];
+struct RowInfo {
+  int pos;     // position of the row's token
+  int stream;  // index into the StreamKV / StreamStep arrays
 };
 
-// Dynamic shared memory the attention kernel may use (the opt-in limit of
-// 227 KB less its static shared memory and a margin).
+// One stream's cache: [layer][kv_head][max_ctx][head_dim] f32.
+struct StreamKV {
+  float* k;
+  float* v;
+  int max_ctx;
+  int pad;
+};
+
+// One stream's state in a decode step. The host writes pos and ctx_len; the
+// kernels write the rest; the host reads it back once per step.
+struct StreamStep {
+  int pos, ctx_len;
+  int n_rows;   // verify rows: drafted + 1
+  int drafted;
+  int ngram;    // matched n-gram length, 0 = none
+  int accepted, produced;
+  int row0;     // first compacted row of this stream in the step's forward
+  uint32_t tokens[kMaxRowsPerStream];  // [last, draft_0 .. draft_{k-1}]
+  uint32_t out[kMaxRowsPerStream];     // produced tokens
+};
+
+// Dynamic shared memory the attention kernels may use (the opt-in limit of
+// 227 KB less static shared memory and a margin).
 constexpr size_t kAttnMaxSmem = 224 * 1024;
 
 // Raise the dynamic shared-memory limit of the attention kernels (once per
@@ -41,18 +57,25 @@ cudaError_t launch_rmsnorm(const float* x, const float* w, int n, float eps, flo
                            const int* m_dev, int M, cudaStream_t s);
 cudaError_t launch_qkv_post(float* qkv, int ld, float* q_out, int nh, int nkv, int hd, const float* qn,
                             const float* kn, int qk_mode, float eps, const float* rope_cos,
-                            const float* rope_sin, float* kc, float* vc, int max_ctx, const int* pos_dev,
-                            int pos0, const int* m_dev, int M, cudaStream_t s);
-size_t attention_smem_bytes(int hd, int hpk, int n_alloc);
-cudaError_t launch_attention(const float* q, float* out, const float* kc, const float* vc, int nh, int nkv,
-                             int hd, int max_ctx, const int* pos_dev, int pos0, const int* m_dev, int M,
-                             float scale, float softcap, int n_alloc, const ExpfTable& et, cudaStream_t s);
+                            const float* rope_sin, const StreamKV* kv, int layer, const RowInfo* rows,
+                            const int* m_dev, int M, cudaStream_t s);
+// Attention over each row's own stream cache (positions 0..pos inclusive).
+// scores: [M][nh][n_alloc] f32 scratch; smax: [M][nh][n_chunks]; inv: [M][nh].
+size_t attention_n_chunks(int n_alloc);
+cudaError_t launch_attention(const float* q, float* out, const StreamKV* kv, int layer, const RowInfo* rows,
+                             const int* m_dev, int M, int nh, int nkv, int hd, float scale, float softcap,
+                             float* scores, float* smax, float* inv, int n_alloc, const ExpfTable& et,
+                             cudaStream_t s);
 cudaError_t launch_swiglu(const float* gu, int ff, float* act, const int* m_dev, int M, const ExpfTable& et,
                           cudaStream_t s);
 cudaError_t launch_argmax(const float* logits, int vocab, const int* m_dev, int M, unsigned long long* best,
                           cudaStream_t s);
-cudaError_t launch_ngram(const uint32_t* ctx, StepState* st, int max_draft, int max_ngram, int min_ngram,
-                         int max_ctx, cudaStream_t s);
-cudaError_t launch_accept(StepState* st, int* filled, int num_layers, cudaStream_t s);
+// Draft search for each of n streams; ctx for stream i at ctx + i * ctx_cap.
+cudaError_t launch_ngram(const uint32_t* ctx, int ctx_cap, StreamStep* st, const StreamKV* kv, int n,
+                         int max_draft, int max_ngram, int min_ngram, cudaStream_t s);
+// Compact the streams' verify rows: rows / ids / *m_active; zero best[].
+cudaError_t launch_plan(StreamStep* st, int n, RowInfo* rows, uint32_t* ids, int* m_active,
+                        unsigned long long* best, int best_len, cudaStream_t s);
+cudaError_t launch_accept(StreamStep* st, int n, const unsigned long long* best, cudaStream_t s);
 
 }  // namespace rai

@@ -139,57 +139,6 @@ struct rai_model {
   }
 };
 
-struct rai_dec {
-  rai_model* m = nullptr;
-  int max_ctx = 0;
-  int n_alloc = 0;  // attention score row stride: max_ctx rounded up to 4
-  int mcap = 0;  // rows the scratch buffers hold
-  cudaStream_t stream = nullptr;
-  std::vector<void*> allocs;
-  float* kc = nullptr;  // [layer][kv_head][max_ctx][head_dim]
-  float* vc = nullptr;
-  int* filled_dev = nullptr;
-  std::vector<size_t> filled;
-  float *hidden = nullptr, *resid = nullptr, *normed = nullptr, *qkv = nullptr, *q = nullptr;
-  float *attn = nullptr, *gu = nullptr, *ff = nullptr, *logits = nullptr;
-  ActBuf act_h, act_q, act_ff, act_head;
-  uint32_t* ids_dev = nullptr;
-  uint32_t* ctx_dev = nullptr;
-  uint32_t* ctx_host = nullptr;
-  rai::StepState* st_dev = nullptr;
-  rai::StepState* st_host = nullptr;
-  cudaGraphExec_t graph = nullptr;
-  size_t graph_kernels = 0;
-  uint32_t graph_key[3] = {0, 0, 0};
-  cudaEvent_t ev0 = nullptr, ev1 = nullptr;
-  float last_us = 0.f;
-
-  template <class T>
-  int alloc(T** p, size_t bytes) {
-    void* q_ = nullptr;
-    cudaError_t e = cudaMalloc(&q_, bytes ? bytes : 16);
-    if (e != cudaSuccess)
-      return fail(RAI_ERR_OOM, "cudaMalloc(" + std::to_string(bytes) + "): " + cudaGetErrorString(e));
-    allocs.push_back(q_);
-    *p = static_cast<T*>(q_);
-    return RAI_OK;
-  }
-  ~rai_dec() {
-    int prev = 0;
-    cudaGetDevice(&prev);
-    cudaSetDevice(m->device);
-    if (graph) cudaGraphExecDestroy(graph);
-    if (stream) cudaStreamSynchronize(stream);
-    for (void* p : allocs) cudaFree(p);
-    if (ctx_host) cudaFreeHost(ctx_host);
-    if (st_host) cudaFreeHost(st_host);
-    if (ev0) cudaEventDestroy(ev0);
-    if (ev1) cudaEventDestroy(ev1);
-    if (stream) cudaStreamDestroy(stream);
-    cudaSetDevice(prev);
-  }
-};
-
 namespace {
 
 // Scoped device switch for entry points.
@@ -315,62 +264,223 @@ int check_supported(const Config& c, const raimodel::Model& L) {
   return RAI_OK;
 }
 
+}  // namespace
+
 // ---------------------------------------------------------------------------
-// Forward over M rows (static), of which *m_dev are active when m_dev is set.
-// Positions are pos + b with pos from pos_dev (device) or pos0 (host).
-int forward(rai_dec* d, int M, const int* m_dev, const int* pos_dev, int pos0, const uint32_t* ids_dev,
-            bool logits) {
-  rai_model* Mo = d->m;
+// Batch: device state for one forward / decode step over n streams that share
+// a model. A decoder owns a batch of one (its own scratch); step_many builds
+// (and caches in the model) a batch over the decoders it is given.
+struct Batch {
+  rai_model* m = nullptr;
+  int n = 0;           // streams
+  int R = 0;           // verify row budget per stream (max_draft + 1)
+  int rows_cap = 0;    // rows the scratch holds
+  int ctx_cap = 0;     // context slots per stream
+  int n_alloc = 0;     // attention score row stride
+  cudaStream_t stream = nullptr;
+  std::vector<void*> allocs;
+  std::vector<rai_dec*> decs;
+  float *hidden = nullptr, *resid = nullptr, *normed = nullptr, *qkv = nullptr, *q = nullptr;
+  float *attn = nullptr, *gu = nullptr, *ff = nullptr, *logits = nullptr;
+  float *scores = nullptr, *smax = nullptr, *inv = nullptr;
+  ActBuf act_h, act_q, act_ff, act_head;
+  rai::RowInfo* rows = nullptr;
+  rai::RowInfo* rows_host = nullptr;
+  uint32_t* ids = nullptr;
+  int* m_active = nullptr;
+  unsigned long long* best = nullptr;
+  rai::StreamKV* kv = nullptr;
+  rai::StreamStep* st = nullptr;
+  rai::StreamStep* st_host = nullptr;
+  uint32_t* ctx = nullptr;
+  uint32_t* ctx_host = nullptr;
+  cudaGraphExec_t graph = nullptr;
+  size_t graph_kernels = 0;
+  uint32_t graph_key[3] = {0, 0, 0};
+  cudaEvent_t ev0 = nullptr, ev1 = nullptr;
+  float last_us = 0.f;
+
+  template <class T>
+  int alloc(T** p, size_t bytes) {
+    void* q_ = nullptr;
+    cudaError_t e = cudaMalloc(&q_, bytes ? bytes : 16);
+    if (e != cudaSuccess)
+      return fail(RAI_ERR_OOM, "cudaMalloc(" + std::to_string(bytes) + "): " + cudaGetErrorString(e));
+    allocs.push_back(q_);
+    *p = static_cast<T*>(q_);
+    return RAI_OK;
+  }
+  ~Batch();
+};
+
+struct rai_dec {
+  rai_model* m = nullptr;
+  int max_ctx = 0;
+  float last_us = 0.f;
+  size_t last_kernels = 0;
+  float* kc = nullptr;  // [layer][kv_head][max_ctx][head_dim]
+  float* vc = nullptr;
+  std::vector<size_t> filled;  // per layer
+  std::unique_ptr<Batch> solo;
+  ~rai_dec();
+};
+
+Batch::~Batch() {
+  int prev = 0;
+  cudaGetDevice(&prev);
+  cudaSetDevice(m->device);
+  if (stream) cudaStreamSynchronize(stream);
+  if (graph) cudaGraphExecDestroy(graph);
+  for (void* p : allocs) cudaFree(p);
+  if (ctx_host) cudaFreeHost(ctx_host);
+  if (st_host) cudaFreeHost(st_host);
+  if (rows_host) cudaFreeHost(rows_host);
+  if (ev0) cudaEventDestroy(ev0);
+  if (ev1) cudaEventDestroy(ev1);
+  if (stream) cudaStreamDestroy(stream);
+  cudaSetDevice(prev);
+}
+
+namespace {
+
+// Cached multi-stream batches per model (keyed by the decoder list).
+std::mutex g_batch_mu;
+std::vector<std::pair<rai_model*, std::unique_ptr<Batch>>> g_batches;
+
+void drop_batches_of(rai_dec* d) {
+  std::lock_guard<std::mutex> lk(g_batch_mu);
+  for (size_t i = 0; i < g_batches.size();) {
+    auto& b = g_batches[i].second;
+    if (std::find(b->decs.begin(), b->decs.end(), d) != b->decs.end()) g_batches.erase(g_batches.begin() + i);
+    else ++i;
+  }
+}
+
+void drop_batches_of_model(rai_model* m) {
+  std::lock_guard<std::mutex> lk(g_batch_mu);
+  for (size_t i = 0; i < g_batches.size();) {
+    if (g_batches[i].first == m) g_batches.erase(g_batches.begin() + i);
+    else ++i;
+  }
+}
+
+int alloc_act(Batch* B, ActBuf* a, int tok, int cols, int gs) {
+  a->tok_alloc = (int)rai::round_up(tok, 8);
+  a->groups = (int)rai::ceil_div(cols, gs);
+  return B->alloc(&a->data, ActBuf::bytes(a->tok_alloc, a->groups));
+}
+
+int create_batch(rai_model* m, const std::vector<rai_dec*>& decs, int R, int rows_cap, std::unique_ptr<Batch>* out) {
+  const Config& c = m->cfg;
+  auto B = std::make_unique<Batch>();
+  B->m = m;
+  B->n = (int)decs.size();
+  B->R = R;
+  B->rows_cap = rows_cap;
+  B->decs = decs;
+  int max_ctx = 0;
+  for (auto* d : decs) max_ctx = std::max(max_ctx, d->max_ctx);
+  B->ctx_cap = max_ctx;
+  B->n_alloc = (int)rai::round_up(max_ctx, 4);
+  RAI_CUDA(cudaStreamCreateWithFlags(&B->stream, cudaStreamNonBlocking));
+  RAI_CUDA(cudaEventCreate(&B->ev0));
+  RAI_CUDA(cudaEventCreate(&B->ev1));
+  const size_t Rw = rows_cap, h = c.hidden_size, qd = c.q_dim(), kvd = c.kv_dim(), ff = c.intermediate_size;
+  const size_t nh = c.num_heads;
+  if (int rc = B->alloc(&B->hidden, Rw * h * 4)) return rc;
+  if (int rc = B->alloc(&B->resid, Rw * h * 4)) return rc;
+  if (int rc = B->alloc(&B->normed, Rw * h * 4)) return rc;
+  if (int rc = B->alloc(&B->qkv, Rw * (qd + 2 * kvd) * 4)) return rc;
+  if (int rc = B->alloc(&B->q, Rw * qd * 4)) return rc;
+  if (int rc = B->alloc(&B->attn, Rw * qd * 4)) return rc;
+  if (int rc = B->alloc(&B->gu, Rw * 2 * ff * 4)) return rc;
+  if (int rc = B->alloc(&B->ff, Rw * ff * 4)) return rc;
+  const size_t lrows = std::min<size_t>(Rw, (size_t)std::max(R * B->n, (int)rai::kMaxRowsPerStream));
+  if (int rc = B->alloc(&B->logits, lrows * c.vocab_size * 4)) return rc;
+  if (int rc = B->alloc(&B->scores, Rw * nh * B->n_alloc * 4)) return rc;
+  if (int rc = B->alloc(&B->smax, Rw * nh * rai::attention_n_chunks(B->n_alloc) * 4)) return rc;
+  if (int rc = B->alloc(&B->inv, Rw * nh * 4)) return rc;
+  if (int rc = alloc_act(B.get(), &B->act_h, (int)Rw, (int)h, c.group_size)) return rc;
+  if (int rc = alloc_act(B.get(), &B->act_q, (int)Rw, (int)qd, c.group_size)) return rc;
+  if (int rc = alloc_act(B.get(), &B->act_ff, (int)Rw, (int)ff, c.group_size)) return rc;
+  int hgs = m->head.wbits == 8 ? (int)c.embed_group_size : (int)c.group_size;
+  if (int rc = alloc_act(B.get(), &B->act_head, (int)lrows, (int)h, hgs)) return rc;
+  if (int rc = B->alloc(&B->rows, Rw * sizeof(rai::RowInfo))) return rc;
+  if (int rc = B->alloc(&B->ids, Rw * 4)) return rc;
+  if (int rc = B->alloc(&B->m_active, 4)) return rc;
+  if (int rc = B->alloc(&B->best, Rw * 8)) return rc;
+  if (int rc = B->alloc(&B->kv, B->n * sizeof(rai::StreamKV))) return rc;
+  if (int rc = B->alloc(&B->st, B->n * sizeof(rai::StreamStep))) return rc;
+  if (int rc = B->alloc(&B->ctx, (size_t)B->n * B->ctx_cap * 4)) return rc;
+  RAI_CUDA(cudaMemset(B->st, 0, B->n * sizeof(rai::StreamStep)));
+  RAI_CUDA(cudaMallocHost(&B->ctx_host, (size_t)B->n * B->ctx_cap * 4));
+  RAI_CUDA(cudaMallocHost(&B->st_host, B->n * sizeof(rai::StreamStep)));
+  RAI_CUDA(cudaMallocHost(&B->rows_host, Rw * sizeof(rai::RowInfo)));
+  std::memset(B->st_host, 0, B->n * sizeof(rai::StreamStep));
+  std::vector<rai::StreamKV> kv(B->n);
+  for (int i = 0; i < B->n; ++i) kv[i] = rai::StreamKV{decs[i]->kc, decs[i]->vc, decs[i]->max_ctx, 0};
+  RAI_CUDA(cudaMemcpy(B->kv, kv.data(), kv.size() * sizeof(rai::StreamKV), cudaMemcpyHostToDevice));
+  if ((size_t)B->n_alloc * 4 > rai::kAttnMaxSmem)
+    return fail(RAI_ERR_UNSUPPORTED, "context window too long for the attention softmax kernel");
+  *out = std::move(B);
+  return RAI_OK;
+}
+
+// ---------------------------------------------------------------------------
+// Forward over M rows (static budget) of which *m_dev are active when m_dev
+// is set; rows[] gives each row's (position, stream), ids[] its token.
+int forward(Batch* B, int M, const int* m_dev, bool logits) {
+  rai_model* Mo = B->m;
   const Config& c = Mo->cfg;
-  cudaStream_t s = d->stream;
+  cudaStream_t s = B->stream;
   const int h = c.hidden_size, nh = c.num_heads, nkv = c.num_kv_heads, hd = c.head_dim;
   const int qd = nh * hd, kvd = nkv * hd, ffd = c.intermediate_size;
   const int gs = c.group_size;
   const float eps = c.norm_eps;
   uint32_t* err = Mo->err_dev;
-  RAI_CUDA(rai::launch_embed(ids_dev, m_dev, M, Mo->embed_codes, Mo->embed_params, c.vocab_size, h,
-                             c.embed_group_size, c.embed_scale, d->hidden, err, s));
+  RAI_CUDA(rai::launch_embed(B->ids, m_dev, M, Mo->embed_codes, Mo->embed_params, c.vocab_size, h,
+                             c.embed_group_size, c.embed_scale, B->hidden, err, s));
+  rai::GemmEpilogue e_res;
+  e_res.mode = rai::kEpiResidual;
+  e_res.residual = B->resid;
   for (size_t li = 0; li < c.num_layers; ++li) {
     const LayerDev& L = Mo->layers[li];
-    float* kc = d->kc + li * (size_t)nkv * d->max_ctx * hd;
-    float* vc = d->vc + li * (size_t)nkv * d->max_ctx * hd;
-    RAI_CUDA(rai::launch_rmsnorm(d->hidden, L.in_norm, h, eps, d->normed, d->resid, m_dev, M, s));
-    RAI_CUDA(rai::quantize_act(d->normed, h, M, m_dev, h, gs, 4, d->act_h, s));
+    RAI_CUDA(rai::launch_rmsnorm(B->hidden, L.in_norm, h, eps, B->normed, B->resid, m_dev, M, s));
+    RAI_CUDA(rai::quantize_act(B->normed, h, M, m_dev, h, gs, 4, B->act_h, s));
     rai::GemmEpilogue e_qkv;
     if (L.bias_qkv) { e_qkv.mode = rai::kEpiBias; e_qkv.bias = L.bias_qkv; }
-    RAI_CUDA(rai::gemm_exact(L.qkv, d->act_h, M, d->qkv, qd + 2 * kvd, e_qkv, err, s));
-    RAI_CUDA(rai::launch_qkv_post(d->qkv, qd + 2 * kvd, d->q, nh, nkv, hd, L.q_norm, L.k_norm, Mo->qk_mode, eps,
-                                  Mo->rope_cos, Mo->rope_sin, kc, vc, d->max_ctx, pos_dev, pos0, m_dev, M, s));
-    RAI_CUDA(rai::launch_attention(d->q, d->attn, kc, vc, nh, nkv, hd, d->max_ctx, pos_dev, pos0, m_dev, M,
-                                   Mo->scale, c.attn_logit_softcap, d->n_alloc, Mo->expf, s));
-    RAI_CUDA(rai::quantize_act(d->attn, qd, M, m_dev, qd, gs, 4, d->act_q, s));
-    rai::GemmEpilogue e_res;
-    e_res.mode = rai::kEpiResidual;
-    e_res.residual = d->resid;
-    RAI_CUDA(rai::gemm_exact(L.o, d->act_q, M, d->hidden, h, e_res, err, s));
-    RAI_CUDA(rai::launch_rmsnorm(d->hidden, L.post_norm, h, eps, d->normed, d->resid, m_dev, M, s));
-    RAI_CUDA(rai::quantize_act(d->normed, h, M, m_dev, h, gs, 4, d->act_h, s));
-    RAI_CUDA(rai::gemm_exact(L.gateup, d->act_h, M, d->gu, 2 * ffd, rai::GemmEpilogue{}, err, s));
-    RAI_CUDA(rai::launch_swiglu(d->gu, ffd, d->ff, m_dev, M, Mo->expf, s));
-    RAI_CUDA(rai::quantize_act(d->ff, ffd, M, m_dev, ffd, gs, 4, d->act_ff, s));
-    RAI_CUDA(rai::gemm_exact(L.down, d->act_ff, M, d->hidden, h, e_res, err, s));
+    RAI_CUDA(rai::gemm_exact(L.qkv, B->act_h, M, B->qkv, qd + 2 * kvd, e_qkv, err, s, false, m_dev));
+    RAI_CUDA(rai::launch_qkv_post(B->qkv, qd + 2 * kvd, B->q, nh, nkv, hd, L.q_norm, L.k_norm, Mo->qk_mode, eps,
+                                  Mo->rope_cos, Mo->rope_sin, B->kv, (int)li, B->rows, m_dev, M, s));
+    RAI_CUDA(rai::launch_attention(B->q, B->attn, B->kv, (int)li, B->rows, m_dev, M, nh, nkv, hd, Mo->scale,
+                                   c.attn_logit_softcap, B->scores, B->smax, B->inv, B->n_alloc, Mo->expf, s));
+    RAI_CUDA(rai::quantize_act(B->attn, qd, M, m_dev, qd, gs, 4, B->act_q, s));
+    RAI_CUDA(rai::gemm_exact(L.o, B->act_q, M, B->hidden, h, e_res, err, s, false, m_dev));
+    RAI_CUDA(rai::launch_rmsnorm(B->hidden, L.post_norm, h, eps, B->normed, B->resid, m_dev, M, s));
+    RAI_CUDA(rai::quantize_act(B->normed, h, M, m_dev, h, gs, 4, B->act_h, s));
+    RAI_CUDA(rai::gemm_exact(L.gateup, B->act_h, M, B->gu, 2 * ffd, rai::GemmEpilogue{}, err, s, false, m_dev));
+    RAI_CUDA(rai::launch_swiglu(B->gu, ffd, B->ff, m_dev, M, Mo->expf, s));
+    RAI_CUDA(rai::quantize_act(B->ff, ffd, M, m_dev, ffd, gs, 4, B->act_ff, s));
+    RAI_CUDA(rai::gemm_exact(L.down, B->act_ff, M, B->hidden, h, e_res, err, s, false, m_dev));
   }
   if (logits) {
-    RAI_CUDA(rai::launch_rmsnorm(d->hidden, Mo->final_norm, h, eps, d->normed, nullptr, m_dev, M, s));
+    RAI_CUDA(rai::launch_rmsnorm(B->hidden, Mo->final_norm, h, eps, B->normed, nullptr, m_dev, M, s));
     bool tied = Mo->head.wbits == 8;
-    RAI_CUDA(rai::quantize_act(d->normed, h, M, m_dev, h, tied ? c.embed_group_size : gs, tied ? 8 : 4,
-                               d->act_head, s));
-    RAI_CUDA(rai::gemm_exact(Mo->head, d->act_head, M, d->logits, c.vocab_size, rai::GemmEpilogue{}, err, s));
+    RAI_CUDA(rai::quantize_act(B->normed, h, M, m_dev, h, tied ? c.embed_group_size : gs, tied ? 8 : 4,
+                               B->act_head, s));
+    RAI_CUDA(rai::gemm_exact(Mo->head, B->act_head, M, B->logits, c.vocab_size, rai::GemmEpilogue{}, err, s,
+                             false, m_dev));
   }
   return RAI_OK;
 }
 
-int check_err(rai_dec* d) {
+int check_err(rai_model* m, cudaStream_t s) {
   uint32_t e = 0;
-  RAI_CUDA(cudaMemcpyAsync(&e, d->m->err_dev, 4, cudaMemcpyDeviceToHost, d->stream));
-  RAI_CUDA(cudaStreamSynchronize(d->stream));
+  RAI_CUDA(cudaMemcpyAsync(&e, m->err_dev, 4, cudaMemcpyDeviceToHost, s));
+  RAI_CUDA(cudaStreamSynchronize(s));
   if (e) {
-    cudaMemsetAsync(d->m->err_dev, 0, 4, d->stream);
+    cudaMemsetAsync(m->err_dev, 0, 4, s);
+    cudaStreamSynchronize(s);
     if (e & rai::kErrWaitTimeout) return fail(RAI_ERR_TIMEOUT, "a device-side wait timed out");
     return fail(RAI_ERR_INVALID, "device kernel rejected its input (token id out of range)");
   }
@@ -389,37 +499,35 @@ int validate_cfg(const rai_lookup_cfg* cfg) {
                 "prompt-lookup decoding requires finite temperature, top_k=0, top_p=1, and repetition_penalty=1");
   if (cfg->temperature != 0.f)
     return fail(RAI_ERR_UNSUPPORTED, "sampled acceptance (temperature > 0); this build runs greedy (temperature 0)");
-  if (cfg->max_draft + 1 > (uint32_t)rai::kMaxRows)
-    return fail(RAI_ERR_INVALID, "max_draft exceeds 32");
+  if (cfg->max_draft + 1 > (uint32_t)rai::kMaxRowsPerStream) return fail(RAI_ERR_INVALID, "max_draft exceeds 32");
   return RAI_OK;
 }
 
-int ensure_graph(rai_dec* d, const rai_lookup_cfg* cfg) {
+int ensure_graph(Batch* B, const rai_lookup_cfg* cfg) {
   uint32_t key[3] = {cfg->max_draft, cfg->max_ngram, cfg->min_ngram};
-  if (d->graph && std::memcmp(key, d->graph_key, sizeof(key)) == 0) return RAI_OK;
-  if (d->graph) {
-    cudaGraphExecDestroy(d->graph);
-    d->graph = nullptr;
+  if (B->graph && std::memcmp(key, B->graph_key, sizeof(key)) == 0) return RAI_OK;
+  if (B->graph) {
+    cudaGraphExecDestroy(B->graph);
+    B->graph = nullptr;
   }
-  const int rows = (int)cfg->max_draft + 1;
-  cudaStream_t s = d->stream;
+  const int R = (int)cfg->max_draft + 1;
+  const int rows = B->n * R;
+  if (rows > B->rows_cap) return fail(RAI_ERR_INVALID, "batch row budget exceeded");
+  cudaStream_t s = B->stream;
   cudaGraph_t g = nullptr;
   RAI_CUDA(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal));
   int rc = RAI_OK;
   do {
-    if (cudaSuccess != rai::launch_ngram(d->ctx_dev, d->st_dev, (int)cfg->max_draft, (int)cfg->max_ngram,
-                                         (int)cfg->min_ngram, d->max_ctx, s)) {
-      rc = fail(RAI_ERR_DEVICE, "ngram launch failed");
+    if (cudaSuccess != rai::launch_ngram(B->ctx, B->ctx_cap, B->st, B->kv, B->n, (int)cfg->max_draft,
+                                         (int)cfg->max_ngram, (int)cfg->min_ngram, s) ||
+        cudaSuccess != rai::launch_plan(B->st, B->n, B->rows, B->ids, B->m_active, B->best, rows, s)) {
+      rc = fail(RAI_ERR_DEVICE, "draft launch failed");
       break;
     }
-    rc = forward(d, rows, &d->st_dev->n_rows, &d->st_dev->pos, 0, d->st_dev->tokens, true);
+    rc = forward(B, rows, B->m_active, true);
     if (rc) break;
-    if (cudaSuccess != rai::launch_argmax(d->logits, d->m->cfg.vocab_size, &d->st_dev->n_rows, rows,
-                                          d->st_dev->amax, s)) {
-      rc = fail(RAI_ERR_DEVICE, "argmax launch failed");
-      break;
-    }
-    if (cudaSuccess != rai::launch_accept(d->st_dev, d->filled_dev, d->m->cfg.num_layers, s)) {
+    if (cudaSuccess != rai::launch_argmax(B->logits, B->m->cfg.vocab_size, B->m_active, rows, B->best, s) ||
+        cudaSuccess != rai::launch_accept(B->st, B->n, B->best, s)) {
       rc = fail(RAI_ERR_DEVICE, "accept launch failed");
       break;
     }
@@ -427,6 +535,7 @@ int ensure_graph(rai_dec* d, const rai_lookup_cfg* cfg) {
   cudaError_t ce = cudaStreamEndCapture(s, &g);
   if (rc) {
     if (g) cudaGraphDestroy(g);
+    (void)cudaGetLastError();
     return rc;
   }
   if (ce != cudaSuccess) return fail(RAI_ERR_DEVICE, std::string("graph capture: ") + cudaGetErrorString(ce));
@@ -434,25 +543,100 @@ int ensure_graph(rai_dec* d, const rai_lookup_cfg* cfg) {
   cudaGraphGetNodes(g, nullptr, &nnodes);
   std::vector<cudaGraphNode_t> nodes(nnodes);
   cudaGraphGetNodes(g, nodes.data(), &nnodes);
-  d->graph_kernels = 0;
+  B->graph_kernels = 0;
   for (auto nd : nodes) {
     cudaGraphNodeType ty;
-    if (cudaGraphNodeGetType(nd, &ty) == cudaSuccess && ty == cudaGraphNodeTypeKernel) ++d->graph_kernels;
+    if (cudaGraphNodeGetType(nd, &ty) == cudaSuccess && ty == cudaGraphNodeTypeKernel) ++B->graph_kernels;
   }
-  cudaError_t ie = cudaGraphInstantiate(&d->graph, g, 0);
+  cudaError_t ie = cudaGraphInstantiate(&B->graph, g, 0);
   cudaGraphDestroy(g);
   if (ie != cudaSuccess) return fail(RAI_ERR_DEVICE, std::string("graph instantiate: ") + cudaGetErrorString(ie));
-  std::memcpy(d->graph_key, key, sizeof(key));
+  std::memcpy(B->graph_key, key, sizeof(key));
   return RAI_OK;
 }
 
-int alloc_act(rai_dec* d, ActBuf* a, int tok, int cols, int gs) {
-  a->tok_alloc = (int)rai::round_up(tok, 8);
-  a->groups = (int)rai::ceil_div(cols, gs);
-  return d->alloc(&a->data, ActBuf::bytes(a->tok_alloc, a->groups));
+// One lookup step for every stream of the batch.
+int step_batch(Batch* B, const size_t* pos, const uint32_t* const* ctx, const size_t* ctx_len,
+               const rai_lookup_cfg* cfg, uint32_t* out_tokens, size_t out_cap, size_t* n_out,
+               rai_lookup_metrics* metrics) {
+  if (int rc = validate_cfg(cfg)) return rc;
+  if (out_cap < cfg->max_draft + 1) return fail(RAI_ERR_INVALID, "out_tokens capacity below max_draft + 1");
+  const Config& c = B->m->cfg;
+  for (int i = 0; i < B->n; ++i) {
+    rai_dec* d = B->decs[i];
+    if (!ctx[i]) return fail(RAI_ERR_INVALID, "null context");
+    if (ctx_len[i] == 0) return fail(RAI_ERR_INVALID, "prompt-lookup step requires a non-empty context");
+    if (pos[i] >= (size_t)d->max_ctx) return fail(RAI_ERR_INVALID, "decode position exceeds the context window");
+    if (ctx_len[i] > (size_t)d->max_ctx) return fail(RAI_ERR_INVALID, "context longer than the window");
+    if (pos[i] > d->filled[0]) return fail(RAI_ERR_INVALID, "KV store would leave a gap");
+    for (size_t t = 0; t < ctx_len[i]; ++t)
+      if (ctx[i][t] >= c.vocab_size)
+        return fail(RAI_ERR_INVALID, "context contains a token outside the model vocabulary");
+  }
+  if (int rc = ensure_graph(B, cfg)) return rc;
+  for (int i = 0; i < B->n; ++i) {
+    std::memcpy(B->ctx_host + (size_t)i * B->ctx_cap, ctx[i], ctx_len[i] * 4);
+    B->st_host[i].pos = (int)pos[i];
+    B->st_host[i].ctx_len = (int)ctx_len[i];
+  }
+  cudaStream_t s = B->stream;
+  size_t max_len = 0;
+  for (int i = 0; i < B->n; ++i) max_len = std::max(max_len, ctx_len[i]);
+  if (B->n == 1) {
+    RAI_CUDA(cudaMemcpyAsync(B->ctx, B->ctx_host, ctx_len[0] * 4, cudaMemcpyHostToDevice, s));
+  } else {
+    RAI_CUDA(cudaMemcpyAsync(B->ctx, B->ctx_host, (size_t)B->n * B->ctx_cap * 4, cudaMemcpyHostToDevice, s));
+  }
+  RAI_CUDA(cudaMemcpyAsync(B->st, B->st_host, B->n * sizeof(rai::StreamStep), cudaMemcpyHostToDevice, s));
+  RAI_CUDA(cudaEventRecord(B->ev0, s));
+  RAI_CUDA(cudaGraphLaunch(B->graph, s));
+  RAI_CUDA(cudaEventRecord(B->ev1, s));
+  RAI_CUDA(cudaMemcpyAsync(B->st_host, B->st, B->n * sizeof(rai::StreamStep), cudaMemcpyDeviceToHost, s));
+  if (int rc = check_err(B->m, s)) return rc;
+  float ms = 0.f;
+  cudaEventElapsedTime(&ms, B->ev0, B->ev1);
+  B->last_us = ms * 1000.f;
+  for (int i = 0; i < B->n; ++i) {
+    const rai::StreamStep& st = B->st_host[i];
+    n_out[i] = (size_t)st.produced;
+    for (int t = 0; t < st.produced; ++t) out_tokens[i * out_cap + t] = st.out[t];
+    for (auto& f : B->decs[i]->filled) f = pos[i] + st.produced;
+    B->decs[i]->last_us = B->last_us;
+    B->decs[i]->last_kernels = B->graph_kernels;
+    if (metrics) {
+      metrics[i].accepted = st.accepted;
+      metrics[i].drafted = st.drafted;
+      metrics[i].produced = st.produced;
+      metrics[i].matched_ngram = st.ngram;
+      metrics[i].accept_rate = st.drafted ? (float)st.accepted / (float)st.drafted : 0.f;
+    }
+  }
+  return RAI_OK;
+}
+
+// Forward `rows` tokens of a single decoder at positions start.. (prefill or
+// logits), through its own batch.
+int forward_solo(rai_dec* d, const uint32_t* ids, size_t start, int rows, bool logits) {
+  Batch* B = d->solo.get();
+  for (int b = 0; b < rows; ++b) B->rows_host[b] = rai::RowInfo{(int)(start + b), 0};
+  cudaStream_t s = B->stream;
+  RAI_CUDA(cudaMemcpyAsync(B->ids, ids, rows * 4, cudaMemcpyHostToDevice, s));
+  RAI_CUDA(cudaMemcpyAsync(B->rows, B->rows_host, rows * sizeof(rai::RowInfo), cudaMemcpyHostToDevice, s));
+  return forward(B, rows, nullptr, logits);
 }
 
 }  // namespace
+
+rai_dec::~rai_dec() {
+  drop_batches_of(this);
+  solo.reset();
+  int prev = 0;
+  cudaGetDevice(&prev);
+  cudaSetDevice(m->device);
+  if (kc) cudaFree(kc);
+  if (vc) cudaFree(vc);
+  cudaSetDevice(prev);
+}
 
 // ===========================================================================
 extern "C" {
@@ -553,7 +737,10 @@ int rai_gpu_model_create(const uint8_t* blob, size_t len, int device, rai_model*
   return RAI_OK;
 }
 
+
 int rai_gpu_model_destroy(rai_model* model) {
+  if (!model) return RAI_OK;
+  drop_batches_of_model(model);
   delete model;
   return RAI_OK;
 }
@@ -589,43 +776,19 @@ int rai_gpu_decoder_create(rai_model* m, size_t max_ctx, rai_dec** out) {
   auto d = std::make_unique<rai_dec>();
   d->m = m;
   d->max_ctx = (int)ctx;
-  d->n_alloc = (int)rai::round_up(ctx, 4);
-  d->mcap = (int)std::max<size_t>(rai::kMaxRows, std::min<size_t>(256, ctx));
-  RAI_CUDA(cudaStreamCreateWithFlags(&d->stream, cudaStreamNonBlocking));
-  RAI_CUDA(cudaEventCreate(&d->ev0));
-  RAI_CUDA(cudaEventCreate(&d->ev1));
   size_t kv = (size_t)c.num_layers * c.num_kv_heads * ctx * c.head_dim * sizeof(float);
-  if (int rc = d->alloc(&d->kc, kv)) return rc;
-  if (int rc = d->alloc(&d->vc, kv)) return rc;
+  void* p = nullptr;
+  cudaError_t e = cudaMalloc(&p, kv);
+  if (e != cudaSuccess) return fail(RAI_ERR_OOM, "cannot allocate the KV cache");
+  d->kc = static_cast<float*>(p);
+  e = cudaMalloc(&p, kv);
+  if (e != cudaSuccess) return fail(RAI_ERR_OOM, "cannot allocate the KV cache");
+  d->vc = static_cast<float*>(p);
   RAI_CUDA(cudaMemset(d->kc, 0, kv));
   RAI_CUDA(cudaMemset(d->vc, 0, kv));
-  if (int rc = d->alloc(&d->filled_dev, c.num_layers * sizeof(int))) return rc;
-  RAI_CUDA(cudaMemset(d->filled_dev, 0, c.num_layers * sizeof(int)));
   d->filled.assign(c.num_layers, 0);
-  const size_t R = d->mcap, h = c.hidden_size, qd = c.q_dim(), kvd = c.kv_dim(), ff = c.intermediate_size;
-  if (int rc = d->alloc(&d->hidden, R * h * 4)) return rc;
-  if (int rc = d->alloc(&d->resid, R * h * 4)) return rc;
-  if (int rc = d->alloc(&d->normed, R * h * 4)) return rc;
-  if (int rc = d->alloc(&d->qkv, R * (qd + 2 * kvd) * 4)) return rc;
-  if (int rc = d->alloc(&d->q, R * qd * 4)) return rc;
-  if (int rc = d->alloc(&d->attn, R * qd * 4)) return rc;
-  if (int rc = d->alloc(&d->gu, R * 2 * ff * 4)) return rc;
-  if (int rc = d->alloc(&d->ff, R * ff * 4)) return rc;
-  if (int rc = d->alloc(&d->logits, (size_t)rai::kMaxRows * c.vocab_size * 4)) return rc;
-  if (int rc = alloc_act(d.get(), &d->act_h, (int)R, (int)h, c.group_size)) return rc;
-  if (int rc = alloc_act(d.get(), &d->act_q, (int)R, (int)qd, c.group_size)) return rc;
-  if (int rc = alloc_act(d.get(), &d->act_ff, (int)R, (int)ff, c.group_size)) return rc;
-  int hgs = m->head.wbits == 8 ? (int)c.embed_group_size : (int)c.group_size;
-  if (int rc = alloc_act(d.get(), &d->act_head, rai::kMaxRows, (int)h, hgs)) return rc;
-  if (int rc = d->alloc(&d->ids_dev, R * 4)) return rc;
-  if (int rc = d->alloc(&d->ctx_dev, ctx * 4)) return rc;
-  if (int rc = d->alloc(&d->st_dev, sizeof(rai::StepState))) return rc;
-  RAI_CUDA(cudaMemset(d->st_dev, 0, sizeof(rai::StepState)));
-  RAI_CUDA(cudaMallocHost(&d->ctx_host, ctx * 4));
-  RAI_CUDA(cudaMallocHost(&d->st_host, sizeof(rai::StepState)));
-  size_t attn_smem = rai::attention_smem_bytes(c.head_dim, c.num_heads / c.num_kv_heads, d->n_alloc);
-  if (attn_smem > rai::kAttnMaxSmem)
-    return fail(RAI_ERR_UNSUPPORTED, "context window too long for the single-pass attention kernel");
+  int rows_cap = (int)std::max<size_t>(rai::kMaxRowsPerStream, std::min<size_t>(256, ctx));
+  if (int rc = create_batch(m, {d.get()}, rai::kMaxRowsPerStream, rows_cap, &d->solo)) return rc;
   *out = d.release();
   return RAI_OK;
 }
@@ -645,92 +808,73 @@ int rai_gpu_prefill(rai_dec* d, const uint32_t* ids, size_t n, size_t* pos_out) 
   DeviceGuard guard(d->m->device);
   size_t m = n - 1;
   *pos_out = m;
-  if (m == 0) return RAI_OK;
-  for (size_t start = 0; start < m; start += d->mcap) {
-    int rows = (int)std::min<size_t>(d->mcap, m - start);
+  Batch* B = d->solo.get();
+  for (size_t start = 0; start < m; start += B->rows_cap) {
+    int rows = (int)std::min<size_t>(B->rows_cap, m - start);
     if (start > d->filled[0]) return fail(RAI_ERR_INVALID, "KV store would leave a gap");
-    RAI_CUDA(cudaMemcpyAsync(d->ids_dev, ids + start, rows * 4, cudaMemcpyHostToDevice, d->stream));
-    if (int rc = forward(d, rows, nullptr, nullptr, (int)start, d->ids_dev, false)) return rc;
-    if (int rc = check_err(d)) return rc;
+    if (int rc = forward_solo(d, ids + start, start, rows, false)) return rc;
+    if (int rc = check_err(d->m, B->stream)) return rc;
     for (auto& f : d->filled) f = std::max(f, start + rows);
   }
-  std::vector<int> fd(d->filled.begin(), d->filled.end());
-  RAI_CUDA(cudaMemcpy(d->filled_dev, fd.data(), fd.size() * 4, cudaMemcpyHostToDevice));
   return RAI_OK;
 }
 
 int rai_gpu_forward_logits(rai_dec* d, const uint32_t* ids, size_t start_pos, size_t batch, float* logits) {
   if (!d || !ids || batch == 0) return fail(RAI_ERR_INVALID, "bad argument");
   const Config& c = d->m->cfg;
-  if (batch > (size_t)rai::kMaxRows) return fail(RAI_ERR_INVALID, "batch exceeds 33 rows");
+  if (batch > (size_t)rai::kMaxRowsPerStream) return fail(RAI_ERR_INVALID, "batch exceeds 33 rows");
   if (start_pos + batch > (size_t)d->max_ctx || start_pos + batch > c.max_context)
     return fail(RAI_ERR_INVALID, "batch position exceeds model context");
   if (start_pos > d->filled[0]) return fail(RAI_ERR_INVALID, "KV store would leave a gap");
   for (size_t i = 0; i < batch; ++i)
     if (ids[i] >= c.vocab_size) return fail(RAI_ERR_INVALID, "token id is out of model vocabulary");
   DeviceGuard guard(d->m->device);
-  RAI_CUDA(cudaMemcpyAsync(d->ids_dev, ids, batch * 4, cudaMemcpyHostToDevice, d->stream));
-  if (int rc = forward(d, (int)batch, nullptr, nullptr, (int)start_pos, d->ids_dev, true)) return rc;
+  Batch* B = d->solo.get();
+  if (int rc = forward_solo(d, ids, start_pos, (int)batch, true)) return rc;
   if (logits)
-    RAI_CUDA(cudaMemcpyAsync(logits, d->logits, batch * c.vocab_size * 4, cudaMemcpyDeviceToHost, d->stream));
-  if (int rc = check_err(d)) return rc;
+    RAI_CUDA(cudaMemcpyAsync(logits, B->logits, batch * c.vocab_size * 4, cudaMemcpyDeviceToHost, B->stream));
+  if (int rc = check_err(d->m, B->stream)) return rc;
   for (auto& f : d->filled) f = std::max(f, start_pos + batch);
-  std::vector<int> fd(d->filled.begin(), d->filled.end());
-  RAI_CUDA(cudaMemcpy(d->filled_dev, fd.data(), fd.size() * 4, cudaMemcpyHostToDevice));
   return RAI_OK;
 }
 
 int rai_gpu_step(rai_dec* d, size_t pos, const uint32_t* ctx, size_t ctx_len, const rai_lookup_cfg* cfg,
                  uint32_t* out_tokens, size_t out_cap, size_t* n_out, rai_lookup_metrics* metrics) {
   if (!d || !ctx || !out_tokens || !n_out) return fail(RAI_ERR_INVALID, "null argument");
-  if (int rc = validate_cfg(cfg)) return rc;
-  if (ctx_len == 0) return fail(RAI_ERR_INVALID, "prompt-lookup step requires a non-empty context");
-  if (pos >= (size_t)d->max_ctx) return fail(RAI_ERR_INVALID, "decode position exceeds the context window");
-  if (ctx_len > (size_t)d->max_ctx) return fail(RAI_ERR_INVALID, "context longer than the window");
-  if (out_cap < cfg->max_draft + 1) return fail(RAI_ERR_INVALID, "out_tokens capacity below max_draft + 1");
-  if (pos > d->filled[0]) return fail(RAI_ERR_INVALID, "KV store would leave a gap");
-  const Config& c = d->m->cfg;
-  for (size_t i = 0; i < ctx_len; ++i)
-    if (ctx[i] >= c.vocab_size) return fail(RAI_ERR_INVALID, "context contains a token outside the model vocabulary");
   DeviceGuard guard(d->m->device);
-  if (int rc = ensure_graph(d, cfg)) return rc;
-  std::memcpy(d->ctx_host, ctx, ctx_len * 4);
-  d->st_host->pos = (int)pos;
-  d->st_host->ctx_len = (int)ctx_len;
-  cudaStream_t s = d->stream;
-  RAI_CUDA(cudaEventRecord(d->ev0, s));
-  RAI_CUDA(cudaMemcpyAsync(d->ctx_dev, d->ctx_host, ctx_len * 4, cudaMemcpyHostToDevice, s));
-  RAI_CUDA(cudaMemcpyAsync(d->st_dev, d->st_host, 2 * sizeof(int), cudaMemcpyHostToDevice, s));
-  RAI_CUDA(cudaGraphLaunch(d->graph, s));
-  RAI_CUDA(cudaMemcpyAsync(d->st_host, d->st_dev, sizeof(rai::StepState), cudaMemcpyDeviceToHost, s));
-  RAI_CUDA(cudaEventRecord(d->ev1, s));
-  if (int rc = check_err(d)) return rc;
-  cudaEventElapsedTime(&d->last_us, d->ev0, d->ev1);
-  d->last_us *= 1000.f;
-  const rai::StepState& st = *d->st_host;
-  *n_out = (size_t)st.produced;
-  for (int i = 0; i < st.produced; ++i) out_tokens[i] = st.out[i];
-  for (auto& f : d->filled) f = pos + st.produced;
-  if (metrics) {
-    metrics->accepted = st.accepted;
-    metrics->drafted = st.drafted;
-    metrics->produced = st.produced;
-    metrics->matched_ngram = st.ngram;
-    metrics->accept_rate = st.drafted ? (float)st.accepted / (float)st.drafted : 0.f;
-  }
-  return RAI_OK;
+  const uint32_t* ctxs[1] = {ctx};
+  return step_batch(d->solo.get(), &pos, ctxs, &ctx_len, cfg, out_tokens, out_cap, n_out, metrics);
 }
 
 int rai_gpu_step_many(rai_dec* const* decs, size_t n, const size_t* pos, const uint32_t* const* ctx,
                       const size_t* ctx_len, const rai_lookup_cfg* cfg, uint32_t* out_tokens, size_t out_cap,
                       size_t* n_out, rai_lookup_metrics* metrics) {
-  if (!decs || !pos || !ctx || !ctx_len || !out_tokens || !n_out) return fail(RAI_ERR_INVALID, "null argument");
+  if (!decs || !pos || !ctx || !ctx_len || !out_tokens || !n_out || n == 0) return fail(RAI_ERR_INVALID, "null argument");
+  if (int rc = validate_cfg(cfg)) return rc;
+  rai_model* m = decs[0]->m;
   for (size_t i = 0; i < n; ++i) {
-    int rc = rai_gpu_step(decs[i], pos[i], ctx[i], ctx_len[i], cfg, out_tokens + i * out_cap, out_cap, n_out + i,
-                          metrics ? metrics + i : nullptr);
-    if (rc) return rc;
+    if (!decs[i] || decs[i]->m != m) return fail(RAI_ERR_INVALID, "step_many decoders must share one model");
+    for (size_t j = 0; j < i; ++j)
+      if (decs[j] == decs[i]) return fail(RAI_ERR_INVALID, "step_many decoder listed twice");
   }
-  return RAI_OK;
+  if (n == 1) return rai_gpu_step(decs[0], pos[0], ctx[0], ctx_len[0], cfg, out_tokens, out_cap, n_out, metrics);
+  DeviceGuard guard(m->device);
+  std::vector<rai_dec*> key(decs, decs + n);
+  const int R = (int)cfg->max_draft + 1;
+  Batch* B = nullptr;
+  {
+    std::lock_guard<std::mutex> lk(g_batch_mu);
+    for (auto& e : g_batches)
+      if (e.first == m && e.second->decs == key && e.second->R >= R) B = e.second.get();
+  }
+  if (!B) {
+    std::unique_ptr<Batch> nb;
+    if (int rc = create_batch(m, key, R, (int)n * R, &nb)) return rc;
+    B = nb.get();
+    std::lock_guard<std::mutex> lk(g_batch_mu);
+    g_batches.emplace_back(m, std::move(nb));
+  }
+  return step_batch(B, pos, ctx, ctx_len, cfg, out_tokens, out_cap, n_out, metrics);
 }
 
 int rai_gpu_kv_filled(const rai_dec* d, size_t layer, size_t* filled) {
@@ -743,9 +887,6 @@ int rai_gpu_kv_filled(const rai_dec* d, size_t layer, size_t* filled) {
 int rai_gpu_kv_truncate(rai_dec* d, size_t len) {
   if (!d) return fail(RAI_ERR_INVALID, "null argument");
   for (auto& f : d->filled) f = std::min(f, len);
-  std::vector<int> fd(d->filled.begin(), d->filled.end());
-  DeviceGuard guard(d->m->device);
-  RAI_CUDA(cudaMemcpy(d->filled_dev, fd.data(), fd.size() * 4, cudaMemcpyHostToDevice));
   return RAI_OK;
 }
 
@@ -763,7 +904,7 @@ int rai_gpu_kv_read(const rai_dec* d, size_t layer, size_t kvh, size_t pos, floa
 
 int rai_gpu_step_kernel_count(const rai_dec* d, size_t* kernels) {
   if (!d || !kernels) return fail(RAI_ERR_INVALID, "null argument");
-  *kernels = d->graph ? d->graph_kernels : 0;
+  *kernels = d->last_kernels;
   return RAI_OK;
 }
 

@@ -158,3 +158,34 @@ def test_window_end_caps_the_draft(tiny_model_paths, oracle):
         assert pos + gmet.produced <= 44
         ctx += gt
         pos += len(gt)
+
+
+@pytest.mark.parametrize("name", ["tiny-llama", "tiny-qwen", "tiny-untied"])
+def test_step_many_matches_independent_oracle_streams(tiny_model_paths, oracle, name):
+    """step_many batches several streams' verify rows into one forward; each
+    stream must still match its own oracle decoder step for step."""
+    import rai_b200
+    gm = rai_b200.RaiModel.load(tiny_model_paths[name])
+    om = oracle.Model.load(tiny_model_paths[name])
+    vocab = gm.config["vocab_size"]
+    n = 5
+    gds = [rai_b200.LookupDecoder(gm, 200 + 8 * i) for i in range(n)]
+    ods = [oracle.Decoder(om, 200 + 8 * i) for i in range(n)]
+    ctxs, poss = [], []
+    for i in range(n):
+        prompt = periodic_prompt(24 + 7 * i, vocab, seed=100 + i)
+        p = gds[i].prefill(prompt)
+        assert p == ods[i].prefill(prompt)
+        ctxs.append(list(prompt))
+        poss.append(p)
+    cfg = rai_b200.LookupConfig(max_draft=6, max_ngram=3, min_ngram=1)
+    for _ in range(10):
+        toks, mets = rai_b200.step_many(gds, poss, ctxs, cfg)
+        for i in range(n):
+            ot, om_ = ods[i].step(poss[i], ctxs[i], 6)
+            assert toks[i] == ot, (i, poss[i], toks[i], ot)
+            assert (mets[i].accepted, mets[i].drafted, mets[i].produced) == \
+                (om_["accepted"], om_["drafted"], om_["produced"])
+            ctxs[i] += toks[i]
+            poss[i] += len(toks[i])
+            assert gds[i].kv_filled(0) == poss[i] == ods[i].kv_filled(0)
