@@ -155,6 +155,14 @@ RAI_API int rai_gpu_w4a8_quantize(const float* input, size_t cols, size_t tokens
 RAI_API int rai_gpu_w4a8_matmul_prequant(float* out, const void* packed, const void* scratch, size_t rows,
                                          size_t cols, size_t tokens, size_t group_size, void* stream);
 
+/* Attention of rai-infer's attention_head_avx2 (rai-infer/src/layers.rs:
+ * 1266-1380) for M query rows over one cache: q [M][nh*hd], k and v
+ * [nkv][max_ctx][hd], row r attends positions 0..positions[r] (host array);
+ * out [M][nh*hd]. Device pointers except `positions`. */
+RAI_API int rai_gpu_attention(const float* q, const float* k, const float* v, const int* positions, size_t M,
+                              size_t nh, size_t nkv, size_t hd, size_t max_ctx, float scale, float* out,
+                              void* stream);
+
 /* Number of kernels one rai_gpu_step replays (the captured CUDA graph's
  * kernel nodes for the decoder's current configuration; 0 before the first
  * step). */

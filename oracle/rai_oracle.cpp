@@ -558,6 +558,41 @@ void orc_attention_head(const float* q, float* out, const float* k_head, const f
   }
 }
 
+// attention_head_avx2 with its intermediates exposed (test diagnostics):
+// e[t] = the exponentials before normalisation, *max and *sum.
+void orc_attention_head_debug(const float* q, float* out, const float* k_head, const float* v_head, size_t pos,
+                              size_t hd, float scale, float* e, float* mx, float* sum) {
+  size_t chunks8 = hd / 8, n_pos = pos + 1;
+  std::vector<float> scores(n_pos);
+  float max_score = -INFINITY;
+  for (size_t t = 0; t < n_pos; ++t) {
+    const float* k = k_head + t * hd;
+    __m256 acc = _mm256_setzero_ps();
+    for (size_t c = 0; c < chunks8; ++c)
+      acc = _mm256_fmadd_ps(_mm256_loadu_ps(q + c * 8), _mm256_loadu_ps(k + c * 8), acc);
+    float sc = hsum8(acc) * scale;
+    scores[t] = sc;
+    if (sc > max_score) max_score = sc;
+  }
+  *mx = max_score;
+  __m256 max_v = _mm256_set1_ps(max_score), sum_acc = _mm256_setzero_ps();
+  size_t c8 = n_pos / 8;
+  for (size_t i = 0; i < c8; ++i) {
+    __m256 ev = schraudolph(_mm256_sub_ps(_mm256_loadu_ps(scores.data() + i * 8), max_v));
+    _mm256_storeu_ps(scores.data() + i * 8, ev);
+    sum_acc = _mm256_add_ps(sum_acc, ev);
+  }
+  float s = hsum8(sum_acc);
+  for (size_t t = c8 * 8; t < n_pos; ++t) {
+    float v = expf(scores[t] - max_score);
+    scores[t] = v;
+    s += v;
+  }
+  *sum = s;
+  for (size_t t = 0; t < n_pos; ++t) e[t] = scores[t];
+  orc_attention_head(q, out, k_head, v_head, pos, hd, scale, 0.f);
+}
+
 // route_experts (layers.rs:1808-1870) with dot_f32 (iterator sum from -0.0).
 void orc_route_experts(const float* hidden, const float* router, size_t ne, size_t width, size_t k,
                        int norm_topk, uint32_t* experts, float* weights) {

@@ -39,6 +39,8 @@ void orc_rope_apply(float* heads, size_t num_heads, size_t head_dim, const float
 void orc_silu_mul(float* gate, const float* up, size_t n);
 void orc_attention_head(const float* q, float* out, const float* k_head, const float* v_head,
                         size_t pos, size_t head_dim, float scale, float softcap);
+void orc_attention_head_debug(const float* q, float* out, const float* k_head, const float* v_head, size_t pos,
+                              size_t head_dim, float scale, float* e, float* mx, float* sum);
 void orc_route_experts(const float* hidden, const float* router, size_t num_experts,
                        size_t width, size_t top_k, int norm_topk, uint32_t* experts,
                        float* weights);

@@ -205,6 +205,8 @@ __global__ void __launch_bounds__(kScoreChunk) attn_scores_kernel(
   __syncthreads();
   const StreamKV sk_ = kv[ri.stream];
   const int t = t0 + tid;
+  // Per-thread maxima stay in registers: every loop over the (at most 8)
+  // heads of the group is fully unrolled with a guard.
   float tmax[8];
 #pragma unroll
   for (int h = 0; h < 8; ++h) tmax[h] = -INFINITY;
@@ -217,27 +219,33 @@ __global__ void __launch_bounds__(kScoreChunk) attn_scores_kernel(
       float4 v = __ldg(kp + i);
       kr[4 * i] = v.x; kr[4 * i + 1] = v.y; kr[4 * i + 2] = v.z; kr[4 * i + 3] = v.w;
     }
-    for (int h = 0; h < hpk; ++h) {
-      const float* qh = sq + h * HD;
-      float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-      for (int cc = 0; cc < HD / 8; ++cc)
+    for (int h = 0; h < 8; ++h) {
+      if (h < hpk) {
+        const float* qh = sq + h * HD;
+        float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-        for (int jj = 0; jj < 8; ++jj) acc[jj] = __fmaf_rn(qh[8 * cc + jj], kr[8 * cc + jj], acc[jj]);
-      float sv = __fmul_rn(hsum8(acc), scale);
-      if (softcap > 0.f) sv = __fmul_rn(softcap, tanhf(__fdiv_rn(sv, softcap)));
-      scores[((size_t)j * nh + kvh * hpk + h) * n_alloc + t] = sv;
-      tmax[h] = sv;
+        for (int cc = 0; cc < HD / 8; ++cc)
+#pragma unroll
+          for (int jj = 0; jj < 8; ++jj) acc[jj] = __fmaf_rn(qh[8 * cc + jj], kr[8 * cc + jj], acc[jj]);
+        float sv = __fmul_rn(hsum8(acc), scale);
+        if (softcap > 0.f) sv = __fmul_rn(softcap, tanhf(__fdiv_rn(sv, softcap)));
+        scores[((size_t)j * nh + kvh * hpk + h) * n_alloc + t] = sv;
+        tmax[h] = sv;
+      }
     }
   }
-  for (int h = 0; h < hpk; ++h) {
+#pragma unroll
+  for (int h = 0; h < 8; ++h) {
     float m = tmax[h];
+#pragma unroll
     for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
     if (lane == 0) red[h][warp] = m;
   }
   __syncthreads();
   if (tid < hpk) {
     float m = red[tid][0];
+#pragma unroll
     for (int w = 1; w < kScoreChunk / 32; ++w) m = fmaxf(m, red[tid][w]);
     smax[((size_t)j * nh + kvh * hpk + tid) * n_chunks + chunk] = m;
   }
@@ -560,6 +568,22 @@ cudaError_t launch_attention(const float* q, float* out, const StreamKV* kv, int
       return cudaErrorInvalidValue;
   }
 #undef RAI_ATTN
+  return cudaGetLastError();
+}
+
+// Test diagnostics: the score pass alone (raw scores and per-chunk maxima).
+cudaError_t launch_attention_scores(const float* q, const StreamKV* kv, int layer, const RowInfo* rows, int M,
+                                    int nh, int nkv, int hd, float scale, float* scores, float* smax, int n_alloc,
+                                    cudaStream_t s) {
+  const int nch = (int)attention_n_chunks(n_alloc);
+  dim3 g1(nkv, M, nch);
+  switch (hd) {
+    case 16: attn_scores_kernel<16><<<g1, kScoreChunk, 0, s>>>(q, kv, layer, rows, nullptr, M, nh, nkv, scale, 0.f, scores, smax, n_alloc, nch); break;
+    case 32: attn_scores_kernel<32><<<g1, kScoreChunk, 0, s>>>(q, kv, layer, rows, nullptr, M, nh, nkv, scale, 0.f, scores, smax, n_alloc, nch); break;
+    case 64: attn_scores_kernel<64><<<g1, kScoreChunk, 0, s>>>(q, kv, layer, rows, nullptr, M, nh, nkv, scale, 0.f, scores, smax, n_alloc, nch); break;
+    case 128: attn_scores_kernel<128><<<g1, kScoreChunk, 0, s>>>(q, kv, layer, rows, nullptr, M, nh, nkv, scale, 0.f, scores, smax, n_alloc, nch); break;
+    default: return cudaErrorInvalidValue;
+  }
   return cudaGetLastError();
 }
 

@@ -66,6 +66,9 @@ cudaError_t launch_attention(const float* q, float* out, const StreamKV* kv, int
                              const int* m_dev, int M, int nh, int nkv, int hd, float scale, float softcap,
                              float* scores, float* smax, float* inv, int n_alloc, const ExpfTable& et,
                              cudaStream_t s);
+cudaError_t launch_attention_scores(const float* q, const StreamKV* kv, int layer, const RowInfo* rows, int M,
+                                    int nh, int nkv, int hd, float scale, float* scores, float* smax, int n_alloc,
+                                    cudaStream_t s);
 cudaError_t launch_swiglu(const float* gu, int ff, float* act, const int* m_dev, int M, const ExpfTable& et,
                           cudaStream_t s);
 cudaError_t launch_argmax(const float* logits, int vocab, const int* m_dev, int M, unsigned long long* best,

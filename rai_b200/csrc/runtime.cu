@@ -223,7 +223,16 @@ std::string lib_dir() {
   return ".";
 }
 
-int load_expf_table(rai_model* M) {
+// One table per device, loaded on first use and kept for the process.
+std::mutex g_expf_mu;
+std::vector<std::pair<int, rai::ExpfTable>> g_expf;
+
+int expf_table(rai::ExpfTable* out) {
+  int dev = 0;
+  RAI_CUDA(cudaGetDevice(&dev));
+  std::lock_guard<std::mutex> lk(g_expf_mu);
+  for (auto& e : g_expf)
+    if (e.first == dev) { *out = e.second; return RAI_OK; }
   const char* env = std::getenv("RAI_EXPF_TABLE");
   std::string path = env ? std::string(env) : lib_dir() + "/expf_exceptions.bin";
   std::ifstream f(path, std::ios::binary);
@@ -234,12 +243,15 @@ int load_expf_table(rai_model* M) {
   std::vector<uint32_t> kv(2 * (size_t)hdr[1]);
   f.read(reinterpret_cast<char*>(kv.data()), kv.size() * 4);
   if (!f) return fail(RAI_ERR_INVALID, "truncated expf table " + path);
-  uint32_t* dev = nullptr;
-  if (int rc = M->alloc(&dev, kv.size() * 4)) return rc;
-  RAI_CUDA(cudaMemcpy(dev, kv.data(), kv.size() * 4, cudaMemcpyHostToDevice));
-  M->expf.keys = dev;
-  M->expf.vals = dev + hdr[1];
-  M->expf.n = (int)hdr[1];
+  uint32_t* d = nullptr;
+  RAI_CUDA(cudaMalloc(&d, kv.size() * 4));
+  RAI_CUDA(cudaMemcpy(d, kv.data(), kv.size() * 4, cudaMemcpyHostToDevice));
+  rai::ExpfTable t;
+  t.keys = d;
+  t.vals = d + hdr[1];
+  t.n = (int)hdr[1];
+  g_expf.emplace_back(dev, t);
+  *out = t;
   return RAI_OK;
 }
 
@@ -674,7 +686,7 @@ int rai_gpu_model_create(const uint8_t* blob, size_t len, int device, rai_model*
   M->qk_mode = c.has_full_qk_norm ? 2 : (c.has_qk_norm ? 1 : 0);
   if (int rc = M->alloc(&M->err_dev, 4)) return rc;
   RAI_CUDA(cudaMemset(M->err_dev, 0, 4));
-  if (int rc = load_expf_table(M.get())) return rc;
+  if (int rc = expf_table(&M->expf)) return rc;
 
   // Upload the blob once; pack from the device copy, then release it.
   uint8_t* blob_dev = nullptr;
@@ -957,6 +969,57 @@ int rai_gpu_w4a8_matmul(float* out, const void* packed, const float* input, size
   w.tiles = (int)rai::ceil_div(rows, rai::kTileRows);
   w.wbits = 4;
   RAI_CUDA(rai::gemm_exact(w, a, (int)tokens, out, (int)rows, rai::GemmEpilogue{}, nullptr, s));
+  return RAI_OK;
+}
+
+int rai_gpu_attention(const float* q, const float* k, const float* v, const int* positions, size_t M, size_t nh,
+                      size_t nkv, size_t hd, size_t max_ctx, float scale, float* out, void* stream) {
+  if (!q || !k || !v || !positions || !out || M == 0) return fail(RAI_ERR_INVALID, "null argument");
+  if (nh % nkv || nh / nkv > 8 || (hd != 16 && hd != 32 && hd != 64 && hd != 128))
+    return fail(RAI_ERR_UNSUPPORTED, "attention shape");
+  for (size_t i = 0; i < M; ++i)
+    if (positions[i] < 0 || (size_t)positions[i] >= max_ctx) return fail(RAI_ERR_INVALID, "position out of range");
+  rai::ExpfTable et;
+  if (int rc = expf_table(&et)) return rc;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  RAI_CUDA(rai::init_layer_attributes());
+  int n_alloc = (int)rai::round_up(max_ctx, 4);
+  size_t nch = rai::attention_n_chunks(n_alloc);
+  std::vector<rai::RowInfo> rows(M);
+  for (size_t i = 0; i < M; ++i) rows[i] = rai::RowInfo{positions[i], 0};
+  rai::StreamKV kv{const_cast<float*>(k), const_cast<float*>(v), (int)max_ctx, 0};
+  char* buf = nullptr;
+  size_t need = M * sizeof(rai::RowInfo) + sizeof(kv) + M * nh * (n_alloc + nch + 1) * 4 + 256;
+  RAI_CUDA(cudaMalloc(&buf, need));
+  struct Free { char* p; ~Free() { cudaFree(p); } } fr{buf};
+  rai::RowInfo* rows_d = reinterpret_cast<rai::RowInfo*>(buf);
+  rai::StreamKV* kv_d = reinterpret_cast<rai::StreamKV*>(buf + M * sizeof(rai::RowInfo));
+  float* scores = reinterpret_cast<float*>(buf + rai::round_up(M * sizeof(rai::RowInfo) + sizeof(kv), 16));
+  float* smax = scores + M * nh * n_alloc;
+  float* inv = smax + M * nh * nch;
+  RAI_CUDA(cudaMemcpyAsync(rows_d, rows.data(), M * sizeof(rai::RowInfo), cudaMemcpyHostToDevice, s));
+  RAI_CUDA(cudaMemcpyAsync(kv_d, &kv, sizeof(kv), cudaMemcpyHostToDevice, s));
+  RAI_CUDA(rai::launch_attention(q, out, kv_d, 0, rows_d, nullptr, (int)M, (int)nh, (int)nkv, (int)hd, scale, 0.f,
+                                 scores, smax, inv, n_alloc, et, s));
+  RAI_CUDA(cudaStreamSynchronize(s));
+  if (const char* dbg = std::getenv("RAI_ATTN_DEBUG_DUMP")) {
+    // Test diagnostics: exponentials [M][nh][n_alloc] then 1/sum [M][nh].
+    std::vector<float> e(M * nh * n_alloc), iv(M * nh), raw(M * nh * n_alloc), mx(M * nh * nch);
+    cudaMemcpy(e.data(), scores, e.size() * 4, cudaMemcpyDeviceToHost);
+    cudaMemcpy(iv.data(), inv, iv.size() * 4, cudaMemcpyDeviceToHost);
+    rai::launch_attention_scores(q, kv_d, 0, rows_d, (int)M, (int)nh, (int)nkv, (int)hd, scale, scores, smax, n_alloc, s);
+    cudaStreamSynchronize(s);
+    cudaMemcpy(raw.data(), scores, raw.size() * 4, cudaMemcpyDeviceToHost);
+    cudaMemcpy(mx.data(), smax, mx.size() * 4, cudaMemcpyDeviceToHost);
+    FILE* f = std::fopen(dbg, "wb");
+    if (f) {
+      std::fwrite(e.data(), 4, e.size(), f);
+      std::fwrite(iv.data(), 4, iv.size(), f);
+      std::fwrite(raw.data(), 4, raw.size(), f);
+      std::fwrite(mx.data(), 4, mx.size(), f);
+      std::fclose(f);
+    }
+  }
   return RAI_OK;
 }
 
