@@ -243,9 +243,16 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--streams", type=int, default=STREAMS)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--gemm-only", action="store_true",
+                    help="time only the isolated verify GEMM (for a small ncu capture) and print it")
     args = ap.parse_args()
     if args.impl == "reference":
         return run_reference(args)
+    if args.gemm_only:
+        import torch
+        torch.cuda.set_device(0)
+        print(json.dumps(measure_gemm_roofline(torch, K_DRAFT + 1, iters=args.steps)), flush=True)
+        return
 
     import torch
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -275,13 +282,9 @@ def main():
     vocab = model.config["vocab_size"]
     mine = [s for s in range(args.streams) if s % world == rank]
     max_ctx = PROMPT + (args.steps + args.warmup + 2) * (K_DRAFT + 1) + 16
-    decs, ctxs, poss = [], [], []
-    for s in mine:
-        d = rai_b200.LookupDecoder(model, max_ctx)
-        prompt = make_prompt(1000 + s, PROMPT, vocab, COPY_FRAC)
-        poss.append(d.prefill(prompt))
-        ctxs.append(list(prompt))
-        decs.append(d)
+    decs = [rai_b200.LookupDecoder(model, max_ctx) for _ in mine]
+    ctxs = [make_prompt(1000 + s, PROMPT, vocab, COPY_FRAC) for s in mine]
+    poss = rai_b200.prefill_many(decs, ctxs)
     cfg = rai_b200.LookupConfig(max_draft=K_DRAFT, max_ngram=3, min_ngram=1)
 
     def one_step():

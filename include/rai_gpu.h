@@ -94,6 +94,11 @@ RAI_API int rai_gpu_decoder_destroy(rai_dec* dec);
  * token but the last through the model; *pos_out = n - 1. */
 RAI_API int rai_gpu_prefill(rai_dec* dec, const uint32_t* ids, size_t n, size_t* pos_out);
 
+/* rai_gpu_prefill for each of n decoders (sharing one model, empty caches),
+ * with all prompts' rows batched into shared forward passes. */
+RAI_API int rai_gpu_prefill_many(rai_dec* const* decs, size_t n, const uint32_t* const* ids,
+                                 const size_t* lens, size_t* pos_out);
+
 /* LookupDecoder::step (rai-infer/src/lookup.rs:260-425). `ctx` is the whole
  * token sequence; its last element lives at `pos`. Writes produced tokens to
  * out_tokens (capacity out_cap >= max_draft + 1), their count to *n_out, and

@@ -151,6 +151,18 @@ class LookupDecoder:
         return us.value
 
 
+def prefill_many(decoders: Sequence[LookupDecoder], prompts: Sequence[Sequence[int]]):
+    """LookupDecoder.prefill for each decoder, batched (rai_gpu_prefill_many)."""
+    n = len(decoders)
+    handles = (C.c_void_p * n)(*[d._h.value for d in decoders])
+    arrs = [_u32(p) for p in prompts]
+    ptrs = (C.c_void_p * n)(*[a.ctypes.data for a in arrs])
+    lens = (C.c_size_t * n)(*[a.size for a in arrs])
+    out = (C.c_size_t * n)()
+    check(native.lib().rai_gpu_prefill_many(handles, n, ptrs, lens, out))
+    return [int(v) for v in out]
+
+
 def step_many(decoders: Sequence[LookupDecoder], positions: Sequence[int], contexts: Sequence[Sequence[int]],
               config: LookupConfig):
     """One step for each decoder (rai_gpu_step_many)."""
@@ -171,4 +183,4 @@ def step_many(decoders: Sequence[LookupDecoder], positions: Sequence[int], conte
             [LookupMetrics._from_c(mets[i]) for i in range(n)])
 
 
-__all__ = ["RaiModel", "LookupDecoder", "LookupConfig", "LookupMetrics", "RaiError", "step_many"]
+__all__ = ["RaiModel", "LookupDecoder", "LookupConfig", "LookupMetrics", "RaiError", "step_many", "prefill_many"]

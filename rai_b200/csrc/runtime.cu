@@ -831,6 +831,58 @@ int rai_gpu_prefill(rai_dec* d, const uint32_t* ids, size_t n, size_t* pos_out) 
   return RAI_OK;
 }
 
+int rai_gpu_prefill_many(rai_dec* const* decs, size_t n, const uint32_t* const* ids, const size_t* lens,
+                         size_t* pos_out) {
+  if (!decs || !ids || !lens || !pos_out || n == 0) return fail(RAI_ERR_INVALID, "null argument");
+  rai_model* m = decs[0]->m;
+  const Config& c = m->cfg;
+  for (size_t i = 0; i < n; ++i) {
+    rai_dec* d = decs[i];
+    if (!d || d->m != m) return fail(RAI_ERR_INVALID, "prefill_many decoders must share one model");
+    for (size_t j = 0; j < i; ++j)
+      if (decs[j] == d) return fail(RAI_ERR_INVALID, "prefill_many decoder listed twice");
+    if (lens[i] == 0) return fail(RAI_ERR_INVALID, "prompt must contain at least one token");
+    if (!ids[i]) return fail(RAI_ERR_INVALID, "null prompt");
+    if (lens[i] > (size_t)d->max_ctx) return fail(RAI_ERR_INVALID, "prompt exceeds the prompt-lookup context window");
+    if (d->filled[0] != 0) return fail(RAI_ERR_INVALID, "prefill_many needs empty caches");
+    for (size_t t = 0; t + 1 < lens[i]; ++t)
+      if (ids[i][t] >= c.vocab_size) return fail(RAI_ERR_INVALID, "token id is out of model vocabulary");
+  }
+  DeviceGuard guard(m->device);
+  // All streams' prompt rows in order, cut into chunks of up to 2048 rows;
+  // a stream's earlier positions are always in an earlier chunk or earlier
+  // in the same chunk, whose K/V are stored before attention runs.
+  const int chunk = 2048;
+  std::unique_ptr<Batch> B;
+  if (int rc = create_batch(m, std::vector<rai_dec*>(decs, decs + n), 1, chunk, &B)) return rc;
+  std::vector<uint32_t> idbuf(chunk);
+  int r = 0;
+  auto flush = [&]() -> int {
+    if (r == 0) return RAI_OK;
+    cudaStream_t s = B->stream;
+    RAI_CUDA(cudaMemcpyAsync(B->ids, idbuf.data(), r * 4, cudaMemcpyHostToDevice, s));
+    RAI_CUDA(cudaMemcpyAsync(B->rows, B->rows_host, r * sizeof(rai::RowInfo), cudaMemcpyHostToDevice, s));
+    if (int rc = forward(B.get(), r, nullptr, false)) return rc;
+    if (int rc = check_err(m, s)) return rc;
+    r = 0;
+    return RAI_OK;
+  };
+  for (size_t i = 0; i < n; ++i) {
+    for (size_t t = 0; t + 1 < lens[i]; ++t) {
+      B->rows_host[r] = rai::RowInfo{(int)t, (int)i};
+      idbuf[r] = ids[i][t];
+      if (++r == chunk)
+        if (int rc = flush()) return rc;
+    }
+  }
+  if (int rc = flush()) return rc;
+  for (size_t i = 0; i < n; ++i) {
+    pos_out[i] = lens[i] - 1;
+    for (auto& f : decs[i]->filled) f = std::max(f, lens[i] - 1);
+  }
+  return RAI_OK;
+}
+
 int rai_gpu_forward_logits(rai_dec* d, const uint32_t* ids, size_t start_pos, size_t batch, float* logits) {
   if (!d || !ids || batch == 0) return fail(RAI_ERR_INVALID, "bad argument");
   const Config& c = d->m->cfg;

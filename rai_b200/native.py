@@ -73,6 +73,7 @@ def lib() -> C.CDLL:
         L.rai_gpu_decoder_create.argtypes = [P, SZ, C.POINTER(P)]
         L.rai_gpu_decoder_destroy.argtypes = [P]
         L.rai_gpu_prefill.argtypes = [P, P, SZ, PSZ]
+        L.rai_gpu_prefill_many.argtypes = [P, SZ, P, P, P]
         L.rai_gpu_step.argtypes = [P, SZ, P, SZ, C.POINTER(LookupCfg), P, SZ, PSZ, C.POINTER(LookupMetricsC)]
         L.rai_gpu_step_many.argtypes = [P, SZ, P, P, P, C.POINTER(LookupCfg), P, SZ, P, P]
         L.rai_gpu_kv_filled.argtypes = [P, SZ, PSZ]

@@ -189,3 +189,23 @@ def test_step_many_matches_independent_oracle_streams(tiny_model_paths, oracle, 
             ctxs[i] += toks[i]
             poss[i] += len(toks[i])
             assert gds[i].kv_filled(0) == poss[i] == ods[i].kv_filled(0)
+
+
+def test_prefill_many_matches_separate_prefills(tiny_model_paths, oracle):
+    import rai_b200
+    gm = rai_b200.RaiModel.load(tiny_model_paths["tiny-llama"])
+    om = oracle.Model.load(tiny_model_paths["tiny-llama"])
+    vocab = gm.config["vocab_size"]
+    prompts = [periodic_prompt(30 + 11 * i, vocab, seed=i) for i in range(4)]
+    gds = [rai_b200.LookupDecoder(gm, 256) for _ in prompts]
+    poss = rai_b200.prefill_many(gds, prompts)
+    assert poss == [len(p) - 1 for p in prompts]
+    for d, p in zip(gds, prompts):
+        od = oracle.Decoder(om, 256)
+        od.prefill(p)
+        assert d.kv_filled(0) == len(p) - 1
+        for layer in (0, 1):
+            for pos in (0, len(p) - 2):
+                gk, gv = d.kv_read(layer, 1, pos)
+                ok, ov = od.kv_read(layer, 1, pos)
+                assert np.array_equal(gk, ok) and np.array_equal(gv, ov)
