@@ -308,9 +308,13 @@ def main():
     tot = np.zeros(6)
     with ClockSampler(local) as clk:
         barrier()
+        # Profiler range (no effect unless run under a profiler started with
+        # capture off): limits a launch-list capture to the timed steps.
+        torch.cuda.profiler.start()
         for _ in range(args.steps):
             tot += np.array(one_step())
         barrier()
+        torch.cuda.profiler.stop()
     dev_s = tot[0] / 1e6
     stats = torch.tensor([dev_s, tot[1], tot[2], tot[3], tot[4], tot[5]], dtype=torch.float64, device="cuda")
     if dist:
