@@ -16,10 +16,12 @@ namespace rai {
 // Device-side error word (per model context): bit 0 = a bounded wait gave up.
 enum : uint32_t { kErrWaitTimeout = 1u, kErrBadInput = 2u };
 
-// A spin on an mbarrier or flag gives up after this many polls (each poll
-// after the first 64 sleeps ~256 ns, so the bound is ~0.5 s) and reports
-// kErrWaitTimeout instead of hanging the GPU.
-constexpr uint32_t kMaxPolls = 1u << 21;
+// A wait on an mbarrier gives up after kMaxPolls polls; each poll suspends
+// the warp in hardware until the phase completes or kSuspendNs elapse, so the
+// bound is ~0.5 s, after which the wait reports kErrWaitTimeout instead of
+// hanging the GPU.
+constexpr uint32_t kSuspendNs = 64 * 1024;
+constexpr uint32_t kMaxPolls = 8192;
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -47,10 +49,10 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
-      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n"
       " selp.u32 %0, 1, 0, p;\n}\n"
       : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(kSuspendNs)
       : "memory");
   return ok != 0;
 }
@@ -58,10 +60,8 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 // Bounded wait: returns false (and sets the error word) if the phase never
 // completes. Callers stop issuing work after a false return.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32_t* err) {
-  for (uint32_t i = 0; i < kMaxPolls; ++i) {
+  for (uint32_t i = 0; i < kMaxPolls; ++i)
     if (mbar_try_wait(bar, parity)) return true;
-    if (i > 64) __nanosleep(256);
-  }
   if (err) atomicOr(err, kErrWaitTimeout);
   return false;
 }

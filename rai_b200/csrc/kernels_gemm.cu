@@ -202,6 +202,39 @@ __device__ __forceinline__ void mma_u8s8(uint32_t a0, uint32_t a1, uint32_t b, i
       : "r"(a0), "r"(a1), "r"(b), "r"(kMagic));
 }
 
+// Packed pairs of f32 for the exact epilogue. mul.rn.f32x2 rounds each half
+// exactly like the scalar mul.rn (checked bit for bit on the device), and
+// sub.rn.f32x2 is only used for (12582912 + dot) - 12582912, which is exact
+// in any rounding mode. Accumulation stays scalar __fadd_rn: a packed
+// mul.rn.f32x2 -> add.rn.f32x2 chain did not reproduce the scalar rounding
+// on sm_100a, so packed adds are not used.
+__device__ __forceinline__ uint64_t f2(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ float2 f2_unpack(uint64_t v) {
+  float2 r;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(r.x), "=f"(r.y) : "l"(v));
+  return r;
+}
+__device__ __forceinline__ uint64_t sub2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ uint64_t mul2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+// acc[0..1] += exact_dot(d0, d1) * c, each term rounded as the reference.
+__device__ __forceinline__ void acc_pair(float* acc, int32_t d0, int32_t d1, uint64_t c, uint64_t magic2) {
+  const float2 pr = f2_unpack(mul2(sub2(f2(__int_as_float(d0), __int_as_float(d1)), magic2), c));
+  acc[0] = __fadd_rn(acc[0], pr.x);
+  acc[1] = __fadd_rn(acc[1], pr.y);
+}
+
 template <int WBITS, int NTILES>
 __global__ void __launch_bounds__(kThreads, NTILES >= 4 ? 1 : 2) gemm_exact_kernel(GemmParams p) {
   constexpr int NT = 8 * NTILES;  // token slots per pass
@@ -277,6 +310,7 @@ __global__ void __launch_bounds__(kThreads, NTILES >= 4 ? 1 : 2) gemm_exact_kern
   pdl_launch_dependents();
   const int gq = lane >> 2, tq = lane & 3;
   const int r0 = warp * 16 + gq;  // tile-local rows r0 and r0 + 8
+  const uint64_t magic2 = f2(kMagicF, kMagicF);
   float facc[NTILES][8][4];
   float zc[NTILES][4];
 #pragma unroll
@@ -338,16 +372,14 @@ __global__ void __launch_bounds__(kThreads, NTILES >= 4 ? 1 : 2) gemm_exact_kern
       const uint32_t B[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
       const float2 xa = XS[n * 8 + 2 * tq], xb = XS[n * 8 + 2 * tq + 1];
       // combined_scale = w_scale * x_scale (gemm.rs:606, 493)
-      const float c00 = __fmul_rn(ws0, xa.x), c01 = __fmul_rn(ws0, xb.x);
-      const float c10 = __fmul_rn(ws1, xa.x), c11 = __fmul_rn(ws1, xb.x);
+      const uint64_t xs2 = f2(xa.x, xb.x);
+      const uint64_t c0 = mul2(f2(ws0, ws0), xs2), c1 = mul2(f2(ws1, ws1), xs2);
 #pragma unroll
       for (int L = 0; L < 8; ++L) {
         int32_t d[4];
         mma_u8s8(A0[L], A1[L], B[L], d);
-        facc[n][L][0] = __fadd_rn(facc[n][L][0], __fmul_rn(__fsub_rn(__int_as_float(d[0]), kMagicF), c00));
-        facc[n][L][1] = __fadd_rn(facc[n][L][1], __fmul_rn(__fsub_rn(__int_as_float(d[1]), kMagicF), c01));
-        facc[n][L][2] = __fadd_rn(facc[n][L][2], __fmul_rn(__fsub_rn(__int_as_float(d[2]), kMagicF), c10));
-        facc[n][L][3] = __fadd_rn(facc[n][L][3], __fmul_rn(__fsub_rn(__int_as_float(d[3]), kMagicF), c11));
+        acc_pair(&facc[n][L][0], d[0], d[1], c0, magic2);
+        acc_pair(&facc[n][L][2], d[2], d[3], c1, magic2);
       }
       // zero correction: sum_g w_zero * x_sum, sequential in g (gemm.rs:666-670)
       zc[n][0] = __fadd_rn(zc[n][0], __fmul_rn(wz0, xa.y));

@@ -17,12 +17,16 @@
 //                       loop (lookup.rs:359-411)
 #include <cuda_runtime.h>
 
+#include <algorithm>
+
 #include "common.cuh"
 #include "layers.h"
 
 namespace rai {
 
 __device__ __forceinline__ int active_rows(const int* m_dev, int M) { return m_dev ? *m_dev : M; }
+
+constexpr int kPvMaxStages = 4;
 
 // ---------------------------------------------------------------------------
 __global__ void embed_kernel(const uint32_t* __restrict__ ids, const int* m_dev, int M,
@@ -182,196 +186,326 @@ __global__ void qkv_post_kernel(const float* __restrict__ qkv, int ld, float* __
 }
 
 // ---------------------------------------------------------------------------
-// Attention, step 1: scores. CTA (kv head, row, chunk of kScoreChunk
-// positions); thread t owns one cached position, keeps its K row in
-// registers and scores it against the group's query heads: 8-lane FMA dot,
-// horizontal-sum tree, times scale (then softcap).
+// Attention over row segments. A segment is a run of up to kSegRows rows of
+// one stream at consecutive positions pos0 .. pos0 + nrows - 1 (a stream's
+// verify rows, or a slice of its prompt), so every K/V row of the stream is
+// read once per segment and shared by all its rows and all query heads of
+// the KV head.
+//
+// Step 1: scores. CTA (kv head, segment, chunk of positions); the chunk's K
+// rows are staged in shared memory (coalesced 16-byte copies into rows
+// padded to HD + 4 floats, so the per-thread row reads are conflict free);
+// thread t owns one position, keeps its K row in registers and scores it
+// against every (row, head) of the segment whose position is >= t: 8-lane
+// FMA dot, horizontal-sum tree, times scale (then softcap).
 template <int HD>
-__global__ void __launch_bounds__(kScoreChunk) attn_scores_kernel(
-    const float* __restrict__ q, const StreamKV* __restrict__ kv, int layer, const RowInfo* __restrict__ rows,
-    const int* m_dev, int M, int nh, int nkv, float scale, float softcap, float* __restrict__ scores,
-    float* __restrict__ smax, int n_alloc, int n_chunks) {
-  __shared__ float sq[8 * HD];
-  __shared__ float red[8][kScoreChunk / 32];
-  const int kvh = blockIdx.x, j = blockIdx.y, chunk = blockIdx.z;
-  if (j >= active_rows(m_dev, M)) return;
-  const RowInfo ri = rows[j];
-  const int n = ri.pos + 1;
-  const int t0 = chunk * kScoreChunk;
-  if (t0 >= n) return;
+struct ScoreCfg {
+  static constexpr int CHUNK = HD >= 128 ? 128 : 256;  // positions (= threads) per CTA
+  static constexpr int LD = HD + 4;                    // padded K row stride (floats)
+};
+
+template <int HD>
+__global__ void __launch_bounds__(ScoreCfg<HD>::CHUNK) attn_scores_kernel(
+    const float* __restrict__ q, const StreamKV* __restrict__ kv, int layer, const AttnSeg* __restrict__ segs,
+    const int* nseg_dev, int nseg_max, int nh, int nkv, float scale, float softcap, float* __restrict__ scores,
+    int n_alloc) {
+  constexpr int CH = ScoreCfg<HD>::CHUNK, LD = ScoreCfg<HD>::LD;
+  extern __shared__ __align__(16) float sm[];
+  float* sk = sm;            // [CH][LD]
+  float* sq = sm + CH * LD;  // [nrows][hpk][HD]
+  const int kvh = blockIdx.x, si = blockIdx.y, chunk = blockIdx.z;
+  if (si >= active_rows(nseg_dev, nseg_max)) return;
+  const AttnSeg sg = segs[si];
+  const int n_max = sg.pos0 + sg.nrows;
+  const int t0 = chunk * CH;
+  if (t0 >= n_max) return;
+  const int cnt = min(CH, n_max - t0);
   const int hpk = nh / nkv;
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  for (int i = tid; i < hpk * HD; i += blockDim.x) sq[i] = q[(size_t)j * nh * HD + (size_t)kvh * hpk * HD + i];
+  const int tid = threadIdx.x;
+  const StreamKV sk_ = kv[sg.stream];
+  const float* kb = sk_.k + (((size_t)layer * nkv + kvh) * sk_.max_ctx + t0) * HD;
+  for (int i = tid; i < cnt * (HD / 4); i += CH) {
+    const int row = i / (HD / 4), c4 = i - row * (HD / 4);
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(sk + row * LD + 4 * c4)),
+                 "l"(kb + 4 * (size_t)i)
+                 : "memory");
+  }
+  asm volatile("cp.async.commit_group;" ::: "memory");
+  const int per_row = hpk * HD;
+  for (int i = tid; i < sg.nrows * per_row; i += CH) {
+    const int r = i / per_row, o = i - r * per_row;
+    sq[i] = q[(size_t)(sg.row0 + r) * nh * HD + (size_t)kvh * per_row + o];
+  }
+  asm volatile("cp.async.wait_group 0;" ::: "memory");
   __syncthreads();
-  const StreamKV sk_ = kv[ri.stream];
+  if (tid >= cnt) return;
   const int t = t0 + tid;
-  // Per-thread maxima stay in registers: every loop over the (at most 8)
-  // heads of the group is fully unrolled with a guard.
-  float tmax[8];
-#pragma unroll
-  for (int h = 0; h < 8; ++h) tmax[h] = -INFINITY;
-  if (t < n) {
-    const float4* kp = reinterpret_cast<const float4*>(
-        sk_.k + (((size_t)layer * nkv + kvh) * sk_.max_ctx + t) * HD);
-    float kr[HD];
+  float kr[HD];
+  {
+    const float4* kp = reinterpret_cast<const float4*>(sk + tid * LD);
 #pragma unroll
     for (int i = 0; i < HD / 4; ++i) {
-      float4 v = __ldg(kp + i);
+      float4 v = kp[i];
       kr[4 * i] = v.x; kr[4 * i + 1] = v.y; kr[4 * i + 2] = v.z; kr[4 * i + 3] = v.w;
     }
+  }
+  // Rows r with pos0 + r >= t see position t.
+  const int r_first = max(0, t - sg.pos0);
+  for (int r = r_first; r < sg.nrows; ++r) {
+    float* srow = scores + ((size_t)(sg.row0 + r) * nh + (size_t)kvh * hpk) * n_alloc + t;
+    for (int h = 0; h < hpk; ++h) {
+      const float4* qh = reinterpret_cast<const float4*>(sq + (r * hpk + h) * HD);
+      float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-    for (int h = 0; h < 8; ++h) {
-      if (h < hpk) {
-        const float* qh = sq + h * HD;
-        float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-        for (int cc = 0; cc < HD / 8; ++cc)
-#pragma unroll
-          for (int jj = 0; jj < 8; ++jj) acc[jj] = __fmaf_rn(qh[8 * cc + jj], kr[8 * cc + jj], acc[jj]);
-        float sv = __fmul_rn(hsum8(acc), scale);
-        if (softcap > 0.f) sv = __fmul_rn(softcap, tanhf(__fdiv_rn(sv, softcap)));
-        scores[((size_t)j * nh + kvh * hpk + h) * n_alloc + t] = sv;
-        tmax[h] = sv;
+      for (int cc = 0; cc < HD / 8; ++cc) {
+        float4 a0 = qh[2 * cc], a1 = qh[2 * cc + 1];
+        acc[0] = __fmaf_rn(a0.x, kr[8 * cc + 0], acc[0]);
+        acc[1] = __fmaf_rn(a0.y, kr[8 * cc + 1], acc[1]);
+        acc[2] = __fmaf_rn(a0.z, kr[8 * cc + 2], acc[2]);
+        acc[3] = __fmaf_rn(a0.w, kr[8 * cc + 3], acc[3]);
+        acc[4] = __fmaf_rn(a1.x, kr[8 * cc + 4], acc[4]);
+        acc[5] = __fmaf_rn(a1.y, kr[8 * cc + 5], acc[5]);
+        acc[6] = __fmaf_rn(a1.z, kr[8 * cc + 6], acc[6]);
+        acc[7] = __fmaf_rn(a1.w, kr[8 * cc + 7], acc[7]);
       }
+      float sv = __fmul_rn(hsum8(acc), scale);
+      if (softcap > 0.f) sv = __fmul_rn(softcap, tanhf(__fdiv_rn(sv, softcap)));
+      srow[(size_t)h * n_alloc] = sv;
     }
-  }
-#pragma unroll
-  for (int h = 0; h < 8; ++h) {
-    float m = tmax[h];
-#pragma unroll
-    for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-    if (lane == 0) red[h][warp] = m;
-  }
-  __syncthreads();
-  if (tid < hpk) {
-    float m = red[tid][0];
-#pragma unroll
-    for (int w = 1; w < kScoreChunk / 32; ++w) m = fmaxf(m, red[tid][w]);
-    smax[((size_t)j * nh + kvh * hpk + tid) * n_chunks + chunk] = m;
   }
 }
 
-// Attention, step 2: softmax of one (row, head). Schraudolph exp for the
-// first (n/8)*8 scores, the host-libm expf for the tail; the sum in 8 lanes
-// (lane j adds scores 8i + j in order), the tree, then the tail added in
-// order; stores exp values in place and 1/sum.
+// Step 2: softmax. CTA (row, kv head); one warp per query head of the group
+// (heads processed in batches of `hb` when the context is long). The head's
+// score row is brought into shared memory with one bulk copy; max;
+// exp(s - max) with Schraudolph for the first (n/8)*8 positions and the
+// host-libm expf for the tail; the sum in 8 lanes (lane j adds positions
+// 8i + j in order), the tree, the tail in order; then p = e * (1/sum)
+// written back in place.
 __global__ void __launch_bounds__(256) attn_softmax_kernel(const RowInfo* __restrict__ rows, const int* m_dev,
-                                                           int M, int nh, float* __restrict__ scores,
-                                                           const float* __restrict__ smax, float* __restrict__ inv,
-                                                           int n_alloc, int n_chunks, ExpfTable et) {
-  extern __shared__ float se[];
-  __shared__ float lanes[8];
-  const int j = blockIdx.x, h = blockIdx.y;
+                                                           int M, int nh, int nkv, float* __restrict__ scores,
+                                                           int n_alloc, int hb, ExpfTable et, uint32_t* err) {
+  extern __shared__ __align__(16) float se_all[];  // [hb][n_alloc]
+  __shared__ __align__(8) uint64_t bars[8];
+  const int j = blockIdx.x, kvh = blockIdx.y;
   if (j >= active_rows(m_dev, M)) return;
   const int n = rows[j].pos + 1;
-  const int nch = (n + kScoreChunk - 1) / kScoreChunk;
-  const float* cm = smax + ((size_t)j * nh + h) * n_chunks;
-  float m = cm[0];
-  for (int c = 1; c < nch; ++c) m = fmaxf(m, cm[c]);
-  float* row = scores + ((size_t)j * nh + h) * n_alloc;
-  const int n8 = (n / 8) * 8;
-  for (int t = threadIdx.x; t < n; t += blockDim.x) {
-    float x = __fsub_rn(row[t], m);
-    float e = t < n8 ? schraudolph(x) : expf_host(x, et);
-    row[t] = e;
-    se[t] = e;
+  const int n8 = (n / 8) * 8, cnt = n8 / 8;
+  const int hpk = nh / nkv;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) {
+    mbar_init(&bars[warp], 1);
+    fence_barrier_init();
   }
-  __syncthreads();
-  if (threadIdx.x < 8) {
-    const int jj = threadIdx.x, cnt = n8 / 8;
-    float acc = 0.f;
-    int i = 0;
-    for (; i + 8 <= cnt; i += 8) {
-      float v[8];
+  __syncwarp();
+  const uint32_t bytes = (uint32_t)((n + 3) / 4) * 16u;
+  uint32_t phase = 0;
+  for (int hbase = 0; hbase < hpk; hbase += hb) {
+    const int hh = warp;
+    if (hh < hb && hbase + hh < hpk) {
+      float* row = scores + ((size_t)j * nh + (size_t)kvh * hpk + hbase + hh) * n_alloc;
+      float* se = se_all + (size_t)hh * n_alloc;
+      if (lane == 0) {
+        mbar_arrive_expect_tx(&bars[warp], bytes);
+        bulk_g2s(se, row, bytes, &bars[warp]);
+      }
+      const bool ok = mbar_wait(&bars[warp], phase, err);
+      phase ^= 1u;
+      if (!__all_sync(0xffffffffu, ok)) return;
+      float m = -INFINITY;
+      for (int t = lane; t < n; t += 32) m = fmaxf(m, se[t]);
 #pragma unroll
-      for (int u = 0; u < 8; ++u) v[u] = se[8 * (i + u) + jj];
+      for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+      for (int t = lane; t < n; t += 32) {
+        float x = __fsub_rn(se[t], m);
+        se[t] = t < n8 ? schraudolph(x) : expf_host(x, et);
+      }
+      __syncwarp();
+      float acc = 0.f;
+      if (lane < 8) {
+        int i = 0;
+        for (; i + 8 <= cnt; i += 8) {
+          float v[8];
 #pragma unroll
-      for (int u = 0; u < 8; ++u) acc = __fadd_rn(acc, v[u]);
+          for (int u = 0; u < 8; ++u) v[u] = se[8 * (i + u) + lane];
+#pragma unroll
+          for (int u = 0; u < 8; ++u) acc = __fadd_rn(acc, v[u]);
+        }
+        for (; i < cnt; ++i) acc = __fadd_rn(acc, se[8 * i + lane]);
+      }
+      float a[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) a[u] = __shfl_sync(0xffffffffu, acc, u);
+      float sum = hsum8(a);
+      for (int t = n8; t < n; ++t) sum = __fadd_rn(sum, se[t]);
+      const float inv = __fdiv_rn(1.0f, sum);
+      for (int t = lane; t < n; t += 32) row[t] = __fmul_rn(se[t], inv);
+      // The next bulk copy into this buffer (async proxy) follows these
+      // generic reads.
+      __syncwarp();
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     }
-    for (; i < cnt; ++i) acc = __fadd_rn(acc, se[8 * i + jj]);
-    lanes[jj] = acc;
-  }
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    float sum = hsum8(lanes);
-    for (int t = n8; t < n; ++t) sum = __fadd_rn(sum, se[t]);
-    inv[(size_t)j * nh + h] = __fdiv_rn(1.0f, sum);
   }
 }
 
-// Attention, step 3: out[h][d] = fma(p_t, v_t[d], out) over t in order, with
-// p_t = e_t * (1/sum). CTA (kv head, row); one thread per (head, dim) chain;
-// V and p tiles staged in shared memory (double-buffered V via cp.async).
+// Step 3: out[row][h][d] = fma(p_t, v_t[d], out) over t in order. CTA
+// (kv head, segment); thread (d pair, head pair) carries 2 x 2 chains for
+// each of the segment's rows (RB >= nrows) in registers, so one V load feeds
+// 2 heads x RB rows and one p load 2 dims. V and p tiles stream through a
+// ring of `ns` shared-memory stages filled by bulk copies (warp 0) that
+// complete on mbarriers. Row r only takes positions t <= pos0 + r.
 template <int HD>
-__global__ void __launch_bounds__(1024) attn_pv_kernel(const StreamKV* __restrict__ kv, int layer,
-                                                       const RowInfo* __restrict__ rows, const int* m_dev, int M,
-                                                       int nh, int nkv, const float* __restrict__ scores,
-                                                       const float* __restrict__ inv, int n_alloc,
-                                                       float* __restrict__ out) {
-  constexpr int VT = 64;
-  extern __shared__ __align__(16) float sm[];
-  const int hpk = nh / nkv;
-  float* vt = sm;                       // [2][VT][HD]
-  float* pt = sm + 2 * VT * HD;         // [hpk][VT]
-  const int kvh = blockIdx.x, j = blockIdx.y;
-  if (j >= active_rows(m_dev, M)) return;
-  const RowInfo ri = rows[j];
-  const int n = ri.pos + 1;
-  const StreamKV sk_ = kv[ri.stream];
-  const float* vbase = sk_.v + ((size_t)layer * nkv + kvh) * sk_.max_ctx * HD;
-  const int tid = threadIdx.x;
-  const int h = tid / HD, d = tid % HD;
-  const bool chain = tid < hpk * HD;
-  const float* erow0 = scores + ((size_t)j * nh + kvh * hpk) * n_alloc;
-  const float* invr = inv + (size_t)j * nh + kvh * hpk;
-  const int ntiles = (n + VT - 1) / VT;
-  auto load_v = [&](int tile, int buf) {
-    int t0 = tile * VT;
-    int cnt = min(VT, n - t0) * HD / 4;
-    const float4* src = reinterpret_cast<const float4*>(vbase + (size_t)t0 * HD);
-    float4* dst = reinterpret_cast<float4*>(vt + (size_t)buf * VT * HD);
-    for (int i = tid; i < cnt; i += blockDim.x) {
-      uint32_t a = smem_u32(dst + i);
-      asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(a), "l"(src + i) : "memory");
+struct PvCfg {
+  static constexpr int VT = HD >= 128 ? 32 : 64;  // positions per tile
+};
+
+template <int HD, int RB>
+__device__ __forceinline__ void pv_body(const float* __restrict__ vbase, const float* __restrict__ p, int nh,
+                                        int hpk, int kvh, const AttnSeg& sg, int n_alloc, int rb_alloc, int ns,
+                                        float* __restrict__ out, float* sm, uint64_t* bars, uint32_t* err) {
+  constexpr int VT = PvCfg<HD>::VT;
+  constexpr int NDP = HD / 2;
+  const int stage_floats = VT * HD + rb_alloc * hpk * VT;
+  const int tid = threadIdx.x, lane = tid & 31;
+  const int dp = tid % NDP, hp = tid / NDP;
+  const int d0 = 2 * dp, h0 = 2 * hp, h1 = 2 * hp + 1;
+  const bool active = h0 < hpk, has_h1 = h1 < hpk;
+  const int nrows = sg.nrows;
+  const int n_max = sg.pos0 + nrows, n_all = sg.pos0 + 1;
+  const int ntiles = (n_max + VT - 1) / VT;
+  const float* prow0 = p + ((size_t)sg.row0 * nh + (size_t)kvh * hpk) * n_alloc;
+  // Warp 0 fills stage `st` with tile `tile`.
+  auto issue = [&](int tile, int st) {
+    const int t0 = tile * VT, cnt = min(VT, n_max - t0), c4 = (cnt + 3) / 4;
+    float* sv = sm + (size_t)st * stage_floats;
+    float* sp = sv + VT * HD;
+    if (lane == 0) {
+      mbar_arrive_expect_tx(&bars[st], (uint32_t)(cnt * HD * 4 + nrows * hpk * c4 * 16));
+      bulk_g2s(sv, vbase + (size_t)t0 * HD, (uint32_t)(cnt * HD * 4), &bars[st]);
     }
-    asm volatile("cp.async.commit_group;" ::: "memory");
+    __syncwarp();
+    for (int i = lane; i < nrows * hpk; i += 32) {
+      const int r = i / hpk, hh = i - r * hpk;
+      bulk_g2s(sp + i * VT, prow0 + ((size_t)r * nh + hh) * n_alloc + t0, (uint32_t)(c4 * 16), &bars[st]);
+    }
   };
-  float acc = 0.f;
-  load_v(0, 0);
-  for (int tile = 0; tile < ntiles; ++tile) {
-    const int t0 = tile * VT, cnt = min(VT, n - t0);
-    // p tile for this block's heads: p = e * inv (the reference's
-    // `*sp *= inv_sum`).
-    for (int i = tid; i < hpk * VT; i += blockDim.x) {
-      int hh = i / VT, tt = i % VT;
-      pt[i] = tt < cnt ? __fmul_rn(erow0[(size_t)hh * n_alloc + t0 + tt], invr[hh]) : 0.f;
-    }
-    if (tile + 1 < ntiles) {
-      load_v(tile + 1, (tile + 1) & 1);
-      asm volatile("cp.async.wait_group 1;" ::: "memory");
-    } else {
-      asm volatile("cp.async.wait_group 0;" ::: "memory");
-    }
-    __syncthreads();
-    if (chain) {
-      const float* vb = vt + (size_t)(tile & 1) * VT * HD + d;
-      const float* pb = pt + h * VT;
-      int t = 0;
-      for (; t + 8 <= cnt; t += 8) {
-        float pv[8], vv[8];
-#pragma unroll
-        for (int u = 0; u < 8; ++u) {
-          pv[u] = pb[t + u];
-          vv[u] = vb[(t + u) * HD];
-        }
-#pragma unroll
-        for (int u = 0; u < 8; ++u) acc = __fmaf_rn(pv[u], vv[u], acc);
-      }
-      for (; t < cnt; ++t) acc = __fmaf_rn(pb[t], vb[t * HD], acc);
-    }
-    __syncthreads();
+  if (tid == 0) {
+    for (int s = 0; s < ns; ++s) mbar_init(&bars[s], 1);
+    fence_barrier_init();
   }
-  if (chain) out[(size_t)j * nh * HD + (size_t)(kvh * hpk + h) * HD + d] = acc;
+  __syncthreads();
+  if (tid < 32)
+    for (int s = 0; s < ns && s < ntiles; ++s) issue(s, s);
+  float acc[RB][4];
+#pragma unroll
+  for (int r = 0; r < RB; ++r) acc[r][0] = acc[r][1] = acc[r][2] = acc[r][3] = 0.f;
+  int tile = 0;
+  for (; tile < ntiles; ++tile) {
+    const int st = tile % ns;
+    const bool ok = mbar_wait(&bars[st], (uint32_t)(tile / ns) & 1u, err);
+    if (!__syncthreads_and(ok)) break;
+    const int t0 = tile * VT, cnt = min(VT, n_max - t0);
+    const float* sv = sm + (size_t)st * stage_floats + d0;
+    const float* sp = sm + (size_t)st * stage_floats + VT * HD;
+    if (active) {
+      const float* p0 = sp + h0 * VT;
+      const float* p1 = sp + (has_h1 ? h1 : h0) * VT;
+      if (t0 + cnt <= n_all) {
+        // Every row sees the whole tile.
+        int t = 0;
+        for (; t + 4 <= cnt; t += 4) {
+          float2 v[4];
+#pragma unroll
+          for (int u = 0; u < 4; ++u) v[u] = *reinterpret_cast<const float2*>(sv + (t + u) * HD);
+#pragma unroll
+          for (int r = 0; r < RB; ++r) {
+            if (r < nrows) {
+              const float4 pa = *reinterpret_cast<const float4*>(p0 + r * hpk * VT + t);
+              const float4 pb = *reinterpret_cast<const float4*>(p1 + r * hpk * VT + t);
+              const float a4[4] = {pa.x, pa.y, pa.z, pa.w};
+              const float b4[4] = {pb.x, pb.y, pb.z, pb.w};
+#pragma unroll
+              for (int u = 0; u < 4; ++u) {
+                acc[r][0] = __fmaf_rn(a4[u], v[u].x, acc[r][0]);
+                acc[r][1] = __fmaf_rn(a4[u], v[u].y, acc[r][1]);
+                acc[r][2] = __fmaf_rn(b4[u], v[u].x, acc[r][2]);
+                acc[r][3] = __fmaf_rn(b4[u], v[u].y, acc[r][3]);
+              }
+            }
+          }
+        }
+        for (; t < cnt; ++t) {
+          const float2 v = *reinterpret_cast<const float2*>(sv + t * HD);
+#pragma unroll
+          for (int r = 0; r < RB; ++r) {
+            if (r < nrows) {
+              const float a = p0[r * hpk * VT + t], b = p1[r * hpk * VT + t];
+              acc[r][0] = __fmaf_rn(a, v.x, acc[r][0]);
+              acc[r][1] = __fmaf_rn(a, v.y, acc[r][1]);
+              acc[r][2] = __fmaf_rn(b, v.x, acc[r][2]);
+              acc[r][3] = __fmaf_rn(b, v.y, acc[r][3]);
+            }
+          }
+        }
+      } else {
+        for (int t = 0; t < cnt; ++t) {
+          const float2 v = *reinterpret_cast<const float2*>(sv + t * HD);
+          const int rmin = t0 + t - sg.pos0;  // rows r >= rmin see position t0 + t
+#pragma unroll
+          for (int r = 0; r < RB; ++r) {
+            if (r < nrows && r >= rmin) {
+              const float a = p0[r * hpk * VT + t], b = p1[r * hpk * VT + t];
+              acc[r][0] = __fmaf_rn(a, v.x, acc[r][0]);
+              acc[r][1] = __fmaf_rn(a, v.y, acc[r][1]);
+              acc[r][2] = __fmaf_rn(b, v.x, acc[r][2]);
+              acc[r][3] = __fmaf_rn(b, v.y, acc[r][3]);
+            }
+          }
+        }
+      }
+    }
+    __syncthreads();
+    if (tid < 32 && tile + ns < ntiles) issue(tile + ns, st);
+  }
+  if (tile < ntiles) {
+    // A wait gave up: let this CTA's copies still in flight land (bounded)
+    // before the CTA exits; the output is not written.
+    if (tid == 0)
+      for (int j = tile; j < ntiles && j < tile + ns; ++j) mbar_wait(&bars[j % ns], (uint32_t)(j / ns) & 1u, nullptr);
+    return;
+  }
+  if (active) {
+#pragma unroll
+    for (int r = 0; r < RB; ++r) {
+      if (r < nrows) {
+        float* o = out + (size_t)(sg.row0 + r) * nh * HD + d0;
+        *reinterpret_cast<float2*>(o + (size_t)(kvh * hpk + h0) * HD) = make_float2(acc[r][0], acc[r][1]);
+        if (has_h1)
+          *reinterpret_cast<float2*>(o + (size_t)(kvh * hpk + h1) * HD) = make_float2(acc[r][2], acc[r][3]);
+      }
+    }
+  }
+}
+
+template <int HD>
+__global__ void __launch_bounds__(256) attn_pv_kernel(const StreamKV* __restrict__ kv, int layer,
+                                                      const AttnSeg* __restrict__ segs, const int* nseg_dev,
+                                                      int nseg_max, int nh, int nkv, const float* __restrict__ p,
+                                                      int n_alloc, int rb_alloc, int ns, float* __restrict__ out,
+                                                      uint32_t* err) {
+  extern __shared__ __align__(16) float sm[];
+  __shared__ __align__(8) uint64_t bars[kPvMaxStages];
+  const int kvh = blockIdx.x, si = blockIdx.y;
+  if (si >= active_rows(nseg_dev, nseg_max)) return;
+  const AttnSeg sg = segs[si];
+  const int hpk = nh / nkv;
+  const StreamKV sk_ = kv[sg.stream];
+  const float* vbase = sk_.v + ((size_t)layer * nkv + kvh) * sk_.max_ctx * HD;
+  if (sg.nrows <= 1) pv_body<HD, 1>(vbase, p, nh, hpk, kvh, sg, n_alloc, rb_alloc, ns, out, sm, bars, err);
+  else if (sg.nrows <= 2) pv_body<HD, 2>(vbase, p, nh, hpk, kvh, sg, n_alloc, rb_alloc, ns, out, sm, bars, err);
+  else if (sg.nrows <= 4) pv_body<HD, 4>(vbase, p, nh, hpk, kvh, sg, n_alloc, rb_alloc, ns, out, sm, bars, err);
+  else if (sg.nrows <= 8) pv_body<HD, 8>(vbase, p, nh, hpk, kvh, sg, n_alloc, rb_alloc, ns, out, sm, bars, err);
+  else pv_body<HD, kSegRows>(vbase, p, nh, hpk, kvh, sg, n_alloc, rb_alloc, ns, out, sm, bars, err);
 }
 
 // ---------------------------------------------------------------------------
@@ -470,26 +604,62 @@ __global__ void ngram_kernel(const uint32_t* __restrict__ ctx_all, int ctx_cap, 
   }
 }
 
-// Compact every stream's verify rows into one row set (prefix sum over the
-// streams), write row metadata and token ids, zero the argmax slots.
-__global__ void plan_kernel(StreamStep* st, int n, RowInfo* rows, uint32_t* ids, int* m_active,
-                            unsigned long long* best, int best_len) {
-  if (threadIdx.x == 0) {
-    int r = 0;
-    for (int i = 0; i < n; ++i) {
-      st[i].row0 = r;
-      r += st[i].n_rows;
-    }
-    *m_active = r;
-  }
+// Compact every stream's verify rows into one row set (block-wide prefix
+// sums over the streams of rows and of attention segments), write row
+// metadata, token ids and segments, zero the argmax slots.
+__global__ void __launch_bounds__(1024) plan_kernel(StreamStep* st, int n, RowInfo* rows, uint32_t* ids,
+                                                    int* m_active, AttnSeg* segs, int* n_segs, int seg_len,
+                                                    unsigned long long* best, int best_len) {
+  __shared__ unsigned long long wsum[32];
+  __shared__ unsigned long long carry;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  if (tid == 0) carry = 0ull;
+  for (int i = tid; i < best_len; i += blockDim.x) best[i] = 0ull;
   __syncthreads();
-  for (int i = threadIdx.x; i < best_len; i += blockDim.x) best[i] = 0ull;
-  for (int i = 0; i < n; ++i) {
-    const int r0 = st[i].row0, nr = st[i].n_rows, p = st[i].pos;
-    for (int b = threadIdx.x; b < nr; b += blockDim.x) {
-      rows[r0 + b] = RowInfo{p + b, i};
-      ids[r0 + b] = st[i].tokens[b];
+  for (int base = 0; base < n; base += blockDim.x) {
+    const int i = base + tid;
+    const int nr = i < n ? st[i].n_rows : 0;
+    const int ns = (nr + seg_len - 1) / seg_len;
+    // (rows << 32) | segments, inclusive scan
+    unsigned long long v = ((unsigned long long)nr << 32) | (unsigned)ns;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      unsigned long long u = __shfl_up_sync(0xffffffffu, v, o);
+      if (lane >= o) v += u;
     }
+    if (lane == 31) wsum[warp] = v;
+    __syncthreads();
+    if (warp == 0) {
+      const int nw = blockDim.x >> 5;
+      unsigned long long w = lane < nw ? wsum[lane] : 0ull;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        unsigned long long u = __shfl_up_sync(0xffffffffu, w, o);
+        if (lane >= o) w += u;
+      }
+      if (lane < nw) wsum[lane] = w;
+    }
+    __syncthreads();
+    const unsigned long long before = carry + (warp ? wsum[warp - 1] : 0ull) + v -
+                                      (((unsigned long long)nr << 32) | (unsigned)ns);
+    if (i < n) {
+      const int r0 = (int)(before >> 32), s0 = (int)(before & 0xFFFFFFFFull);
+      const int p = st[i].pos;
+      st[i].row0 = r0;
+      for (int b = 0; b < nr; ++b) {
+        rows[r0 + b] = RowInfo{p + b, i};
+        ids[r0 + b] = st[i].tokens[b];
+      }
+      for (int k = 0; k < ns; ++k)
+        segs[s0 + k] = AttnSeg{r0 + k * seg_len, min(seg_len, nr - k * seg_len), i, p + k * seg_len};
+    }
+    __syncthreads();
+    if (tid == 0) carry += wsum[(blockDim.x >> 5) - 1];
+    __syncthreads();
+  }
+  if (tid == 0) {
+    *m_active = (int)(carry >> 32);
+    *n_segs = (int)(carry & 0xFFFFFFFFull);
   }
 }
 
@@ -538,26 +708,53 @@ cudaError_t launch_qkv_post(float* qkv, int ld, float* q_out, int nh, int nkv, i
 
 size_t attention_n_chunks(int n_alloc) { return (size_t)(n_alloc + kScoreChunk - 1) / kScoreChunk; }
 
-static size_t pv_smem_bytes(int hd, int hpk) { return (size_t)(2 * 64 * hd + hpk * 64) * sizeof(float); }
+namespace {
+int score_chunk(int hd) { return hd >= 128 ? 128 : 256; }
+size_t scores_smem_bytes(int hd, int hpk, int seg_rows) {
+  return ((size_t)score_chunk(hd) * (hd + 4) + (size_t)seg_rows * hpk * hd) * sizeof(float);
+}
+size_t pv_stage_bytes(int hd, int hpk, int rb_alloc) {
+  const int vt = hd >= 128 ? 32 : 64;
+  return (size_t)(vt * hd + rb_alloc * hpk * vt) * sizeof(float);
+}
+int pv_threads(int hd, int hpk) { return ((hd / 2) * ((hpk + 1) / 2) + 31) / 32 * 32; }
+}  // namespace
+
+int build_segments(const RowInfo* rows, int M, int seg_len, AttnSeg* segs) {
+  int n = 0;
+  for (int i = 0; i < M;) {
+    int j = i + 1;
+    while (j < M && j - i < seg_len && rows[j].stream == rows[i].stream && rows[j].pos == rows[j - 1].pos + 1) ++j;
+    segs[n++] = AttnSeg{i, j - i, rows[i].stream, rows[i].pos};
+    i = j;
+  }
+  return n;
+}
 
 cudaError_t launch_attention(const float* q, float* out, const StreamKV* kv, int layer, const RowInfo* rows,
-                             const int* m_dev, int M, int nh, int nkv, int hd, float scale, float softcap,
-                             float* scores, float* smax, float* inv, int n_alloc, const ExpfTable& et,
-                             cudaStream_t s) {
+                             const int* m_dev, int M, const AttnSeg* segs, const int* nseg_dev, int nseg_max,
+                             int seg_rows, int nh, int nkv, int hd, float scale, float softcap, float* scores,
+                             int n_alloc, const ExpfTable& et, uint32_t* err, cudaStream_t s) {
   const int hpk = nh / nkv;
-  const int nch = (int)attention_n_chunks(n_alloc);
-  dim3 g1(nkv, M, nch), g2(M, nh), g3(nkv, M);
-  const size_t sm2 = (size_t)n_alloc * sizeof(float);
-  const size_t sm3 = pv_smem_bytes(hd, hpk);
-  const int t3 = (hpk * hd + 31) / 32 * 32;
-  if (sm2 > kAttnMaxSmem || sm3 > kAttnMaxSmem || hpk > 8 || t3 > 1024) return cudaErrorInvalidValue;
-#define RAI_ATTN(HDV)                                                                                   \
-  case HDV:                                                                                             \
-    attn_scores_kernel<HDV><<<g1, kScoreChunk, 0, s>>>(q, kv, layer, rows, m_dev, M, nh, nkv, scale,    \
-                                                       softcap, scores, smax, n_alloc, nch);            \
-    attn_softmax_kernel<<<g2, 256, sm2, s>>>(rows, m_dev, M, nh, scores, smax, inv, n_alloc, nch, et);  \
-    attn_pv_kernel<HDV><<<g3, t3, sm3, s>>>(kv, layer, rows, m_dev, M, nh, nkv, scores, inv, n_alloc,   \
-                                            out);                                                       \
+  if (seg_rows < 1 || seg_rows > kSegRows || hpk > 8 || n_alloc % 4) return cudaErrorInvalidValue;
+  const int nch = (n_alloc + score_chunk(hd) - 1) / score_chunk(hd);
+  const size_t sm1 = scores_smem_bytes(hd, hpk, seg_rows);
+  int hb = (int)std::min<size_t>((size_t)hpk, kAttnMaxSmem / ((size_t)n_alloc * sizeof(float)));
+  const size_t stage = pv_stage_bytes(hd, hpk, seg_rows);
+  // Stages: as many as fit ~110 KB (two CTAs per SM), at least 2, at most 4.
+  const int ns = (int)std::max<size_t>(2, std::min<size_t>(kPvMaxStages, (110 * 1024) / stage));
+  const size_t sm3 = (size_t)ns * stage;
+  const int t3 = pv_threads(hd, hpk);
+  if (hb < 1 || sm1 > kAttnMaxSmem || sm3 > kAttnMaxSmem || t3 > 256) return cudaErrorInvalidValue;
+  const size_t sm2 = (size_t)hb * n_alloc * sizeof(float);
+  dim3 g1(nkv, nseg_max, nch), g2(M, nkv), g3(nkv, nseg_max);
+#define RAI_ATTN(HDV)                                                                                        \
+  case HDV:                                                                                                  \
+    attn_scores_kernel<HDV><<<g1, ScoreCfg<HDV>::CHUNK, sm1, s>>>(q, kv, layer, segs, nseg_dev, nseg_max,    \
+                                                                  nh, nkv, scale, softcap, scores, n_alloc); \
+    attn_softmax_kernel<<<g2, 256, sm2, s>>>(rows, m_dev, M, nh, nkv, scores, n_alloc, hb, et, err);         \
+    attn_pv_kernel<HDV><<<g3, t3, sm3, s>>>(kv, layer, segs, nseg_dev, nseg_max, nh, nkv, scores, n_alloc,   \
+                                            seg_rows, ns, out, err);                                         \
     break;
   switch (hd) {
     RAI_ATTN(16)
@@ -571,29 +768,19 @@ cudaError_t launch_attention(const float* q, float* out, const StreamKV* kv, int
   return cudaGetLastError();
 }
 
-// Test diagnostics: the score pass alone (raw scores and per-chunk maxima).
-cudaError_t launch_attention_scores(const float* q, const StreamKV* kv, int layer, const RowInfo* rows, int M,
-                                    int nh, int nkv, int hd, float scale, float* scores, float* smax, int n_alloc,
-                                    cudaStream_t s) {
-  const int nch = (int)attention_n_chunks(n_alloc);
-  dim3 g1(nkv, M, nch);
-  switch (hd) {
-    case 16: attn_scores_kernel<16><<<g1, kScoreChunk, 0, s>>>(q, kv, layer, rows, nullptr, M, nh, nkv, scale, 0.f, scores, smax, n_alloc, nch); break;
-    case 32: attn_scores_kernel<32><<<g1, kScoreChunk, 0, s>>>(q, kv, layer, rows, nullptr, M, nh, nkv, scale, 0.f, scores, smax, n_alloc, nch); break;
-    case 64: attn_scores_kernel<64><<<g1, kScoreChunk, 0, s>>>(q, kv, layer, rows, nullptr, M, nh, nkv, scale, 0.f, scores, smax, n_alloc, nch); break;
-    case 128: attn_scores_kernel<128><<<g1, kScoreChunk, 0, s>>>(q, kv, layer, rows, nullptr, M, nh, nkv, scale, 0.f, scores, smax, n_alloc, nch); break;
-    default: return cudaErrorInvalidValue;
-  }
-  return cudaGetLastError();
-}
-
 cudaError_t init_layer_attributes() {
   const int bytes = (int)kAttnMaxSmem;
   cudaError_t e = cudaFuncSetAttribute(attn_softmax_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
-  if (e == cudaSuccess) e = cudaFuncSetAttribute(attn_pv_kernel<16>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
-  if (e == cudaSuccess) e = cudaFuncSetAttribute(attn_pv_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
-  if (e == cudaSuccess) e = cudaFuncSetAttribute(attn_pv_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
-  if (e == cudaSuccess) e = cudaFuncSetAttribute(attn_pv_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+#define RAI_ATTR(HDV)                                                                                     \
+  if (e == cudaSuccess)                                                                                   \
+    e = cudaFuncSetAttribute(attn_pv_kernel<HDV>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);    \
+  if (e == cudaSuccess)                                                                                   \
+    e = cudaFuncSetAttribute(attn_scores_kernel<HDV>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  RAI_ATTR(16)
+  RAI_ATTR(32)
+  RAI_ATTR(64)
+  RAI_ATTR(128)
+#undef RAI_ATTR
   return e;
 }
 
@@ -619,9 +806,10 @@ cudaError_t launch_ngram(const uint32_t* ctx, int ctx_cap, StreamStep* st, const
   return cudaGetLastError();
 }
 
-cudaError_t launch_plan(StreamStep* st, int n, RowInfo* rows, uint32_t* ids, int* m_active,
-                        unsigned long long* best, int best_len, cudaStream_t s) {
-  plan_kernel<<<1, 256, 0, s>>>(st, n, rows, ids, m_active, best, best_len);
+cudaError_t launch_plan(StreamStep* st, int n, RowInfo* rows, uint32_t* ids, int* m_active, AttnSeg* segs,
+                        int* n_segs, int seg_len, unsigned long long* best, int best_len, cudaStream_t s) {
+  if (seg_len < 1 || seg_len > kSegRows) return cudaErrorInvalidValue;
+  plan_kernel<<<1, 1024, 0, s>>>(st, n, rows, ids, m_active, segs, n_segs, seg_len, best, best_len);
   return cudaGetLastError();
 }
 

@@ -15,10 +15,24 @@ namespace rai {
 
 constexpr int kMaxRowsPerStream = 33;  // max_draft <= 32 (rai run's --lookup-k limit) + 1
 constexpr int kScoreChunk = 256;       // positions per attention-score CTA
+constexpr int kSegRows = 16;           // max rows per attention segment
+// Rows per segment in a decode step: a stream's verify rows (1 .. k+1 of
+// them) are cut into pieces this long so every attention CTA carries about
+// the same work; prompt rows (uniform) use kSegRows.
+constexpr int kStepSegRows = 2;
 
 struct RowInfo {
   int pos;     // position of the row's token
   int stream;  // index into the StreamKV / StreamStep arrays
+};
+
+// A run of rows of one stream at consecutive positions pos0 .. pos0 + nrows - 1
+// (nrows <= kSegRows): the unit the attention kernels share K/V reads over.
+struct AttnSeg {
+  int row0;
+  int nrows;
+  int stream;
+  int pos0;
 };
 
 // One stream's cache: [layer][kv_head][max_ctx][head_dim] f32.
@@ -60,15 +74,17 @@ cudaError_t launch_qkv_post(float* qkv, int ld, float* q_out, int nh, int nkv, i
                             const float* rope_sin, const StreamKV* kv, int layer, const RowInfo* rows,
                             const int* m_dev, int M, cudaStream_t s);
 // Attention over each row's own stream cache (positions 0..pos inclusive).
-// scores: [M][nh][n_alloc] f32 scratch; smax: [M][nh][n_chunks]; inv: [M][nh].
+// segs: the rows grouped into segments (*nseg_dev of them when set, else
+// nseg_max); seg_rows bounds nrows over the segments. scores:
+// [M][nh][n_alloc] f32 scratch (holds p on return).
 size_t attention_n_chunks(int n_alloc);
 cudaError_t launch_attention(const float* q, float* out, const StreamKV* kv, int layer, const RowInfo* rows,
-                             const int* m_dev, int M, int nh, int nkv, int hd, float scale, float softcap,
-                             float* scores, float* smax, float* inv, int n_alloc, const ExpfTable& et,
-                             cudaStream_t s);
-cudaError_t launch_attention_scores(const float* q, const StreamKV* kv, int layer, const RowInfo* rows, int M,
-                                    int nh, int nkv, int hd, float scale, float* scores, float* smax, int n_alloc,
-                                    cudaStream_t s);
+                             const int* m_dev, int M, const AttnSeg* segs, const int* nseg_dev, int nseg_max,
+                             int seg_rows, int nh, int nkv, int hd, float scale, float softcap, float* scores,
+                             int n_alloc, const ExpfTable& et, uint32_t* err, cudaStream_t s);
+// Group host rows into segments (runs of one stream at consecutive
+// positions, at most seg_len <= kSegRows long); returns the count (<= M).
+int build_segments(const RowInfo* rows, int M, int seg_len, AttnSeg* segs);
 cudaError_t launch_swiglu(const float* gu, int ff, float* act, const int* m_dev, int M, const ExpfTable& et,
                           cudaStream_t s);
 cudaError_t launch_argmax(const float* logits, int vocab, const int* m_dev, int M, unsigned long long* best,
@@ -76,9 +92,10 @@ cudaError_t launch_argmax(const float* logits, int vocab, const int* m_dev, int 
 // Draft search for each of n streams; ctx for stream i at ctx + i * ctx_cap.
 cudaError_t launch_ngram(const uint32_t* ctx, int ctx_cap, StreamStep* st, const StreamKV* kv, int n,
                          int max_draft, int max_ngram, int min_ngram, cudaStream_t s);
-// Compact the streams' verify rows: rows / ids / *m_active; zero best[].
-cudaError_t launch_plan(StreamStep* st, int n, RowInfo* rows, uint32_t* ids, int* m_active,
-                        unsigned long long* best, int best_len, cudaStream_t s);
+// Compact the streams' verify rows: rows / ids / *m_active, attention
+// segments / *n_segs; zero best[].
+cudaError_t launch_plan(StreamStep* st, int n, RowInfo* rows, uint32_t* ids, int* m_active, AttnSeg* segs,
+                        int* n_segs, int seg_len, unsigned long long* best, int best_len, cudaStream_t s);
 cudaError_t launch_accept(StreamStep* st, int n, const unsigned long long* best, cudaStream_t s);
 
 }  // namespace rai

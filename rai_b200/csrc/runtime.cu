@@ -294,10 +294,13 @@ struct Batch {
   std::vector<rai_dec*> decs;
   float *hidden = nullptr, *resid = nullptr, *normed = nullptr, *qkv = nullptr, *q = nullptr;
   float *attn = nullptr, *gu = nullptr, *ff = nullptr, *logits = nullptr;
-  float *scores = nullptr, *smax = nullptr, *inv = nullptr;
+  float* scores = nullptr;  // attention scores, then p, [rows][nh][n_alloc]
   ActBuf act_h, act_q, act_ff, act_head;
   rai::RowInfo* rows = nullptr;
   rai::RowInfo* rows_host = nullptr;
+  rai::AttnSeg* segs = nullptr;  // attention segments of the rows
+  rai::AttnSeg* segs_host = nullptr;
+  int* n_segs = nullptr;  // segment count written by the plan kernel
   uint32_t* ids = nullptr;
   int* m_active = nullptr;
   unsigned long long* best = nullptr;
@@ -347,6 +350,7 @@ Batch::~Batch() {
   if (ctx_host) cudaFreeHost(ctx_host);
   if (st_host) cudaFreeHost(st_host);
   if (rows_host) cudaFreeHost(rows_host);
+  if (segs_host) cudaFreeHost(segs_host);
   if (ev0) cudaEventDestroy(ev0);
   if (ev1) cudaEventDestroy(ev1);
   if (stream) cudaStreamDestroy(stream);
@@ -410,8 +414,6 @@ int create_batch(rai_model* m, const std::vector<rai_dec*>& decs, int R, int row
   const size_t lrows = std::min<size_t>(Rw, (size_t)std::max(R * B->n, (int)rai::kMaxRowsPerStream));
   if (int rc = B->alloc(&B->logits, lrows * c.vocab_size * 4)) return rc;
   if (int rc = B->alloc(&B->scores, Rw * nh * B->n_alloc * 4)) return rc;
-  if (int rc = B->alloc(&B->smax, Rw * nh * rai::attention_n_chunks(B->n_alloc) * 4)) return rc;
-  if (int rc = B->alloc(&B->inv, Rw * nh * 4)) return rc;
   if (int rc = alloc_act(B.get(), &B->act_h, (int)Rw, (int)h, c.group_size)) return rc;
   if (int rc = alloc_act(B.get(), &B->act_q, (int)Rw, (int)qd, c.group_size)) return rc;
   if (int rc = alloc_act(B.get(), &B->act_ff, (int)Rw, (int)ff, c.group_size)) return rc;
@@ -420,6 +422,8 @@ int create_batch(rai_model* m, const std::vector<rai_dec*>& decs, int R, int row
   if (int rc = B->alloc(&B->rows, Rw * sizeof(rai::RowInfo))) return rc;
   if (int rc = B->alloc(&B->ids, Rw * 4)) return rc;
   if (int rc = B->alloc(&B->m_active, 4)) return rc;
+  if (int rc = B->alloc(&B->segs, Rw * sizeof(rai::AttnSeg))) return rc;
+  if (int rc = B->alloc(&B->n_segs, 4)) return rc;
   if (int rc = B->alloc(&B->best, Rw * 8)) return rc;
   if (int rc = B->alloc(&B->kv, B->n * sizeof(rai::StreamKV))) return rc;
   if (int rc = B->alloc(&B->st, B->n * sizeof(rai::StreamStep))) return rc;
@@ -428,6 +432,7 @@ int create_batch(rai_model* m, const std::vector<rai_dec*>& decs, int R, int row
   RAI_CUDA(cudaMallocHost(&B->ctx_host, (size_t)B->n * B->ctx_cap * 4));
   RAI_CUDA(cudaMallocHost(&B->st_host, B->n * sizeof(rai::StreamStep)));
   RAI_CUDA(cudaMallocHost(&B->rows_host, Rw * sizeof(rai::RowInfo)));
+  RAI_CUDA(cudaMallocHost(&B->segs_host, Rw * sizeof(rai::AttnSeg)));
   std::memset(B->st_host, 0, B->n * sizeof(rai::StreamStep));
   std::vector<rai::StreamKV> kv(B->n);
   for (int i = 0; i < B->n; ++i) kv[i] = rai::StreamKV{decs[i]->kc, decs[i]->vc, decs[i]->max_ctx, 0};
@@ -440,8 +445,10 @@ int create_batch(rai_model* m, const std::vector<rai_dec*>& decs, int R, int row
 
 // ---------------------------------------------------------------------------
 // Forward over M rows (static budget) of which *m_dev are active when m_dev
-// is set; rows[] gives each row's (position, stream), ids[] its token.
-int forward(Batch* B, int M, const int* m_dev, bool logits) {
+// is set; rows[] gives each row's (position, stream), ids[] its token; the
+// rows' attention segments are segs[] (nseg of them, or *nseg_dev when set;
+// at most seg_rows rows each).
+int forward(Batch* B, int M, const int* m_dev, int nseg, const int* nseg_dev, int seg_rows, bool logits) {
   rai_model* Mo = B->m;
   const Config& c = Mo->cfg;
   cudaStream_t s = B->stream;
@@ -464,8 +471,9 @@ int forward(Batch* B, int M, const int* m_dev, bool logits) {
     RAI_CUDA(rai::gemm_exact(L.qkv, B->act_h, M, B->qkv, qd + 2 * kvd, e_qkv, err, s, false, m_dev));
     RAI_CUDA(rai::launch_qkv_post(B->qkv, qd + 2 * kvd, B->q, nh, nkv, hd, L.q_norm, L.k_norm, Mo->qk_mode, eps,
                                   Mo->rope_cos, Mo->rope_sin, B->kv, (int)li, B->rows, m_dev, M, s));
-    RAI_CUDA(rai::launch_attention(B->q, B->attn, B->kv, (int)li, B->rows, m_dev, M, nh, nkv, hd, Mo->scale,
-                                   c.attn_logit_softcap, B->scores, B->smax, B->inv, B->n_alloc, Mo->expf, s));
+    RAI_CUDA(rai::launch_attention(B->q, B->attn, B->kv, (int)li, B->rows, m_dev, M, B->segs, nseg_dev, nseg,
+                                   seg_rows, nh, nkv, hd, Mo->scale, c.attn_logit_softcap, B->scores, B->n_alloc,
+                                   Mo->expf, err, s));
     RAI_CUDA(rai::quantize_act(B->attn, qd, M, m_dev, qd, gs, 4, B->act_q, s));
     RAI_CUDA(rai::gemm_exact(L.o, B->act_q, M, B->hidden, h, e_res, err, s, false, m_dev));
     RAI_CUDA(rai::launch_rmsnorm(B->hidden, L.post_norm, h, eps, B->normed, B->resid, m_dev, M, s));
@@ -532,11 +540,14 @@ int ensure_graph(Batch* B, const rai_lookup_cfg* cfg) {
   do {
     if (cudaSuccess != rai::launch_ngram(B->ctx, B->ctx_cap, B->st, B->kv, B->n, (int)cfg->max_draft,
                                          (int)cfg->max_ngram, (int)cfg->min_ngram, s) ||
-        cudaSuccess != rai::launch_plan(B->st, B->n, B->rows, B->ids, B->m_active, B->best, rows, s)) {
+        cudaSuccess != rai::launch_plan(B->st, B->n, B->rows, B->ids, B->m_active, B->segs, B->n_segs,
+                                        std::min(R, rai::kStepSegRows), B->best, rows, s)) {
       rc = fail(RAI_ERR_DEVICE, "draft launch failed");
       break;
     }
-    rc = forward(B, rows, B->m_active, true);
+    const int seg_rows = std::min(R, rai::kStepSegRows);
+    const int nseg = B->n * ((R + seg_rows - 1) / seg_rows);
+    rc = forward(B, rows, B->m_active, nseg, B->n_segs, seg_rows, true);
     if (rc) break;
     if (cudaSuccess != rai::launch_argmax(B->logits, B->m->cfg.vocab_size, B->m_active, rows, B->best, s) ||
         cudaSuccess != rai::launch_accept(B->st, B->n, B->best, s)) {
@@ -626,6 +637,18 @@ int step_batch(Batch* B, const size_t* pos, const uint32_t* const* ctx, const si
   return RAI_OK;
 }
 
+// Forward over host-described rows (B->rows_host[0..M), ids already queued):
+// segments are built on the host and copied with the rows.
+int forward_host_rows(Batch* B, int M, bool logits) {
+  cudaStream_t s = B->stream;
+  const int nseg = rai::build_segments(B->rows_host, M, rai::kSegRows, B->segs_host);
+  int seg_rows = 1;
+  for (int i = 0; i < nseg; ++i) seg_rows = std::max(seg_rows, B->segs_host[i].nrows);
+  RAI_CUDA(cudaMemcpyAsync(B->rows, B->rows_host, M * sizeof(rai::RowInfo), cudaMemcpyHostToDevice, s));
+  RAI_CUDA(cudaMemcpyAsync(B->segs, B->segs_host, nseg * sizeof(rai::AttnSeg), cudaMemcpyHostToDevice, s));
+  return forward(B, M, nullptr, nseg, nullptr, seg_rows, logits);
+}
+
 // Forward `rows` tokens of a single decoder at positions start.. (prefill or
 // logits), through its own batch.
 int forward_solo(rai_dec* d, const uint32_t* ids, size_t start, int rows, bool logits) {
@@ -633,8 +656,7 @@ int forward_solo(rai_dec* d, const uint32_t* ids, size_t start, int rows, bool l
   for (int b = 0; b < rows; ++b) B->rows_host[b] = rai::RowInfo{(int)(start + b), 0};
   cudaStream_t s = B->stream;
   RAI_CUDA(cudaMemcpyAsync(B->ids, ids, rows * 4, cudaMemcpyHostToDevice, s));
-  RAI_CUDA(cudaMemcpyAsync(B->rows, B->rows_host, rows * sizeof(rai::RowInfo), cudaMemcpyHostToDevice, s));
-  return forward(B, rows, nullptr, logits);
+  return forward_host_rows(B, rows, logits);
 }
 
 }  // namespace
@@ -861,8 +883,7 @@ int rai_gpu_prefill_many(rai_dec* const* decs, size_t n, const uint32_t* const* 
     if (r == 0) return RAI_OK;
     cudaStream_t s = B->stream;
     RAI_CUDA(cudaMemcpyAsync(B->ids, idbuf.data(), r * 4, cudaMemcpyHostToDevice, s));
-    RAI_CUDA(cudaMemcpyAsync(B->rows, B->rows_host, r * sizeof(rai::RowInfo), cudaMemcpyHostToDevice, s));
-    if (int rc = forward(B.get(), r, nullptr, false)) return rc;
+    if (int rc = forward_host_rows(B.get(), r, false)) return rc;
     if (int rc = check_err(m, s)) return rc;
     r = 0;
     return RAI_OK;
@@ -1036,42 +1057,36 @@ int rai_gpu_attention(const float* q, const float* k, const float* v, const int*
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   RAI_CUDA(rai::init_layer_attributes());
   int n_alloc = (int)rai::round_up(max_ctx, 4);
-  size_t nch = rai::attention_n_chunks(n_alloc);
   std::vector<rai::RowInfo> rows(M);
   for (size_t i = 0; i < M; ++i) rows[i] = rai::RowInfo{positions[i], 0};
+  std::vector<rai::AttnSeg> segs(M);
+  const int nseg = rai::build_segments(rows.data(), (int)M, rai::kSegRows, segs.data());
+  int seg_rows = 1;
+  for (int i = 0; i < nseg; ++i) seg_rows = std::max(seg_rows, segs[i].nrows);
   rai::StreamKV kv{const_cast<float*>(k), const_cast<float*>(v), (int)max_ctx, 0};
   char* buf = nullptr;
-  size_t need = M * sizeof(rai::RowInfo) + sizeof(kv) + M * nh * (n_alloc + nch + 1) * 4 + 256;
+  const size_t off_seg = rai::round_up(M * sizeof(rai::RowInfo), 16);
+  const size_t off_kv = off_seg + rai::round_up(nseg * sizeof(rai::AttnSeg), 16);
+  const size_t off_err = rai::round_up(off_kv + sizeof(kv), 16);
+  const size_t off_sc = off_err + 16;
+  const size_t need = off_sc + M * nh * n_alloc * 4;
   RAI_CUDA(cudaMalloc(&buf, need));
   struct Free { char* p; ~Free() { cudaFree(p); } } fr{buf};
   rai::RowInfo* rows_d = reinterpret_cast<rai::RowInfo*>(buf);
-  rai::StreamKV* kv_d = reinterpret_cast<rai::StreamKV*>(buf + M * sizeof(rai::RowInfo));
-  float* scores = reinterpret_cast<float*>(buf + rai::round_up(M * sizeof(rai::RowInfo) + sizeof(kv), 16));
-  float* smax = scores + M * nh * n_alloc;
-  float* inv = smax + M * nh * nch;
+  rai::AttnSeg* segs_d = reinterpret_cast<rai::AttnSeg*>(buf + off_seg);
+  rai::StreamKV* kv_d = reinterpret_cast<rai::StreamKV*>(buf + off_kv);
+  float* scores = reinterpret_cast<float*>(buf + off_sc);
+  uint32_t* err_d = reinterpret_cast<uint32_t*>(buf + off_err);
+  RAI_CUDA(cudaMemsetAsync(err_d, 0, 4, s));
   RAI_CUDA(cudaMemcpyAsync(rows_d, rows.data(), M * sizeof(rai::RowInfo), cudaMemcpyHostToDevice, s));
+  RAI_CUDA(cudaMemcpyAsync(segs_d, segs.data(), nseg * sizeof(rai::AttnSeg), cudaMemcpyHostToDevice, s));
   RAI_CUDA(cudaMemcpyAsync(kv_d, &kv, sizeof(kv), cudaMemcpyHostToDevice, s));
-  RAI_CUDA(rai::launch_attention(q, out, kv_d, 0, rows_d, nullptr, (int)M, (int)nh, (int)nkv, (int)hd, scale, 0.f,
-                                 scores, smax, inv, n_alloc, et, s));
+  RAI_CUDA(rai::launch_attention(q, out, kv_d, 0, rows_d, nullptr, (int)M, segs_d, nullptr, nseg, seg_rows, (int)nh,
+                                 (int)nkv, (int)hd, scale, 0.f, scores, n_alloc, et, err_d, s));
+  uint32_t e = 0;
+  RAI_CUDA(cudaMemcpyAsync(&e, err_d, 4, cudaMemcpyDeviceToHost, s));
   RAI_CUDA(cudaStreamSynchronize(s));
-  if (const char* dbg = std::getenv("RAI_ATTN_DEBUG_DUMP")) {
-    // Test diagnostics: exponentials [M][nh][n_alloc] then 1/sum [M][nh].
-    std::vector<float> e(M * nh * n_alloc), iv(M * nh), raw(M * nh * n_alloc), mx(M * nh * nch);
-    cudaMemcpy(e.data(), scores, e.size() * 4, cudaMemcpyDeviceToHost);
-    cudaMemcpy(iv.data(), inv, iv.size() * 4, cudaMemcpyDeviceToHost);
-    rai::launch_attention_scores(q, kv_d, 0, rows_d, (int)M, (int)nh, (int)nkv, (int)hd, scale, scores, smax, n_alloc, s);
-    cudaStreamSynchronize(s);
-    cudaMemcpy(raw.data(), scores, raw.size() * 4, cudaMemcpyDeviceToHost);
-    cudaMemcpy(mx.data(), smax, mx.size() * 4, cudaMemcpyDeviceToHost);
-    FILE* f = std::fopen(dbg, "wb");
-    if (f) {
-      std::fwrite(e.data(), 4, e.size(), f);
-      std::fwrite(iv.data(), 4, iv.size(), f);
-      std::fwrite(raw.data(), 4, raw.size(), f);
-      std::fwrite(mx.data(), 4, mx.size(), f);
-      std::fclose(f);
-    }
-  }
+  if (e) return fail(RAI_ERR_TIMEOUT, "a device-side wait timed out");
   return RAI_OK;
 }
 

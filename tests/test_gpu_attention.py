@@ -9,7 +9,8 @@ torch = pytest.importorskip("torch")
 
 
 @pytest.mark.parametrize("hd,nh,nkv", [(16, 4, 2), (32, 8, 2), (64, 14, 2), (64, 32, 4), (128, 2, 1), (128, 32, 8)])
-@pytest.mark.parametrize("positions", [[0, 1, 2, 3], [6, 7, 8, 9, 15, 16], [255, 256, 257, 300, 1029]])
+@pytest.mark.parametrize("positions", [[0, 1, 2, 3], [6, 7, 8, 9, 15, 16], [255, 256, 257, 300, 1029],
+                                       list(range(40, 60)), [5, 6, 7, 30, 31, 32, 33, 2, 3]])
 def test_attention_bit_exact(oracle, hd, nh, nkv, positions):
     from rai_b200 import native
     rng = np.random.default_rng(hd * 1000 + nh + len(positions))
