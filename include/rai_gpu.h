@@ -152,6 +152,20 @@ RAI_API int rai_gpu_w4a8_matmul(float* out, const void* packed, const float* inp
                         size_t cols, size_t tokens, size_t group_size, void* scratch,
                         size_t scratch_bytes, void* stream);
 
+/* rai_gpu_w4a8_matmul without a caller scratch buffer and without any
+ * allocation: the quantized activations go to a 2 MiB file-scope device
+ * array of the library (one per device). No reference counterpart: this
+ * entry exists for callers that may not allocate device memory. Limit:
+ * rai_gpu_w4a8_scratch_bytes(tokens, cols, group_size) <= 2 MiB (e.g. 64
+ * tokens x 14336 columns at group 128), else RAI_ERR_INVALID. Call with the
+ * stream's device current. The array's address is looked up on the first
+ * call per device, so make that call before capturing a stream. The array
+ * keeps the last call's contents; every byte the GEMM reads is rewritten by
+ * the same call. Calls on one device share the array, so calls that overlap
+ * in time (different streams or host threads) race: serialize them. */
+RAI_API int rai_gpu_w4a8_matmul_static(float* out, const void* packed, const float* input, size_t rows,
+                                       size_t cols, size_t tokens, size_t group_size, void* stream);
+
 /* The two launches of rai_gpu_w4a8_matmul separately: quantize `input`
  * (tokens x cols f32) into `scratch`, then the GEMM kernel alone on an
  * already-quantized scratch (e.g. to time it). */

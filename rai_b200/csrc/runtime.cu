@@ -672,6 +672,38 @@ rai_dec::~rai_dec() {
   cudaSetDevice(prev);
 }
 
+// ---------------------------------------------------------------------------
+// Static scratch of rai_gpu_w4a8_matmul_static: the quantized activations
+// live in a file-scope device array instead of caller- or library-allocated
+// memory. Its device address is looked up once per device (with that device
+// current) and cached.
+namespace {
+constexpr size_t kStaticScratchBytes = 2u << 20;  // 2 MiB per device
+__device__ __align__(256) uint8_t g_w4a8_static_scratch[kStaticScratchBytes];
+
+constexpr int kMaxDevices = 64;
+std::mutex g_static_mu;
+void* g_static_scratch_ptr[kMaxDevices] = {};
+
+int static_scratch(void** out) {
+  int dev = 0;
+  RAI_CUDA(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= kMaxDevices) return fail(RAI_ERR_UNSUPPORTED, "device ordinal beyond the static scratch table");
+  std::lock_guard<std::mutex> lk(g_static_mu);
+  if (!g_static_scratch_ptr[dev]) {
+    void* p = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&p, g_w4a8_static_scratch);
+    if (e != cudaSuccess) {
+      (void)cudaGetLastError();
+      return fail(RAI_ERR_DEVICE, std::string("cudaGetSymbolAddress(static scratch): ") + cudaGetErrorString(e));
+    }
+    g_static_scratch_ptr[dev] = p;
+  }
+  *out = g_static_scratch_ptr[dev];
+  return RAI_OK;
+}
+}  // namespace
+
 // ===========================================================================
 extern "C" {
 
@@ -1126,6 +1158,20 @@ int rai_gpu_w4a8_matmul_prequant(float* out, const void* packed, const void* scr
   RAI_CUDA(rai::gemm_exact(w, a, (int)tokens, out, (int)rows, rai::GemmEpilogue{}, nullptr,
                            static_cast<cudaStream_t>(stream)));
   return RAI_OK;
+}
+
+int rai_gpu_w4a8_matmul_static(float* out, const void* packed, const float* input, size_t rows, size_t cols,
+                               size_t tokens, size_t gs, void* stream) {
+  if (!out || !packed || !input) return fail(RAI_ERR_INVALID, "null argument");
+  if (gs != 64 && gs != 128) return fail(RAI_ERR_UNSUPPORTED, "group_size must be 64 or 128");
+  if (tokens == 0 || rows == 0 || cols == 0 || cols % 2) return fail(RAI_ERR_INVALID, "bad dimensions");
+  const size_t need = rai_gpu_w4a8_scratch_bytes(tokens, cols, gs);
+  if (need > kStaticScratchBytes)
+    return fail(RAI_ERR_INVALID, "tokens x groups exceed the 2 MiB static scratch (136 B per token per group, "
+                                 "tokens rounded up to 8)");
+  void* scratch = nullptr;
+  if (int rc = static_scratch(&scratch)) return rc;
+  return rai_gpu_w4a8_matmul(out, packed, input, rows, cols, tokens, gs, scratch, need, stream);
 }
 
 }  // extern "C"
