@@ -4,6 +4,8 @@
 #include <stddef.h>
 #include <stdint.h>
 
+#include "common.cuh"
+
 namespace rai {
 
 // ---- W4A8 / W8A8 exact linear (kernels_gemm.cu) ----
@@ -67,6 +69,13 @@ cudaError_t quantize_act(const float* x, int ldx, int M, const int* m_dev, int K
 
 // out[t * ld_out + r] (= epilogue(dot)) for t < M, r < rows. With m_dev set,
 // M is the static row budget (grid size) and *m_dev the active row count.
+// RMSNorm of x (n wide; x copied to `residual` when set) quantized straight
+// into `act` (one kernel).
+cudaError_t norm_quant(const float* x, const float* w, int n, float eps, float* residual, int M,
+                       const int* m_dev, int gs, int wbits, ActBuf act, cudaStream_t s);
+// SwiGLU of gate/up rows [gate | up] (2*ff wide) quantized straight into `act`.
+cudaError_t swiglu_quant(const float* gu, int ff, int M, const int* m_dev, int gs, const ExpfTable& et, ActBuf act,
+                         cudaStream_t s);
 cudaError_t gemm_exact(const PackedLinear& w, const ActBuf& act, int M, float* out, int ld_out,
                        const GemmEpilogue& epi, uint32_t* err, cudaStream_t s, bool pdl = false,
                        const int* m_dev = nullptr);

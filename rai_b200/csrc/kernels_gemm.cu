@@ -35,8 +35,15 @@ namespace rai {
 
 namespace {
 
-constexpr int kConsumerWarps = 4;
-constexpr int kThreads = (kConsumerWarps + 1) * 32;
+// Consumer warps per CTA: 4 row slabs of 16 rows; with 32-token tiles each
+// slab is split into two warps of 16 tokens, so every SM scheduler has two
+// consumer warps to interleave.
+template <int NTILES>
+struct GemmCfg {
+  static constexpr int kConsumerWarps = NTILES >= 4 ? 8 : 4;
+  static constexpr int kThreads = (kConsumerWarps + 1) * 32;
+  static constexpr int kTilesPerWarp = NTILES >= 4 ? NTILES / 2 : NTILES;
+};
 constexpr uint32_t kMagic = 0x4B400000u;  // 12582912.0f
 constexpr float kMagicF = 12582912.0f;
 
@@ -108,56 +115,38 @@ __global__ void pack8_kernel(const uint8_t* __restrict__ codes, const uint8_t* _
 }
 
 // ---------------------------------------------------------------------------
-// Activation quantization: one warp per (token, group).
+// Activation quantization of one (token, group) by one warp.
 // ---------------------------------------------------------------------------
 // Logical byte (slot t, lane L, elem b) of a token row is at t*32 + 4L + b;
 // 16-byte unit u = offset/16 is stored at unit u ^ (token & 7) so the GEMM's
-// B-fragment loads are bank-conflict free.
-__global__ void quantize_kernel(const float* __restrict__ x, int ldx, int M, const int* m_dev,
-                                int K, int gs, int wbits, uint8_t* __restrict__ act, int tok_alloc) {
-  __shared__ float sx[8][128];
-  __shared__ uint32_t sqw[8][32];
-  int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  int g = blockIdx.x;
-  int tok = blockIdx.y * 8 + warp;
-  if (tok >= tok_alloc) return;
-  int mact = m_dev ? *m_dev : M;
-  uint8_t* blk = act + (size_t)g * tok_alloc * kActTokBytes;
+// B-fragment loads are bank-conflict free. xs: the group's len values in
+// shared memory; sqw: 32 words of per-warp shared scratch.
+__device__ __forceinline__ void quant_group_warp(const float* xs, int len, int wbits, int tok, uint8_t* blk,
+                                                 int tok_alloc, uint32_t* sqw) {
+  const int lane = threadIdx.x & 31;
   uint32_t* qrow = reinterpret_cast<uint32_t*>(blk + (size_t)tok * kActRowBytes);
   float2* sc = reinterpret_cast<float2*>(blk + (size_t)tok_alloc * kActRowBytes) + tok;
-  if (tok >= mact) {
-    qrow[lane] = 0;
-    if (lane == 0) *sc = make_float2(0.f, 0.f);
-    return;
-  }
-  const float* xr = x + (size_t)tok * ldx + (size_t)g * gs;
-  int len = min(gs, K - g * gs);
   float amax = 0.f;
-  for (int i = lane; i < gs; i += 32) {
-    float v = i < len ? xr[i] : 0.f;
-    sx[warp][i] = v;
-    amax = fmaxf(amax, fabsf(v));
-  }
+  for (int i = lane; i < len; i += 32) amax = fmaxf(amax, fabsf(xs[i]));
   for (int o = 16; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
   const float lim = wbits == 4 ? 127.f : 63.f;
   const float lo = wbits == 4 ? -128.f : -63.f;
-  float scale = amax > 1e-10f ? __fdiv_rn(amax, lim) : 1.0f;
-  float inv = __fdiv_rn(1.0f, scale);
-  uint8_t* sq = reinterpret_cast<uint8_t*>(sqw[warp]);
-  sqw[warp][lane] = 0;
+  const float scale = amax > 1e-10f ? __fdiv_rn(amax, lim) : 1.0f;
+  const float inv = __fdiv_rn(1.0f, scale);
+  uint8_t* sq = reinterpret_cast<uint8_t*>(sqw);
+  sqw[lane] = 0;
   __syncwarp();
   for (int col = lane; col < len; col += 32) {
-    float r = rintf(__fmul_rn(sx[warp][col], inv));
+    float r = rintf(__fmul_rn(xs[col], inv));
     r = fminf(r, lim);
     r = fmaxf(r, lo);
-    int qv = (int)r;
+    const int qv = (int)r;
     int off;
     if (wbits == 4) {
-      int c = col >> 6, rr = col & 63, L = rr >> 3, b = (rr & 7) >> 1, p = rr & 1;
+      const int c = col >> 6, rr = col & 63, L = rr >> 3, b = (rr & 7) >> 1, p = rr & 1;
       off = (2 * c + p) * 32 + 4 * L + b;
     } else {
-      int t = col >> 5, rr = col & 31;
-      off = t * 32 + rr;  // lane L = rr / 4, elem b = rr % 4
+      off = (col >> 5) * 32 + (col & 31);  // lane L = (col & 31) / 4, elem b = col % 4
     }
     sq[off] = (uint8_t)(int8_t)qv;
   }
@@ -165,19 +154,164 @@ __global__ void quantize_kernel(const float* __restrict__ x, int ldx, int M, con
   // Group sum: lane j accumulates columns 8i + j in order, then the tree.
   float accj = 0.f;
   if (lane < 8) {
-    int chunks8 = len / 8;
-    for (int i = 0; i < chunks8; ++i) accj = __fadd_rn(accj, sx[warp][8 * i + lane]);
+    const int chunks8 = len / 8;
+    for (int i = 0; i < chunks8; ++i) accj = __fadd_rn(accj, xs[8 * i + lane]);
   }
   float a[8];
 #pragma unroll
   for (int j = 0; j < 8; ++j) a[j] = __shfl_sync(0xffffffffu, accj, j);
   float sum = hsum8(a);
-  for (int i = (len / 8) * 8; i < len; ++i) sum = __fadd_rn(sum, sx[warp][i]);
+  for (int i = (len / 8) * 8; i < len; ++i) sum = __fadd_rn(sum, xs[i]);
   // Swizzled store: lane writes 4 bytes of logical unit u = lane / 4.
-  int u = lane >> 2;
-  int phys = ((u ^ (tok & 7)) << 2) | (lane & 3);
-  qrow[phys] = sqw[warp][lane];
+  const int u = lane >> 2;
+  const int phys = ((u ^ (tok & 7)) << 2) | (lane & 3);
+  qrow[phys] = sqw[lane];
   if (lane == 0) *sc = make_float2(scale, sum);
+  __syncwarp();
+}
+
+// Zero codes and (scale, sum) of one (token, group): tokens past the active
+// count up to the next multiple of 8 (the GEMM reads tokens in groups of 8).
+__device__ __forceinline__ void zero_group_warp(int tok, uint8_t* blk, int tok_alloc) {
+  const int lane = threadIdx.x & 31;
+  reinterpret_cast<uint32_t*>(blk + (size_t)tok * kActRowBytes)[lane] = 0;
+  if (lane == 0) reinterpret_cast<float2*>(blk + (size_t)tok_alloc * kActRowBytes)[tok] = make_float2(0.f, 0.f);
+}
+
+// One warp per (token, group) of x.
+__global__ void quantize_kernel(const float* __restrict__ x, int ldx, int M, const int* m_dev,
+                                int K, int gs, int wbits, uint8_t* __restrict__ act, int tok_alloc) {
+  __shared__ float sx[8][128];
+  __shared__ uint32_t sqw[8][32];
+  pdl_wait_prior();
+  pdl_launch_dependents();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = blockIdx.x;
+  const int tok = blockIdx.y * 8 + warp;
+  if (tok >= tok_alloc) return;
+  const int mact = m_dev ? *m_dev : M;
+  uint8_t* blk = act + (size_t)g * tok_alloc * kActTokBytes;
+  if (tok >= mact) {
+    zero_group_warp(tok, blk, tok_alloc);
+    return;
+  }
+  const float* xr = x + (size_t)tok * ldx + (size_t)g * gs;
+  const int len = min(gs, K - g * gs);
+  for (int i = lane; i < len; i += 32) sx[warp][i] = xr[i];
+  __syncwarp();
+  quant_group_warp(sx[warp], len, wbits, tok, blk, tok_alloc, sqw[warp]);
+}
+
+// RMSNorm of rai-infer (rms_norm_with_residual_avx2 / rms_norm_avx2,
+// layers.rs:433-497, 325-376) fused with the quantization of its output:
+// one CTA per token. Sum of squares in two 8-lane FMA accumulators over
+// 16-element strides (+ one extra 8-chunk into the first), lane-wise add,
+// tree, scalar tail; inv = 1/sqrt(ss/n + eps); y = (x * inv) * w; y is then
+// quantized group by group (one warp per group). With `residual` set, x is
+// also copied there (the residual stream).
+__global__ void __launch_bounds__(256) norm_quant_kernel(const float* __restrict__ x, const float* __restrict__ w,
+                                                         int n, float eps, float* __restrict__ residual,
+                                                         const int* m_dev, int M, int gs, int wbits,
+                                                         uint8_t* __restrict__ act, int tok_alloc) {
+  extern __shared__ __align__(16) float sxn[];  // n floats
+  __shared__ float lanes[16];
+  __shared__ float s_inv;
+  __shared__ uint32_t sqw[8][32];
+  pdl_wait_prior();
+  pdl_launch_dependents();
+  const int b = blockIdx.x;
+  const int warp = threadIdx.x >> 5;
+  const int mact = m_dev ? *m_dev : M;
+  const int groups = (n + gs - 1) / gs;
+  if (b >= mact) {
+    if (b < ((mact + 7) & ~7) && b < tok_alloc)
+      for (int g = warp; g < groups; g += 8) zero_group_warp(b, act + (size_t)g * tok_alloc * kActTokBytes, tok_alloc);
+    return;
+  }
+  const float* xr = x + (size_t)b * n;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    const float v = xr[i];
+    sxn[i] = v;
+    if (residual) residual[(size_t)b * n + i] = v;
+  }
+  __syncthreads();
+  const int chunks8 = n / 8, chunks16 = chunks8 / 2;
+  if (threadIdx.x < 16) {
+    const int j = threadIdx.x & 7, half = threadIdx.x >> 3;
+    float acc = 0.f;
+    int c = 0;
+    for (; c + 8 <= chunks16; c += 8) {
+      float v[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) v[u] = sxn[16 * (c + u) + 8 * half + j];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) acc = __fmaf_rn(v[u], v[u], acc);
+    }
+    for (; c < chunks16; ++c) {
+      const float v = sxn[16 * c + 8 * half + j];
+      acc = __fmaf_rn(v, v, acc);
+    }
+    if (half == 0 && 16 * chunks16 + 8 <= n) {
+      const float v = sxn[16 * chunks16 + j];
+      acc = __fmaf_rn(v, v, acc);
+    }
+    lanes[threadIdx.x] = acc;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float a[8];
+    for (int j = 0; j < 8; ++j) a[j] = __fadd_rn(lanes[j], lanes[8 + j]);
+    float ss = hsum8(a);
+    for (int i = chunks8 * 8; i < n; ++i) ss = __fadd_rn(ss, __fmul_rn(sxn[i], sxn[i]));
+    s_inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)n), eps)));
+  }
+  __syncthreads();
+  const float inv = s_inv;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) sxn[i] = __fmul_rn(__fmul_rn(sxn[i], inv), w[i]);
+  __syncthreads();
+  for (int g = warp; g < groups; g += 8)
+    quant_group_warp(sxn + g * gs, min(gs, n - g * gs), wbits, b, act + (size_t)g * tok_alloc * kActTokBytes,
+                     tok_alloc, sqw[warp]);
+}
+
+// SwiGLU of rai-infer (silu_mul_avx2, layers.rs:850-883) fused with the
+// quantization of its output: one warp per (token, group) of the ff-wide
+// activation; gate/up rows are [gate | up] of width 2*ff. Schraudolph's exp
+// for the first (ff/8)*8 columns, the host-libm expf for the tail;
+// y = (x / (1 + e)) * up.
+__global__ void swiglu_quant_kernel(const float* __restrict__ gu, int ff, const int* m_dev, int M, int gs,
+                                    ExpfTable et, uint8_t* __restrict__ act, int tok_alloc) {
+  __shared__ float sx[8][128];
+  __shared__ uint32_t sqw[8][32];
+  pdl_wait_prior();
+  pdl_launch_dependents();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = blockIdx.x;
+  const int tok = blockIdx.y * 8 + warp;
+  if (tok >= tok_alloc) return;
+  const int mact = m_dev ? *m_dev : M;
+  uint8_t* blk = act + (size_t)g * tok_alloc * kActTokBytes;
+  if (tok >= mact) {
+    zero_group_warp(tok, blk, tok_alloc);
+    return;
+  }
+  const int len = min(gs, ff - g * gs);
+  const float* row = gu + (size_t)tok * 2 * ff;
+  const int vec_end = (ff / 8) * 8;
+  for (int i = lane; i < len; i += 32) {
+    const int col = g * gs + i;
+    const float xv = row[col], u = row[ff + col];
+    float sv;
+    if (col < vec_end) {
+      const float e = schraudolph(__fmul_rn(xv, -1.0f));
+      sv = __fdiv_rn(xv, __fadd_rn(1.0f, e));
+    } else {
+      sv = __fdiv_rn(xv, __fadd_rn(1.0f, expf_host(-xv, et)));
+    }
+    sx[warp][i] = __fmul_rn(sv, u);
+  }
+  __syncwarp();
+  quant_group_warp(sx[warp], len, 4, tok, blk, tok_alloc, sqw[warp]);
 }
 
 // ---------------------------------------------------------------------------
@@ -192,6 +326,7 @@ struct GemmParams {
   uint32_t* err;
   const int* m_dev;  // active token count (device); overrides M when set
   int rows, groups, M, tok_alloc, ld_out, mode, stages;
+  int tiles;  // 64-row tiles; work item i = (row tile i % tiles, token chunk i / tiles)
 };
 
 __device__ __forceinline__ void mma_u8s8(uint32_t a0, uint32_t a1, uint32_t b, int32_t d[4]) {
@@ -236,8 +371,10 @@ __device__ __forceinline__ void acc_pair(float* acc, int32_t d0, int32_t d1, uin
 }
 
 template <int WBITS, int NTILES>
-__global__ void __launch_bounds__(kThreads, NTILES >= 4 ? 1 : 2) gemm_exact_kernel(GemmParams p) {
-  constexpr int NT = 8 * NTILES;  // token slots per pass
+__global__ void __launch_bounds__(GemmCfg<NTILES>::kThreads, NTILES >= 3 ? 1 : 2) gemm_exact_kernel(GemmParams p) {
+  constexpr int kConsumerWarps = GemmCfg<NTILES>::kConsumerWarps;
+  constexpr int NW = GemmCfg<NTILES>::kTilesPerWarp;  // N tiles per consumer warp
+  constexpr int NT = 8 * NTILES;  // token slots per work item
   constexpr int kStageBytes = kBlockBytes + NT * kActTokBytes;
   extern __shared__ __align__(128) uint8_t smem[];
   const int S = p.stages;
@@ -245,15 +382,19 @@ __global__ void __launch_bounds__(kThreads, NTILES >= 4 ? 1 : 2) gemm_exact_kern
   uint64_t* empty = full + S;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int tile = blockIdx.x;
-  const int t0 = blockIdx.y * kTokChunk;
-  const int G = p.groups;
-  // Token chunks beyond the active row count (produced on the device) exit
-  // before touching any barrier.
-  if (p.m_dev) {
-    const int mact = *p.m_dev;
-    if (t0 >= mact) return;
-    p.M = mact;
+  const int G = p.groups, tiles = p.tiles;
+  // Persistent CTAs: each walks work items blockIdx.x, + gridDim.x, ...
+  // (chunk-major, so a CTA's first item is token chunk 0 whenever
+  // blockIdx.x < tiles). Chunk 0 always has work: the producer of such a
+  // "lead" CTA requests its first item's weights before waiting on the
+  // previous kernel (programmatic dependent launch). Other CTAs wait first
+  // and exit, before touching any barrier, when they have no item.
+  const bool lead = (int)blockIdx.x < tiles;
+  int mact = p.M;
+  if (!lead) {
+    pdl_wait_prior();
+    if (p.m_dev) mact = *p.m_dev;
+    if ((int)(blockIdx.x / tiles) * kTokChunk >= mact) return;
   }
 
   if (threadIdx.x == 0) {
@@ -268,171 +409,200 @@ __global__ void __launch_bounds__(kThreads, NTILES >= 4 ? 1 : 2) gemm_exact_kern
   if (warp == kConsumerWarps) {
     // ---------------- producer ----------------
     if (lane == 0) {
-      const int nt = min(NT, p.M - t0);
-      const int npad = (nt + 7) & ~7;
-      const uint32_t bytes = kBlockBytes + npad * kActTokBytes;
-      const size_t act_gstride = (size_t)p.tok_alloc * kActTokBytes;
-      auto issue_act = [&](int g, uint8_t* st) {
-        const uint8_t* ab = p.act + (size_t)g * act_gstride;
-        bulk_g2s(st + kBlockBytes, ab + (size_t)t0 * kActRowBytes, npad * kActRowBytes, &full[g % S]);
-        bulk_g2s(st + kBlockBytes + NT * kActRowBytes,
-                 ab + (size_t)p.tok_alloc * kActRowBytes + (size_t)t0 * 8, npad * 8, &full[g % S]);
-      };
-      // Weights do not depend on the previous kernel, so the first ring's
-      // worth is requested before waiting on it (programmatic dependent
-      // launch); activations are requested after.
       const int pre = min(S, G);
-      for (int g = 0; g < pre; ++g) {
-        mbar_arrive_expect_tx(&full[g], bytes);
-        bulk_g2s(smem + (size_t)g * kStageBytes, p.w + ((size_t)tile * G + g) * kBlockBytes, kBlockBytes,
-                 &full[g]);
+      if (lead) {
+        // Weights do not depend on the previous kernel: the first item's
+        // first ring's worth is requested before waiting on it.
+        for (int g = 0; g < pre; ++g) {
+          mbar_expect_tx(&full[g], kBlockBytes);
+          bulk_g2s(smem + (size_t)g * kStageBytes, p.w + ((size_t)blockIdx.x * G + g) * kBlockBytes, kBlockBytes,
+                   &full[g]);
+        }
+        pdl_wait_prior();
+        if (p.m_dev) mact = *p.m_dev;
       }
-      pdl_wait_prior();
-      for (int g = 0; g < pre; ++g) issue_act(g, smem + (size_t)g * kStageBytes);
-      int g = pre;
-      for (; g < G; ++g) {
-        const int s = g % S, n = g / S;
-        if (!mbar_wait(&empty[s], (n - 1) & 1, p.err)) break;
-        uint8_t* st = smem + (size_t)s * kStageBytes;
-        mbar_arrive_expect_tx(&full[s], bytes);
-        bulk_g2s(st, p.w + ((size_t)tile * G + g) * kBlockBytes, kBlockBytes, &full[s]);
-        issue_act(g, st);
+      const size_t act_gstride = (size_t)p.tok_alloc * kActTokBytes;
+      uint32_t gc = 0;  // groups issued by this CTA so far (ring position)
+      bool ok = true, first = true;
+      for (int item = blockIdx.x; ok; item += gridDim.x, first = false) {
+        const int tile = item % tiles, t0 = (item / tiles) * kTokChunk;
+        if (t0 >= mact) break;
+        const int nt = min(NT, mact - t0);
+        const int npad = (nt + 7) & ~7;
+        const uint32_t abytes = npad * kActTokBytes;
+        for (int g = 0; g < G; ++g, ++gc) {
+          const int s = gc % S;
+          const uint32_t n = gc / S;
+          if (n > 0 && !mbar_wait(&empty[s], (n - 1) & 1, p.err)) { ok = false; break; }
+          uint8_t* st = smem + (size_t)s * kStageBytes;
+          const bool prefetched = lead && first && g < pre;
+          mbar_arrive_expect_tx(&full[s], prefetched ? abytes : kBlockBytes + abytes);
+          if (!prefetched)
+            bulk_g2s(st, p.w + ((size_t)tile * G + g) * kBlockBytes, kBlockBytes, &full[s]);
+          const uint8_t* ab = p.act + (size_t)g * act_gstride;
+          bulk_g2s(st + kBlockBytes, ab + (size_t)t0 * kActRowBytes, npad * kActRowBytes, &full[s]);
+          bulk_g2s(st + kBlockBytes + NT * kActRowBytes, ab + (size_t)p.tok_alloc * kActRowBytes + (size_t)t0 * 8,
+                   npad * 8, &full[s]);
+        }
       }
-      if (g < G) {
+      if (!ok) {
         // Gave up: wait (bounded) for the copies still in flight, then exit.
-        for (int gg = (g > S ? g - S : 0); gg < g; ++gg) mbar_wait(&full[gg % S], (gg / S) & 1, nullptr);
+        const uint32_t lo = gc > (uint32_t)S ? gc - S : 0;
+        for (uint32_t gg = lo; gg < gc; ++gg) mbar_wait(&full[gg % S], (gg / S) & 1, nullptr);
       }
     }
     return;
   }
 
   // ---------------- consumers ----------------
+  if (lead) {
+    pdl_wait_prior();
+    if (p.m_dev) mact = *p.m_dev;
+  }
   pdl_launch_dependents();
   const int gq = lane >> 2, tq = lane & 3;
-  const int r0 = warp * 16 + gq;  // tile-local rows r0 and r0 + 8
+  const int r0 = (warp & 3) * 16 + gq;  // tile-local rows r0 and r0 + 8
+  const int nbase = (warp >> 2) * NW;   // this warp's first N tile
   const uint64_t magic2 = f2(kMagicF, kMagicF);
-  float facc[NTILES][8][4];
-  float zc[NTILES][4];
+  uint32_t gc = 0;
+  for (int item = blockIdx.x;; item += gridDim.x) {
+    const int tile = item % tiles, t0 = (item / tiles) * kTokChunk;
+    if (t0 >= mact) break;
+    float facc[NW][8][4];
+    float zc[NW][4];
 #pragma unroll
-  for (int n = 0; n < NTILES; ++n) {
+    for (int n = 0; n < NW; ++n) {
 #pragma unroll
-    for (int i = 0; i < 4; ++i) zc[n][i] = 0.f;
+      for (int i = 0; i < 4; ++i) zc[n][i] = 0.f;
 #pragma unroll
-    for (int L = 0; L < 8; ++L)
+      for (int L = 0; L < 8; ++L)
 #pragma unroll
-      for (int i = 0; i < 4; ++i) facc[n][L][i] = 0.f;
-  }
+        for (int i = 0; i < 4; ++i) facc[n][L][i] = 0.f;
+    }
 
-  bool ok = true;
-  for (int g = 0; g < G; ++g) {
-    const int s = g % S;
-    if (!mbar_wait(&full[s], (g / S) & 1, p.err)) { ok = false; break; }
-    const uint8_t* st = smem + (size_t)s * kStageBytes;
-    const uint8_t* W = st;
-    const uint32_t* P = reinterpret_cast<const uint32_t*>(st + kWeightStageBytes);
-    const uint8_t* Q = st + kBlockBytes;
-    const float2* XS = reinterpret_cast<const float2*>(st + kBlockBytes + NT * kActRowBytes);
+    for (int g = 0; g < G; ++g, ++gc) {
+      const int s = gc % S;
+      if (!mbar_wait(&full[s], (gc / S) & 1, p.err)) return;
+      const uint8_t* st = smem + (size_t)s * kStageBytes;
+      const uint8_t* W = st;
+      const uint32_t* P = reinterpret_cast<const uint32_t*>(st + kWeightStageBytes);
+      const uint8_t* Q = st + kBlockBytes;
+      const float2* XS = reinterpret_cast<const float2*>(st + kBlockBytes + NT * kActRowBytes);
 
-    uint32_t A0[8], A1[8];
-    if (WBITS == 4) {
-      uint4 wa = *reinterpret_cast<const uint4*>(W + r0 * kRowGroupBytes + tq * 16);
-      uint4 wb = *reinterpret_cast<const uint4*>(W + (r0 + 8) * kRowGroupBytes + tq * 16);
-      const uint32_t wa_[4] = {wa.x, wa.y, wa.z, wa.w}, wb_[4] = {wb.x, wb.y, wb.z, wb.w};
+      uint32_t A0[8], A1[8];
+      if (WBITS == 4) {
+        uint4 wa = *reinterpret_cast<const uint4*>(W + r0 * kRowGroupBytes + tq * 16);
+        uint4 wb = *reinterpret_cast<const uint4*>(W + (r0 + 8) * kRowGroupBytes + tq * 16);
+        const uint32_t wa_[4] = {wa.x, wa.y, wa.z, wa.w}, wb_[4] = {wb.x, wb.y, wb.z, wb.w};
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        A0[2 * j] = wa_[j] & 0x0F0F0F0Fu;
-        A0[2 * j + 1] = (wa_[j] >> 4) & 0x0F0F0F0Fu;
-        A1[2 * j] = wb_[j] & 0x0F0F0F0Fu;
-        A1[2 * j + 1] = (wb_[j] >> 4) & 0x0F0F0F0Fu;
-      }
-    } else {
-      if (tq < 2) {
-        const uint4* pa = reinterpret_cast<const uint4*>(W + r0 * kRowGroupBytes + tq * 32);
-        const uint4* pb = reinterpret_cast<const uint4*>(W + (r0 + 8) * kRowGroupBytes + tq * 32);
-        uint4 a_lo = pa[0], a_hi = pa[1], b_lo = pb[0], b_hi = pb[1];
-        A0[0] = a_lo.x; A0[1] = a_lo.y; A0[2] = a_lo.z; A0[3] = a_lo.w;
-        A0[4] = a_hi.x; A0[5] = a_hi.y; A0[6] = a_hi.z; A0[7] = a_hi.w;
-        A1[0] = b_lo.x; A1[1] = b_lo.y; A1[2] = b_lo.z; A1[3] = b_lo.w;
-        A1[4] = b_hi.x; A1[5] = b_hi.y; A1[6] = b_hi.z; A1[7] = b_hi.w;
+        for (int j = 0; j < 4; ++j) {
+          A0[2 * j] = wa_[j] & 0x0F0F0F0Fu;
+          A0[2 * j + 1] = (wa_[j] >> 4) & 0x0F0F0F0Fu;
+          A1[2 * j] = wb_[j] & 0x0F0F0F0Fu;
+          A1[2 * j + 1] = (wb_[j] >> 4) & 0x0F0F0F0Fu;
+        }
       } else {
+        if (tq < 2) {
+          const uint4* pa = reinterpret_cast<const uint4*>(W + r0 * kRowGroupBytes + tq * 32);
+          const uint4* pb = reinterpret_cast<const uint4*>(W + (r0 + 8) * kRowGroupBytes + tq * 32);
+          uint4 a_lo = pa[0], a_hi = pa[1], b_lo = pb[0], b_hi = pb[1];
+          A0[0] = a_lo.x; A0[1] = a_lo.y; A0[2] = a_lo.z; A0[3] = a_lo.w;
+          A0[4] = a_hi.x; A0[5] = a_hi.y; A0[6] = a_hi.z; A0[7] = a_hi.w;
+          A1[0] = b_lo.x; A1[1] = b_lo.y; A1[2] = b_lo.z; A1[3] = b_lo.w;
+          A1[4] = b_hi.x; A1[5] = b_hi.y; A1[6] = b_hi.z; A1[7] = b_hi.w;
+        } else {
 #pragma unroll
-        for (int L = 0; L < 8; ++L) A0[L] = A1[L] = 0u;
+          for (int L = 0; L < 8; ++L) A0[L] = A1[L] = 0u;
+        }
       }
-    }
-    const uint32_t p0 = P[r0], p1 = P[r0 + 8];
-    const float ws0 = f16_bits_to_f32((uint16_t)(p0 & 0xFFFF)), wz0 = f16_bits_to_f32((uint16_t)(p0 >> 16));
-    const float ws1 = f16_bits_to_f32((uint16_t)(p1 & 0xFFFF)), wz1 = f16_bits_to_f32((uint16_t)(p1 >> 16));
+      const uint32_t p0 = P[r0], p1 = P[r0 + 8];
+      const float ws0 = f16_bits_to_f32((uint16_t)(p0 & 0xFFFF)), wz0 = f16_bits_to_f32((uint16_t)(p0 >> 16));
+      const float ws1 = f16_bits_to_f32((uint16_t)(p1 & 0xFFFF)), wz1 = f16_bits_to_f32((uint16_t)(p1 >> 16));
 
 #pragma unroll
-    for (int n = 0; n < NTILES; ++n) {
-      const int tb = n * 8 + gq;  // B-fragment token (column gq of the N tile)
-      const uint8_t* qrow = Q + tb * kActRowBytes;
-      const uint4 u0 = *reinterpret_cast<const uint4*>(qrow + (((2 * tq) ^ (tb & 7)) << 4));
-      const uint4 u1 = *reinterpret_cast<const uint4*>(qrow + (((2 * tq + 1) ^ (tb & 7)) << 4));
-      const uint32_t B[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
-      const float2 xa = XS[n * 8 + 2 * tq], xb = XS[n * 8 + 2 * tq + 1];
-      // combined_scale = w_scale * x_scale (gemm.rs:606, 493)
-      const uint64_t xs2 = f2(xa.x, xb.x);
-      const uint64_t c0 = mul2(f2(ws0, ws0), xs2), c1 = mul2(f2(ws1, ws1), xs2);
+      for (int n = 0; n < NW; ++n) {
+        const int tb = (nbase + n) * 8 + gq;  // B-fragment token (column gq of the N tile)
+        const uint8_t* qrow = Q + tb * kActRowBytes;
+        const uint4 u0 = *reinterpret_cast<const uint4*>(qrow + (((2 * tq) ^ (tb & 7)) << 4));
+        const uint4 u1 = *reinterpret_cast<const uint4*>(qrow + (((2 * tq + 1) ^ (tb & 7)) << 4));
+        const uint32_t B[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
+        const float2 xa = XS[(nbase + n) * 8 + 2 * tq], xb = XS[(nbase + n) * 8 + 2 * tq + 1];
+        // combined_scale = w_scale * x_scale (gemm.rs:606, 493)
+        const uint64_t xs2 = f2(xa.x, xb.x);
+        const uint64_t c0 = mul2(f2(ws0, ws0), xs2), c1 = mul2(f2(ws1, ws1), xs2);
 #pragma unroll
-      for (int L = 0; L < 8; ++L) {
-        int32_t d[4];
-        mma_u8s8(A0[L], A1[L], B[L], d);
-        acc_pair(&facc[n][L][0], d[0], d[1], c0, magic2);
-        acc_pair(&facc[n][L][2], d[2], d[3], c1, magic2);
+        for (int L = 0; L < 8; ++L) {
+          int32_t d[4];
+          mma_u8s8(A0[L], A1[L], B[L], d);
+          acc_pair(&facc[n][L][0], d[0], d[1], c0, magic2);
+          acc_pair(&facc[n][L][2], d[2], d[3], c1, magic2);
+        }
+        // zero correction: sum_g w_zero * x_sum, sequential in g (gemm.rs:666-670)
+        zc[n][0] = __fadd_rn(zc[n][0], __fmul_rn(wz0, xa.y));
+        zc[n][1] = __fadd_rn(zc[n][1], __fmul_rn(wz0, xb.y));
+        zc[n][2] = __fadd_rn(zc[n][2], __fmul_rn(wz1, xa.y));
+        zc[n][3] = __fadd_rn(zc[n][3], __fmul_rn(wz1, xb.y));
       }
-      // zero correction: sum_g w_zero * x_sum, sequential in g (gemm.rs:666-670)
-      zc[n][0] = __fadd_rn(zc[n][0], __fmul_rn(wz0, xa.y));
-      zc[n][1] = __fadd_rn(zc[n][1], __fmul_rn(wz0, xb.y));
-      zc[n][2] = __fadd_rn(zc[n][2], __fmul_rn(wz1, xa.y));
-      zc[n][3] = __fadd_rn(zc[n][3], __fmul_rn(wz1, xb.y));
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[s]);
     }
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&empty[s]);
-  }
-  if (!ok) return;
 
-  // Epilogue: horizontal-sum tree + zero correction, then bias / residual.
+    // Epilogue: horizontal-sum tree + zero correction, then bias / residual.
 #pragma unroll
-  for (int n = 0; n < NTILES; ++n) {
+    for (int n = 0; n < NW; ++n) {
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const int row = tile * kTileRows + r0 + ((i & 2) ? 8 : 0);
-      const int tok = t0 + n * 8 + 2 * tq + (i & 1);
-      if (row >= p.rows || tok >= p.M) continue;
-      float a[8];
+      for (int i = 0; i < 4; ++i) {
+        const int row = tile * kTileRows + r0 + ((i & 2) ? 8 : 0);
+        const int tok = t0 + (nbase + n) * 8 + 2 * tq + (i & 1);
+        if (row >= p.rows || tok >= mact) continue;
+        float a[8];
 #pragma unroll
-      for (int L = 0; L < 8; ++L) a[L] = facc[n][L][i];
-      float v = __fadd_rn(hsum8(a), zc[n][i]);
-      const size_t o = (size_t)tok * p.ld_out + row;
-      if (p.mode == kEpiBias) v = __fadd_rn(v, p.bias[row]);
-      else if (p.mode == kEpiResidual) v = __fadd_rn(p.residual[o], v);
-      p.out[o] = v;
+        for (int L = 0; L < 8; ++L) a[L] = facc[n][L][i];
+        float v = __fadd_rn(hsum8(a), zc[n][i]);
+        const size_t o = (size_t)tok * p.ld_out + row;
+        if (p.mode == kEpiBias) v = __fadd_rn(v, p.bias[row]);
+        else if (p.mode == kEpiResidual) v = __fadd_rn(p.residual[o], v);
+        p.out[o] = v;
+      }
     }
   }
+}
+
+int sm_count() {
+  static int n[64] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+  if (!n[dev] && cudaDeviceGetAttribute(&n[dev], cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) n[dev] = 148;
+  return n[dev];
 }
 
 template <int WBITS, int NTILES>
 cudaError_t launch_gemm(const GemmParams& gp, int tiles, int chunks, cudaStream_t s, bool pdl) {
   constexpr int NT = 8 * NTILES;
   constexpr int kStageBytes = kBlockBytes + NT * kActTokBytes;
-  int stages = (int)(((NTILES >= 4 ? 200 : 100) * 1024) / kStageBytes);
+  int stages = (int)(((NTILES >= 3 ? 200 : 100) * 1024) / kStageBytes);
   if (stages > 24) stages = 24;
   if (stages > gp.groups) stages = gp.groups < 2 ? 2 : gp.groups;
   GemmParams p = gp;
   p.stages = stages;
+  p.tiles = tiles;
   size_t smem = (size_t)stages * kStageBytes + 2 * stages * sizeof(uint64_t);
   auto kern = gemm_exact_kernel<WBITS, NTILES>;
+  // One persistent wave: as many CTAs as are resident at once (1 or 2 per
+  // SM), never more than the work items of the static token budget.
+  const long items = (long)tiles * chunks;
+  const long wave = (long)sm_count() * (NTILES >= 3 ? 1 : 2);
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(tiles, chunks);
-  cfg.blockDim = dim3(kThreads);
+  cfg.gridDim = dim3((unsigned)(items < wave ? items : wave));
+  cfg.blockDim = dim3(GemmCfg<NTILES>::kThreads);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = s;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = pdl ? 1 : 0;
+  cfg.numAttrs = 1;  // programmatic dependent launch (see pdl_wait_prior)
+  (void)pdl;
   return cudaLaunchKernelEx(&cfg, kern, p);
 }
 
@@ -473,8 +643,21 @@ cudaError_t pack_linear8(const uint8_t* codes, const uint8_t* params, int rows, 
 cudaError_t quantize_act(const float* x, int ldx, int M, const int* m_dev, int K, int gs, int wbits,
                          ActBuf act, cudaStream_t s) {
   dim3 grid((unsigned)act.groups, (unsigned)ceil_div(act.tok_alloc, 8));
-  quantize_kernel<<<grid, 256, 0, s>>>(x, ldx, M, m_dev, K, gs, wbits, act.data, act.tok_alloc);
-  return cudaGetLastError();
+  return launch_pdl(quantize_kernel, grid, dim3(256), 0, s, x, ldx, M, m_dev, K, gs, wbits, act.data,
+                    act.tok_alloc);
+}
+
+cudaError_t norm_quant(const float* x, const float* w, int n, float eps, float* residual, int M,
+                       const int* m_dev, int gs, int wbits, ActBuf act, cudaStream_t s) {
+  const int rows = (int)min((size_t)act.tok_alloc, round_up((size_t)M, 8));
+  return launch_pdl(norm_quant_kernel, dim3((unsigned)rows), dim3(256), (size_t)n * sizeof(float), s, x, w, n, eps,
+                    residual, m_dev, M, gs, wbits, act.data, act.tok_alloc);
+}
+
+cudaError_t swiglu_quant(const float* gu, int ff, int M, const int* m_dev, int gs, const ExpfTable& et, ActBuf act,
+                         cudaStream_t s) {
+  dim3 grid((unsigned)act.groups, (unsigned)ceil_div(act.tok_alloc, 8));
+  return launch_pdl(swiglu_quant_kernel, grid, dim3(256), 0, s, gu, ff, m_dev, M, gs, et, act.data, act.tok_alloc);
 }
 
 cudaError_t gemm_exact(const PackedLinear& w, const ActBuf& act, int M, float* out, int ld_out,

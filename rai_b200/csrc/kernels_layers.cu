@@ -33,6 +33,8 @@ __global__ void embed_kernel(const uint32_t* __restrict__ ids, const int* m_dev,
                              const uint8_t* __restrict__ codes, const uint8_t* __restrict__ params,
                              int vocab, int hidden, int gs, float embed_scale, float* __restrict__ out,
                              uint32_t* err) {
+  pdl_wait_prior();
+  pdl_launch_dependents();
   int b = blockIdx.x;
   if (b >= active_rows(m_dev, M)) return;
   uint32_t tok = ids[b];
@@ -50,62 +52,6 @@ __global__ void embed_kernel(const uint32_t* __restrict__ ids, const int* m_dev,
     if (embed_scale != 1.0f) v = __fmul_rn(v, embed_scale);
     out[(size_t)b * hidden + c] = v;
   }
-}
-
-// ---------------------------------------------------------------------------
-// One CTA per row. Sum of squares in two 8-lane FMA accumulators over
-// 16-element strides (+ one extra 8-chunk into sq0), lane-wise add, tree,
-// scalar tail; inv = 1/sqrt(ss/n + eps); out = (x * inv) * w.
-__global__ void rmsnorm_kernel(const float* __restrict__ x, const float* __restrict__ w, int n,
-                               float eps, float* __restrict__ out, float* __restrict__ residual,
-                               const int* m_dev, int M) {
-  extern __shared__ float sx[];
-  __shared__ float lanes[16];
-  __shared__ float s_inv;
-  int b = blockIdx.x;
-  if (b >= active_rows(m_dev, M)) return;
-  const float* xr = x + (size_t)b * n;
-  for (int i = threadIdx.x; i < n; i += blockDim.x) {
-    float v = xr[i];
-    sx[i] = v;
-    if (residual) residual[(size_t)b * n + i] = v;
-  }
-  __syncthreads();
-  int chunks8 = n / 8, chunks16 = chunks8 / 2;
-  if (threadIdx.x < 16) {
-    int j = threadIdx.x & 7, half = threadIdx.x >> 3;
-    float acc = 0.f;
-    int c = 0;
-    // Loads are independent of the chain: fetch eight strides ahead.
-    for (; c + 8 <= chunks16; c += 8) {
-      float v[8];
-#pragma unroll
-      for (int u = 0; u < 8; ++u) v[u] = sx[16 * (c + u) + 8 * half + j];
-#pragma unroll
-      for (int u = 0; u < 8; ++u) acc = __fmaf_rn(v[u], v[u], acc);
-    }
-    for (; c < chunks16; ++c) {
-      float v = sx[16 * c + 8 * half + j];
-      acc = __fmaf_rn(v, v, acc);
-    }
-    if (half == 0 && 16 * chunks16 + 8 <= n) {
-      float v = sx[16 * chunks16 + j];
-      acc = __fmaf_rn(v, v, acc);
-    }
-    lanes[threadIdx.x] = acc;
-  }
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    float a[8];
-    for (int j = 0; j < 8; ++j) a[j] = __fadd_rn(lanes[j], lanes[8 + j]);
-    float ss = hsum8(a);
-    for (int i = chunks8 * 8; i < n; ++i) ss = __fadd_rn(ss, __fmul_rn(sx[i], sx[i]));
-    s_inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)n), eps)));
-  }
-  __syncthreads();
-  float inv = s_inv;
-  for (int i = threadIdx.x; i < n; i += blockDim.x)
-    out[(size_t)b * n + i] = __fmul_rn(__fmul_rn(sx[i], inv), w[i]);
 }
 
 // ---------------------------------------------------------------------------
@@ -137,6 +83,8 @@ __global__ void qkv_post_kernel(const float* __restrict__ qkv, int ld, float* __
                                 int qk_mode, float eps, const float* __restrict__ rope_cos,
                                 const float* __restrict__ rope_sin, const StreamKV* __restrict__ kv, int layer,
                                 const RowInfo* __restrict__ rows, const int* m_dev, int M) {
+  pdl_wait_prior();
+  pdl_launch_dependents();
   extern __shared__ float srow[];  // q | k
   __shared__ float s_inv[2];
   int b = blockIdx.x;
@@ -209,6 +157,8 @@ __global__ void __launch_bounds__(ScoreCfg<HD>::CHUNK) attn_scores_kernel(
     const float* __restrict__ q, const StreamKV* __restrict__ kv, int layer, const AttnSeg* __restrict__ segs,
     const int* nseg_dev, int nseg_max, int nh, int nkv, float scale, float softcap, float* __restrict__ scores,
     int n_alloc) {
+  pdl_wait_prior();
+  pdl_launch_dependents();
   constexpr int CH = ScoreCfg<HD>::CHUNK, LD = ScoreCfg<HD>::LD;
   extern __shared__ __align__(16) float sm[];
   float* sk = sm;            // [CH][LD]
@@ -285,6 +235,8 @@ __global__ void __launch_bounds__(ScoreCfg<HD>::CHUNK) attn_scores_kernel(
 __global__ void __launch_bounds__(256) attn_softmax_kernel(const RowInfo* __restrict__ rows, const int* m_dev,
                                                            int M, int nh, int nkv, float* __restrict__ scores,
                                                            int n_alloc, int hb, ExpfTable et, uint32_t* err) {
+  pdl_wait_prior();
+  pdl_launch_dependents();
   extern __shared__ __align__(16) float se_all[];  // [hb][n_alloc]
   __shared__ __align__(8) uint64_t bars[8];
   const int j = blockIdx.x, kvh = blockIdx.y;
@@ -349,11 +301,13 @@ __global__ void __launch_bounds__(256) attn_softmax_kernel(const RowInfo* __rest
 }
 
 // Step 3: out[row][h][d] = fma(p_t, v_t[d], out) over t in order. CTA
-// (kv head, segment); thread (d pair, head pair) carries 2 x 2 chains for
-// each of the segment's rows (RB >= nrows) in registers, so one V load feeds
-// 2 heads x RB rows and one p load 2 dims. V and p tiles stream through a
-// ring of `ns` shared-memory stages filled by bulk copies (warp 0) that
-// complete on mbarriers. Row r only takes positions t <= pos0 + r.
+// (kv head, segment); thread (d pair, head) carries the 2 chains of its dims
+// for each of the segment's rows (RB >= nrows) in registers: one p load
+// (4 positions) feeds 2 dims, one V load (2 dims) feeds RB rows; positions
+// are taken 8 at a time with all loads issued before the FMAs. V and p tiles
+// stream through a ring of `ns` shared-memory stages filled by bulk copies
+// (warp 0) that complete on mbarriers. Row r only takes positions
+// t <= pos0 + r.
 template <int HD>
 struct PvCfg {
   static constexpr int VT = HD >= 128 ? 32 : 64;  // positions per tile
@@ -367,9 +321,9 @@ __device__ __forceinline__ void pv_body(const float* __restrict__ vbase, const f
   constexpr int NDP = HD / 2;
   const int stage_floats = VT * HD + rb_alloc * hpk * VT;
   const int tid = threadIdx.x, lane = tid & 31;
-  const int dp = tid % NDP, hp = tid / NDP;
-  const int d0 = 2 * dp, h0 = 2 * hp, h1 = 2 * hp + 1;
-  const bool active = h0 < hpk, has_h1 = h1 < hpk;
+  const int dp = tid % NDP, h = tid / NDP;
+  const int d0 = 2 * dp;
+  const bool active = h < hpk;
   const int nrows = sg.nrows;
   const int n_max = sg.pos0 + nrows, n_all = sg.pos0 + 1;
   const int ntiles = (n_max + VT - 1) / VT;
@@ -396,9 +350,9 @@ __device__ __forceinline__ void pv_body(const float* __restrict__ vbase, const f
   __syncthreads();
   if (tid < 32)
     for (int s = 0; s < ns && s < ntiles; ++s) issue(s, s);
-  float acc[RB][4];
+  float acc[RB][2];
 #pragma unroll
-  for (int r = 0; r < RB; ++r) acc[r][0] = acc[r][1] = acc[r][2] = acc[r][3] = 0.f;
+  for (int r = 0; r < RB; ++r) acc[r][0] = acc[r][1] = 0.f;
   int tile = 0;
   for (; tile < ntiles; ++tile) {
     const int st = tile % ns;
@@ -406,30 +360,25 @@ __device__ __forceinline__ void pv_body(const float* __restrict__ vbase, const f
     if (!__syncthreads_and(ok)) break;
     const int t0 = tile * VT, cnt = min(VT, n_max - t0);
     const float* sv = sm + (size_t)st * stage_floats + d0;
-    const float* sp = sm + (size_t)st * stage_floats + VT * HD;
+    const float* ph = sm + (size_t)st * stage_floats + VT * HD + (active ? h : 0) * VT;
     if (active) {
-      const float* p0 = sp + h0 * VT;
-      const float* p1 = sp + (has_h1 ? h1 : h0) * VT;
       if (t0 + cnt <= n_all) {
         // Every row sees the whole tile.
         int t = 0;
-        for (; t + 4 <= cnt; t += 4) {
-          float2 v[4];
+        for (; t + 8 <= cnt; t += 8) {
+          float2 v[8];
 #pragma unroll
-          for (int u = 0; u < 4; ++u) v[u] = *reinterpret_cast<const float2*>(sv + (t + u) * HD);
+          for (int u = 0; u < 8; ++u) v[u] = *reinterpret_cast<const float2*>(sv + (t + u) * HD);
 #pragma unroll
           for (int r = 0; r < RB; ++r) {
             if (r < nrows) {
-              const float4 pa = *reinterpret_cast<const float4*>(p0 + r * hpk * VT + t);
-              const float4 pb = *reinterpret_cast<const float4*>(p1 + r * hpk * VT + t);
-              const float a4[4] = {pa.x, pa.y, pa.z, pa.w};
-              const float b4[4] = {pb.x, pb.y, pb.z, pb.w};
+              const float4 pa = *reinterpret_cast<const float4*>(ph + r * hpk * VT + t);
+              const float4 pb = *reinterpret_cast<const float4*>(ph + r * hpk * VT + t + 4);
+              const float p8[8] = {pa.x, pa.y, pa.z, pa.w, pb.x, pb.y, pb.z, pb.w};
 #pragma unroll
-              for (int u = 0; u < 4; ++u) {
-                acc[r][0] = __fmaf_rn(a4[u], v[u].x, acc[r][0]);
-                acc[r][1] = __fmaf_rn(a4[u], v[u].y, acc[r][1]);
-                acc[r][2] = __fmaf_rn(b4[u], v[u].x, acc[r][2]);
-                acc[r][3] = __fmaf_rn(b4[u], v[u].y, acc[r][3]);
+              for (int u = 0; u < 8; ++u) {
+                acc[r][0] = __fmaf_rn(p8[u], v[u].x, acc[r][0]);
+                acc[r][1] = __fmaf_rn(p8[u], v[u].y, acc[r][1]);
               }
             }
           }
@@ -439,11 +388,9 @@ __device__ __forceinline__ void pv_body(const float* __restrict__ vbase, const f
 #pragma unroll
           for (int r = 0; r < RB; ++r) {
             if (r < nrows) {
-              const float a = p0[r * hpk * VT + t], b = p1[r * hpk * VT + t];
+              const float a = ph[r * hpk * VT + t];
               acc[r][0] = __fmaf_rn(a, v.x, acc[r][0]);
               acc[r][1] = __fmaf_rn(a, v.y, acc[r][1]);
-              acc[r][2] = __fmaf_rn(b, v.x, acc[r][2]);
-              acc[r][3] = __fmaf_rn(b, v.y, acc[r][3]);
             }
           }
         }
@@ -454,11 +401,9 @@ __device__ __forceinline__ void pv_body(const float* __restrict__ vbase, const f
 #pragma unroll
           for (int r = 0; r < RB; ++r) {
             if (r < nrows && r >= rmin) {
-              const float a = p0[r * hpk * VT + t], b = p1[r * hpk * VT + t];
+              const float a = ph[r * hpk * VT + t];
               acc[r][0] = __fmaf_rn(a, v.x, acc[r][0]);
               acc[r][1] = __fmaf_rn(a, v.y, acc[r][1]);
-              acc[r][2] = __fmaf_rn(b, v.x, acc[r][2]);
-              acc[r][3] = __fmaf_rn(b, v.y, acc[r][3]);
             }
           }
         }
@@ -476,23 +421,21 @@ __device__ __forceinline__ void pv_body(const float* __restrict__ vbase, const f
   }
   if (active) {
 #pragma unroll
-    for (int r = 0; r < RB; ++r) {
-      if (r < nrows) {
-        float* o = out + (size_t)(sg.row0 + r) * nh * HD + d0;
-        *reinterpret_cast<float2*>(o + (size_t)(kvh * hpk + h0) * HD) = make_float2(acc[r][0], acc[r][1]);
-        if (has_h1)
-          *reinterpret_cast<float2*>(o + (size_t)(kvh * hpk + h1) * HD) = make_float2(acc[r][2], acc[r][3]);
-      }
-    }
+    for (int r = 0; r < RB; ++r)
+      if (r < nrows)
+        *reinterpret_cast<float2*>(out + (size_t)(sg.row0 + r) * nh * HD + (size_t)(kvh * hpk + h) * HD + d0) =
+            make_float2(acc[r][0], acc[r][1]);
   }
 }
 
 template <int HD>
-__global__ void __launch_bounds__(256) attn_pv_kernel(const StreamKV* __restrict__ kv, int layer,
+__global__ void __launch_bounds__(512) attn_pv_kernel(const StreamKV* __restrict__ kv, int layer,
                                                       const AttnSeg* __restrict__ segs, const int* nseg_dev,
                                                       int nseg_max, int nh, int nkv, const float* __restrict__ p,
                                                       int n_alloc, int rb_alloc, int ns, float* __restrict__ out,
                                                       uint32_t* err) {
+  pdl_wait_prior();
+  pdl_launch_dependents();
   extern __shared__ __align__(16) float sm[];
   __shared__ __align__(8) uint64_t bars[kPvMaxStages];
   const int kvh = blockIdx.x, si = blockIdx.y;
@@ -509,25 +452,6 @@ __global__ void __launch_bounds__(256) attn_pv_kernel(const StreamKV* __restrict
 }
 
 // ---------------------------------------------------------------------------
-// act[b][i] = silu(gate) * up with gate/up rows [gate | up] of width 2*ff.
-__global__ void swiglu_kernel(const float* __restrict__ gu, int ff, float* __restrict__ act,
-                              const int* m_dev, int M, ExpfTable et) {
-  int b = blockIdx.y;
-  if (b >= active_rows(m_dev, M)) return;
-  int i = blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= ff) return;
-  float x = gu[(size_t)b * 2 * ff + i], u = gu[(size_t)b * 2 * ff + ff + i];
-  float s;
-  if (i < (ff / 8) * 8) {
-    float e = schraudolph(__fmul_rn(x, -1.0f));
-    s = __fdiv_rn(x, __fadd_rn(1.0f, e));
-  } else {
-    s = __fdiv_rn(x, __fadd_rn(1.0f, expf_host(-x, et)));
-  }
-  act[(size_t)b * ff + i] = __fmul_rn(s, u);
-}
-
-// ---------------------------------------------------------------------------
 // Argmax with the reference's total order (NaN -> -inf first) and ties to
 // the LAST index: max over (orderable key << 32 | index).
 __device__ __forceinline__ unsigned long long argmax_key(float v, uint32_t idx) {
@@ -540,6 +464,8 @@ __device__ __forceinline__ unsigned long long argmax_key(float v, uint32_t idx) 
 
 __global__ void argmax_kernel(const float* __restrict__ logits, int vocab, const int* m_dev, int M,
                               unsigned long long* __restrict__ best) {
+  pdl_wait_prior();
+  pdl_launch_dependents();
   int b = blockIdx.y;
   if (b >= active_rows(m_dev, M)) return;
   unsigned long long k = 0;
@@ -562,6 +488,8 @@ __global__ void argmax_kernel(const float* __restrict__ logits, int vocab, const
 // max_ctx - pos - 1.
 __global__ void ngram_kernel(const uint32_t* __restrict__ ctx_all, int ctx_cap, StreamStep* st_all,
                              const StreamKV* __restrict__ kv, int max_draft, int max_ngram, int min_ngram) {
+  pdl_wait_prior();
+  pdl_launch_dependents();
   __shared__ int best;
   const int sidx = blockIdx.x;
   StreamStep* st = st_all + sidx;
@@ -610,6 +538,8 @@ __global__ void ngram_kernel(const uint32_t* __restrict__ ctx_all, int ctx_cap, 
 __global__ void __launch_bounds__(1024) plan_kernel(StreamStep* st, int n, RowInfo* rows, uint32_t* ids,
                                                     int* m_active, AttnSeg* segs, int* n_segs, int seg_len,
                                                     unsigned long long* best, int best_len) {
+  pdl_wait_prior();
+  pdl_launch_dependents();
   __shared__ unsigned long long wsum[32];
   __shared__ unsigned long long carry;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -666,6 +596,8 @@ __global__ void __launch_bounds__(1024) plan_kernel(StreamStep* st, int n, RowIn
 // Greedy acceptance per stream: accept d_i while argmax_i == d_i; the first
 // mismatch is replaced by argmax_i; if all are accepted the bonus is argmax_k.
 __global__ void accept_kernel(StreamStep* st_all, const unsigned long long* __restrict__ best) {
+  pdl_wait_prior();
+  pdl_launch_dependents();
   if (threadIdx.x != 0) return;
   StreamStep* st = st_all + blockIdx.x;
   const int dl = st->drafted, r0 = st->row0;
@@ -686,14 +618,8 @@ __global__ void accept_kernel(StreamStep* st_all, const unsigned long long* __re
 cudaError_t launch_embed(const uint32_t* ids, const int* m_dev, int M, const uint8_t* codes,
                          const uint8_t* params, int vocab, int hidden, int gs, float embed_scale,
                          float* out, uint32_t* err, cudaStream_t s) {
-  embed_kernel<<<M, 256, 0, s>>>(ids, m_dev, M, codes, params, vocab, hidden, gs, embed_scale, out, err);
-  return cudaGetLastError();
-}
-
-cudaError_t launch_rmsnorm(const float* x, const float* w, int n, float eps, float* out, float* residual,
-                           const int* m_dev, int M, cudaStream_t s) {
-  rmsnorm_kernel<<<M, 256, n * sizeof(float), s>>>(x, w, n, eps, out, residual, m_dev, M);
-  return cudaGetLastError();
+  return launch_pdl(embed_kernel, dim3(M), dim3(256), 0, s, ids, m_dev, M, codes, params, vocab, hidden, gs,
+                    embed_scale, out, err);
 }
 
 cudaError_t launch_qkv_post(float* qkv, int ld, float* q_out, int nh, int nkv, int hd, const float* qn,
@@ -701,9 +627,9 @@ cudaError_t launch_qkv_post(float* qkv, int ld, float* q_out, int nh, int nkv, i
                             const float* rope_sin, const StreamKV* kv, int layer, const RowInfo* rows,
                             const int* m_dev, int M, cudaStream_t s) {
   size_t smem = (size_t)(nh + nkv) * hd * sizeof(float);
-  qkv_post_kernel<<<M, 256, smem, s>>>(qkv, ld, q_out, nh, nkv, hd, qn, kn, qk_mode, eps, rope_cos, rope_sin,
+  return launch_pdl(qkv_post_kernel, dim3(M), dim3(256), smem, s, qkv, ld, q_out, nh, nkv, hd, qn, kn, qk_mode, eps, rope_cos, rope_sin,
                                        kv, layer, rows, m_dev, M);
-  return cudaGetLastError();
+
 }
 
 size_t attention_n_chunks(int n_alloc) { return (size_t)(n_alloc + kScoreChunk - 1) / kScoreChunk; }
@@ -717,7 +643,7 @@ size_t pv_stage_bytes(int hd, int hpk, int rb_alloc) {
   const int vt = hd >= 128 ? 32 : 64;
   return (size_t)(vt * hd + rb_alloc * hpk * vt) * sizeof(float);
 }
-int pv_threads(int hd, int hpk) { return ((hd / 2) * ((hpk + 1) / 2) + 31) / 32 * 32; }
+int pv_threads(int hd, int hpk) { return ((hd / 2) * hpk + 31) / 32 * 32; }
 }  // namespace
 
 int build_segments(const RowInfo* rows, int M, int seg_len, AttnSeg* segs) {
@@ -741,21 +667,24 @@ cudaError_t launch_attention(const float* q, float* out, const StreamKV* kv, int
   const size_t sm1 = scores_smem_bytes(hd, hpk, seg_rows);
   int hb = (int)std::min<size_t>((size_t)hpk, kAttnMaxSmem / ((size_t)n_alloc * sizeof(float)));
   const size_t stage = pv_stage_bytes(hd, hpk, seg_rows);
-  // Stages: as many as fit ~110 KB (two CTAs per SM), at least 2, at most 4.
-  const int ns = (int)std::max<size_t>(2, std::min<size_t>(kPvMaxStages, (110 * 1024) / stage));
+  // Stages: as many as fit ~72 KB (three CTAs per SM), at least 2, at most 4.
+  const int ns = (int)std::max<size_t>(2, std::min<size_t>(kPvMaxStages, (72 * 1024) / stage));
   const size_t sm3 = (size_t)ns * stage;
   const int t3 = pv_threads(hd, hpk);
-  if (hb < 1 || sm1 > kAttnMaxSmem || sm3 > kAttnMaxSmem || t3 > 256) return cudaErrorInvalidValue;
+  if (hb < 1 || sm1 > kAttnMaxSmem || sm3 > kAttnMaxSmem || t3 > 512) return cudaErrorInvalidValue;
   const size_t sm2 = (size_t)hb * n_alloc * sizeof(float);
   dim3 g1(nkv, nseg_max, nch), g2(M, nkv), g3(nkv, nseg_max);
 #define RAI_ATTN(HDV)                                                                                        \
   case HDV:                                                                                                  \
-    attn_scores_kernel<HDV><<<g1, ScoreCfg<HDV>::CHUNK, sm1, s>>>(q, kv, layer, segs, nseg_dev, nseg_max,    \
-                                                                  nh, nkv, scale, softcap, scores, n_alloc); \
-    attn_softmax_kernel<<<g2, 256, sm2, s>>>(rows, m_dev, M, nh, nkv, scores, n_alloc, hb, et, err);         \
-    attn_pv_kernel<HDV><<<g3, t3, sm3, s>>>(kv, layer, segs, nseg_dev, nseg_max, nh, nkv, scores, n_alloc,   \
-                                            seg_rows, ns, out, err);                                         \
-    break;
+    if (cudaError_t e = launch_pdl(attn_scores_kernel<HDV>, g1, dim3(ScoreCfg<HDV>::CHUNK), sm1, s, q, kv,   \
+                                   layer, segs, nseg_dev, nseg_max, nh, nkv, scale, softcap, scores,        \
+                                   n_alloc))                                                                \
+      return e;                                                                                             \
+    if (cudaError_t e = launch_pdl(attn_softmax_kernel, g2, dim3(256), sm2, s, rows, m_dev, M, nh, nkv,      \
+                                   scores, n_alloc, hb, et, err))                                           \
+      return e;                                                                                             \
+    return launch_pdl(attn_pv_kernel<HDV>, g3, dim3(t3), sm3, s, kv, layer, segs, nseg_dev, nseg_max, nh,   \
+                      nkv, (const float*)scores, n_alloc, seg_rows, ns, out, err);
   switch (hd) {
     RAI_ATTN(16)
     RAI_ATTN(32)
@@ -784,38 +713,28 @@ cudaError_t init_layer_attributes() {
   return e;
 }
 
-cudaError_t launch_swiglu(const float* gu, int ff, float* act, const int* m_dev, int M, const ExpfTable& et,
-                          cudaStream_t s) {
-  dim3 grid((ff + 255) / 256, M);
-  swiglu_kernel<<<grid, 256, 0, s>>>(gu, ff, act, m_dev, M, et);
-  return cudaGetLastError();
-}
-
 cudaError_t launch_argmax(const float* logits, int vocab, const int* m_dev, int M, unsigned long long* best,
                           cudaStream_t s) {
   int blocks = (vocab + 4095) / 4096;
   if (blocks > 64) blocks = 64;
   dim3 grid(blocks, M);
-  argmax_kernel<<<grid, 256, 0, s>>>(logits, vocab, m_dev, M, best);
-  return cudaGetLastError();
+  return launch_pdl(argmax_kernel, grid, dim3(256), 0, s, logits, vocab, m_dev, M, best);
 }
 
 cudaError_t launch_ngram(const uint32_t* ctx, int ctx_cap, StreamStep* st, const StreamKV* kv, int n,
                          int max_draft, int max_ngram, int min_ngram, cudaStream_t s) {
-  ngram_kernel<<<n, 1024, 0, s>>>(ctx, ctx_cap, st, kv, max_draft, max_ngram, min_ngram);
-  return cudaGetLastError();
+  return launch_pdl(ngram_kernel, dim3(n), dim3(1024), 0, s, ctx, ctx_cap, st, kv, max_draft, max_ngram, min_ngram);
 }
 
 cudaError_t launch_plan(StreamStep* st, int n, RowInfo* rows, uint32_t* ids, int* m_active, AttnSeg* segs,
                         int* n_segs, int seg_len, unsigned long long* best, int best_len, cudaStream_t s) {
   if (seg_len < 1 || seg_len > kSegRows) return cudaErrorInvalidValue;
-  plan_kernel<<<1, 1024, 0, s>>>(st, n, rows, ids, m_active, segs, n_segs, seg_len, best, best_len);
-  return cudaGetLastError();
+  return launch_pdl(plan_kernel, dim3(1), dim3(1024), 0, s, st, n, rows, ids, m_active, segs, n_segs, seg_len, best,
+                    best_len);
 }
 
 cudaError_t launch_accept(StreamStep* st, int n, const unsigned long long* best, cudaStream_t s) {
-  accept_kernel<<<n, 32, 0, s>>>(st, best);
-  return cudaGetLastError();
+  return launch_pdl(accept_kernel, dim3(n), dim3(32), 0, s, st, (const unsigned long long*)best);
 }
 
 }  // namespace rai

@@ -67,8 +67,6 @@ cudaError_t init_layer_attributes();
 cudaError_t launch_embed(const uint32_t* ids, const int* m_dev, int M, const uint8_t* codes,
                          const uint8_t* params, int vocab, int hidden, int gs, float embed_scale,
                          float* out, uint32_t* err, cudaStream_t s);
-cudaError_t launch_rmsnorm(const float* x, const float* w, int n, float eps, float* out, float* residual,
-                           const int* m_dev, int M, cudaStream_t s);
 cudaError_t launch_qkv_post(float* qkv, int ld, float* q_out, int nh, int nkv, int hd, const float* qn,
                             const float* kn, int qk_mode, float eps, const float* rope_cos,
                             const float* rope_sin, const StreamKV* kv, int layer, const RowInfo* rows,
@@ -85,8 +83,6 @@ cudaError_t launch_attention(const float* q, float* out, const StreamKV* kv, int
 // Group host rows into segments (runs of one stream at consecutive
 // positions, at most seg_len <= kSegRows long); returns the count (<= M).
 int build_segments(const RowInfo* rows, int M, int seg_len, AttnSeg* segs);
-cudaError_t launch_swiglu(const float* gu, int ff, float* act, const int* m_dev, int M, const ExpfTable& et,
-                          cudaStream_t s);
 cudaError_t launch_argmax(const float* logits, int vocab, const int* m_dev, int M, unsigned long long* best,
                           cudaStream_t s);
 // Draft search for each of n streams; ctx for stream i at ctx + i * ctx_cap.

@@ -464,8 +464,7 @@ int forward(Batch* B, int M, const int* m_dev, int nseg, const int* nseg_dev, in
   e_res.residual = B->resid;
   for (size_t li = 0; li < c.num_layers; ++li) {
     const LayerDev& L = Mo->layers[li];
-    RAI_CUDA(rai::launch_rmsnorm(B->hidden, L.in_norm, h, eps, B->normed, B->resid, m_dev, M, s));
-    RAI_CUDA(rai::quantize_act(B->normed, h, M, m_dev, h, gs, 4, B->act_h, s));
+    RAI_CUDA(rai::norm_quant(B->hidden, L.in_norm, h, eps, B->resid, M, m_dev, gs, 4, B->act_h, s));
     rai::GemmEpilogue e_qkv;
     if (L.bias_qkv) { e_qkv.mode = rai::kEpiBias; e_qkv.bias = L.bias_qkv; }
     RAI_CUDA(rai::gemm_exact(L.qkv, B->act_h, M, B->qkv, qd + 2 * kvd, e_qkv, err, s, false, m_dev));
@@ -476,18 +475,15 @@ int forward(Batch* B, int M, const int* m_dev, int nseg, const int* nseg_dev, in
                                    Mo->expf, err, s));
     RAI_CUDA(rai::quantize_act(B->attn, qd, M, m_dev, qd, gs, 4, B->act_q, s));
     RAI_CUDA(rai::gemm_exact(L.o, B->act_q, M, B->hidden, h, e_res, err, s, false, m_dev));
-    RAI_CUDA(rai::launch_rmsnorm(B->hidden, L.post_norm, h, eps, B->normed, B->resid, m_dev, M, s));
-    RAI_CUDA(rai::quantize_act(B->normed, h, M, m_dev, h, gs, 4, B->act_h, s));
+    RAI_CUDA(rai::norm_quant(B->hidden, L.post_norm, h, eps, B->resid, M, m_dev, gs, 4, B->act_h, s));
     RAI_CUDA(rai::gemm_exact(L.gateup, B->act_h, M, B->gu, 2 * ffd, rai::GemmEpilogue{}, err, s, false, m_dev));
-    RAI_CUDA(rai::launch_swiglu(B->gu, ffd, B->ff, m_dev, M, Mo->expf, s));
-    RAI_CUDA(rai::quantize_act(B->ff, ffd, M, m_dev, ffd, gs, 4, B->act_ff, s));
+    RAI_CUDA(rai::swiglu_quant(B->gu, ffd, M, m_dev, gs, Mo->expf, B->act_ff, s));
     RAI_CUDA(rai::gemm_exact(L.down, B->act_ff, M, B->hidden, h, e_res, err, s, false, m_dev));
   }
   if (logits) {
-    RAI_CUDA(rai::launch_rmsnorm(B->hidden, Mo->final_norm, h, eps, B->normed, nullptr, m_dev, M, s));
-    bool tied = Mo->head.wbits == 8;
-    RAI_CUDA(rai::quantize_act(B->normed, h, M, m_dev, h, tied ? c.embed_group_size : gs, tied ? 8 : 4,
-                               B->act_head, s));
+    const bool tied = Mo->head.wbits == 8;
+    RAI_CUDA(rai::norm_quant(B->hidden, Mo->final_norm, h, eps, nullptr, M, m_dev, tied ? c.embed_group_size : gs,
+                             tied ? 8 : 4, B->act_head, s));
     RAI_CUDA(rai::gemm_exact(Mo->head, B->act_head, M, B->logits, c.vocab_size, rai::GemmEpilogue{}, err, s,
                              false, m_dev));
   }
