@@ -71,8 +71,17 @@ cudaError_t quantize_act(const float* x, int ldx, int M, const int* m_dev, int K
 // M is the static row budget (grid size) and *m_dev the active row count.
 // RMSNorm of x (n wide; x copied to `residual` when set) quantized straight
 // into `act` (one kernel).
+// act.data may be null (no quantization); normed_out (optional) receives the
+// normalized rows as f32.
 cudaError_t norm_quant(const float* x, const float* w, int n, float eps, float* residual, int M,
-                       const int* m_dev, int gs, int wbits, ActBuf act, cudaStream_t s);
+                       const int* m_dev, int gs, int wbits, ActBuf act, cudaStream_t s,
+                       float* normed_out = nullptr);
+// Grouped form of gemm_exact over ne same-shaped weight sets (expert e at
+// w.data + e * w_stride): expert e multiplies activation rows off[e] ..
+// off[e] + cnt[e] (device arrays; off[e] a multiple of 8) and writes the same
+// output rows.
+cudaError_t gemm_grouped(const PackedLinear& w, size_t w_stride, int ne, const int* off, const int* cnt,
+                         const ActBuf& act, float* out, int ld_out, uint32_t* err, cudaStream_t s);
 // SwiGLU of gate/up rows [gate | up] (2*ff wide) quantized straight into `act`.
 cudaError_t swiglu_quant(const float* gu, int ff, int M, const int* m_dev, int gs, const ExpfTable& et, ActBuf act,
                          cudaStream_t s);

@@ -30,6 +30,7 @@
 
 #include "common.cuh"
 #include "kernels.h"
+#include "quant.cuh"
 
 namespace rai {
 
@@ -114,70 +115,6 @@ __global__ void pack8_kernel(const uint8_t* __restrict__ codes, const uint8_t* _
   out[i] = v;
 }
 
-// ---------------------------------------------------------------------------
-// Activation quantization of one (token, group) by one warp.
-// ---------------------------------------------------------------------------
-// Logical byte (slot t, lane L, elem b) of a token row is at t*32 + 4L + b;
-// 16-byte unit u = offset/16 is stored at unit u ^ (token & 7) so the GEMM's
-// B-fragment loads are bank-conflict free. xs: the group's len values in
-// shared memory; sqw: 32 words of per-warp shared scratch.
-__device__ __forceinline__ void quant_group_warp(const float* xs, int len, int wbits, int tok, uint8_t* blk,
-                                                 int tok_alloc, uint32_t* sqw) {
-  const int lane = threadIdx.x & 31;
-  uint32_t* qrow = reinterpret_cast<uint32_t*>(blk + (size_t)tok * kActRowBytes);
-  float2* sc = reinterpret_cast<float2*>(blk + (size_t)tok_alloc * kActRowBytes) + tok;
-  float amax = 0.f;
-  for (int i = lane; i < len; i += 32) amax = fmaxf(amax, fabsf(xs[i]));
-  for (int o = 16; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-  const float lim = wbits == 4 ? 127.f : 63.f;
-  const float lo = wbits == 4 ? -128.f : -63.f;
-  const float scale = amax > 1e-10f ? __fdiv_rn(amax, lim) : 1.0f;
-  const float inv = __fdiv_rn(1.0f, scale);
-  uint8_t* sq = reinterpret_cast<uint8_t*>(sqw);
-  sqw[lane] = 0;
-  __syncwarp();
-  for (int col = lane; col < len; col += 32) {
-    float r = rintf(__fmul_rn(xs[col], inv));
-    r = fminf(r, lim);
-    r = fmaxf(r, lo);
-    const int qv = (int)r;
-    int off;
-    if (wbits == 4) {
-      const int c = col >> 6, rr = col & 63, L = rr >> 3, b = (rr & 7) >> 1, p = rr & 1;
-      off = (2 * c + p) * 32 + 4 * L + b;
-    } else {
-      off = (col >> 5) * 32 + (col & 31);  // lane L = (col & 31) / 4, elem b = col % 4
-    }
-    sq[off] = (uint8_t)(int8_t)qv;
-  }
-  __syncwarp();
-  // Group sum: lane j accumulates columns 8i + j in order, then the tree.
-  float accj = 0.f;
-  if (lane < 8) {
-    const int chunks8 = len / 8;
-    for (int i = 0; i < chunks8; ++i) accj = __fadd_rn(accj, xs[8 * i + lane]);
-  }
-  float a[8];
-#pragma unroll
-  for (int j = 0; j < 8; ++j) a[j] = __shfl_sync(0xffffffffu, accj, j);
-  float sum = hsum8(a);
-  for (int i = (len / 8) * 8; i < len; ++i) sum = __fadd_rn(sum, xs[i]);
-  // Swizzled store: lane writes 4 bytes of logical unit u = lane / 4.
-  const int u = lane >> 2;
-  const int phys = ((u ^ (tok & 7)) << 2) | (lane & 3);
-  qrow[phys] = sqw[lane];
-  if (lane == 0) *sc = make_float2(scale, sum);
-  __syncwarp();
-}
-
-// Zero codes and (scale, sum) of one (token, group): tokens past the active
-// count up to the next multiple of 8 (the GEMM reads tokens in groups of 8).
-__device__ __forceinline__ void zero_group_warp(int tok, uint8_t* blk, int tok_alloc) {
-  const int lane = threadIdx.x & 31;
-  reinterpret_cast<uint32_t*>(blk + (size_t)tok * kActRowBytes)[lane] = 0;
-  if (lane == 0) reinterpret_cast<float2*>(blk + (size_t)tok_alloc * kActRowBytes)[tok] = make_float2(0.f, 0.f);
-}
-
 // One warp per (token, group) of x.
 __global__ void quantize_kernel(const float* __restrict__ x, int ldx, int M, const int* m_dev,
                                 int K, int gs, int wbits, uint8_t* __restrict__ act, int tok_alloc) {
@@ -192,7 +129,8 @@ __global__ void quantize_kernel(const float* __restrict__ x, int ldx, int M, con
   const int mact = m_dev ? *m_dev : M;
   uint8_t* blk = act + (size_t)g * tok_alloc * kActTokBytes;
   if (tok >= mact) {
-    zero_group_warp(tok, blk, tok_alloc);
+    // The GEMM reads tokens in groups of 8: zero up to the next multiple.
+    if (tok < ((mact + 7) & ~7)) zero_group_warp(tok, blk, tok_alloc);
     return;
   }
   const float* xr = x + (size_t)tok * ldx + (size_t)g * gs;
@@ -211,8 +149,9 @@ __global__ void quantize_kernel(const float* __restrict__ x, int ldx, int M, con
 // also copied there (the residual stream).
 __global__ void __launch_bounds__(256) norm_quant_kernel(const float* __restrict__ x, const float* __restrict__ w,
                                                          int n, float eps, float* __restrict__ residual,
-                                                         const int* m_dev, int M, int gs, int wbits,
-                                                         uint8_t* __restrict__ act, int tok_alloc) {
+                                                         float* __restrict__ normed_out, const int* m_dev, int M,
+                                                         int gs, int wbits, uint8_t* __restrict__ act,
+                                                         int tok_alloc) {
   extern __shared__ __align__(16) float sxn[];  // n floats
   __shared__ float lanes[16];
   __shared__ float s_inv;
@@ -224,7 +163,7 @@ __global__ void __launch_bounds__(256) norm_quant_kernel(const float* __restrict
   const int mact = m_dev ? *m_dev : M;
   const int groups = (n + gs - 1) / gs;
   if (b >= mact) {
-    if (b < ((mact + 7) & ~7) && b < tok_alloc)
+    if (act && b < ((mact + 7) & ~7) && b < tok_alloc)
       for (int g = warp; g < groups; g += 8) zero_group_warp(b, act + (size_t)g * tok_alloc * kActTokBytes, tok_alloc);
     return;
   }
@@ -267,8 +206,13 @@ __global__ void __launch_bounds__(256) norm_quant_kernel(const float* __restrict
   }
   __syncthreads();
   const float inv = s_inv;
-  for (int i = threadIdx.x; i < n; i += blockDim.x) sxn[i] = __fmul_rn(__fmul_rn(sxn[i], inv), w[i]);
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    const float y = __fmul_rn(__fmul_rn(sxn[i], inv), w[i]);
+    sxn[i] = y;
+    if (normed_out) normed_out[(size_t)b * n + i] = y;
+  }
   __syncthreads();
+  if (!act) return;
   for (int g = warp; g < groups; g += 8)
     quant_group_warp(sxn + g * gs, min(gs, n - g * gs), wbits, b, act + (size_t)g * tok_alloc * kActTokBytes,
                      tok_alloc, sqw[warp]);
@@ -292,7 +236,8 @@ __global__ void swiglu_quant_kernel(const float* __restrict__ gu, int ff, const 
   const int mact = m_dev ? *m_dev : M;
   uint8_t* blk = act + (size_t)g * tok_alloc * kActTokBytes;
   if (tok >= mact) {
-    zero_group_warp(tok, blk, tok_alloc);
+    // The GEMM reads tokens in groups of 8: zero up to the next multiple.
+    if (tok < ((mact + 7) & ~7)) zero_group_warp(tok, blk, tok_alloc);
     return;
   }
   const int len = min(gs, ff - g * gs);
@@ -327,7 +272,41 @@ struct GemmParams {
   const int* m_dev;  // active token count (device); overrides M when set
   int rows, groups, M, tok_alloc, ld_out, mode, stages;
   int tiles;  // 64-row tiles; work item i = (row tile i % tiles, token chunk i / tiles)
+  // Grouped (mixture-of-experts) form, when moe_off is set: ne weight sets of
+  // the same shape at w + e * w_stride; expert e's tokens are activation rows
+  // moe_off[e] .. moe_off[e] + moe_cnt[e] (moe_off[e] a multiple of 8).
+  const int* moe_off;
+  const int* moe_cnt;
+  int ne;
+  size_t w_stride;
 };
+
+constexpr int kMaxExperts = 256;
+
+// A work item: the weight set, 64-row tile and token range it covers.
+struct GemmItem {
+  const uint8_t* w;
+  int tile, t0, nt;
+};
+
+// Dense form: item = (row tile item % tiles, token chunk item / tiles).
+// Grouped form: items run expert by expert (cum[e] = items before expert e).
+template <int NT>
+__device__ __forceinline__ bool decode_item(const GemmParams& p, const int* cum, int mact, int item, GemmItem* it) {
+  if (!p.moe_off) {
+    const int t0 = (item / p.tiles) * kTokChunk;
+    if (t0 >= mact) return false;
+    *it = GemmItem{p.w, item % p.tiles, t0, min(NT, mact - t0)};
+    return true;
+  }
+  if (item >= cum[p.ne]) return false;
+  int e = 0;
+  while (cum[e + 1] <= item) ++e;
+  const int local = item - cum[e], chunk = local / p.tiles;
+  *it = GemmItem{p.w + (size_t)e * p.w_stride, local % p.tiles, p.moe_off[e] + chunk * kTokChunk,
+                 min(kTokChunk, p.moe_cnt[e] - chunk * kTokChunk)};
+  return true;
+}
 
 __device__ __forceinline__ void mma_u8s8(uint32_t a0, uint32_t a1, uint32_t b, int32_t d[4]) {
   asm volatile(
@@ -389,12 +368,27 @@ __global__ void __launch_bounds__(GemmCfg<NTILES>::kThreads, NTILES >= 3 ? 1 : 2
   // "lead" CTA requests its first item's weights before waiting on the
   // previous kernel (programmatic dependent launch). Other CTAs wait first
   // and exit, before touching any barrier, when they have no item.
-  const bool lead = (int)blockIdx.x < tiles;
+  // The grouped form learns its items from the routing (written by earlier
+  // kernels), so none of its CTAs is a lead.
+  const bool lead = !p.moe_off && (int)blockIdx.x < tiles;
+  __shared__ int cum[kMaxExperts + 1];
   int mact = p.M;
   if (!lead) {
     pdl_wait_prior();
     if (p.m_dev) mact = *p.m_dev;
-    if ((int)(blockIdx.x / tiles) * kTokChunk >= mact) return;
+    if (!p.moe_off && (int)(blockIdx.x / tiles) * kTokChunk >= mact) return;
+    if (p.moe_off) {
+      if (threadIdx.x == 0) {
+        int c = 0;
+        for (int e = 0; e < p.ne; ++e) {
+          cum[e] = c;
+          c += tiles * ((p.moe_cnt[e] + kTokChunk - 1) / kTokChunk);
+        }
+        cum[p.ne] = c;
+      }
+      __syncthreads();
+      if ((int)blockIdx.x >= cum[p.ne]) return;
+    }
   }
 
   if (threadIdx.x == 0) {
@@ -425,10 +419,10 @@ __global__ void __launch_bounds__(GemmCfg<NTILES>::kThreads, NTILES >= 3 ? 1 : 2
       uint32_t gc = 0;  // groups issued by this CTA so far (ring position)
       bool ok = true, first = true;
       for (int item = blockIdx.x; ok; item += gridDim.x, first = false) {
-        const int tile = item % tiles, t0 = (item / tiles) * kTokChunk;
-        if (t0 >= mact) break;
-        const int nt = min(NT, mact - t0);
-        const int npad = (nt + 7) & ~7;
+        GemmItem it;
+        if (!decode_item<NT>(p, cum, mact, item, &it)) break;
+        const int tile = it.tile, t0 = it.t0;
+        const int npad = (it.nt + 7) & ~7;
         const uint32_t abytes = npad * kActTokBytes;
         for (int g = 0; g < G; ++g, ++gc) {
           const int s = gc % S;
@@ -438,7 +432,7 @@ __global__ void __launch_bounds__(GemmCfg<NTILES>::kThreads, NTILES >= 3 ? 1 : 2
           const bool prefetched = lead && first && g < pre;
           mbar_arrive_expect_tx(&full[s], prefetched ? abytes : kBlockBytes + abytes);
           if (!prefetched)
-            bulk_g2s(st, p.w + ((size_t)tile * G + g) * kBlockBytes, kBlockBytes, &full[s]);
+            bulk_g2s(st, it.w + ((size_t)tile * G + g) * kBlockBytes, kBlockBytes, &full[s]);
           const uint8_t* ab = p.act + (size_t)g * act_gstride;
           bulk_g2s(st + kBlockBytes, ab + (size_t)t0 * kActRowBytes, npad * kActRowBytes, &full[s]);
           bulk_g2s(st + kBlockBytes + NT * kActRowBytes, ab + (size_t)p.tok_alloc * kActRowBytes + (size_t)t0 * 8,
@@ -466,8 +460,9 @@ __global__ void __launch_bounds__(GemmCfg<NTILES>::kThreads, NTILES >= 3 ? 1 : 2
   const uint64_t magic2 = f2(kMagicF, kMagicF);
   uint32_t gc = 0;
   for (int item = blockIdx.x;; item += gridDim.x) {
-    const int tile = item % tiles, t0 = (item / tiles) * kTokChunk;
-    if (t0 >= mact) break;
+    GemmItem it;
+    if (!decode_item<NT>(p, cum, mact, item, &it)) break;
+    const int tile = it.tile, t0 = it.t0;
     float facc[NW][8][4];
     float zc[NW][4];
 #pragma unroll
@@ -554,7 +549,7 @@ __global__ void __launch_bounds__(GemmCfg<NTILES>::kThreads, NTILES >= 3 ? 1 : 2
       for (int i = 0; i < 4; ++i) {
         const int row = tile * kTileRows + r0 + ((i & 2) ? 8 : 0);
         const int tok = t0 + (nbase + n) * 8 + 2 * tq + (i & 1);
-        if (row >= p.rows || tok >= mact) continue;
+        if (row >= p.rows || tok - t0 >= it.nt) continue;
         float a[8];
 #pragma unroll
         for (int L = 0; L < 8; ++L) a[L] = facc[n][L][i];
@@ -648,10 +643,32 @@ cudaError_t quantize_act(const float* x, int ldx, int M, const int* m_dev, int K
 }
 
 cudaError_t norm_quant(const float* x, const float* w, int n, float eps, float* residual, int M,
-                       const int* m_dev, int gs, int wbits, ActBuf act, cudaStream_t s) {
-  const int rows = (int)min((size_t)act.tok_alloc, round_up((size_t)M, 8));
+                       const int* m_dev, int gs, int wbits, ActBuf act, cudaStream_t s, float* normed_out) {
+  const int rows = act.data ? (int)min((size_t)act.tok_alloc, round_up((size_t)M, 8)) : M;
   return launch_pdl(norm_quant_kernel, dim3((unsigned)rows), dim3(256), (size_t)n * sizeof(float), s, x, w, n, eps,
-                    residual, m_dev, M, gs, wbits, act.data, act.tok_alloc);
+                    residual, normed_out, m_dev, M, gs, wbits, act.data, act.tok_alloc);
+}
+
+cudaError_t gemm_grouped(const PackedLinear& w, size_t w_stride, int ne, const int* off, const int* cnt,
+                         const ActBuf& act, float* out, int ld_out, uint32_t* err, cudaStream_t s) {
+  if (ne < 1 || ne > kMaxExperts || w.wbits != 4) return cudaErrorInvalidValue;
+  GemmParams gp = {};
+  gp.w = w.data;
+  gp.act = act.data;
+  gp.out = out;
+  gp.err = err;
+  gp.rows = w.rows;
+  gp.groups = w.groups;
+  gp.M = act.tok_alloc;
+  gp.tok_alloc = act.tok_alloc;
+  gp.ld_out = ld_out;
+  gp.mode = kEpiStore;
+  gp.moe_off = off;
+  gp.moe_cnt = cnt;
+  gp.ne = ne;
+  gp.w_stride = w_stride;
+  // Items are known only on the device: one full persistent wave.
+  return launch_gemm<4, 4>(gp, w.tiles, 1 << 20, s, true);
 }
 
 cudaError_t swiglu_quant(const float* gu, int ff, int M, const int* m_dev, int gs, const ExpfTable& et, ActBuf act,

@@ -1,0 +1,239 @@
+// Mixture-of-experts MLP block on the device (rai-infer/src/model.rs:208-261,
+// route_experts layers.rs:1808-1870), bit for bit:
+//   router logit e = sequential f32 sum over i of router[e][i] * x[i],
+//     starting from -0.0 (Rust iterator sum), no FMA;
+//   softmax: max, expf(v - max) (host libm), sequential sum, v / sum;
+//   top-k by repeated strict '>' scans in expert order (the first maximum
+//     wins); optional renormalization by the sequential sum of the picks;
+//   out = 0; for each pick in order: out += weight * expert_out (mul, add);
+//   hidden = residual + out.
+// Each (token, pick) pair runs the expert's SwiGLU MLP through the exact
+// W4A8 GEMM (per-row arithmetic does not depend on which tokens share a
+// launch), grouped by expert: pairs are sorted by expert into segments that
+// start at multiples of 8 rows.
+#include <cuda_runtime.h>
+
+#include "common.cuh"
+#include "kernels.h"
+#include "moe.h"
+#include "quant.cuh"
+
+namespace rai {
+
+namespace {
+
+__device__ __forceinline__ int active(const int* m_dev, int M) { return m_dev ? *m_dev : M; }
+
+// Router logits: CTA = kRouterTok tokens x ne experts (one thread per expert);
+// the tokens' normalized rows sit in shared memory.
+constexpr int kRouterTok = 4;
+
+__global__ void __launch_bounds__(kMaxMoeExperts) router_kernel(const float* __restrict__ x, const float* __restrict__ router,
+                                                         int h, int ne, const int* m_dev, int M,
+                                                         float* __restrict__ logits) {
+  extern __shared__ __align__(16) float sx[];  // [kRouterTok][h]
+  pdl_wait_prior();
+  pdl_launch_dependents();
+  const int b0 = blockIdx.x * kRouterTok;
+  const int mact = active(m_dev, M);
+  if (b0 >= mact) return;
+  const int nt = min(kRouterTok, mact - b0);
+  for (int i = threadIdx.x; i < nt * h; i += blockDim.x) sx[i] = x[(size_t)b0 * h + i];
+  __syncthreads();
+  const int e = threadIdx.x;
+  if (e >= ne) return;
+  const float* r = router + (size_t)e * h;
+  float acc[kRouterTok];
+#pragma unroll
+  for (int t = 0; t < kRouterTok; ++t) acc[t] = -0.0f;
+  for (int i = 0; i < h; i += 4) {
+    const float4 rv = *reinterpret_cast<const float4*>(r + i);
+    const float r4[4] = {rv.x, rv.y, rv.z, rv.w};
+#pragma unroll
+    for (int t = 0; t < kRouterTok; ++t) {
+      if (t < nt) {
+#pragma unroll
+        for (int u = 0; u < 4; ++u) acc[t] = __fadd_rn(acc[t], __fmul_rn(r4[u], sx[t * h + i + u]));
+      }
+    }
+  }
+#pragma unroll
+  for (int t = 0; t < kRouterTok; ++t)
+    if (t < nt) logits[(size_t)(b0 + t) * ne + e] = acc[t];
+}
+
+// Softmax, top-k and optional renormalization: one thread per token.
+__global__ void route_kernel(float* __restrict__ logits, int ne, int k, int norm_topk, const int* m_dev, int M,
+                             int* __restrict__ experts, float* __restrict__ weights, ExpfTable et) {
+  pdl_wait_prior();
+  pdl_launch_dependents();
+  const int b = blockIdx.x * blockDim.x + threadIdx.x;
+  if (b >= active(m_dev, M)) return;
+  float* p = logits + (size_t)b * ne;
+  float mx = -INFINITY;
+  for (int e = 0; e < ne; ++e) mx = fmaxf(mx, p[e]);
+  float sum = 0.0f;
+  for (int e = 0; e < ne; ++e) {
+    const float v = expf_host(__fsub_rn(p[e], mx), et);
+    p[e] = v;
+    sum = __fadd_rn(sum, v);
+  }
+  for (int e = 0; e < ne; ++e) p[e] = __fdiv_rn(p[e], sum);
+  uint32_t taken[kMaxMoeExperts / 32];
+  for (int i = 0; i < kMaxMoeExperts / 32; ++i) taken[i] = 0u;
+  int count = 0;
+  for (int s = 0; s < k; ++s) {
+    int best = -1;
+    float bv = -INFINITY;
+    for (int e = 0; e < ne; ++e)
+      if (!(taken[e >> 5] >> (e & 31) & 1u) && p[e] > bv) {
+        bv = p[e];
+        best = e;
+      }
+    if (best < 0) break;
+    taken[best >> 5] |= 1u << (best & 31);
+    experts[(size_t)b * k + count] = best;
+    weights[(size_t)b * k + count] = bv;
+    ++count;
+  }
+  for (int s = count; s < k; ++s) {
+    experts[(size_t)b * k + s] = -1;
+    weights[(size_t)b * k + s] = 0.f;
+  }
+  if (norm_topk) {
+    float total = -0.0f;
+    for (int s = 0; s < count; ++s) total = __fadd_rn(total, weights[(size_t)b * k + s]);
+    if (total > 0.0f)
+      for (int s = 0; s < count; ++s) weights[(size_t)b * k + s] = __fdiv_rn(weights[(size_t)b * k + s], total);
+  }
+}
+
+// Sort the (token, pick) pairs by expert: counts, segment offsets (each
+// rounded up to a multiple of 8 rows), then every pair's row. Order within
+// an expert's segment does not affect any result. One CTA.
+__global__ void __launch_bounds__(1024) moe_sort_kernel(const int* __restrict__ experts, int k, int ne,
+                                                        const int* m_dev, int M, int* __restrict__ cnt,
+                                                        int* __restrict__ off, int* __restrict__ row_of_pair,
+                                                        int* __restrict__ pair_of_row, int* __restrict__ n_rows,
+                                                        int rows_cap) {
+  __shared__ int scnt[kMaxMoeExperts], soff[kMaxMoeExperts + 1], sfill[kMaxMoeExperts];
+  pdl_wait_prior();
+  pdl_launch_dependents();
+  const int np = active(m_dev, M) * k;
+  for (int e = threadIdx.x; e < ne; e += blockDim.x) {
+    scnt[e] = 0;
+    sfill[e] = 0;
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < np; i += blockDim.x) {
+    const int e = experts[i];
+    if (e >= 0) atomicAdd(&scnt[e], 1);
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int o = 0;
+    for (int e = 0; e < ne; ++e) {
+      soff[e] = o;
+      o += (scnt[e] + 7) & ~7;
+    }
+    soff[ne] = o;
+    *n_rows = o;
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < ne; e += blockDim.x) {
+    cnt[e] = scnt[e];
+    off[e] = soff[e];
+  }
+  // Padding rows between segments map to no pair.
+  for (int r = threadIdx.x; r < soff[ne] && r < rows_cap; r += blockDim.x) pair_of_row[r] = -1;
+  __syncthreads();
+  for (int i = threadIdx.x; i < np; i += blockDim.x) {
+    const int e = experts[i];
+    if (e < 0) {
+      row_of_pair[i] = -1;
+      continue;
+    }
+    const int r = soff[e] + atomicAdd(&sfill[e], 1);
+    row_of_pair[i] = r;
+    pair_of_row[r] = i;
+  }
+}
+
+// Quantize the normalized rows of the pairs into expert-sorted activation
+// rows (one warp per (row, group)); padding rows are zero.
+__global__ void moe_gather_quant_kernel(const float* __restrict__ x, int h, int k, const int* __restrict__ pair_of_row,
+                                        const int* __restrict__ n_rows, int gs, uint8_t* __restrict__ act,
+                                        int tok_alloc) {
+  __shared__ float sx[8][128];
+  __shared__ uint32_t sqw[8][32];
+  pdl_wait_prior();
+  pdl_launch_dependents();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = blockIdx.x;
+  const int r = blockIdx.y * 8 + warp;
+  if (r >= *n_rows || r >= tok_alloc) return;
+  uint8_t* blk = act + (size_t)g * tok_alloc * kActTokBytes;
+  const int pair = pair_of_row[r];
+  if (pair < 0) {
+    zero_group_warp(r, blk, tok_alloc);
+    return;
+  }
+  const float* xr = x + (size_t)(pair / k) * h + (size_t)g * gs;
+  const int len = min(gs, h - g * gs);
+  for (int i = lane; i < len; i += 32) sx[warp][i] = xr[i];
+  __syncwarp();
+  quant_group_warp(sx[warp], len, 4, r, blk, tok_alloc, sqw[warp]);
+}
+
+// out = residual + sum over picks (in order) of weight * expert_out.
+__global__ void moe_combine_kernel(const float* __restrict__ eo, const int* __restrict__ row_of_pair,
+                                   const float* __restrict__ weights, int k, int h, const float* __restrict__ residual,
+                                   float* __restrict__ out, const int* m_dev, int M) {
+  pdl_wait_prior();
+  pdl_launch_dependents();
+  const int b = blockIdx.y;
+  if (b >= active(m_dev, M)) return;
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= h) return;
+  float acc = 0.0f;
+  for (int s = 0; s < k; ++s) {
+    const int r = row_of_pair[(size_t)b * k + s];
+    if (r < 0) continue;
+    acc = __fadd_rn(acc, __fmul_rn(weights[(size_t)b * k + s], eo[(size_t)r * h + i]));
+  }
+  out[(size_t)b * h + i] = __fadd_rn(residual[(size_t)b * h + i], acc);
+}
+
+}  // namespace
+
+cudaError_t moe_route(const float* x, const float* router, int h, int ne, int k, bool norm_topk, const int* m_dev,
+                      int M, const ExpfTable& et, const MoeBuffers& mb, cudaStream_t s) {
+  if (ne < 2 || ne > kMaxMoeExperts || k < 1 || k > ne || h % 4) return cudaErrorInvalidValue;
+  if (cudaError_t e = launch_pdl(router_kernel, dim3((unsigned)ceil_div(M, kRouterTok)), dim3(kMaxMoeExperts),
+                                 (size_t)kRouterTok * h * sizeof(float), s, x, router, h, ne, m_dev, M, mb.logits))
+    return e;
+  if (cudaError_t e = launch_pdl(route_kernel, dim3((unsigned)ceil_div(M, 128)), dim3(128), 0, s, mb.logits, ne, k,
+                                 (int)norm_topk, m_dev, M, mb.experts, mb.weights, et))
+    return e;
+  return launch_pdl(moe_sort_kernel, dim3(1), dim3(1024), 0, s, (const int*)mb.experts, k, ne, m_dev, M, mb.cnt,
+                    mb.off, mb.row_of_pair, mb.pair_of_row, mb.n_rows, mb.rows_cap);
+}
+
+cudaError_t moe_gather_quant(const float* x, int h, int k, int gs, const MoeBuffers& mb, ActBuf act, cudaStream_t s) {
+  dim3 grid((unsigned)act.groups, (unsigned)ceil_div(act.tok_alloc, 8));
+  return launch_pdl(moe_gather_quant_kernel, grid, dim3(256), 0, s, x, h, k, (const int*)mb.pair_of_row,
+                    (const int*)mb.n_rows, gs, act.data, act.tok_alloc);
+}
+
+cudaError_t moe_combine(const float* eo, int k, int h, const float* residual, float* out, const int* m_dev, int M,
+                        const MoeBuffers& mb, cudaStream_t s) {
+  dim3 grid((unsigned)ceil_div(h, 256), (unsigned)M);
+  return launch_pdl(moe_combine_kernel, grid, dim3(256), 0, s, eo, (const int*)mb.row_of_pair,
+                    (const float*)mb.weights, k, h, residual, out, m_dev, M);
+}
+
+cudaError_t init_moe_attributes() {
+  return cudaFuncSetAttribute(router_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024);
+}
+
+}  // namespace rai

@@ -24,6 +24,7 @@
 #include "common.cuh"
 #include "kernels.h"
 #include "layers.h"
+#include "moe.h"
 #include "raimodel_format.h"
 
 namespace {
@@ -94,6 +95,12 @@ void build_rope(const Config& c, float theta, std::vector<float>& cs, std::vecto
 
 struct LayerDev {
   PackedLinear qkv, o, gateup, down;
+  // Mixture-of-experts layers: every expert's gate|up and down packed back to
+  // back (expert e at data + e * stride); router [ne][hidden] f32.
+  bool moe = false;
+  PackedLinear x_gateup, x_down;
+  size_t x_gu_stride = 0, x_dn_stride = 0;
+  float* router = nullptr;
   float* bias_qkv = nullptr;
   float* in_norm = nullptr;
   float* post_norm = nullptr;
@@ -172,13 +179,13 @@ int upload_vec(rai_model* M, const uint8_t* blob, const raimodel::Vec32& v, floa
 // Pack one or more raw linears with the same cols into one device linear
 // (rows concatenated in order).
 int pack_concat(rai_model* M, const uint8_t* blob_dev, const std::vector<const raimodel::Linear*>& parts,
-                PackedLinear* out) {
+                PackedLinear* out, uint8_t* dst = nullptr) {
   size_t cols = parts[0]->cols, gs = parts[0]->group_size, ng = parts[0]->num_groups();
   size_t rows = 0;
   for (auto* p : parts) rows += p->rows;
-  uint8_t* packed = nullptr;
-  int rc = M->alloc(&packed, rai::packed_linear_bytes(rows, cols, gs));
-  if (rc) return rc;
+  uint8_t* packed = dst;
+  if (!packed)
+    if (int rc = M->alloc(&packed, rai::packed_linear_bytes(rows, cols, gs))) return rc;
   const uint8_t *nib = nullptr, *par = nullptr;
   void* tmp = nullptr;
   if (parts.size() == 1) {
@@ -264,7 +271,8 @@ int check_supported(const Config& c, const raimodel::Model& L) {
   if (c.has_sandwich_norm || c.post_norm) return fail(RAI_ERR_UNSUPPORTED, "sandwich / post-norm placement");
   if (c.global_layer_stride) return fail(RAI_ERR_UNSUPPORTED, "per-layer RoPE bases");
   if (c.final_logit_softcap > 0.f) return fail(RAI_ERR_UNSUPPORTED, "final logit softcap");
-  if (c.num_experts) return fail(RAI_ERR_UNSUPPORTED, "mixture-of-experts layers");
+  if (c.num_experts > rai::kMaxMoeExperts) return fail(RAI_ERR_UNSUPPORTED, "more than 256 experts");
+  if (c.num_experts && c.hidden_size % 4) return fail(RAI_ERR_UNSUPPORTED, "MoE hidden size not a multiple of 4");
   if ((c.bias_mask & 7) != 0 && (c.bias_mask & 7) != 7)
     return fail(RAI_ERR_UNSUPPORTED, "bias on only some of q/k/v");
   if (c.bias_mask & 0x78) return fail(RAI_ERR_UNSUPPORTED, "bias on o/gate/up/down projections");
@@ -296,6 +304,10 @@ struct Batch {
   float *attn = nullptr, *gu = nullptr, *ff = nullptr, *logits = nullptr;
   float* scores = nullptr;  // attention scores, then p, [rows][nh][n_alloc]
   ActBuf act_h, act_q, act_ff, act_head;
+  // Mixture-of-experts scratch (models with experts only).
+  rai::MoeBuffers moe;
+  ActBuf moe_act_x, moe_act_f;
+  float *moe_gu = nullptr, *moe_eo = nullptr;
   rai::RowInfo* rows = nullptr;
   rai::RowInfo* rows_host = nullptr;
   rai::AttnSeg* segs = nullptr;  // attention segments of the rows
@@ -422,6 +434,23 @@ int create_batch(rai_model* m, const std::vector<rai_dec*>& decs, int R, int row
   if (int rc = B->alloc(&B->rows, Rw * sizeof(rai::RowInfo))) return rc;
   if (int rc = B->alloc(&B->ids, Rw * 4)) return rc;
   if (int rc = B->alloc(&B->m_active, 4)) return rc;
+  if (c.num_experts) {
+    const size_t ne = c.num_experts, k = c.experts_per_token, ffe = c.intermediate_size;
+    rai::MoeBuffers& mb = B->moe;
+    mb.rows_cap = (int)(Rw * k + 8 * ne);
+    if (int rc = B->alloc(&mb.logits, Rw * ne * 4)) return rc;
+    if (int rc = B->alloc(&mb.experts, Rw * k * 4)) return rc;
+    if (int rc = B->alloc(&mb.weights, Rw * k * 4)) return rc;
+    if (int rc = B->alloc(&mb.cnt, ne * 4)) return rc;
+    if (int rc = B->alloc(&mb.off, ne * 4)) return rc;
+    if (int rc = B->alloc(&mb.row_of_pair, Rw * k * 4)) return rc;
+    if (int rc = B->alloc(&mb.pair_of_row, (size_t)mb.rows_cap * 4)) return rc;
+    if (int rc = B->alloc(&mb.n_rows, 4)) return rc;
+    if (int rc = alloc_act(B.get(), &B->moe_act_x, mb.rows_cap, (int)h, c.group_size)) return rc;
+    if (int rc = alloc_act(B.get(), &B->moe_act_f, mb.rows_cap, (int)ffe, c.group_size)) return rc;
+    if (int rc = B->alloc(&B->moe_gu, (size_t)mb.rows_cap * 2 * ffe * 4)) return rc;
+    if (int rc = B->alloc(&B->moe_eo, (size_t)mb.rows_cap * h * 4)) return rc;
+  }
   if (int rc = B->alloc(&B->segs, Rw * sizeof(rai::AttnSeg))) return rc;
   if (int rc = B->alloc(&B->n_segs, 4)) return rc;
   if (int rc = B->alloc(&B->best, Rw * 8)) return rc;
@@ -475,6 +504,21 @@ int forward(Batch* B, int M, const int* m_dev, int nseg, const int* nseg_dev, in
                                    Mo->expf, err, s));
     RAI_CUDA(rai::quantize_act(B->attn, qd, M, m_dev, qd, gs, 4, B->act_q, s));
     RAI_CUDA(rai::gemm_exact(L.o, B->act_q, M, B->hidden, h, e_res, err, s, false, m_dev));
+    if (L.moe) {
+      // mlp_block (model.rs:208-261): route, expert SwiGLU MLPs grouped by
+      // expert, weighted sum in pick order, residual add.
+      const int ne = (int)c.num_experts, k = (int)c.experts_per_token;
+      const rai::MoeBuffers& mb = B->moe;
+      RAI_CUDA(rai::norm_quant(B->hidden, L.post_norm, h, eps, B->resid, M, m_dev, gs, 4, ActBuf{}, s, B->normed));
+      RAI_CUDA(rai::moe_route(B->normed, L.router, h, ne, k, c.norm_topk_prob, m_dev, M, Mo->expf, mb, s));
+      RAI_CUDA(rai::moe_gather_quant(B->normed, h, k, gs, mb, B->moe_act_x, s));
+      RAI_CUDA(rai::gemm_grouped(L.x_gateup, L.x_gu_stride, ne, mb.off, mb.cnt, B->moe_act_x, B->moe_gu, 2 * ffd, err,
+                                 s));
+      RAI_CUDA(rai::swiglu_quant(B->moe_gu, ffd, mb.rows_cap, mb.n_rows, gs, Mo->expf, B->moe_act_f, s));
+      RAI_CUDA(rai::gemm_grouped(L.x_down, L.x_dn_stride, ne, mb.off, mb.cnt, B->moe_act_f, B->moe_eo, h, err, s));
+      RAI_CUDA(rai::moe_combine(B->moe_eo, k, h, B->resid, B->hidden, m_dev, M, mb, s));
+      continue;
+    }
     RAI_CUDA(rai::norm_quant(B->hidden, L.post_norm, h, eps, B->resid, M, m_dev, gs, 4, B->act_h, s));
     RAI_CUDA(rai::gemm_exact(L.gateup, B->act_h, M, B->gu, 2 * ffd, rai::GemmEpilogue{}, err, s, false, m_dev));
     RAI_CUDA(rai::swiglu_quant(B->gu, ffd, M, m_dev, gs, Mo->expf, B->act_ff, s));
@@ -727,6 +771,7 @@ int rai_gpu_model_create(const uint8_t* blob, size_t len, int device, rai_model*
   DeviceGuard guard(device);
   RAI_CUDA(rai::init_gemm_attributes());
   RAI_CUDA(rai::init_layer_attributes());
+  RAI_CUDA(rai::init_moe_attributes());
   auto M = std::make_unique<rai_model>();
   M->device = device;
   M->layout = std::move(layout);
@@ -757,8 +802,30 @@ int rai_gpu_model_create(const uint8_t* blob, size_t len, int device, rai_model*
     LayerDev& D = M->layers[li];
     if (int rc = pack_concat(M.get(), blob_dev, {&L.proj[0], &L.proj[1], &L.proj[2]}, &D.qkv)) return rc;
     if (int rc = pack_concat(M.get(), blob_dev, {&L.proj[3]}, &D.o)) return rc;
-    if (int rc = pack_concat(M.get(), blob_dev, {&L.proj[4], &L.proj[5]}, &D.gateup)) return rc;
-    if (int rc = pack_concat(M.get(), blob_dev, {&L.proj[6]}, &D.down)) return rc;
+    if (c.num_experts) {
+      // Expert 0 is stored as the layer's gate/up/down, experts 1.. in
+      // L.experts (format.rs:436-477).
+      D.moe = true;
+      const size_t ne = c.num_experts, ff = L.proj[4].rows, hs = c.hidden_size, gsz = c.group_size;
+      D.x_gu_stride = rai::packed_linear_bytes(2 * ff, hs, gsz);
+      D.x_dn_stride = rai::packed_linear_bytes(hs, ff, gsz);
+      uint8_t *gu = nullptr, *dn = nullptr;
+      if (int rc = M->alloc(&gu, D.x_gu_stride * ne)) return rc;
+      if (int rc = M->alloc(&dn, D.x_dn_stride * ne)) return rc;
+      for (size_t e = 0; e < ne; ++e) {
+        const raimodel::Linear* g = e == 0 ? &L.proj[4] : &L.experts[3 * (e - 1)];
+        const raimodel::Linear* u = e == 0 ? &L.proj[5] : &L.experts[3 * (e - 1) + 1];
+        const raimodel::Linear* d = e == 0 ? &L.proj[6] : &L.experts[3 * (e - 1) + 2];
+        if (int rc = pack_concat(M.get(), blob_dev, {g, u}, &D.x_gateup, gu + e * D.x_gu_stride)) return rc;
+        if (int rc = pack_concat(M.get(), blob_dev, {d}, &D.x_down, dn + e * D.x_dn_stride)) return rc;
+      }
+      D.x_gateup.data = gu;
+      D.x_down.data = dn;
+      if (int rc = upload_vec(M.get(), blob, L.router, &D.router)) return rc;
+    } else {
+      if (int rc = pack_concat(M.get(), blob_dev, {&L.proj[4], &L.proj[5]}, &D.gateup)) return rc;
+      if (int rc = pack_concat(M.get(), blob_dev, {&L.proj[6]}, &D.down)) return rc;
+    }
     if (int rc = upload_vec(M.get(), blob, L.input_norm, &D.in_norm)) return rc;
     if (int rc = upload_vec(M.get(), blob, L.post_attn_norm, &D.post_norm)) return rc;
     if ((c.bias_mask & 7) == 7) {

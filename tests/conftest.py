@@ -45,7 +45,7 @@ def tiny_model_paths(tmp_path_factory):
         "tiny-tied": os.path.join(GOLDEN, "tiny-tied.raimodel"),
         "tiny-untied": os.path.join(GOLDEN, "tiny-untied.raimodel"),
     }
-    for name in ("tiny-llama", "tiny-qwen", "tiny-llama3"):
+    for name in ("tiny-llama", "tiny-qwen", "tiny-llama3", "tiny-moe"):
         p = str(d / f"{name}.raimodel")
         convert.write_synthetic(p, name, seed=7)
         paths[name] = p

@@ -14,7 +14,7 @@ from conftest import periodic_prompt
 pytestmark = pytest.mark.gpu
 torch = pytest.importorskip("torch")
 
-MODELS = ["tiny-tied", "tiny-untied", "tiny-llama", "tiny-qwen", "tiny-llama3"]
+MODELS = ["tiny-tied", "tiny-untied", "tiny-llama", "tiny-qwen", "tiny-llama3", "tiny-moe"]
 
 
 def _open(paths, name, oracle, max_ctx=256):
