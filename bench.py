@@ -11,6 +11,11 @@ ranks (64 / N per GPU, no collective). A step = one lookup step
 the GPU. Weights (550 MB) exceed L2 (126 MB), so no flush is needed.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
+                    [--config tinyllama|qwen|llama8b|olmoe] [--gemm-sweep]
+
+--config picks another BASELINE config (1: qwen, 3: llama8b single GPU,
+4: olmoe single GPU); --gemm-sweep runs config 5 (isolated W4A8 GEMM at the
+Llama-3.1-8B shapes, M in {1..512}).
 
 Prints one JSON line (rank 0). `value` = tokens produced by all streams per
 second of device time (CUDA events around each step's graph, max over ranks);
@@ -32,12 +37,26 @@ import numpy as np
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
-MODEL = "tinyllama-1.1b"
-STREAMS = 64
-PROMPT = 1024
-COPY_FRAC = 0.40
-K_DRAFT = 8
 METRIC = "accepted tok/s per stream + verify-step us at k=8; W4A8 GEMM HBM GB/s vs peak"
+
+# BASELINE configs (BASELINE.json "configs"): model preset, streams, prompt
+# recipe, draft length, the dominant verify GEMM (N x K) for the roofline, and
+# the prompt length of the bounded CPU-baseline sample.
+CONFIGS = {
+    "tinyllama": dict(preset="tinyllama-1.1b", streams=64, prompt=1024, recipe=("copy", 0.40), k=8,
+                      gemm=(2 * 5632, 2048), cpu_prompt=1024,
+                      desc="64 streams, 1024-token prompts (40% copied spans)"),
+    "qwen": dict(preset="qwen2.5-0.5b", streams=1, prompt=256, recipe=("spans", 3, 24), k=8,
+                 gemm=(2 * 4864, 896), cpu_prompt=256,
+                 desc="1 stream, 256-token prompt with three copied 24-token spans"),
+    "llama8b": dict(preset="llama3.1-8b", streams=1, prompt=2048, recipe=("random",), k=8,
+                    gemm=(2 * 14336, 4096), cpu_prompt=64,
+                    desc="1 stream, 2048 random prompt tokens"),
+    "olmoe": dict(preset="olmoe-1b-7b", streams=1, prompt=512, recipe=("copy", 0.30), k=8,
+                  gemm=(3 * 2048, 2048), cpu_prompt=512,
+                  desc="1 stream, 512-token prompt (30% copied spans)"),
+}
+CFG = CONFIGS["tinyllama"]
 
 
 def make_prompt(seed: int, n: int, vocab: int, copy_frac: float) -> list:
@@ -56,11 +75,33 @@ def make_prompt(seed: int, n: int, vocab: int, copy_frac: float) -> list:
     return [int(t) for t in ids]
 
 
+def make_spans_prompt(seed: int, n: int, vocab: int, spans: int, span_len: int) -> list:
+    """Uniform random ids with `spans` spans of `span_len` tokens copied
+    verbatim from earlier in the prompt."""
+    rng = np.random.default_rng(seed)
+    ids = list(rng.integers(0, vocab, size=n))
+    for i in range(spans):
+        dst = int(rng.integers(n // 2, n - span_len)) if i else n - span_len
+        src = int(rng.integers(0, dst - span_len))
+        ids[dst:dst + span_len] = ids[src:src + span_len]
+    return [int(t) for t in ids]
+
+
+def prompt_for(cfg: dict, seed: int, n: int, vocab: int) -> list:
+    kind = cfg["recipe"][0]
+    if kind == "copy":
+        return make_prompt(seed, n, vocab, cfg["recipe"][1])
+    if kind == "spans":
+        return make_spans_prompt(seed, n, vocab, cfg["recipe"][1], cfg["recipe"][2])
+    return [int(t) for t in np.random.default_rng(seed).integers(0, vocab, size=n)]
+
+
 def model_path(rank: int, world: int) -> str:
     from rai_b200 import convert
-    path = os.path.join(tempfile.gettempdir(), f"rai_bench_{MODEL}.raimodel")
+    preset = CFG["preset"]
+    path = os.path.join(tempfile.gettempdir(), f"rai_bench_{preset}.raimodel")
     if rank == 0 and not os.path.exists(path):
-        convert.write_synthetic(path + f".{os.getpid()}", MODEL, seed=0, fast=True)
+        convert.write_synthetic(path + f".{os.getpid()}", preset, seed=0, fast=True)
         os.replace(path + f".{os.getpid()}", path)
     return path
 
@@ -144,15 +185,15 @@ def gemm_traffic_from_profile():
     return None
 
 
-def measure_gemm_roofline(torch, k_rows: int, iters: int = 50):
-    """Time the exact W4A8 GEMM kernel alone (quantize once, then the GEMM
-    launch on pre-quantized activations) at the fused gate/up shape of the
-    model (N = 2*5632, K = 2048) with k_rows verify rows, rotating through
-    enough weight copies to exceed L2, CUDA events on the launching stream."""
+def measure_gemm(torch, N: int, K: int, M: int, iters: int = 50, gs: int = 128):
+    """Time the exact W4A8 GEMM kernel alone (activations quantized once, then
+    the GEMM launch on them) for N output rows, K columns and M tokens,
+    rotating through enough packed weight copies to exceed L2, CUDA events
+    on the launching stream. Weights in the reference format: codes uniform
+    0..15, scale f16 U(0.001, 0.02), zero = -8 scale."""
     from rai_b200 import native
     L = native.lib()
     dev = torch.device("cuda")
-    N, K, gs = 2 * 5632, 2048, 128
     nbytes = L.rai_gpu_w4a8_packed_bytes(N, K, gs)
     copies = max(2, int(np.ceil(3 * 126e6 / nbytes)))
     rng = np.random.default_rng(0)
@@ -166,54 +207,78 @@ def measure_gemm_roofline(torch, k_rows: int, iters: int = 50):
         p = torch.empty(nbytes, dtype=torch.uint8, device=dev)
         native.check(L.rai_gpu_w4a8_pack(nib.data_ptr(), par.data_ptr(), N, K, gs, p.data_ptr(), s))
         packs.append(p)
-    x = torch.randn(k_rows, K, device=dev)
-    sb = L.rai_gpu_w4a8_scratch_bytes(k_rows, K, gs)
+    x = torch.randn(M, K, device=dev)
+    sb = L.rai_gpu_w4a8_scratch_bytes(M, K, gs)
     scratch = torch.empty(sb, dtype=torch.uint8, device=dev)
-    out = torch.empty(k_rows, N, device=dev)
-    native.check(L.rai_gpu_w4a8_quantize(x.data_ptr(), K, k_rows, gs, scratch.data_ptr(), sb, s))
+    out = torch.empty(M, N, device=dev)
+    native.check(L.rai_gpu_w4a8_quantize(x.data_ptr(), K, M, gs, scratch.data_ptr(), sb, s))
     for i in range(5):
         native.check(L.rai_gpu_w4a8_matmul_prequant(out.data_ptr(), packs[i % copies].data_ptr(),
-                                                    scratch.data_ptr(), N, K, k_rows, gs, s))
+                                                    scratch.data_ptr(), N, K, M, gs, s))
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
     for i in range(iters):
         native.check(L.rai_gpu_w4a8_matmul_prequant(out.data_ptr(), packs[i % copies].data_ptr(),
-                                                    scratch.data_ptr(), N, K, k_rows, gs, s))
+                                                    scratch.data_ptr(), N, K, M, gs, s))
     e1.record()
     torch.cuda.synchronize()
     us = e0.elapsed_time(e1) * 1e3 / iters
-    alg = N * K // 2 + N * (K // gs) * 4  # gemm_bench.rs:73-76 accounting
-    return {"kernel": "gemm_exact_kernel<4,2> (W4A8 verify GEMM, gate/up 11264x2048, M=%d)" % k_rows,
-            "us_per_launch": us, "alg_bytes": alg, "gbs": alg / us / 1e3}
+    alg = N * K // 2 + N * (-(-K // gs)) * 4  # gemm_bench.rs:73-76 accounting
+    del packs
+    torch.cuda.empty_cache()
+    return {"N": N, "K": K, "M": M, "us_per_launch": us, "alg_bytes": alg, "gbs": alg / us / 1e3,
+            "int8_tops": 2.0 * M * N * K / us / 1e6}
 
 
-def cpu_baseline_run(steps: int, warmup: int, threads: int | None = None):
+def measure_gemm_roofline(torch, k_rows: int, iters: int = 50):
+    N, K = CFG["gemm"]
+    r = measure_gemm(torch, N, K, k_rows, iters)
+    r["kernel"] = f"gemm_exact_kernel (W4A8 verify GEMM, {N}x{K}, M={k_rows})"
+    return r
+
+
+def gemm_sweep(torch, iters: int):
+    """the isolated W4A8 GEMM at the Llama-3.1-8B
+    projection shapes (K x N), M in {1,2,4,8,9,16,64,512}."""
+    out = []
+    for K, N in [(4096, 4096), (4096, 1024), (4096, 14336), (14336, 4096)]:
+        for M in [1, 2, 4, 8, 9, 16, 64, 512]:
+            r = measure_gemm(torch, N, K, M, iters)
+            out.append({k: (round(v, 3) if isinstance(v, float) else v) for k, v in r.items()})
+    return out
+
+
+def cpu_baseline_run(steps: int, warmup: int):
     """The oracle port of the reference's AVX2 path on the host cores: one
-    stream of the same workload, prefill, `warmup` untimed steps, then
-    `steps` timed lookup steps. Returns (tok/s, produced, seconds, sample)."""
+    stream of the same workload (prompt of the config's CPU sample length),
+    prefill, `warmup` untimed steps, then `steps` timed lookup steps.
+    Returns (tok/s, produced, seconds, sample)."""
     from oracle import oracle as O
     O.build()
     path = model_path(0, 1)
     m = O.Model.load(path)
     vocab = m.config["vocab"]
-    prompt = make_prompt(1000, PROMPT, vocab, COPY_FRAC)
-    d = O.Decoder(m, PROMPT + (steps + warmup + 2) * (K_DRAFT + 1) + 16)
+    k = CFG["k"]
+    n = CFG["cpu_prompt"]
+    prompt = prompt_for(CFG, 1000, n, vocab)
+    d = O.Decoder(m, n + (steps + warmup + 2) * (k + 1) + 16)
     pos = d.prefill(prompt)
     ctx = list(prompt)
     for _ in range(warmup):
-        t, _m = d.step(pos, ctx, K_DRAFT)
+        t, _m = d.step(pos, ctx, k)
         ctx += t
         pos += len(t)
     produced = 0
     t0 = time.perf_counter()
     for _ in range(steps):
-        t, _m = d.step(pos, ctx, K_DRAFT)
+        t, _m = d.step(pos, ctx, k)
         ctx += t
         pos += len(t)
         produced += len(t)
     dt = time.perf_counter() - t0
-    sample = f"1 stream of {MODEL}, {PROMPT}-token prompt, {steps} timed lookup steps (k={K_DRAFT})"
+    sample = (f"1 stream of {CFG['preset']}, {n}-token prompt, {steps} timed lookup steps (k={k}); "
+              "streams are independent, so the job rate is the per-stream rate")
     return produced / dt, produced, dt, sample
 
 
@@ -230,8 +295,8 @@ def run_reference(args):
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt * 1e3 / args.steps,
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "int8xu4->int32->f32",
         "data": "synthetic",
-        "config": {"workload": f"{MODEL} prompt-lookup k={K_DRAFT}, {PROMPT}-token prompts, 40% copied spans",
-                   "streams": 1, "sample": sample},
+        "config": {"workload": f"{CFG['preset']} prompt-lookup k={CFG['k']}: {CFG['desc']}, greedy",
+                   "streams": CFG["streams"], "sample": sample},
         "cpu_baseline": {"value": tps, "unit": "tok/s", "cores": cores, "kind": "port", "sample": sample},
         "e2e": {"value": tps, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
@@ -244,17 +309,37 @@ def main():
     ap.add_argument("--steps", type=int, default=30)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--streams", type=int, default=STREAMS)
+    ap.add_argument("--config", default="tinyllama", choices=sorted(CONFIGS),
+                    help="BASELINE config (default: config 2, the headline)")
+    ap.add_argument("--streams", type=int, default=None, help="override the config's stream count")
+    ap.add_argument("--gemm-sweep", action="store_true",
+                    help="BASELINE config 5: isolated W4A8 GEMM sweep at the Llama-3.1-8B shapes")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--gemm-only", action="store_true",
                     help="time only the isolated verify GEMM (for a small ncu capture) and print it")
+    ap.add_argument("--gemm-shape", default=None, help="N,K,M for --gemm-only (default: the config's verify GEMM)")
     args = ap.parse_args()
+    global CFG
+    CFG = dict(CONFIGS[args.config])
+    if args.streams:
+        CFG["streams"] = args.streams
     if args.impl == "reference":
         return run_reference(args)
     if args.gemm_only:
         import torch
         torch.cuda.set_device(0)
-        print(json.dumps(measure_gemm_roofline(torch, K_DRAFT + 1, iters=args.steps)), flush=True)
+        if args.gemm_shape:
+            n_, k_, m_ = (int(v) for v in args.gemm_shape.split(","))
+            print(json.dumps(measure_gemm(torch, n_, k_, m_, iters=args.steps)), flush=True)
+        else:
+            print(json.dumps(measure_gemm_roofline(torch, CFG["k"] + 1, iters=args.steps)), flush=True)
+        return
+    if args.gemm_sweep:
+        import torch
+        torch.cuda.set_device(0)
+        line = {"metric": "W4A8 GEMM sweep (BASELINE config 5)", "unit": "us / GB/s", "dtype": "int8xu4->int32->f32",
+                "data": "synthetic", "peak_hbm_gbs": peaks()[0], "results": gemm_sweep(torch, max(args.steps, 20))}
+        print(json.dumps(line), flush=True)
         return
 
     import torch
@@ -283,10 +368,11 @@ def main():
         dist.barrier()
     model = rai_b200.RaiModel.load(path, device=local)
     vocab = model.config["vocab_size"]
-    mine = [s for s in range(args.streams) if s % world == rank]
-    max_ctx = PROMPT + (args.steps + args.warmup + 2) * (K_DRAFT + 1) + 16
+    mine = [s for s in range(CFG["streams"]) if s % world == rank]
+    K_DRAFT = CFG["k"]
+    max_ctx = CFG["prompt"] + (args.steps + args.warmup + 2) * (K_DRAFT + 1) + 16
     decs = [rai_b200.LookupDecoder(model, max_ctx) for _ in mine]
-    ctxs = [make_prompt(1000 + s, PROMPT, vocab, COPY_FRAC) for s in mine]
+    ctxs = [prompt_for(CFG, 1000 + s, CFG["prompt"], vocab) for s in mine]
     poss = rai_b200.prefill_many(decs, ctxs)
     cfg = rai_b200.LookupConfig(max_draft=K_DRAFT, max_ngram=3, min_ngram=1)
 
@@ -334,20 +420,20 @@ def main():
     if rank == 0:
         peak, peak_kind = peaks()
         gem = measure_gemm_roofline(torch, K_DRAFT + 1)
-        traffic = gemm_traffic_from_profile()
+        traffic = gemm_traffic_from_profile() if args.config == "tinyllama" else None
+        wmb = convert.weight_bytes_per_step(convert.PRESETS[CFG["preset"]]) / 1e6
         value = produced / dev_s
         e2e = produced / host_s
-        total_streams = args.streams
+        total_streams = CFG["streams"]
         steps_per_stream = args.steps
         line = {
             "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": dev_s * 1e3 / args.steps, "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "int8xu4->int32->f32", "data": "synthetic",
-            "config": {"workload": f"{MODEL} prompt-lookup k={K_DRAFT}: {total_streams} streams, "
-                                   f"{PROMPT}-token prompts (40% copied spans), greedy",
+            "config": {"workload": f"{CFG['preset']} prompt-lookup k={K_DRAFT}: {CFG['desc']}, greedy",
                        "streams": total_streams, "k": K_DRAFT,
                        "parallelism": f"dp{world} (streams sharded; each GPU batches its streams' verify rows)",
-                       "l2": "weights 550 MB > L2 126 MB; no flush needed"},
+                       "l2": f"weights {wmb:.0f} MB (+ KV) per step > L2 126 MB; no flush needed"},
             "per_stream_tok_s": produced / dev_s / total_streams,
             "verify_step_us": dev_s * 1e6 / steps_per_stream,
             "tokens_per_step": produced / (total_streams * steps_per_stream),

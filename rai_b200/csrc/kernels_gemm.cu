@@ -416,7 +416,9 @@ __global__ void __launch_bounds__(GemmCfg<NTILES>::kThreads, NTILES >= 3 ? 1 : 2
         if (p.m_dev) mact = *p.m_dev;
       }
       const size_t act_gstride = (size_t)p.tok_alloc * kActTokBytes;
-      uint32_t gc = 0;  // groups issued by this CTA so far (ring position)
+      uint32_t gc = 0;  // groups issued by this CTA so far
+      int s = 0;        // ring stage of group gc (gc % S, kept incrementally)
+      uint32_t n = 0;   // times stage s has been filled before (gc / S)
       bool ok = true, first = true;
       for (int item = blockIdx.x; ok; item += gridDim.x, first = false) {
         GemmItem it;
@@ -425,8 +427,6 @@ __global__ void __launch_bounds__(GemmCfg<NTILES>::kThreads, NTILES >= 3 ? 1 : 2
         const int npad = (it.nt + 7) & ~7;
         const uint32_t abytes = npad * kActTokBytes;
         for (int g = 0; g < G; ++g, ++gc) {
-          const int s = gc % S;
-          const uint32_t n = gc / S;
           if (n > 0 && !mbar_wait(&empty[s], (n - 1) & 1, p.err)) { ok = false; break; }
           uint8_t* st = smem + (size_t)s * kStageBytes;
           const bool prefetched = lead && first && g < pre;
@@ -437,6 +437,10 @@ __global__ void __launch_bounds__(GemmCfg<NTILES>::kThreads, NTILES >= 3 ? 1 : 2
           bulk_g2s(st + kBlockBytes, ab + (size_t)t0 * kActRowBytes, npad * kActRowBytes, &full[s]);
           bulk_g2s(st + kBlockBytes + NT * kActRowBytes, ab + (size_t)p.tok_alloc * kActRowBytes + (size_t)t0 * 8,
                    npad * 8, &full[s]);
+          if (++s == S) {
+            s = 0;
+            ++n;
+          }
         }
       }
       if (!ok) {
@@ -458,7 +462,8 @@ __global__ void __launch_bounds__(GemmCfg<NTILES>::kThreads, NTILES >= 3 ? 1 : 2
   const int r0 = (warp & 3) * 16 + gq;  // tile-local rows r0 and r0 + 8
   const int nbase = (warp >> 2) * NW;   // this warp's first N tile
   const uint64_t magic2 = f2(kMagicF, kMagicF);
-  uint32_t gc = 0;
+  int cs = 0;          // ring stage of the next group
+  uint32_t cphase = 0;  // its fill parity
   for (int item = blockIdx.x;; item += gridDim.x) {
     GemmItem it;
     if (!decode_item<NT>(p, cum, mact, item, &it)) break;
@@ -475,9 +480,13 @@ __global__ void __launch_bounds__(GemmCfg<NTILES>::kThreads, NTILES >= 3 ? 1 : 2
         for (int i = 0; i < 4; ++i) facc[n][L][i] = 0.f;
     }
 
-    for (int g = 0; g < G; ++g, ++gc) {
-      const int s = gc % S;
-      if (!mbar_wait(&full[s], (gc / S) & 1, p.err)) return;
+    for (int g = 0; g < G; ++g) {
+      const int s = cs;
+      if (!mbar_wait(&full[s], cphase, p.err)) return;
+      if (++cs == S) {
+        cs = 0;
+        cphase ^= 1u;
+      }
       const uint8_t* st = smem + (size_t)s * kStageBytes;
       const uint8_t* W = st;
       const uint32_t* P = reinterpret_cast<const uint32_t*>(st + kWeightStageBytes);
@@ -563,6 +572,290 @@ __global__ void __launch_bounds__(GemmCfg<NTILES>::kThreads, NTILES >= 3 ? 1 : 2
   }
 }
 
+// Consumer-only barrier with a vote: true iff every consumer's flag is true.
+__device__ __forceinline__ bool __syncthreads_and_consumers(bool flag, int nthreads) {
+  __shared__ int any_bad;
+  if (threadIdx.x == 0) any_bad = 0;
+  asm volatile("bar.sync 1, %0;" ::"r"(nthreads) : "memory");
+  if (!flag) atomicOr(&any_bad, 1);
+  asm volatile("bar.sync 1, %0;" ::"r"(nthreads) : "memory");
+  const bool ok = any_bad == 0;
+  return ok;
+}
+
+// Named barrier over the consumer warps only (the producer warp has left).
+__device__ __forceinline__ void consumers_sync(int nthreads) {
+  asm volatile("bar.sync 1, %0;" ::"r"(nthreads) : "memory");
+}
+
+// Lane-split form for linears with few rows (the per-warp work of the main
+// kernel then leaves most SMs idle): CTA = 16 weight rows x (8 * NTILES)
+// tokens. Consumer warp j owns the reference lanes 2j, 2j + 1: the eight lane
+// accumulators of a (token, row) are independent until the final horizontal
+// sum, so splitting them over four warps is exact and gives four times the
+// warps. Warp 4 is the producer: per group it bulk-copies the CTA's rows of
+// the packed weight block (codes + params) and the token tile's activation
+// codes and (scale, sum) pairs into a ring of stages. The lane accumulators
+// meet in shared memory for the horizontal sum.
+template <int WBITS, int NTILES>
+__global__ void __launch_bounds__(160, 4) gemm_lanes_kernel(GemmParams p) {
+  constexpr int RS = 1;
+  constexpr int T = 8 * NTILES;  // token slots per CTA
+  constexpr int kConsumers = 4 * RS;
+  constexpr int kCodeBytes = 1024 * RS, kParBytes = 64 * RS;
+  constexpr int kStageBytes = kCodeBytes + kParBytes + T * kActTokBytes;
+  constexpr int kXchgBytes = RS * NTILES * 9 * 128 * (int)sizeof(float);
+  extern __shared__ __align__(128) uint8_t smem[];
+  const int S = p.stages;
+  // The lane-exchange area reuses the ring; the mbarriers sit past both.
+  const int bar_off = S * kStageBytes > kXchgBytes ? S * kStageBytes : kXchgBytes;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + bar_off);
+  uint64_t* empty = full + S;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int tile = blockIdx.x / (4 / RS), sub = blockIdx.x % (4 / RS);
+  const int t0 = blockIdx.y * T;
+  const int G = p.groups;
+  // Token chunk 0 always has work: its producer requests the weights before
+  // waiting on the previous kernel (programmatic dependent launch). Other
+  // chunks wait first and exit, before touching any barrier, when they lie
+  // beyond the active row count (produced on the device).
+  const bool lead = blockIdx.y == 0;
+  if (!lead) {
+    pdl_wait_prior();
+    if (p.m_dev) {
+      const int mact = *p.m_dev;
+      if (t0 >= mact) return;
+      p.M = mact;
+    }
+  }
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kConsumers);
+    }
+    fence_barrier_init();
+  }
+  __syncthreads();
+
+  if (warp == kConsumers) {
+    // ---------------- producer ----------------
+    if (lane == 0) {
+      const int pre = min(S, G);
+      auto issue_w = [&](int g, uint8_t* st) {
+        uint64_t* bar = full + (st - smem) / kStageBytes;
+        const uint8_t* blk = p.w + ((size_t)tile * G + g) * kBlockBytes;
+        bulk_g2s(st, blk + sub * kCodeBytes, kCodeBytes, bar);
+        bulk_g2s(st + kCodeBytes, blk + kWeightStageBytes + sub * kParBytes, kParBytes, bar);
+      };
+      if (lead) {
+        // Weights do not depend on the previous kernel: the first ring's
+        // worth is requested before waiting on it.
+        for (int g = 0; g < pre; ++g) {
+          mbar_expect_tx(&full[g], kCodeBytes + kParBytes);
+          issue_w(g, smem + (size_t)g * kStageBytes);
+        }
+        pdl_wait_prior();
+        if (p.m_dev) p.M = *p.m_dev;
+      }
+      const int nt = min(T, p.M - t0);
+      const int npad = (nt + 7) & ~7;
+      const uint32_t abytes = npad * kActTokBytes;
+      const uint32_t bytes = kCodeBytes + kParBytes + abytes;
+      const size_t act_gstride = (size_t)p.tok_alloc * kActTokBytes;
+      auto issue_act = [&](int g, uint8_t* st) {
+        uint64_t* bar = full + (st - smem) / kStageBytes;
+        const uint8_t* ab = p.act + (size_t)g * act_gstride;
+        uint8_t* d = st + kCodeBytes + kParBytes;
+        bulk_g2s(d, ab + (size_t)t0 * kActRowBytes, npad * kActRowBytes, bar);
+        bulk_g2s(d + T * kActRowBytes, ab + (size_t)p.tok_alloc * kActRowBytes + (size_t)t0 * 8, npad * 8, bar);
+      };
+      for (int g = 0; g < pre; ++g) {
+        mbar_arrive_expect_tx(&full[g], lead ? abytes : bytes);
+        if (!lead) issue_w(g, smem + (size_t)g * kStageBytes);
+        issue_act(g, smem + (size_t)g * kStageBytes);
+      }
+      int g = pre;
+      int s = pre % S;                     // stage of group g
+      uint32_t n = (uint32_t)(pre / S);    // its previous fills
+      for (; g < G; ++g) {
+        if (!mbar_wait(&empty[s], (n - 1) & 1, p.err)) break;
+        uint8_t* st = smem + (size_t)s * kStageBytes;
+        mbar_arrive_expect_tx(&full[s], bytes);
+        issue_w(g, st);
+        issue_act(g, st);
+        if (++s == S) {
+          s = 0;
+          ++n;
+        }
+      }
+      if (g < G) {
+        // Gave up: wait (bounded) for the copies still in flight, then exit.
+        for (int gg = (g > S ? g - S : 0); gg < g; ++gg) mbar_wait(&full[gg % S], (gg / S) & 1, nullptr);
+      }
+    }
+    return;
+  }
+
+  // ---------------- consumers ----------------
+  if (lead) {
+    pdl_wait_prior();
+    if (p.m_dev) p.M = *p.m_dev;
+  }
+  pdl_launch_dependents();
+  const int slab = warp >> 2, j = warp & 3;
+  const int gq = lane >> 2, tq = lane & 3;
+  const int rl = slab * 16 + gq;  // CTA-local rows rl and rl + 8
+  const uint64_t magic2 = f2(kMagicF, kMagicF);
+  // acc[n][l][i]: lane 2j + l; i = 0, 1: row rl, tokens 2tq, 2tq + 1;
+  // i = 2, 3: row rl + 8 (the mma C-fragment order).
+  float acc[NTILES][2][4];
+  float zc[NTILES][4];
+#pragma unroll
+  for (int n = 0; n < NTILES; ++n) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) zc[n][i] = acc[n][0][i] = acc[n][1][i] = 0.f;
+  }
+
+  bool ok = true;
+  int cs = 0;
+  uint32_t cphase = 0;
+  for (int g = 0; g < G; ++g) {
+    const int s = cs;
+    if (!mbar_wait(&full[s], cphase, p.err)) { ok = false; break; }
+    if (++cs == S) {
+      cs = 0;
+      cphase ^= 1u;
+    }
+    const uint8_t* st = smem + (size_t)s * kStageBytes;
+    const uint8_t* W = st;
+    const uint32_t* P = reinterpret_cast<const uint32_t*>(st + kCodeBytes);
+    const uint8_t* Q = st + kCodeBytes + kParBytes;
+    const float2* XS = reinterpret_cast<const float2*>(Q + T * kActRowBytes);
+
+    uint32_t a0[2], a1[2];
+    if (WBITS == 4) {
+      const uint32_t wa = *reinterpret_cast<const uint32_t*>(W + rl * kRowGroupBytes + tq * 16 + 4 * j);
+      const uint32_t wb = *reinterpret_cast<const uint32_t*>(W + (rl + 8) * kRowGroupBytes + tq * 16 + 4 * j);
+      a0[0] = wa & 0x0F0F0F0Fu;
+      a0[1] = (wa >> 4) & 0x0F0F0F0Fu;
+      a1[0] = wb & 0x0F0F0F0Fu;
+      a1[1] = (wb >> 4) & 0x0F0F0F0Fu;
+    } else {
+      if (tq < 2) {
+        const uint2 wa = *reinterpret_cast<const uint2*>(W + rl * kRowGroupBytes + tq * 32 + 8 * j);
+        const uint2 wb = *reinterpret_cast<const uint2*>(W + (rl + 8) * kRowGroupBytes + tq * 32 + 8 * j);
+        a0[0] = wa.x; a0[1] = wa.y;
+        a1[0] = wb.x; a1[1] = wb.y;
+      } else {
+        a0[0] = a0[1] = a1[0] = a1[1] = 0u;
+      }
+    }
+    const uint32_t p0 = P[rl], p1 = P[rl + 8];
+    const float ws0 = f16_bits_to_f32((uint16_t)(p0 & 0xFFFF)), ws1 = f16_bits_to_f32((uint16_t)(p1 & 0xFFFF));
+    const uint64_t ws0_2 = f2(ws0, ws0), ws1_2 = f2(ws1, ws1);
+
+#pragma unroll
+    for (int n = 0; n < NTILES; ++n) {
+      const int tb = n * 8 + gq;  // B-fragment token (column gq of the N tile)
+      const uint8_t* qrow = Q + tb * kActRowBytes;
+      const int unit = (2 * tq + (j >> 1)) ^ (tb & 7);
+      const uint2 bw = *reinterpret_cast<const uint2*>(qrow + (unit << 4) + 8 * (j & 1));
+      const float2 xa = XS[n * 8 + 2 * tq], xb = XS[n * 8 + 2 * tq + 1];
+      // combined_scale = w_scale * x_scale (gemm.rs:606, 493)
+      const uint64_t xs2 = f2(xa.x, xb.x);
+      const uint64_t c0 = mul2(ws0_2, xs2), c1 = mul2(ws1_2, xs2);
+      int32_t d[4];
+      mma_u8s8(a0[0], a1[0], bw.x, d);
+      acc_pair(&acc[n][0][0], d[0], d[1], c0, magic2);
+      acc_pair(&acc[n][0][2], d[2], d[3], c1, magic2);
+      mma_u8s8(a0[1], a1[1], bw.y, d);
+      acc_pair(&acc[n][1][0], d[0], d[1], c0, magic2);
+      acc_pair(&acc[n][1][2], d[2], d[3], c1, magic2);
+      if (j == (n & 3)) {
+        // zero correction: sum_g w_zero * x_sum, sequential in g
+        // (gemm.rs:666-670); N tile n's is kept by warp j = n % 4.
+        const float wz0 = f16_bits_to_f32((uint16_t)(p0 >> 16)), wz1 = f16_bits_to_f32((uint16_t)(p1 >> 16));
+        const uint64_t xsum2 = f2(xa.y, xb.y);
+        const float2 z0 = f2_unpack(mul2(f2(wz0, wz0), xsum2)), z1 = f2_unpack(mul2(f2(wz1, wz1), xsum2));
+        zc[n][0] = __fadd_rn(zc[n][0], z0.x);
+        zc[n][1] = __fadd_rn(zc[n][1], z0.y);
+        zc[n][2] = __fadd_rn(zc[n][2], z1.x);
+        zc[n][3] = __fadd_rn(zc[n][3], z1.y);
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[s]);
+  }
+  if (!__syncthreads_and_consumers(ok, kConsumers * 32)) return;
+
+  // Exchange the lane accumulators through shared memory (the ring is idle:
+  // every stage's copies have landed), then horizontal-sum tree + zero
+  // correction, then bias / residual. X[slab][n][L][lane][i], L = 8 is zc.
+  float* X = reinterpret_cast<float*>(smem);
+  auto xidx = [&](int n, int L) { return (((slab * NTILES + n) * 9 + L) * 32 + lane) * 4; };
+#pragma unroll
+  for (int n = 0; n < NTILES; ++n) {
+#pragma unroll
+    for (int l = 0; l < 2; ++l)
+      *reinterpret_cast<float4*>(X + xidx(n, 2 * j + l)) =
+          make_float4(acc[n][l][0], acc[n][l][1], acc[n][l][2], acc[n][l][3]);
+    if (j == (n & 3))
+      *reinterpret_cast<float4*>(X + xidx(n, 8)) = make_float4(zc[n][0], zc[n][1], zc[n][2], zc[n][3]);
+  }
+  consumers_sync(kConsumers * 32);
+  for (int n = j; n < NTILES; n += 4) {
+    float v[9][4];
+#pragma unroll
+    for (int L = 0; L < 9; ++L) {
+      const float4 q = *reinterpret_cast<const float4*>(X + xidx(n, L));
+      v[L][0] = q.x; v[L][1] = q.y; v[L][2] = q.z; v[L][3] = q.w;
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int row = tile * kTileRows + sub * 16 * RS + rl + ((i & 2) ? 8 : 0);
+      const int tok = t0 + n * 8 + 2 * tq + (i & 1);
+      if (row >= p.rows || tok >= p.M) continue;
+      float a[8];
+#pragma unroll
+      for (int L = 0; L < 8; ++L) a[L] = v[L][i];
+      float val = __fadd_rn(hsum8(a), v[8][i]);
+      const size_t o = (size_t)tok * p.ld_out + row;
+      if (p.mode == kEpiBias) val = __fadd_rn(val, p.bias[row]);
+      else if (p.mode == kEpiResidual) val = __fadd_rn(p.residual[o], val);
+      p.out[o] = val;
+    }
+  }
+}
+
+template <int WBITS, int NTILES>
+cudaError_t launch_gemm_lanes(const GemmParams& gp, int tiles, int chunks, cudaStream_t s) {
+  constexpr int T = 8 * NTILES;
+  constexpr int kStageBytes = 1088 + T * kActTokBytes;
+  constexpr size_t kXchg = (size_t)NTILES * 9 * 128 * sizeof(float);
+  // Ring sized for ~4 CTAs per SM.
+  int stages = (int)((50 * 1024) / kStageBytes);
+  if (stages > 24) stages = 24;
+  if (stages > gp.groups) stages = gp.groups;
+  if (stages < 2) stages = 2;
+  GemmParams p = gp;
+  p.stages = stages;
+  p.tiles = tiles;
+  const size_t ring = (size_t)stages * kStageBytes;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(tiles * 4, chunks);
+  cfg.blockDim = dim3(160);
+  cfg.dynamicSmemBytes = (ring > kXchg ? ring : kXchg) + 2 * stages * sizeof(uint64_t);
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, gemm_lanes_kernel<WBITS, NTILES>, p);
+}
+
 int sm_count() {
   static int n[64] = {};
   int dev = 0;
@@ -612,6 +905,7 @@ cudaError_t init_gemm_attributes() {
   };
   set(gemm_exact_kernel<4, 1>); set(gemm_exact_kernel<4, 2>); set(gemm_exact_kernel<4, 3>); set(gemm_exact_kernel<4, 4>);
   set(gemm_exact_kernel<8, 1>); set(gemm_exact_kernel<8, 2>); set(gemm_exact_kernel<8, 3>); set(gemm_exact_kernel<8, 4>);
+  set(gemm_lanes_kernel<4, 1>); set(gemm_lanes_kernel<4, 2>); set(gemm_lanes_kernel<4, 3>); set(gemm_lanes_kernel<4, 4>);
   return e;
 }
 
@@ -697,6 +991,15 @@ cudaError_t gemm_exact(const PackedLinear& w, const ActBuf& act, int M, float* o
   int per = M < kTokChunk ? M : kTokChunk;
   int ntiles = (per + 7) / 8;
   int chunks = (int)ceil_div(M, kTokChunk);
+  // Few 16-row slabs per SM: spread each slab's lanes over four warps.
+  if (w.wbits == 4 && M <= 16 && (long)ceil_div(w.rows, 16) < 4L * sm_count()) {
+    switch (ntiles) {
+      case 1: return launch_gemm_lanes<4, 1>(gp, w.tiles, chunks, s);
+      case 2: return launch_gemm_lanes<4, 2>(gp, w.tiles, chunks, s);
+      case 3: return launch_gemm_lanes<4, 3>(gp, w.tiles, chunks, s);
+      default: return launch_gemm_lanes<4, 4>(gp, w.tiles, chunks, s);
+    }
+  }
   if (w.wbits == 4) {
     switch (ntiles) {
       case 1: return launch_gemm<4, 1>(gp, w.tiles, chunks, s, pdl);

@@ -354,9 +354,10 @@ __device__ __forceinline__ void pv_body(const float* __restrict__ vbase, const f
 #pragma unroll
   for (int r = 0; r < RB; ++r) acc[r][0] = acc[r][1] = 0.f;
   int tile = 0;
+  int st = 0;           // ring stage of this tile (tile % ns, kept incrementally)
+  uint32_t phase = 0;   // its fill parity
   for (; tile < ntiles; ++tile) {
-    const int st = tile % ns;
-    const bool ok = mbar_wait(&bars[st], (uint32_t)(tile / ns) & 1u, err);
+    const bool ok = mbar_wait(&bars[st], phase, err);
     if (!__syncthreads_and(ok)) break;
     const int t0 = tile * VT, cnt = min(VT, n_max - t0);
     const float* sv = sm + (size_t)st * stage_floats + d0;
@@ -411,6 +412,10 @@ __device__ __forceinline__ void pv_body(const float* __restrict__ vbase, const f
     }
     __syncthreads();
     if (tid < 32 && tile + ns < ntiles) issue(tile + ns, st);
+    if (++st == ns) {
+      st = 0;
+      phase ^= 1u;
+    }
   }
   if (tile < ntiles) {
     // A wait gave up: let this CTA's copies still in flight land (bounded)
