@@ -89,6 +89,23 @@ __device__ __forceinline__ void pdl_wait_prior() {
   asm volatile("griddepcontrol.wait;" ::: "memory");
 }
 
+// SM count of the current device (cached per device).
+inline int device_sm_count() {
+  static int n[64] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+  if (!n[dev] && cudaDeviceGetAttribute(&n[dev], cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) n[dev] = 148;
+  return n[dev];
+}
+
+// Grid size for kernels that loop over their (device-counted) rows or
+// segments: the static budget `want`, capped at about two waves of CTAs so
+// that a budget far above the active count does not launch idle CTAs.
+inline int grid_cap(int want, int per_sm = 2) {
+  const int cap = per_sm * device_sm_count();
+  return want < cap ? (want > 0 ? want : 1) : cap;
+}
+
 // Launch with programmatic stream serialization: the kernel may be scheduled
 // while the previous kernel in the stream still runs. Every kernel of this
 // library therefore calls pdl_wait_prior() before reading anything an earlier

@@ -28,6 +28,8 @@
 // the dot as f32 without an I2F conversion.
 #include <cuda_runtime.h>
 
+#include <algorithm>
+
 #include "common.cuh"
 #include "kernels.h"
 #include "quant.cuh"
@@ -124,20 +126,22 @@ __global__ void quantize_kernel(const float* __restrict__ x, int ldx, int M, con
   pdl_launch_dependents();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = blockIdx.x;
-  const int tok = blockIdx.y * 8 + warp;
-  if (tok >= tok_alloc) return;
   const int mact = m_dev ? *m_dev : M;
+  // The GEMM reads tokens in groups of 8: rows up to the next multiple of 8
+  // past the active count are zeroed.
+  const int rows = min(tok_alloc, (mact + 7) & ~7);
   uint8_t* blk = act + (size_t)g * tok_alloc * kActTokBytes;
-  if (tok >= mact) {
-    // The GEMM reads tokens in groups of 8: zero up to the next multiple.
-    if (tok < ((mact + 7) & ~7)) zero_group_warp(tok, blk, tok_alloc);
-    return;
-  }
-  const float* xr = x + (size_t)tok * ldx + (size_t)g * gs;
   const int len = min(gs, K - g * gs);
-  for (int i = lane; i < len; i += 32) sx[warp][i] = xr[i];
-  __syncwarp();
-  quant_group_warp(sx[warp], len, wbits, tok, blk, tok_alloc, sqw[warp]);
+  for (int tok = blockIdx.y * 8 + warp; tok < rows; tok += gridDim.y * 8) {
+    if (tok >= mact) {
+      zero_group_warp(tok, blk, tok_alloc);
+      continue;
+    }
+    const float* xr = x + (size_t)tok * ldx + (size_t)g * gs;
+    for (int i = lane; i < len; i += 32) sx[warp][i] = xr[i];
+    __syncwarp();
+    quant_group_warp(sx[warp], len, wbits, tok, blk, tok_alloc, sqw[warp]);
+  }
 }
 
 // RMSNorm of rai-infer (rms_norm_with_residual_avx2 / rms_norm_avx2,
@@ -158,14 +162,14 @@ __global__ void __launch_bounds__(256) norm_quant_kernel(const float* __restrict
   __shared__ uint32_t sqw[8][32];
   pdl_wait_prior();
   pdl_launch_dependents();
-  const int b = blockIdx.x;
   const int warp = threadIdx.x >> 5;
   const int mact = m_dev ? *m_dev : M;
   const int groups = (n + gs - 1) / gs;
+  const int rows = act ? min(tok_alloc, (mact + 7) & ~7) : mact;
+  for (int b = blockIdx.x; b < rows; b += gridDim.x) {
   if (b >= mact) {
-    if (act && b < ((mact + 7) & ~7) && b < tok_alloc)
-      for (int g = warp; g < groups; g += 8) zero_group_warp(b, act + (size_t)g * tok_alloc * kActTokBytes, tok_alloc);
-    return;
+    for (int g = warp; g < groups; g += 8) zero_group_warp(b, act + (size_t)g * tok_alloc * kActTokBytes, tok_alloc);
+    continue;
   }
   const float* xr = x + (size_t)b * n;
   for (int i = threadIdx.x; i < n; i += blockDim.x) {
@@ -212,10 +216,12 @@ __global__ void __launch_bounds__(256) norm_quant_kernel(const float* __restrict
     if (normed_out) normed_out[(size_t)b * n + i] = y;
   }
   __syncthreads();
-  if (!act) return;
-  for (int g = warp; g < groups; g += 8)
-    quant_group_warp(sxn + g * gs, min(gs, n - g * gs), wbits, b, act + (size_t)g * tok_alloc * kActTokBytes,
-                     tok_alloc, sqw[warp]);
+  if (act)
+    for (int g = warp; g < groups; g += 8)
+      quant_group_warp(sxn + g * gs, min(gs, n - g * gs), wbits, b, act + (size_t)g * tok_alloc * kActTokBytes,
+                       tok_alloc, sqw[warp]);
+  __syncthreads();  // the shared row is reused by the next row
+  }
 }
 
 // SwiGLU of rai-infer (silu_mul_avx2, layers.rs:850-883) fused with the
@@ -231,18 +237,17 @@ __global__ void swiglu_quant_kernel(const float* __restrict__ gu, int ff, const 
   pdl_launch_dependents();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = blockIdx.x;
-  const int tok = blockIdx.y * 8 + warp;
-  if (tok >= tok_alloc) return;
   const int mact = m_dev ? *m_dev : M;
+  const int rows = min(tok_alloc, (mact + 7) & ~7);
   uint8_t* blk = act + (size_t)g * tok_alloc * kActTokBytes;
-  if (tok >= mact) {
-    // The GEMM reads tokens in groups of 8: zero up to the next multiple.
-    if (tok < ((mact + 7) & ~7)) zero_group_warp(tok, blk, tok_alloc);
-    return;
-  }
   const int len = min(gs, ff - g * gs);
-  const float* row = gu + (size_t)tok * 2 * ff;
   const int vec_end = (ff / 8) * 8;
+  for (int tok = blockIdx.y * 8 + warp; tok < rows; tok += gridDim.y * 8) {
+  if (tok >= mact) {
+    zero_group_warp(tok, blk, tok_alloc);
+    continue;
+  }
+  const float* row = gu + (size_t)tok * 2 * ff;
   for (int i = lane; i < len; i += 32) {
     const int col = g * gs + i;
     const float xv = row[col], u = row[ff + col];
@@ -257,6 +262,7 @@ __global__ void swiglu_quant_kernel(const float* __restrict__ gu, int ff, const 
   }
   __syncwarp();
   quant_group_warp(sx[warp], len, 4, tok, blk, tok_alloc, sqw[warp]);
+  }
 }
 
 // ---------------------------------------------------------------------------
@@ -856,13 +862,7 @@ cudaError_t launch_gemm_lanes(const GemmParams& gp, int tiles, int chunks, cudaS
   return cudaLaunchKernelEx(&cfg, gemm_lanes_kernel<WBITS, NTILES>, p);
 }
 
-int sm_count() {
-  static int n[64] = {};
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
-  if (!n[dev] && cudaDeviceGetAttribute(&n[dev], cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) n[dev] = 148;
-  return n[dev];
-}
+int sm_count() { return device_sm_count(); }
 
 template <int WBITS, int NTILES>
 cudaError_t launch_gemm(const GemmParams& gp, int tiles, int chunks, cudaStream_t s, bool pdl) {
@@ -931,7 +931,8 @@ cudaError_t pack_linear8(const uint8_t* codes, const uint8_t* params, int rows, 
 
 cudaError_t quantize_act(const float* x, int ldx, int M, const int* m_dev, int K, int gs, int wbits,
                          ActBuf act, cudaStream_t s) {
-  dim3 grid((unsigned)act.groups, (unsigned)ceil_div(act.tok_alloc, 8));
+  const int chunks = (int)ceil_div(act.tok_alloc, 8);
+  dim3 grid((unsigned)act.groups, (unsigned)std::max(1, std::min(chunks, grid_cap(act.groups * chunks, 4) / act.groups)));
   return launch_pdl(quantize_kernel, grid, dim3(256), 0, s, x, ldx, M, m_dev, K, gs, wbits, act.data,
                     act.tok_alloc);
 }
@@ -939,7 +940,7 @@ cudaError_t quantize_act(const float* x, int ldx, int M, const int* m_dev, int K
 cudaError_t norm_quant(const float* x, const float* w, int n, float eps, float* residual, int M,
                        const int* m_dev, int gs, int wbits, ActBuf act, cudaStream_t s, float* normed_out) {
   const int rows = act.data ? (int)min((size_t)act.tok_alloc, round_up((size_t)M, 8)) : M;
-  return launch_pdl(norm_quant_kernel, dim3((unsigned)rows), dim3(256), (size_t)n * sizeof(float), s, x, w, n, eps,
+  return launch_pdl(norm_quant_kernel, dim3((unsigned)grid_cap(rows, 1)), dim3(256), (size_t)n * sizeof(float), s, x, w, n, eps,
                     residual, normed_out, m_dev, M, gs, wbits, act.data, act.tok_alloc);
 }
 
@@ -967,7 +968,8 @@ cudaError_t gemm_grouped(const PackedLinear& w, size_t w_stride, int ne, const i
 
 cudaError_t swiglu_quant(const float* gu, int ff, int M, const int* m_dev, int gs, const ExpfTable& et, ActBuf act,
                          cudaStream_t s) {
-  dim3 grid((unsigned)act.groups, (unsigned)ceil_div(act.tok_alloc, 8));
+  const int chunks = (int)ceil_div(act.tok_alloc, 8);
+  dim3 grid((unsigned)act.groups, (unsigned)std::max(1, std::min(chunks, grid_cap(act.groups * chunks, 4) / act.groups)));
   return launch_pdl(swiglu_quant_kernel, grid, dim3(256), 0, s, gu, ff, m_dev, M, gs, et, act.data, act.tok_alloc);
 }
 

@@ -35,22 +35,23 @@ __global__ void embed_kernel(const uint32_t* __restrict__ ids, const int* m_dev,
                              uint32_t* err) {
   pdl_wait_prior();
   pdl_launch_dependents();
-  int b = blockIdx.x;
-  if (b >= active_rows(m_dev, M)) return;
-  uint32_t tok = ids[b];
-  if (tok >= (uint32_t)vocab) {
-    if (threadIdx.x == 0) atomicOr(err, kErrBadInput);
-    return;
-  }
-  int ng = (hidden + gs - 1) / gs;
-  for (int c = threadIdx.x; c < hidden; c += blockDim.x) {
-    int g = c / gs;
-    const uint8_t* p = params + ((size_t)tok * ng + g) * 4;
-    float scale = f16_bits_to_f32((uint16_t)(p[0] | (p[1] << 8)));
-    float zero = f16_bits_to_f32((uint16_t)(p[2] | (p[3] << 8)));
-    float v = __fadd_rn(__fmul_rn((float)codes[(size_t)tok * hidden + c], scale), zero);
-    if (embed_scale != 1.0f) v = __fmul_rn(v, embed_scale);
-    out[(size_t)b * hidden + c] = v;
+  const int mact = active_rows(m_dev, M);
+  const int ng = (hidden + gs - 1) / gs;
+  for (int b = blockIdx.x; b < mact; b += gridDim.x) {
+    const uint32_t tok = ids[b];
+    if (tok >= (uint32_t)vocab) {
+      if (threadIdx.x == 0) atomicOr(err, kErrBadInput);
+      continue;
+    }
+    for (int c = threadIdx.x; c < hidden; c += blockDim.x) {
+      const int g = c / gs;
+      const uint8_t* p = params + ((size_t)tok * ng + g) * 4;
+      const float scale = f16_bits_to_f32((uint16_t)(p[0] | (p[1] << 8)));
+      const float zero = f16_bits_to_f32((uint16_t)(p[2] | (p[3] << 8)));
+      float v = __fadd_rn(__fmul_rn((float)codes[(size_t)tok * hidden + c], scale), zero);
+      if (embed_scale != 1.0f) v = __fmul_rn(v, embed_scale);
+      out[(size_t)b * hidden + c] = v;
+    }
   }
 }
 
@@ -87,8 +88,8 @@ __global__ void qkv_post_kernel(const float* __restrict__ qkv, int ld, float* __
   pdl_launch_dependents();
   extern __shared__ float srow[];  // q | k
   __shared__ float s_inv[2];
-  int b = blockIdx.x;
-  if (b >= active_rows(m_dev, M)) return;
+  const int mact = active_rows(m_dev, M);
+  for (int b = blockIdx.x; b < mact; b += gridDim.x) {
   const RowInfo ri = rows[b];
   const StreamKV sk_ = kv[ri.stream];
   const int pos = ri.pos;
@@ -131,6 +132,8 @@ __global__ void qkv_post_kernel(const float* __restrict__ qkv, int ld, float* __
     sk_.k[o] = sk[i];
     sk_.v[o] = vrow[i];
   }
+  __syncthreads();  // shared rows are reused by the next row
+  }
 }
 
 // ---------------------------------------------------------------------------
@@ -163,12 +166,13 @@ __global__ void __launch_bounds__(ScoreCfg<HD>::CHUNK) attn_scores_kernel(
   extern __shared__ __align__(16) float sm[];
   float* sk = sm;            // [CH][LD]
   float* sq = sm + CH * LD;  // [nrows][hpk][HD]
-  const int kvh = blockIdx.x, si = blockIdx.y, chunk = blockIdx.z;
-  if (si >= active_rows(nseg_dev, nseg_max)) return;
+  const int kvh = blockIdx.x, chunk = blockIdx.z;
+  const int nseg = active_rows(nseg_dev, nseg_max);
+  for (int si = blockIdx.y; si < nseg; si += gridDim.y) {
   const AttnSeg sg = segs[si];
   const int n_max = sg.pos0 + sg.nrows;
   const int t0 = chunk * CH;
-  if (t0 >= n_max) return;
+  if (t0 >= n_max) continue;
   const int cnt = min(CH, n_max - t0);
   const int hpk = nh / nkv;
   const int tid = threadIdx.x;
@@ -188,7 +192,7 @@ __global__ void __launch_bounds__(ScoreCfg<HD>::CHUNK) attn_scores_kernel(
   }
   asm volatile("cp.async.wait_group 0;" ::: "memory");
   __syncthreads();
-  if (tid >= cnt) return;
+  if (tid < cnt) {
   const int t = t0 + tid;
   float kr[HD];
   {
@@ -223,6 +227,9 @@ __global__ void __launch_bounds__(ScoreCfg<HD>::CHUNK) attn_scores_kernel(
       srow[(size_t)h * n_alloc] = sv;
     }
   }
+  }
+  __syncthreads();  // the K and q tiles are reused by the next segment
+  }
 }
 
 // Step 2: softmax. CTA (row, kv head); one warp per query head of the group
@@ -239,10 +246,8 @@ __global__ void __launch_bounds__(256) attn_softmax_kernel(const RowInfo* __rest
   pdl_launch_dependents();
   extern __shared__ __align__(16) float se_all[];  // [hb][n_alloc]
   __shared__ __align__(8) uint64_t bars[8];
-  const int j = blockIdx.x, kvh = blockIdx.y;
-  if (j >= active_rows(m_dev, M)) return;
-  const int n = rows[j].pos + 1;
-  const int n8 = (n / 8) * 8, cnt = n8 / 8;
+  const int kvh = blockIdx.y;
+  const int mact = active_rows(m_dev, M);
   const int hpk = nh / nkv;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (lane == 0) {
@@ -250,8 +255,11 @@ __global__ void __launch_bounds__(256) attn_softmax_kernel(const RowInfo* __rest
     fence_barrier_init();
   }
   __syncwarp();
-  const uint32_t bytes = (uint32_t)((n + 3) / 4) * 16u;
   uint32_t phase = 0;
+  for (int j = blockIdx.x; j < mact; j += gridDim.x) {
+  const int n = rows[j].pos + 1;
+  const int n8 = (n / 8) * 8, cnt = n8 / 8;
+  const uint32_t bytes = (uint32_t)((n + 3) / 4) * 16u;
   for (int hbase = 0; hbase < hpk; hbase += hb) {
     const int hh = warp;
     if (hh < hb && hbase + hh < hpk) {
@@ -298,6 +306,7 @@ __global__ void __launch_bounds__(256) attn_softmax_kernel(const RowInfo* __rest
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     }
   }
+  }
 }
 
 // Step 3: out[row][h][d] = fma(p_t, v_t[d], out) over t in order. CTA
@@ -313,10 +322,14 @@ struct PvCfg {
   static constexpr int VT = HD >= 128 ? 32 : 64;  // positions per tile
 };
 
+// The stage ring persists across the segments a CTA handles: `head` is the
+// next stage to consume (stages fill in the same order) and bit s of `bits`
+// is the parity stage s's next fill completes.
 template <int HD, int RB>
-__device__ __forceinline__ void pv_body(const float* __restrict__ vbase, const float* __restrict__ p, int nh,
+__device__ __forceinline__ bool pv_body(const float* __restrict__ vbase, const float* __restrict__ p, int nh,
                                         int hpk, int kvh, const AttnSeg& sg, int n_alloc, int rb_alloc, int ns,
-                                        float* __restrict__ out, float* sm, uint64_t* bars, uint32_t* err) {
+                                        float* __restrict__ out, float* sm, uint64_t* bars, uint32_t* err,
+                                        int& head, uint32_t& bits) {
   constexpr int VT = PvCfg<HD>::VT;
   constexpr int NDP = HD / 2;
   const int stage_floats = VT * HD + rb_alloc * hpk * VT;
@@ -343,21 +356,22 @@ __device__ __forceinline__ void pv_body(const float* __restrict__ vbase, const f
       bulk_g2s(sp + i * VT, prow0 + ((size_t)r * nh + hh) * n_alloc + t0, (uint32_t)(c4 * 16), &bars[st]);
     }
   };
-  if (tid == 0) {
-    for (int s = 0; s < ns; ++s) mbar_init(&bars[s], 1);
-    fence_barrier_init();
+  if (tid < 32) {
+    int f = head;
+    for (int j = 0; j < ns && j < ntiles; ++j) {
+      issue(j, f);
+      if (++f == ns) f = 0;
+    }
   }
-  __syncthreads();
-  if (tid < 32)
-    for (int s = 0; s < ns && s < ntiles; ++s) issue(s, s);
   float acc[RB][2];
 #pragma unroll
   for (int r = 0; r < RB; ++r) acc[r][0] = acc[r][1] = 0.f;
   int tile = 0;
-  int st = 0;           // ring stage of this tile (tile % ns, kept incrementally)
-  uint32_t phase = 0;   // its fill parity
   for (; tile < ntiles; ++tile) {
-    const bool ok = mbar_wait(&bars[st], phase, err);
+    const int st = head;
+    const bool ok = mbar_wait(&bars[st], (bits >> st) & 1u, err);
+    bits ^= 1u << st;
+    if (++head == ns) head = 0;
     if (!__syncthreads_and(ok)) break;
     const int t0 = tile * VT, cnt = min(VT, n_max - t0);
     const float* sv = sm + (size_t)st * stage_floats + d0;
@@ -412,17 +426,21 @@ __device__ __forceinline__ void pv_body(const float* __restrict__ vbase, const f
     }
     __syncthreads();
     if (tid < 32 && tile + ns < ntiles) issue(tile + ns, st);
-    if (++st == ns) {
-      st = 0;
-      phase ^= 1u;
-    }
   }
   if (tile < ntiles) {
-    // A wait gave up: let this CTA's copies still in flight land (bounded)
-    // before the CTA exits; the output is not written.
-    if (tid == 0)
-      for (int j = tile; j < ntiles && j < tile + ns; ++j) mbar_wait(&bars[j % ns], (uint32_t)(j / ns) & 1u, nullptr);
-    return;
+    // A wait gave up (tile's stage was already retired above): let this
+    // CTA's other copies still in flight land (bounded) before the CTA
+    // exits; the output is not written.
+    if (tid == 0) {
+      int h2 = head;
+      uint32_t b2 = bits;
+      for (int j = tile + 1; j < ntiles && j < tile + ns; ++j) {
+        mbar_wait(&bars[h2], (b2 >> h2) & 1u, nullptr);
+        b2 ^= 1u << h2;
+        if (++h2 == ns) h2 = 0;
+      }
+    }
+    return false;
   }
   if (active) {
 #pragma unroll
@@ -431,6 +449,7 @@ __device__ __forceinline__ void pv_body(const float* __restrict__ vbase, const f
         *reinterpret_cast<float2*>(out + (size_t)(sg.row0 + r) * nh * HD + (size_t)(kvh * hpk + h) * HD + d0) =
             make_float2(acc[r][0], acc[r][1]);
   }
+  return true;
 }
 
 template <int HD>
@@ -443,17 +462,30 @@ __global__ void __launch_bounds__(512) attn_pv_kernel(const StreamKV* __restrict
   pdl_launch_dependents();
   extern __shared__ __align__(16) float sm[];
   __shared__ __align__(8) uint64_t bars[kPvMaxStages];
-  const int kvh = blockIdx.x, si = blockIdx.y;
-  if (si >= active_rows(nseg_dev, nseg_max)) return;
-  const AttnSeg sg = segs[si];
+  const int kvh = blockIdx.x;
+  const int nseg = active_rows(nseg_dev, nseg_max);
+  if ((int)blockIdx.y >= nseg) return;
   const int hpk = nh / nkv;
-  const StreamKV sk_ = kv[sg.stream];
-  const float* vbase = sk_.v + ((size_t)layer * nkv + kvh) * sk_.max_ctx * HD;
-  if (sg.nrows <= 1) pv_body<HD, 1>(vbase, p, nh, hpk, kvh, sg, n_alloc, rb_alloc, ns, out, sm, bars, err);
-  else if (sg.nrows <= 2) pv_body<HD, 2>(vbase, p, nh, hpk, kvh, sg, n_alloc, rb_alloc, ns, out, sm, bars, err);
-  else if (sg.nrows <= 4) pv_body<HD, 4>(vbase, p, nh, hpk, kvh, sg, n_alloc, rb_alloc, ns, out, sm, bars, err);
-  else if (sg.nrows <= 8) pv_body<HD, 8>(vbase, p, nh, hpk, kvh, sg, n_alloc, rb_alloc, ns, out, sm, bars, err);
-  else pv_body<HD, kSegRows>(vbase, p, nh, hpk, kvh, sg, n_alloc, rb_alloc, ns, out, sm, bars, err);
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < ns; ++s) mbar_init(&bars[s], 1);
+    fence_barrier_init();
+  }
+  __syncthreads();
+  int head = 0;
+  uint32_t bits = 0;
+  for (int si = blockIdx.y; si < nseg; si += gridDim.y) {
+    const AttnSeg sg = segs[si];
+    const StreamKV sk_ = kv[sg.stream];
+    const float* vbase = sk_.v + ((size_t)layer * nkv + kvh) * sk_.max_ctx * HD;
+    bool ok;
+    if (sg.nrows <= 1) ok = pv_body<HD, 1>(vbase, p, nh, hpk, kvh, sg, n_alloc, rb_alloc, ns, out, sm, bars, err, head, bits);
+    else if (sg.nrows <= 2) ok = pv_body<HD, 2>(vbase, p, nh, hpk, kvh, sg, n_alloc, rb_alloc, ns, out, sm, bars, err, head, bits);
+    else if (sg.nrows <= 4) ok = pv_body<HD, 4>(vbase, p, nh, hpk, kvh, sg, n_alloc, rb_alloc, ns, out, sm, bars, err, head, bits);
+    else if (sg.nrows <= 8) ok = pv_body<HD, 8>(vbase, p, nh, hpk, kvh, sg, n_alloc, rb_alloc, ns, out, sm, bars, err, head, bits);
+    else ok = pv_body<HD, kSegRows>(vbase, p, nh, hpk, kvh, sg, n_alloc, rb_alloc, ns, out, sm, bars, err, head, bits);
+    if (!ok) return;
+    __syncthreads();  // the stages are refilled for the next segment
+  }
 }
 
 // ---------------------------------------------------------------------------
@@ -471,19 +503,20 @@ __global__ void argmax_kernel(const float* __restrict__ logits, int vocab, const
                               unsigned long long* __restrict__ best) {
   pdl_wait_prior();
   pdl_launch_dependents();
-  int b = blockIdx.y;
-  if (b >= active_rows(m_dev, M)) return;
-  unsigned long long k = 0;
-  const float* row = logits + (size_t)b * vocab;
-  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < vocab; i += gridDim.x * blockDim.x) {
-    unsigned long long c = argmax_key(row[i], (uint32_t)i);
-    k = c > k ? c : k;
+  const int mact = active_rows(m_dev, M);
+  for (int b = blockIdx.y; b < mact; b += gridDim.y) {
+    unsigned long long k = 0;
+    const float* row = logits + (size_t)b * vocab;
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < vocab; i += gridDim.x * blockDim.x) {
+      unsigned long long c = argmax_key(row[i], (uint32_t)i);
+      k = c > k ? c : k;
+    }
+    for (int o = 16; o; o >>= 1) {
+      unsigned long long c = __shfl_xor_sync(0xffffffffu, k, o);
+      k = c > k ? c : k;
+    }
+    if ((threadIdx.x & 31) == 0) atomicMax(best + b, k);
   }
-  for (int o = 16; o; o >>= 1) {
-    unsigned long long c = __shfl_xor_sync(0xffffffffu, k, o);
-    k = c > k ? c : k;
-  }
-  if ((threadIdx.x & 31) == 0) atomicMax(best + b, k);
 }
 
 // ---------------------------------------------------------------------------
@@ -623,7 +656,7 @@ __global__ void accept_kernel(StreamStep* st_all, const unsigned long long* __re
 cudaError_t launch_embed(const uint32_t* ids, const int* m_dev, int M, const uint8_t* codes,
                          const uint8_t* params, int vocab, int hidden, int gs, float embed_scale,
                          float* out, uint32_t* err, cudaStream_t s) {
-  return launch_pdl(embed_kernel, dim3(M), dim3(256), 0, s, ids, m_dev, M, codes, params, vocab, hidden, gs,
+  return launch_pdl(embed_kernel, dim3(grid_cap(M, 1)), dim3(256), 0, s, ids, m_dev, M, codes, params, vocab, hidden, gs,
                     embed_scale, out, err);
 }
 
@@ -632,7 +665,7 @@ cudaError_t launch_qkv_post(float* qkv, int ld, float* q_out, int nh, int nkv, i
                             const float* rope_sin, const StreamKV* kv, int layer, const RowInfo* rows,
                             const int* m_dev, int M, cudaStream_t s) {
   size_t smem = (size_t)(nh + nkv) * hd * sizeof(float);
-  return launch_pdl(qkv_post_kernel, dim3(M), dim3(256), smem, s, qkv, ld, q_out, nh, nkv, hd, qn, kn, qk_mode, eps, rope_cos, rope_sin,
+  return launch_pdl(qkv_post_kernel, dim3(grid_cap(M, 1)), dim3(256), smem, s, qkv, ld, q_out, nh, nkv, hd, qn, kn, qk_mode, eps, rope_cos, rope_sin,
                                        kv, layer, rows, m_dev, M);
 
 }
@@ -678,7 +711,11 @@ cudaError_t launch_attention(const float* q, float* out, const StreamKV* kv, int
   const int t3 = pv_threads(hd, hpk);
   if (hb < 1 || sm1 > kAttnMaxSmem || sm3 > kAttnMaxSmem || t3 > 512) return cudaErrorInvalidValue;
   const size_t sm2 = (size_t)hb * n_alloc * sizeof(float);
-  dim3 g1(nkv, nseg_max, nch), g2(M, nkv), g3(nkv, nseg_max);
+  // Segment and row dimensions loop inside the kernels; the grids cover
+  // about two waves.
+  const int seg_grid = std::max(1, grid_cap(nseg_max * nkv * nch, 8) / (nkv * nch));
+  dim3 g1(nkv, std::min(nseg_max, seg_grid), nch), g2(grid_cap(M, 1), nkv),
+      g3(nkv, std::min(nseg_max, std::max(1, grid_cap(nseg_max * nkv, 3) / nkv)));
 #define RAI_ATTN(HDV)                                                                                        \
   case HDV:                                                                                                  \
     if (cudaError_t e = launch_pdl(attn_scores_kernel<HDV>, g1, dim3(ScoreCfg<HDV>::CHUNK), sm1, s, q, kv,   \
@@ -722,7 +759,7 @@ cudaError_t launch_argmax(const float* logits, int vocab, const int* m_dev, int 
                           cudaStream_t s) {
   int blocks = (vocab + 4095) / 4096;
   if (blocks > 64) blocks = 64;
-  dim3 grid(blocks, M);
+  dim3 grid(blocks, std::max(1, std::min(M, grid_cap(blocks * M, 2) / blocks)));
   return launch_pdl(argmax_kernel, grid, dim3(256), 0, s, logits, vocab, m_dev, M, best);
 }
 
