@@ -154,19 +154,21 @@ __device__ __forceinline__ float schraudolph(float x) {
 // the host expf rounds differently, from a table generated at build time by
 // running that expf over every binary32 input (csrc/gen_expf_table.c).
 struct ExpfTable {
-  const uint32_t* keys = nullptr;  // sorted input bit patterns
-  const uint32_t* vals = nullptr;  // host expf result bits
+  const uint32_t* keys = nullptr;   // sorted input bit patterns
+  const uint32_t* vals = nullptr;   // host expf result bits
+  const uint32_t* start = nullptr;  // [kExpfBuckets + 1] key ranges by top 16 bits
   int n = 0;
 };
+constexpr int kExpfBuckets = 1 << 16;
 
 __device__ __forceinline__ float expf_host(float x, const ExpfTable& t) {
-  float r = (float)exp((double)x);
-  uint32_t k = __float_as_uint(x);
-  int lo = 0, hi = t.n - 1;
+  const float r = (float)exp((double)x);
+  const uint32_t k = __float_as_uint(x);
+  int lo = (int)__ldg(t.start + (k >> 16)), hi = (int)__ldg(t.start + (k >> 16) + 1) - 1;
   while (lo <= hi) {
-    int mid = (lo + hi) >> 1;
-    uint32_t v = t.keys[mid];
-    if (v == k) return __uint_as_float(t.vals[mid]);
+    const int mid = (lo + hi) >> 1;
+    const uint32_t v = __ldg(t.keys + mid);
+    if (v == k) return __uint_as_float(__ldg(t.vals + mid));
     if (v < k) lo = mid + 1; else hi = mid - 1;
   }
   return r;

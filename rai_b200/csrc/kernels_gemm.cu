@@ -156,10 +156,14 @@ __global__ void __launch_bounds__(256) norm_quant_kernel(const float* __restrict
                                                          float* __restrict__ normed_out, const int* m_dev, int M,
                                                          int gs, int wbits, uint8_t* __restrict__ act,
                                                          int tok_alloc) {
-  extern __shared__ __align__(16) float sxn[];  // n floats
+  extern __shared__ __align__(16) float sxn[];  // n floats of the row, then n of w
+  float* sw = sxn + n;
   __shared__ float lanes[16];
   __shared__ float s_inv;
   __shared__ uint32_t sqw[8][32];
+  // The norm weights are model constants: fetched while the previous kernel
+  // (programmatic dependent launch) still runs.
+  for (int i = threadIdx.x; i < n; i += blockDim.x) sw[i] = w[i];
   pdl_wait_prior();
   pdl_launch_dependents();
   const int warp = threadIdx.x >> 5;
@@ -211,7 +215,7 @@ __global__ void __launch_bounds__(256) norm_quant_kernel(const float* __restrict
   __syncthreads();
   const float inv = s_inv;
   for (int i = threadIdx.x; i < n; i += blockDim.x) {
-    const float y = __fmul_rn(__fmul_rn(sxn[i], inv), w[i]);
+    const float y = __fmul_rn(__fmul_rn(sxn[i], inv), sw[i]);
     sxn[i] = y;
     if (normed_out) normed_out[(size_t)b * n + i] = y;
   }
@@ -940,7 +944,7 @@ cudaError_t quantize_act(const float* x, int ldx, int M, const int* m_dev, int K
 cudaError_t norm_quant(const float* x, const float* w, int n, float eps, float* residual, int M,
                        const int* m_dev, int gs, int wbits, ActBuf act, cudaStream_t s, float* normed_out) {
   const int rows = act.data ? (int)min((size_t)act.tok_alloc, round_up((size_t)M, 8)) : M;
-  return launch_pdl(norm_quant_kernel, dim3((unsigned)grid_cap(rows, 1)), dim3(256), (size_t)n * sizeof(float), s, x, w, n, eps,
+  return launch_pdl(norm_quant_kernel, dim3((unsigned)grid_cap(rows, 1)), dim3(256), 2 * (size_t)n * sizeof(float), s, x, w, n, eps,
                     residual, normed_out, m_dev, M, gs, wbits, act.data, act.tok_alloc);
 }
 

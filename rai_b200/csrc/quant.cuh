@@ -50,8 +50,14 @@ __device__ __forceinline__ void quant_group_warp(const float* xs, int len, int w
   // Group sum: lane j accumulates columns 8i + j in order, then the tree.
   float accj = 0.f;
   if (lane < 8) {
+    // len <= 128: at most 16 chunks; all loads issued before the ordered adds.
     const int chunks8 = len / 8;
-    for (int i = 0; i < chunks8; ++i) accj = __fadd_rn(accj, xs[8 * i + lane]);
+    float v[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) v[i] = i < chunks8 ? xs[8 * i + lane] : 0.f;
+#pragma unroll
+    for (int i = 0; i < 16; ++i)
+      if (i < chunks8) accj = __fadd_rn(accj, v[i]);
   }
   float a[8];
 #pragma unroll

@@ -250,13 +250,23 @@ int expf_table(rai::ExpfTable* out) {
   std::vector<uint32_t> kv(2 * (size_t)hdr[1]);
   f.read(reinterpret_cast<char*>(kv.data()), kv.size() * 4);
   if (!f) return fail(RAI_ERR_INVALID, "truncated expf table " + path);
+  // Bucket index over the sorted keys: bucket b = keys whose top 16 bits are
+  // b occupy [start[b], start[b + 1]).
+  const size_t n = hdr[1];
+  std::vector<uint32_t> start(rai::kExpfBuckets + 1, 0);
+  for (size_t i = 0, b = 0; b <= (size_t)rai::kExpfBuckets; ++b) {
+    while (i < n && (kv[i] >> 16) < b) ++i;
+    start[b] = (uint32_t)i;
+  }
   uint32_t* d = nullptr;
-  RAI_CUDA(cudaMalloc(&d, kv.size() * 4));
+  RAI_CUDA(cudaMalloc(&d, (kv.size() + start.size()) * 4));
   RAI_CUDA(cudaMemcpy(d, kv.data(), kv.size() * 4, cudaMemcpyHostToDevice));
+  RAI_CUDA(cudaMemcpy(d + kv.size(), start.data(), start.size() * 4, cudaMemcpyHostToDevice));
   rai::ExpfTable t;
   t.keys = d;
-  t.vals = d + hdr[1];
-  t.n = (int)hdr[1];
+  t.vals = d + n;
+  t.start = d + kv.size();
+  t.n = (int)n;
   g_expf.emplace_back(dev, t);
   *out = t;
   return RAI_OK;
