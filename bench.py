@@ -256,6 +256,7 @@ def cpu_baseline_run(steps: int, warmup: int):
     Returns (tok/s, produced, seconds, sample)."""
     from oracle import oracle as O
     O.build()
+    O.set_num_threads(len(os.sched_getaffinity(0)))  # all host threads this process may use
     path = model_path(0, 1)
     m = O.Model.load(path)
     vocab = m.config["vocab"]

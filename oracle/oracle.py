@@ -94,6 +94,12 @@ def num_threads() -> int:
     return lib().orc_num_threads()
 
 
+def set_num_threads(n: int) -> None:
+    """OpenMP threads of the restated kernels (a launcher such as torchrun may
+    have set OMP_NUM_THREADS=1)."""
+    lib().orc_set_num_threads(int(n))
+
+
 # ---- kernels ---------------------------------------------------------------
 
 def quantize_input(x: np.ndarray, group_size: int):

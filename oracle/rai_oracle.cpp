@@ -669,6 +669,7 @@ size_t orc_argmax(const float* v, size_t n) {
 }
 
 int orc_num_threads(void) { return omp_get_max_threads(); }
+void orc_set_num_threads(int n) { if (n > 0) omp_set_num_threads(n); }
 
 size_t orc_last_error(char* buf, size_t len) {
   if (buf && len) {

@@ -71,6 +71,7 @@ int orc_kv_read(const orc_decoder* d, size_t layer, size_t kv_head, size_t pos, 
                 float* v);
 size_t orc_last_error(char* buf, size_t len);
 int orc_num_threads(void);
+void orc_set_num_threads(int n);
 
 #ifdef __cplusplus
 }
