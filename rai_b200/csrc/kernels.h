@@ -16,6 +16,12 @@ constexpr int kParamStageBytes = kTileRows * 4;                    // 256
 constexpr int kBlockBytes = kWeightStageBytes + kParamStageBytes;  // 4352
 constexpr int kActRowBytes = 128;      // quantized activation bytes per (token, group)
 constexpr int kActTokBytes = kActRowBytes + 8;  // + (scale, sum) f32 pair
+// Quantized activations are stored in blocks of 8 tokens x 1 group:
+// [token / 8][group] blocks of 8 x 128 code bytes then 8 (scale, sum)
+// pairs, so the activations of consecutive groups of one 8-token block are
+// contiguous (one bulk copy per block for several groups).
+constexpr int kActBlockTok = 8;
+constexpr int kActBlockBytes = kActBlockTok * kActTokBytes;  // 1088
 constexpr int kTokChunk = 32;          // tokens per CTA pass
 
 inline size_t ceil_div(size_t a, size_t b) { return (a + b - 1) / b; }

@@ -130,17 +130,17 @@ __global__ void quantize_kernel(const float* __restrict__ x, int ldx, int M, con
   // The GEMM reads tokens in groups of 8: rows up to the next multiple of 8
   // past the active count are zeroed.
   const int rows = min(tok_alloc, (mact + 7) & ~7);
-  uint8_t* blk = act + (size_t)g * tok_alloc * kActTokBytes;
+  const int groups = gridDim.x;
   const int len = min(gs, K - g * gs);
   for (int tok = blockIdx.y * 8 + warp; tok < rows; tok += gridDim.y * 8) {
     if (tok >= mact) {
-      zero_group_warp(tok, blk, tok_alloc);
+      zero_group_warp(tok, act, groups, g);
       continue;
     }
     const float* xr = x + (size_t)tok * ldx + (size_t)g * gs;
     for (int i = lane; i < len; i += 32) sx[warp][i] = xr[i];
     __syncwarp();
-    quant_group_warp(sx[warp], len, wbits, tok, blk, tok_alloc, sqw[warp]);
+    quant_group_warp(sx[warp], len, wbits, tok, act, groups, g, sqw[warp]);
   }
 }
 
@@ -172,7 +172,7 @@ __global__ void __launch_bounds__(256) norm_quant_kernel(const float* __restrict
   const int rows = act ? min(tok_alloc, (mact + 7) & ~7) : mact;
   for (int b = blockIdx.x; b < rows; b += gridDim.x) {
   if (b >= mact) {
-    for (int g = warp; g < groups; g += 8) zero_group_warp(b, act + (size_t)g * tok_alloc * kActTokBytes, tok_alloc);
+    for (int g = warp; g < groups; g += 8) zero_group_warp(b, act, groups, g);
     continue;
   }
   const float* xr = x + (size_t)b * n;
@@ -222,8 +222,7 @@ __global__ void __launch_bounds__(256) norm_quant_kernel(const float* __restrict
   __syncthreads();
   if (act)
     for (int g = warp; g < groups; g += 8)
-      quant_group_warp(sxn + g * gs, min(gs, n - g * gs), wbits, b, act + (size_t)g * tok_alloc * kActTokBytes,
-                       tok_alloc, sqw[warp]);
+      quant_group_warp(sxn + g * gs, min(gs, n - g * gs), wbits, b, act, groups, g, sqw[warp]);
   __syncthreads();  // the shared row is reused by the next row
   }
 }
@@ -243,12 +242,12 @@ __global__ void swiglu_quant_kernel(const float* __restrict__ gu, int ff, const 
   const int g = blockIdx.x;
   const int mact = m_dev ? *m_dev : M;
   const int rows = min(tok_alloc, (mact + 7) & ~7);
-  uint8_t* blk = act + (size_t)g * tok_alloc * kActTokBytes;
+  const int groups = gridDim.x;
   const int len = min(gs, ff - g * gs);
   const int vec_end = (ff / 8) * 8;
   for (int tok = blockIdx.y * 8 + warp; tok < rows; tok += gridDim.y * 8) {
   if (tok >= mact) {
-    zero_group_warp(tok, blk, tok_alloc);
+    zero_group_warp(tok, act, groups, g);
     continue;
   }
   const float* row = gu + (size_t)tok * 2 * ff;
@@ -265,7 +264,7 @@ __global__ void swiglu_quant_kernel(const float* __restrict__ gu, int ff, const 
     sx[warp][i] = __fmul_rn(sv, u);
   }
   __syncwarp();
-  quant_group_warp(sx[warp], len, 4, tok, blk, tok_alloc, sqw[warp]);
+  quant_group_warp(sx[warp], len, 4, tok, act, groups, g, sqw[warp]);
   }
 }
 
@@ -359,12 +358,26 @@ __device__ __forceinline__ void acc_pair(float* acc, int32_t d0, int32_t d1, uin
   acc[1] = __fadd_rn(acc[1], pr.y);
 }
 
+// Groups per pipeline stage: a stage carries kGPS consecutive groups of the
+// tile's packed weights (one contiguous bulk copy) and the matching
+// activation blocks (one copy per 8-token block), so the bulk-copy and
+// mbarrier overhead is paid once per kGPS groups.
+constexpr int kGPS = 4;
+
+template <int NTILES>
+struct StageCfg {
+  static constexpr int kBlocks = NTILES;  // 8-token activation blocks per item
+  static constexpr int kActOff = kGPS * kBlockBytes;
+  static constexpr int kBytes = kGPS * kBlockBytes + kBlocks * kGPS * kActBlockBytes;
+};
+
 template <int WBITS, int NTILES>
 __global__ void __launch_bounds__(GemmCfg<NTILES>::kThreads, NTILES >= 3 ? 1 : 2) gemm_exact_kernel(GemmParams p) {
   constexpr int kConsumerWarps = GemmCfg<NTILES>::kConsumerWarps;
   constexpr int NW = GemmCfg<NTILES>::kTilesPerWarp;  // N tiles per consumer warp
-  constexpr int NT = 8 * NTILES;  // token slots per work item
-  constexpr int kStageBytes = kBlockBytes + NT * kActTokBytes;
+  constexpr int NT = 8 * NTILES;                      // token slots per work item
+  constexpr int kStageBytes = StageCfg<NTILES>::kBytes;
+  constexpr int kActOff = StageCfg<NTILES>::kActOff;
   extern __shared__ __align__(128) uint8_t smem[];
   const int S = p.stages;
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + (size_t)S * kStageBytes);
@@ -372,13 +385,14 @@ __global__ void __launch_bounds__(GemmCfg<NTILES>::kThreads, NTILES >= 3 ? 1 : 2
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int G = p.groups, tiles = p.tiles;
+  const int nsg = (G + kGPS - 1) / kGPS;  // stages per work item
   // Persistent CTAs: each walks work items blockIdx.x, + gridDim.x, ...
   // (chunk-major, so a CTA's first item is token chunk 0 whenever
   // blockIdx.x < tiles). Chunk 0 always has work: the producer of such a
   // "lead" CTA requests its first item's weights before waiting on the
   // previous kernel (programmatic dependent launch). Other CTAs wait first
-  // and exit, before touching any barrier, when they have no item.
-  // The grouped form learns its items from the routing (written by earlier
+  // and exit, before touching any barrier, when they have no item. The
+  // grouped form learns its items from the routing (written by earlier
   // kernels), so none of its CTAs is a lead.
   const bool lead = !p.moe_off && (int)blockIdx.x < tiles;
   __shared__ int cum[kMaxExperts + 1];
@@ -413,40 +427,39 @@ __global__ void __launch_bounds__(GemmCfg<NTILES>::kThreads, NTILES >= 3 ? 1 : 2
   if (warp == kConsumerWarps) {
     // ---------------- producer ----------------
     if (lane == 0) {
-      const int pre = min(S, G);
+      const int pre = min(S, nsg);
       if (lead) {
         // Weights do not depend on the previous kernel: the first item's
         // first ring's worth is requested before waiting on it.
-        for (int g = 0; g < pre; ++g) {
-          mbar_expect_tx(&full[g], kBlockBytes);
-          bulk_g2s(smem + (size_t)g * kStageBytes, p.w + ((size_t)blockIdx.x * G + g) * kBlockBytes, kBlockBytes,
-                   &full[g]);
+        for (int q = 0; q < pre; ++q) {
+          const int g0 = q * kGPS, ng = min(kGPS, G - g0);
+          mbar_expect_tx(&full[q], ng * kBlockBytes);
+          bulk_g2s(smem + (size_t)q * kStageBytes, p.w + ((size_t)blockIdx.x * G + g0) * kBlockBytes,
+                   ng * kBlockBytes, &full[q]);
         }
         pdl_wait_prior();
         if (p.m_dev) mact = *p.m_dev;
       }
-      const size_t act_gstride = (size_t)p.tok_alloc * kActTokBytes;
-      uint32_t gc = 0;  // groups issued by this CTA so far
-      int s = 0;        // ring stage of group gc (gc % S, kept incrementally)
-      uint32_t n = 0;   // times stage s has been filled before (gc / S)
+      int s = 0;       // ring stage of the next fill
+      uint32_t n = 0;  // previous fills of stage s
       bool ok = true, first = true;
       for (int item = blockIdx.x; ok; item += gridDim.x, first = false) {
         GemmItem it;
         if (!decode_item<NT>(p, cum, mact, item, &it)) break;
-        const int tile = it.tile, t0 = it.t0;
-        const int npad = (it.nt + 7) & ~7;
-        const uint32_t abytes = npad * kActTokBytes;
-        for (int g = 0; g < G; ++g, ++gc) {
+        const int nb = (it.nt + 7) >> 3;  // 8-token activation blocks
+        const uint8_t* ab = p.act + (size_t)(it.t0 >> 3) * G * kActBlockBytes;
+        for (int q = 0; q < nsg; ++q) {
           if (n > 0 && !mbar_wait(&empty[s], (n - 1) & 1, p.err)) { ok = false; break; }
+          const int g0 = q * kGPS, ng = min(kGPS, G - g0);
           uint8_t* st = smem + (size_t)s * kStageBytes;
-          const bool prefetched = lead && first && g < pre;
-          mbar_arrive_expect_tx(&full[s], prefetched ? abytes : kBlockBytes + abytes);
+          const bool prefetched = lead && first && q < pre;
+          const uint32_t abytes = nb * ng * kActBlockBytes;
+          mbar_arrive_expect_tx(&full[s], prefetched ? abytes : ng * kBlockBytes + abytes);
           if (!prefetched)
-            bulk_g2s(st, it.w + ((size_t)tile * G + g) * kBlockBytes, kBlockBytes, &full[s]);
-          const uint8_t* ab = p.act + (size_t)g * act_gstride;
-          bulk_g2s(st + kBlockBytes, ab + (size_t)t0 * kActRowBytes, npad * kActRowBytes, &full[s]);
-          bulk_g2s(st + kBlockBytes + NT * kActRowBytes, ab + (size_t)p.tok_alloc * kActRowBytes + (size_t)t0 * 8,
-                   npad * 8, &full[s]);
+            bulk_g2s(st, it.w + ((size_t)it.tile * G + g0) * kBlockBytes, ng * kBlockBytes, &full[s]);
+          for (int b = 0; b < nb; ++b)
+            bulk_g2s(st + kActOff + b * kGPS * kActBlockBytes, ab + ((size_t)b * G + g0) * kActBlockBytes,
+                     ng * kActBlockBytes, &full[s]);
           if (++s == S) {
             s = 0;
             ++n;
@@ -454,9 +467,14 @@ __global__ void __launch_bounds__(GemmCfg<NTILES>::kThreads, NTILES >= 3 ? 1 : 2
         }
       }
       if (!ok) {
-        // Gave up: wait (bounded) for the copies still in flight, then exit.
-        const uint32_t lo = gc > (uint32_t)S ? gc - S : 0;
-        for (uint32_t gg = lo; gg < gc; ++gg) mbar_wait(&full[gg % S], (gg / S) & 1, nullptr);
+        // Gave up: wait (bounded) for this CTA's copies still in flight.
+        for (int k = 0; k < S; ++k) {
+          if (++s == S) {
+            s = 0;
+            ++n;
+          }
+          if (n > 0) mbar_wait(&full[s], (n - 1) & 1, nullptr);
+        }
       }
     }
     return;
@@ -472,7 +490,7 @@ __global__ void __launch_bounds__(GemmCfg<NTILES>::kThreads, NTILES >= 3 ? 1 : 2
   const int r0 = (warp & 3) * 16 + gq;  // tile-local rows r0 and r0 + 8
   const int nbase = (warp >> 2) * NW;   // this warp's first N tile
   const uint64_t magic2 = f2(kMagicF, kMagicF);
-  int cs = 0;          // ring stage of the next group
+  int cs = 0;           // ring stage of the next stage to consume
   uint32_t cphase = 0;  // its fill parity
   for (int item = blockIdx.x;; item += gridDim.x) {
     GemmItem it;
@@ -490,7 +508,7 @@ __global__ void __launch_bounds__(GemmCfg<NTILES>::kThreads, NTILES >= 3 ? 1 : 2
         for (int i = 0; i < 4; ++i) facc[n][L][i] = 0.f;
     }
 
-    for (int g = 0; g < G; ++g) {
+    for (int q = 0; q < nsg; ++q) {
       const int s = cs;
       if (!mbar_wait(&full[s], cphase, p.err)) return;
       if (++cs == S) {
@@ -498,64 +516,69 @@ __global__ void __launch_bounds__(GemmCfg<NTILES>::kThreads, NTILES >= 3 ? 1 : 2
         cphase ^= 1u;
       }
       const uint8_t* st = smem + (size_t)s * kStageBytes;
-      const uint8_t* W = st;
-      const uint32_t* P = reinterpret_cast<const uint32_t*>(st + kWeightStageBytes);
-      const uint8_t* Q = st + kBlockBytes;
-      const float2* XS = reinterpret_cast<const float2*>(st + kBlockBytes + NT * kActRowBytes);
+      const int ng = min(kGPS, G - q * kGPS);
+#pragma unroll 1
+      for (int gi = 0; gi < ng; ++gi) {
+        const uint8_t* W = st + gi * kBlockBytes;
+        const uint32_t* P = reinterpret_cast<const uint32_t*>(W + kWeightStageBytes);
+        const uint8_t* A = st + kActOff + gi * kActBlockBytes;  // + block * kGPS * kActBlockBytes
 
-      uint32_t A0[8], A1[8];
-      if (WBITS == 4) {
-        uint4 wa = *reinterpret_cast<const uint4*>(W + r0 * kRowGroupBytes + tq * 16);
-        uint4 wb = *reinterpret_cast<const uint4*>(W + (r0 + 8) * kRowGroupBytes + tq * 16);
-        const uint32_t wa_[4] = {wa.x, wa.y, wa.z, wa.w}, wb_[4] = {wb.x, wb.y, wb.z, wb.w};
+        uint32_t A0[8], A1[8];
+        if (WBITS == 4) {
+          uint4 wa = *reinterpret_cast<const uint4*>(W + r0 * kRowGroupBytes + tq * 16);
+          uint4 wb = *reinterpret_cast<const uint4*>(W + (r0 + 8) * kRowGroupBytes + tq * 16);
+          const uint32_t wa_[4] = {wa.x, wa.y, wa.z, wa.w}, wb_[4] = {wb.x, wb.y, wb.z, wb.w};
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          A0[2 * j] = wa_[j] & 0x0F0F0F0Fu;
-          A0[2 * j + 1] = (wa_[j] >> 4) & 0x0F0F0F0Fu;
-          A1[2 * j] = wb_[j] & 0x0F0F0F0Fu;
-          A1[2 * j + 1] = (wb_[j] >> 4) & 0x0F0F0F0Fu;
-        }
-      } else {
-        if (tq < 2) {
-          const uint4* pa = reinterpret_cast<const uint4*>(W + r0 * kRowGroupBytes + tq * 32);
-          const uint4* pb = reinterpret_cast<const uint4*>(W + (r0 + 8) * kRowGroupBytes + tq * 32);
-          uint4 a_lo = pa[0], a_hi = pa[1], b_lo = pb[0], b_hi = pb[1];
-          A0[0] = a_lo.x; A0[1] = a_lo.y; A0[2] = a_lo.z; A0[3] = a_lo.w;
-          A0[4] = a_hi.x; A0[5] = a_hi.y; A0[6] = a_hi.z; A0[7] = a_hi.w;
-          A1[0] = b_lo.x; A1[1] = b_lo.y; A1[2] = b_lo.z; A1[3] = b_lo.w;
-          A1[4] = b_hi.x; A1[5] = b_hi.y; A1[6] = b_hi.z; A1[7] = b_hi.w;
+          for (int j = 0; j < 4; ++j) {
+            A0[2 * j] = wa_[j] & 0x0F0F0F0Fu;
+            A0[2 * j + 1] = (wa_[j] >> 4) & 0x0F0F0F0Fu;
+            A1[2 * j] = wb_[j] & 0x0F0F0F0Fu;
+            A1[2 * j + 1] = (wb_[j] >> 4) & 0x0F0F0F0Fu;
+          }
         } else {
+          if (tq < 2) {
+            const uint4* pa = reinterpret_cast<const uint4*>(W + r0 * kRowGroupBytes + tq * 32);
+            const uint4* pb = reinterpret_cast<const uint4*>(W + (r0 + 8) * kRowGroupBytes + tq * 32);
+            uint4 a_lo = pa[0], a_hi = pa[1], b_lo = pb[0], b_hi = pb[1];
+            A0[0] = a_lo.x; A0[1] = a_lo.y; A0[2] = a_lo.z; A0[3] = a_lo.w;
+            A0[4] = a_hi.x; A0[5] = a_hi.y; A0[6] = a_hi.z; A0[7] = a_hi.w;
+            A1[0] = b_lo.x; A1[1] = b_lo.y; A1[2] = b_lo.z; A1[3] = b_lo.w;
+            A1[4] = b_hi.x; A1[5] = b_hi.y; A1[6] = b_hi.z; A1[7] = b_hi.w;
+          } else {
 #pragma unroll
-          for (int L = 0; L < 8; ++L) A0[L] = A1[L] = 0u;
+            for (int L = 0; L < 8; ++L) A0[L] = A1[L] = 0u;
+          }
         }
-      }
-      const uint32_t p0 = P[r0], p1 = P[r0 + 8];
-      const float ws0 = f16_bits_to_f32((uint16_t)(p0 & 0xFFFF)), wz0 = f16_bits_to_f32((uint16_t)(p0 >> 16));
-      const float ws1 = f16_bits_to_f32((uint16_t)(p1 & 0xFFFF)), wz1 = f16_bits_to_f32((uint16_t)(p1 >> 16));
+        const uint32_t p0 = P[r0], p1 = P[r0 + 8];
+        const float ws0 = f16_bits_to_f32((uint16_t)(p0 & 0xFFFF)), wz0 = f16_bits_to_f32((uint16_t)(p0 >> 16));
+        const float ws1 = f16_bits_to_f32((uint16_t)(p1 & 0xFFFF)), wz1 = f16_bits_to_f32((uint16_t)(p1 >> 16));
 
 #pragma unroll
-      for (int n = 0; n < NW; ++n) {
-        const int tb = (nbase + n) * 8 + gq;  // B-fragment token (column gq of the N tile)
-        const uint8_t* qrow = Q + tb * kActRowBytes;
-        const uint4 u0 = *reinterpret_cast<const uint4*>(qrow + (((2 * tq) ^ (tb & 7)) << 4));
-        const uint4 u1 = *reinterpret_cast<const uint4*>(qrow + (((2 * tq + 1) ^ (tb & 7)) << 4));
-        const uint32_t B[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
-        const float2 xa = XS[(nbase + n) * 8 + 2 * tq], xb = XS[(nbase + n) * 8 + 2 * tq + 1];
-        // combined_scale = w_scale * x_scale (gemm.rs:606, 493)
-        const uint64_t xs2 = f2(xa.x, xb.x);
-        const uint64_t c0 = mul2(f2(ws0, ws0), xs2), c1 = mul2(f2(ws1, ws1), xs2);
+        for (int n = 0; n < NW; ++n) {
+          // N tile (nbase + n) = activation block (nbase + n); token gq of it.
+          const uint8_t* blk = A + (nbase + n) * kGPS * kActBlockBytes;
+          const uint8_t* qrow = blk + gq * kActRowBytes;
+          const uint4 u0 = *reinterpret_cast<const uint4*>(qrow + (((2 * tq) ^ gq) << 4));
+          const uint4 u1 = *reinterpret_cast<const uint4*>(qrow + (((2 * tq + 1) ^ gq) << 4));
+          const uint32_t B[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
+          const float2* XS = reinterpret_cast<const float2*>(blk + kActBlockTok * kActRowBytes);
+          const float2 xa = XS[2 * tq], xb = XS[2 * tq + 1];
+          // combined_scale = w_scale * x_scale (gemm.rs:606, 493)
+          const uint64_t xs2 = f2(xa.x, xb.x);
+          const uint64_t c0 = mul2(f2(ws0, ws0), xs2), c1 = mul2(f2(ws1, ws1), xs2);
 #pragma unroll
-        for (int L = 0; L < 8; ++L) {
-          int32_t d[4];
-          mma_u8s8(A0[L], A1[L], B[L], d);
-          acc_pair(&facc[n][L][0], d[0], d[1], c0, magic2);
-          acc_pair(&facc[n][L][2], d[2], d[3], c1, magic2);
+          for (int L = 0; L < 8; ++L) {
+            int32_t d[4];
+            mma_u8s8(A0[L], A1[L], B[L], d);
+            acc_pair(&facc[n][L][0], d[0], d[1], c0, magic2);
+            acc_pair(&facc[n][L][2], d[2], d[3], c1, magic2);
+          }
+          // zero correction: sum_g w_zero * x_sum, sequential in g (gemm.rs:666-670)
+          zc[n][0] = __fadd_rn(zc[n][0], __fmul_rn(wz0, xa.y));
+          zc[n][1] = __fadd_rn(zc[n][1], __fmul_rn(wz0, xb.y));
+          zc[n][2] = __fadd_rn(zc[n][2], __fmul_rn(wz1, xa.y));
+          zc[n][3] = __fadd_rn(zc[n][3], __fmul_rn(wz1, xb.y));
         }
-        // zero correction: sum_g w_zero * x_sum, sequential in g (gemm.rs:666-670)
-        zc[n][0] = __fadd_rn(zc[n][0], __fmul_rn(wz0, xa.y));
-        zc[n][1] = __fadd_rn(zc[n][1], __fmul_rn(wz0, xb.y));
-        zc[n][2] = __fadd_rn(zc[n][2], __fmul_rn(wz1, xa.y));
-        zc[n][3] = __fadd_rn(zc[n][3], __fmul_rn(wz1, xb.y));
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[s]);
@@ -582,299 +605,16 @@ __global__ void __launch_bounds__(GemmCfg<NTILES>::kThreads, NTILES >= 3 ? 1 : 2
   }
 }
 
-// Consumer-only barrier with a vote: true iff every consumer's flag is true.
-__device__ __forceinline__ bool __syncthreads_and_consumers(bool flag, int nthreads) {
-  __shared__ int any_bad;
-  if (threadIdx.x == 0) any_bad = 0;
-  asm volatile("bar.sync 1, %0;" ::"r"(nthreads) : "memory");
-  if (!flag) atomicOr(&any_bad, 1);
-  asm volatile("bar.sync 1, %0;" ::"r"(nthreads) : "memory");
-  const bool ok = any_bad == 0;
-  return ok;
-}
-
-// Named barrier over the consumer warps only (the producer warp has left).
-__device__ __forceinline__ void consumers_sync(int nthreads) {
-  asm volatile("bar.sync 1, %0;" ::"r"(nthreads) : "memory");
-}
-
-// Lane-split form for linears with few rows (the per-warp work of the main
-// kernel then leaves most SMs idle): CTA = 16 weight rows x (8 * NTILES)
-// tokens. Consumer warp j owns the reference lanes 2j, 2j + 1: the eight lane
-// accumulators of a (token, row) are independent until the final horizontal
-// sum, so splitting them over four warps is exact and gives four times the
-// warps. Warp 4 is the producer: per group it bulk-copies the CTA's rows of
-// the packed weight block (codes + params) and the token tile's activation
-// codes and (scale, sum) pairs into a ring of stages. The lane accumulators
-// meet in shared memory for the horizontal sum.
-template <int WBITS, int NTILES>
-__global__ void __launch_bounds__(160, 4) gemm_lanes_kernel(GemmParams p) {
-  constexpr int RS = 1;
-  constexpr int T = 8 * NTILES;  // token slots per CTA
-  constexpr int kConsumers = 4 * RS;
-  constexpr int kCodeBytes = 1024 * RS, kParBytes = 64 * RS;
-  constexpr int kStageBytes = kCodeBytes + kParBytes + T * kActTokBytes;
-  constexpr int kXchgBytes = RS * NTILES * 9 * 128 * (int)sizeof(float);
-  extern __shared__ __align__(128) uint8_t smem[];
-  const int S = p.stages;
-  // The lane-exchange area reuses the ring; the mbarriers sit past both.
-  const int bar_off = S * kStageBytes > kXchgBytes ? S * kStageBytes : kXchgBytes;
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + bar_off);
-  uint64_t* empty = full + S;
-
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int tile = blockIdx.x / (4 / RS), sub = blockIdx.x % (4 / RS);
-  const int t0 = blockIdx.y * T;
-  const int G = p.groups;
-  // Token chunk 0 always has work: its producer requests the weights before
-  // waiting on the previous kernel (programmatic dependent launch). Other
-  // chunks wait first and exit, before touching any barrier, when they lie
-  // beyond the active row count (produced on the device).
-  const bool lead = blockIdx.y == 0;
-  if (!lead) {
-    pdl_wait_prior();
-    if (p.m_dev) {
-      const int mact = *p.m_dev;
-      if (t0 >= mact) return;
-      p.M = mact;
-    }
-  }
-
-  if (threadIdx.x == 0) {
-    for (int s = 0; s < S; ++s) {
-      mbar_init(&full[s], 1);
-      mbar_init(&empty[s], kConsumers);
-    }
-    fence_barrier_init();
-  }
-  __syncthreads();
-
-  if (warp == kConsumers) {
-    // ---------------- producer ----------------
-    if (lane == 0) {
-      const int pre = min(S, G);
-      auto issue_w = [&](int g, uint8_t* st) {
-        uint64_t* bar = full + (st - smem) / kStageBytes;
-        const uint8_t* blk = p.w + ((size_t)tile * G + g) * kBlockBytes;
-        bulk_g2s(st, blk + sub * kCodeBytes, kCodeBytes, bar);
-        bulk_g2s(st + kCodeBytes, blk + kWeightStageBytes + sub * kParBytes, kParBytes, bar);
-      };
-      if (lead) {
-        // Weights do not depend on the previous kernel: the first ring's
-        // worth is requested before waiting on it.
-        for (int g = 0; g < pre; ++g) {
-          mbar_expect_tx(&full[g], kCodeBytes + kParBytes);
-          issue_w(g, smem + (size_t)g * kStageBytes);
-        }
-        pdl_wait_prior();
-        if (p.m_dev) p.M = *p.m_dev;
-      }
-      const int nt = min(T, p.M - t0);
-      const int npad = (nt + 7) & ~7;
-      const uint32_t abytes = npad * kActTokBytes;
-      const uint32_t bytes = kCodeBytes + kParBytes + abytes;
-      const size_t act_gstride = (size_t)p.tok_alloc * kActTokBytes;
-      auto issue_act = [&](int g, uint8_t* st) {
-        uint64_t* bar = full + (st - smem) / kStageBytes;
-        const uint8_t* ab = p.act + (size_t)g * act_gstride;
-        uint8_t* d = st + kCodeBytes + kParBytes;
-        bulk_g2s(d, ab + (size_t)t0 * kActRowBytes, npad * kActRowBytes, bar);
-        bulk_g2s(d + T * kActRowBytes, ab + (size_t)p.tok_alloc * kActRowBytes + (size_t)t0 * 8, npad * 8, bar);
-      };
-      for (int g = 0; g < pre; ++g) {
-        mbar_arrive_expect_tx(&full[g], lead ? abytes : bytes);
-        if (!lead) issue_w(g, smem + (size_t)g * kStageBytes);
-        issue_act(g, smem + (size_t)g * kStageBytes);
-      }
-      int g = pre;
-      int s = pre % S;                     // stage of group g
-      uint32_t n = (uint32_t)(pre / S);    // its previous fills
-      for (; g < G; ++g) {
-        if (!mbar_wait(&empty[s], (n - 1) & 1, p.err)) break;
-        uint8_t* st = smem + (size_t)s * kStageBytes;
-        mbar_arrive_expect_tx(&full[s], bytes);
-        issue_w(g, st);
-        issue_act(g, st);
-        if (++s == S) {
-          s = 0;
-          ++n;
-        }
-      }
-      if (g < G) {
-        // Gave up: wait (bounded) for the copies still in flight, then exit.
-        for (int gg = (g > S ? g - S : 0); gg < g; ++gg) mbar_wait(&full[gg % S], (gg / S) & 1, nullptr);
-      }
-    }
-    return;
-  }
-
-  // ---------------- consumers ----------------
-  if (lead) {
-    pdl_wait_prior();
-    if (p.m_dev) p.M = *p.m_dev;
-  }
-  pdl_launch_dependents();
-  const int slab = warp >> 2, j = warp & 3;
-  const int gq = lane >> 2, tq = lane & 3;
-  const int rl = slab * 16 + gq;  // CTA-local rows rl and rl + 8
-  const uint64_t magic2 = f2(kMagicF, kMagicF);
-  // acc[n][l][i]: lane 2j + l; i = 0, 1: row rl, tokens 2tq, 2tq + 1;
-  // i = 2, 3: row rl + 8 (the mma C-fragment order).
-  float acc[NTILES][2][4];
-  float zc[NTILES][4];
-#pragma unroll
-  for (int n = 0; n < NTILES; ++n) {
-#pragma unroll
-    for (int i = 0; i < 4; ++i) zc[n][i] = acc[n][0][i] = acc[n][1][i] = 0.f;
-  }
-
-  bool ok = true;
-  int cs = 0;
-  uint32_t cphase = 0;
-  for (int g = 0; g < G; ++g) {
-    const int s = cs;
-    if (!mbar_wait(&full[s], cphase, p.err)) { ok = false; break; }
-    if (++cs == S) {
-      cs = 0;
-      cphase ^= 1u;
-    }
-    const uint8_t* st = smem + (size_t)s * kStageBytes;
-    const uint8_t* W = st;
-    const uint32_t* P = reinterpret_cast<const uint32_t*>(st + kCodeBytes);
-    const uint8_t* Q = st + kCodeBytes + kParBytes;
-    const float2* XS = reinterpret_cast<const float2*>(Q + T * kActRowBytes);
-
-    uint32_t a0[2], a1[2];
-    if (WBITS == 4) {
-      const uint32_t wa = *reinterpret_cast<const uint32_t*>(W + rl * kRowGroupBytes + tq * 16 + 4 * j);
-      const uint32_t wb = *reinterpret_cast<const uint32_t*>(W + (rl + 8) * kRowGroupBytes + tq * 16 + 4 * j);
-      a0[0] = wa & 0x0F0F0F0Fu;
-      a0[1] = (wa >> 4) & 0x0F0F0F0Fu;
-      a1[0] = wb & 0x0F0F0F0Fu;
-      a1[1] = (wb >> 4) & 0x0F0F0F0Fu;
-    } else {
-      if (tq < 2) {
-        const uint2 wa = *reinterpret_cast<const uint2*>(W + rl * kRowGroupBytes + tq * 32 + 8 * j);
-        const uint2 wb = *reinterpret_cast<const uint2*>(W + (rl + 8) * kRowGroupBytes + tq * 32 + 8 * j);
-        a0[0] = wa.x; a0[1] = wa.y;
-        a1[0] = wb.x; a1[1] = wb.y;
-      } else {
-        a0[0] = a0[1] = a1[0] = a1[1] = 0u;
-      }
-    }
-    const uint32_t p0 = P[rl], p1 = P[rl + 8];
-    const float ws0 = f16_bits_to_f32((uint16_t)(p0 & 0xFFFF)), ws1 = f16_bits_to_f32((uint16_t)(p1 & 0xFFFF));
-    const uint64_t ws0_2 = f2(ws0, ws0), ws1_2 = f2(ws1, ws1);
-
-#pragma unroll
-    for (int n = 0; n < NTILES; ++n) {
-      const int tb = n * 8 + gq;  // B-fragment token (column gq of the N tile)
-      const uint8_t* qrow = Q + tb * kActRowBytes;
-      const int unit = (2 * tq + (j >> 1)) ^ (tb & 7);
-      const uint2 bw = *reinterpret_cast<const uint2*>(qrow + (unit << 4) + 8 * (j & 1));
-      const float2 xa = XS[n * 8 + 2 * tq], xb = XS[n * 8 + 2 * tq + 1];
-      // combined_scale = w_scale * x_scale (gemm.rs:606, 493)
-      const uint64_t xs2 = f2(xa.x, xb.x);
-      const uint64_t c0 = mul2(ws0_2, xs2), c1 = mul2(ws1_2, xs2);
-      int32_t d[4];
-      mma_u8s8(a0[0], a1[0], bw.x, d);
-      acc_pair(&acc[n][0][0], d[0], d[1], c0, magic2);
-      acc_pair(&acc[n][0][2], d[2], d[3], c1, magic2);
-      mma_u8s8(a0[1], a1[1], bw.y, d);
-      acc_pair(&acc[n][1][0], d[0], d[1], c0, magic2);
-      acc_pair(&acc[n][1][2], d[2], d[3], c1, magic2);
-      if (j == (n & 3)) {
-        // zero correction: sum_g w_zero * x_sum, sequential in g
-        // (gemm.rs:666-670); N tile n's is kept by warp j = n % 4.
-        const float wz0 = f16_bits_to_f32((uint16_t)(p0 >> 16)), wz1 = f16_bits_to_f32((uint16_t)(p1 >> 16));
-        const uint64_t xsum2 = f2(xa.y, xb.y);
-        const float2 z0 = f2_unpack(mul2(f2(wz0, wz0), xsum2)), z1 = f2_unpack(mul2(f2(wz1, wz1), xsum2));
-        zc[n][0] = __fadd_rn(zc[n][0], z0.x);
-        zc[n][1] = __fadd_rn(zc[n][1], z0.y);
-        zc[n][2] = __fadd_rn(zc[n][2], z1.x);
-        zc[n][3] = __fadd_rn(zc[n][3], z1.y);
-      }
-    }
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&empty[s]);
-  }
-  if (!__syncthreads_and_consumers(ok, kConsumers * 32)) return;
-
-  // Exchange the lane accumulators through shared memory (the ring is idle:
-  // every stage's copies have landed), then horizontal-sum tree + zero
-  // correction, then bias / residual. X[slab][n][L][lane][i], L = 8 is zc.
-  float* X = reinterpret_cast<float*>(smem);
-  auto xidx = [&](int n, int L) { return (((slab * NTILES + n) * 9 + L) * 32 + lane) * 4; };
-#pragma unroll
-  for (int n = 0; n < NTILES; ++n) {
-#pragma unroll
-    for (int l = 0; l < 2; ++l)
-      *reinterpret_cast<float4*>(X + xidx(n, 2 * j + l)) =
-          make_float4(acc[n][l][0], acc[n][l][1], acc[n][l][2], acc[n][l][3]);
-    if (j == (n & 3))
-      *reinterpret_cast<float4*>(X + xidx(n, 8)) = make_float4(zc[n][0], zc[n][1], zc[n][2], zc[n][3]);
-  }
-  consumers_sync(kConsumers * 32);
-  for (int n = j; n < NTILES; n += 4) {
-    float v[9][4];
-#pragma unroll
-    for (int L = 0; L < 9; ++L) {
-      const float4 q = *reinterpret_cast<const float4*>(X + xidx(n, L));
-      v[L][0] = q.x; v[L][1] = q.y; v[L][2] = q.z; v[L][3] = q.w;
-    }
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const int row = tile * kTileRows + sub * 16 * RS + rl + ((i & 2) ? 8 : 0);
-      const int tok = t0 + n * 8 + 2 * tq + (i & 1);
-      if (row >= p.rows || tok >= p.M) continue;
-      float a[8];
-#pragma unroll
-      for (int L = 0; L < 8; ++L) a[L] = v[L][i];
-      float val = __fadd_rn(hsum8(a), v[8][i]);
-      const size_t o = (size_t)tok * p.ld_out + row;
-      if (p.mode == kEpiBias) val = __fadd_rn(val, p.bias[row]);
-      else if (p.mode == kEpiResidual) val = __fadd_rn(p.residual[o], val);
-      p.out[o] = val;
-    }
-  }
-}
-
-template <int WBITS, int NTILES>
-cudaError_t launch_gemm_lanes(const GemmParams& gp, int tiles, int chunks, cudaStream_t s) {
-  constexpr int T = 8 * NTILES;
-  constexpr int kStageBytes = 1088 + T * kActTokBytes;
-  constexpr size_t kXchg = (size_t)NTILES * 9 * 128 * sizeof(float);
-  // Ring sized for ~4 CTAs per SM.
-  int stages = (int)((50 * 1024) / kStageBytes);
-  if (stages > 24) stages = 24;
-  if (stages > gp.groups) stages = gp.groups;
-  if (stages < 2) stages = 2;
-  GemmParams p = gp;
-  p.stages = stages;
-  p.tiles = tiles;
-  const size_t ring = (size_t)stages * kStageBytes;
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(tiles * 4, chunks);
-  cfg.blockDim = dim3(160);
-  cfg.dynamicSmemBytes = (ring > kXchg ? ring : kXchg) + 2 * stages * sizeof(uint64_t);
-  cfg.stream = s;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, gemm_lanes_kernel<WBITS, NTILES>, p);
-}
-
 int sm_count() { return device_sm_count(); }
 
 template <int WBITS, int NTILES>
 cudaError_t launch_gemm(const GemmParams& gp, int tiles, int chunks, cudaStream_t s, bool pdl) {
-  constexpr int NT = 8 * NTILES;
-  constexpr int kStageBytes = kBlockBytes + NT * kActTokBytes;
-  int stages = (int)(((NTILES >= 3 ? 200 : 100) * 1024) / kStageBytes);
-  if (stages > 24) stages = 24;
-  if (stages > gp.groups) stages = gp.groups < 2 ? 2 : gp.groups;
+  constexpr int kStageBytes = StageCfg<NTILES>::kBytes;
+  const int nsg = (gp.groups + kGPS - 1) / kGPS;
+  int stages = (int)(((NTILES >= 3 ? 200 : 104) * 1024) / kStageBytes);
+  if (stages > 8) stages = 8;
+  if (stages > nsg) stages = nsg;
+  if (stages < 2) stages = 2;
   GemmParams p = gp;
   p.stages = stages;
   p.tiles = tiles;
@@ -909,7 +649,6 @@ cudaError_t init_gemm_attributes() {
   };
   set(gemm_exact_kernel<4, 1>); set(gemm_exact_kernel<4, 2>); set(gemm_exact_kernel<4, 3>); set(gemm_exact_kernel<4, 4>);
   set(gemm_exact_kernel<8, 1>); set(gemm_exact_kernel<8, 2>); set(gemm_exact_kernel<8, 3>); set(gemm_exact_kernel<8, 4>);
-  set(gemm_lanes_kernel<4, 1>); set(gemm_lanes_kernel<4, 2>); set(gemm_lanes_kernel<4, 3>); set(gemm_lanes_kernel<4, 4>);
   return e;
 }
 
@@ -997,15 +736,6 @@ cudaError_t gemm_exact(const PackedLinear& w, const ActBuf& act, int M, float* o
   int per = M < kTokChunk ? M : kTokChunk;
   int ntiles = (per + 7) / 8;
   int chunks = (int)ceil_div(M, kTokChunk);
-  // Few 16-row slabs per SM: spread each slab's lanes over four warps.
-  if (w.wbits == 4 && M <= 16 && (long)ceil_div(w.rows, 16) < 4L * sm_count()) {
-    switch (ntiles) {
-      case 1: return launch_gemm_lanes<4, 1>(gp, w.tiles, chunks, s);
-      case 2: return launch_gemm_lanes<4, 2>(gp, w.tiles, chunks, s);
-      case 3: return launch_gemm_lanes<4, 3>(gp, w.tiles, chunks, s);
-      default: return launch_gemm_lanes<4, 4>(gp, w.tiles, chunks, s);
-    }
-  }
   if (w.wbits == 4) {
     switch (ntiles) {
       case 1: return launch_gemm<4, 1>(gp, w.tiles, chunks, s, pdl);

@@ -172,17 +172,17 @@ __global__ void moe_gather_quant_kernel(const float* __restrict__ x, int h, int 
   const int g = blockIdx.x;
   const int r = blockIdx.y * 8 + warp;
   if (r >= *n_rows || r >= tok_alloc) return;
-  uint8_t* blk = act + (size_t)g * tok_alloc * kActTokBytes;
+  const int groups = gridDim.x;
   const int pair = pair_of_row[r];
   if (pair < 0) {
-    zero_group_warp(r, blk, tok_alloc);
+    zero_group_warp(r, act, groups, g);
     return;
   }
   const float* xr = x + (size_t)(pair / k) * h + (size_t)g * gs;
   const int len = min(gs, h - g * gs);
   for (int i = lane; i < len; i += 32) sx[warp][i] = xr[i];
   __syncwarp();
-  quant_group_warp(sx[warp], len, 4, r, blk, tok_alloc, sqw[warp]);
+  quant_group_warp(sx[warp], len, 4, r, act, groups, g, sqw[warp]);
 }
 
 // out = residual + sum over picks (in order) of weight * expert_out.

@@ -16,12 +16,18 @@ namespace rai {
 // Logical byte (slot t, lane L, elem b) of a token row is at t*32 + 4L + b;
 // 16-byte unit u = offset/16 is stored at unit u ^ (token & 7) so the GEMM's
 // B-fragment loads are bank-conflict free. xs: the group's len values in
-// shared memory; sqw: 32 words of per-warp shared scratch.
-__device__ __forceinline__ void quant_group_warp(const float* xs, int len, int wbits, int tok, uint8_t* blk,
-                                                 int tok_alloc, uint32_t* sqw) {
+// shared memory; sqw: 32 words of per-warp shared scratch. act: the
+// activation buffer of `groups` groups (8-token x group blocks).
+__device__ __forceinline__ uint8_t* act_block(uint8_t* act, int groups, int tok, int g) {
+  return act + ((size_t)(tok >> 3) * groups + g) * kActBlockBytes;
+}
+
+__device__ __forceinline__ void quant_group_warp(const float* xs, int len, int wbits, int tok, uint8_t* act,
+                                                 int groups, int g, uint32_t* sqw) {
   const int lane = threadIdx.x & 31;
-  uint32_t* qrow = reinterpret_cast<uint32_t*>(blk + (size_t)tok * kActRowBytes);
-  float2* sc = reinterpret_cast<float2*>(blk + (size_t)tok_alloc * kActRowBytes) + tok;
+  uint8_t* blk = act_block(act, groups, tok, g);
+  uint32_t* qrow = reinterpret_cast<uint32_t*>(blk + (tok & 7) * kActRowBytes);
+  float2* sc = reinterpret_cast<float2*>(blk + kActBlockTok * kActRowBytes) + (tok & 7);
   float amax = 0.f;
   for (int i = lane; i < len; i += 32) amax = fmaxf(amax, fabsf(xs[i]));
   for (int o = 16; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
@@ -74,10 +80,11 @@ __device__ __forceinline__ void quant_group_warp(const float* xs, int len, int w
 
 // Zero codes and (scale, sum) of one (token, group): tokens past the active
 // count up to the next multiple of 8 (the GEMM reads tokens in groups of 8).
-__device__ __forceinline__ void zero_group_warp(int tok, uint8_t* blk, int tok_alloc) {
+__device__ __forceinline__ void zero_group_warp(int tok, uint8_t* act, int groups, int g) {
   const int lane = threadIdx.x & 31;
-  reinterpret_cast<uint32_t*>(blk + (size_t)tok * kActRowBytes)[lane] = 0;
-  if (lane == 0) reinterpret_cast<float2*>(blk + (size_t)tok_alloc * kActRowBytes)[tok] = make_float2(0.f, 0.f);
+  uint8_t* blk = act_block(act, groups, tok, g);
+  reinterpret_cast<uint32_t*>(blk + (tok & 7) * kActRowBytes)[lane] = 0;
+  if (lane == 0) reinterpret_cast<float2*>(blk + kActBlockTok * kActRowBytes)[tok & 7] = make_float2(0.f, 0.f);
 }
 
 }  // namespace rai
