@@ -38,14 +38,26 @@ namespace rai {
 
 namespace {
 
-// Consumer warps per CTA: 4 row slabs of 16 rows; with 32-token tiles each
-// slab is split into two warps of 16 tokens, so every SM scheduler has two
-// consumer warps to interleave.
-template <int NTILES>
+// Kernel variant. Consumer warps per CTA: 4 row slabs of 16 rows, each slab
+// split over LG warps by reference lane pair (lanes j and j+4 form pair j:
+// they share a packed weight word and are the first two terms the
+// horizontal sum adds) and over TS warps by 8-token N tiles. The lane
+// accumulators are independent, so neither split changes any rounding; the
+// LG warps of a slab meet once per work item to finish the horizontal sum.
+// MINB: CTAs per SM the launch is sized for; UNROLL: groups unrolled in the
+// consumer loop.
+template <int NT_, int LG_, int TS_, int MINB_, int UNROLL_>
 struct GemmCfg {
-  static constexpr int kConsumerWarps = NTILES >= 4 ? 8 : 4;
+  static constexpr int NTILES = NT_, LG = LG_, TS = TS_, kMinBlocks = MINB_, kUnroll = UNROLL_;
+  static_assert(LG == 1 || LG == 2 || LG == 4, "lane groups");
+  static_assert(NTILES % TS == 0, "token split");
+  static constexpr int kConsumerWarps = 4 * LG * TS;
   static constexpr int kThreads = (kConsumerWarps + 1) * 32;
-  static constexpr int kTilesPerWarp = NTILES >= 4 ? NTILES / 2 : NTILES;
+  static constexpr int kTilesPerWarp = NTILES / TS;
+  static constexpr int kPairs = 4 / LG;  // lane pairs per consumer warp
+  // Partial horizontal sums handed to the slab's first lane group:
+  // [slab][token split][LG-1][N tile][4][32] floats.
+  static constexpr int kCombBytes = 4 * TS * (LG - 1) * kTilesPerWarp * 4 * 32 * 4;
 };
 constexpr uint32_t kMagic = 0x4B400000u;  // 12582912.0f
 constexpr float kMagicF = 12582912.0f;
@@ -55,9 +67,10 @@ constexpr float kMagicF = 12582912.0f;
 // ---------------------------------------------------------------------------
 // 4-bit block (tile, group): row r's 64 bytes are 4 slots of 16 bytes. Slot t
 // (chunk c = t >> 1, column parity p = t & 1) word j, byte b holds in its low
-// nibble the code of group column 64c + 8(2j) + 2b + p (reference lane 2j)
-// and in its high nibble column 64c + 8(2j+1) + 2b + p (lane 2j+1). Chunk 1
-// is zero when the group is 64 wide.
+// nibble the code of group column 64c + 8j + 2b + p (reference lane j) and
+// in its high nibble column 64c + 8(j+4) + 2b + p (lane j+4): the lanes that
+// the horizontal sum adds first share a word. Chunk 1 is zero when the
+// group is 64 wide.
 __global__ void pack4_kernel(const uint8_t* __restrict__ nib, const uint8_t* __restrict__ params,
                              int rows, int cols, int gs, int groups, uint8_t* __restrict__ out,
                              size_t total) {
@@ -75,9 +88,9 @@ __global__ void pack4_kernel(const uint8_t* __restrict__ nib, const uint8_t* __r
     int c = t >> 1, p = t & 1;
     if (row < rows && 64 * c < gs) {
       size_t rowbase = (size_t)row * (cols / 2) + (size_t)g * gs / 2;
-      int col0 = 64 * c + 8 * (2 * j) + 2 * b;  // even column of the byte
+      int col0 = 64 * c + 8 * j + 2 * b;  // even column of the byte
       uint8_t lo = nib[rowbase + col0 / 2];
-      uint8_t hi = nib[rowbase + (col0 + 8) / 2];
+      uint8_t hi = nib[rowbase + (col0 + 32) / 2];
       uint8_t c0 = p ? (lo >> 4) : (lo & 0xF);
       uint8_t c1 = p ? (hi >> 4) : (hi & 0xF);
       v = (uint8_t)(c0 | (c1 << 4));
@@ -371,17 +384,39 @@ struct StageCfg {
   static constexpr int kBytes = kGPS * kBlockBytes + kBlocks * kGPS * kActBlockBytes;
 };
 
-template <int WBITS, int NTILES>
-__global__ void __launch_bounds__(GemmCfg<NTILES>::kThreads, NTILES >= 3 ? 1 : 2) gemm_exact_kernel(GemmParams p) {
-  constexpr int kConsumerWarps = GemmCfg<NTILES>::kConsumerWarps;
-  constexpr int NW = GemmCfg<NTILES>::kTilesPerWarp;  // N tiles per consumer warp
-  constexpr int NT = 8 * NTILES;                      // token slots per work item
+// Lane-pair fragments of one consumer warp: pair jj covers reference lanes
+// j = j0 + jj ([0]) and j + 4 ([1]).
+template <int NP>
+__device__ __forceinline__ void load_words(const uint8_t* p, uint32_t (&w)[NP]) {
+  if constexpr (NP == 4) {
+    const uint4 v = *reinterpret_cast<const uint4*>(p);
+    w[0] = v.x; w[1] = v.y; w[2] = v.z; w[3] = v.w;
+  } else if constexpr (NP == 2) {
+    const uint2 v = *reinterpret_cast<const uint2*>(p);
+    w[0] = v.x; w[1] = v.y;
+  } else {
+    w[0] = *reinterpret_cast<const uint32_t*>(p);
+  }
+}
+
+template <int WBITS, class Cfg>
+__global__ void __launch_bounds__(Cfg::kThreads, Cfg::kMinBlocks) gemm_exact_kernel(GemmParams p) {
+  constexpr int NTILES = Cfg::NTILES, LG = Cfg::LG;
+  static_assert(WBITS == 4 || LG == 1, "the tied head runs unsplit");
+  constexpr int kConsumerWarps = Cfg::kConsumerWarps;
+  constexpr int NW = Cfg::kTilesPerWarp;  // N tiles per consumer warp
+  constexpr int NP = Cfg::kPairs;         // lane pairs per consumer warp
+  constexpr int NT = 8 * NTILES;          // token slots per work item
   constexpr int kStageBytes = StageCfg<NTILES>::kBytes;
   constexpr int kActOff = StageCfg<NTILES>::kActOff;
   extern __shared__ __align__(128) uint8_t smem[];
   const int S = p.stages;
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + (size_t)S * kStageBytes);
   uint64_t* empty = full + S;
+  constexpr int kSlabTeams = 4 * Cfg::TS;  // (slab, token split) warp teams
+  uint64_t* cfull = empty + S;            // per team: the other lane groups posted their sums
+  uint64_t* cfree = cfull + kSlabTeams;   // per team: the first lane group has read them
+  float* comb = reinterpret_cast<float*>(cfree + kSlabTeams);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int G = p.groups, tiles = p.tiles;
@@ -419,6 +454,10 @@ __global__ void __launch_bounds__(GemmCfg<NTILES>::kThreads, NTILES >= 3 ? 1 : 2
     for (int s = 0; s < S; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], kConsumerWarps);
+    }
+    for (int k = 0; k < kSlabTeams; ++k) {
+      mbar_init(&cfull[k], LG > 1 ? LG - 1 : 1);
+      mbar_init(&cfree[k], 1);
     }
     fence_barrier_init();
   }
@@ -487,25 +526,33 @@ __global__ void __launch_bounds__(GemmCfg<NTILES>::kThreads, NTILES >= 3 ? 1 : 2
   }
   pdl_launch_dependents();
   const int gq = lane >> 2, tq = lane & 3;
-  const int r0 = (warp & 3) * 16 + gq;  // tile-local rows r0 and r0 + 8
-  const int nbase = (warp >> 2) * NW;   // this warp's first N tile
+  const int slab = warp & 3;
+  const int lg = (warp >> 2) % LG;                     // lane group within the slab
+  const int team = slab + 4 * ((warp >> 2) / LG);      // (slab, token split)
+  const int r0 = slab * 16 + gq;                       // tile-local rows r0 and r0 + 8
+  const int nbase = ((warp >> 2) / LG) * NW;           // this warp's first N tile
+  const int j0 = lg * NP;                              // first lane pair
   const uint64_t magic2 = f2(kMagicF, kMagicF);
   int cs = 0;           // ring stage of the next stage to consume
   uint32_t cphase = 0;  // its fill parity
+  uint32_t nitems = 0;  // items finished by this warp
   for (int item = blockIdx.x;; item += gridDim.x) {
     GemmItem it;
     if (!decode_item<NT>(p, cum, mact, item, &it)) break;
     const int tile = it.tile, t0 = it.t0;
-    float facc[NW][8][4];
+    const int nbi = (it.nt + 7) >> 3;  // 8-token blocks holding this item's tokens
+    float facc[NW][NP][2][4];
     float zc[NW][4];
 #pragma unroll
     for (int n = 0; n < NW; ++n) {
 #pragma unroll
       for (int i = 0; i < 4; ++i) zc[n][i] = 0.f;
 #pragma unroll
-      for (int L = 0; L < 8; ++L)
+      for (int jj = 0; jj < NP; ++jj)
 #pragma unroll
-        for (int i = 0; i < 4; ++i) facc[n][L][i] = 0.f;
+        for (int h = 0; h < 2; ++h)
+#pragma unroll
+          for (int i = 0; i < 4; ++i) facc[n][jj][h][i] = 0.f;
     }
 
     for (int q = 0; q < nsg; ++q) {
@@ -517,74 +564,153 @@ __global__ void __launch_bounds__(GemmCfg<NTILES>::kThreads, NTILES >= 3 ? 1 : 2
       }
       const uint8_t* st = smem + (size_t)s * kStageBytes;
       const int ng = min(kGPS, G - q * kGPS);
-#pragma unroll 1
-      for (int gi = 0; gi < ng; ++gi) {
+      // A warp whose N tiles all lie past the item's tokens only frees the stage.
+#pragma unroll(Cfg::kUnroll)
+      for (int gi = 0; gi < (nbase < nbi ? ng : 0); ++gi) {
         const uint8_t* W = st + gi * kBlockBytes;
         const uint32_t* P = reinterpret_cast<const uint32_t*>(W + kWeightStageBytes);
         const uint8_t* A = st + kActOff + gi * kActBlockBytes;  // + block * kGPS * kActBlockBytes
 
-        uint32_t A0[8], A1[8];
-        if (WBITS == 4) {
-          uint4 wa = *reinterpret_cast<const uint4*>(W + r0 * kRowGroupBytes + tq * 16);
-          uint4 wb = *reinterpret_cast<const uint4*>(W + (r0 + 8) * kRowGroupBytes + tq * 16);
-          const uint32_t wa_[4] = {wa.x, wa.y, wa.z, wa.w}, wb_[4] = {wb.x, wb.y, wb.z, wb.w};
+        uint32_t A0[NP][2], A1[NP][2];
+        if constexpr (WBITS == 4) {
+          // Word j of the thread's 16-byte slot: lane j (low nibbles), lane j + 4 (high).
+          uint32_t wa[NP], wb[NP];
+          load_words<NP>(W + r0 * kRowGroupBytes + tq * 16 + j0 * 4, wa);
+          load_words<NP>(W + (r0 + 8) * kRowGroupBytes + tq * 16 + j0 * 4, wb);
 #pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            A0[2 * j] = wa_[j] & 0x0F0F0F0Fu;
-            A0[2 * j + 1] = (wa_[j] >> 4) & 0x0F0F0F0Fu;
-            A1[2 * j] = wb_[j] & 0x0F0F0F0Fu;
-            A1[2 * j + 1] = (wb_[j] >> 4) & 0x0F0F0F0Fu;
+          for (int jj = 0; jj < NP; ++jj) {
+            A0[jj][0] = wa[jj] & 0x0F0F0F0Fu;
+            A0[jj][1] = (wa[jj] >> 4) & 0x0F0F0F0Fu;
+            A1[jj][0] = wb[jj] & 0x0F0F0F0Fu;
+            A1[jj][1] = (wb[jj] >> 4) & 0x0F0F0F0Fu;
           }
         } else {
+          // 8-bit codes: word L of the thread's 32 bytes is lane L.
           if (tq < 2) {
             const uint4* pa = reinterpret_cast<const uint4*>(W + r0 * kRowGroupBytes + tq * 32);
             const uint4* pb = reinterpret_cast<const uint4*>(W + (r0 + 8) * kRowGroupBytes + tq * 32);
-            uint4 a_lo = pa[0], a_hi = pa[1], b_lo = pb[0], b_hi = pb[1];
-            A0[0] = a_lo.x; A0[1] = a_lo.y; A0[2] = a_lo.z; A0[3] = a_lo.w;
-            A0[4] = a_hi.x; A0[5] = a_hi.y; A0[6] = a_hi.z; A0[7] = a_hi.w;
-            A1[0] = b_lo.x; A1[1] = b_lo.y; A1[2] = b_lo.z; A1[3] = b_lo.w;
-            A1[4] = b_hi.x; A1[5] = b_hi.y; A1[6] = b_hi.z; A1[7] = b_hi.w;
+            const uint4 a_lo = pa[0], a_hi = pa[1], b_lo = pb[0], b_hi = pb[1];
+            const uint32_t a_[8] = {a_lo.x, a_lo.y, a_lo.z, a_lo.w, a_hi.x, a_hi.y, a_hi.z, a_hi.w};
+            const uint32_t b_[8] = {b_lo.x, b_lo.y, b_lo.z, b_lo.w, b_hi.x, b_hi.y, b_hi.z, b_hi.w};
+#pragma unroll
+            for (int jj = 0; jj < NP; ++jj) {
+              A0[jj][0] = a_[jj]; A0[jj][1] = a_[jj + 4];
+              A1[jj][0] = b_[jj]; A1[jj][1] = b_[jj + 4];
+            }
           } else {
 #pragma unroll
-            for (int L = 0; L < 8; ++L) A0[L] = A1[L] = 0u;
+            for (int jj = 0; jj < NP; ++jj) A0[jj][0] = A0[jj][1] = A1[jj][0] = A1[jj][1] = 0u;
           }
         }
         const uint32_t p0 = P[r0], p1 = P[r0 + 8];
-        const float ws0 = f16_bits_to_f32((uint16_t)(p0 & 0xFFFF)), wz0 = f16_bits_to_f32((uint16_t)(p0 >> 16));
-        const float ws1 = f16_bits_to_f32((uint16_t)(p1 & 0xFFFF)), wz1 = f16_bits_to_f32((uint16_t)(p1 >> 16));
+        const float ws0 = f16_bits_to_f32((uint16_t)(p0 & 0xFFFF));
+        const float ws1 = f16_bits_to_f32((uint16_t)(p1 & 0xFFFF));
 
 #pragma unroll
         for (int n = 0; n < NW; ++n) {
+          if (nbase + n >= nbi) break;  // N tiles past the item's tokens
           // N tile (nbase + n) = activation block (nbase + n); token gq of it.
           const uint8_t* blk = A + (nbase + n) * kGPS * kActBlockBytes;
           const uint8_t* qrow = blk + gq * kActRowBytes;
-          const uint4 u0 = *reinterpret_cast<const uint4*>(qrow + (((2 * tq) ^ gq) << 4));
-          const uint4 u1 = *reinterpret_cast<const uint4*>(qrow + (((2 * tq + 1) ^ gq) << 4));
-          const uint32_t B[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
+          uint32_t B[NP][2];
+          if constexpr (WBITS == 4) {
+            // Unit 2tq holds lanes (0,4,1,5), unit 2tq+1 lanes (2,6,3,7).
+            if constexpr (NP == 4) {
+              const uint4 u0 = *reinterpret_cast<const uint4*>(qrow + (((2 * tq) ^ gq) << 4));
+              const uint4 u1 = *reinterpret_cast<const uint4*>(qrow + (((2 * tq + 1) ^ gq) << 4));
+              B[0][0] = u0.x; B[0][1] = u0.y; B[1][0] = u0.z; B[1][1] = u0.w;
+              B[2][0] = u1.x; B[2][1] = u1.y; B[3][0] = u1.z; B[3][1] = u1.w;
+            } else if constexpr (NP == 2) {
+              const uint4 u = *reinterpret_cast<const uint4*>(qrow + (((2 * tq + lg) ^ gq) << 4));
+              B[0][0] = u.x; B[0][1] = u.y; B[1][0] = u.z; B[1][1] = u.w;
+            } else {
+              const uint2 u =
+                  *reinterpret_cast<const uint2*>(qrow + (((2 * tq + (lg >> 1)) ^ gq) << 4) + (lg & 1) * 8);
+              B[0][0] = u.x; B[0][1] = u.y;
+            }
+          } else {
+            // Tied head: unit 2tq holds lanes 0..3, unit 2tq+1 lanes 4..7.
+            const uint4 u0 = *reinterpret_cast<const uint4*>(qrow + (((2 * tq) ^ gq) << 4));
+            const uint4 u1 = *reinterpret_cast<const uint4*>(qrow + (((2 * tq + 1) ^ gq) << 4));
+            const uint32_t x0[4] = {u0.x, u0.y, u0.z, u0.w}, x1[4] = {u1.x, u1.y, u1.z, u1.w};
+#pragma unroll
+            for (int jj = 0; jj < NP; ++jj) {
+              B[jj][0] = x0[jj];
+              B[jj][1] = x1[jj];
+            }
+          }
           const float2* XS = reinterpret_cast<const float2*>(blk + kActBlockTok * kActRowBytes);
           const float2 xa = XS[2 * tq], xb = XS[2 * tq + 1];
           // combined_scale = w_scale * x_scale (gemm.rs:606, 493)
           const uint64_t xs2 = f2(xa.x, xb.x);
           const uint64_t c0 = mul2(f2(ws0, ws0), xs2), c1 = mul2(f2(ws1, ws1), xs2);
 #pragma unroll
-          for (int L = 0; L < 8; ++L) {
-            int32_t d[4];
-            mma_u8s8(A0[L], A1[L], B[L], d);
-            acc_pair(&facc[n][L][0], d[0], d[1], c0, magic2);
-            acc_pair(&facc[n][L][2], d[2], d[3], c1, magic2);
+          for (int jj = 0; jj < NP; ++jj) {
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+              int32_t d[4];
+              mma_u8s8(A0[jj][h], A1[jj][h], B[jj][h], d);
+              acc_pair(&facc[n][jj][h][0], d[0], d[1], c0, magic2);
+              acc_pair(&facc[n][jj][h][2], d[2], d[3], c1, magic2);
+            }
           }
-          // zero correction: sum_g w_zero * x_sum, sequential in g (gemm.rs:666-670)
-          zc[n][0] = __fadd_rn(zc[n][0], __fmul_rn(wz0, xa.y));
-          zc[n][1] = __fadd_rn(zc[n][1], __fmul_rn(wz0, xb.y));
-          zc[n][2] = __fadd_rn(zc[n][2], __fmul_rn(wz1, xa.y));
-          zc[n][3] = __fadd_rn(zc[n][3], __fmul_rn(wz1, xb.y));
+          if (lg == 0) {
+            // zero correction: sum_g w_zero * x_sum, sequential in g (gemm.rs:666-670)
+            const float wz0 = f16_bits_to_f32((uint16_t)(p0 >> 16));
+            const float wz1 = f16_bits_to_f32((uint16_t)(p1 >> 16));
+            zc[n][0] = __fadd_rn(zc[n][0], __fmul_rn(wz0, xa.y));
+            zc[n][1] = __fadd_rn(zc[n][1], __fmul_rn(wz0, xb.y));
+            zc[n][2] = __fadd_rn(zc[n][2], __fmul_rn(wz1, xa.y));
+            zc[n][3] = __fadd_rn(zc[n][3], __fmul_rn(wz1, xb.y));
+          }
         }
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[s]);
     }
 
-    // Epilogue: horizontal-sum tree + zero correction, then bias / residual.
+    // Horizontal-sum tree ((a0+a4)+(a1+a5)) + ((a2+a6)+(a3+a7)): pair j
+    // gives s_j = a_j + a_{j+4}; a warp finishes the pairs it holds.
+    float part[NW][4];
+#pragma unroll
+    for (int n = 0; n < NW; ++n)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        float sj[NP];
+#pragma unroll
+        for (int jj = 0; jj < NP; ++jj) sj[jj] = __fadd_rn(facc[n][jj][0][i], facc[n][jj][1][i]);
+        if constexpr (NP == 4) part[n][i] = __fadd_rn(__fadd_rn(sj[0], sj[1]), __fadd_rn(sj[2], sj[3]));
+        else if constexpr (NP == 2) part[n][i] = __fadd_rn(sj[0], sj[1]);
+        else part[n][i] = sj[0];
+      }
+    if constexpr (LG > 1) {
+      float* cb = comb + (size_t)team * (LG - 1) * NW * 4 * 32;
+      if (lg > 0) {
+        if (nitems > 0 && !mbar_wait(&cfree[team], (nitems - 1) & 1, p.err)) return;
+#pragma unroll
+        for (int n = 0; n < NW; ++n)
+#pragma unroll
+          for (int i = 0; i < 4; ++i) cb[(((lg - 1) * NW + n) * 4 + i) * 32 + lane] = part[n][i];
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&cfull[team]);
+        ++nitems;
+        continue;
+      }
+      if (!mbar_wait(&cfull[team], nitems & 1, p.err)) return;
+#pragma unroll
+      for (int n = 0; n < NW; ++n)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float* c = cb + (n * 4 + i) * 32 + lane;  // lane group g at c[(g - 1) * NW * 128]
+          if constexpr (LG == 2) part[n][i] = __fadd_rn(part[n][i], c[0]);
+          else part[n][i] = __fadd_rn(__fadd_rn(part[n][i], c[0]), __fadd_rn(c[NW * 128], c[2 * NW * 128]));
+        }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&cfree[team]);
+    }
+    ++nitems;
+
+    // Epilogue: + zero correction, then bias / residual.
 #pragma unroll
     for (int n = 0; n < NW; ++n) {
 #pragma unroll
@@ -592,10 +718,7 @@ __global__ void __launch_bounds__(GemmCfg<NTILES>::kThreads, NTILES >= 3 ? 1 : 2
         const int row = tile * kTileRows + r0 + ((i & 2) ? 8 : 0);
         const int tok = t0 + (nbase + n) * 8 + 2 * tq + (i & 1);
         if (row >= p.rows || tok - t0 >= it.nt) continue;
-        float a[8];
-#pragma unroll
-        for (int L = 0; L < 8; ++L) a[L] = facc[n][L][i];
-        float v = __fadd_rn(hsum8(a), zc[n][i]);
+        float v = __fadd_rn(part[n][i], zc[n][i]);
         const size_t o = (size_t)tok * p.ld_out + row;
         if (p.mode == kEpiBias) v = __fadd_rn(v, p.bias[row]);
         else if (p.mode == kEpiResidual) v = __fadd_rn(p.residual[o], v);
@@ -607,26 +730,53 @@ __global__ void __launch_bounds__(GemmCfg<NTILES>::kThreads, NTILES >= 3 ? 1 : 2
 
 int sm_count() { return device_sm_count(); }
 
-template <int WBITS, int NTILES>
-cudaError_t launch_gemm(const GemmParams& gp, int tiles, int chunks, cudaStream_t s, bool pdl) {
-  constexpr int kStageBytes = StageCfg<NTILES>::kBytes;
-  const int nsg = (gp.groups + kGPS - 1) / kGPS;
-  int stages = (int)(((NTILES >= 3 ? 200 : 104) * 1024) / kStageBytes);
+template <class Cfg>
+size_t gemm_smem_bytes(int stages) {
+  return (size_t)stages * StageCfg<Cfg::NTILES>::kBytes + (2 * stages + 8 * Cfg::TS) * sizeof(uint64_t) +
+         Cfg::kCombBytes;
+}
+
+// Dynamic shared memory limit raised for every variant (the static arrays
+// and the per-CTA reservation stay within the SM's 228 KB).
+constexpr int kGemmSmemMax = 210 * 1024;
+
+// Ring stages that fit kMinBlocks CTAs per SM (228 KB of shared memory per
+// SM, less each CTA's static arrays), at most 8 and at most the item's.
+template <class Cfg>
+int gemm_stages(int groups) {
+  int per_cta = (228 * 1024) / Cfg::kMinBlocks - 3 * 1024;
+  if (per_cta > kGemmSmemMax) per_cta = kGemmSmemMax;
+  int stages = (int)((per_cta - gemm_smem_bytes<Cfg>(0)) / StageCfg<Cfg::NTILES>::kBytes);
+  const int nsg = (groups + kGPS - 1) / kGPS;
   if (stages > 8) stages = 8;
   if (stages > nsg) stages = nsg;
-  if (stages < 2) stages = 2;
+  return stages < 2 ? 2 : stages;
+}
+
+template <int WBITS, class Cfg>
+cudaError_t launch_gemm(const GemmParams& gp, int tiles, int chunks, cudaStream_t s) {
+  const int stages = gemm_stages<Cfg>(gp.groups);
   GemmParams p = gp;
   p.stages = stages;
   p.tiles = tiles;
-  size_t smem = (size_t)stages * kStageBytes + 2 * stages * sizeof(uint64_t);
-  auto kern = gemm_exact_kernel<WBITS, NTILES>;
-  // One persistent wave: as many CTAs as are resident at once (1 or 2 per
-  // SM), never more than the work items of the static token budget.
+  auto kern = gemm_exact_kernel<WBITS, Cfg>;
+  const size_t smem = gemm_smem_bytes<Cfg>(stages);
+  // One persistent wave: as many CTAs as are resident at once, never more
+  // than the work items of the static token budget. Residency is measured
+  // once for the largest ring this variant uses.
+  static const int resident = [] {
+    int n = 0;
+    const size_t full = gemm_smem_bytes<Cfg>(gemm_stages<Cfg>(1 << 20));
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, gemm_exact_kernel<WBITS, Cfg>, Cfg::kThreads, full) !=
+            cudaSuccess || n < 1)
+      n = 1;
+    return n;
+  }();
   const long items = (long)tiles * chunks;
-  const long wave = (long)sm_count() * (NTILES >= 3 ? 1 : 2);
+  const long wave = (long)sm_count() * resident;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)(items < wave ? items : wave));
-  cfg.blockDim = dim3(GemmCfg<NTILES>::kThreads);
+  cfg.blockDim = dim3(Cfg::kThreads);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = s;
   cudaLaunchAttribute attr[1];
@@ -634,21 +784,32 @@ cudaError_t launch_gemm(const GemmParams& gp, int tiles, int chunks, cudaStream_
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;  // programmatic dependent launch (see pdl_wait_prior)
-  (void)pdl;
   return cudaLaunchKernelEx(&cfg, kern, p);
 }
+
+// Variants used, by N tiles per item: 4-bit linear and 8-bit tied head.
+using Gemm4N1 = GemmCfg<1, 1, 1, 2, 4>;
+using Gemm4N2 = GemmCfg<2, 1, 1, 2, 1>;
+using Gemm4N3 = GemmCfg<3, 1, 1, 1, 1>;
+using Gemm4N4 = GemmCfg<4, 1, 2, 1, 1>;
+using Gemm8N1 = GemmCfg<1, 1, 1, 2, 1>;
+using Gemm8N2 = GemmCfg<2, 1, 1, 2, 1>;
+using Gemm8N3 = GemmCfg<3, 1, 1, 1, 1>;
+using Gemm8N4 = GemmCfg<4, 1, 2, 1, 1>;
 
 }  // namespace
 
 cudaError_t init_gemm_attributes() {
   // Raised once per process, before any stream capture.
-  const int bytes = 210 * 1024;
+  const int bytes = kGemmSmemMax;
   cudaError_t e = cudaSuccess;
   auto set = [&](auto kern) {
     if (e == cudaSuccess) e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
   };
-  set(gemm_exact_kernel<4, 1>); set(gemm_exact_kernel<4, 2>); set(gemm_exact_kernel<4, 3>); set(gemm_exact_kernel<4, 4>);
-  set(gemm_exact_kernel<8, 1>); set(gemm_exact_kernel<8, 2>); set(gemm_exact_kernel<8, 3>); set(gemm_exact_kernel<8, 4>);
+  set(gemm_exact_kernel<4, Gemm4N1>); set(gemm_exact_kernel<4, Gemm4N2>);
+  set(gemm_exact_kernel<4, Gemm4N3>); set(gemm_exact_kernel<4, Gemm4N4>);
+  set(gemm_exact_kernel<8, Gemm8N1>); set(gemm_exact_kernel<8, Gemm8N2>);
+  set(gemm_exact_kernel<8, Gemm8N3>); set(gemm_exact_kernel<8, Gemm8N4>);
   return e;
 }
 
@@ -706,7 +867,7 @@ cudaError_t gemm_grouped(const PackedLinear& w, size_t w_stride, int ne, const i
   gp.ne = ne;
   gp.w_stride = w_stride;
   // Items are known only on the device: one full persistent wave.
-  return launch_gemm<4, 4>(gp, w.tiles, 1 << 20, s, true);
+  return launch_gemm<4, Gemm4N4>(gp, w.tiles, 1 << 20, s);
 }
 
 cudaError_t swiglu_quant(const float* gu, int ff, int M, const int* m_dev, int gs, const ExpfTable& et, ActBuf act,
@@ -736,19 +897,20 @@ cudaError_t gemm_exact(const PackedLinear& w, const ActBuf& act, int M, float* o
   int per = M < kTokChunk ? M : kTokChunk;
   int ntiles = (per + 7) / 8;
   int chunks = (int)ceil_div(M, kTokChunk);
+  (void)pdl;  // every GEMM launch uses programmatic dependent launch
   if (w.wbits == 4) {
     switch (ntiles) {
-      case 1: return launch_gemm<4, 1>(gp, w.tiles, chunks, s, pdl);
-      case 2: return launch_gemm<4, 2>(gp, w.tiles, chunks, s, pdl);
-      case 3: return launch_gemm<4, 3>(gp, w.tiles, chunks, s, pdl);
-      default: return launch_gemm<4, 4>(gp, w.tiles, chunks, s, pdl);
+      case 1: return launch_gemm<4, Gemm4N1>(gp, w.tiles, chunks, s);
+      case 2: return launch_gemm<4, Gemm4N2>(gp, w.tiles, chunks, s);
+      case 3: return launch_gemm<4, Gemm4N3>(gp, w.tiles, chunks, s);
+      default: return launch_gemm<4, Gemm4N4>(gp, w.tiles, chunks, s);
     }
   }
   switch (ntiles) {
-    case 1: return launch_gemm<8, 1>(gp, w.tiles, chunks, s, pdl);
-    case 2: return launch_gemm<8, 2>(gp, w.tiles, chunks, s, pdl);
-    case 3: return launch_gemm<8, 3>(gp, w.tiles, chunks, s, pdl);
-    default: return launch_gemm<8, 4>(gp, w.tiles, chunks, s, pdl);
+    case 1: return launch_gemm<8, Gemm8N1>(gp, w.tiles, chunks, s);
+    case 2: return launch_gemm<8, Gemm8N2>(gp, w.tiles, chunks, s);
+    case 3: return launch_gemm<8, Gemm8N3>(gp, w.tiles, chunks, s);
+    default: return launch_gemm<8, Gemm8N4>(gp, w.tiles, chunks, s);
   }
 }
 

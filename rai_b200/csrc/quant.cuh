@@ -13,11 +13,14 @@ namespace rai {
 
 // Activation quantization of one (token, group) by one warp.
 // ---------------------------------------------------------------------------
-// Logical byte (slot t, lane L, elem b) of a token row is at t*32 + 4L + b;
-// 16-byte unit u = offset/16 is stored at unit u ^ (token & 7) so the GEMM's
-// B-fragment loads are bank-conflict free. xs: the group's len values in
-// shared memory; sqw: 32 words of per-warp shared scratch. act: the
-// activation buffer of `groups` groups (8-token x group blocks).
+// Logical byte (slot t, lane L, elem b) of a token row is at
+// t*32 + 4*pos(L) + b, with pos(L) = 2*(L & 3) + (L >> 2) for the 4-bit
+// weights (lanes j and j+4 adjacent, matching the packed weight words) and
+// pos(L) = L for the tied head; 16-byte unit u = offset/16 is stored at unit
+// u ^ (token & 7) so the GEMM's B-fragment loads are bank-conflict free.
+// xs: the group's len values in shared memory; sqw: 32 words of per-warp
+// shared scratch. act: the activation buffer of `groups` groups (8-token x
+// group blocks).
 __device__ __forceinline__ uint8_t* act_block(uint8_t* act, int groups, int tok, int g) {
   return act + ((size_t)(tok >> 3) * groups + g) * kActBlockBytes;
 }
@@ -46,7 +49,7 @@ __device__ __forceinline__ void quant_group_warp(const float* xs, int len, int w
     int off;
     if (wbits == 4) {
       const int c = col >> 6, rr = col & 63, L = rr >> 3, b = (rr & 7) >> 1, p = rr & 1;
-      off = (2 * c + p) * 32 + 4 * L + b;
+      off = (2 * c + p) * 32 + 4 * (2 * (L & 3) + (L >> 2)) + b;
     } else {
       off = (col >> 5) * 32 + (col & 31);  // lane L = (col & 31) / 4, elem b = col % 4
     }
