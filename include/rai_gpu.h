@@ -85,6 +85,25 @@ RAI_API int rai_gpu_model_create(const uint8_t* blob, size_t len, int device, ra
 RAI_API int rai_gpu_model_destroy(rai_model* model);
 RAI_API int rai_gpu_model_info(const rai_model* model, rai_model_info* info);
 
+/* Tensor-parallel form of rai_gpu_model_create (no reference counterpart:
+ * rai-infer runs one CPU process). One process per GPU; rank tp_rank of
+ * tp_size in {2, 4, 8} uploads only its shard: every linear is split by
+ * whole output rows (its query / KV heads, its ff columns, its slice of the
+ * hidden rows for o / down, its vocabulary rows), so each rank computes
+ * complete reference dot products and the results are identical to one GPU.
+ * Ranks exchange the attention and SwiGLU outputs and the hidden rows over
+ * NVLink through an exchange arena: after every rank has created its model,
+ * pass each rank's 64-byte handle (rai_gpu_tp_handle, in rank order, to every
+ * rank) to rai_gpu_tp_connect, and bring all ranks to a host barrier before
+ * any rank creates a decoder. All ranks then make the same calls (decoder
+ * create, prefill, step) with the same arguments; each returns the same
+ * tokens. Not on tensor-parallel models: rai_gpu_forward_logits and
+ * rai_gpu_prefill_many. Mixture-of-experts models are refused. */
+RAI_API int rai_gpu_model_create_tp(const uint8_t* blob, size_t len, int device, int tp_rank, int tp_size,
+                                    rai_model** out);
+RAI_API int rai_gpu_tp_handle(rai_model* model, void* handle, size_t cap);
+RAI_API int rai_gpu_tp_connect(rai_model* model, const void* handles, size_t n);
+
 /* LookupDecoder::new (rai-infer/src/lookup.rs:192-209): context window =
  * min(max_ctx, model max_context); allocates the KV cache on the device. */
 RAI_API int rai_gpu_decoder_create(rai_model* model, size_t max_ctx, rai_dec** out);

@@ -54,24 +54,48 @@ class LookupMetrics:
 
 
 class RaiModel:
-    """A .raimodel uploaded to one GPU (validated like RaiModelFile::open)."""
+    """A .raimodel uploaded to one GPU (validated like RaiModelFile::open).
 
-    def __init__(self, blob: bytes, device: int = 0):
+    With tp_size > 1 this process holds rank tp_rank's tensor-parallel shard
+    (one process per GPU); every rank must then call `tp_connect` (see
+    rai_b200.tp.connect) before creating decoders."""
+
+    TP_HANDLE_BYTES = 64
+
+    def __init__(self, blob: bytes, device: int = 0, tp_rank: int = 0, tp_size: int = 1):
         self._blob = np.frombuffer(blob, np.uint8)
         h = C.c_void_p()
-        check(native.lib().rai_gpu_model_create(self._blob.ctypes.data_as(C.c_void_p), self._blob.size,
-                                                device, C.byref(h)))
+        if tp_size == 1 and tp_rank == 0:
+            check(native.lib().rai_gpu_model_create(self._blob.ctypes.data_as(C.c_void_p), self._blob.size,
+                                                    device, C.byref(h)))
+        else:
+            check(native.lib().rai_gpu_model_create_tp(self._blob.ctypes.data_as(C.c_void_p), self._blob.size,
+                                                       device, tp_rank, tp_size, C.byref(h)))
         self._h = h
         self._blob = None
         info = native.ModelInfo()
         check(native.lib().rai_gpu_model_info(h, C.byref(info)))
         self.config = {f: getattr(info, f) for f, _ in native.ModelInfo._fields_}
         self.device = device
+        self.tp_rank, self.tp_size = tp_rank, tp_size
 
     @classmethod
-    def load(cls, path: str, device: int = 0) -> "RaiModel":
+    def load(cls, path: str, device: int = 0, tp_rank: int = 0, tp_size: int = 1) -> "RaiModel":
         with open(path, "rb") as f:
-            return cls(f.read(), device)
+            return cls(f.read(), device, tp_rank, tp_size)
+
+    def tp_handle(self) -> bytes:
+        """This rank's exchange-arena handle (64 bytes) for the other ranks."""
+        buf = (C.c_uint8 * self.TP_HANDLE_BYTES)()
+        check(native.lib().rai_gpu_tp_handle(self._h, buf, self.TP_HANDLE_BYTES))
+        return bytes(buf)
+
+    def tp_connect(self, handles: Sequence[bytes]) -> None:
+        """Map every rank's arena (handles in rank order, this rank's included)."""
+        if len(handles) != self.tp_size or any(len(h) != self.TP_HANDLE_BYTES for h in handles):
+            raise ValueError("tp_connect needs one 64-byte handle per rank")
+        blob = b"".join(handles)
+        check(native.lib().rai_gpu_tp_connect(self._h, blob, len(handles)))
 
     def close(self) -> None:
         if getattr(self, "_h", None):

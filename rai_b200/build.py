@@ -18,7 +18,7 @@ ROOT = os.path.dirname(HERE)
 CSRC = os.path.join(HERE, "csrc")
 LIB = os.path.join(HERE, "librai_gpu.so")
 SOURCES = ["kernels_gemm.cu", "kernels_layers.cu", "kernels_moe.cu", "runtime.cu", "convert_host.cpp"]
-HEADERS = ["common.cuh", "kernels.h", "layers.h", "moe.h", "quant.cuh", "raimodel_format.h"]
+HEADERS = ["common.cuh", "kernels.h", "layers.h", "moe.h", "quant.cuh", "raimodel_format.h", "tp.cuh"]
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",

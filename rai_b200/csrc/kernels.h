@@ -5,6 +5,7 @@
 #include <stdint.h>
 
 #include "common.cuh"
+#include "tp.cuh"
 
 namespace rai {
 
@@ -70,8 +71,10 @@ cudaError_t pack_linear8(const uint8_t* codes, const uint8_t* params, int rows, 
 // group of gs, +-127) or the tied 8-bit head (wbits = 8: per group of gs,
 // +-63). Tokens in [M, tok_alloc) are zero-filled. `m_dev`, if non-null,
 // overrides M with a device-resident active row count.
+// With dst set (tensor parallelism), the codes go to every destination
+// buffer at group g + dst->g_off instead of act (act gives tok_alloc).
 cudaError_t quantize_act(const float* x, int ldx, int M, const int* m_dev, int K, int gs, int wbits,
-                         ActBuf act, cudaStream_t s);
+                         ActBuf act, cudaStream_t s, const ActDst* dst = nullptr);
 
 // out[t * ld_out + r] (= epilogue(dot)) for t < M, r < rows. With m_dev set,
 // M is the static row budget (grid size) and *m_dev the active row count.
@@ -79,9 +82,12 @@ cudaError_t quantize_act(const float* x, int ldx, int M, const int* m_dev, int K
 // into `act` (one kernel).
 // act.data may be null (no quantization); normed_out (optional) receives the
 // normalized rows as f32.
+// With tp set (world > 1) and slot >= 0, x is first awaited as exchange
+// `slot` (every rank's projection rows, see tp.cuh).
 cudaError_t norm_quant(const float* x, const float* w, int n, float eps, float* residual, int M,
                        const int* m_dev, int gs, int wbits, ActBuf act, cudaStream_t s,
-                       float* normed_out = nullptr);
+                       float* normed_out = nullptr, const TpLink* tp = nullptr, int slot = -1,
+                       uint32_t* err = nullptr);
 // Grouped form of gemm_exact over ne same-shaped weight sets (expert e at
 // w.data + e * w_stride): expert e multiplies activation rows off[e] ..
 // off[e] + cnt[e] (device arrays; off[e] a multiple of 8) and writes the same
@@ -89,10 +95,22 @@ cudaError_t norm_quant(const float* x, const float* w, int n, float eps, float* 
 cudaError_t gemm_grouped(const PackedLinear& w, size_t w_stride, int ne, const int* off, const int* cnt,
                          const ActBuf& act, float* out, int ld_out, uint32_t* err, cudaStream_t s);
 // SwiGLU of gate/up rows [gate | up] (2*ff wide) quantized straight into `act`.
+// Tensor parallelism: gu holds this rank's ff slice (columns col_off ..
+// col_off + ff of ff_full) and the codes go to every rank through dst.
 cudaError_t swiglu_quant(const float* gu, int ff, int M, const int* m_dev, int gs, const ExpfTable& et, ActBuf act,
-                         cudaStream_t s);
+                         cudaStream_t s, const ActDst* dst = nullptr, int col_off = 0, int ff_full = 0);
+
+// Tensor-parallel extras of one GEMM launch: wait for exchange wait_slot
+// before reading the activations; write the result also to outs[1..n_out)
+// (outs[0] is `out`).
+struct GemmTp {
+  TpLink link;
+  int wait_slot = -1;
+  int n_out = 1;
+  float* outs[kMaxTp] = {};
+};
 cudaError_t gemm_exact(const PackedLinear& w, const ActBuf& act, int M, float* out, int ld_out,
                        const GemmEpilogue& epi, uint32_t* err, cudaStream_t s, bool pdl = false,
-                       const int* m_dev = nullptr);
+                       const int* m_dev = nullptr, const GemmTp* tp = nullptr);
 
 }  // namespace rai

@@ -131,8 +131,11 @@ __global__ void pack8_kernel(const uint8_t* __restrict__ codes, const uint8_t* _
 }
 
 // One warp per (token, group) of x.
+// With several destinations (tensor parallelism) every rank's buffer gets
+// the codes at group g + dst.g_off, and the stores are fenced at system
+// scope before the kernel ends.
 __global__ void quantize_kernel(const float* __restrict__ x, int ldx, int M, const int* m_dev,
-                                int K, int gs, int wbits, uint8_t* __restrict__ act, int tok_alloc) {
+                                int K, int gs, int wbits, ActDst dst, int tok_alloc) {
   __shared__ float sx[8][128];
   __shared__ uint32_t sqw[8][32];
   pdl_wait_prior();
@@ -143,18 +146,18 @@ __global__ void quantize_kernel(const float* __restrict__ x, int ldx, int M, con
   // The GEMM reads tokens in groups of 8: rows up to the next multiple of 8
   // past the active count are zeroed.
   const int rows = min(tok_alloc, (mact + 7) & ~7);
-  const int groups = gridDim.x;
   const int len = min(gs, K - g * gs);
   for (int tok = blockIdx.y * 8 + warp; tok < rows; tok += gridDim.y * 8) {
     if (tok >= mact) {
-      zero_group_warp(tok, act, groups, g);
+      zero_group_warp(tok, dst, g);
       continue;
     }
     const float* xr = x + (size_t)tok * ldx + (size_t)g * gs;
     for (int i = lane; i < len; i += 32) sx[warp][i] = xr[i];
     __syncwarp();
-    quant_group_warp(sx[warp], len, wbits, tok, act, groups, g, sqw[warp]);
+    quant_group_warp(sx[warp], len, wbits, tok, dst, g, sqw[warp]);
   }
+  if (dst.n > 1) __threadfence_system();
 }
 
 // RMSNorm of rai-infer (rms_norm_with_residual_avx2 / rms_norm_avx2,
@@ -168,7 +171,7 @@ __global__ void __launch_bounds__(256) norm_quant_kernel(const float* __restrict
                                                          int n, float eps, float* __restrict__ residual,
                                                          float* __restrict__ normed_out, const int* m_dev, int M,
                                                          int gs, int wbits, uint8_t* __restrict__ act,
-                                                         int tok_alloc) {
+                                                         int tok_alloc, TpLink tp, int slot, uint32_t* err) {
   extern __shared__ __align__(16) float sxn[];  // n floats of the row, then n of w
   float* sw = sxn + n;
   __shared__ float lanes[16];
@@ -179,6 +182,8 @@ __global__ void __launch_bounds__(256) norm_quant_kernel(const float* __restrict
   for (int i = threadIdx.x; i < n; i += blockDim.x) sw[i] = w[i];
   pdl_wait_prior();
   pdl_launch_dependents();
+  // Tensor parallelism: x is assembled from every rank's projection rows.
+  if (slot >= 0 && !tp_exchange(tp, slot, 0, err)) return;
   const int warp = threadIdx.x >> 5;
   const int mact = m_dev ? *m_dev : M;
   const int groups = (n + gs - 1) / gs;
@@ -245,8 +250,11 @@ __global__ void __launch_bounds__(256) norm_quant_kernel(const float* __restrict
 // activation; gate/up rows are [gate | up] of width 2*ff. Schraudolph's exp
 // for the first (ff/8)*8 columns, the host-libm expf for the tail;
 // y = (x / (1 + e)) * up.
+// Under tensor parallelism the rows hold this rank's ff slice (columns
+// col_off .. col_off + ff of the model's ff_full); the Schraudolph / expf
+// split follows the model's column index.
 __global__ void swiglu_quant_kernel(const float* __restrict__ gu, int ff, const int* m_dev, int M, int gs,
-                                    ExpfTable et, uint8_t* __restrict__ act, int tok_alloc) {
+                                    ExpfTable et, ActDst dst, int tok_alloc, int col_off, int ff_full) {
   __shared__ float sx[8][128];
   __shared__ uint32_t sqw[8][32];
   pdl_wait_prior();
@@ -255,12 +263,11 @@ __global__ void swiglu_quant_kernel(const float* __restrict__ gu, int ff, const 
   const int g = blockIdx.x;
   const int mact = m_dev ? *m_dev : M;
   const int rows = min(tok_alloc, (mact + 7) & ~7);
-  const int groups = gridDim.x;
   const int len = min(gs, ff - g * gs);
-  const int vec_end = (ff / 8) * 8;
+  const int vec_end = (ff_full / 8) * 8;
   for (int tok = blockIdx.y * 8 + warp; tok < rows; tok += gridDim.y * 8) {
   if (tok >= mact) {
-    zero_group_warp(tok, act, groups, g);
+    zero_group_warp(tok, dst, g);
     continue;
   }
   const float* row = gu + (size_t)tok * 2 * ff;
@@ -268,7 +275,7 @@ __global__ void swiglu_quant_kernel(const float* __restrict__ gu, int ff, const 
     const int col = g * gs + i;
     const float xv = row[col], u = row[ff + col];
     float sv;
-    if (col < vec_end) {
+    if (col + col_off < vec_end) {
       const float e = schraudolph(__fmul_rn(xv, -1.0f));
       sv = __fdiv_rn(xv, __fadd_rn(1.0f, e));
     } else {
@@ -277,8 +284,9 @@ __global__ void swiglu_quant_kernel(const float* __restrict__ gu, int ff, const 
     sx[warp][i] = __fmul_rn(sv, u);
   }
   __syncwarp();
-  quant_group_warp(sx[warp], len, 4, tok, act, groups, g, sqw[warp]);
+  quant_group_warp(sx[warp], len, 4, tok, dst, g, sqw[warp]);
   }
+  if (dst.n > 1) __threadfence_system();
 }
 
 // ---------------------------------------------------------------------------
@@ -301,6 +309,13 @@ struct GemmParams {
   const int* moe_cnt;
   int ne;
   size_t w_stride;
+  // Tensor parallelism: the activations are complete once exchange slot
+  // wait_slot (>= 0) is; the result rows also go to outs[1 .. n_out) (the
+  // peers' copies of `out`).
+  TpLink tp;
+  int wait_slot;
+  int n_out;
+  float* outs[kMaxTp];
 };
 
 constexpr int kMaxExperts = 256;
@@ -479,9 +494,18 @@ __global__ void __launch_bounds__(Cfg::kThreads, Cfg::kMinBlocks) gemm_exact_ker
         pdl_wait_prior();
         if (p.m_dev) mact = *p.m_dev;
       }
+      bool ok = true, first = true;
+      if (p.wait_slot >= 0) {
+        // The activations come from every rank: CTA 0 signals that this
+        // rank's producer kernel is done, then all wait for the others. The
+        // peers wrote them with generic stores; the copies below read them
+        // through the async proxy.
+        if (blockIdx.x == 0) tp_signal(p.tp, p.wait_slot);
+        ok = tp_wait(p.tp, p.wait_slot, 0, p.err);
+        asm volatile("fence.proxy.async;" ::: "memory");
+      }
       int s = 0;       // ring stage of the next fill
       uint32_t n = 0;  // previous fills of stage s
-      bool ok = true, first = true;
       for (int item = blockIdx.x; ok; item += gridDim.x, first = false) {
         GemmItem it;
         if (!decode_item<NT>(p, cum, mact, item, &it)) break;
@@ -723,9 +747,11 @@ __global__ void __launch_bounds__(Cfg::kThreads, Cfg::kMinBlocks) gemm_exact_ker
         if (p.mode == kEpiBias) v = __fadd_rn(v, p.bias[row]);
         else if (p.mode == kEpiResidual) v = __fadd_rn(p.residual[o], v);
         p.out[o] = v;
+        for (int d = 1; d < p.n_out; ++d) p.outs[d][o] = v;
       }
     }
   }
+  if (p.n_out > 1) __threadfence_system();
 }
 
 int sm_count() { return device_sm_count(); }
@@ -834,18 +860,26 @@ cudaError_t pack_linear8(const uint8_t* codes, const uint8_t* params, int rows, 
 }
 
 cudaError_t quantize_act(const float* x, int ldx, int M, const int* m_dev, int K, int gs, int wbits,
-                         ActBuf act, cudaStream_t s) {
+                         ActBuf act, cudaStream_t s, const ActDst* dst) {
+  const int groups = (int)ceil_div(K, gs);  // groups this kernel quantizes
+  ActDst d;
+  if (dst) d = *dst;
+  else { d.data[0] = act.data; d.n = 1; d.groups = act.groups; d.g_off = 0; }
   const int chunks = (int)ceil_div(act.tok_alloc, 8);
-  dim3 grid((unsigned)act.groups, (unsigned)std::max(1, std::min(chunks, grid_cap(act.groups * chunks, 4) / act.groups)));
-  return launch_pdl(quantize_kernel, grid, dim3(256), 0, s, x, ldx, M, m_dev, K, gs, wbits, act.data,
-                    act.tok_alloc);
+  dim3 grid((unsigned)groups, (unsigned)std::max(1, std::min(chunks, grid_cap(groups * chunks, 4) / groups)));
+  return launch_pdl(quantize_kernel, grid, dim3(256), 0, s, x, ldx, M, m_dev, K, gs, wbits, d, act.tok_alloc);
 }
 
 cudaError_t norm_quant(const float* x, const float* w, int n, float eps, float* residual, int M,
-                       const int* m_dev, int gs, int wbits, ActBuf act, cudaStream_t s, float* normed_out) {
+                       const int* m_dev, int gs, int wbits, ActBuf act, cudaStream_t s, float* normed_out,
+                       const TpLink* tp, int slot, uint32_t* err) {
   const int rows = act.data ? (int)min((size_t)act.tok_alloc, round_up((size_t)M, 8)) : M;
-  return launch_pdl(norm_quant_kernel, dim3((unsigned)grid_cap(rows, 1)), dim3(256), 2 * (size_t)n * sizeof(float), s, x, w, n, eps,
-                    residual, normed_out, m_dev, M, gs, wbits, act.data, act.tok_alloc);
+  TpLink link;
+  if (tp && tp->world > 1 && slot >= 0) link = *tp;
+  else slot = -1;
+  return launch_pdl(norm_quant_kernel, dim3((unsigned)grid_cap(rows, 1)), dim3(256), 2 * (size_t)n * sizeof(float),
+                    s, x, w, n, eps, residual, normed_out, m_dev, M, gs, wbits, act.data, act.tok_alloc, link, slot,
+                    err);
 }
 
 cudaError_t gemm_grouped(const PackedLinear& w, size_t w_stride, int ne, const int* off, const int* cnt,
@@ -866,21 +900,36 @@ cudaError_t gemm_grouped(const PackedLinear& w, size_t w_stride, int ne, const i
   gp.moe_cnt = cnt;
   gp.ne = ne;
   gp.w_stride = w_stride;
+  gp.wait_slot = -1;
   // Items are known only on the device: one full persistent wave.
   return launch_gemm<4, Gemm4N4>(gp, w.tiles, 1 << 20, s);
 }
 
 cudaError_t swiglu_quant(const float* gu, int ff, int M, const int* m_dev, int gs, const ExpfTable& et, ActBuf act,
-                         cudaStream_t s) {
+                         cudaStream_t s, const ActDst* dst, int col_off, int ff_full) {
+  const int groups = (int)ceil_div(ff, gs);
+  ActDst d;
+  if (dst) d = *dst;
+  else { d.data[0] = act.data; d.n = 1; d.groups = act.groups; d.g_off = 0; }
   const int chunks = (int)ceil_div(act.tok_alloc, 8);
-  dim3 grid((unsigned)act.groups, (unsigned)std::max(1, std::min(chunks, grid_cap(act.groups * chunks, 4) / act.groups)));
-  return launch_pdl(swiglu_quant_kernel, grid, dim3(256), 0, s, gu, ff, m_dev, M, gs, et, act.data, act.tok_alloc);
+  dim3 grid((unsigned)groups, (unsigned)std::max(1, std::min(chunks, grid_cap(groups * chunks, 4) / groups)));
+  return launch_pdl(swiglu_quant_kernel, grid, dim3(256), 0, s, gu, ff, m_dev, M, gs, et, d, act.tok_alloc, col_off,
+                    ff_full > 0 ? ff_full : ff);
 }
 
 cudaError_t gemm_exact(const PackedLinear& w, const ActBuf& act, int M, float* out, int ld_out,
-                       const GemmEpilogue& epi, uint32_t* err, cudaStream_t s, bool pdl, const int* m_dev) {
+                       const GemmEpilogue& epi, uint32_t* err, cudaStream_t s, bool pdl, const int* m_dev,
+                       const GemmTp* tp) {
   if (M <= 0) return cudaSuccess;
   GemmParams gp = {};
+  gp.wait_slot = -1;
+  gp.n_out = 1;
+  if (tp && tp->link.world > 1) {
+    gp.tp = tp->link;
+    gp.wait_slot = tp->wait_slot;
+    gp.n_out = tp->n_out > 0 ? tp->n_out : 1;
+    for (int d = 0; d < gp.n_out; ++d) gp.outs[d] = tp->outs[d];
+  }
   gp.m_dev = m_dev;
   gp.w = w.data;
   gp.act = act.data;

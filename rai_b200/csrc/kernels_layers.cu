@@ -32,9 +32,15 @@ constexpr int kPvMaxStages = 4;
 __global__ void embed_kernel(const uint32_t* __restrict__ ids, const int* m_dev, int M,
                              const uint8_t* __restrict__ codes, const uint8_t* __restrict__ params,
                              int vocab, int hidden, int gs, float embed_scale, float* __restrict__ out,
-                             uint32_t* err) {
+                             uint32_t* err, uint32_t* epoch, int with_logits) {
   pdl_wait_prior();
   pdl_launch_dependents();
+  // Tensor parallelism: count this forward (and whether it ends in logits)
+  // for the exchange waits of the kernels after this one.
+  if (epoch && blockIdx.x == 0 && threadIdx.x == 0) {
+    epoch[0] += 1u;
+    if (with_logits) epoch[1] += 1u;
+  }
   const int mact = active_rows(m_dev, M);
   const int ng = (hidden + gs - 1) / gs;
   for (int b = blockIdx.x; b < mact; b += gridDim.x) {
@@ -499,8 +505,16 @@ __device__ __forceinline__ unsigned long long argmax_key(float v, uint32_t idx) 
   return ((unsigned long long)u << 32) | idx;
 }
 
+// Tensor parallelism: logits hold vocabulary rows vocab_off .. vocab_off +
+// vocab; the keys carry the model's token ids and are folded into every
+// rank's best[] (dst), so all ranks end with the same argmax.
+struct BestDst {
+  unsigned long long* p[kMaxTp];
+  int n;
+};
+
 __global__ void argmax_kernel(const float* __restrict__ logits, int vocab, const int* m_dev, int M,
-                              unsigned long long* __restrict__ best) {
+                              BestDst best, int vocab_off) {
   pdl_wait_prior();
   pdl_launch_dependents();
   const int mact = active_rows(m_dev, M);
@@ -508,15 +522,17 @@ __global__ void argmax_kernel(const float* __restrict__ logits, int vocab, const
     unsigned long long k = 0;
     const float* row = logits + (size_t)b * vocab;
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < vocab; i += gridDim.x * blockDim.x) {
-      unsigned long long c = argmax_key(row[i], (uint32_t)i);
+      unsigned long long c = argmax_key(row[i], (uint32_t)(i + vocab_off));
       k = c > k ? c : k;
     }
     for (int o = 16; o; o >>= 1) {
       unsigned long long c = __shfl_xor_sync(0xffffffffu, k, o);
       k = c > k ? c : k;
     }
-    if ((threadIdx.x & 31) == 0) atomicMax(best + b, k);
+    if ((threadIdx.x & 31) == 0)
+      for (int d = 0; d < best.n; ++d) atomicMax(best.p[d] + b, k);
   }
+  if (best.n > 1) __threadfence_system();
 }
 
 // ---------------------------------------------------------------------------
@@ -633,9 +649,13 @@ __global__ void __launch_bounds__(1024) plan_kernel(StreamStep* st, int n, RowIn
 
 // Greedy acceptance per stream: accept d_i while argmax_i == d_i; the first
 // mismatch is replaced by argmax_i; if all are accepted the bonus is argmax_k.
-__global__ void accept_kernel(StreamStep* st_all, const unsigned long long* __restrict__ best) {
+__global__ void accept_kernel(StreamStep* st_all, const unsigned long long* __restrict__ best, TpLink tp, int slot,
+                              uint32_t* err) {
   pdl_wait_prior();
   pdl_launch_dependents();
+  // Tensor parallelism: best[] holds every rank's vocabulary slice once the
+  // logits exchange completes.
+  if (slot >= 0 && !tp_exchange(tp, slot, 1, err)) return;
   if (threadIdx.x != 0) return;
   StreamStep* st = st_all + blockIdx.x;
   const int dl = st->drafted, r0 = st->row0;
@@ -655,9 +675,9 @@ __global__ void accept_kernel(StreamStep* st_all, const unsigned long long* __re
 // Host launchers.
 cudaError_t launch_embed(const uint32_t* ids, const int* m_dev, int M, const uint8_t* codes,
                          const uint8_t* params, int vocab, int hidden, int gs, float embed_scale,
-                         float* out, uint32_t* err, cudaStream_t s) {
+                         float* out, uint32_t* err, cudaStream_t s, uint32_t* epoch, bool with_logits) {
   return launch_pdl(embed_kernel, dim3(grid_cap(M, 1)), dim3(256), 0, s, ids, m_dev, M, codes, params, vocab, hidden, gs,
-                    embed_scale, out, err);
+                    embed_scale, out, err, epoch, (int)with_logits);
 }
 
 cudaError_t launch_qkv_post(float* qkv, int ld, float* q_out, int nh, int nkv, int hd, const float* qn,
@@ -756,11 +776,18 @@ cudaError_t init_layer_attributes() {
 }
 
 cudaError_t launch_argmax(const float* logits, int vocab, const int* m_dev, int M, unsigned long long* best,
-                          cudaStream_t s) {
+                          cudaStream_t s, int vocab_off, unsigned long long* const* peers, int n_peers) {
   int blocks = (vocab + 4095) / 4096;
   if (blocks > 64) blocks = 64;
   dim3 grid(blocks, std::max(1, std::min(M, grid_cap(blocks * M, 2) / blocks)));
-  return launch_pdl(argmax_kernel, grid, dim3(256), 0, s, logits, vocab, m_dev, M, best);
+  BestDst d = {};
+  d.p[0] = best;
+  d.n = 1;
+  if (peers && n_peers > 1) {
+    d.n = n_peers;
+    for (int i = 0; i < n_peers; ++i) d.p[i] = peers[i];
+  }
+  return launch_pdl(argmax_kernel, grid, dim3(256), 0, s, logits, vocab, m_dev, M, d, vocab_off);
 }
 
 cudaError_t launch_ngram(const uint32_t* ctx, int ctx_cap, StreamStep* st, const StreamKV* kv, int n,
@@ -775,8 +802,12 @@ cudaError_t launch_plan(StreamStep* st, int n, RowInfo* rows, uint32_t* ids, int
                     best_len);
 }
 
-cudaError_t launch_accept(StreamStep* st, int n, const unsigned long long* best, cudaStream_t s) {
-  return launch_pdl(accept_kernel, dim3(n), dim3(32), 0, s, st, (const unsigned long long*)best);
+cudaError_t launch_accept(StreamStep* st, int n, const unsigned long long* best, cudaStream_t s, const TpLink* tp,
+                          int slot, uint32_t* err) {
+  TpLink link;
+  if (tp && tp->world > 1 && slot >= 0) link = *tp;
+  else slot = -1;
+  return launch_pdl(accept_kernel, dim3(n), dim3(32), 0, s, st, (const unsigned long long*)best, link, slot, err);
 }
 
 }  // namespace rai

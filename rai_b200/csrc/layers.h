@@ -10,6 +10,7 @@
 #include <stdint.h>
 
 #include "common.cuh"
+#include "tp.cuh"
 
 namespace rai {
 
@@ -64,9 +65,12 @@ constexpr size_t kAttnMaxSmem = 224 * 1024;
 // process, before any stream capture).
 cudaError_t init_layer_attributes();
 
+// epoch (tensor parallelism, may be null): [0] += 1 per forward, [1] += 1
+// when it ends in logits.
 cudaError_t launch_embed(const uint32_t* ids, const int* m_dev, int M, const uint8_t* codes,
                          const uint8_t* params, int vocab, int hidden, int gs, float embed_scale,
-                         float* out, uint32_t* err, cudaStream_t s);
+                         float* out, uint32_t* err, cudaStream_t s, uint32_t* epoch = nullptr,
+                         bool with_logits = false);
 cudaError_t launch_qkv_post(float* qkv, int ld, float* q_out, int nh, int nkv, int hd, const float* qn,
                             const float* kn, int qk_mode, float eps, const float* rope_cos,
                             const float* rope_sin, const StreamKV* kv, int layer, const RowInfo* rows,
@@ -83,8 +87,11 @@ cudaError_t launch_attention(const float* q, float* out, const StreamKV* kv, int
 // Group host rows into segments (runs of one stream at consecutive
 // positions, at most seg_len <= kSegRows long); returns the count (<= M).
 int build_segments(const RowInfo* rows, int M, int seg_len, AttnSeg* segs);
+// Tensor parallelism: logits are vocabulary rows vocab_off.. of the model and
+// the keys go to every rank's best[] (peers, n_peers of them, own included).
 cudaError_t launch_argmax(const float* logits, int vocab, const int* m_dev, int M, unsigned long long* best,
-                          cudaStream_t s);
+                          cudaStream_t s, int vocab_off = 0, unsigned long long* const* peers = nullptr,
+                          int n_peers = 0);
 // Draft search for each of n streams; ctx for stream i at ctx + i * ctx_cap.
 cudaError_t launch_ngram(const uint32_t* ctx, int ctx_cap, StreamStep* st, const StreamKV* kv, int n,
                          int max_draft, int max_ngram, int min_ngram, cudaStream_t s);
@@ -92,6 +99,8 @@ cudaError_t launch_ngram(const uint32_t* ctx, int ctx_cap, StreamStep* st, const
 // segments / *n_segs; zero best[].
 cudaError_t launch_plan(StreamStep* st, int n, RowInfo* rows, uint32_t* ids, int* m_active, AttnSeg* segs,
                         int* n_segs, int seg_len, unsigned long long* best, int best_len, cudaStream_t s);
-cudaError_t launch_accept(StreamStep* st, int n, const unsigned long long* best, cudaStream_t s);
+// With tp (world > 1) and slot >= 0, best[] is awaited as exchange `slot`.
+cudaError_t launch_accept(StreamStep* st, int n, const unsigned long long* best, cudaStream_t s,
+                          const TpLink* tp = nullptr, int slot = -1, uint32_t* err = nullptr);
 
 }  // namespace rai

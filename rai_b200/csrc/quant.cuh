@@ -8,6 +8,7 @@
 
 #include "common.cuh"
 #include "kernels.h"
+#include "tp.cuh"
 
 namespace rai {
 
@@ -25,12 +26,9 @@ __device__ __forceinline__ uint8_t* act_block(uint8_t* act, int groups, int tok,
   return act + ((size_t)(tok >> 3) * groups + g) * kActBlockBytes;
 }
 
-__device__ __forceinline__ void quant_group_warp(const float* xs, int len, int wbits, int tok, uint8_t* act,
-                                                 int groups, int g, uint32_t* sqw) {
+__device__ __forceinline__ void quant_group_warp(const float* xs, int len, int wbits, int tok, const ActDst& dst,
+                                                 int g, uint32_t* sqw) {
   const int lane = threadIdx.x & 31;
-  uint8_t* blk = act_block(act, groups, tok, g);
-  uint32_t* qrow = reinterpret_cast<uint32_t*>(blk + (tok & 7) * kActRowBytes);
-  float2* sc = reinterpret_cast<float2*>(blk + kActBlockTok * kActRowBytes) + (tok & 7);
   float amax = 0.f;
   for (int i = lane; i < len; i += 32) amax = fmaxf(amax, fabsf(xs[i]));
   for (int o = 16; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
@@ -73,21 +71,46 @@ __device__ __forceinline__ void quant_group_warp(const float* xs, int len, int w
   for (int j = 0; j < 8; ++j) a[j] = __shfl_sync(0xffffffffu, accj, j);
   float sum = hsum8(a);
   for (int i = (len / 8) * 8; i < len; ++i) sum = __fadd_rn(sum, xs[i]);
-  // Swizzled store: lane writes 4 bytes of logical unit u = lane / 4.
+  // Swizzled store: lane writes 4 bytes of logical unit u = lane / 4, to
+  // every destination (the peers' buffers under tensor parallelism).
   const int u = lane >> 2;
   const int phys = ((u ^ (tok & 7)) << 2) | (lane & 3);
-  qrow[phys] = sqw[lane];
-  if (lane == 0) *sc = make_float2(scale, sum);
+  const uint32_t word = sqw[lane];
+  for (int d = 0; d < dst.n; ++d) {
+    uint8_t* blk = act_block(dst.data[d], dst.groups, tok, g + dst.g_off);
+    reinterpret_cast<uint32_t*>(blk + (tok & 7) * kActRowBytes)[phys] = word;
+    if (lane == 0) reinterpret_cast<float2*>(blk + kActBlockTok * kActRowBytes)[tok & 7] = make_float2(scale, sum);
+  }
   __syncwarp();
+}
+
+__device__ __forceinline__ ActDst act_dst(uint8_t* act, int groups) {
+  ActDst d;
+  d.data[0] = act;
+  d.n = 1;
+  d.groups = groups;
+  d.g_off = 0;
+  return d;
+}
+
+__device__ __forceinline__ void quant_group_warp(const float* xs, int len, int wbits, int tok, uint8_t* act,
+                                                 int groups, int g, uint32_t* sqw) {
+  quant_group_warp(xs, len, wbits, tok, act_dst(act, groups), g, sqw);
 }
 
 // Zero codes and (scale, sum) of one (token, group): tokens past the active
 // count up to the next multiple of 8 (the GEMM reads tokens in groups of 8).
-__device__ __forceinline__ void zero_group_warp(int tok, uint8_t* act, int groups, int g) {
+__device__ __forceinline__ void zero_group_warp(int tok, const ActDst& dst, int g) {
   const int lane = threadIdx.x & 31;
-  uint8_t* blk = act_block(act, groups, tok, g);
-  reinterpret_cast<uint32_t*>(blk + (tok & 7) * kActRowBytes)[lane] = 0;
-  if (lane == 0) reinterpret_cast<float2*>(blk + kActBlockTok * kActRowBytes)[tok & 7] = make_float2(0.f, 0.f);
+  for (int d = 0; d < dst.n; ++d) {
+    uint8_t* blk = act_block(dst.data[d], dst.groups, tok, g + dst.g_off);
+    reinterpret_cast<uint32_t*>(blk + (tok & 7) * kActRowBytes)[lane] = 0;
+    if (lane == 0) reinterpret_cast<float2*>(blk + kActBlockTok * kActRowBytes)[tok & 7] = make_float2(0.f, 0.f);
+  }
+}
+
+__device__ __forceinline__ void zero_group_warp(int tok, uint8_t* act, int groups, int g) {
+  zero_group_warp(tok, act_dst(act, groups), g);
 }
 
 }  // namespace rai

@@ -126,6 +126,18 @@ struct rai_model {
   uint32_t* err_dev = nullptr;
   rai::ExpfTable expf;
 
+  // Tensor parallelism (tp_world > 1): this rank's shard of every linear
+  // (whole output rows), and the exchange arena every rank maps.
+  int tp_rank = 0, tp_world = 1;
+  int nh_l = 0, nkv_l = 0, ff_l = 0;  // heads / ff columns this rank computes
+  int h_l = 0;                         // o / down output rows per rank (hidden slice)
+  int v_l = 0, v_off = 0;              // LM head rows of this rank
+  uint8_t* arena = nullptr;
+  size_t arena_bytes = 0, arena_used = 0, flags_used = 0;
+  uint8_t* peer_arena[rai::kMaxTp] = {};
+  bool tp_connected = false;
+  std::vector<void*> ipc_opened;
+
   template <class T>
   int alloc(T** p, size_t bytes) {
     void* q = nullptr;
@@ -141,6 +153,7 @@ struct rai_model {
     int prev = 0;
     cudaGetDevice(&prev);
     cudaSetDevice(device);
+    for (void* p : ipc_opened) cudaIpcCloseMemHandle(p);
     for (void* p : allocs) cudaFree(p);
     cudaSetDevice(prev);
   }
@@ -176,31 +189,40 @@ int upload_vec(rai_model* M, const uint8_t* blob, const raimodel::Vec32& v, floa
   return upload(M, h.data(), h.size() * 4, reinterpret_cast<void**>(dev));
 }
 
-// Pack one or more raw linears with the same cols into one device linear
+// Rows row0 .. row0 + rows of a raw linear (all of it by default). Codes are
+// [rows][cols/2] and params [rows][groups][4], so a row range is contiguous.
+struct RowRange {
+  const raimodel::Linear* L;
+  size_t row0, rows;
+};
+RowRange whole(const raimodel::Linear* L) { return RowRange{L, 0, L->rows}; }
+
+// Pack one or more raw row ranges with the same cols into one device linear
 // (rows concatenated in order).
-int pack_concat(rai_model* M, const uint8_t* blob_dev, const std::vector<const raimodel::Linear*>& parts,
-                PackedLinear* out, uint8_t* dst = nullptr) {
-  size_t cols = parts[0]->cols, gs = parts[0]->group_size, ng = parts[0]->num_groups();
+int pack_concat(rai_model* M, const uint8_t* blob_dev, const std::vector<RowRange>& parts, PackedLinear* out,
+                uint8_t* dst = nullptr) {
+  size_t cols = parts[0].L->cols, gs = parts[0].L->group_size, ng = parts[0].L->num_groups();
   size_t rows = 0;
-  for (auto* p : parts) rows += p->rows;
+  for (auto& p : parts) rows += p.rows;
   uint8_t* packed = dst;
   if (!packed)
     if (int rc = M->alloc(&packed, rai::packed_linear_bytes(rows, cols, gs))) return rc;
   const uint8_t *nib = nullptr, *par = nullptr;
   void* tmp = nullptr;
   if (parts.size() == 1) {
-    nib = blob_dev + parts[0]->nib_off;
-    par = blob_dev + parts[0]->params_off;
+    nib = blob_dev + parts[0].L->nib_off + parts[0].row0 * (cols / 2);
+    par = blob_dev + parts[0].L->params_off + parts[0].row0 * ng * 4;
   } else {
     size_t nb = rows * cols / 2, pb = rows * ng * 4;
     RAI_CUDA(cudaMalloc(&tmp, nb + pb));
     uint8_t* t = static_cast<uint8_t*>(tmp);
     size_t no = 0, po = 0;
-    for (auto* p : parts) {
-      RAI_CUDA(cudaMemcpy(t + no, blob_dev + p->nib_off, p->nib_len, cudaMemcpyDeviceToDevice));
-      RAI_CUDA(cudaMemcpy(t + nb + po, blob_dev + p->params_off, p->params_len, cudaMemcpyDeviceToDevice));
-      no += p->nib_len;
-      po += p->params_len;
+    for (auto& p : parts) {
+      const size_t nl = p.rows * (cols / 2), pl = p.rows * ng * 4;
+      RAI_CUDA(cudaMemcpy(t + no, blob_dev + p.L->nib_off + p.row0 * (cols / 2), nl, cudaMemcpyDeviceToDevice));
+      RAI_CUDA(cudaMemcpy(t + nb + po, blob_dev + p.L->params_off + p.row0 * ng * 4, pl, cudaMemcpyDeviceToDevice));
+      no += nl;
+      po += pl;
     }
     nib = t;
     par = t + nb;
@@ -294,6 +316,29 @@ int check_supported(const Config& c, const raimodel::Model& L) {
   return RAI_OK;
 }
 
+// Tensor-parallel split (see tp.cuh): every linear column-parallel, so
+// heads, ff columns and hidden rows must divide evenly, and each rank's
+// attention output and ff slice must be whole activation groups.
+int check_tp(const Config& c, int rank, int world) {
+  if (world == 1 && rank == 0) return RAI_OK;
+  if (!(world == 2 || world == 4 || world == 8)) return fail(RAI_ERR_INVALID, "tensor-parallel size must be 1, 2, 4 or 8");
+  if (rank < 0 || rank >= world) return fail(RAI_ERR_INVALID, "tensor-parallel rank out of range");
+  if (c.num_experts) return fail(RAI_ERR_UNSUPPORTED, "tensor parallelism of mixture-of-experts layers");
+  if (c.has_full_qk_norm) return fail(RAI_ERR_UNSUPPORTED, "tensor parallelism with full-width QK norm");
+  if (c.num_heads % world || c.num_kv_heads % world)
+    return fail(RAI_ERR_UNSUPPORTED, "heads or KV heads not divisible by the tensor-parallel size");
+  if ((c.num_heads / world) * c.head_dim % c.group_size)
+    return fail(RAI_ERR_UNSUPPORTED, "a rank's attention output is not whole activation groups");
+  if (c.intermediate_size % (world * c.group_size))
+    return fail(RAI_ERR_UNSUPPORTED, "a rank's ff slice is not whole activation groups");
+  if (c.hidden_size % world) return fail(RAI_ERR_UNSUPPORTED, "hidden size not divisible by the tensor-parallel size");
+  return RAI_OK;
+}
+
+// Arena layout: exchange flag slots first (never reused: slot counters only
+// grow), then the batches' exchanged buffers.
+constexpr size_t kArenaFlagBytes = 1u << 20;
+
 }  // namespace
 
 // ---------------------------------------------------------------------------
@@ -331,6 +376,14 @@ struct Batch {
   rai::StreamStep* st_host = nullptr;
   uint32_t* ctx = nullptr;
   uint32_t* ctx_host = nullptr;
+  // Tensor parallelism: hidden, act_q, act_ff and best live in the model's
+  // exchange arena; *_peer[t] are rank t's copies (own included).
+  rai::TpLink tp;
+  uint32_t* epoch = nullptr;
+  float* hidden_peer[rai::kMaxTp] = {};
+  uint8_t* act_q_peer[rai::kMaxTp] = {};
+  uint8_t* act_ff_peer[rai::kMaxTp] = {};
+  unsigned long long* best_peer[rai::kMaxTp] = {};
   cudaGraphExec_t graph = nullptr;
   size_t graph_kernels = 0;
   uint32_t graph_key[3] = {0, 0, 0};
@@ -408,6 +461,21 @@ int alloc_act(Batch* B, ActBuf* a, int tok, int cols, int gs) {
   return B->alloc(&a->data, ActBuf::bytes(a->tok_alloc, a->groups));
 }
 
+// Exchanged buffers of a tensor-parallel batch: carved from the arena at the
+// same offset on every rank (all ranks create the same batches in the same
+// order), so rank t's copy is peer_arena[t] + offset. Never freed before the
+// model: a peer may still write into a region this rank has left.
+template <class T>
+int arena_alloc(rai_model* m, size_t bytes, T** local, T** peers) {
+  const size_t off = rai::round_up(m->arena_used, 256);
+  if (off + bytes > m->arena_bytes)
+    return fail(RAI_ERR_OOM, "tensor-parallel exchange arena exhausted (raise RAI_TP_ARENA_MB)");
+  m->arena_used = off + bytes;
+  *local = reinterpret_cast<T*>(m->arena + off);
+  for (int t = 0; t < m->tp_world; ++t) peers[t] = reinterpret_cast<T*>(m->peer_arena[t] + off);
+  return RAI_OK;
+}
+
 int create_batch(rai_model* m, const std::vector<rai_dec*>& decs, int R, int rows_cap, std::unique_ptr<Batch>* out) {
   const Config& c = m->cfg;
   auto B = std::make_unique<Batch>();
@@ -425,20 +493,48 @@ int create_batch(rai_model* m, const std::vector<rai_dec*>& decs, int R, int row
   RAI_CUDA(cudaEventCreate(&B->ev1));
   const size_t Rw = rows_cap, h = c.hidden_size, qd = c.q_dim(), kvd = c.kv_dim(), ff = c.intermediate_size;
   const size_t nh = c.num_heads;
-  if (int rc = B->alloc(&B->hidden, Rw * h * 4)) return rc;
+  // This rank's share (everything when not tensor-parallel).
+  const size_t W = m->tp_world, qd_l = qd / W, kvd_l = kvd / W, ff_l = ff / W, nh_l = nh / W;
+  const bool tp = W > 1;
+  if (tp && !m->tp_connected) return fail(RAI_ERR_INVALID, "tensor-parallel model not connected (rai_gpu_tp_connect)");
+  if (tp) {
+    const size_t slots = c.num_layers * rai::kXchPerLayer + 1;
+    if (m->flags_used + slots * 8 > kArenaFlagBytes) return fail(RAI_ERR_OOM, "tensor-parallel flag slots exhausted");
+    B->tp.world = (int)W;
+    B->tp.rank = m->tp_rank;
+    for (size_t t = 0; t < W; ++t)
+      B->tp.flags[t] = reinterpret_cast<unsigned long long*>(m->peer_arena[t] + m->flags_used);
+    m->flags_used += slots * 8;
+    if (int rc = B->alloc(&B->epoch, 8)) return rc;
+    RAI_CUDA(cudaMemset(B->epoch, 0, 8));
+    B->tp.epoch = B->epoch;
+    if (int rc = arena_alloc(m, Rw * h * 4, &B->hidden, B->hidden_peer)) return rc;
+  } else {
+    if (int rc = B->alloc(&B->hidden, Rw * h * 4)) return rc;
+  }
   if (int rc = B->alloc(&B->resid, Rw * h * 4)) return rc;
   if (int rc = B->alloc(&B->normed, Rw * h * 4)) return rc;
-  if (int rc = B->alloc(&B->qkv, Rw * (qd + 2 * kvd) * 4)) return rc;
-  if (int rc = B->alloc(&B->q, Rw * qd * 4)) return rc;
-  if (int rc = B->alloc(&B->attn, Rw * qd * 4)) return rc;
-  if (int rc = B->alloc(&B->gu, Rw * 2 * ff * 4)) return rc;
-  if (int rc = B->alloc(&B->ff, Rw * ff * 4)) return rc;
+  if (int rc = B->alloc(&B->qkv, Rw * (qd_l + 2 * kvd_l) * 4)) return rc;
+  if (int rc = B->alloc(&B->q, Rw * qd_l * 4)) return rc;
+  if (int rc = B->alloc(&B->attn, Rw * qd_l * 4)) return rc;
+  if (int rc = B->alloc(&B->gu, Rw * 2 * ff_l * 4)) return rc;
+  if (int rc = B->alloc(&B->ff, Rw * ff_l * 4)) return rc;
   const size_t lrows = std::min<size_t>(Rw, (size_t)std::max(R * B->n, (int)rai::kMaxRowsPerStream));
-  if (int rc = B->alloc(&B->logits, lrows * c.vocab_size * 4)) return rc;
-  if (int rc = B->alloc(&B->scores, Rw * nh * B->n_alloc * 4)) return rc;
+  if (int rc = B->alloc(&B->logits, lrows * (size_t)m->v_l * 4)) return rc;
+  if (int rc = B->alloc(&B->scores, Rw * nh_l * B->n_alloc * 4)) return rc;
   if (int rc = alloc_act(B.get(), &B->act_h, (int)Rw, (int)h, c.group_size)) return rc;
-  if (int rc = alloc_act(B.get(), &B->act_q, (int)Rw, (int)qd, c.group_size)) return rc;
-  if (int rc = alloc_act(B.get(), &B->act_ff, (int)Rw, (int)ff, c.group_size)) return rc;
+  if (tp) {
+    auto tp_act = [&](ActBuf* a, size_t cols, uint8_t** peers) -> int {
+      a->tok_alloc = (int)rai::round_up(Rw, 8);
+      a->groups = (int)rai::ceil_div(cols, c.group_size);
+      return arena_alloc(m, ActBuf::bytes(a->tok_alloc, a->groups), &a->data, peers);
+    };
+    if (int rc = tp_act(&B->act_q, qd, B->act_q_peer)) return rc;
+    if (int rc = tp_act(&B->act_ff, ff, B->act_ff_peer)) return rc;
+  } else {
+    if (int rc = alloc_act(B.get(), &B->act_q, (int)Rw, (int)qd, c.group_size)) return rc;
+    if (int rc = alloc_act(B.get(), &B->act_ff, (int)Rw, (int)ff, c.group_size)) return rc;
+  }
   int hgs = m->head.wbits == 8 ? (int)c.embed_group_size : (int)c.group_size;
   if (int rc = alloc_act(B.get(), &B->act_head, (int)lrows, (int)h, hgs)) return rc;
   if (int rc = B->alloc(&B->rows, Rw * sizeof(rai::RowInfo))) return rc;
@@ -463,7 +559,11 @@ int create_batch(rai_model* m, const std::vector<rai_dec*>& decs, int R, int row
   }
   if (int rc = B->alloc(&B->segs, Rw * sizeof(rai::AttnSeg))) return rc;
   if (int rc = B->alloc(&B->n_segs, 4)) return rc;
-  if (int rc = B->alloc(&B->best, Rw * 8)) return rc;
+  if (tp) {
+    if (int rc = arena_alloc(m, Rw * 8, &B->best, B->best_peer)) return rc;
+  } else {
+    if (int rc = B->alloc(&B->best, Rw * 8)) return rc;
+  }
   if (int rc = B->alloc(&B->kv, B->n * sizeof(rai::StreamKV))) return rc;
   if (int rc = B->alloc(&B->st, B->n * sizeof(rai::StreamStep))) return rc;
   if (int rc = B->alloc(&B->ctx, (size_t)B->n * B->ctx_cap * 4)) return rc;
@@ -491,19 +591,46 @@ int forward(Batch* B, int M, const int* m_dev, int nseg, const int* nseg_dev, in
   rai_model* Mo = B->m;
   const Config& c = Mo->cfg;
   cudaStream_t s = B->stream;
-  const int h = c.hidden_size, nh = c.num_heads, nkv = c.num_kv_heads, hd = c.head_dim;
-  const int qd = nh * hd, kvd = nkv * hd, ffd = c.intermediate_size;
+  const int h = c.hidden_size, hd = c.head_dim;
   const int gs = c.group_size;
   const float eps = c.norm_eps;
   uint32_t* err = Mo->err_dev;
+  // Tensor parallelism (see tp.cuh): this rank's heads / ff columns /
+  // hidden rows; W == 1 is the whole model.
+  const int W = Mo->tp_world, r = Mo->tp_rank;
+  const bool tp = W > 1;
+  const int nh = Mo->nh_l, nkv = Mo->nkv_l, ffd = Mo->ff_l, h_l = Mo->h_l;
+  const int qd = nh * hd, kvd = nkv * hd;
+  const rai::TpLink* link = tp ? &B->tp : nullptr;
+  auto slot = [&](size_t li, int k) { return (int)li * rai::kXchPerLayer + k; };
+  // Destinations of the exchanged activations and hidden rows: own copy first.
+  rai::ActDst dst_q, dst_ff;
+  rai::GemmTp gtp;
+  if (tp) {
+    dst_q.n = dst_ff.n = W;
+    dst_q.groups = B->act_q.groups;
+    dst_ff.groups = B->act_ff.groups;
+    dst_q.g_off = r * (qd / gs);
+    dst_ff.g_off = r * (ffd / gs);
+    gtp.link = B->tp;
+    gtp.n_out = W;
+    for (int t = 0, k = 0; t < W; ++t) {
+      const int d = t == r ? 0 : ++k;  // slot 0 is this rank
+      dst_q.data[d] = B->act_q_peer[t];
+      dst_ff.data[d] = B->act_ff_peer[t];
+      gtp.outs[d] = B->hidden_peer[t] + (size_t)r * h_l;
+    }
+  }
+  float* hid_out = B->hidden + (tp ? (size_t)r * h_l : 0);  // this rank's o / down rows
   RAI_CUDA(rai::launch_embed(B->ids, m_dev, M, Mo->embed_codes, Mo->embed_params, c.vocab_size, h,
-                             c.embed_group_size, c.embed_scale, B->hidden, err, s));
+                             c.embed_group_size, c.embed_scale, B->hidden, err, s, tp ? B->epoch : nullptr, logits));
   rai::GemmEpilogue e_res;
   e_res.mode = rai::kEpiResidual;
-  e_res.residual = B->resid;
+  e_res.residual = B->resid + (tp ? (size_t)r * h_l : 0);
   for (size_t li = 0; li < c.num_layers; ++li) {
     const LayerDev& L = Mo->layers[li];
-    RAI_CUDA(rai::norm_quant(B->hidden, L.in_norm, h, eps, B->resid, M, m_dev, gs, 4, B->act_h, s));
+    RAI_CUDA(rai::norm_quant(B->hidden, L.in_norm, h, eps, B->resid, M, m_dev, gs, 4, B->act_h, s, nullptr, link,
+                             tp && li > 0 ? slot(li - 1, rai::kXchHiddenDown) : -1, err));
     rai::GemmEpilogue e_qkv;
     if (L.bias_qkv) { e_qkv.mode = rai::kEpiBias; e_qkv.bias = L.bias_qkv; }
     RAI_CUDA(rai::gemm_exact(L.qkv, B->act_h, M, B->qkv, qd + 2 * kvd, e_qkv, err, s, false, m_dev));
@@ -512,8 +639,9 @@ int forward(Batch* B, int M, const int* m_dev, int nseg, const int* nseg_dev, in
     RAI_CUDA(rai::launch_attention(B->q, B->attn, B->kv, (int)li, B->rows, m_dev, M, B->segs, nseg_dev, nseg,
                                    seg_rows, nh, nkv, hd, Mo->scale, c.attn_logit_softcap, B->scores, B->n_alloc,
                                    Mo->expf, err, s));
-    RAI_CUDA(rai::quantize_act(B->attn, qd, M, m_dev, qd, gs, 4, B->act_q, s));
-    RAI_CUDA(rai::gemm_exact(L.o, B->act_q, M, B->hidden, h, e_res, err, s, false, m_dev));
+    RAI_CUDA(rai::quantize_act(B->attn, qd, M, m_dev, qd, gs, 4, B->act_q, s, tp ? &dst_q : nullptr));
+    if (tp) gtp.wait_slot = slot(li, rai::kXchActQ);
+    RAI_CUDA(rai::gemm_exact(L.o, B->act_q, M, hid_out, h, e_res, err, s, false, m_dev, tp ? &gtp : nullptr));
     if (L.moe) {
       // mlp_block (model.rs:208-261): route, expert SwiGLU MLPs grouped by
       // expert, weighted sum in pick order, residual add.
@@ -529,18 +657,25 @@ int forward(Batch* B, int M, const int* m_dev, int nseg, const int* nseg_dev, in
       RAI_CUDA(rai::moe_combine(B->moe_eo, k, h, B->resid, B->hidden, m_dev, M, mb, s));
       continue;
     }
-    RAI_CUDA(rai::norm_quant(B->hidden, L.post_norm, h, eps, B->resid, M, m_dev, gs, 4, B->act_h, s));
+    RAI_CUDA(rai::norm_quant(B->hidden, L.post_norm, h, eps, B->resid, M, m_dev, gs, 4, B->act_h, s, nullptr, link,
+                             tp ? slot(li, rai::kXchHiddenO) : -1, err));
     RAI_CUDA(rai::gemm_exact(L.gateup, B->act_h, M, B->gu, 2 * ffd, rai::GemmEpilogue{}, err, s, false, m_dev));
-    RAI_CUDA(rai::swiglu_quant(B->gu, ffd, M, m_dev, gs, Mo->expf, B->act_ff, s));
-    RAI_CUDA(rai::gemm_exact(L.down, B->act_ff, M, B->hidden, h, e_res, err, s, false, m_dev));
+    RAI_CUDA(rai::swiglu_quant(B->gu, ffd, M, m_dev, gs, Mo->expf, B->act_ff, s, tp ? &dst_ff : nullptr, r * ffd,
+                               (int)c.intermediate_size));
+    if (tp) gtp.wait_slot = slot(li, rai::kXchActFF);
+    RAI_CUDA(rai::gemm_exact(L.down, B->act_ff, M, hid_out, h, e_res, err, s, false, m_dev, tp ? &gtp : nullptr));
   }
-  if (logits) {
+  if (logits || tp) {
+    // Under tensor parallelism the last layer's hidden exchange is awaited
+    // here even without logits, so a forward always completes all its slots.
     const bool tied = Mo->head.wbits == 8;
     RAI_CUDA(rai::norm_quant(B->hidden, Mo->final_norm, h, eps, nullptr, M, m_dev, tied ? c.embed_group_size : gs,
-                             tied ? 8 : 4, B->act_head, s));
-    RAI_CUDA(rai::gemm_exact(Mo->head, B->act_head, M, B->logits, c.vocab_size, rai::GemmEpilogue{}, err, s,
-                             false, m_dev));
+                             tied ? 8 : 4, logits ? B->act_head : ActBuf{}, s, nullptr, link,
+                             tp ? slot(c.num_layers - 1, rai::kXchHiddenDown) : -1, err));
   }
+  if (logits)
+    RAI_CUDA(rai::gemm_exact(Mo->head, B->act_head, M, B->logits, Mo->v_l, rai::GemmEpilogue{}, err, s, false,
+                             m_dev));
   return RAI_OK;
 }
 
@@ -599,8 +734,13 @@ int ensure_graph(Batch* B, const rai_lookup_cfg* cfg) {
     const int nseg = B->n * ((R + seg_rows - 1) / seg_rows);
     rc = forward(B, rows, B->m_active, nseg, B->n_segs, seg_rows, true);
     if (rc) break;
-    if (cudaSuccess != rai::launch_argmax(B->logits, B->m->cfg.vocab_size, B->m_active, rows, B->best, s) ||
-        cudaSuccess != rai::launch_accept(B->st, B->n, B->best, s)) {
+    rai_model* m = B->m;
+    const bool tp = m->tp_world > 1;
+    const int lslot = (int)m->cfg.num_layers * rai::kXchPerLayer;  // the logits exchange
+    if (cudaSuccess != rai::launch_argmax(B->logits, m->v_l, B->m_active, rows, B->best, s, m->v_off,
+                                          tp ? B->best_peer : nullptr, m->tp_world) ||
+        cudaSuccess != rai::launch_accept(B->st, B->n, B->best, s, tp ? &B->tp : nullptr, tp ? lslot : -1,
+                                          m->err_dev)) {
       rc = fail(RAI_ERR_DEVICE, "accept launch failed");
       break;
     }
@@ -766,7 +906,7 @@ size_t rai_gpu_last_error(char* buf, size_t len) {
   return g_last_error.size();
 }
 
-int rai_gpu_model_create(const uint8_t* blob, size_t len, int device, rai_model** out) {
+static int create_model(const uint8_t* blob, size_t len, int device, int tp_rank, int tp_world, rai_model** out) {
   if (!blob || !out) return fail(RAI_ERR_INVALID, "null argument");
   *out = nullptr;
   // Host-side validation first (RaiModelFile::open), so a malformed file is
@@ -775,6 +915,7 @@ int rai_gpu_model_create(const uint8_t* blob, size_t len, int device, rai_model*
   std::string err;
   if (!raimodel::open(blob, len, layout, err)) return fail(RAI_ERR_FORMAT, err);
   if (int rc = check_supported(layout.cfg, layout)) return rc;
+  if (int rc = check_tp(layout.cfg, tp_rank, tp_world)) return rc;
   int ndev = 0;
   if (cudaGetDeviceCount(&ndev) != cudaSuccess || ndev == 0) return fail(RAI_ERR_DEVICE, "no CUDA device");
   if (device < 0 || device >= ndev) return fail(RAI_ERR_INVALID, "device index out of range");
@@ -788,6 +929,19 @@ int rai_gpu_model_create(const uint8_t* blob, size_t len, int device, rai_model*
   M->cfg = M->layout.cfg;
   const Config& c = M->cfg;
   M->scale = c.attention_scale();
+  // This rank's shard (the whole model when tp_world == 1).
+  const int W = tp_world, r = tp_rank;
+  M->tp_rank = r;
+  M->tp_world = W;
+  M->nh_l = (int)c.num_heads / W;
+  M->nkv_l = (int)c.num_kv_heads / W;
+  M->ff_l = (int)c.intermediate_size / W;
+  M->h_l = (int)c.hidden_size / W;
+  M->v_l = (int)rai::ceil_div(c.vocab_size, W);
+  M->v_off = r * M->v_l;
+  M->v_l = std::min<int>(M->v_l, (int)c.vocab_size - M->v_off);
+  const size_t qd_l = (size_t)M->nh_l * c.head_dim, kvd_l = (size_t)M->nkv_l * c.head_dim;
+  const size_t ff_l = M->ff_l, h_l = M->h_l;
   M->qk_mode = c.has_full_qk_norm ? 2 : (c.has_qk_norm ? 1 : 0);
   if (int rc = M->alloc(&M->err_dev, 4)) return rc;
   RAI_CUDA(cudaMemset(M->err_dev, 0, 4));
@@ -810,8 +964,12 @@ int rai_gpu_model_create(const uint8_t* blob, size_t len, int device, rai_model*
   for (size_t li = 0; li < c.num_layers; ++li) {
     const raimodel::Layer& L = M->layout.layers[li];
     LayerDev& D = M->layers[li];
-    if (int rc = pack_concat(M.get(), blob_dev, {&L.proj[0], &L.proj[1], &L.proj[2]}, &D.qkv)) return rc;
-    if (int rc = pack_concat(M.get(), blob_dev, {&L.proj[3]}, &D.o)) return rc;
+    if (int rc = pack_concat(M.get(), blob_dev,
+                             {RowRange{&L.proj[0], r * qd_l, qd_l}, RowRange{&L.proj[1], r * kvd_l, kvd_l},
+                              RowRange{&L.proj[2], r * kvd_l, kvd_l}},
+                             &D.qkv))
+      return rc;
+    if (int rc = pack_concat(M.get(), blob_dev, {RowRange{&L.proj[3], r * h_l, h_l}}, &D.o)) return rc;
     if (c.num_experts) {
       // Expert 0 is stored as the layer's gate/up/down, experts 1.. in
       // L.experts (format.rs:436-477).
@@ -826,15 +984,19 @@ int rai_gpu_model_create(const uint8_t* blob, size_t len, int device, rai_model*
         const raimodel::Linear* g = e == 0 ? &L.proj[4] : &L.experts[3 * (e - 1)];
         const raimodel::Linear* u = e == 0 ? &L.proj[5] : &L.experts[3 * (e - 1) + 1];
         const raimodel::Linear* d = e == 0 ? &L.proj[6] : &L.experts[3 * (e - 1) + 2];
-        if (int rc = pack_concat(M.get(), blob_dev, {g, u}, &D.x_gateup, gu + e * D.x_gu_stride)) return rc;
-        if (int rc = pack_concat(M.get(), blob_dev, {d}, &D.x_down, dn + e * D.x_dn_stride)) return rc;
+        if (int rc = pack_concat(M.get(), blob_dev, {whole(g), whole(u)}, &D.x_gateup, gu + e * D.x_gu_stride))
+          return rc;
+        if (int rc = pack_concat(M.get(), blob_dev, {whole(d)}, &D.x_down, dn + e * D.x_dn_stride)) return rc;
       }
       D.x_gateup.data = gu;
       D.x_down.data = dn;
       if (int rc = upload_vec(M.get(), blob, L.router, &D.router)) return rc;
     } else {
-      if (int rc = pack_concat(M.get(), blob_dev, {&L.proj[4], &L.proj[5]}, &D.gateup)) return rc;
-      if (int rc = pack_concat(M.get(), blob_dev, {&L.proj[6]}, &D.down)) return rc;
+      if (int rc = pack_concat(M.get(), blob_dev,
+                               {RowRange{&L.proj[4], r * ff_l, ff_l}, RowRange{&L.proj[5], r * ff_l, ff_l}},
+                               &D.gateup))
+        return rc;
+      if (int rc = pack_concat(M.get(), blob_dev, {RowRange{&L.proj[6], r * h_l, h_l}}, &D.down)) return rc;
     }
     if (int rc = upload_vec(M.get(), blob, L.input_norm, &D.in_norm)) return rc;
     if (int rc = upload_vec(M.get(), blob, L.post_attn_norm, &D.post_norm)) return rc;
@@ -842,7 +1004,8 @@ int rai_gpu_model_create(const uint8_t* blob, size_t len, int device, rai_model*
       std::vector<float> b;
       for (int p = 0; p < 3; ++p) {
         auto v = raimodel::read_vec(blob, L.bias[p]);
-        b.insert(b.end(), v.begin(), v.end());
+        const size_t w = p == 0 ? qd_l : kvd_l;  // this rank's rows of q / k / v
+        b.insert(b.end(), v.begin() + r * w, v.begin() + (r + 1) * w);
       }
       if (int rc = upload(M.get(), b.data(), b.size() * 4, reinterpret_cast<void**>(&D.bias_qkv))) return rc;
     }
@@ -853,26 +1016,89 @@ int rai_gpu_model_create(const uint8_t* blob, size_t len, int device, rai_model*
   }
   if (int rc = upload_vec(M.get(), blob, M->layout.final_norm, &M->final_norm)) return rc;
   if (M->layout.has_lm_head) {
-    if (int rc = pack_concat(M.get(), blob_dev, {&M->layout.lm_head}, &M->head)) return rc;
+    if (int rc = pack_concat(M.get(), blob_dev, {RowRange{&M->layout.lm_head, (size_t)M->v_off, (size_t)M->v_l}},
+                             &M->head))
+      return rc;
   } else {
+    // Tied head: this rank's vocabulary rows of the 8-bit embedding table.
+    const size_t vl = M->v_l, eng = rai::ceil_div(E.hidden, E.group_size);
     uint8_t* packed = nullptr;
-    if (int rc = M->alloc(&packed, rai::packed_linear_bytes(E.vocab, E.hidden, E.group_size))) return rc;
-    RAI_CUDA(rai::pack_linear8(M->embed_codes, M->embed_params, (int)E.vocab, (int)E.hidden, (int)E.group_size,
-                               packed, 0));
+    if (int rc = M->alloc(&packed, rai::packed_linear_bytes(vl, E.hidden, E.group_size))) return rc;
+    RAI_CUDA(rai::pack_linear8(M->embed_codes + (size_t)M->v_off * E.hidden,
+                               M->embed_params + (size_t)M->v_off * eng * 4, (int)vl, (int)E.hidden,
+                               (int)E.group_size, packed, 0));
     M->head.data = packed;
-    M->head.rows = (int)E.vocab;
+    M->head.rows = (int)vl;
     M->head.cols = (int)E.hidden;
     M->head.group_size = (int)E.group_size;
-    M->head.groups = (int)rai::ceil_div(E.hidden, E.group_size);
-    M->head.tiles = (int)rai::ceil_div(E.vocab, rai::kTileRows);
+    M->head.groups = (int)eng;
+    M->head.tiles = (int)rai::ceil_div(vl, rai::kTileRows);
     M->head.wbits = 8;
   }
   std::vector<float> cs, sn;
   build_rope(c, c.rope_theta, cs, sn);
   if (int rc = upload(M.get(), cs.data(), cs.size() * 4, reinterpret_cast<void**>(&M->rope_cos))) return rc;
   if (int rc = upload(M.get(), sn.data(), sn.size() * 4, reinterpret_cast<void**>(&M->rope_sin))) return rc;
+  if (W > 1) {
+    // Exchange arena: every rank maps every other rank's (rai_gpu_tp_connect).
+    const char* env = std::getenv("RAI_TP_ARENA_MB");
+    const size_t mb = env ? std::strtoull(env, nullptr, 10) : 1024;
+    M->arena_bytes = std::max<size_t>(mb, 16) << 20;
+    if (int rc = M->alloc(&M->arena, M->arena_bytes)) return rc;
+    RAI_CUDA(cudaMemset(M->arena, 0, M->arena_bytes));
+    M->flags_used = 0;
+    M->arena_used = kArenaFlagBytes;
+  }
   RAI_CUDA(cudaDeviceSynchronize());
   *out = M.release();
+  return RAI_OK;
+}
+
+int rai_gpu_model_create(const uint8_t* blob, size_t len, int device, rai_model** out) {
+  return create_model(blob, len, device, 0, 1, out);
+}
+
+int rai_gpu_model_create_tp(const uint8_t* blob, size_t len, int device, int tp_rank, int tp_size,
+                            rai_model** out) {
+  return create_model(blob, len, device, tp_rank, tp_size, out);
+}
+
+int rai_gpu_tp_handle(rai_model* m, void* handle, size_t cap) {
+  if (!m || !handle) return fail(RAI_ERR_INVALID, "null argument");
+  if (m->tp_world < 2) return fail(RAI_ERR_INVALID, "model is not tensor-parallel");
+  if (cap < sizeof(cudaIpcMemHandle_t)) return fail(RAI_ERR_INVALID, "handle buffer below 64 bytes");
+  DeviceGuard guard(m->device);
+  cudaIpcMemHandle_t h;
+  RAI_CUDA(cudaIpcGetMemHandle(&h, m->arena));
+  std::memcpy(handle, &h, sizeof(h));
+  return RAI_OK;
+}
+
+int rai_gpu_tp_connect(rai_model* m, const void* handles, size_t n) {
+  if (!m || !handles) return fail(RAI_ERR_INVALID, "null argument");
+  if (m->tp_world < 2) return fail(RAI_ERR_INVALID, "model is not tensor-parallel");
+  if (n != (size_t)m->tp_world) return fail(RAI_ERR_INVALID, "one arena handle per rank expected");
+  if (m->tp_connected) return fail(RAI_ERR_INVALID, "already connected");
+  DeviceGuard guard(m->device);
+  const uint8_t* hb = static_cast<const uint8_t*>(handles);
+  for (int t = 0; t < m->tp_world; ++t) {
+    if (t == m->tp_rank) {
+      m->peer_arena[t] = m->arena;
+      continue;
+    }
+    cudaIpcMemHandle_t h;
+    std::memcpy(&h, hb + (size_t)t * sizeof(h), sizeof(h));
+    void* p = nullptr;
+    cudaError_t e = cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess);
+    if (e != cudaSuccess) {
+      (void)cudaGetLastError();
+      return fail(RAI_ERR_DEVICE, std::string("cudaIpcOpenMemHandle(rank ") + std::to_string(t) +
+                                      "): " + cudaGetErrorString(e));
+    }
+    m->ipc_opened.push_back(p);
+    m->peer_arena[t] = static_cast<uint8_t*>(p);
+  }
+  m->tp_connected = true;
   return RAI_OK;
 }
 
@@ -915,7 +1141,8 @@ int rai_gpu_decoder_create(rai_model* m, size_t max_ctx, rai_dec** out) {
   auto d = std::make_unique<rai_dec>();
   d->m = m;
   d->max_ctx = (int)ctx;
-  size_t kv = (size_t)c.num_layers * c.num_kv_heads * ctx * c.head_dim * sizeof(float);
+  // Under tensor parallelism a rank caches only its own KV heads.
+  size_t kv = (size_t)c.num_layers * m->nkv_l * ctx * c.head_dim * sizeof(float);
   void* p = nullptr;
   cudaError_t e = cudaMalloc(&p, kv);
   if (e != cudaSuccess) return fail(RAI_ERR_OOM, "cannot allocate the KV cache");
@@ -963,6 +1190,8 @@ int rai_gpu_prefill_many(rai_dec* const* decs, size_t n, const uint32_t* const* 
   if (!decs || !ids || !lens || !pos_out || n == 0) return fail(RAI_ERR_INVALID, "null argument");
   rai_model* m = decs[0]->m;
   const Config& c = m->cfg;
+  if (m->tp_world > 1)
+    return fail(RAI_ERR_UNSUPPORTED, "prefill_many on a tensor-parallel model (use rai_gpu_prefill per decoder)");
   for (size_t i = 0; i < n; ++i) {
     rai_dec* d = decs[i];
     if (!d || d->m != m) return fail(RAI_ERR_INVALID, "prefill_many decoders must share one model");
@@ -1011,6 +1240,8 @@ int rai_gpu_prefill_many(rai_dec* const* decs, size_t n, const uint32_t* const* 
 
 int rai_gpu_forward_logits(rai_dec* d, const uint32_t* ids, size_t start_pos, size_t batch, float* logits) {
   if (!d || !ids || batch == 0) return fail(RAI_ERR_INVALID, "bad argument");
+  if (d->m->tp_world > 1)
+    return fail(RAI_ERR_UNSUPPORTED, "forward_logits on a tensor-parallel model (each rank holds a vocabulary slice)");
   const Config& c = d->m->cfg;
   if (batch > (size_t)rai::kMaxRowsPerStream) return fail(RAI_ERR_INVALID, "batch exceeds 33 rows");
   if (start_pos + batch > (size_t)d->max_ctx || start_pos + batch > c.max_context)
@@ -1083,10 +1314,11 @@ int rai_gpu_kv_truncate(rai_dec* d, size_t len) {
 int rai_gpu_kv_read(const rai_dec* d, size_t layer, size_t kvh, size_t pos, float* k, float* v) {
   if (!d || !k || !v) return fail(RAI_ERR_INVALID, "null argument");
   const Config& c = d->m->cfg;
-  if (layer >= c.num_layers || kvh >= c.num_kv_heads) return fail(RAI_ERR_INVALID, "KV cache head is out of range");
+  const size_t nkv = (size_t)d->m->nkv_l;  // this rank's KV heads under tensor parallelism
+  if (layer >= c.num_layers || kvh >= nkv) return fail(RAI_ERR_INVALID, "KV cache head is out of range");
   if (pos >= d->filled[layer]) return fail(RAI_ERR_INVALID, "KV read at unwritten position");
   DeviceGuard guard(d->m->device);
-  size_t off = ((layer * c.num_kv_heads + kvh) * (size_t)d->max_ctx + pos) * c.head_dim;
+  size_t off = ((layer * nkv + kvh) * (size_t)d->max_ctx + pos) * c.head_dim;
   RAI_CUDA(cudaMemcpy(k, d->kc + off, c.head_dim * 4, cudaMemcpyDeviceToHost));
   RAI_CUDA(cudaMemcpy(v, d->vc + off, c.head_dim * 4, cudaMemcpyDeviceToHost));
   return RAI_OK;

@@ -68,6 +68,9 @@ def lib() -> C.CDLL:
                               "(there is no CPU fallback for the decode path)")
         L = C.CDLL(LIB_PATH)
         L.rai_gpu_model_create.argtypes = [P, SZ, C.c_int, C.POINTER(P)]
+        L.rai_gpu_model_create_tp.argtypes = [P, SZ, C.c_int, C.c_int, C.c_int, C.POINTER(P)]
+        L.rai_gpu_tp_handle.argtypes = [P, P, SZ]
+        L.rai_gpu_tp_connect.argtypes = [P, P, SZ]
         L.rai_gpu_model_destroy.argtypes = [P]
         L.rai_gpu_model_info.argtypes = [P, C.POINTER(ModelInfo)]
         L.rai_gpu_decoder_create.argtypes = [P, SZ, C.POINTER(P)]
