@@ -13,9 +13,11 @@ the GPU. Weights (550 MB) exceed L2 (126 MB), so no flush is needed.
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
                     [--config tinyllama|qwen|llama8b|olmoe] [--gemm-sweep]
 
---config picks another BASELINE config (1: qwen, 3: llama8b single GPU,
-4: olmoe single GPU); --gemm-sweep runs config 5 (isolated W4A8 GEMM at the
-Llama-3.1-8B shapes, M in {1..512}).
+--config picks another BASELINE config (1: qwen, 3: llama8b, 4: olmoe
+single GPU); --gemm-sweep runs config 5 (isolated W4A8 GEMM at the
+Llama-3.1-8B shapes, M in {1..512}). With N > 1 GPUs config 3 runs tensor
+parallel (tpN: every rank holds a column-parallel shard and all ranks run
+the same stream; exchanges over NVLink), the others data parallel.
 
 Prints one JSON line (rank 0). `value` = tokens produced by all streams per
 second of device time (CUDA events around each step's graph, max over ranks);
@@ -50,7 +52,7 @@ CONFIGS = {
                  gemm=(2 * 4864, 896), cpu_prompt=256,
                  desc="1 stream, 256-token prompt with three copied 24-token spans"),
     "llama8b": dict(preset="llama3.1-8b", streams=1, prompt=2048, recipe=("random",), k=8,
-                    gemm=(2 * 14336, 4096), cpu_prompt=64,
+                    gemm=(2 * 14336, 4096), cpu_prompt=64, tp=True,
                     desc="1 stream, 2048 random prompt tokens"),
     "olmoe": dict(preset="olmoe-1b-7b", streams=1, prompt=512, recipe=("copy", 0.30), k=8,
                   gemm=(3 * 2048, 2048), cpu_prompt=512,
@@ -367,14 +369,27 @@ def main():
     path = model_path(rank, world)
     if dist:
         dist.barrier()
-    model = rai_b200.RaiModel.load(path, device=local)
+    # Tensor parallel (config 3 on N > 1 GPUs): each rank holds its shard and
+    # every rank runs every stream; otherwise streams are dealt to the ranks.
+    tp_mode = world > 1 and CFG.get("tp", False)
+    if tp_mode:
+        from rai_b200 import tp as tpmod
+        model = rai_b200.RaiModel.load(path, device=local, tp_rank=rank, tp_size=world)
+        tpmod.connect(model)
+        mine = list(range(CFG["streams"]))
+        CFG["gemm"] = (CFG["gemm"][0] // world, CFG["gemm"][1])
+    else:
+        model = rai_b200.RaiModel.load(path, device=local)
+        mine = [s for s in range(CFG["streams"]) if s % world == rank]
     vocab = model.config["vocab_size"]
-    mine = [s for s in range(CFG["streams"]) if s % world == rank]
     K_DRAFT = CFG["k"]
     max_ctx = CFG["prompt"] + (args.steps + args.warmup + 2) * (K_DRAFT + 1) + 16
     decs = [rai_b200.LookupDecoder(model, max_ctx) for _ in mine]
     ctxs = [prompt_for(CFG, 1000 + s, CFG["prompt"], vocab) for s in mine]
-    poss = rai_b200.prefill_many(decs, ctxs)
+    if tp_mode:
+        poss = [d.prefill(c) for d, c in zip(decs, ctxs)]
+    else:
+        poss = rai_b200.prefill_many(decs, ctxs)
     cfg = rai_b200.LookupConfig(max_draft=K_DRAFT, max_ngram=3, min_ngram=1)
 
     def one_step():
@@ -411,7 +426,8 @@ def main():
         t_max = stats[:2].clone()
         dist.all_reduce(t_max, op=dist.ReduceOp.MAX)
         sums = stats[2:].clone()
-        dist.all_reduce(sums, op=dist.ReduceOp.SUM)
+        # Tensor parallel: every rank produced the same tokens (count once).
+        dist.all_reduce(sums, op=dist.ReduceOp.MAX if tp_mode else dist.ReduceOp.SUM)
         stats = torch.cat([t_max, sums])
     dev_s, host_s, produced, drafted, accepted, h2d = [float(v) for v in stats.cpu()]
     nk = C.c_size_t()
@@ -433,7 +449,9 @@ def main():
             "scaling": "strong", "vs_baseline": None, "dtype": "int8xu4->int32->f32", "data": "synthetic",
             "config": {"workload": f"{CFG['preset']} prompt-lookup k={K_DRAFT}: {CFG['desc']}, greedy",
                        "streams": total_streams, "k": K_DRAFT,
-                       "parallelism": f"dp{world} (streams sharded; each GPU batches its streams' verify rows)",
+                       "parallelism": (f"tp{world} (column-parallel shards, NVLink exchanges fused into the "
+                                       "kernels; every rank runs every stream)") if tp_mode else
+                                      f"dp{world} (streams sharded; each GPU batches its streams' verify rows)",
                        "l2": f"weights {wmb:.0f} MB (+ KV) per step > L2 126 MB; no flush needed"},
             "per_stream_tok_s": produced / dev_s / total_streams,
             "verify_step_us": dev_s * 1e6 / steps_per_stream,
@@ -441,7 +459,7 @@ def main():
             "accept_rate": accepted / drafted if drafted else 0.0,
             "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": int(h2d / args.steps),
                     "d2h_bytes_per_step": int(288 * total_streams + 4)},
-            "gpu_launches": launches * world,
+            "gpu_launches": launches * world,  # every rank launches the same step graph
             "roofline": {"bound": "hbm", "achieved": gem["gbs"], "peak": peak, "unit": "GB/s",
                          "frac": gem["gbs"] / peak, "traffic": traffic, "kernel": gem["kernel"],
                          "us_per_launch": gem["us_per_launch"], "peak_kind": peak_kind},
