@@ -17,7 +17,8 @@ the GPU. Weights (550 MB) exceed L2 (126 MB), so no flush is needed.
 single GPU); --gemm-sweep runs config 5 (isolated W4A8 GEMM at the
 Llama-3.1-8B shapes, M in {1..512}). With N > 1 GPUs config 3 runs tensor
 parallel (tpN: every rank holds a column-parallel shard and all ranks run
-the same stream; exchanges over NVLink), the others data parallel.
+the same stream; exchanges over NVLink), config 4 expert parallel (epN:
+64/N experts per rank, attention replicated), the others data parallel.
 
 Prints one JSON line (rank 0). `value` = tokens produced by all streams per
 second of device time (CUDA events around each step's graph, max over ranks);
@@ -55,7 +56,7 @@ CONFIGS = {
                     gemm=(2 * 14336, 4096), cpu_prompt=64, tp=True,
                     desc="1 stream, 2048 random prompt tokens"),
     "olmoe": dict(preset="olmoe-1b-7b", streams=1, prompt=512, recipe=("copy", 0.30), k=8,
-                  gemm=(3 * 2048, 2048), cpu_prompt=512,
+                  gemm=(3 * 2048, 2048), cpu_prompt=512, tp=True, ep=True,
                   desc="1 stream, 512-token prompt (30% copied spans)"),
 }
 CFG = CONFIGS["tinyllama"]
@@ -377,7 +378,8 @@ def main():
         model = rai_b200.RaiModel.load(path, device=local, tp_rank=rank, tp_size=world)
         tpmod.connect(model)
         mine = list(range(CFG["streams"]))
-        CFG["gemm"] = (CFG["gemm"][0] // world, CFG["gemm"][1])
+        if not CFG.get("ep"):
+            CFG["gemm"] = (CFG["gemm"][0] // world, CFG["gemm"][1])
     else:
         model = rai_b200.RaiModel.load(path, device=local)
         mine = [s for s in range(CFG["streams"]) if s % world == rank]
@@ -449,7 +451,9 @@ def main():
             "scaling": "strong", "vs_baseline": None, "dtype": "int8xu4->int32->f32", "data": "synthetic",
             "config": {"workload": f"{CFG['preset']} prompt-lookup k={K_DRAFT}: {CFG['desc']}, greedy",
                        "streams": total_streams, "k": K_DRAFT,
-                       "parallelism": (f"tp{world} (column-parallel shards, NVLink exchanges fused into the "
+                       "parallelism": (f"ep{world} ({64 // world} experts per rank, attention replicated; expert "
+                                       "rows written into every rank over NVLink)") if tp_mode and CFG.get("ep") else
+                                      (f"tp{world} (column-parallel shards, NVLink exchanges fused into the "
                                        "kernels; every rank runs every stream)") if tp_mode else
                                       f"dp{world} (streams sharded; each GPU batches its streams' verify rows)",
                        "l2": f"weights {wmb:.0f} MB (+ KV) per step > L2 126 MB; no flush needed"},

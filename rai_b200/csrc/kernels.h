@@ -92,8 +92,13 @@ cudaError_t norm_quant(const float* x, const float* w, int n, float eps, float* 
 // w.data + e * w_stride): expert e multiplies activation rows off[e] ..
 // off[e] + cnt[e] (device arrays; off[e] a multiple of 8) and writes the same
 // output rows.
+// Expert parallelism: the ne weight sets are model experts e0 .. e0 + ne
+// (off / cnt indexed by model expert); with tp, result rows also go to
+// tp->outs[1..n_out).
+struct GemmTp;
 cudaError_t gemm_grouped(const PackedLinear& w, size_t w_stride, int ne, const int* off, const int* cnt,
-                         const ActBuf& act, float* out, int ld_out, uint32_t* err, cudaStream_t s);
+                         const ActBuf& act, float* out, int ld_out, uint32_t* err, cudaStream_t s, int e0 = 0,
+                         const GemmTp* tp = nullptr);
 // SwiGLU of gate/up rows [gate | up] (2*ff wide) quantized straight into `act`.
 // Tensor parallelism: gu holds this rank's ff slice (columns col_off ..
 // col_off + ff of ff_full) and the codes go to every rank through dst.

@@ -307,7 +307,8 @@ struct GemmParams {
   // moe_off[e] .. moe_off[e] + moe_cnt[e] (moe_off[e] a multiple of 8).
   const int* moe_off;
   const int* moe_cnt;
-  int ne;
+  int ne;       // weight sets (experts) of this launch: model experts moe_e0 .. moe_e0 + ne
+  int moe_e0;
   size_t w_stride;
   // Tensor parallelism: the activations are complete once exchange slot
   // wait_slot (>= 0) is; the result rows also go to outs[1 .. n_out) (the
@@ -340,8 +341,8 @@ __device__ __forceinline__ bool decode_item(const GemmParams& p, const int* cum,
   int e = 0;
   while (cum[e + 1] <= item) ++e;
   const int local = item - cum[e], chunk = local / p.tiles;
-  *it = GemmItem{p.w + (size_t)e * p.w_stride, local % p.tiles, p.moe_off[e] + chunk * kTokChunk,
-                 min(kTokChunk, p.moe_cnt[e] - chunk * kTokChunk)};
+  *it = GemmItem{p.w + (size_t)e * p.w_stride, local % p.tiles, p.moe_off[p.moe_e0 + e] + chunk * kTokChunk,
+                 min(kTokChunk, p.moe_cnt[p.moe_e0 + e] - chunk * kTokChunk)};
   return true;
 }
 
@@ -456,7 +457,7 @@ __global__ void __launch_bounds__(Cfg::kThreads, Cfg::kMinBlocks) gemm_exact_ker
         int c = 0;
         for (int e = 0; e < p.ne; ++e) {
           cum[e] = c;
-          c += tiles * ((p.moe_cnt[e] + kTokChunk - 1) / kTokChunk);
+          c += tiles * ((p.moe_cnt[p.moe_e0 + e] + kTokChunk - 1) / kTokChunk);
         }
         cum[p.ne] = c;
       }
@@ -883,7 +884,8 @@ cudaError_t norm_quant(const float* x, const float* w, int n, float eps, float* 
 }
 
 cudaError_t gemm_grouped(const PackedLinear& w, size_t w_stride, int ne, const int* off, const int* cnt,
-                         const ActBuf& act, float* out, int ld_out, uint32_t* err, cudaStream_t s) {
+                         const ActBuf& act, float* out, int ld_out, uint32_t* err, cudaStream_t s, int e0,
+                         const GemmTp* tp) {
   if (ne < 1 || ne > kMaxExperts || w.wbits != 4) return cudaErrorInvalidValue;
   GemmParams gp = {};
   gp.w = w.data;
@@ -899,8 +901,14 @@ cudaError_t gemm_grouped(const PackedLinear& w, size_t w_stride, int ne, const i
   gp.moe_off = off;
   gp.moe_cnt = cnt;
   gp.ne = ne;
+  gp.moe_e0 = e0;
   gp.w_stride = w_stride;
   gp.wait_slot = -1;
+  gp.n_out = 1;
+  if (tp && tp->link.world > 1) {
+    gp.n_out = tp->n_out > 0 ? tp->n_out : 1;
+    for (int d = 0; d < gp.n_out; ++d) gp.outs[d] = tp->outs[d];
+  }
   // Items are known only on the device: one full persistent wave.
   return launch_gemm<4, Gemm4N4>(gp, w.tiles, 1 << 20, s);
 }

@@ -109,14 +109,17 @@ __global__ void route_kernel(float* __restrict__ logits, int ne, int k, int norm
 }
 
 // Sort the (token, pick) pairs by expert: counts, segment offsets (each
-// rounded up to a multiple of 8 rows), then every pair's row. Order within
-// an expert's segment does not affect any result. One CTA.
+// rounded up to a multiple of 8 rows), then every pair's row. Within an
+// expert's segment pairs keep their index order (a stable counting sort:
+// warp match masks, per-warp counts, prefix over warps), so every rank of an
+// expert-parallel group puts each pair on the same row. One CTA.
 __global__ void __launch_bounds__(1024) moe_sort_kernel(const int* __restrict__ experts, int k, int ne,
                                                         const int* m_dev, int M, int* __restrict__ cnt,
                                                         int* __restrict__ off, int* __restrict__ row_of_pair,
                                                         int* __restrict__ pair_of_row, int* __restrict__ n_rows,
                                                         int rows_cap) {
   __shared__ int scnt[kMaxMoeExperts], soff[kMaxMoeExperts + 1], sfill[kMaxMoeExperts];
+  __shared__ int wcnt[32][kMaxMoeExperts];  // per-warp counts, then per-warp starts
   pdl_wait_prior();
   pdl_launch_dependents();
   const int np = active(m_dev, M) * k;
@@ -147,15 +150,36 @@ __global__ void __launch_bounds__(1024) moe_sort_kernel(const int* __restrict__ 
   // Padding rows between segments map to no pair.
   for (int r = threadIdx.x; r < soff[ne] && r < rows_cap; r += blockDim.x) pair_of_row[r] = -1;
   __syncthreads();
-  for (int i = threadIdx.x; i < np; i += blockDim.x) {
-    const int e = experts[i];
-    if (e < 0) {
-      row_of_pair[i] = -1;
-      continue;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+  for (int base = 0; base < np; base += blockDim.x) {
+    const int i = base + threadIdx.x;
+    const int e = i < np ? experts[i] : -1;
+    for (int t = threadIdx.x; t < nw * ne; t += blockDim.x) wcnt[t / ne][t % ne] = 0;
+    __syncthreads();
+    const unsigned same = __match_any_sync(0xffffffffu, e);
+    const int below = __popc(same & ((1u << lane) - 1u));  // same-expert pairs earlier in this warp
+    if (e >= 0 && below == 0) wcnt[warp][e] = __popc(same);
+    __syncthreads();
+    for (int x = threadIdx.x; x < ne; x += blockDim.x) {
+      int run = sfill[x];
+      for (int w = 0; w < nw; ++w) {
+        const int c = wcnt[w][x];
+        wcnt[w][x] = run;
+        run += c;
+      }
+      sfill[x] = run;
     }
-    const int r = soff[e] + atomicAdd(&sfill[e], 1);
-    row_of_pair[i] = r;
-    pair_of_row[r] = i;
+    __syncthreads();
+    if (i < np) {
+      if (e < 0) {
+        row_of_pair[i] = -1;
+      } else {
+        const int r = soff[e] + wcnt[warp][e] + below;
+        row_of_pair[i] = r;
+        pair_of_row[r] = i;
+      }
+    }
+    __syncthreads();
   }
 }
 
@@ -188,9 +212,13 @@ __global__ void moe_gather_quant_kernel(const float* __restrict__ x, int h, int 
 // out = residual + sum over picks (in order) of weight * expert_out.
 __global__ void moe_combine_kernel(const float* __restrict__ eo, const int* __restrict__ row_of_pair,
                                    const float* __restrict__ weights, int k, int h, const float* __restrict__ residual,
-                                   float* __restrict__ out, const int* m_dev, int M) {
+                                   float* __restrict__ out, const int* m_dev, int M, TpLink tp, int slot,
+                                   uint32_t* err) {
   pdl_wait_prior();
   pdl_launch_dependents();
+  // Expert parallelism: eo holds every rank's experts' rows once exchange
+  // `slot` completes.
+  if (slot >= 0 && !tp_exchange(tp, slot, 0, err)) return;
   const int b = blockIdx.y;
   if (b >= active(m_dev, M)) return;
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
@@ -226,10 +254,13 @@ cudaError_t moe_gather_quant(const float* x, int h, int k, int gs, const MoeBuff
 }
 
 cudaError_t moe_combine(const float* eo, int k, int h, const float* residual, float* out, const int* m_dev, int M,
-                        const MoeBuffers& mb, cudaStream_t s) {
+                        const MoeBuffers& mb, cudaStream_t s, const TpLink* tp, int slot, uint32_t* err) {
   dim3 grid((unsigned)ceil_div(h, 256), (unsigned)M);
+  TpLink link;
+  if (tp && tp->world > 1 && slot >= 0) link = *tp;
+  else slot = -1;
   return launch_pdl(moe_combine_kernel, grid, dim3(256), 0, s, eo, (const int*)mb.row_of_pair,
-                    (const float*)mb.weights, k, h, residual, out, m_dev, M);
+                    (const float*)mb.weights, k, h, residual, out, m_dev, M, link, slot, err);
 }
 
 cudaError_t init_moe_attributes() {

@@ -30,8 +30,11 @@ cudaError_t moe_route(const float* x, const float* router, int h, int ne, int k,
 // Quantize x's rows into expert-sorted activation rows.
 cudaError_t moe_gather_quant(const float* x, int h, int k, int gs, const MoeBuffers& mb, ActBuf act, cudaStream_t s);
 // out[b] = residual[b] + sum over picks (in order) of weight * eo[row].
+// Expert parallelism: with tp (world > 1) and slot >= 0, eo is first awaited
+// as exchange `slot` (every rank's experts' rows).
 cudaError_t moe_combine(const float* eo, int k, int h, const float* residual, float* out, const int* m_dev, int M,
-                        const MoeBuffers& mb, cudaStream_t s);
+                        const MoeBuffers& mb, cudaStream_t s, const TpLink* tp = nullptr, int slot = -1,
+                        uint32_t* err = nullptr);
 cudaError_t init_moe_attributes();
 
 }  // namespace rai

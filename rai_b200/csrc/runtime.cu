@@ -132,6 +132,10 @@ struct rai_model {
   int nh_l = 0, nkv_l = 0, ff_l = 0;  // heads / ff columns this rank computes
   int h_l = 0;                         // o / down output rows per rank (hidden slice)
   int v_l = 0, v_off = 0;              // LM head rows of this rank
+  // Mixture-of-experts models split by experts instead (expert parallel):
+  // rank r holds experts e0 .. e0 + ne_l; attention and the head are whole.
+  bool ep = false;
+  int ne_l = 0, e0 = 0;
   uint8_t* arena = nullptr;
   size_t arena_bytes = 0, arena_used = 0, flags_used = 0;
   uint8_t* peer_arena[rai::kMaxTp] = {};
@@ -323,7 +327,11 @@ int check_tp(const Config& c, int rank, int world) {
   if (world == 1 && rank == 0) return RAI_OK;
   if (!(world == 2 || world == 4 || world == 8)) return fail(RAI_ERR_INVALID, "tensor-parallel size must be 1, 2, 4 or 8");
   if (rank < 0 || rank >= world) return fail(RAI_ERR_INVALID, "tensor-parallel rank out of range");
-  if (c.num_experts) return fail(RAI_ERR_UNSUPPORTED, "tensor parallelism of mixture-of-experts layers");
+  if (c.num_experts) {
+    // Expert parallel: whole experts per rank.
+    if (c.num_experts % world) return fail(RAI_ERR_UNSUPPORTED, "experts not divisible by the parallel size");
+    return RAI_OK;
+  }
   if (c.has_full_qk_norm) return fail(RAI_ERR_UNSUPPORTED, "tensor parallelism with full-width QK norm");
   if (c.num_heads % world || c.num_kv_heads % world)
     return fail(RAI_ERR_UNSUPPORTED, "heads or KV heads not divisible by the tensor-parallel size");
@@ -384,6 +392,7 @@ struct Batch {
   uint8_t* act_q_peer[rai::kMaxTp] = {};
   uint8_t* act_ff_peer[rai::kMaxTp] = {};
   unsigned long long* best_peer[rai::kMaxTp] = {};
+  float* moe_eo_peer[rai::kMaxTp] = {};  // expert parallelism: rank t's expert-output rows
   cudaGraphExec_t graph = nullptr;
   size_t graph_kernels = 0;
   uint32_t graph_key[3] = {0, 0, 0};
@@ -493,21 +502,24 @@ int create_batch(rai_model* m, const std::vector<rai_dec*>& decs, int R, int row
   RAI_CUDA(cudaEventCreate(&B->ev1));
   const size_t Rw = rows_cap, h = c.hidden_size, qd = c.q_dim(), kvd = c.kv_dim(), ff = c.intermediate_size;
   const size_t nh = c.num_heads;
-  // This rank's share (everything when not tensor-parallel).
-  const size_t W = m->tp_world, qd_l = qd / W, kvd_l = kvd / W, ff_l = ff / W, nh_l = nh / W;
-  const bool tp = W > 1;
-  if (tp && !m->tp_connected) return fail(RAI_ERR_INVALID, "tensor-parallel model not connected (rai_gpu_tp_connect)");
-  if (tp) {
+  // This rank's share of the dense parts (everything unless tensor parallel).
+  const bool tp = m->tp_world > 1 && !m->ep, ep = m->tp_world > 1 && m->ep;
+  const size_t W = tp ? m->tp_world : 1, qd_l = qd / W, kvd_l = kvd / W, ff_l = ff / W, nh_l = nh / W;
+  if ((tp || ep) && !m->tp_connected)
+    return fail(RAI_ERR_INVALID, "multi-GPU model not connected (rai_gpu_tp_connect)");
+  if (tp || ep) {
     const size_t slots = c.num_layers * rai::kXchPerLayer + 1;
     if (m->flags_used + slots * 8 > kArenaFlagBytes) return fail(RAI_ERR_OOM, "tensor-parallel flag slots exhausted");
-    B->tp.world = (int)W;
+    B->tp.world = m->tp_world;
     B->tp.rank = m->tp_rank;
-    for (size_t t = 0; t < W; ++t)
+    for (int t = 0; t < m->tp_world; ++t)
       B->tp.flags[t] = reinterpret_cast<unsigned long long*>(m->peer_arena[t] + m->flags_used);
     m->flags_used += slots * 8;
     if (int rc = B->alloc(&B->epoch, 8)) return rc;
     RAI_CUDA(cudaMemset(B->epoch, 0, 8));
     B->tp.epoch = B->epoch;
+  }
+  if (tp) {
     if (int rc = arena_alloc(m, Rw * h * 4, &B->hidden, B->hidden_peer)) return rc;
   } else {
     if (int rc = B->alloc(&B->hidden, Rw * h * 4)) return rc;
@@ -555,7 +567,12 @@ int create_batch(rai_model* m, const std::vector<rai_dec*>& decs, int R, int row
     if (int rc = alloc_act(B.get(), &B->moe_act_x, mb.rows_cap, (int)h, c.group_size)) return rc;
     if (int rc = alloc_act(B.get(), &B->moe_act_f, mb.rows_cap, (int)ffe, c.group_size)) return rc;
     if (int rc = B->alloc(&B->moe_gu, (size_t)mb.rows_cap * 2 * ffe * 4)) return rc;
-    if (int rc = B->alloc(&B->moe_eo, (size_t)mb.rows_cap * h * 4)) return rc;
+    if (ep) {
+      // Expert parallel: every rank writes its experts' rows into each copy.
+      if (int rc = arena_alloc(m, (size_t)mb.rows_cap * h * 4, &B->moe_eo, B->moe_eo_peer)) return rc;
+    } else {
+      if (int rc = B->alloc(&B->moe_eo, (size_t)mb.rows_cap * h * 4)) return rc;
+    }
   }
   if (int rc = B->alloc(&B->segs, Rw * sizeof(rai::AttnSeg))) return rc;
   if (int rc = B->alloc(&B->n_segs, 4)) return rc;
@@ -598,7 +615,8 @@ int forward(Batch* B, int M, const int* m_dev, int nseg, const int* nseg_dev, in
   // Tensor parallelism (see tp.cuh): this rank's heads / ff columns /
   // hidden rows; W == 1 is the whole model.
   const int W = Mo->tp_world, r = Mo->tp_rank;
-  const bool tp = W > 1;
+  const bool tp = W > 1 && !Mo->ep;
+  const bool ep = W > 1 && Mo->ep;  // expert parallel: only the MoE experts are split
   const int nh = Mo->nh_l, nkv = Mo->nkv_l, ffd = Mo->ff_l, h_l = Mo->h_l;
   const int qd = nh * hd, kvd = nkv * hd;
   const rai::TpLink* link = tp ? &B->tp : nullptr;
@@ -622,8 +640,15 @@ int forward(Batch* B, int M, const int* m_dev, int nseg, const int* nseg_dev, in
     }
   }
   float* hid_out = B->hidden + (tp ? (size_t)r * h_l : 0);  // this rank's o / down rows
+  rai::GemmTp gep;  // expert parallel: the down projection's rows go to every rank
+  if (ep) {
+    gep.link = B->tp;
+    gep.n_out = W;
+    for (int t = 0, k = 0; t < W; ++t) gep.outs[t == r ? 0 : ++k] = B->moe_eo_peer[t];
+  }
   RAI_CUDA(rai::launch_embed(B->ids, m_dev, M, Mo->embed_codes, Mo->embed_params, c.vocab_size, h,
-                             c.embed_group_size, c.embed_scale, B->hidden, err, s, tp ? B->epoch : nullptr, logits));
+                             c.embed_group_size, c.embed_scale, B->hidden, err, s, (tp || ep) ? B->epoch : nullptr,
+                             logits));
   rai::GemmEpilogue e_res;
   e_res.mode = rai::kEpiResidual;
   e_res.residual = B->resid + (tp ? (size_t)r * h_l : 0);
@@ -645,16 +670,22 @@ int forward(Batch* B, int M, const int* m_dev, int nseg, const int* nseg_dev, in
     if (L.moe) {
       // mlp_block (model.rs:208-261): route, expert SwiGLU MLPs grouped by
       // expert, weighted sum in pick order, residual add.
+      // Expert parallel: routing and the sort run on every rank (the sort is
+      // stable, so every rank assigns the same rows); each rank runs its own
+      // experts and writes their rows into every rank's expert outputs; the
+      // combine waits for all of them.
       const int ne = (int)c.num_experts, k = (int)c.experts_per_token;
       const rai::MoeBuffers& mb = B->moe;
       RAI_CUDA(rai::norm_quant(B->hidden, L.post_norm, h, eps, B->resid, M, m_dev, gs, 4, ActBuf{}, s, B->normed));
       RAI_CUDA(rai::moe_route(B->normed, L.router, h, ne, k, c.norm_topk_prob, m_dev, M, Mo->expf, mb, s));
       RAI_CUDA(rai::moe_gather_quant(B->normed, h, k, gs, mb, B->moe_act_x, s));
-      RAI_CUDA(rai::gemm_grouped(L.x_gateup, L.x_gu_stride, ne, mb.off, mb.cnt, B->moe_act_x, B->moe_gu, 2 * ffd, err,
-                                 s));
+      RAI_CUDA(rai::gemm_grouped(L.x_gateup, L.x_gu_stride, Mo->ne_l, mb.off, mb.cnt, B->moe_act_x, B->moe_gu, 2 * ffd,
+                                 err, s, Mo->e0));
       RAI_CUDA(rai::swiglu_quant(B->moe_gu, ffd, mb.rows_cap, mb.n_rows, gs, Mo->expf, B->moe_act_f, s));
-      RAI_CUDA(rai::gemm_grouped(L.x_down, L.x_dn_stride, ne, mb.off, mb.cnt, B->moe_act_f, B->moe_eo, h, err, s));
-      RAI_CUDA(rai::moe_combine(B->moe_eo, k, h, B->resid, B->hidden, m_dev, M, mb, s));
+      RAI_CUDA(rai::gemm_grouped(L.x_down, L.x_dn_stride, Mo->ne_l, mb.off, mb.cnt, B->moe_act_f, B->moe_eo, h, err, s,
+                                 Mo->e0, ep ? &gep : nullptr));
+      RAI_CUDA(rai::moe_combine(B->moe_eo, k, h, B->resid, B->hidden, m_dev, M, mb, s, ep ? &B->tp : nullptr,
+                                ep ? slot(li, rai::kXchActFF) : -1, err));
       continue;
     }
     RAI_CUDA(rai::norm_quant(B->hidden, L.post_norm, h, eps, B->resid, M, m_dev, gs, 4, B->act_h, s, nullptr, link,
@@ -735,10 +766,10 @@ int ensure_graph(Batch* B, const rai_lookup_cfg* cfg) {
     rc = forward(B, rows, B->m_active, nseg, B->n_segs, seg_rows, true);
     if (rc) break;
     rai_model* m = B->m;
-    const bool tp = m->tp_world > 1;
+    const bool tp = m->tp_world > 1 && !m->ep;
     const int lslot = (int)m->cfg.num_layers * rai::kXchPerLayer;  // the logits exchange
     if (cudaSuccess != rai::launch_argmax(B->logits, m->v_l, B->m_active, rows, B->best, s, m->v_off,
-                                          tp ? B->best_peer : nullptr, m->tp_world) ||
+                                          tp ? B->best_peer : nullptr, tp ? m->tp_world : 1) ||
         cudaSuccess != rai::launch_accept(B->st, B->n, B->best, s, tp ? &B->tp : nullptr, tp ? lslot : -1,
                                           m->err_dev)) {
       rc = fail(RAI_ERR_DEVICE, "accept launch failed");
@@ -930,15 +961,21 @@ static int create_model(const uint8_t* blob, size_t len, int device, int tp_rank
   const Config& c = M->cfg;
   M->scale = c.attention_scale();
   // This rank's shard (the whole model when tp_world == 1).
-  const int W = tp_world, r = tp_rank;
+  const int r = tp_rank;
   M->tp_rank = r;
-  M->tp_world = W;
+  M->tp_world = tp_world;
+  M->ep = tp_world > 1 && c.num_experts > 0;
+  M->ne_l = (int)c.num_experts / tp_world;
+  M->e0 = r * M->ne_l;
+  // Tensor-parallel split factor of the dense parts (1 under expert parallelism).
+  const int W = M->ep ? 1 : tp_world;
+  const int rw = M->ep ? 0 : r;
   M->nh_l = (int)c.num_heads / W;
   M->nkv_l = (int)c.num_kv_heads / W;
   M->ff_l = (int)c.intermediate_size / W;
   M->h_l = (int)c.hidden_size / W;
   M->v_l = (int)rai::ceil_div(c.vocab_size, W);
-  M->v_off = r * M->v_l;
+  M->v_off = rw * M->v_l;
   M->v_l = std::min<int>(M->v_l, (int)c.vocab_size - M->v_off);
   const size_t qd_l = (size_t)M->nh_l * c.head_dim, kvd_l = (size_t)M->nkv_l * c.head_dim;
   const size_t ff_l = M->ff_l, h_l = M->h_l;
@@ -965,38 +1002,40 @@ static int create_model(const uint8_t* blob, size_t len, int device, int tp_rank
     const raimodel::Layer& L = M->layout.layers[li];
     LayerDev& D = M->layers[li];
     if (int rc = pack_concat(M.get(), blob_dev,
-                             {RowRange{&L.proj[0], r * qd_l, qd_l}, RowRange{&L.proj[1], r * kvd_l, kvd_l},
-                              RowRange{&L.proj[2], r * kvd_l, kvd_l}},
+                             {RowRange{&L.proj[0], rw * qd_l, qd_l}, RowRange{&L.proj[1], rw * kvd_l, kvd_l},
+                              RowRange{&L.proj[2], rw * kvd_l, kvd_l}},
                              &D.qkv))
       return rc;
-    if (int rc = pack_concat(M.get(), blob_dev, {RowRange{&L.proj[3], r * h_l, h_l}}, &D.o)) return rc;
+    if (int rc = pack_concat(M.get(), blob_dev, {RowRange{&L.proj[3], rw * h_l, h_l}}, &D.o)) return rc;
     if (c.num_experts) {
       // Expert 0 is stored as the layer's gate/up/down, experts 1.. in
       // L.experts (format.rs:436-477).
       D.moe = true;
-      const size_t ne = c.num_experts, ff = L.proj[4].rows, hs = c.hidden_size, gsz = c.group_size;
+      // This rank's experts (all of them unless expert parallel).
+      const size_t ne = M->ne_l, ff = L.proj[4].rows, hs = c.hidden_size, gsz = c.group_size;
       D.x_gu_stride = rai::packed_linear_bytes(2 * ff, hs, gsz);
       D.x_dn_stride = rai::packed_linear_bytes(hs, ff, gsz);
       uint8_t *gu = nullptr, *dn = nullptr;
       if (int rc = M->alloc(&gu, D.x_gu_stride * ne)) return rc;
       if (int rc = M->alloc(&dn, D.x_dn_stride * ne)) return rc;
-      for (size_t e = 0; e < ne; ++e) {
+      for (size_t j = 0; j < ne; ++j) {
+        const size_t e = M->e0 + j;
         const raimodel::Linear* g = e == 0 ? &L.proj[4] : &L.experts[3 * (e - 1)];
         const raimodel::Linear* u = e == 0 ? &L.proj[5] : &L.experts[3 * (e - 1) + 1];
         const raimodel::Linear* d = e == 0 ? &L.proj[6] : &L.experts[3 * (e - 1) + 2];
-        if (int rc = pack_concat(M.get(), blob_dev, {whole(g), whole(u)}, &D.x_gateup, gu + e * D.x_gu_stride))
+        if (int rc = pack_concat(M.get(), blob_dev, {whole(g), whole(u)}, &D.x_gateup, gu + j * D.x_gu_stride))
           return rc;
-        if (int rc = pack_concat(M.get(), blob_dev, {whole(d)}, &D.x_down, dn + e * D.x_dn_stride)) return rc;
+        if (int rc = pack_concat(M.get(), blob_dev, {whole(d)}, &D.x_down, dn + j * D.x_dn_stride)) return rc;
       }
       D.x_gateup.data = gu;
       D.x_down.data = dn;
       if (int rc = upload_vec(M.get(), blob, L.router, &D.router)) return rc;
     } else {
       if (int rc = pack_concat(M.get(), blob_dev,
-                               {RowRange{&L.proj[4], r * ff_l, ff_l}, RowRange{&L.proj[5], r * ff_l, ff_l}},
+                               {RowRange{&L.proj[4], rw * ff_l, ff_l}, RowRange{&L.proj[5], rw * ff_l, ff_l}},
                                &D.gateup))
         return rc;
-      if (int rc = pack_concat(M.get(), blob_dev, {RowRange{&L.proj[6], r * h_l, h_l}}, &D.down)) return rc;
+      if (int rc = pack_concat(M.get(), blob_dev, {RowRange{&L.proj[6], rw * h_l, h_l}}, &D.down)) return rc;
     }
     if (int rc = upload_vec(M.get(), blob, L.input_norm, &D.in_norm)) return rc;
     if (int rc = upload_vec(M.get(), blob, L.post_attn_norm, &D.post_norm)) return rc;
@@ -1005,7 +1044,7 @@ static int create_model(const uint8_t* blob, size_t len, int device, int tp_rank
       for (int p = 0; p < 3; ++p) {
         auto v = raimodel::read_vec(blob, L.bias[p]);
         const size_t w = p == 0 ? qd_l : kvd_l;  // this rank's rows of q / k / v
-        b.insert(b.end(), v.begin() + r * w, v.begin() + (r + 1) * w);
+        b.insert(b.end(), v.begin() + rw * w, v.begin() + (rw + 1) * w);
       }
       if (int rc = upload(M.get(), b.data(), b.size() * 4, reinterpret_cast<void**>(&D.bias_qkv))) return rc;
     }
@@ -1039,7 +1078,7 @@ static int create_model(const uint8_t* blob, size_t len, int device, int tp_rank
   build_rope(c, c.rope_theta, cs, sn);
   if (int rc = upload(M.get(), cs.data(), cs.size() * 4, reinterpret_cast<void**>(&M->rope_cos))) return rc;
   if (int rc = upload(M.get(), sn.data(), sn.size() * 4, reinterpret_cast<void**>(&M->rope_sin))) return rc;
-  if (W > 1) {
+  if (tp_world > 1) {
     // Exchange arena: every rank maps every other rank's (rai_gpu_tp_connect).
     const char* env = std::getenv("RAI_TP_ARENA_MB");
     const size_t mb = env ? std::strtoull(env, nullptr, 10) : 1024;
@@ -1240,7 +1279,7 @@ int rai_gpu_prefill_many(rai_dec* const* decs, size_t n, const uint32_t* const* 
 
 int rai_gpu_forward_logits(rai_dec* d, const uint32_t* ids, size_t start_pos, size_t batch, float* logits) {
   if (!d || !ids || batch == 0) return fail(RAI_ERR_INVALID, "bad argument");
-  if (d->m->tp_world > 1)
+  if (d->m->tp_world > 1 && !d->m->ep)
     return fail(RAI_ERR_UNSUPPORTED, "forward_logits on a tensor-parallel model (each rank holds a vocabulary slice)");
   const Config& c = d->m->cfg;
   if (batch > (size_t)rai::kMaxRowsPerStream) return fail(RAI_ERR_INVALID, "batch exceeds 33 rows");

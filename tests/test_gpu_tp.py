@@ -1,5 +1,6 @@
 """Tensor-parallel decode (one process per GPU, NVLink exchange through the
-mapped arenas) against the single-GPU path on the same model and prompts.
+mapped arenas) against the single-GPU path on the same model and prompts;
+mixture-of-experts models run expert parallel through the same entry points.
 
 Tolerance: none. Every linear is split by whole output rows, so each rank
 computes complete reference dot products; the produced tokens, the
@@ -27,6 +28,9 @@ SHAPES = {
                       rope_theta=5e5, llama3=(8.0, 1.0, 4.0, 64)),
     "tp-qwen-tied": dict(hidden=256, layers=2, heads=4, kv_heads=2, head_dim=64, ff=512, vocab=700, max_ctx=512,
                          rope_theta=1e6, norm_eps=1e-6, tied=True, qkv_bias=True),
+    # Mixture of experts: split by experts (8 experts, top 2, full-width QK norm).
+    "ep-moe": dict(hidden=256, layers=2, heads=2, kv_heads=2, head_dim=128, ff=128, vocab=384, max_ctx=512,
+                   num_experts=8, experts_per_token=2, full_qk_norm=True),
 }
 
 
@@ -84,3 +88,5 @@ def test_tp_decode_matches_one_gpu(tp_models, tmp_path, name, world):
         assert got["many"] == ref["many"], f"rank {r}: batched steps differ"
         for key, val in got["kv"].items():
             assert val == ref["kv"][key], f"rank {r}: KV rows of layer/head {key} differ"
+        if "logits" in ref:
+            assert got["logits"] == ref["logits"], f"rank {r}: logits differ"

@@ -36,13 +36,20 @@ def run(path, world, rank, steps, k, device):
         ctx = ctx + toks
         pos += len(toks)
     nl = model.config["num_layers"]
-    nkv_l = model.config["num_kv_heads"] // world
+    # Mixture-of-experts models split by experts: every rank caches all heads.
+    ep = model.config["num_experts"] > 0
+    nkv_l = model.config["num_kv_heads"] // (1 if ep else world)
     kv = {}
     for layer in (0, nl - 1):
         for j in range(nkv_l):
             gk, gv = dec.kv_read(layer, j, pos - 1)
-            kv[f"{layer}/{rank * nkv_l + j}"] = [gk.view(np.uint32).tolist(), gv.view(np.uint32).tolist()]
+            head = j if ep else rank * nkv_l + j
+            kv[f"{layer}/{head}"] = [gk.view(np.uint32).tolist(), gv.view(np.uint32).tolist()]
     out["kv"] = kv
+    if ep:
+        # Expert parallel keeps the whole head on every rank: logits too.
+        lg = dec.forward_logits(ctx[-4:], pos)
+        out["logits"] = lg.view(np.uint32).tolist()
     decs = [rai_b200.LookupDecoder(model, 256) for _ in range(2)]
     ctxs = [periodic_prompt(30 + 9 * i, vocab, seed=20 + i) for i in range(2)]
     poss = [d.prefill(c) for d, c in zip(decs, ctxs)]
