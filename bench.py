@@ -393,16 +393,24 @@ def main():
     else:
         poss = rai_b200.prefill_many(decs, ctxs)
     cfg = rai_b200.LookupConfig(max_draft=K_DRAFT, max_ngram=3, min_ngram=1)
+    # Each stream's token history lives in a preallocated uint32 buffer; the
+    # step gets views of it, so the call converts nothing on the host.
+    bufs = [np.zeros(max_ctx, np.uint32) for _ in mine]
+    lens = [len(c) for c in ctxs]
+    for b, c in zip(bufs, ctxs):
+        b[: len(c)] = c
 
     def one_step():
+        views = [b[:n] for b, n in zip(bufs, lens)]
         t0 = time.perf_counter()
-        toks, mets = rai_b200.step_many(decs, poss, ctxs, cfg)
+        toks, mets = rai_b200.step_many(decs, poss, views, cfg)
         host_s = time.perf_counter() - t0
         dev_us = decs[0].last_step_us()
-        h2d = sum(4 * len(c) for c in ctxs) + len(decs) * 288
+        h2d = sum(4 * n for n in lens) + len(decs) * 288
         produced = drafted = accepted = 0
         for i, (t, met) in enumerate(zip(toks, mets)):
-            ctxs[i] += t
+            bufs[i][lens[i]: lens[i] + len(t)] = t
+            lens[i] += len(t)
             poss[i] += len(t)
             produced += met.produced
             drafted += met.drafted
