@@ -74,9 +74,19 @@ def _launch(path, world, tmp, steps=6, k=8):
     return [json.load(open(o)) for o in outs]
 
 
+def _splits(kw, world):
+    """Whether the shard rules accept this shape at `world` ranks."""
+    if kw.get("num_experts"):
+        return kw["num_experts"] % world == 0
+    return (kw["heads"] % world == 0 and kw["kv_heads"] % world == 0
+            and (kw["heads"] // world) * kw["head_dim"] % 128 == 0 and kw["ff"] % (world * 128) == 0)
+
+
 @pytest.mark.parametrize("name", list(SHAPES))
 @pytest.mark.parametrize("world", [2, 4])
 def test_tp_decode_matches_one_gpu(tp_models, tmp_path, name, world):
+    if not _splits(SHAPES[name], world):
+        pytest.skip(f"{name} does not split over {world} ranks")
     if torch.cuda.device_count() < world:
         pytest.skip(f"needs {world} GPUs")
     ref = _launch(tp_models[name], 1, tmp_path)[0]
