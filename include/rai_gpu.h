@@ -4,8 +4,8 @@
  * (rai-infer/src/lookup.rs LookupDecoder, rai-infer/src/model.rs RaiModel,
  * rai-infer/src/kv_cache.rs KVCache). The host keeps the .raimodel loader,
  * tokenizer and sampling loop; this library uploads the model once and runs
- * draft lookup, the (k+1)-row verify forward, greedy acceptance and KV
- * rollback on the GPU with no host round-trip inside a step.
+ * draft lookup, the (k+1)-row verify forward, greedy or sampled acceptance
+ * and KV rollback on the GPU with no host round-trip inside a step.
  *
  * Conventions: every function returns an int status (RAI_OK = 0, negative on
  * error) and never aborts or unwinds; rai_gpu_last_error() returns the
@@ -44,11 +44,14 @@ typedef struct rai_model rai_model;
 typedef struct rai_dec rai_dec;
 
 /* LookupConfig (rai-infer/src/lookup.rs:63-93) plus the SamplerConfig fields
- * the reference validates (lookup.rs:457-475). temperature == 0 selects
- * greedy acceptance, the t -> 0 limit of the reference's exact rule (accept a
- * drafted token iff it is the target argmax; correction and bonus are
- * argmaxes). top_k must be 0, top_p 1 and repetition_penalty 1, as in the
- * reference. */
+ * the reference validates (lookup.rs:457-475). temperature > 1e-6 runs the
+ * reference's sampled rule (accept a draft with its target probability,
+ * otherwise sample the correction from the target without it; a bonus token
+ * when all are accepted), with random numbers seeded by rai_gpu_set_seed.
+ * temperature == 0 selects greedy acceptance, the t -> 0 limit of that rule
+ * (accept a drafted token iff it is the target argmax; correction and bonus
+ * are argmaxes), which the reference itself refuses. top_k must be 0, top_p
+ * 1 and repetition_penalty 1, as in the reference. */
 typedef struct {
   uint32_t max_draft;   /* K: tokens copied per step, >= 1 */
   uint32_t max_ngram;   /* longest suffix n-gram tried first */
@@ -97,8 +100,10 @@ RAI_API int rai_gpu_model_info(const rai_model* model, rai_model_info* info);
  * rank) to rai_gpu_tp_connect, and bring all ranks to a host barrier before
  * any rank creates a decoder. All ranks then make the same calls (decoder
  * create, prefill, step) with the same arguments; each returns the same
- * tokens. Not on tensor-parallel models: rai_gpu_forward_logits and
- * rai_gpu_prefill_many. Mixture-of-experts models are refused. */
+ * tokens. Mixture-of-experts models are split by experts instead (expert
+ * parallel: whole experts per rank, attention and head replicated). Not on
+ * multi-GPU models: rai_gpu_prefill_many; not under tensor parallelism:
+ * rai_gpu_forward_logits and sampled acceptance. */
 RAI_API int rai_gpu_model_create_tp(const uint8_t* blob, size_t len, int device, int tp_rank, int tp_size,
                                     rai_model** out);
 RAI_API int rai_gpu_tp_handle(rai_model* model, void* handle, size_t cap);
@@ -125,6 +130,14 @@ RAI_API int rai_gpu_prefill_many(rai_dec* const* decs, size_t n, const uint32_t*
 RAI_API int rai_gpu_step(rai_dec* dec, size_t pos, const uint32_t* ctx, size_t ctx_len,
                  const rai_lookup_cfg* cfg, uint32_t* out_tokens, size_t out_cap,
                  size_t* n_out, rai_lookup_metrics* metrics);
+
+/* Seed of the decoder's random numbers for sampled acceptance
+ * (temperature > 1e-6), standing in for the reference's `&mut impl Rng`
+ * argument of LookupDecoder::step (rai-infer/src/lookup.rs:260-266); each
+ * step then uses the next draws. The stream is Philox4x32-10, not the
+ * reference's StdRng, so sampled outputs match the reference in
+ * distribution, not token for token. Default seed 0. */
+RAI_API int rai_gpu_set_seed(rai_dec* dec, uint64_t seed);
 
 /* One step for each of n decoders sharing one model and device, batched so
  * their verify rows share every weight read (one forward over
@@ -200,6 +213,16 @@ RAI_API int rai_gpu_w4a8_matmul_prequant(float* out, const void* packed, const v
 RAI_API int rai_gpu_attention(const float* q, const float* k, const float* v, const int* positions, size_t M,
                               size_t nh, size_t nkv, size_t hd, size_t max_ctx, float scale, float* out,
                               void* stream);
+
+/* The sampled acceptance of one prompt-lookup step (the loop of
+ * LookupDecoder::step, rai-infer/src/lookup.rs:359-403) on given verify-row
+ * logits: logits [n_drafted + 1][vocab] (device), draft tokens (host),
+ * temperature > 1e-6, random numbers of (seed, step) as rai_gpu_step draws
+ * them. Writes the produced tokens (host, capacity n_drafted + 1), their
+ * count and the accepted count. */
+RAI_API int rai_gpu_sample_accept(const float* logits, size_t vocab, const uint32_t* draft, size_t n_drafted,
+                                  float temperature, uint64_t seed, uint64_t step, uint32_t* out,
+                                  size_t* n_out, size_t* accepted);
 
 /* Number of kernels one rai_gpu_step replays (the captured CUDA graph's
  * kernel nodes for the decoder's current configuration; 0 before the first

@@ -153,6 +153,10 @@ class LookupDecoder:
                                                   out.ctypes.data_as(C.c_void_p)))
         return out
 
+    def set_seed(self, seed: int) -> None:
+        """Seed the random numbers of sampled acceptance (temperature > 0)."""
+        check(native.lib().rai_gpu_set_seed(self._h, seed))
+
     def kv_filled(self, layer: int = 0) -> int:
         f = C.c_size_t()
         check(native.lib().rai_gpu_kv_filled(self._h, layer, C.byref(f)))

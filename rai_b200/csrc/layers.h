@@ -55,6 +55,9 @@ struct StreamStep {
   int row0;     // first compacted row of this stream in the step's forward
   uint32_t tokens[kMaxRowsPerStream];  // [last, draft_0 .. draft_{k-1}]
   uint32_t out[kMaxRowsPerStream];     // produced tokens
+  // Sampled acceptance: the decoder's seed and its step count (the
+  // random-number counter of this step).
+  uint32_t rng_seed_lo, rng_seed_hi, rng_step_lo, rng_step_hi;
 };
 
 // Dynamic shared memory the attention kernels may use (the opt-in limit of
@@ -99,6 +102,11 @@ cudaError_t launch_ngram(const uint32_t* ctx, int ctx_cap, StreamStep* st, const
 // segments / *n_segs; zero best[].
 cudaError_t launch_plan(StreamStep* st, int n, RowInfo* rows, uint32_t* ids, int* m_active, AttnSeg* segs,
                         int* n_segs, int seg_len, unsigned long long* best, int best_len, cudaStream_t s);
+// Sampled acceptance (temperature > 0) of every stream from its verify rows'
+// logits (vocab wide): accept / correction / bonus tokens and counts, as
+// launch_accept does for greedy.
+cudaError_t launch_sample_accept(StreamStep* st, int n, const float* logits, int vocab, float temperature,
+                                 cudaStream_t s);
 // With tp (world > 1) and slot >= 0, best[] is awaited as exchange `slot`.
 cudaError_t launch_accept(StreamStep* st, int n, const unsigned long long* best, cudaStream_t s,
                           const TpLink* tp = nullptr, int slot = -1, uint32_t* err = nullptr);

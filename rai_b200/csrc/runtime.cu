@@ -395,7 +395,7 @@ struct Batch {
   float* moe_eo_peer[rai::kMaxTp] = {};  // expert parallelism: rank t's expert-output rows
   cudaGraphExec_t graph = nullptr;
   size_t graph_kernels = 0;
-  uint32_t graph_key[3] = {0, 0, 0};
+  uint32_t graph_key[4] = {0, 0, 0, 0};
   cudaEvent_t ev0 = nullptr, ev1 = nullptr;
   float last_us = 0.f;
 
@@ -415,6 +415,8 @@ struct Batch {
 struct rai_dec {
   rai_model* m = nullptr;
   int max_ctx = 0;
+  // Sampled acceptance: seed (rai_gpu_set_seed) and steps taken since.
+  uint64_t rng_seed = 0, rng_steps = 0;
   float last_us = 0.f;
   size_t last_kernels = 0;
   float* kc = nullptr;  // [layer][kv_head][max_ctx][head_dim]
@@ -733,14 +735,18 @@ int validate_cfg(const rai_lookup_cfg* cfg) {
       cfg->repetition_penalty != 1.0f)
     return fail(RAI_ERR_INVALID,
                 "prompt-lookup decoding requires finite temperature, top_k=0, top_p=1, and repetition_penalty=1");
-  if (cfg->temperature != 0.f)
-    return fail(RAI_ERR_UNSUPPORTED, "sampled acceptance (temperature > 0); this build runs greedy (temperature 0)");
+  // temperature 0 is the greedy limit of the reference's rule (which refuses
+  // t <= 1e-6); t > 1e-6 samples as the reference does.
+  if (cfg->temperature != 0.f && !(cfg->temperature > 1e-6f))
+    return fail(RAI_ERR_INVALID, "prompt-lookup decoding requires temperature 0 (greedy) or temperature > 1e-6");
   if (cfg->max_draft + 1 > (uint32_t)rai::kMaxRowsPerStream) return fail(RAI_ERR_INVALID, "max_draft exceeds 32");
   return RAI_OK;
 }
 
 int ensure_graph(Batch* B, const rai_lookup_cfg* cfg) {
-  uint32_t key[3] = {cfg->max_draft, cfg->max_ngram, cfg->min_ngram};
+  uint32_t tbits = 0;
+  std::memcpy(&tbits, &cfg->temperature, 4);
+  uint32_t key[4] = {cfg->max_draft, cfg->max_ngram, cfg->min_ngram, tbits};
   if (B->graph && std::memcmp(key, B->graph_key, sizeof(key)) == 0) return RAI_OK;
   if (B->graph) {
     cudaGraphExecDestroy(B->graph);
@@ -768,10 +774,17 @@ int ensure_graph(Batch* B, const rai_lookup_cfg* cfg) {
     rai_model* m = B->m;
     const bool tp = m->tp_world > 1 && !m->ep;
     const int lslot = (int)m->cfg.num_layers * rai::kXchPerLayer;  // the logits exchange
-    if (cudaSuccess != rai::launch_argmax(B->logits, m->v_l, B->m_active, rows, B->best, s, m->v_off,
-                                          tp ? B->best_peer : nullptr, tp ? m->tp_world : 1) ||
-        cudaSuccess != rai::launch_accept(B->st, B->n, B->best, s, tp ? &B->tp : nullptr, tp ? lslot : -1,
-                                          m->err_dev)) {
+    if (cfg->temperature > 0.f) {
+      // Sampled acceptance (full vocabulary rows on this GPU; refused under
+      // tensor parallelism before capture).
+      if (cudaSuccess != rai::launch_sample_accept(B->st, B->n, B->logits, m->v_l, cfg->temperature, s)) {
+        rc = fail(RAI_ERR_DEVICE, "accept launch failed");
+        break;
+      }
+    } else if (cudaSuccess != rai::launch_argmax(B->logits, m->v_l, B->m_active, rows, B->best, s, m->v_off,
+                                                 tp ? B->best_peer : nullptr, tp ? m->tp_world : 1) ||
+               cudaSuccess != rai::launch_accept(B->st, B->n, B->best, s, tp ? &B->tp : nullptr, tp ? lslot : -1,
+                                                 m->err_dev)) {
       rc = fail(RAI_ERR_DEVICE, "accept launch failed");
       break;
     }
@@ -805,6 +818,8 @@ int step_batch(Batch* B, const size_t* pos, const uint32_t* const* ctx, const si
                rai_lookup_metrics* metrics) {
   if (int rc = validate_cfg(cfg)) return rc;
   if (out_cap < cfg->max_draft + 1) return fail(RAI_ERR_INVALID, "out_tokens capacity below max_draft + 1");
+  if (cfg->temperature > 0.f && B->m->tp_world > 1 && !B->m->ep)
+    return fail(RAI_ERR_UNSUPPORTED, "sampled acceptance on a tensor-parallel model (each rank holds a vocabulary slice)");
   const Config& c = B->m->cfg;
   for (int i = 0; i < B->n; ++i) {
     rai_dec* d = B->decs[i];
@@ -822,6 +837,11 @@ int step_batch(Batch* B, const size_t* pos, const uint32_t* const* ctx, const si
     std::memcpy(B->ctx_host + (size_t)i * B->ctx_cap, ctx[i], ctx_len[i] * 4);
     B->st_host[i].pos = (int)pos[i];
     B->st_host[i].ctx_len = (int)ctx_len[i];
+    const rai_dec* d = B->decs[i];
+    B->st_host[i].rng_seed_lo = (uint32_t)d->rng_seed;
+    B->st_host[i].rng_seed_hi = (uint32_t)(d->rng_seed >> 32);
+    B->st_host[i].rng_step_lo = (uint32_t)d->rng_steps;
+    B->st_host[i].rng_step_hi = (uint32_t)(d->rng_steps >> 32);
   }
   cudaStream_t s = B->stream;
   size_t max_len = 0;
@@ -845,6 +865,7 @@ int step_batch(Batch* B, const size_t* pos, const uint32_t* const* ctx, const si
     n_out[i] = (size_t)st.produced;
     for (int t = 0; t < st.produced; ++t) out_tokens[i * out_cap + t] = st.out[t];
     for (auto& f : B->decs[i]->filled) f = pos[i] + st.produced;
+    ++B->decs[i]->rng_steps;
     B->decs[i]->last_us = B->last_us;
     B->decs[i]->last_kernels = B->graph_kernels;
     if (metrics) {
@@ -1335,6 +1356,42 @@ int rai_gpu_step_many(rai_dec* const* decs, size_t n, const size_t* pos, const u
     g_batches.emplace_back(m, std::move(nb));
   }
   return step_batch(B, pos, ctx, ctx_len, cfg, out_tokens, out_cap, n_out, metrics);
+}
+
+int rai_gpu_sample_accept(const float* logits, size_t vocab, const uint32_t* draft, size_t n_drafted,
+                          float temperature, uint64_t seed, uint64_t step, uint32_t* out, size_t* n_out,
+                          size_t* accepted) {
+  if (!logits || !out || !n_out || !accepted || (n_drafted && !draft) || vocab == 0)
+    return fail(RAI_ERR_INVALID, "null argument");
+  if (n_drafted + 1 > (size_t)rai::kMaxRowsPerStream) return fail(RAI_ERR_INVALID, "more than 32 drafts");
+  if (!(std::isfinite(temperature) && temperature > 1e-6f))
+    return fail(RAI_ERR_INVALID, "sampled acceptance requires a finite temperature > 1e-6");
+  rai::StreamStep h = {};
+  h.drafted = (int)n_drafted;
+  h.n_rows = (int)n_drafted + 1;
+  h.row0 = 0;
+  for (size_t i = 0; i < n_drafted; ++i) h.tokens[1 + i] = draft[i];
+  h.rng_seed_lo = (uint32_t)seed;
+  h.rng_seed_hi = (uint32_t)(seed >> 32);
+  h.rng_step_lo = (uint32_t)step;
+  h.rng_step_hi = (uint32_t)(step >> 32);
+  rai::StreamStep* d = nullptr;
+  RAI_CUDA(cudaMalloc(&d, sizeof(h)));
+  struct Free { void* p; ~Free() { cudaFree(p); } } fr{d};
+  RAI_CUDA(cudaMemcpy(d, &h, sizeof(h), cudaMemcpyHostToDevice));
+  RAI_CUDA(rai::launch_sample_accept(d, 1, logits, (int)vocab, temperature, 0));
+  RAI_CUDA(cudaMemcpy(&h, d, sizeof(h), cudaMemcpyDeviceToHost));
+  *n_out = (size_t)h.produced;
+  *accepted = (size_t)h.accepted;
+  for (int i = 0; i < h.produced; ++i) out[i] = h.out[i];
+  return RAI_OK;
+}
+
+int rai_gpu_set_seed(rai_dec* d, uint64_t seed) {
+  if (!d) return fail(RAI_ERR_INVALID, "null argument");
+  d->rng_seed = seed;
+  d->rng_steps = 0;
+  return RAI_OK;
 }
 
 int rai_gpu_kv_filled(const rai_dec* d, size_t layer, size_t* filled) {
