@@ -131,6 +131,14 @@ RAI_API int rai_gpu_step(rai_dec* dec, size_t pos, const uint32_t* ctx, size_t c
                  const rai_lookup_cfg* cfg, uint32_t* out_tokens, size_t out_cap,
                  size_t* n_out, rai_lookup_metrics* metrics);
 
+/* One token without a draft search: the no-match path of
+ * LookupDecoder::step (decode_one, rai-infer/src/lookup.rs:428-454) as its
+ * own call, i.e. plain autoregressive decoding. Runs `last_token` at `pos`
+ * (KV stored there), then samples the next token (temperature > 1e-6, the
+ * decoder's random numbers) or takes the argmax (temperature 0). The cache
+ * is left filled to pos + 1. */
+RAI_API int rai_gpu_decode_one(rai_dec* dec, size_t pos, uint32_t last_token, float temperature, uint32_t* token);
+
 /* Seed of the decoder's random numbers for sampled acceptance
  * (temperature > 1e-6), standing in for the reference's `&mut impl Rng`
  * argument of LookupDecoder::step (rai-infer/src/lookup.rs:260-266); each

@@ -153,6 +153,13 @@ class LookupDecoder:
                                                   out.ctypes.data_as(C.c_void_p)))
         return out
 
+    def decode_one(self, pos: int, last_token: int, temperature: float = 0.0) -> int:
+        """One token with no draft search (plain decoding): runs last_token at
+        pos and returns the next token (argmax at temperature 0)."""
+        tok = C.c_uint32()
+        check(native.lib().rai_gpu_decode_one(self._h, pos, last_token, temperature, C.byref(tok)))
+        return tok.value
+
     def set_seed(self, seed: int) -> None:
         """Seed the random numbers of sampled acceptance (temperature > 0)."""
         check(native.lib().rai_gpu_set_seed(self._h, seed))

@@ -813,10 +813,13 @@ int ensure_graph(Batch* B, const rai_lookup_cfg* cfg) {
 }
 
 // One lookup step for every stream of the batch.
+// lookup = false: no draft search (decode_one), cfg carries only the
+// temperature.
 int step_batch(Batch* B, const size_t* pos, const uint32_t* const* ctx, const size_t* ctx_len,
                const rai_lookup_cfg* cfg, uint32_t* out_tokens, size_t out_cap, size_t* n_out,
-               rai_lookup_metrics* metrics) {
-  if (int rc = validate_cfg(cfg)) return rc;
+               rai_lookup_metrics* metrics, bool lookup = true) {
+  if (lookup)
+    if (int rc = validate_cfg(cfg)) return rc;
   if (out_cap < cfg->max_draft + 1) return fail(RAI_ERR_INVALID, "out_tokens capacity below max_draft + 1");
   if (cfg->temperature > 0.f && B->m->tp_world > 1 && !B->m->ep)
     return fail(RAI_ERR_UNSUPPORTED, "sampled acceptance on a tensor-parallel model (each rank holds a vocabulary slice)");
@@ -1356,6 +1359,23 @@ int rai_gpu_step_many(rai_dec* const* decs, size_t n, const size_t* pos, const u
     g_batches.emplace_back(m, std::move(nb));
   }
   return step_batch(B, pos, ctx, ctx_len, cfg, out_tokens, out_cap, n_out, metrics);
+}
+
+int rai_gpu_decode_one(rai_dec* d, size_t pos, uint32_t last_token, float temperature, uint32_t* token) {
+  if (!d || !token) return fail(RAI_ERR_INVALID, "null argument");
+  if (!std::isfinite(temperature) || (temperature != 0.f && !(temperature > 1e-6f)))
+    return fail(RAI_ERR_INVALID, "decoding requires temperature 0 (greedy) or temperature > 1e-6");
+  if (last_token >= d->m->cfg.vocab_size) return fail(RAI_ERR_INVALID, "token id is out of model vocabulary");
+  DeviceGuard guard(d->m->device);
+  // The step graph with no draft search: one verify row, the bonus token.
+  rai_lookup_cfg cfg = {1, 0, 1, temperature, 0, 1.0f, 1.0f};
+  const uint32_t* ctxs[1] = {&last_token};
+  const size_t len = 1;
+  uint32_t out[2] = {0, 0};
+  size_t n = 0;
+  if (int rc = step_batch(d->solo.get(), &pos, ctxs, &len, &cfg, out, 2, &n, nullptr, false)) return rc;
+  *token = out[0];
+  return RAI_OK;
 }
 
 int rai_gpu_sample_accept(const float* logits, size_t vocab, const uint32_t* draft, size_t n_drafted,

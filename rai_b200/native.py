@@ -81,6 +81,7 @@ def lib() -> C.CDLL:
         L.rai_gpu_step_many.argtypes = [P, SZ, P, P, P, C.POINTER(LookupCfg), P, SZ, P, P]
         L.rai_gpu_kv_filled.argtypes = [P, SZ, PSZ]
         L.rai_gpu_set_seed.argtypes = [P, C.c_uint64]
+        L.rai_gpu_decode_one.argtypes = [P, SZ, C.c_uint32, C.c_float, C.POINTER(C.c_uint32)]
         L.rai_gpu_sample_accept.argtypes = [P, SZ, P, SZ, C.c_float, C.c_uint64, C.c_uint64, P, PSZ, PSZ]
         L.rai_gpu_kv_truncate.argtypes = [P, SZ]
         L.rai_gpu_kv_read.argtypes = [P, SZ, SZ, SZ, P, P]

@@ -209,3 +209,20 @@ def test_prefill_many_matches_separate_prefills(tiny_model_paths, oracle):
                 gk, gv = d.kv_read(layer, 1, pos)
                 ok, ov = od.kv_read(layer, 1, pos)
                 assert np.array_equal(gk, ok) and np.array_equal(gv, ov)
+
+
+@pytest.mark.parametrize("name", ["tiny-llama", "tiny-qwen", "tiny-moe"])
+def test_decode_one_matches_oracle_greedy_decoding(tiny_model_paths, oracle, name):
+    """rai_gpu_decode_one (no draft search) = the oracle's one-row forward and
+    argmax, token after token; the cache watermark follows."""
+    gm, om, gd, od = _open(tiny_model_paths, name, oracle)
+    prompt = periodic_prompt(16, gm.config["vocab_size"], seed=21)
+    pos = gd.prefill(prompt)
+    assert od.prefill(prompt) == pos
+    last = prompt[-1]
+    for _ in range(6):
+        got = gd.decode_one(pos, last)
+        want = oracle.argmax(od.forward_logits([last], pos)[0])
+        assert got == want
+        assert gd.kv_filled(0) == pos + 1
+        last, pos = got, pos + 1

@@ -170,3 +170,20 @@ def test_sampled_step_through_the_decoder(tiny_model_paths, oracle):
         assert met.drafted == dl
         want, acc = _accept(logits, draft, t, seed=s, step=0)
         assert toks == want and met.accepted == acc
+
+
+def test_decode_one_samples_like_the_bonus_rule(tiny_model_paths, oracle):
+    """Sampled decode_one draws what rai_gpu_sample_accept draws (no drafts)
+    for the oracle's logits of that row, with the decoder's seed and step."""
+    import rai_b200
+    gm = rai_b200.RaiModel.load(tiny_model_paths["tiny-llama"])
+    om = oracle.Model.load(tiny_model_paths["tiny-llama"])
+    prompt = periodic_prompt(16, 512, seed=4)
+    gd = rai_b200.LookupDecoder(gm, 128)
+    od = oracle.Decoder(om, 128)
+    pos = gd.prefill(prompt)
+    assert od.prefill(prompt) == pos
+    logits = od.forward_logits([prompt[-1]], pos)
+    for s in range(10):
+        gd.set_seed(s)
+        assert gd.decode_one(pos, prompt[-1], 0.8) == _accept(logits, [], 0.8, seed=s, step=0)[0][0]
