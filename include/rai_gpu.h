@@ -72,6 +72,19 @@ typedef struct {
   float accept_rate;
 } rai_lookup_metrics;
 
+/* SpeculativeConfig (rai-infer/src/speculative.rs): draft tokens per step
+ * and the SamplerConfig fields validate_speculative_config checks
+ * (speculative.rs:396-407). temperature == 0 selects the greedy limit. */
+typedef struct {
+  uint32_t draft_k;     /* >= 1 */
+  float temperature;    /* 0 = greedy, else > 1e-6 */
+  uint32_t top_k;       /* must be 0 */
+  float top_p;          /* must be 1 */
+  float repetition_penalty; /* must be 1 */
+} rai_spec_cfg;
+
+typedef struct rai_spec rai_spec;
+
 /* ModelConfig fields the host loop needs (rai-infer/src/format.rs:162-265). */
 typedef struct {
   uint32_t hidden_size, num_layers, num_heads, num_kv_heads, head_dim;
@@ -146,6 +159,25 @@ RAI_API int rai_gpu_decode_one(rai_dec* dec, size_t pos, uint32_t last_token, fl
  * reference's StdRng, so sampled outputs match the reference in
  * distribution, not token for token. Default seed 0. */
 RAI_API int rai_gpu_set_seed(rai_dec* dec, uint64_t seed);
+
+/* Draft-model speculative decoding (SpeculativeDecoder,
+ * rai-infer/src/speculative.rs): a target and a smaller draft model with one
+ * vocabulary on one device. create = SpeculativeDecoder::new with both KV
+ * caches; prefill runs the prompt (all but the last token) through both;
+ * step (speculative.rs:180-392): the draft proposes k = min(draft_k,
+ * window - pos - 1) tokens one row at a time, the target verifies all k + 1
+ * rows in one forward, the reference's rule accepts (greedy limit at
+ * temperature 0: accept iff the target argmax; sampled: min(1, p_t / p_d),
+ * correction from max(0, p_t - p_d), bonus when all accept, after which the
+ * draft runs its last proposal), and both caches roll back to pos +
+ * produced. metrics: accepted, drafted = k, produced (matched_ngram = 0).
+ * set_seed seeds the sampled draws (Philox, distributional parity). */
+RAI_API int rai_gpu_spec_create(rai_model* target, rai_model* draft, size_t max_ctx, rai_spec** out);
+RAI_API int rai_gpu_spec_destroy(rai_spec* spec);
+RAI_API int rai_gpu_spec_set_seed(rai_spec* spec, uint64_t seed);
+RAI_API int rai_gpu_spec_prefill(rai_spec* spec, const uint32_t* ids, size_t n, size_t* pos_out);
+RAI_API int rai_gpu_spec_step(rai_spec* spec, size_t pos, uint32_t last_token, const rai_spec_cfg* cfg,
+                              uint32_t* out_tokens, size_t out_cap, size_t* n_out, rai_lookup_metrics* metrics);
 
 /* One step for each of n decoders sharing one model and device, batched so
  * their verify rows share every weight read (one forward over
@@ -222,15 +254,17 @@ RAI_API int rai_gpu_attention(const float* q, const float* k, const float* v, co
                               size_t nh, size_t nkv, size_t hd, size_t max_ctx, float scale, float* out,
                               void* stream);
 
-/* The sampled acceptance of one prompt-lookup step (the loop of
- * LookupDecoder::step, rai-infer/src/lookup.rs:359-403) on given verify-row
- * logits: logits [n_drafted + 1][vocab] (device), draft tokens (host),
- * temperature > 1e-6, random numbers of (seed, step) as rai_gpu_step draws
- * them. Writes the produced tokens (host, capacity n_drafted + 1), their
- * count and the accepted count. */
-RAI_API int rai_gpu_sample_accept(const float* logits, size_t vocab, const uint32_t* draft, size_t n_drafted,
-                                  float temperature, uint64_t seed, uint64_t step, uint32_t* out,
-                                  size_t* n_out, size_t* accepted);
+/* The sampled acceptance of one step on given verify-row logits: the loop
+ * of LookupDecoder::step (rai-infer/src/lookup.rs:359-403) when
+ * draft_logits is null (point-mass draft distribution), the loop of
+ * SpeculativeDecoder::step (speculative.rs:300-355) with the draft model's
+ * logits [n_drafted][vocab] otherwise. logits [n_drafted + 1][vocab]
+ * (device), draft tokens (host), temperature > 1e-6, random numbers of
+ * (seed, step) as the decoders draw them. Writes the produced tokens (host,
+ * capacity n_drafted + 1), their count and the accepted count. */
+RAI_API int rai_gpu_sample_accept(const float* logits, const float* draft_logits, size_t vocab,
+                                  const uint32_t* draft, size_t n_drafted, float temperature, uint64_t seed,
+                                  uint64_t step, uint32_t* out, size_t* n_out, size_t* accepted);
 
 /* Number of kernels one rai_gpu_step replays (the captured CUDA graph's
  * kernel nodes for the decoder's current configuration; 0 before the first

@@ -186,6 +186,45 @@ class LookupDecoder:
         return us.value
 
 
+class SpeculativeDecoder:
+    """Draft-model speculative decoding (rai-infer's SpeculativeDecoder): the
+    draft model proposes draft_k tokens, the target verifies them in one
+    batched forward; temperature 0 is the greedy limit."""
+
+    def __init__(self, target: RaiModel, draft: RaiModel, max_ctx: int):
+        self.target, self.draft = target, draft
+        h = C.c_void_p()
+        check(native.lib().rai_gpu_spec_create(target._h, draft._h, max_ctx, C.byref(h)))
+        self._h = h
+
+    def close(self) -> None:
+        if getattr(self, "_h", None):
+            native.lib().rai_gpu_spec_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        self.close()
+
+    def set_seed(self, seed: int) -> None:
+        check(native.lib().rai_gpu_spec_set_seed(self._h, seed))
+
+    def prefill(self, prompt_tokens: Sequence[int]) -> int:
+        ids = _u32(prompt_tokens)
+        pos = C.c_size_t()
+        check(native.lib().rai_gpu_spec_prefill(self._h, ids.ctypes.data_as(C.c_void_p), ids.size, C.byref(pos)))
+        return pos.value
+
+    def step(self, pos: int, last_token: int, draft_k: int, temperature: float = 0.0):
+        cap = draft_k + 1
+        out = np.zeros(cap, np.uint32)
+        n = C.c_size_t()
+        met = native.LookupMetricsC()
+        cfg = native.SpecCfg(draft_k, temperature, 0, 1.0, 1.0)
+        check(native.lib().rai_gpu_spec_step(self._h, pos, last_token, C.byref(cfg), out.ctypes.data_as(C.c_void_p),
+                                             cap, C.byref(n), C.byref(met)))
+        return [int(t) for t in out[: n.value]], LookupMetrics._from_c(met)
+
+
 def prefill_many(decoders: Sequence[LookupDecoder], prompts: Sequence[Sequence[int]]):
     """LookupDecoder.prefill for each decoder, batched (rai_gpu_prefill_many)."""
     n = len(decoders)
@@ -218,4 +257,5 @@ def step_many(decoders: Sequence[LookupDecoder], positions: Sequence[int], conte
             [LookupMetrics._from_c(mets[i]) for i in range(n)])
 
 
-__all__ = ["RaiModel", "LookupDecoder", "LookupConfig", "LookupMetrics", "RaiError", "step_many", "prefill_many"]
+__all__ = ["RaiModel", "LookupDecoder", "LookupConfig", "LookupMetrics", "RaiError", "SpeculativeDecoder",
+           "step_many", "prefill_many"]

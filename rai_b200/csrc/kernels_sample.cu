@@ -127,18 +127,16 @@ __device__ RowSoftmax row_softmax(const float* row, int V, float t, bool mul, fl
   return r;
 }
 
-// Inverse-CDF search over q(j) = p(j) (j != excl): the first j whose
-// cumulative f64 sum reaches `target` (strict: exceeds it). Each thread owns
-// a contiguous chunk; chunk sums are scanned across the block. Returns -1
-// when no index qualifies (rounding at the end of the range).
-__device__ int cdf_search(const float* row, const RowSoftmax& sm, int excl, double target, bool strict, double* redd,
-                          int* res) {
-  const int V = sm.V;
+// Inverse-CDF search over weights q(j): the first j whose cumulative f64
+// sum reaches `target` (strict: exceeds it). Each thread owns a contiguous
+// chunk; chunk sums are scanned across the block. Returns -1 when no index
+// qualifies (rounding at the end of the range).
+template <class Q>
+__device__ int cdf_search(int V, Q q, double target, bool strict, double* redd, int* res) {
   const int chunk = (V + blockDim.x - 1) / blockDim.x;
   const int j0 = min(V, (int)threadIdx.x * chunk), j1 = min(V, j0 + chunk);
   double mine = 0.0;
-  for (int j = j0; j < j1; ++j)
-    if (j != excl) mine += (double)sm.p(row, j);
+  for (int j = j0; j < j1; ++j) mine += (double)q(j);
   // Exclusive scan of the chunk sums in thread order.
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   double incl = mine;
@@ -155,8 +153,7 @@ __device__ int cdf_search(const float* row, const RowSoftmax& sm, int excl, doub
   double cum = base + incl - mine;  // sum of every earlier chunk
   if (j0 < j1 && (strict ? base + incl > target : base + incl >= target) && !(strict ? cum > target : cum >= target)) {
     for (int j = j0; j < j1; ++j) {
-      if (j == excl) continue;
-      cum += (double)sm.p(row, j);
+      cum += (double)q(j);
       if (strict ? cum > target : cum >= target) {
         atomicMin(res, j);  // the first chunk that qualifies holds the answer
         break;
@@ -168,9 +165,12 @@ __device__ int cdf_search(const float* row, const RowSoftmax& sm, int excl, doub
   return found == 0x7fffffff ? -1 : found;
 }
 
+// draft_logits (optional): the draft model's logits of each draft row
+// (speculative decoding, speculative.rs:300-355); without them the draft
+// distribution is the point mass of prompt lookup (lookup.rs:362-366).
 __global__ void __launch_bounds__(kSampleThreads) sample_accept_kernel(StreamStep* st_all,
                                                                        const float* __restrict__ logits, int V,
-                                                                       float t) {
+                                                                       float t, const float* __restrict__ draft_logits) {
   pdl_wait_prior();
   pdl_launch_dependents();
   __shared__ float redf[32];
@@ -186,7 +186,14 @@ __global__ void __launch_bounds__(kSampleThreads) sample_accept_kernel(StreamSte
     const int d = (int)st->tokens[1 + i];
     const RowSoftmax sm = row_softmax(row, V, t, false, redf, redi);
     const float p_target = sm.p(row, d);
-    const float accept_prob = fminf(p_target, 1.0f);  // p_draft = 1 (point mass)
+    const float* drow = draft_logits ? draft_logits + (size_t)i * V : nullptr;
+    RowSoftmax dsm;
+    float p_draft = 1.0f;  // point mass at d
+    if (drow) {
+      dsm = row_softmax(drow, V, t, false, redf, redi);
+      p_draft = dsm.p(drow, d);
+    }
+    const float accept_prob = p_draft > 0.f ? fminf(__fdiv_rn(p_target, p_draft), 1.0f) : (p_target > 0.f ? 1.0f : 0.0f);
     const float u = uniform_f32(*st, draw++);
     if (u < accept_prob) {
       if (threadIdx.x == 0) st->out[produced] = (uint32_t)d;
@@ -194,21 +201,24 @@ __global__ void __launch_bounds__(kSampleThreads) sample_accept_kernel(StreamSte
       ++accepted;
       continue;
     }
-    // Correction from p_target without d (adjusted = max(0, p - onehot)).
+    // Correction from max(0, p_target - p_draft) (sample_correction).
+    auto q = [&](int j) -> float {
+      const float pd = drow ? dsm.p(drow, j) : (j == d ? 1.0f : 0.0f);
+      return fmaxf(__fsub_rn(sm.p(row, j), pd), 0.0f);
+    };
     double adj = 0.0;
-    for (int j = threadIdx.x; j < V; j += blockDim.x)
-      if (j != d) adj += (double)sm.p(row, j);
+    for (int j = threadIdx.x; j < V; j += blockDim.x) adj += (double)q(j);
     const double adj_sum = block_reduce(adj, [](double a, double b) { return a + b; }, redd);
     int tok;
     if (!isfinite(adj_sum) || adj_sum <= 0.0) {
       // Degenerate residual: sample_token on the target row.
       const RowSoftmax s2 = row_softmax(row, V, t, true, redf, redi);
       const float r = uniform_f32(*st, draw++);
-      tok = cdf_search(row, s2, -1, (double)r, true, redd, &res);
+      tok = cdf_search(V, [&](int j) { return s2.p(row, j); }, (double)r, true, redd, &res);
       if (tok < 0) tok = V - 1;
     } else {
       const double target = uniform_f64(*st, draw++) * adj_sum;
-      tok = cdf_search(row, sm, d, target, false, redd, &res);
+      tok = cdf_search(V, q, target, false, redd, &res);
       if (tok < 0) tok = V - 1;
     }
     if (threadIdx.x == 0) st->out[produced] = (uint32_t)tok;
@@ -219,7 +229,7 @@ __global__ void __launch_bounds__(kSampleThreads) sample_accept_kernel(StreamSte
     const float* row = logits + (size_t)(r0 + dl) * V;
     const RowSoftmax sm = row_softmax(row, V, t, true, redf, redi);
     const float r = uniform_f32(*st, draw++);
-    int tok = cdf_search(row, sm, -1, (double)r, true, redd, &res);
+    int tok = cdf_search(V, [&](int j) { return sm.p(row, j); }, (double)r, true, redd, &res);
     if (tok < 0) {
       // Fallback of sample_token: the highest probability (last index on ties).
       float best = -1.f;
@@ -242,8 +252,9 @@ __global__ void __launch_bounds__(kSampleThreads) sample_accept_kernel(StreamSte
 }  // namespace
 
 cudaError_t launch_sample_accept(StreamStep* st, int n, const float* logits, int vocab, float temperature,
-                                 cudaStream_t s) {
-  return launch_pdl(sample_accept_kernel, dim3(n), dim3(kSampleThreads), 0, s, st, logits, vocab, temperature);
+                                 cudaStream_t s, const float* draft_logits) {
+  return launch_pdl(sample_accept_kernel, dim3(n), dim3(kSampleThreads), 0, s, st, logits, vocab, temperature,
+                    draft_logits);
 }
 
 }  // namespace rai

@@ -105,8 +105,10 @@ cudaError_t launch_plan(StreamStep* st, int n, RowInfo* rows, uint32_t* ids, int
 // Sampled acceptance (temperature > 0) of every stream from its verify rows'
 // logits (vocab wide): accept / correction / bonus tokens and counts, as
 // launch_accept does for greedy.
+// draft_logits (optional, one stream): the draft model's logits per draft
+// row for speculative decoding; null = the point mass of prompt lookup.
 cudaError_t launch_sample_accept(StreamStep* st, int n, const float* logits, int vocab, float temperature,
-                                 cudaStream_t s);
+                                 cudaStream_t s, const float* draft_logits = nullptr);
 // With tp (world > 1) and slot >= 0, best[] is awaited as exchange `slot`.
 cudaError_t launch_accept(StreamStep* st, int n, const unsigned long long* best, cudaStream_t s,
                           const TpLink* tp = nullptr, int slot = -1, uint32_t* err = nullptr);

@@ -443,6 +443,21 @@ Batch::~Batch() {
   cudaSetDevice(prev);
 }
 
+// Draft-model speculative decoder (rai-infer/src/speculative.rs): a target
+// and a draft decoder on one device, plus the acceptance state.
+struct rai_spec {
+  rai_dec* td = nullptr;  // target
+  rai_dec* dd = nullptr;  // draft
+  int max_ctx = 0;
+  int vocab = 0;
+  float* draft_logits = nullptr;      // [kMaxRowsPerStream][vocab]
+  rai::StreamStep* st = nullptr;      // one stream's step state
+  unsigned long long* best = nullptr; // [kMaxRowsPerStream] argmax keys (greedy)
+  rai::StreamStep* st_host = nullptr;
+  uint64_t seed = 0, steps = 0;
+  ~rai_spec();
+};
+
 namespace {
 
 // Cached multi-stream batches per model (keyed by the decoder list).
@@ -906,6 +921,21 @@ int forward_solo(rai_dec* d, const uint32_t* ids, size_t start, int rows, bool l
 
 }  // namespace
 
+rai_spec::~rai_spec() {
+  if (td) {
+    int prev = 0;
+    cudaGetDevice(&prev);
+    cudaSetDevice(td->m->device);
+    if (draft_logits) cudaFree(draft_logits);
+    if (st) cudaFree(st);
+    if (best) cudaFree(best);
+    if (st_host) cudaFreeHost(st_host);
+    cudaSetDevice(prev);
+  }
+  delete dd;
+  delete td;
+}
+
 rai_dec::~rai_dec() {
   drop_batches_of(this);
   solo.reset();
@@ -1361,6 +1391,138 @@ int rai_gpu_step_many(rai_dec* const* decs, size_t n, const size_t* pos, const u
   return step_batch(B, pos, ctx, ctx_len, cfg, out_tokens, out_cap, n_out, metrics);
 }
 
+int rai_gpu_spec_create(rai_model* target, rai_model* draft, size_t max_ctx, rai_spec** out) {
+  if (!target || !draft || !out) return fail(RAI_ERR_INVALID, "null argument");
+  *out = nullptr;
+  if (target->device != draft->device) return fail(RAI_ERR_INVALID, "target and draft models must share a device");
+  if (target->cfg.vocab_size != draft->cfg.vocab_size)
+    return fail(RAI_ERR_INVALID, "target and draft models must share a vocabulary");
+  if (target->tp_world > 1 || draft->tp_world > 1)
+    return fail(RAI_ERR_UNSUPPORTED, "speculative decoding on multi-GPU models");
+  auto S = std::make_unique<rai_spec>();
+  if (int rc = rai_gpu_decoder_create(target, max_ctx, &S->td)) return rc;
+  if (int rc = rai_gpu_decoder_create(draft, max_ctx, &S->dd)) return rc;
+  S->max_ctx = std::min(S->td->max_ctx, S->dd->max_ctx);
+  S->vocab = (int)target->cfg.vocab_size;
+  DeviceGuard guard(target->device);
+  RAI_CUDA(cudaMalloc(&S->draft_logits, (size_t)rai::kMaxRowsPerStream * S->vocab * 4));
+  RAI_CUDA(cudaMalloc(&S->st, sizeof(rai::StreamStep)));
+  RAI_CUDA(cudaMalloc(&S->best, rai::kMaxRowsPerStream * 8));
+  RAI_CUDA(cudaMallocHost(&S->st_host, sizeof(rai::StreamStep)));
+  *out = S.release();
+  return RAI_OK;
+}
+
+int rai_gpu_spec_destroy(rai_spec* s) {
+  delete s;
+  return RAI_OK;
+}
+
+int rai_gpu_spec_set_seed(rai_spec* s, uint64_t seed) {
+  if (!s) return fail(RAI_ERR_INVALID, "null argument");
+  s->seed = seed;
+  s->steps = 0;
+  // The draft model's sampling draws from its own stream of the same seed.
+  rai_gpu_set_seed(s->dd, seed ^ 0x9E3779B97F4A7C15ull);
+  rai_gpu_set_seed(s->td, seed ^ 0xBB67AE8584CAA73Bull);
+  return RAI_OK;
+}
+
+int rai_gpu_spec_prefill(rai_spec* s, const uint32_t* ids, size_t n, size_t* pos_out) {
+  if (!s || !pos_out) return fail(RAI_ERR_INVALID, "null argument");
+  size_t p2 = 0;
+  if (int rc = rai_gpu_prefill(s->td, ids, n, pos_out)) return rc;
+  return rai_gpu_prefill(s->dd, ids, n, &p2);
+}
+
+int rai_gpu_spec_step(rai_spec* s, size_t pos, uint32_t last_token, const rai_spec_cfg* cfg, uint32_t* out,
+                      size_t out_cap, size_t* n_out, rai_lookup_metrics* metrics) {
+  if (!s || !cfg || !out || !n_out) return fail(RAI_ERR_INVALID, "null argument");
+  // validate_speculative_config (speculative.rs:396-407); temperature 0 is
+  // the greedy limit (an extension, as for prompt lookup).
+  if (cfg->draft_k == 0) return fail(RAI_ERR_INVALID, "speculative draft_k must be non-zero");
+  if (cfg->draft_k + 1 > (uint32_t)rai::kMaxRowsPerStream) return fail(RAI_ERR_INVALID, "draft_k exceeds 32");
+  const float t = cfg->temperature;
+  if (!std::isfinite(t) || (t != 0.f && !(t > 1e-6f)))
+    return fail(RAI_ERR_INVALID, "speculative decoding requires temperature 0 (greedy) or a finite temperature > 1e-6");
+  if (cfg->top_k != 0 || cfg->top_p != 1.0f || cfg->repetition_penalty != 1.0f)
+    return fail(RAI_ERR_INVALID, "speculative decoding requires top_k=0, top_p=1, and repetition_penalty=1");
+  if (pos >= (size_t)s->max_ctx) return fail(RAI_ERR_INVALID, "decode position exceeds the speculative context window");
+  if ((int)last_token >= s->vocab) return fail(RAI_ERR_INVALID, "token id is out of model vocabulary");
+  if (pos > s->td->filled[0] || pos > s->dd->filled[0]) return fail(RAI_ERR_INVALID, "KV store would leave a gap");
+  const size_t k = std::min<size_t>(cfg->draft_k, (size_t)s->max_ctx - pos - 1);
+  if (out_cap < k + 1) return fail(RAI_ERR_INVALID, "out_tokens capacity below draft_k + 1");
+  DeviceGuard guard(s->td->m->device);
+  if (k == 0) {
+    uint32_t tok = 0;
+    if (int rc = rai_gpu_decode_one(s->td, pos, last_token, t, &tok)) return rc;
+    out[0] = tok;
+    *n_out = 1;
+    if (metrics) *metrics = rai_lookup_metrics{0, 0, 1, 0, 0.f};
+    ++s->steps;
+    return RAI_OK;
+  }
+  // Phase 1: the draft model proposes k tokens one row at a time; each row's
+  // logits are kept for the acceptance.
+  Batch* DB = s->dd->solo.get();
+  std::vector<uint32_t> ids(k + 1);
+  ids[0] = last_token;
+  uint32_t cur = last_token;
+  for (size_t i = 0; i < k; ++i) {
+    uint32_t next = 0;
+    if (int rc = rai_gpu_decode_one(s->dd, pos + i, cur, t, &next)) return rc;
+    RAI_CUDA(cudaMemcpyAsync(s->draft_logits + i * s->vocab, DB->logits, (size_t)s->vocab * 4,
+                             cudaMemcpyDeviceToDevice, DB->stream));
+    ids[i + 1] = next;
+    cur = next;
+  }
+  RAI_CUDA(cudaStreamSynchronize(DB->stream));
+  // Phase 2: the target verifies all k + 1 rows in one forward.
+  Batch* TB = s->td->solo.get();
+  if (int rc = forward_solo(s->td, ids.data(), pos, (int)k + 1, true)) return rc;
+  for (auto& f : s->td->filled) f = std::max(f, pos + k + 1);
+  // Phase 3: accept / reject.
+  rai::StreamStep& h = *s->st_host;
+  std::memset(&h, 0, sizeof(h));
+  h.pos = (int)pos;
+  h.drafted = (int)k;
+  h.n_rows = (int)k + 1;
+  h.row0 = 0;
+  for (size_t i = 0; i <= k; ++i) h.tokens[i] = ids[i];
+  h.rng_seed_lo = (uint32_t)s->seed;
+  h.rng_seed_hi = (uint32_t)(s->seed >> 32);
+  h.rng_step_lo = (uint32_t)s->steps;
+  h.rng_step_hi = (uint32_t)(s->steps >> 32);
+  cudaStream_t st = TB->stream;
+  RAI_CUDA(cudaMemcpyAsync(s->st, &h, sizeof(h), cudaMemcpyHostToDevice, st));
+  if (t > 0.f) {
+    RAI_CUDA(rai::launch_sample_accept(s->st, 1, TB->logits, s->vocab, t, st, s->draft_logits));
+  } else {
+    RAI_CUDA(cudaMemsetAsync(s->best, 0, (k + 1) * 8, st));
+    RAI_CUDA(rai::launch_argmax(TB->logits, s->vocab, nullptr, (int)k + 1, s->best, st));
+    RAI_CUDA(rai::launch_accept(s->st, 1, s->best, st));
+  }
+  RAI_CUDA(cudaMemcpyAsync(&h, s->st, sizeof(h), cudaMemcpyDeviceToHost, st));
+  if (int rc = check_err(s->td->m, st)) return rc;
+  const size_t produced = (size_t)h.produced;
+  if ((size_t)h.accepted == k) {
+    // Every draft accepted: the draft model has not yet run its last
+    // proposal; run it so its cache has no missing position.
+    if (int rc = forward_solo(s->dd, &ids[k], pos + k, 1, false)) return rc;
+    if (int rc = check_err(s->dd->m, DB->stream)) return rc;
+  }
+  // Roll both caches back to the produced frontier.
+  for (auto& f : s->td->filled) f = pos + produced;
+  for (auto& f : s->dd->filled) f = pos + produced;
+  for (size_t i = 0; i < produced; ++i) out[i] = h.out[i];
+  *n_out = produced;
+  if (metrics)
+    *metrics = rai_lookup_metrics{(uint32_t)h.accepted, (uint32_t)k, (uint32_t)produced, 0,
+                                  (float)h.accepted / (float)k};
+  ++s->steps;
+  return RAI_OK;
+}
+
 int rai_gpu_decode_one(rai_dec* d, size_t pos, uint32_t last_token, float temperature, uint32_t* token) {
   if (!d || !token) return fail(RAI_ERR_INVALID, "null argument");
   if (!std::isfinite(temperature) || (temperature != 0.f && !(temperature > 1e-6f)))
@@ -1378,9 +1540,9 @@ int rai_gpu_decode_one(rai_dec* d, size_t pos, uint32_t last_token, float temper
   return RAI_OK;
 }
 
-int rai_gpu_sample_accept(const float* logits, size_t vocab, const uint32_t* draft, size_t n_drafted,
-                          float temperature, uint64_t seed, uint64_t step, uint32_t* out, size_t* n_out,
-                          size_t* accepted) {
+int rai_gpu_sample_accept(const float* logits, const float* draft_logits, size_t vocab, const uint32_t* draft,
+                          size_t n_drafted, float temperature, uint64_t seed, uint64_t step, uint32_t* out,
+                          size_t* n_out, size_t* accepted) {
   if (!logits || !out || !n_out || !accepted || (n_drafted && !draft) || vocab == 0)
     return fail(RAI_ERR_INVALID, "null argument");
   if (n_drafted + 1 > (size_t)rai::kMaxRowsPerStream) return fail(RAI_ERR_INVALID, "more than 32 drafts");
@@ -1399,7 +1561,7 @@ int rai_gpu_sample_accept(const float* logits, size_t vocab, const uint32_t* dra
   RAI_CUDA(cudaMalloc(&d, sizeof(h)));
   struct Free { void* p; ~Free() { cudaFree(p); } } fr{d};
   RAI_CUDA(cudaMemcpy(d, &h, sizeof(h), cudaMemcpyHostToDevice));
-  RAI_CUDA(rai::launch_sample_accept(d, 1, logits, (int)vocab, temperature, 0));
+  RAI_CUDA(rai::launch_sample_accept(d, 1, logits, (int)vocab, temperature, 0, draft_logits));
   RAI_CUDA(cudaMemcpy(&h, d, sizeof(h), cudaMemcpyDeviceToHost));
   *n_out = (size_t)h.produced;
   *accepted = (size_t)h.accepted;

@@ -42,6 +42,11 @@ class LookupCfg(C.Structure):
                 ("repetition_penalty", C.c_float)]
 
 
+class SpecCfg(C.Structure):
+    _fields_ = [("draft_k", C.c_uint32), ("temperature", C.c_float), ("top_k", C.c_uint32), ("top_p", C.c_float),
+                ("repetition_penalty", C.c_float)]
+
+
 class LookupMetricsC(C.Structure):
     _fields_ = [("accepted", C.c_uint32), ("drafted", C.c_uint32), ("produced", C.c_uint32),
                 ("matched_ngram", C.c_uint32), ("accept_rate", C.c_float)]
@@ -81,8 +86,13 @@ def lib() -> C.CDLL:
         L.rai_gpu_step_many.argtypes = [P, SZ, P, P, P, C.POINTER(LookupCfg), P, SZ, P, P]
         L.rai_gpu_kv_filled.argtypes = [P, SZ, PSZ]
         L.rai_gpu_set_seed.argtypes = [P, C.c_uint64]
+        L.rai_gpu_spec_create.argtypes = [P, P, SZ, C.POINTER(P)]
+        L.rai_gpu_spec_destroy.argtypes = [P]
+        L.rai_gpu_spec_set_seed.argtypes = [P, C.c_uint64]
+        L.rai_gpu_spec_prefill.argtypes = [P, P, SZ, PSZ]
+        L.rai_gpu_spec_step.argtypes = [P, SZ, C.c_uint32, C.POINTER(SpecCfg), P, SZ, PSZ, C.POINTER(LookupMetricsC)]
         L.rai_gpu_decode_one.argtypes = [P, SZ, C.c_uint32, C.c_float, C.POINTER(C.c_uint32)]
-        L.rai_gpu_sample_accept.argtypes = [P, SZ, P, SZ, C.c_float, C.c_uint64, C.c_uint64, P, PSZ, PSZ]
+        L.rai_gpu_sample_accept.argtypes = [P, P, SZ, P, SZ, C.c_float, C.c_uint64, C.c_uint64, P, PSZ, PSZ]
         L.rai_gpu_kv_truncate.argtypes = [P, SZ]
         L.rai_gpu_kv_read.argtypes = [P, SZ, SZ, SZ, P, P]
         L.rai_gpu_forward_logits.argtypes = [P, P, SZ, SZ, P]

@@ -79,8 +79,8 @@ def _accept(logits, draft, t, seed, step=0):
     d = np.ascontiguousarray(draft, np.uint32)
     out = np.zeros(len(draft) + 1, np.uint32)
     n, acc = C.c_size_t(), C.c_size_t()
-    native.check(L.rai_gpu_sample_accept(lg.data_ptr(), logits.shape[1], d.ctypes.data if d.size else None, d.size,
-                                         t, seed, step, out.ctypes.data, C.byref(n), C.byref(acc)))
+    native.check(L.rai_gpu_sample_accept(lg.data_ptr(), None, logits.shape[1], d.ctypes.data if d.size else None,
+                                         d.size, t, seed, step, out.ctypes.data, C.byref(n), C.byref(acc)))
     return [int(v) for v in out[: n.value]], acc.value
 
 
