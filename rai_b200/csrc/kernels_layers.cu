@@ -27,6 +27,8 @@ namespace rai {
 __device__ __forceinline__ int active_rows(const int* m_dev, int M) { return m_dev ? *m_dev : M; }
 
 constexpr int kPvMaxStages = 4;
+constexpr int kPvStepHeads = 2;  // heads per P.V thread for short segments
+constexpr int kPvStepRows = 4;   // ... of at most this many rows
 
 // ---------------------------------------------------------------------------
 __global__ void embed_kernel(const uint32_t* __restrict__ ids, const int* m_dev, int M,
@@ -316,10 +318,13 @@ __global__ void __launch_bounds__(256) attn_softmax_kernel(const RowInfo* __rest
 }
 
 // Step 3: out[row][h][d] = fma(p_t, v_t[d], out) over t in order. CTA
-// (kv head, segment); thread (d pair, head) carries the 2 chains of its dims
-// for each of the segment's rows (RB >= nrows) in registers: one p load
-// (4 positions) feeds 2 dims, one V load (2 dims) feeds RB rows; positions
-// are taken 8 at a time with all loads issued before the FMAs. V and p tiles
+// (kv head, segment); thread (d pair, group of HPT heads) carries the 2
+// chains of its dims for each of its heads and each of the segment's rows
+// (RB >= nrows) in registers: one p load (4 positions) feeds 2 dims, one V
+// load (2 dims) feeds RB rows x HPT heads, so the V tile is read from shared
+// memory hpk / HPT times (HPT > 1 for short segments, where those V reads
+// would otherwise bound the kernel); positions are taken 8 at a time with
+// all loads issued before the FMAs. V and p tiles
 // stream through a ring of `ns` shared-memory stages filled by bulk copies
 // (warp 0) that complete on mbarriers. Row r only takes positions
 // t <= pos0 + r.
@@ -331,7 +336,7 @@ struct PvCfg {
 // The stage ring persists across the segments a CTA handles: `head` is the
 // next stage to consume (stages fill in the same order) and bit s of `bits`
 // is the parity stage s's next fill completes.
-template <int HD, int RB>
+template <int HD, int RB, int HPT>
 __device__ __forceinline__ bool pv_body(const float* __restrict__ vbase, const float* __restrict__ p, int nh,
                                         int hpk, int kvh, const AttnSeg& sg, int n_alloc, int rb_alloc, int ns,
                                         float* __restrict__ out, float* sm, uint64_t* bars, uint32_t* err,
@@ -340,9 +345,12 @@ __device__ __forceinline__ bool pv_body(const float* __restrict__ vbase, const f
   constexpr int NDP = HD / 2;
   const int stage_floats = VT * HD + rb_alloc * hpk * VT;
   const int tid = threadIdx.x, lane = tid & 31;
-  const int dp = tid % NDP, h = tid / NDP;
+  const int dp = tid % NDP, h0 = (tid / NDP) * HPT;
   const int d0 = 2 * dp;
-  const bool active = h < hpk;
+  const bool active = h0 < hpk;
+  bool hv[HPT];  // head h0 + j exists (hpk need not be a multiple of HPT)
+#pragma unroll
+  for (int j = 0; j < HPT; ++j) hv[j] = h0 + j < hpk;
   const int nrows = sg.nrows;
   const int n_max = sg.pos0 + nrows, n_all = sg.pos0 + 1;
   const int ntiles = (n_max + VT - 1) / VT;
@@ -369,9 +377,11 @@ __device__ __forceinline__ bool pv_body(const float* __restrict__ vbase, const f
       if (++f == ns) f = 0;
     }
   }
-  float acc[RB][2];
+  float acc[RB][HPT][2];
 #pragma unroll
-  for (int r = 0; r < RB; ++r) acc[r][0] = acc[r][1] = 0.f;
+  for (int r = 0; r < RB; ++r)
+#pragma unroll
+    for (int j = 0; j < HPT; ++j) acc[r][j][0] = acc[r][j][1] = 0.f;
   int tile = 0;
   for (; tile < ntiles; ++tile) {
     const int st = head;
@@ -381,7 +391,8 @@ __device__ __forceinline__ bool pv_body(const float* __restrict__ vbase, const f
     if (!__syncthreads_and(ok)) break;
     const int t0 = tile * VT, cnt = min(VT, n_max - t0);
     const float* sv = sm + (size_t)st * stage_floats + d0;
-    const float* ph = sm + (size_t)st * stage_floats + VT * HD + (active ? h : 0) * VT;
+    // p of (row r, head h0 + j) at ph + (r * hpk + j) * VT.
+    const float* ph = sm + (size_t)st * stage_floats + VT * HD + (active ? h0 : 0) * VT;
     if (active) {
       if (t0 + cnt <= n_all) {
         // Every row sees the whole tile.
@@ -392,14 +403,18 @@ __device__ __forceinline__ bool pv_body(const float* __restrict__ vbase, const f
           for (int u = 0; u < 8; ++u) v[u] = *reinterpret_cast<const float2*>(sv + (t + u) * HD);
 #pragma unroll
           for (int r = 0; r < RB; ++r) {
-            if (r < nrows) {
-              const float4 pa = *reinterpret_cast<const float4*>(ph + r * hpk * VT + t);
-              const float4 pb = *reinterpret_cast<const float4*>(ph + r * hpk * VT + t + 4);
-              const float p8[8] = {pa.x, pa.y, pa.z, pa.w, pb.x, pb.y, pb.z, pb.w};
 #pragma unroll
-              for (int u = 0; u < 8; ++u) {
-                acc[r][0] = __fmaf_rn(p8[u], v[u].x, acc[r][0]);
-                acc[r][1] = __fmaf_rn(p8[u], v[u].y, acc[r][1]);
+            for (int j = 0; j < HPT; ++j) {
+              if (r < nrows && hv[j]) {
+                const float* pj = ph + (r * hpk + j) * VT + t;
+                const float4 pa = *reinterpret_cast<const float4*>(pj);
+                const float4 pb = *reinterpret_cast<const float4*>(pj + 4);
+                const float p8[8] = {pa.x, pa.y, pa.z, pa.w, pb.x, pb.y, pb.z, pb.w};
+#pragma unroll
+                for (int u = 0; u < 8; ++u) {
+                  acc[r][j][0] = __fmaf_rn(p8[u], v[u].x, acc[r][j][0]);
+                  acc[r][j][1] = __fmaf_rn(p8[u], v[u].y, acc[r][j][1]);
+                }
               }
             }
           }
@@ -408,10 +423,13 @@ __device__ __forceinline__ bool pv_body(const float* __restrict__ vbase, const f
           const float2 v = *reinterpret_cast<const float2*>(sv + t * HD);
 #pragma unroll
           for (int r = 0; r < RB; ++r) {
-            if (r < nrows) {
-              const float a = ph[r * hpk * VT + t];
-              acc[r][0] = __fmaf_rn(a, v.x, acc[r][0]);
-              acc[r][1] = __fmaf_rn(a, v.y, acc[r][1]);
+#pragma unroll
+            for (int j = 0; j < HPT; ++j) {
+              if (r < nrows && hv[j]) {
+                const float a = ph[(r * hpk + j) * VT + t];
+                acc[r][j][0] = __fmaf_rn(a, v.x, acc[r][j][0]);
+                acc[r][j][1] = __fmaf_rn(a, v.y, acc[r][j][1]);
+              }
             }
           }
         }
@@ -421,10 +439,13 @@ __device__ __forceinline__ bool pv_body(const float* __restrict__ vbase, const f
           const int rmin = t0 + t - sg.pos0;  // rows r >= rmin see position t0 + t
 #pragma unroll
           for (int r = 0; r < RB; ++r) {
-            if (r < nrows && r >= rmin) {
-              const float a = ph[r * hpk * VT + t];
-              acc[r][0] = __fmaf_rn(a, v.x, acc[r][0]);
-              acc[r][1] = __fmaf_rn(a, v.y, acc[r][1]);
+#pragma unroll
+            for (int j = 0; j < HPT; ++j) {
+              if (r < nrows && r >= rmin && hv[j]) {
+                const float a = ph[(r * hpk + j) * VT + t];
+                acc[r][j][0] = __fmaf_rn(a, v.x, acc[r][j][0]);
+                acc[r][j][1] = __fmaf_rn(a, v.y, acc[r][j][1]);
+              }
             }
           }
         }
@@ -451,14 +472,18 @@ __device__ __forceinline__ bool pv_body(const float* __restrict__ vbase, const f
   if (active) {
 #pragma unroll
     for (int r = 0; r < RB; ++r)
-      if (r < nrows)
-        *reinterpret_cast<float2*>(out + (size_t)(sg.row0 + r) * nh * HD + (size_t)(kvh * hpk + h) * HD + d0) =
-            make_float2(acc[r][0], acc[r][1]);
+#pragma unroll
+      for (int j = 0; j < HPT; ++j)
+        if (r < nrows && hv[j])
+          *reinterpret_cast<float2*>(out + (size_t)(sg.row0 + r) * nh * HD + (size_t)(kvh * hpk + h0 + j) * HD +
+                                     d0) = make_float2(acc[r][j][0], acc[r][j][1]);
   }
   return true;
 }
 
-template <int HD>
+// HPT > 1 serves segments of at most kPvStepRows rows (the launch
+// guarantees it).
+template <int HD, int HPT>
 __global__ void __launch_bounds__(512) attn_pv_kernel(const StreamKV* __restrict__ kv, int layer,
                                                       const AttnSeg* __restrict__ segs, const int* nseg_dev,
                                                       int nseg_max, int nh, int nkv, const float* __restrict__ p,
@@ -484,11 +509,18 @@ __global__ void __launch_bounds__(512) attn_pv_kernel(const StreamKV* __restrict
     const StreamKV sk_ = kv[sg.stream];
     const float* vbase = sk_.v + ((size_t)layer * nkv + kvh) * sk_.max_ctx * HD;
     bool ok;
-    if (sg.nrows <= 1) ok = pv_body<HD, 1>(vbase, p, nh, hpk, kvh, sg, n_alloc, rb_alloc, ns, out, sm, bars, err, head, bits);
-    else if (sg.nrows <= 2) ok = pv_body<HD, 2>(vbase, p, nh, hpk, kvh, sg, n_alloc, rb_alloc, ns, out, sm, bars, err, head, bits);
-    else if (sg.nrows <= 4) ok = pv_body<HD, 4>(vbase, p, nh, hpk, kvh, sg, n_alloc, rb_alloc, ns, out, sm, bars, err, head, bits);
-    else if (sg.nrows <= 8) ok = pv_body<HD, 8>(vbase, p, nh, hpk, kvh, sg, n_alloc, rb_alloc, ns, out, sm, bars, err, head, bits);
-    else ok = pv_body<HD, kSegRows>(vbase, p, nh, hpk, kvh, sg, n_alloc, rb_alloc, ns, out, sm, bars, err, head, bits);
+#define RAI_PV(RB) pv_body<HD, RB, HPT>(vbase, p, nh, hpk, kvh, sg, n_alloc, rb_alloc, ns, out, sm, bars, err, head, bits)
+    if (sg.nrows <= 1) ok = RAI_PV(1);
+    else if (sg.nrows <= 2) ok = RAI_PV(2);
+    else if (sg.nrows <= 4) ok = RAI_PV(4);
+    else if constexpr (HPT == 1) {
+      if (sg.nrows <= 8) ok = RAI_PV(8);
+      else ok = RAI_PV(kSegRows);
+    } else {
+      ok = false;
+      if (threadIdx.x == 0) atomicOr(err, kErrBadInput);
+    }
+#undef RAI_PV
     if (!ok) return;
     __syncthreads();  // the stages are refilled for the next segment
   }
@@ -701,7 +733,14 @@ size_t pv_stage_bytes(int hd, int hpk, int rb_alloc) {
   const int vt = hd >= 128 ? 32 : 64;
   return (size_t)(vt * hd + rb_alloc * hpk * vt) * sizeof(float);
 }
-int pv_threads(int hd, int hpk) { return ((hd / 2) * hpk + 31) / 32 * 32; }
+// Heads per P.V thread: kPvStepHeads for short segments when there are
+// enough (kv head, segment) CTAs to fill the GPU several times over (the
+// shared-memory V reads then bound the kernel); one otherwise, where the
+// kernel is latency bound and wants the most threads.
+int pv_heads_per_thread(int hpk, int seg_rows, int nseg_max, int nkv) {
+  return seg_rows <= kPvStepRows && nseg_max * nkv >= 4 * device_sm_count() ? std::min(hpk, kPvStepHeads) : 1;
+}
+int pv_threads(int hd, int hpk, int hpt) { return ((hd / 2) * ((hpk + hpt - 1) / hpt) + 31) / 32 * 32; }
 }  // namespace
 
 int build_segments(const RowInfo* rows, int M, int seg_len, AttnSeg* segs) {
@@ -728,7 +767,8 @@ cudaError_t launch_attention(const float* q, float* out, const StreamKV* kv, int
   // Stages: as many as fit ~72 KB (three CTAs per SM), at least 2, at most 4.
   const int ns = (int)std::max<size_t>(2, std::min<size_t>(kPvMaxStages, (72 * 1024) / stage));
   const size_t sm3 = (size_t)ns * stage;
-  const int t3 = pv_threads(hd, hpk);
+  const int hpt = pv_heads_per_thread(hpk, seg_rows, nseg_max, nkv);
+  const int t3 = pv_threads(hd, hpk, hpt);
   if (hb < 1 || sm1 > kAttnMaxSmem || sm3 > kAttnMaxSmem || t3 > 512) return cudaErrorInvalidValue;
   const size_t sm2 = (size_t)hb * n_alloc * sizeof(float);
   // Segment and row dimensions loop inside the kernels; the grids cover
@@ -745,8 +785,11 @@ cudaError_t launch_attention(const float* q, float* out, const StreamKV* kv, int
     if (cudaError_t e = launch_pdl(attn_softmax_kernel, g2, dim3(256), sm2, s, rows, m_dev, M, nh, nkv,      \
                                    scores, n_alloc, hb, et, err))                                           \
       return e;                                                                                             \
-    return launch_pdl(attn_pv_kernel<HDV>, g3, dim3(t3), sm3, s, kv, layer, segs, nseg_dev, nseg_max, nh,   \
-                      nkv, (const float*)scores, n_alloc, seg_rows, ns, out, err);
+    return hpt > 1 ? launch_pdl(attn_pv_kernel<HDV, kPvStepHeads>, g3, dim3(t3), sm3, s, kv, layer, segs,   \
+                                nseg_dev, nseg_max, nh, nkv, (const float*)scores, n_alloc, seg_rows, ns, out, \
+                                err)                                                                           \
+                   : launch_pdl(attn_pv_kernel<HDV, 1>, g3, dim3(t3), sm3, s, kv, layer, segs, nseg_dev,       \
+                                nseg_max, nh, nkv, (const float*)scores, n_alloc, seg_rows, ns, out, err);
   switch (hd) {
     RAI_ATTN(16)
     RAI_ATTN(32)
@@ -764,7 +807,10 @@ cudaError_t init_layer_attributes() {
   cudaError_t e = cudaFuncSetAttribute(attn_softmax_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
 #define RAI_ATTR(HDV)                                                                                     \
   if (e == cudaSuccess)                                                                                   \
-    e = cudaFuncSetAttribute(attn_pv_kernel<HDV>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);    \
+    e = cudaFuncSetAttribute(attn_pv_kernel<HDV, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes); \
+  if (e == cudaSuccess)                                                                                   \
+    e = cudaFuncSetAttribute(attn_pv_kernel<HDV, kPvStepHeads>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
+                             bytes);                                                                      \
   if (e == cudaSuccess)                                                                                   \
     e = cudaFuncSetAttribute(attn_scores_kernel<HDV>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
   RAI_ATTR(16)

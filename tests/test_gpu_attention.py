@@ -37,3 +37,48 @@ def test_attention_bit_exact(oracle, hd, nh, nkv, positions):
             if not np.array_equal(g.view(np.uint32), want.view(np.uint32)):
                 bad.append((r, p, h, float(np.max(np.abs(g - want)))))
     assert not bad, bad[:8]
+
+
+def _short_runs(n_seg, lengths=(1, 2, 1, 3, 4)):
+    """Positions in runs of 1-4 consecutive positions, one position apart:
+    n_seg attention segments of at most 4 rows."""
+    pos, p = [], 3
+    for i in range(n_seg):
+        n = lengths[i % len(lengths)]
+        pos += list(range(p, p + n))
+        p += n + 1
+    return pos
+
+
+@pytest.mark.parametrize("hd,nh,nkv", [(64, 32, 4), (64, 14, 2), (128, 32, 8), (32, 8, 2)])
+def test_attention_many_short_segments(oracle, hd, nh, nkv):
+    """Enough (kv head, segment) pairs of at most 4 rows (here >= 640, four
+    times a 148-SM part's SM count) that P.V gives each thread several query
+    heads of its KV head; bit-exact with the oracle, including a head count
+    per KV head that is not a multiple of the heads per thread (14 / 2)."""
+    from rai_b200 import native
+    n_seg = max(160, 640 // nkv)
+    positions = _short_runs(n_seg)
+    rng = np.random.default_rng(hd + nh * 7 + nkv)
+    max_ctx = max(positions) + 2
+    M = len(positions)
+    q = rng.standard_normal((M, nh * hd)).astype(np.float32)
+    k = rng.standard_normal((nkv, max_ctx, hd)).astype(np.float32)
+    v = rng.standard_normal((nkv, max_ctx, hd)).astype(np.float32)
+    scale = np.float32(1.0) / np.sqrt(np.float32(hd))
+    dev = torch.device("cuda", 0)
+    qd, kd, vd = (torch.from_numpy(a).to(dev) for a in (q, k, v))
+    out = torch.full((M, nh * hd), float("nan"), device=dev)
+    pos = np.asarray(positions, np.int32)
+    native.check(native.lib().rai_gpu_attention(qd.data_ptr(), kd.data_ptr(), vd.data_ptr(),
+                                                pos.ctypes.data, M, nh, nkv, hd, max_ctx, float(scale),
+                                                out.data_ptr(), torch.cuda.current_stream().cuda_stream))
+    got = out.cpu().numpy()
+    hpk = nh // nkv
+    bad = []
+    for r, p in enumerate(positions):
+        for h in range(nh):
+            want = oracle.attention_head(q[r, h * hd:(h + 1) * hd], k[h // hpk], v[h // hpk], p, float(scale))
+            if not np.array_equal(got[r, h * hd:(h + 1) * hd].view(np.uint32), want.view(np.uint32)):
+                bad.append((r, p, h))
+    assert not bad, (len(bad), bad[:8])
