@@ -80,6 +80,39 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
       : "memory");
 }
 
+// 16-byte asynchronous copy global -> shared (both addresses 16-byte
+// aligned), completing with the thread's next commit group.
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+// Wait until at most N of this thread's commit groups are still in flight.
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+// Stage n floats of global memory in shared memory, cooperatively (thread
+// `tid` of `nthr`): 16-byte asynchronous copies when both ends are 16-byte
+// aligned and n is a multiple of 4, so every copy is in flight at once;
+// otherwise plain loads, four per thread issued before their stores. The
+// caller completes the staging with cp_async_wait<0>() and a barrier.
+__device__ __forceinline__ void stage_f32(float* dst, const float* src, int n, int tid, int nthr) {
+  if (((reinterpret_cast<uintptr_t>(src) | (uintptr_t)smem_u32(dst)) & 15u) == 0 && (n & 3) == 0) {
+    for (int i = 4 * tid; i < n; i += 4 * nthr) cp_async16(dst + i, src + i);
+  } else {
+    for (int i = tid; i < n; i += 4 * nthr) {
+      float v[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) v[u] = i + u * nthr < n ? src[i + u * nthr] : 0.f;
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
+        if (i + u * nthr < n) dst[i + u * nthr] = v[u];
+    }
+  }
+  cp_async_commit();
+}
+
 // Programmatic dependent launch: let the next kernel in the stream start its
 // prologue, and wait for the previous kernel's results before reading them.
 __device__ __forceinline__ void pdl_launch_dependents() {

@@ -136,7 +136,7 @@ __global__ void pack8_kernel(const uint8_t* __restrict__ codes, const uint8_t* _
 // scope before the kernel ends.
 __global__ void quantize_kernel(const float* __restrict__ x, int ldx, int M, const int* m_dev,
                                 int K, int gs, int wbits, ActDst dst, int tok_alloc) {
-  __shared__ float sx[8][128];
+  __shared__ __align__(16) float sx[8][128];
   __shared__ uint32_t sqw[8][32];
   pdl_wait_prior();
   pdl_launch_dependents();
@@ -153,7 +153,8 @@ __global__ void quantize_kernel(const float* __restrict__ x, int ldx, int M, con
       continue;
     }
     const float* xr = x + (size_t)tok * ldx + (size_t)g * gs;
-    for (int i = lane; i < len; i += 32) sx[warp][i] = xr[i];
+    stage_f32(sx[warp], xr, len, lane, 32);
+    cp_async_wait<0>();
     __syncwarp();
     quant_group_warp(sx[warp], len, wbits, tok, dst, g, sqw[warp]);
   }
@@ -179,7 +180,7 @@ __global__ void __launch_bounds__(256) norm_quant_kernel(const float* __restrict
   __shared__ uint32_t sqw[8][32];
   // The norm weights are model constants: fetched while the previous kernel
   // (programmatic dependent launch) still runs.
-  for (int i = threadIdx.x; i < n; i += blockDim.x) sw[i] = w[i];
+  stage_f32(sw, w, n, threadIdx.x, blockDim.x);
   pdl_wait_prior();
   pdl_launch_dependents();
   // Tensor parallelism: x is assembled from every rank's projection rows.
@@ -193,13 +194,11 @@ __global__ void __launch_bounds__(256) norm_quant_kernel(const float* __restrict
     for (int g = warp; g < groups; g += 8) zero_group_warp(b, act, groups, g);
     continue;
   }
-  const float* xr = x + (size_t)b * n;
-  for (int i = threadIdx.x; i < n; i += blockDim.x) {
-    const float v = xr[i];
-    sxn[i] = v;
-    if (residual) residual[(size_t)b * n + i] = v;
-  }
+  stage_f32(sxn, x + (size_t)b * n, n, threadIdx.x, blockDim.x);
+  cp_async_wait<0>();
   __syncthreads();
+  if (residual)
+    for (int i = threadIdx.x; i < n; i += blockDim.x) residual[(size_t)b * n + i] = sxn[i];
   const int chunks8 = n / 8, chunks16 = chunks8 / 2;
   if (threadIdx.x < 16) {
     const int j = threadIdx.x & 7, half = threadIdx.x >> 3;
@@ -255,7 +254,7 @@ __global__ void __launch_bounds__(256) norm_quant_kernel(const float* __restrict
 // split follows the model's column index.
 __global__ void swiglu_quant_kernel(const float* __restrict__ gu, int ff, const int* m_dev, int M, int gs,
                                     ExpfTable et, ActDst dst, int tok_alloc, int col_off, int ff_full) {
-  __shared__ float sx[8][128];
+  __shared__ __align__(16) float sx[8][128];
   __shared__ uint32_t sqw[8][32];
   pdl_wait_prior();
   pdl_launch_dependents();
@@ -271,17 +270,27 @@ __global__ void swiglu_quant_kernel(const float* __restrict__ gu, int ff, const 
     continue;
   }
   const float* row = gu + (size_t)tok * 2 * ff;
-  for (int i = lane; i < len; i += 32) {
+  // len <= 128: every lane's gate and up values are loaded before the math.
+  float xv[4], uv[4];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const int i = lane + 32 * k;
+    xv[k] = i < len ? row[g * gs + i] : 0.f;
+    uv[k] = i < len ? row[ff + g * gs + i] : 0.f;
+  }
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const int i = lane + 32 * k;
+    if (i >= len) continue;
     const int col = g * gs + i;
-    const float xv = row[col], u = row[ff + col];
     float sv;
     if (col + col_off < vec_end) {
-      const float e = schraudolph(__fmul_rn(xv, -1.0f));
-      sv = __fdiv_rn(xv, __fadd_rn(1.0f, e));
+      const float e = schraudolph(__fmul_rn(xv[k], -1.0f));
+      sv = __fdiv_rn(xv[k], __fadd_rn(1.0f, e));
     } else {
-      sv = __fdiv_rn(xv, __fadd_rn(1.0f, expf_host(-xv, et)));
+      sv = __fdiv_rn(xv[k], __fadd_rn(1.0f, expf_host(-xv[k], et)));
     }
-    sx[warp][i] = __fmul_rn(sv, u);
+    sx[warp][i] = __fmul_rn(sv, uv[k]);
   }
   __syncwarp();
   quant_group_warp(sx[warp], len, 4, tok, dst, g, sqw[warp]);

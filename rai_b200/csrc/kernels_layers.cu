@@ -94,7 +94,7 @@ __global__ void qkv_post_kernel(const float* __restrict__ qkv, int ld, float* __
                                 const RowInfo* __restrict__ rows, const int* m_dev, int M) {
   pdl_wait_prior();
   pdl_launch_dependents();
-  extern __shared__ float srow[];  // q | k
+  extern __shared__ __align__(16) float srow[];  // q | k
   __shared__ float s_inv[2];
   const int mact = active_rows(m_dev, M);
   for (int b = blockIdx.x; b < mact; b += gridDim.x) {
@@ -103,7 +103,8 @@ __global__ void qkv_post_kernel(const float* __restrict__ qkv, int ld, float* __
   const int pos = ri.pos;
   int qd = nh * hd, kvd = nkv * hd, half = hd / 2, chunked = (half / 8) * 8;
   const float* row = qkv + (size_t)b * ld;
-  for (int i = threadIdx.x; i < qd + kvd; i += blockDim.x) srow[i] = row[i];
+  stage_f32(srow, row, qd + kvd, threadIdx.x, blockDim.x);
+  cp_async_wait<0>();
   __syncthreads();
   float* sq = srow;
   float* sk = srow + qd;
@@ -134,11 +135,24 @@ __global__ void qkv_post_kernel(const float* __restrict__ qkv, int ld, float* __
   for (int i = threadIdx.x; i < qd; i += blockDim.x) q_out[(size_t)b * qd + i] = sq[i];
   const float* vrow = row + qd + kvd;
   const size_t lbase = (size_t)layer * nkv * sk_.max_ctx * hd;
-  for (int i = threadIdx.x; i < kvd; i += blockDim.x) {
-    int h = i / hd, d = i % hd;
-    size_t o = lbase + ((size_t)h * sk_.max_ctx + pos) * hd + d;
-    sk_.k[o] = sk[i];
-    sk_.v[o] = vrow[i];
+  // v goes from the projection row to the cache: four loads per thread in
+  // flight before their stores.
+  for (int i0 = threadIdx.x; i0 < kvd; i0 += 4 * blockDim.x) {
+    float vv[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int i = i0 + u * blockDim.x;
+      vv[u] = i < kvd ? vrow[i] : 0.f;
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int i = i0 + u * blockDim.x;
+      if (i >= kvd) continue;
+      const int h = i / hd, d = i % hd;
+      const size_t o = lbase + ((size_t)h * sk_.max_ctx + pos) * hd + d;
+      sk_.k[o] = sk[i];
+      sk_.v[o] = vv[u];
+    }
   }
   __syncthreads();  // shared rows are reused by the next row
   }
@@ -526,6 +540,147 @@ __global__ void __launch_bounds__(512) attn_pv_kernel(const StreamKV* __restrict
   }
 }
 
+// P.V for launches with fewer (kv head, segment) pairs than SMs (one or a
+// few streams), where a CTA streaming its whole V block is bound by the
+// bytes it can keep in flight: the head dimension is cut into DS slices of
+// HDS = HD / DS columns, CTA (kv head, segment, slice); thread (d pair of the
+// slice, head) carries the same FMA chains as pv_body (out = fma(p_t, v_t[d],
+// out) over t in order), so results are identical. V slices and p tiles
+// stream through a kPvsStages-deep ring of 16-byte cp.async copies issued by
+// every thread (one barrier per tile).
+constexpr int kPvsStages = 4;
+constexpr int kPvsTile = 64;  // positions per tile
+
+template <int HD, int DS, int RB>
+__device__ __forceinline__ void pvs_body(const float* __restrict__ vbase, const float* __restrict__ p, int nh,
+                                         int hpk, int kvh, const AttnSeg& sg, int n_alloc, int rb_alloc,
+                                         float* __restrict__ out, float* sm) {
+  constexpr int HDS = HD / DS, VT = kPvsTile, NDP = HDS / 2, NS = kPvsStages, V4 = HDS / 4;
+  const int stage_floats = VT * HDS + rb_alloc * hpk * VT;
+  const int tid = threadIdx.x, nthr = blockDim.x;
+  const int dp = tid % NDP, h = tid / NDP;
+  const int d0 = 2 * dp;
+  const bool active = h < hpk;
+  const int nrows = sg.nrows;
+  const int n_max = sg.pos0 + nrows, n_all = sg.pos0 + 1;
+  const int ntiles = (n_max + VT - 1) / VT;
+  const float* prow0 = p + ((size_t)sg.row0 * nh + (size_t)kvh * hpk) * n_alloc;
+  const float* vsl = vbase + (size_t)blockIdx.z * HDS;
+  // Every thread's share of tile `tile` (none past the end: the group is
+  // still committed so the wait counts stay uniform).
+  auto load = [&](int tile) {
+    if (tile < ntiles) {
+      const int t0 = tile * VT, cnt = min(VT, n_max - t0), c4 = (cnt + 3) / 4;
+      float* sv = sm + (size_t)(tile % NS) * stage_floats;
+      float* sp = sv + VT * HDS;
+      for (int i = tid; i < cnt * V4; i += nthr) {
+        const int r = i / V4, c = i - r * V4;
+        cp_async16(sv + r * HDS + 4 * c, vsl + (size_t)(t0 + r) * HD + 4 * c);
+      }
+      for (int i = tid; i < nrows * hpk * c4; i += nthr) {
+        const int rh = i / c4, c = i - rh * c4;
+        const int r = rh / hpk, hh = rh - r * hpk;
+        cp_async16(sp + rh * VT + 4 * c, prow0 + ((size_t)r * nh + hh) * n_alloc + t0 + 4 * c);
+      }
+    }
+    cp_async_commit();
+  };
+#pragma unroll
+  for (int j = 0; j < NS - 1; ++j) load(j);
+  float acc[RB][2];
+#pragma unroll
+  for (int r = 0; r < RB; ++r) acc[r][0] = acc[r][1] = 0.f;
+  for (int tile = 0; tile < ntiles; ++tile) {
+    cp_async_wait<NS - 2>();  // this thread's copies of `tile` have landed
+    __syncthreads();          // ... and everyone's; stage (tile - 1) % NS is free
+    load(tile + NS - 1);
+    const int t0 = tile * VT, cnt = min(VT, n_max - t0);
+    const float* sv = sm + (size_t)(tile % NS) * stage_floats + d0;
+    const float* ph = sm + (size_t)(tile % NS) * stage_floats + VT * HDS + (active ? h : 0) * VT;
+    if (!active) continue;
+    if (t0 + cnt <= n_all) {
+      int t = 0;
+      for (; t + 8 <= cnt; t += 8) {
+        float2 v[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) v[u] = *reinterpret_cast<const float2*>(sv + (t + u) * HDS);
+#pragma unroll
+        for (int r = 0; r < RB; ++r) {
+          if (r < nrows) {
+            const float4 pa = *reinterpret_cast<const float4*>(ph + r * hpk * VT + t);
+            const float4 pb = *reinterpret_cast<const float4*>(ph + r * hpk * VT + t + 4);
+            const float p8[8] = {pa.x, pa.y, pa.z, pa.w, pb.x, pb.y, pb.z, pb.w};
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+              acc[r][0] = __fmaf_rn(p8[u], v[u].x, acc[r][0]);
+              acc[r][1] = __fmaf_rn(p8[u], v[u].y, acc[r][1]);
+            }
+          }
+        }
+      }
+      for (; t < cnt; ++t) {
+        const float2 v = *reinterpret_cast<const float2*>(sv + t * HDS);
+#pragma unroll
+        for (int r = 0; r < RB; ++r) {
+          if (r < nrows) {
+            const float a = ph[r * hpk * VT + t];
+            acc[r][0] = __fmaf_rn(a, v.x, acc[r][0]);
+            acc[r][1] = __fmaf_rn(a, v.y, acc[r][1]);
+          }
+        }
+      }
+    } else {
+      for (int t = 0; t < cnt; ++t) {
+        const float2 v = *reinterpret_cast<const float2*>(sv + t * HDS);
+        const int rmin = t0 + t - sg.pos0;  // rows r >= rmin see position t0 + t
+#pragma unroll
+        for (int r = 0; r < RB; ++r) {
+          if (r < nrows && r >= rmin) {
+            const float a = ph[r * hpk * VT + t];
+            acc[r][0] = __fmaf_rn(a, v.x, acc[r][0]);
+            acc[r][1] = __fmaf_rn(a, v.y, acc[r][1]);
+          }
+        }
+      }
+    }
+  }
+  if (active) {
+#pragma unroll
+    for (int r = 0; r < RB; ++r)
+      if (r < nrows)
+        *reinterpret_cast<float2*>(out + (size_t)(sg.row0 + r) * nh * HD + (size_t)(kvh * hpk + h) * HD +
+                                   (size_t)blockIdx.z * HDS + d0) = make_float2(acc[r][0], acc[r][1]);
+  }
+}
+
+template <int HD, int DS>
+__global__ void __launch_bounds__(256) attn_pv_split_kernel(const StreamKV* __restrict__ kv, int layer,
+                                                            const AttnSeg* __restrict__ segs, const int* nseg_dev,
+                                                            int nseg_max, int nh, int nkv,
+                                                            const float* __restrict__ p, int n_alloc, int rb_alloc,
+                                                            float* __restrict__ out) {
+  pdl_wait_prior();
+  pdl_launch_dependents();
+  extern __shared__ __align__(16) float sm[];
+  const int kvh = blockIdx.x;
+  const int nseg = active_rows(nseg_dev, nseg_max);
+  const int hpk = nh / nkv;
+  for (int si = blockIdx.y; si < nseg; si += gridDim.y) {
+    const AttnSeg sg = segs[si];
+    const StreamKV sk_ = kv[sg.stream];
+    const float* vbase = sk_.v + ((size_t)layer * nkv + kvh) * sk_.max_ctx * HD;
+#define RAI_PVS(RB) pvs_body<HD, DS, RB>(vbase, p, nh, hpk, kvh, sg, n_alloc, rb_alloc, out, sm)
+    if (sg.nrows <= 1) RAI_PVS(1);
+    else if (sg.nrows <= 2) RAI_PVS(2);
+    else if (sg.nrows <= 4) RAI_PVS(4);
+    else if (sg.nrows <= 8) RAI_PVS(8);
+    else RAI_PVS(kSegRows);
+#undef RAI_PVS
+    cp_async_wait<0>();
+    __syncthreads();  // the ring is refilled for the next segment
+  }
+}
+
 // ---------------------------------------------------------------------------
 // Argmax with the reference's total order (NaN -> -inf first) and ties to
 // the LAST index: max over (orderable key << 32 | index).
@@ -741,6 +896,19 @@ int pv_heads_per_thread(int hpk, int seg_rows, int nseg_max, int nkv) {
   return seg_rows <= kPvStepRows && nseg_max * nkv >= 4 * device_sm_count() ? std::min(hpk, kPvStepHeads) : 1;
 }
 int pv_threads(int hd, int hpk, int hpt) { return ((hd / 2) * ((hpk + hpt - 1) / hpt) + 31) / 32 * 32; }
+// Head-dimension slices of the split P.V: the most (up to 8, at least 8
+// columns each) that keep the launch within two CTAs per SM, when the
+// (kv head, segment) pairs alone do not fill the SMs; 1 = the pv_body path.
+int pv_dim_slices(int hd, int nseg_max, int nkv) {
+  const int base = nseg_max * nkv, sms = device_sm_count();
+  if (base >= sms) return 1;
+  int ds = 1;
+  while (ds < 8 && hd / (2 * ds) >= 8 && base * 2 * ds <= 2 * sms) ds *= 2;
+  return ds;
+}
+size_t pvs_smem_bytes(int hd, int ds, int hpk, int rb_alloc) {
+  return (size_t)kPvsStages * ((size_t)kPvsTile * (hd / ds) + (size_t)rb_alloc * hpk * kPvsTile) * sizeof(float);
+}
 }  // namespace
 
 int build_segments(const RowInfo* rows, int M, int seg_len, AttnSeg* segs) {
@@ -753,6 +921,32 @@ int build_segments(const RowInfo* rows, int M, int seg_len, AttnSeg* segs) {
   }
   return n;
 }
+
+namespace {
+template <int HD>
+cudaError_t launch_pv_split(int ds, dim3 g, int threads, size_t smem, cudaStream_t s, const StreamKV* kv, int layer,
+                            const AttnSeg* segs, const int* nseg_dev, int nseg_max, int nh, int nkv,
+                            const float* p, int n_alloc, int rb_alloc, float* out) {
+  switch (ds) {
+    case 2:
+      if constexpr (HD / 2 >= 8)
+        return launch_pdl(attn_pv_split_kernel<HD, 2>, g, dim3(threads), smem, s, kv, layer, segs, nseg_dev,
+                          nseg_max, nh, nkv, p, n_alloc, rb_alloc, out);
+      break;
+    case 4:
+      if constexpr (HD / 4 >= 8)
+        return launch_pdl(attn_pv_split_kernel<HD, 4>, g, dim3(threads), smem, s, kv, layer, segs, nseg_dev,
+                          nseg_max, nh, nkv, p, n_alloc, rb_alloc, out);
+      break;
+    case 8:
+      if constexpr (HD / 8 >= 8)
+        return launch_pdl(attn_pv_split_kernel<HD, 8>, g, dim3(threads), smem, s, kv, layer, segs, nseg_dev,
+                          nseg_max, nh, nkv, p, n_alloc, rb_alloc, out);
+      break;
+  }
+  return cudaErrorInvalidValue;
+}
+}  // namespace
 
 cudaError_t launch_attention(const float* q, float* out, const StreamKV* kv, int layer, const RowInfo* rows,
                              const int* m_dev, int M, const AttnSeg* segs, const int* nseg_dev, int nseg_max,
@@ -769,7 +963,11 @@ cudaError_t launch_attention(const float* q, float* out, const StreamKV* kv, int
   const size_t sm3 = (size_t)ns * stage;
   const int hpt = pv_heads_per_thread(hpk, seg_rows, nseg_max, nkv);
   const int t3 = pv_threads(hd, hpk, hpt);
-  if (hb < 1 || sm1 > kAttnMaxSmem || sm3 > kAttnMaxSmem || t3 > 512) return cudaErrorInvalidValue;
+  const int ds = pv_dim_slices(hd, nseg_max, nkv);
+  const int t3s = ((hd / ds / 2) * hpk + 31) / 32 * 32;
+  const size_t sm3s = pvs_smem_bytes(hd, ds, hpk, seg_rows);
+  if (hb < 1 || sm1 > kAttnMaxSmem || sm3 > kAttnMaxSmem || t3 > 512 || sm3s > kAttnMaxSmem || t3s > 256)
+    return cudaErrorInvalidValue;
   const size_t sm2 = (size_t)hb * n_alloc * sizeof(float);
   // Segment and row dimensions loop inside the kernels; the grids cover
   // about two waves.
@@ -785,6 +983,9 @@ cudaError_t launch_attention(const float* q, float* out, const StreamKV* kv, int
     if (cudaError_t e = launch_pdl(attn_softmax_kernel, g2, dim3(256), sm2, s, rows, m_dev, M, nh, nkv,      \
                                    scores, n_alloc, hb, et, err))                                           \
       return e;                                                                                             \
+    if (ds > 1)                                                                                             \
+      return launch_pv_split<HDV>(ds, dim3(nkv, nseg_max, ds), t3s, sm3s, s, kv, layer, segs, nseg_dev,     \
+                                  nseg_max, nh, nkv, (const float*)scores, n_alloc, seg_rows, out);         \
     return hpt > 1 ? launch_pdl(attn_pv_kernel<HDV, kPvStepHeads>, g3, dim3(t3), sm3, s, kv, layer, segs,   \
                                 nseg_dev, nseg_max, nh, nkv, (const float*)scores, n_alloc, seg_rows, ns, out, \
                                 err)                                                                           \
@@ -802,12 +1003,29 @@ cudaError_t launch_attention(const float* q, float* out, const StreamKV* kv, int
   return cudaGetLastError();
 }
 
+namespace {
+template <int HD>
+cudaError_t set_pv_split_attributes(int bytes) {
+  cudaError_t e = cudaSuccess;
+  if constexpr (HD / 2 >= 8)
+    e = cudaFuncSetAttribute(attn_pv_split_kernel<HD, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if constexpr (HD / 4 >= 8)
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(attn_pv_split_kernel<HD, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if constexpr (HD / 8 >= 8)
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(attn_pv_split_kernel<HD, 8>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  return e;
+}
+}  // namespace
+
 cudaError_t init_layer_attributes() {
   const int bytes = (int)kAttnMaxSmem;
   cudaError_t e = cudaFuncSetAttribute(attn_softmax_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
 #define RAI_ATTR(HDV)                                                                                     \
   if (e == cudaSuccess)                                                                                   \
     e = cudaFuncSetAttribute(attn_pv_kernel<HDV, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes); \
+  if (e == cudaSuccess) e = set_pv_split_attributes<HDV>(bytes);                                          \
   if (e == cudaSuccess)                                                                                   \
     e = cudaFuncSetAttribute(attn_pv_kernel<HDV, kPvStepHeads>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
                              bytes);                                                                      \

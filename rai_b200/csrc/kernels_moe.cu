@@ -38,7 +38,8 @@ __global__ void __launch_bounds__(kMaxMoeExperts) router_kernel(const float* __r
   const int mact = active(m_dev, M);
   if (b0 >= mact) return;
   const int nt = min(kRouterTok, mact - b0);
-  for (int i = threadIdx.x; i < nt * h; i += blockDim.x) sx[i] = x[(size_t)b0 * h + i];
+  stage_f32(sx, x + (size_t)b0 * h, nt * h, threadIdx.x, blockDim.x);
+  cp_async_wait<0>();
   __syncthreads();
   const int e = threadIdx.x;
   if (e >= ne) return;
@@ -188,7 +189,7 @@ __global__ void __launch_bounds__(1024) moe_sort_kernel(const int* __restrict__ 
 __global__ void moe_gather_quant_kernel(const float* __restrict__ x, int h, int k, const int* __restrict__ pair_of_row,
                                         const int* __restrict__ n_rows, int gs, uint8_t* __restrict__ act,
                                         int tok_alloc) {
-  __shared__ float sx[8][128];
+  __shared__ __align__(16) float sx[8][128];
   __shared__ uint32_t sqw[8][32];
   pdl_wait_prior();
   pdl_launch_dependents();
@@ -204,7 +205,8 @@ __global__ void moe_gather_quant_kernel(const float* __restrict__ x, int h, int 
   }
   const float* xr = x + (size_t)(pair / k) * h + (size_t)g * gs;
   const int len = min(gs, h - g * gs);
-  for (int i = lane; i < len; i += 32) sx[warp][i] = xr[i];
+  stage_f32(sx[warp], xr, len, lane, 32);
+  cp_async_wait<0>();
   __syncwarp();
   quant_group_warp(sx[warp], len, 4, r, act, groups, g, sqw[warp]);
 }

@@ -51,14 +51,20 @@ def _short_runs(n_seg, lengths=(1, 2, 1, 3, 4)):
 
 
 @pytest.mark.parametrize("hd,nh,nkv", [(64, 32, 4), (64, 14, 2), (128, 32, 8), (32, 8, 2)])
-def test_attention_many_short_segments(oracle, hd, nh, nkv):
-    """Enough (kv head, segment) pairs of at most 4 rows (here >= 640, four
-    times a 148-SM part's SM count) that P.V gives each thread several query
-    heads of its KV head; bit-exact with the oracle, including a head count
-    per KV head that is not a multiple of the heads per thread (14 / 2)."""
+@pytest.mark.parametrize("runs", ["short", "long"])
+def test_attention_many_segments(oracle, hd, nh, nkv, runs):
+    """Launches with many (kv head, segment) pairs, bit-exact with the oracle.
+    short: segments of at most 4 rows, >= 640 pairs (four times a 148-SM
+    part's SM count), so P.V gives each thread several query heads of its KV
+    head (including 14 / 2 heads, not a multiple of the heads per thread).
+    long: segments of 5-8 rows, >= 160 pairs: one head per thread, each CTA
+    streaming its whole V block. (The small launches of the other tests take
+    the head-dimension split P.V.)"""
     from rai_b200 import native
-    n_seg = max(160, 640 // nkv)
-    positions = _short_runs(n_seg)
+    if runs == "short":
+        positions = _short_runs(max(160, 640 // nkv))
+    else:
+        positions = _short_runs(max(20, 160 // nkv), lengths=(6, 5, 8))
     rng = np.random.default_rng(hd + nh * 7 + nkv)
     max_ctx = max(positions) + 2
     M = len(positions)
