@@ -541,29 +541,55 @@ __global__ void __launch_bounds__(512) attn_pv_kernel(const StreamKV* __restrict
 }
 
 // P.V for launches with fewer (kv head, segment) pairs than SMs (one or a
-// few streams), where a CTA streaming its whole V block is bound by the
-// bytes it can keep in flight: the head dimension is cut into DS slices of
-// HDS = HD / DS columns, CTA (kv head, segment, slice); thread (d pair of the
-// slice, head) carries the same FMA chains as pv_body (out = fma(p_t, v_t[d],
-// out) over t in order), so results are identical. V slices and p tiles
-// stream through a kPvsStages-deep ring of 16-byte cp.async copies issued by
-// every thread (one barrier per tile).
+// few streams). There the kernel is bound by each thread's serial chain over
+// the positions, so the work is spread as thin as the exact order allows:
+// the head dimension is cut into DS slices of HDS = HD / DS columns, CTA
+// (kv head, segment, slice), thread (one column of the slice, head), which
+// carries out[r][h][d] = fma(p_t, v_t[d], out) over t in order for each of
+// the segment's rows (the chains of pv_body, so results are identical). The
+// rows' FMAs are interleaved per position (independent chains back to back).
+// V slices and p tiles stream through a kPvsStages-deep ring of 16-byte
+// cp.async copies issued by every thread (one barrier per tile).
 constexpr int kPvsStages = 4;
 constexpr int kPvsTile = 64;  // positions per tile
+constexpr int kPvsMaxSlices = 16;
+
+// Rows r0 .. r0 + RG - 1 (those < nrows) over the 8 positions t .. t + 7 of
+// a full tile: p from shared memory, v[] already loaded.
+template <int RG>
+__device__ __forceinline__ void pvs_rows8(float* acc, const float* ph, int pstride, int r0, int nrows, int t,
+                                          const float (&v)[8]) {
+  float p8[RG][8];
+#pragma unroll
+  for (int r = 0; r < RG; ++r) {
+    if (r0 + r < nrows) {
+      const float4 pa = *reinterpret_cast<const float4*>(ph + (r0 + r) * pstride + t);
+      const float4 pb = *reinterpret_cast<const float4*>(ph + (r0 + r) * pstride + t + 4);
+      p8[r][0] = pa.x; p8[r][1] = pa.y; p8[r][2] = pa.z; p8[r][3] = pa.w;
+      p8[r][4] = pb.x; p8[r][5] = pb.y; p8[r][6] = pb.z; p8[r][7] = pb.w;
+    }
+  }
+#pragma unroll
+  for (int u = 0; u < 8; ++u)
+#pragma unroll
+    for (int r = 0; r < RG; ++r)
+      if (r0 + r < nrows) acc[r0 + r] = __fmaf_rn(p8[r][u], v[u], acc[r0 + r]);
+}
 
 template <int HD, int DS, int RB>
 __device__ __forceinline__ void pvs_body(const float* __restrict__ vbase, const float* __restrict__ p, int nh,
                                          int hpk, int kvh, const AttnSeg& sg, int n_alloc, int rb_alloc,
                                          float* __restrict__ out, float* sm) {
-  constexpr int HDS = HD / DS, VT = kPvsTile, NDP = HDS / 2, NS = kPvsStages, V4 = HDS / 4;
+  constexpr int HDS = HD / DS, VT = kPvsTile, NS = kPvsStages, V4 = HDS / 4;
+  constexpr int RG = RB < 4 ? RB : 4;  // rows per interleaved group
   const int stage_floats = VT * HDS + rb_alloc * hpk * VT;
   const int tid = threadIdx.x, nthr = blockDim.x;
-  const int dp = tid % NDP, h = tid / NDP;
-  const int d0 = 2 * dp;
+  const int d = tid % HDS, h = tid / HDS;
   const bool active = h < hpk;
   const int nrows = sg.nrows;
   const int n_max = sg.pos0 + nrows, n_all = sg.pos0 + 1;
   const int ntiles = (n_max + VT - 1) / VT;
+  const int pstride = hpk * VT;  // p of (row r, head h) at ph + r * pstride
   const float* prow0 = p + ((size_t)sg.row0 * nh + (size_t)kvh * hpk) * n_alloc;
   const float* vsl = vbase + (size_t)blockIdx.z * HDS;
   // Every thread's share of tile `tile` (none past the end: the group is
@@ -573,9 +599,10 @@ __device__ __forceinline__ void pvs_body(const float* __restrict__ vbase, const 
       const int t0 = tile * VT, cnt = min(VT, n_max - t0), c4 = (cnt + 3) / 4;
       float* sv = sm + (size_t)(tile % NS) * stage_floats;
       float* sp = sv + VT * HDS;
+      const float* vt0 = vsl + (size_t)t0 * HD;
       for (int i = tid; i < cnt * V4; i += nthr) {
         const int r = i / V4, c = i - r * V4;
-        cp_async16(sv + r * HDS + 4 * c, vsl + (size_t)(t0 + r) * HD + 4 * c);
+        cp_async16(sv + 4 * i, vt0 + r * HD + 4 * c);
       }
       for (int i = tid; i < nrows * hpk * c4; i += nthr) {
         const int rh = i / c4, c = i - rh * c4;
@@ -587,60 +614,39 @@ __device__ __forceinline__ void pvs_body(const float* __restrict__ vbase, const 
   };
 #pragma unroll
   for (int j = 0; j < NS - 1; ++j) load(j);
-  float acc[RB][2];
+  float acc[RB];
 #pragma unroll
-  for (int r = 0; r < RB; ++r) acc[r][0] = acc[r][1] = 0.f;
+  for (int r = 0; r < RB; ++r) acc[r] = 0.f;
   for (int tile = 0; tile < ntiles; ++tile) {
     cp_async_wait<NS - 2>();  // this thread's copies of `tile` have landed
     __syncthreads();          // ... and everyone's; stage (tile - 1) % NS is free
     load(tile + NS - 1);
-    const int t0 = tile * VT, cnt = min(VT, n_max - t0);
-    const float* sv = sm + (size_t)(tile % NS) * stage_floats + d0;
-    const float* ph = sm + (size_t)(tile % NS) * stage_floats + VT * HDS + (active ? h : 0) * VT;
     if (!active) continue;
+    const int t0 = tile * VT, cnt = min(VT, n_max - t0);
+    const float* sv = sm + (size_t)(tile % NS) * stage_floats + d;
+    const float* ph = sm + (size_t)(tile % NS) * stage_floats + VT * HDS + h * VT;
     if (t0 + cnt <= n_all) {
       int t = 0;
       for (; t + 8 <= cnt; t += 8) {
-        float2 v[8];
+        float v[8];
 #pragma unroll
-        for (int u = 0; u < 8; ++u) v[u] = *reinterpret_cast<const float2*>(sv + (t + u) * HDS);
+        for (int u = 0; u < 8; ++u) v[u] = sv[(t + u) * HDS];
 #pragma unroll
-        for (int r = 0; r < RB; ++r) {
-          if (r < nrows) {
-            const float4 pa = *reinterpret_cast<const float4*>(ph + r * hpk * VT + t);
-            const float4 pb = *reinterpret_cast<const float4*>(ph + r * hpk * VT + t + 4);
-            const float p8[8] = {pa.x, pa.y, pa.z, pa.w, pb.x, pb.y, pb.z, pb.w};
-#pragma unroll
-            for (int u = 0; u < 8; ++u) {
-              acc[r][0] = __fmaf_rn(p8[u], v[u].x, acc[r][0]);
-              acc[r][1] = __fmaf_rn(p8[u], v[u].y, acc[r][1]);
-            }
-          }
-        }
+        for (int r0 = 0; r0 < RB; r0 += RG) pvs_rows8<RG>(acc, ph, pstride, r0, nrows, t, v);
       }
       for (; t < cnt; ++t) {
-        const float2 v = *reinterpret_cast<const float2*>(sv + t * HDS);
+        const float v = sv[t * HDS];
 #pragma unroll
-        for (int r = 0; r < RB; ++r) {
-          if (r < nrows) {
-            const float a = ph[r * hpk * VT + t];
-            acc[r][0] = __fmaf_rn(a, v.x, acc[r][0]);
-            acc[r][1] = __fmaf_rn(a, v.y, acc[r][1]);
-          }
-        }
+        for (int r = 0; r < RB; ++r)
+          if (r < nrows) acc[r] = __fmaf_rn(ph[r * pstride + t], v, acc[r]);
       }
     } else {
       for (int t = 0; t < cnt; ++t) {
-        const float2 v = *reinterpret_cast<const float2*>(sv + t * HDS);
+        const float v = sv[t * HDS];
         const int rmin = t0 + t - sg.pos0;  // rows r >= rmin see position t0 + t
 #pragma unroll
-        for (int r = 0; r < RB; ++r) {
-          if (r < nrows && r >= rmin) {
-            const float a = ph[r * hpk * VT + t];
-            acc[r][0] = __fmaf_rn(a, v.x, acc[r][0]);
-            acc[r][1] = __fmaf_rn(a, v.y, acc[r][1]);
-          }
-        }
+        for (int r = 0; r < RB; ++r)
+          if (r < nrows && r >= rmin) acc[r] = __fmaf_rn(ph[r * pstride + t], v, acc[r]);
       }
     }
   }
@@ -648,8 +654,7 @@ __device__ __forceinline__ void pvs_body(const float* __restrict__ vbase, const 
 #pragma unroll
     for (int r = 0; r < RB; ++r)
       if (r < nrows)
-        *reinterpret_cast<float2*>(out + (size_t)(sg.row0 + r) * nh * HD + (size_t)(kvh * hpk + h) * HD +
-                                   (size_t)blockIdx.z * HDS + d0) = make_float2(acc[r][0], acc[r][1]);
+        out[(size_t)(sg.row0 + r) * nh * HD + (size_t)(kvh * hpk + h) * HD + (size_t)blockIdx.z * HDS + d] = acc[r];
   }
 }
 
@@ -896,15 +901,16 @@ int pv_heads_per_thread(int hpk, int seg_rows, int nseg_max, int nkv) {
   return seg_rows <= kPvStepRows && nseg_max * nkv >= 4 * device_sm_count() ? std::min(hpk, kPvStepHeads) : 1;
 }
 int pv_threads(int hd, int hpk, int hpt) { return ((hd / 2) * ((hpk + hpt - 1) / hpt) + 31) / 32 * 32; }
-// Head-dimension slices of the split P.V: the most (up to 8, at least 8
-// columns each) that keep the launch within two CTAs per SM, when the
+// Head-dimension slices of the split P.V: the most (up to kPvsMaxSlices, at
+// least 4 columns each) that keep the launch within two CTAs per SM, and at
+// least enough for a CTA of at most 256 threads (HDS x hpk), when the
 // (kv head, segment) pairs alone do not fill the SMs; 1 = the pv_body path.
-int pv_dim_slices(int hd, int nseg_max, int nkv) {
+int pv_dim_slices(int hd, int hpk, int nseg_max, int nkv) {
   const int base = nseg_max * nkv, sms = device_sm_count();
   if (base >= sms) return 1;
   int ds = 1;
-  while (ds < 8 && hd / (2 * ds) >= 8 && base * 2 * ds <= 2 * sms) ds *= 2;
-  return ds;
+  while (ds < kPvsMaxSlices && hd / (2 * ds) >= 4 && (base * 2 * ds <= 2 * sms || (hd / ds) * hpk > 256)) ds *= 2;
+  return ds > 1 && (hd / ds) * hpk <= 256 ? ds : 1;
 }
 size_t pvs_smem_bytes(int hd, int ds, int hpk, int rb_alloc) {
   return (size_t)kPvsStages * ((size_t)kPvsTile * (hd / ds) + (size_t)rb_alloc * hpk * kPvsTile) * sizeof(float);
@@ -928,21 +934,17 @@ cudaError_t launch_pv_split(int ds, dim3 g, int threads, size_t smem, cudaStream
                             const AttnSeg* segs, const int* nseg_dev, int nseg_max, int nh, int nkv,
                             const float* p, int n_alloc, int rb_alloc, float* out) {
   switch (ds) {
-    case 2:
-      if constexpr (HD / 2 >= 8)
-        return launch_pdl(attn_pv_split_kernel<HD, 2>, g, dim3(threads), smem, s, kv, layer, segs, nseg_dev,
-                          nseg_max, nh, nkv, p, n_alloc, rb_alloc, out);
-      break;
-    case 4:
-      if constexpr (HD / 4 >= 8)
-        return launch_pdl(attn_pv_split_kernel<HD, 4>, g, dim3(threads), smem, s, kv, layer, segs, nseg_dev,
-                          nseg_max, nh, nkv, p, n_alloc, rb_alloc, out);
-      break;
-    case 8:
-      if constexpr (HD / 8 >= 8)
-        return launch_pdl(attn_pv_split_kernel<HD, 8>, g, dim3(threads), smem, s, kv, layer, segs, nseg_dev,
-                          nseg_max, nh, nkv, p, n_alloc, rb_alloc, out);
-      break;
+#define RAI_PVS_CASE(DSV)                                                                                    \
+  case DSV:                                                                                                  \
+    if constexpr (HD / DSV >= 4)                                                                             \
+      return launch_pdl(attn_pv_split_kernel<HD, DSV>, g, dim3(threads), smem, s, kv, layer, segs, nseg_dev, \
+                        nseg_max, nh, nkv, p, n_alloc, rb_alloc, out);                                       \
+    break;
+    RAI_PVS_CASE(2)
+    RAI_PVS_CASE(4)
+    RAI_PVS_CASE(8)
+    RAI_PVS_CASE(16)
+#undef RAI_PVS_CASE
   }
   return cudaErrorInvalidValue;
 }
@@ -963,10 +965,11 @@ cudaError_t launch_attention(const float* q, float* out, const StreamKV* kv, int
   const size_t sm3 = (size_t)ns * stage;
   const int hpt = pv_heads_per_thread(hpk, seg_rows, nseg_max, nkv);
   const int t3 = pv_threads(hd, hpk, hpt);
-  const int ds = pv_dim_slices(hd, nseg_max, nkv);
-  const int t3s = ((hd / ds / 2) * hpk + 31) / 32 * 32;
+  const int ds = pv_dim_slices(hd, hpk, nseg_max, nkv);
+  const int t3s = ((hd / ds) * hpk + 31) / 32 * 32;
   const size_t sm3s = pvs_smem_bytes(hd, ds, hpk, seg_rows);
-  if (hb < 1 || sm1 > kAttnMaxSmem || sm3 > kAttnMaxSmem || t3 > 512 || sm3s > kAttnMaxSmem || t3s > 256)
+  if (hb < 1 || sm1 > kAttnMaxSmem || sm3 > kAttnMaxSmem || t3 > 512 ||
+      (ds > 1 && (sm3s > kAttnMaxSmem || t3s > 256)))
     return cudaErrorInvalidValue;
   const size_t sm2 = (size_t)hb * n_alloc * sizeof(float);
   // Segment and row dimensions loop inside the kernels; the grids cover
@@ -1007,14 +1010,15 @@ namespace {
 template <int HD>
 cudaError_t set_pv_split_attributes(int bytes) {
   cudaError_t e = cudaSuccess;
-  if constexpr (HD / 2 >= 8)
-    e = cudaFuncSetAttribute(attn_pv_split_kernel<HD, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
-  if constexpr (HD / 4 >= 8)
-    if (e == cudaSuccess)
-      e = cudaFuncSetAttribute(attn_pv_split_kernel<HD, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
-  if constexpr (HD / 8 >= 8)
-    if (e == cudaSuccess)
-      e = cudaFuncSetAttribute(attn_pv_split_kernel<HD, 8>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+#define RAI_PVS_ATTR(DSV)                                                                                    \
+  if constexpr (HD / DSV >= 4)                                                                               \
+    if (e == cudaSuccess)                                                                                    \
+      e = cudaFuncSetAttribute(attn_pv_split_kernel<HD, DSV>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  RAI_PVS_ATTR(2)
+  RAI_PVS_ATTR(4)
+  RAI_PVS_ATTR(8)
+  RAI_PVS_ATTR(16)
+#undef RAI_PVS_ATTR
   return e;
 }
 }  // namespace
