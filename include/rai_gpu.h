@@ -214,8 +214,10 @@ RAI_API size_t rai_gpu_last_error(char* buf, size_t len);
  * w4a8_matvec, gemm.rs:1336-1392): out[t * rows + r] = sum over the row's
  * groups of the int8-quantized input against 4-bit codes with f16
  * (scale, zero), bit-identical to the AVX2 kernel. Weights are first packed
- * once into the device layout; `scratch` holds the quantized activations
- * (rai_gpu_w4a8_scratch_bytes). group_size must be 64 or 128. */
+ * once into the device layouts (the mma.sync kernel's 4-bit blocks, then the
+ * u8 image of the opt-in tcgen05 kernel, RAI_GEMM_TC=1; the buffer is opaque
+ * and rai_gpu_w4a8_packed_bytes covers both); `scratch` holds the quantized
+ * activations (rai_gpu_w4a8_scratch_bytes). group_size must be 64 or 128. */
 RAI_API size_t rai_gpu_w4a8_packed_bytes(size_t rows, size_t cols, size_t group_size);
 RAI_API int rai_gpu_w4a8_pack(const uint8_t* nibbles, const uint8_t* params, size_t rows, size_t cols,
                       size_t group_size, void* packed, void* stream);

@@ -33,10 +33,20 @@ struct PackedLinear {
   const uint8_t* data = nullptr;  // [tile][group] blocks of kBlockBytes
   int rows = 0, cols = 0, group_size = 0, groups = 0, tiles = 0;
   int wbits = 4;                   // 4: u4 codes (+ f16 scale/zero), 8: u8 embedding codes
+  const uint8_t* tc = nullptr;     // tcgen05 weight image (4-bit linears; null: mma.sync path only)
 };
 
 inline size_t packed_linear_bytes(size_t rows, size_t cols, size_t gs) {
   return ceil_div(rows, kTileRows) * ceil_div(cols, gs) * (size_t)kBlockBytes;
+}
+
+// Weight image of the tcgen05 linear: per (128-row tile, group) the u8 codes
+// in the MMA's shared-memory layout (16 KB) then the rows' f16 (scale, zero).
+constexpr int kTcRows = 128;
+constexpr int kTcImgBytes = kTcRows * 128;
+constexpr int kTcBlockBytes = kTcImgBytes + kTcRows * 4;  // 16896
+inline size_t tc_image_bytes(size_t rows, size_t cols, size_t gs) {
+  return ceil_div(rows, kTcRows) * ceil_div(cols, gs) * (size_t)kTcBlockBytes;
 }
 
 // Quantized-activation staging for one linear input: per group a block of
@@ -117,5 +127,15 @@ struct GemmTp {
 cudaError_t gemm_exact(const PackedLinear& w, const ActBuf& act, int M, float* out, int ld_out,
                        const GemmEpilogue& epi, uint32_t* err, cudaStream_t s, bool pdl = false,
                        const int* m_dev = nullptr, const GemmTp* tp = nullptr);
+
+// The same linear (4-bit weights, one output buffer, no exchange) on the
+// tcgen05 tensor cores; gemm_exact takes this path when RAI_GEMM_TC=1 and the
+// linear has a tcgen05 weight image.
+bool gemm_tc_enabled();
+cudaError_t init_gemm_tc_attributes();
+cudaError_t pack_linear4_tc(const uint8_t* nibbles, const uint8_t* params, int rows, int cols, int gs, uint8_t* out,
+                            cudaStream_t s);
+cudaError_t gemm_tc(const PackedLinear& w, const ActBuf& act, int M, float* out, int ld_out, const GemmEpilogue& epi,
+                    uint32_t* err, cudaStream_t s, const int* m_dev);
 
 }  // namespace rai

@@ -846,6 +846,7 @@ cudaError_t init_gemm_attributes() {
   set(gemm_exact_kernel<4, Gemm4N3>); set(gemm_exact_kernel<4, Gemm4N4>);
   set(gemm_exact_kernel<8, Gemm8N1>); set(gemm_exact_kernel<8, Gemm8N2>);
   set(gemm_exact_kernel<8, Gemm8N3>); set(gemm_exact_kernel<8, Gemm8N4>);
+  if (e == cudaSuccess) e = init_gemm_tc_attributes();
   return e;
 }
 
@@ -938,6 +939,9 @@ cudaError_t gemm_exact(const PackedLinear& w, const ActBuf& act, int M, float* o
                        const GemmEpilogue& epi, uint32_t* err, cudaStream_t s, bool pdl, const int* m_dev,
                        const GemmTp* tp) {
   if (M <= 0) return cudaSuccess;
+  const bool exchange = tp && tp->link.world > 1;
+  if (w.wbits == 4 && w.tc && !exchange && gemm_tc_enabled())
+    return gemm_tc(w, act, M, out, ld_out, epi, err, s, m_dev);
   GemmParams gp = {};
   gp.wait_slot = -1;
   gp.n_out = 1;

@@ -232,9 +232,17 @@ int pack_concat(rai_model* M, const uint8_t* blob_dev, const std::vector<RowRang
     par = t + nb;
   }
   RAI_CUDA(rai::pack_linear4(nib, par, (int)rows, (int)cols, (int)gs, packed, 0));
+  // The tcgen05 weight image (dense linears; the grouped expert weights,
+  // packed into a caller's buffer, keep the mma.sync path only).
+  uint8_t* tc = nullptr;
+  if (!dst && rai::gemm_tc_enabled()) {
+    if (int rc = M->alloc(&tc, rai::tc_image_bytes(rows, cols, gs))) return rc;
+    RAI_CUDA(rai::pack_linear4_tc(nib, par, (int)rows, (int)cols, (int)gs, tc, 0));
+  }
   RAI_CUDA(cudaDeviceSynchronize());
   if (tmp) cudaFree(tmp);
   out->data = packed;
+  out->tc = tc;
   out->rows = (int)rows;
   out->cols = (int)cols;
   out->group_size = (int)gs;
@@ -1615,8 +1623,28 @@ int rai_gpu_last_step_us(const rai_dec* d, float* us) {
 }
 
 // ---- kernel-level entry points ----
+// A packed buffer holds the mma.sync blocks, then (at tc_offset) the
+// tcgen05 weight image.
+namespace {
+size_t tc_offset(size_t rows, size_t cols, size_t gs) {
+  return rai::round_up(rai::packed_linear_bytes(rows, cols, gs), 256);
+}
+PackedLinear packed_view(const void* packed, size_t rows, size_t cols, size_t gs) {
+  PackedLinear w;
+  w.data = static_cast<const uint8_t*>(packed);
+  w.tc = w.data + tc_offset(rows, cols, gs);
+  w.rows = (int)rows;
+  w.cols = (int)cols;
+  w.group_size = (int)gs;
+  w.groups = (int)rai::ceil_div(cols, gs);
+  w.tiles = (int)rai::ceil_div(rows, rai::kTileRows);
+  w.wbits = 4;
+  return w;
+}
+}  // namespace
+
 size_t rai_gpu_w4a8_packed_bytes(size_t rows, size_t cols, size_t gs) {
-  return rai::packed_linear_bytes(rows, cols, gs);
+  return tc_offset(rows, cols, gs) + rai::tc_image_bytes(rows, cols, gs);
 }
 
 int rai_gpu_w4a8_pack(const uint8_t* nibbles, const uint8_t* params, size_t rows, size_t cols, size_t gs,
@@ -1627,6 +1655,9 @@ int rai_gpu_w4a8_pack(const uint8_t* nibbles, const uint8_t* params, size_t rows
   if (rai::ceil_div(cols, gs) > raimodel::kMaxGroups) return fail(RAI_ERR_INVALID, "quantization group count exceeds kernel capacity");
   RAI_CUDA(rai::pack_linear4(nibbles, params, (int)rows, (int)cols, (int)gs, static_cast<uint8_t*>(packed),
                              static_cast<cudaStream_t>(stream)));
+  RAI_CUDA(rai::pack_linear4_tc(nibbles, params, (int)rows, (int)cols, (int)gs,
+                                static_cast<uint8_t*>(packed) + tc_offset(rows, cols, gs),
+                                static_cast<cudaStream_t>(stream)));
   return RAI_OK;
 }
 
@@ -1648,14 +1679,7 @@ int rai_gpu_w4a8_matmul(float* out, const void* packed, const float* input, size
   a.tok_alloc = (int)rai::round_up(tokens, 8);
   a.groups = (int)rai::ceil_div(cols, gs);
   RAI_CUDA(rai::quantize_act(input, (int)cols, (int)tokens, nullptr, (int)cols, (int)gs, 4, a, s));
-  PackedLinear w;
-  w.data = static_cast<const uint8_t*>(packed);
-  w.rows = (int)rows;
-  w.cols = (int)cols;
-  w.group_size = (int)gs;
-  w.groups = a.groups;
-  w.tiles = (int)rai::ceil_div(rows, rai::kTileRows);
-  w.wbits = 4;
+  const PackedLinear w = packed_view(packed, rows, cols, gs);
   RAI_CUDA(rai::gemm_exact(w, a, (int)tokens, out, (int)rows, rai::GemmEpilogue{}, nullptr, s));
   return RAI_OK;
 }
@@ -1730,14 +1754,7 @@ int rai_gpu_w4a8_matmul_prequant(float* out, const void* packed, const void* scr
   a.data = static_cast<uint8_t*>(const_cast<void*>(scratch));
   a.tok_alloc = (int)rai::round_up(tokens, 8);
   a.groups = (int)rai::ceil_div(cols, gs);
-  PackedLinear w;
-  w.data = static_cast<const uint8_t*>(packed);
-  w.rows = (int)rows;
-  w.cols = (int)cols;
-  w.group_size = (int)gs;
-  w.groups = a.groups;
-  w.tiles = (int)rai::ceil_div(rows, rai::kTileRows);
-  w.wbits = 4;
+  const PackedLinear w = packed_view(packed, rows, cols, gs);
   RAI_CUDA(rai::gemm_exact(w, a, (int)tokens, out, (int)rows, rai::GemmEpilogue{}, nullptr,
                            static_cast<cudaStream_t>(stream)));
   return RAI_OK;

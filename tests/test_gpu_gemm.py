@@ -86,3 +86,22 @@ def test_repeated_launches_are_deterministic(oracle):
     a = gpu_matmul(nib, params, x, N, K, 128)
     b = gpu_matmul(nib, params, x, N, K, 128)
     assert np.array_equal(a.view(np.uint32), b.view(np.uint32))
+
+
+def test_tcgen05_path_bit_exact(tiny_model_paths):
+    """The opt-in tcgen05 linear (RAI_GEMM_TC=1, read once per process, so
+    it runs in a child process): GEMM shapes and lookup steps of a tiny model
+    equal the oracle bit for bit."""
+    import json
+    import os
+    import subprocess
+    import sys
+    here = os.path.dirname(os.path.abspath(__file__))
+    env = dict(os.environ, RAI_GEMM_TC="1")
+    r = subprocess.run([sys.executable, os.path.join(here, "tc_worker.py"), tiny_model_paths["tiny-llama"]],
+                       env=env, capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0, r.stderr[-2000:]
+    res = json.loads(r.stdout.strip().splitlines()[-1])
+    assert all(row[-1] == 0 for row in res["gemm"]), res["gemm"]
+    for g, o in res["decode"]:
+        assert g == o
