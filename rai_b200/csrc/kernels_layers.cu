@@ -415,19 +415,50 @@ __device__ __forceinline__ bool pv_body(const float* __restrict__ vbase, const f
           float2 v[8];
 #pragma unroll
           for (int u = 0; u < 8; ++u) v[u] = *reinterpret_cast<const float2*>(sv + (t + u) * HD);
+          if constexpr (HPT > 1) {
+            // (row, head) chains in groups of up to 4: their p loads first,
+            // then per position one FMA of each chain (independent chains
+            // back to back).
+            constexpr int NPR = RB * HPT, PG = NPR < 4 ? NPR : 4;
 #pragma unroll
-          for (int r = 0; r < RB; ++r) {
+            for (int q0 = 0; q0 < NPR; q0 += PG) {
+              float p8[PG][8];
+              bool lv[PG];
 #pragma unroll
-            for (int j = 0; j < HPT; ++j) {
-              if (r < nrows && hv[j]) {
-                const float* pj = ph + (r * hpk + j) * VT + t;
+              for (int q = 0; q < PG; ++q) {
+                const int r = (q0 + q) / HPT, j = (q0 + q) % HPT;
+                lv[q] = r < nrows && hv[j];
+                if (lv[q]) {
+                  const float* pj = ph + (r * hpk + j) * VT + t;
+                  const float4 pa = *reinterpret_cast<const float4*>(pj);
+                  const float4 pb = *reinterpret_cast<const float4*>(pj + 4);
+                  p8[q][0] = pa.x; p8[q][1] = pa.y; p8[q][2] = pa.z; p8[q][3] = pa.w;
+                  p8[q][4] = pb.x; p8[q][5] = pb.y; p8[q][6] = pb.z; p8[q][7] = pb.w;
+                }
+              }
+#pragma unroll
+              for (int u = 0; u < 8; ++u)
+#pragma unroll
+                for (int q = 0; q < PG; ++q) {
+                  const int r = (q0 + q) / HPT, j = (q0 + q) % HPT;
+                  if (lv[q]) {
+                    acc[r][j][0] = __fmaf_rn(p8[q][u], v[u].x, acc[r][j][0]);
+                    acc[r][j][1] = __fmaf_rn(p8[q][u], v[u].y, acc[r][j][1]);
+                  }
+                }
+            }
+          } else {
+#pragma unroll
+            for (int r = 0; r < RB; ++r) {
+              if (r < nrows) {
+                const float* pj = ph + r * hpk * VT + t;
                 const float4 pa = *reinterpret_cast<const float4*>(pj);
                 const float4 pb = *reinterpret_cast<const float4*>(pj + 4);
                 const float p8[8] = {pa.x, pa.y, pa.z, pa.w, pb.x, pb.y, pb.z, pb.w};
 #pragma unroll
                 for (int u = 0; u < 8; ++u) {
-                  acc[r][j][0] = __fmaf_rn(p8[u], v[u].x, acc[r][j][0]);
-                  acc[r][j][1] = __fmaf_rn(p8[u], v[u].y, acc[r][j][1]);
+                  acc[r][0][0] = __fmaf_rn(p8[u], v[u].x, acc[r][0][0]);
+                  acc[r][0][1] = __fmaf_rn(p8[u], v[u].y, acc[r][0][1]);
                 }
               }
             }
