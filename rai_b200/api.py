@@ -110,6 +110,16 @@ def _u32(a: Sequence[int]) -> np.ndarray:
     return np.ascontiguousarray(np.asarray(a, dtype=np.uint32))
 
 
+def _addr(a: np.ndarray) -> int:
+    """Device-call address of a contiguous array's data (the buffer protocol
+    is several times cheaper than .ctypes / __array_interface__; read-only
+    or empty arrays take the slower route)."""
+    try:
+        return C.addressof(C.c_char.from_buffer(a))
+    except (TypeError, ValueError):
+        return a.__array_interface__["data"][0]
+
+
 class LookupDecoder:
     """Prompt-lookup decoder: n-gram draft, one batched verify, greedy accept,
     KV rollback -- all on the device."""
@@ -237,24 +247,37 @@ def prefill_many(decoders: Sequence[LookupDecoder], prompts: Sequence[Sequence[i
     return [int(v) for v in out]
 
 
+# numpy view of an array of LookupMetricsC (same field order and widths).
+_METRICS_DTYPE = np.dtype([("accepted", "<u4"), ("drafted", "<u4"), ("produced", "<u4"),
+                           ("matched_ngram", "<u4"), ("accept_rate", "<f4")])
+
+
 def step_many(decoders: Sequence[LookupDecoder], positions: Sequence[int], contexts: Sequence[Sequence[int]],
               config: LookupConfig):
-    """One step for each decoder (rai_gpu_step_many)."""
+    """One step for each decoder (rai_gpu_step_many). The per-stream
+    marshalling is kept short (context addresses through the buffer
+    protocol, results read through one numpy view each): about half the
+    host time per step of building ctypes objects stream by stream."""
     n = len(decoders)
     cap = config.max_draft + 1
     handles = (C.c_void_p * n)(*[d._h.value for d in decoders])
-    pos = (C.c_size_t * n)(*positions)
+    pos = np.ascontiguousarray(positions, dtype=np.uintp)
     arrs = [_u32(c) for c in contexts]
-    ctxp = (C.c_void_p * n)(*[a.ctypes.data for a in arrs])
-    lens = (C.c_size_t * n)(*[a.size for a in arrs])
+    ctxp = np.array([_addr(a) for a in arrs], dtype=np.uintp)
+    lens = np.array([a.size for a in arrs], dtype=np.uintp)
     out = np.zeros((n, cap), np.uint32)
-    nout = (C.c_size_t * n)()
-    mets = (native.LookupMetricsC * n)()
+    nout = np.zeros(n, np.uintp)
+    mets = np.zeros(n, _METRICS_DTYPE)
     cfg = config._c()
-    check(native.lib().rai_gpu_step_many(handles, n, pos, ctxp, lens, C.byref(cfg), out.ctypes.data_as(C.c_void_p),
-                                         cap, nout, mets))
-    return ([[int(t) for t in out[i, : nout[i]]] for i in range(n)],
-            [LookupMetrics._from_c(mets[i]) for i in range(n)])
+    check(native.lib().rai_gpu_step_many(handles, n, pos.ctypes.data_as(C.c_void_p),
+                                         ctxp.ctypes.data_as(C.c_void_p), lens.ctypes.data_as(C.c_void_p),
+                                         C.byref(cfg), out.ctypes.data_as(C.c_void_p), cap,
+                                         nout.ctypes.data_as(C.c_void_p), mets.ctypes.data_as(C.c_void_p)))
+    rows, counts = out.tolist(), nout.tolist()
+    acc, dr, pr = mets["accepted"].tolist(), mets["drafted"].tolist(), mets["produced"].tolist()
+    mg, ar = mets["matched_ngram"].tolist(), mets["accept_rate"].tolist()
+    return ([rows[i][: counts[i]] for i in range(n)],
+            [LookupMetrics(acc[i], dr[i], pr[i], ar[i], mg[i] or None) for i in range(n)])
 
 
 __all__ = ["RaiModel", "LookupDecoder", "LookupConfig", "LookupMetrics", "RaiError", "SpeculativeDecoder",
