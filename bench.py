@@ -40,6 +40,10 @@ import numpy as np
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
+# Bytes of the per-stream step record the library copies to the device and
+# back each step (sizeof(rai::StreamStep), rai_b200/csrc/layers.h).
+STREAM_STEP_BYTES = 312
+
 METRIC = "accepted tok/s per stream + verify-step us at k=8; W4A8 GEMM HBM GB/s vs peak"
 
 # BASELINE configs (BASELINE.json "configs"): model preset, streams, prompt
@@ -388,34 +392,22 @@ def main():
     max_ctx = CFG["prompt"] + (args.steps + args.warmup + 2) * (K_DRAFT + 1) + 16
     decs = [rai_b200.LookupDecoder(model, max_ctx) for _ in mine]
     ctxs = [prompt_for(CFG, 1000 + s, CFG["prompt"], vocab) for s in mine]
-    if tp_mode:
-        poss = [d.prefill(c) for d, c in zip(decs, ctxs)]
-    else:
-        poss = rai_b200.prefill_many(decs, ctxs)
+    # The streams' histories live in the StepBatch (the serving-loop API):
+    # a step is one C call on precomputed pointers plus a vectorized append.
+    batch = rai_b200.StepBatch(decs)
+    batch.prefill(ctxs, batched=not tp_mode)
     cfg = rai_b200.LookupConfig(max_draft=K_DRAFT, max_ngram=3, min_ngram=1)
-    # Each stream's token history lives in a preallocated uint32 buffer; the
-    # step gets views of it, so the call converts nothing on the host.
-    bufs = [np.zeros(max_ctx, np.uint32) for _ in mine]
-    lens = [len(c) for c in ctxs]
-    for b, c in zip(bufs, ctxs):
-        b[: len(c)] = c
+    # Host -> device per step: every stream's context slot (the library
+    # uploads the whole batch context buffer) and its step record.
+    h2d_step = len(decs) * (int(batch.windows.max()) * 4 + STREAM_STEP_BYTES)
 
     def one_step():
-        views = [b[:n] for b, n in zip(bufs, lens)]
         t0 = time.perf_counter()
-        toks, mets = rai_b200.step_many(decs, poss, views, cfg)
+        toks, counts, mets = batch.step(cfg)
         host_s = time.perf_counter() - t0
         dev_us = decs[0].last_step_us()
-        h2d = sum(4 * n for n in lens) + len(decs) * 288
-        produced = drafted = accepted = 0
-        for i, (t, met) in enumerate(zip(toks, mets)):
-            bufs[i][lens[i]: lens[i] + len(t)] = t
-            lens[i] += len(t)
-            poss[i] += len(t)
-            produced += met.produced
-            drafted += met.drafted
-            accepted += met.accepted
-        return dev_us, host_s, produced, drafted, accepted, h2d
+        return (dev_us, host_s, int(mets["produced"].sum()), int(mets["drafted"].sum()),
+                int(mets["accepted"].sum()), h2d_step)
 
     for _ in range(args.warmup):
         one_step()
@@ -470,7 +462,7 @@ def main():
             "tokens_per_step": produced / (total_streams * steps_per_stream),
             "accept_rate": accepted / drafted if drafted else 0.0,
             "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": int(h2d / args.steps),
-                    "d2h_bytes_per_step": int(288 * total_streams + 4)},
+                    "d2h_bytes_per_step": int(STREAM_STEP_BYTES * total_streams + 4)},
             "gpu_launches": launches * world,  # every rank launches the same step graph
             "roofline": {"bound": "hbm", "achieved": gem["gbs"], "peak": peak, "unit": "GB/s",
                          "frac": gem["gbs"] / peak, "traffic": traffic, "kernel": gem["kernel"],

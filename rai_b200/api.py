@@ -280,5 +280,75 @@ def step_many(decoders: Sequence[LookupDecoder], positions: Sequence[int], conte
             [LookupMetrics(acc[i], dr[i], pr[i], ar[i], mg[i] or None) for i in range(n)])
 
 
+class StepBatch:
+    """A fixed set of decoders stepped together, for serving loops: each
+    stream's token history lives in one array this object owns
+    (`history[i, :lengths[i]]`), so a step is one rai_gpu_step_many call on
+    precomputed pointers plus a vectorized append of the produced tokens,
+    instead of per-stream marshalling. Results are those of step_many on the
+    same histories and positions (the reference's step(pos, context) for
+    each stream, pos + 1 == len(context))."""
+
+    def __init__(self, decoders: Sequence[LookupDecoder]):
+        self.decoders = list(decoders)
+        n = len(self.decoders)
+        if n == 0:
+            raise ValueError("StepBatch needs at least one decoder")
+        # Each stream keeps its decoder's window: a step never takes it past
+        # position windows[i], so its history holds at most windows[i] + 1
+        # tokens.
+        self.windows = np.array([d.max_ctx for d in self.decoders], np.int64)
+        self._handles = (C.c_void_p * n)(*[d._h.value for d in self.decoders])
+        self._width = int(self.windows.max()) + 1
+        self.history = np.zeros((n, self._width), np.uint32)
+        self.lengths = np.zeros(n, np.uintp)
+        self.positions = np.zeros(n, np.uintp)
+        self._ptrs = (self.history.ctypes.data + np.arange(n, dtype=np.uintp) * (self._width * 4)).astype(np.uintp)
+        self._nout = np.zeros(n, np.uintp)
+        self._mets = np.zeros(n, _METRICS_DTYPE)
+        self._out = np.zeros((n, 1), np.uint32)
+
+    def prefill(self, prompts: Sequence[Sequence[int]], batched: bool = True) -> list:
+        """Prefill every decoder (prefill_many, or one prefill per decoder
+        when `batched` is false, e.g. for tensor-parallel shards); each
+        prompt becomes its stream's history. Returns the positions."""
+        if len(prompts) != len(self.decoders):
+            raise ValueError("one prompt per decoder")
+        arrs = [_u32(p) for p in prompts]
+        if any(a.size > w for a, w in zip(arrs, self.windows)):
+            raise ValueError("prompt longer than its decoder's context window")
+        if batched:
+            positions = prefill_many(self.decoders, arrs)
+        else:
+            positions = [d.prefill(a) for d, a in zip(self.decoders, arrs)]
+        for i, a in enumerate(arrs):
+            self.history[i, : a.size] = a
+            self.lengths[i] = a.size
+        self.positions[:] = positions
+        return positions
+
+    def step(self, config: LookupConfig):
+        """One step of every stream. Returns (tokens, counts, metrics): stream
+        i produced tokens[i, :counts[i]]; metrics is a structured array with
+        the LookupMetrics fields (matched_ngram 0 = none). The arrays are
+        reused by the next step."""
+        n = len(self.decoders)
+        cap = config.max_draft + 1
+        if self._out.shape[1] != cap:
+            self._out = np.zeros((n, cap), np.uint32)
+        cfg = config._c()
+        P = C.c_void_p
+        check(native.lib().rai_gpu_step_many(self._handles, n, self.positions.ctypes.data_as(P),
+                                             self._ptrs.ctypes.data_as(P), self.lengths.ctypes.data_as(P),
+                                             C.byref(cfg), self._out.ctypes.data_as(P), cap,
+                                             self._nout.ctypes.data_as(P), self._mets.ctypes.data_as(P)))
+        produced = self._nout.astype(np.int64)
+        r, c = np.nonzero(np.arange(cap)[None, :] < produced[:, None])
+        self.history[r, self.lengths[r].astype(np.int64) + c] = self._out[r, c]
+        self.lengths += self._nout
+        self.positions += self._nout
+        return self._out, self._nout, self._mets
+
+
 __all__ = ["RaiModel", "LookupDecoder", "LookupConfig", "LookupMetrics", "RaiError", "SpeculativeDecoder",
-           "step_many", "prefill_many"]
+           "StepBatch", "step_many", "prefill_many"]

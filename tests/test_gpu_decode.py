@@ -191,6 +191,42 @@ def test_step_many_matches_independent_oracle_streams(tiny_model_paths, oracle, 
             assert gds[i].kv_filled(0) == poss[i] == ods[i].kv_filled(0)
 
 
+@pytest.mark.parametrize("name", ["tiny-llama", "tiny-qwen"])
+def test_step_batch_matches_independent_oracle_streams(tiny_model_paths, oracle, name):
+    """StepBatch (the batch owns each stream's history and appends what a
+    step produces) gives every stream the oracle's tokens and metrics, and
+    its histories stay equal to the oracle's contexts, until a window fills."""
+    import rai_b200
+    gm = rai_b200.RaiModel.load(tiny_model_paths[name])
+    om = oracle.Model.load(tiny_model_paths[name])
+    vocab = gm.config["vocab_size"]
+    n = 4
+    windows = [48 + 8 * i for i in range(n)]
+    gds = [rai_b200.LookupDecoder(gm, w) for w in windows]
+    ods = [oracle.Decoder(om, w) for w in windows]
+    prompts = [periodic_prompt(20 + 5 * i, vocab, seed=200 + i) for i in range(n)]
+    batch = rai_b200.StepBatch(gds)
+    assert batch.windows.tolist() == windows
+    poss = batch.prefill(prompts)
+    assert poss == [od.prefill(p) for od, p in zip(ods, prompts)]
+    ctxs = [list(p) for p in prompts]
+    cfg = rai_b200.LookupConfig(max_draft=6, max_ngram=3, min_ngram=1)
+    steps = 0
+    while all(int(p) + 1 < w for p, w in zip(batch.positions, windows)):
+        toks, counts, mets = batch.step(cfg)
+        steps += 1
+        for i in range(n):
+            ot, om_ = ods[i].step(poss[i], ctxs[i], 6)
+            assert toks[i, : counts[i]].tolist() == ot, (i, poss[i])
+            assert (int(mets["accepted"][i]), int(mets["drafted"][i]), int(mets["produced"][i])) == \
+                (om_["accepted"], om_["drafted"], om_["produced"])
+            ctxs[i] += ot
+            poss[i] += len(ot)
+            assert batch.history[i, : int(batch.lengths[i])].tolist() == ctxs[i]
+            assert int(batch.positions[i]) == poss[i] == len(ctxs[i]) - 1
+    assert steps > 3
+
+
 def test_prefill_many_matches_separate_prefills(tiny_model_paths, oracle):
     import rai_b200
     gm = rai_b200.RaiModel.load(tiny_model_paths["tiny-llama"])
