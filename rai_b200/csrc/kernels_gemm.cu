@@ -29,6 +29,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <cstdlib>
 
 #include "common.cuh"
 #include "kernels.h"
@@ -45,13 +46,18 @@ namespace {
 // accumulators are independent, so neither split changes any rounding; the
 // LG warps of a slab meet once per work item to finish the horizontal sum.
 // MINB: CTAs per SM the launch is sized for; UNROLL: groups unrolled in the
-// consumer loop.
-template <int NT_, int LG_, int TS_, int MINB_, int UNROLL_>
+// consumer loop. SPLIT (for launches with fewer tiles than SMs): a 64-row
+// tile is shared by LG CTAs, each owning 4 / LG slabs with 4 consumer warps,
+// and a slab's LG lane groups sit on LG different warp schedulers, so each
+// SM carries 64 / LG rows and the per-group chain is cut LG ways.
+template <int NT_, int LG_, int TS_, int MINB_, int UNROLL_, bool SPLIT_ = false>
 struct GemmCfg {
   static constexpr int NTILES = NT_, LG = LG_, TS = TS_, kMinBlocks = MINB_, kUnroll = UNROLL_;
+  static constexpr bool SPLIT = SPLIT_;
   static_assert(LG == 1 || LG == 2 || LG == 4, "lane groups");
   static_assert(NTILES % TS == 0, "token split");
-  static constexpr int kConsumerWarps = 4 * LG * TS;
+  static_assert(!SPLIT || TS == 1, "a split tile has no token split");
+  static constexpr int kConsumerWarps = SPLIT ? 4 * TS : 4 * LG * TS;
   static constexpr int kThreads = (kConsumerWarps + 1) * 32;
   static constexpr int kTilesPerWarp = NTILES / TS;
   static constexpr int kPairs = 4 / LG;  // lane pairs per consumer warp
@@ -310,7 +316,8 @@ struct GemmParams {
   uint32_t* err;
   const int* m_dev;  // active token count (device); overrides M when set
   int rows, groups, M, tok_alloc, ld_out, mode, stages;
-  int tiles;  // 64-row tiles; work item i = (row tile i % tiles, token chunk i / tiles)
+  int tiles;  // work item i = (row tile i % tiles, token chunk i / tiles); tiles = 64-row tiles x split
+  int split;  // CTAs per 64-row tile (1, or the lane groups of a SPLIT variant)
   // Grouped (mixture-of-experts) form, when moe_off is set: ne weight sets of
   // the same shape at w + e * w_stride; expert e's tokens are activation rows
   // moe_off[e] .. moe_off[e] + moe_cnt[e] (moe_off[e] a multiple of 8).
@@ -330,10 +337,11 @@ struct GemmParams {
 
 constexpr int kMaxExperts = 256;
 
-// A work item: the weight set, 64-row tile and token range it covers.
+// A work item: the weight set, 64-row tile (and its part `sub` of `split`)
+// and token range it covers.
 struct GemmItem {
   const uint8_t* w;
-  int tile, t0, nt;
+  int tile, t0, nt, sub;
 };
 
 // Dense form: item = (row tile item % tiles, token chunk item / tiles).
@@ -343,7 +351,8 @@ __device__ __forceinline__ bool decode_item(const GemmParams& p, const int* cum,
   if (!p.moe_off) {
     const int t0 = (item / p.tiles) * kTokChunk;
     if (t0 >= mact) return false;
-    *it = GemmItem{p.w, item % p.tiles, t0, min(NT, mact - t0)};
+    const int x = item % p.tiles;
+    *it = GemmItem{p.w, x / p.split, t0, min(NT, mact - t0), x % p.split};
     return true;
   }
   if (item >= cum[p.ne]) return false;
@@ -351,7 +360,7 @@ __device__ __forceinline__ bool decode_item(const GemmParams& p, const int* cum,
   while (cum[e + 1] <= item) ++e;
   const int local = item - cum[e], chunk = local / p.tiles;
   *it = GemmItem{p.w + (size_t)e * p.w_stride, local % p.tiles, p.moe_off[p.moe_e0 + e] + chunk * kTokChunk,
-                 min(kTokChunk, p.moe_cnt[p.moe_e0 + e] - chunk * kTokChunk)};
+                 min(kTokChunk, p.moe_cnt[p.moe_e0 + e] - chunk * kTokChunk), 0};
   return true;
 }
 
@@ -498,7 +507,7 @@ __global__ void __launch_bounds__(Cfg::kThreads, Cfg::kMinBlocks) gemm_exact_ker
         for (int q = 0; q < pre; ++q) {
           const int g0 = q * kGPS, ng = min(kGPS, G - g0);
           mbar_expect_tx(&full[q], ng * kBlockBytes);
-          bulk_g2s(smem + (size_t)q * kStageBytes, p.w + ((size_t)blockIdx.x * G + g0) * kBlockBytes,
+          bulk_g2s(smem + (size_t)q * kStageBytes, p.w + ((size_t)(blockIdx.x / p.split) * G + g0) * kBlockBytes,
                    ng * kBlockBytes, &full[q]);
         }
         pdl_wait_prior();
@@ -560,12 +569,12 @@ __global__ void __launch_bounds__(Cfg::kThreads, Cfg::kMinBlocks) gemm_exact_ker
   }
   pdl_launch_dependents();
   const int gq = lane >> 2, tq = lane & 3;
-  const int slab = warp & 3;
-  const int lg = (warp >> 2) % LG;                     // lane group within the slab
-  const int team = slab + 4 * ((warp >> 2) / LG);      // (slab, token split)
-  const int r0 = slab * 16 + gq;                       // tile-local rows r0 and r0 + 8
-  const int nbase = ((warp >> 2) / LG) * NW;           // this warp's first N tile
-  const int j0 = lg * NP;                              // first lane pair
+  // SPLIT: warp w = (slab w / LG of the item's part, lane group w % LG).
+  const int lg = Cfg::SPLIT ? warp % LG : (warp >> 2) % LG;  // lane group within the slab
+  const int team = Cfg::SPLIT ? warp / LG : (warp & 3) + 4 * ((warp >> 2) / LG);  // (slab, token split)
+  const int nbase = Cfg::SPLIT ? 0 : ((warp >> 2) / LG) * NW;  // this warp's first N tile
+  const int j0 = lg * NP;                                      // first lane pair
+  int r0 = (warp & 3) * 16 + gq;                               // tile-local rows r0 and r0 + 8
   const uint64_t magic2 = f2(kMagicF, kMagicF);
   int cs = 0;           // ring stage of the next stage to consume
   uint32_t cphase = 0;  // its fill parity
@@ -574,6 +583,7 @@ __global__ void __launch_bounds__(Cfg::kThreads, Cfg::kMinBlocks) gemm_exact_ker
     GemmItem it;
     if (!decode_item<NT>(p, cum, mact, item, &it)) break;
     const int tile = it.tile, t0 = it.t0;
+    if constexpr (Cfg::SPLIT) r0 = (it.sub * (4 / LG) + warp / LG) * 16 + gq;
     const int nbi = (it.nt + 7) >> 3;  // 8-token blocks holding this item's tokens
     float facc[NW][NP][2][4];
     float zc[NW][4];
@@ -794,6 +804,8 @@ cudaError_t launch_gemm(const GemmParams& gp, int tiles, int chunks, cudaStream_
   const int stages = gemm_stages<Cfg>(gp.groups);
   GemmParams p = gp;
   p.stages = stages;
+  p.split = Cfg::SPLIT ? Cfg::LG : 1;
+  tiles *= p.split;
   p.tiles = tiles;
   auto kern = gemm_exact_kernel<WBITS, Cfg>;
   const size_t smem = gemm_smem_bytes<Cfg>(stages);
@@ -828,10 +840,29 @@ using Gemm4N1 = GemmCfg<1, 1, 1, 2, 4>;
 using Gemm4N2 = GemmCfg<2, 1, 1, 2, 1>;
 using Gemm4N3 = GemmCfg<3, 1, 1, 1, 1>;
 using Gemm4N4 = GemmCfg<4, 1, 2, 1, 1>;
+// Launches with fewer tiles than SMs: each 64-row tile split over 2 or 4
+// CTAs.
+using Gemm4N1S2 = GemmCfg<1, 2, 1, 2, 4, true>;
+using Gemm4N1S4 = GemmCfg<1, 4, 1, 2, 4, true>;
+using Gemm4N2S2 = GemmCfg<2, 2, 1, 2, 1, true>;
+using Gemm4N2S4 = GemmCfg<2, 4, 1, 2, 1, true>;
 using Gemm8N1 = GemmCfg<1, 1, 1, 2, 1>;
 using Gemm8N2 = GemmCfg<2, 1, 1, 2, 1>;
 using Gemm8N3 = GemmCfg<3, 1, 1, 1, 1>;
 using Gemm8N4 = GemmCfg<4, 1, 2, 1, 1>;
+
+// CTAs per 64-row tile for a launch of `items` (tile, token chunk) items:
+// 1 when the items fill the SMs, 2 or 4 when most SMs would otherwise idle.
+// RAI_GEMM_SPLIT=1|2|4 forces one.
+int gemm_split(long items) {
+  static const int forced = [] {
+    const char* e = std::getenv("RAI_GEMM_SPLIT");
+    return e ? std::atoi(e) : 0;
+  }();
+  if (forced == 1 || forced == 2 || forced == 4) return forced;
+  const long sms = sm_count();
+  return items * 4 <= sms ? 4 : items * 2 <= sms ? 2 : 1;
+}
 
 }  // namespace
 
@@ -844,6 +875,8 @@ cudaError_t init_gemm_attributes() {
   };
   set(gemm_exact_kernel<4, Gemm4N1>); set(gemm_exact_kernel<4, Gemm4N2>);
   set(gemm_exact_kernel<4, Gemm4N3>); set(gemm_exact_kernel<4, Gemm4N4>);
+  set(gemm_exact_kernel<4, Gemm4N1S2>); set(gemm_exact_kernel<4, Gemm4N1S4>);
+  set(gemm_exact_kernel<4, Gemm4N2S2>); set(gemm_exact_kernel<4, Gemm4N2S4>);
   set(gemm_exact_kernel<8, Gemm8N1>); set(gemm_exact_kernel<8, Gemm8N2>);
   set(gemm_exact_kernel<8, Gemm8N3>); set(gemm_exact_kernel<8, Gemm8N4>);
   if (e == cudaSuccess) e = init_gemm_tc_attributes();
@@ -969,9 +1002,16 @@ cudaError_t gemm_exact(const PackedLinear& w, const ActBuf& act, int M, float* o
   int chunks = (int)ceil_div(M, kTokChunk);
   (void)pdl;  // every GEMM launch uses programmatic dependent launch
   if (w.wbits == 4) {
+    const int split = gemm_split(w.tiles * chunks);
     switch (ntiles) {
-      case 1: return launch_gemm<4, Gemm4N1>(gp, w.tiles, chunks, s);
-      case 2: return launch_gemm<4, Gemm4N2>(gp, w.tiles, chunks, s);
+      case 1:
+        if (split == 4) return launch_gemm<4, Gemm4N1S4>(gp, w.tiles, chunks, s);
+        if (split == 2) return launch_gemm<4, Gemm4N1S2>(gp, w.tiles, chunks, s);
+        return launch_gemm<4, Gemm4N1>(gp, w.tiles, chunks, s);
+      case 2:
+        if (split == 4) return launch_gemm<4, Gemm4N2S4>(gp, w.tiles, chunks, s);
+        if (split == 2) return launch_gemm<4, Gemm4N2S2>(gp, w.tiles, chunks, s);
+        return launch_gemm<4, Gemm4N2>(gp, w.tiles, chunks, s);
       case 3: return launch_gemm<4, Gemm4N3>(gp, w.tiles, chunks, s);
       default: return launch_gemm<4, Gemm4N4>(gp, w.tiles, chunks, s);
     }
