@@ -171,12 +171,16 @@ class ClockSampler:
 
 
 def peaks():
-    try:
-        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
-            p = json.load(f)
-        return float(p["hbm_gbs"]), "measured"
-    except Exception:
-        return 6650.0, "fallback"
+    """HBM copy bandwidth measured on this pool's B200s: the per-pod file, or
+    the copy build() keeps beside the library; else the earlier pool
+    measurement (fallback)."""
+    for path in (os.path.join(ROOT, "MEASURED_PEAKS.json"), os.path.join(ROOT, "rai_b200", "measured_peaks.json")):
+        try:
+            with open(path) as f:
+                return float(json.load(f)["hbm_gbs"]), "measured"
+        except (OSError, ValueError, KeyError, TypeError):
+            continue
+    return 6650.0, "fallback"
 
 
 def gemm_traffic_from_profile():
