@@ -5,8 +5,10 @@ hidden 2048, 32/4 heads x 64, FFN 5632, vocab 32000), seeded synthetic
 weights RTN-quantized to the reference's .raimodel format; 64 independent
 streams with distinct seeds, each a 1024-token prompt of which 40% are spans
 copied from earlier positions; greedy prompt-lookup with k = 8
-(max_ngram 3, min_ngram 1). Streams are sharded data-parallel over the
-ranks (64 / N per GPU, no collective). A step = one lookup step
+(max_ngram 3, min_ngram 1). Streams are independent units, sharded
+data-parallel with no collective: on N GPUs every rank runs 64 streams of
+its own (64 N in all, weak scaling); --split-streams deals one 64-stream
+job over the ranks instead (64 / N per GPU, strong scaling). A step = one lookup step
 (draft + (k+1)-row verify + greedy accept + KV rollback) of every stream on
 the GPU. Weights (550 MB) exceed L2 (126 MB), so no flush is needed.
 
@@ -18,7 +20,8 @@ single GPU); --gemm-sweep runs config 5 (isolated W4A8 GEMM at the
 Llama-3.1-8B shapes, M in {1..512}). With N > 1 GPUs config 3 runs tensor
 parallel (tpN: every rank holds a column-parallel shard and all ranks run
 the same stream; exchanges over NVLink), config 4 expert parallel (epN:
-64/N experts per rank, attention replicated), the others data parallel.
+64/N experts per rank, attention replicated), the others data parallel
+(config 1: one independent replica stream per GPU).
 
 Prints one JSON line (rank 0). `value` = tokens produced by all streams per
 second of device time (CUDA events around each step's graph, max over ranks);
@@ -52,10 +55,10 @@ METRIC = "accepted tok/s per stream + verify-step us at k=8; W4A8 GEMM HBM GB/s 
 CONFIGS = {
     "tinyllama": dict(preset="tinyllama-1.1b", streams=64, prompt=1024, recipe=("copy", 0.40), k=8,
                       gemm=(2 * 5632, 2048), cpu_prompt=1024,
-                      desc="64 streams, 1024-token prompts (40% copied spans)"),
+                      desc="64 streams per GPU, 1024-token prompts (40% copied spans)"),
     "qwen": dict(preset="qwen2.5-0.5b", streams=1, prompt=256, recipe=("spans", 3, 24), k=8,
                  gemm=(2 * 4864, 896), cpu_prompt=256,
-                 desc="1 stream, 256-token prompt with three copied 24-token spans"),
+                 desc="1 stream per GPU, 256-token prompt with three copied 24-token spans"),
     "llama8b": dict(preset="llama3.1-8b", streams=1, prompt=2048, recipe=("random",), k=8,
                     gemm=(2 * 14336, 4096), cpu_prompt=64, tp=True,
                     desc="1 stream, 2048 random prompt tokens"),
@@ -302,13 +305,17 @@ def run_reference(args):
     O.build()
     tps, produced, dt, sample = cpu_baseline_run(args.steps, args.warmup)
     cores = O.num_threads()
+    # The same job accounting as this bench's own arm at N GPUs (weak
+    # scaling: the config's streams on every GPU); the host's job rate is its
+    # per-stream rate whatever the stream count.
+    weak = not (args.gpus > 1 and CFG.get("tp", False)) and not args.split_streams
     line = {
         "impl": "reference", "metric": METRIC, "value": tps, "unit": "tok/s", "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt * 1e3 / args.steps,
-        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "int8xu4->int32->f32",
-        "data": "synthetic",
+        "higher_is_better": True, "scaling": "weak" if weak else "strong", "vs_baseline": None,
+        "dtype": "int8xu4->int32->f32", "data": "synthetic",
         "config": {"workload": f"{CFG['preset']} prompt-lookup k={CFG['k']}: {CFG['desc']}, greedy",
-                   "streams": CFG["streams"], "sample": sample},
+                   "streams": CFG["streams"] * (args.gpus if weak else 1), "sample": sample},
         "cpu_baseline": {"value": tps, "unit": "tok/s", "cores": cores, "kind": "port", "sample": sample},
         "e2e": {"value": tps, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
@@ -324,6 +331,9 @@ def main():
     ap.add_argument("--config", default="tinyllama", choices=sorted(CONFIGS),
                     help="BASELINE config (default: config 2, the headline)")
     ap.add_argument("--streams", type=int, default=None, help="override the config's stream count")
+    ap.add_argument("--split-streams", action="store_true",
+                    help="data parallel: deal the config's streams over the ranks (strong scaling) instead of "
+                         "running them on every rank (weak scaling)")
     ap.add_argument("--gemm-sweep", action="store_true",
                     help="BASELINE config 5: isolated W4A8 GEMM sweep at the Llama-3.1-8B shapes")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -363,7 +373,8 @@ def main():
     if world > 1:
         import datetime
         import torch.distributed as dist
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600))
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
+                                device_id=torch.device("cuda", local))
 
     def barrier():
         if dist:
@@ -375,6 +386,9 @@ def main():
     from rai_b200 import native
     import ctypes as C
 
+    if args.split_streams and not CFG.get("tp", False) and CFG["streams"] < world:
+        # Every rank sees the same condition, so all of them stop here.
+        raise SystemExit(f"--split-streams: {CFG['streams']} streams cannot cover {world} ranks")
     path = model_path(rank, world)
     if dist:
         dist.barrier()
@@ -388,9 +402,13 @@ def main():
         mine = list(range(CFG["streams"]))
         if not CFG.get("ep"):
             CFG["gemm"] = (CFG["gemm"][0] // world, CFG["gemm"][1])
-    else:
+    elif args.split_streams:
         model = rai_b200.RaiModel.load(path, device=local)
         mine = [s for s in range(CFG["streams"]) if s % world == rank]
+    else:
+        # Weak scaling: this rank's own streams (distinct seeds across ranks).
+        model = rai_b200.RaiModel.load(path, device=local)
+        mine = [rank * CFG["streams"] + s for s in range(CFG["streams"])]
     vocab = model.config["vocab_size"]
     K_DRAFT = CFG["k"]
     max_ctx = CFG["prompt"] + (args.steps + args.warmup + 2) * (K_DRAFT + 1) + 16
@@ -447,19 +465,22 @@ def main():
         wmb = convert.weight_bytes_per_step(convert.PRESETS[CFG["preset"]]) / 1e6
         value = produced / dev_s
         e2e = produced / host_s
-        total_streams = CFG["streams"]
+        weak = not tp_mode and not args.split_streams
+        total_streams = CFG["streams"] * (world if weak else 1)
         steps_per_stream = args.steps
         line = {
             "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": dev_s * 1e3 / args.steps, "higher_is_better": True,
-            "scaling": "strong", "vs_baseline": None, "dtype": "int8xu4->int32->f32", "data": "synthetic",
+            "scaling": "weak" if weak else "strong", "vs_baseline": None, "dtype": "int8xu4->int32->f32",
+            "data": "synthetic",
             "config": {"workload": f"{CFG['preset']} prompt-lookup k={K_DRAFT}: {CFG['desc']}, greedy",
-                       "streams": total_streams, "k": K_DRAFT,
+                       "streams": total_streams, "streams_per_gpu": len(mine), "k": K_DRAFT,
                        "parallelism": (f"ep{world} ({64 // world} experts per rank, attention replicated; expert "
                                        "rows written into every rank over NVLink)") if tp_mode and CFG.get("ep") else
                                       (f"tp{world} (column-parallel shards, NVLink exchanges fused into the "
                                        "kernels; every rank runs every stream)") if tp_mode else
-                                      f"dp{world} (streams sharded; each GPU batches its streams' verify rows)",
+                                      (f"dp{world} ({len(mine)} streams per GPU, no collective; each GPU batches "
+                                       "its streams' verify rows)"),
                        "l2": f"weights {wmb:.0f} MB (+ KV) per step > L2 126 MB; no flush needed"},
             "per_stream_tok_s": produced / dev_s / total_streams,
             "verify_step_us": dev_s * 1e6 / steps_per_stream,
