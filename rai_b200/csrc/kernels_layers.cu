@@ -27,6 +27,8 @@ namespace rai {
 __device__ __forceinline__ int active_rows(const int* m_dev, int M) { return m_dev ? *m_dev : M; }
 
 constexpr int kPvMaxStages = 4;
+constexpr int kPvMaxThreads = 512 + 32;  // P.V compute threads + the producer warp
+constexpr int kPvMaxThreadsH2 = 256 + 32;  // ... with two heads per thread (hd <= 128, hpk <= 8)
 constexpr int kPvStepHeads = 2;  // heads per P.V thread for short segments
 constexpr int kPvStepRows = 4;   // ... of at most this many rows
 
@@ -340,21 +342,75 @@ __global__ void __launch_bounds__(256) attn_softmax_kernel(const RowInfo* __rest
 // would otherwise bound the kernel); positions are taken 8 at a time with
 // all loads issued before the FMAs. V and p tiles
 // stream through a ring of `ns` shared-memory stages filled by bulk copies
-// (warp 0) that complete on mbarriers. Row r only takes positions
-// t <= pos0 + r.
+// that complete on mbarriers ("full"). The copies are issued by a producer
+// warp (the CTA's last warp), which refills a stage once every compute warp
+// has released it (one "empty" mbarrier per stage), so neither the issue of
+// a tile's 1 + rows x heads copies nor a CTA-wide barrier sits between the
+// compute warps' tiles. Row r only takes positions t <= pos0 + r.
 template <int HD>
 struct PvCfg {
   static constexpr int VT = HD >= 128 ? 32 : 64;  // positions per tile
 };
 
-// The stage ring persists across the segments a CTA handles: `head` is the
-// next stage to consume (stages fill in the same order) and bit s of `bits`
-// is the parity stage s's next fill completes.
+// The producer warp walks the CTA's segments and tiles in the compute warps'
+// order. Fill f goes to stage f % ns; from the second round on it first
+// waits (bounded) until the compute warps released the stage's previous
+// tile. If a wait gives up it lets its fills still in flight land (bounded)
+// and returns, so no copy outlives the CTA.
+template <int HD>
+__device__ __forceinline__ void pv_produce(const StreamKV* __restrict__ kv, int layer,
+                                           const AttnSeg* __restrict__ segs, int nseg, int nh, int nkv, int hpk,
+                                           int kvh, const float* __restrict__ p, int n_alloc, int rb_alloc, int ns,
+                                           float* sm, uint64_t* full, uint64_t* empty, uint32_t* err) {
+  constexpr int VT = PvCfg<HD>::VT;
+  const int lane = threadIdx.x & 31;
+  const int stage_floats = VT * HD + rb_alloc * hpk * VT;
+  int st = 0;          // stage of the next fill
+  uint32_t ebits = 0;  // bit s: parity of stage s's next release
+  int fills = 0;
+  for (int si = blockIdx.y; si < nseg; si += gridDim.y) {
+    const AttnSeg sg = segs[si];
+    const StreamKV sk_ = kv[sg.stream];
+    const float* vbase = sk_.v + ((size_t)layer * nkv + kvh) * sk_.max_ctx * HD;
+    const float* prow0 = p + ((size_t)sg.row0 * nh + (size_t)kvh * hpk) * n_alloc;
+    const int nrows = sg.nrows, n_max = sg.pos0 + nrows, ntiles = (n_max + VT - 1) / VT;
+    for (int tile = 0; tile < ntiles; ++tile) {
+      if (fills >= ns) {
+        const bool ok = mbar_wait(&empty[st], (ebits >> st) & 1u, err);
+        ebits ^= 1u << st;
+        if (!__all_sync(0xffffffffu, ok)) {
+          if (lane == 0)
+            for (int f = fills > ns ? fills - ns : 0; f < fills; ++f)
+              mbar_wait(&full[f % ns], (uint32_t)(f / ns) & 1u, nullptr);
+          return;
+        }
+      }
+      const int t0 = tile * VT, cnt = min(VT, n_max - t0), c4 = (cnt + 3) / 4;
+      float* sv = sm + (size_t)st * stage_floats;
+      float* sp = sv + VT * HD;
+      if (lane == 0) {
+        mbar_arrive_expect_tx(&full[st], (uint32_t)(cnt * HD * 4 + nrows * hpk * c4 * 16));
+        bulk_g2s(sv, vbase + (size_t)t0 * HD, (uint32_t)(cnt * HD * 4), &full[st]);
+      }
+      __syncwarp();
+      for (int i = lane; i < nrows * hpk; i += 32) {
+        const int r = i / hpk, hh = i - r * hpk;
+        bulk_g2s(sp + i * VT, prow0 + ((size_t)r * nh + hh) * n_alloc + t0, (uint32_t)(c4 * 16), &full[st]);
+      }
+      ++fills;
+      if (++st == ns) st = 0;
+    }
+  }
+}
+
+// A compute warp's tiles of one segment. The stage ring persists across the
+// segments a CTA handles: `head` is the next stage to consume and bit s of
+// `bits` is the parity stage s's next fill completes. Returns false (output
+// not written) if a wait gave up.
 template <int HD, int RB, int HPT>
-__device__ __forceinline__ bool pv_body(const float* __restrict__ vbase, const float* __restrict__ p, int nh,
-                                        int hpk, int kvh, const AttnSeg& sg, int n_alloc, int rb_alloc, int ns,
-                                        float* __restrict__ out, float* sm, uint64_t* bars, uint32_t* err,
-                                        int& head, uint32_t& bits) {
+__device__ __forceinline__ bool pv_consume(int nh, int hpk, int kvh, const AttnSeg& sg, int rb_alloc, int ns,
+                                           float* __restrict__ out, const float* sm, uint64_t* full,
+                                           uint64_t* empty, uint32_t* err, int& head, uint32_t& bits) {
   constexpr int VT = PvCfg<HD>::VT;
   constexpr int NDP = HD / 2;
   const int stage_floats = VT * HD + rb_alloc * hpk * VT;
@@ -368,41 +424,17 @@ __device__ __forceinline__ bool pv_body(const float* __restrict__ vbase, const f
   const int nrows = sg.nrows;
   const int n_max = sg.pos0 + nrows, n_all = sg.pos0 + 1;
   const int ntiles = (n_max + VT - 1) / VT;
-  const float* prow0 = p + ((size_t)sg.row0 * nh + (size_t)kvh * hpk) * n_alloc;
-  // Warp 0 fills stage `st` with tile `tile`.
-  auto issue = [&](int tile, int st) {
-    const int t0 = tile * VT, cnt = min(VT, n_max - t0), c4 = (cnt + 3) / 4;
-    float* sv = sm + (size_t)st * stage_floats;
-    float* sp = sv + VT * HD;
-    if (lane == 0) {
-      mbar_arrive_expect_tx(&bars[st], (uint32_t)(cnt * HD * 4 + nrows * hpk * c4 * 16));
-      bulk_g2s(sv, vbase + (size_t)t0 * HD, (uint32_t)(cnt * HD * 4), &bars[st]);
-    }
-    __syncwarp();
-    for (int i = lane; i < nrows * hpk; i += 32) {
-      const int r = i / hpk, hh = i - r * hpk;
-      bulk_g2s(sp + i * VT, prow0 + ((size_t)r * nh + hh) * n_alloc + t0, (uint32_t)(c4 * 16), &bars[st]);
-    }
-  };
-  if (tid < 32) {
-    int f = head;
-    for (int j = 0; j < ns && j < ntiles; ++j) {
-      issue(j, f);
-      if (++f == ns) f = 0;
-    }
-  }
   float acc[RB][HPT][2];
 #pragma unroll
   for (int r = 0; r < RB; ++r)
 #pragma unroll
     for (int j = 0; j < HPT; ++j) acc[r][j][0] = acc[r][j][1] = 0.f;
-  int tile = 0;
-  for (; tile < ntiles; ++tile) {
+  for (int tile = 0; tile < ntiles; ++tile) {
     const int st = head;
-    const bool ok = mbar_wait(&bars[st], (bits >> st) & 1u, err);
+    const bool ok = mbar_wait(&full[st], (bits >> st) & 1u, err);
     bits ^= 1u << st;
     if (++head == ns) head = 0;
-    if (!__syncthreads_and(ok)) break;
+    if (!__all_sync(0xffffffffu, ok)) return false;
     const int t0 = tile * VT, cnt = min(VT, n_max - t0);
     const float* sv = sm + (size_t)st * stage_floats + d0;
     // p of (row r, head h0 + j) at ph + (r * hpk + j) * VT.
@@ -496,23 +528,9 @@ __device__ __forceinline__ bool pv_body(const float* __restrict__ vbase, const f
         }
       }
     }
-    __syncthreads();
-    if (tid < 32 && tile + ns < ntiles) issue(tile + ns, st);
-  }
-  if (tile < ntiles) {
-    // A wait gave up (tile's stage was already retired above): let this
-    // CTA's other copies still in flight land (bounded) before the CTA
-    // exits; the output is not written.
-    if (tid == 0) {
-      int h2 = head;
-      uint32_t b2 = bits;
-      for (int j = tile + 1; j < ntiles && j < tile + ns; ++j) {
-        mbar_wait(&bars[h2], (b2 >> h2) & 1u, nullptr);
-        b2 ^= 1u << h2;
-        if (++h2 == ns) h2 = 0;
-      }
-    }
-    return false;
+    // This warp is done with the stage.
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[st]);
   }
   if (active) {
 #pragma unroll
@@ -527,9 +545,9 @@ __device__ __forceinline__ bool pv_body(const float* __restrict__ vbase, const f
 }
 
 // HPT > 1 serves segments of at most kPvStepRows rows (the launch
-// guarantees it).
+// guarantees it). Block: the compute warps plus one producer warp.
 template <int HD, int HPT>
-__global__ void __launch_bounds__(512) attn_pv_kernel(const StreamKV* __restrict__ kv, int layer,
+__global__ void __launch_bounds__(HPT > 1 ? kPvMaxThreadsH2 : kPvMaxThreads) attn_pv_kernel(const StreamKV* __restrict__ kv, int layer,
                                                       const AttnSeg* __restrict__ segs, const int* nseg_dev,
                                                       int nseg_max, int nh, int nkv, const float* __restrict__ p,
                                                       int n_alloc, int rb_alloc, int ns, float* __restrict__ out,
@@ -537,24 +555,30 @@ __global__ void __launch_bounds__(512) attn_pv_kernel(const StreamKV* __restrict
   pdl_wait_prior();
   pdl_launch_dependents();
   extern __shared__ __align__(16) float sm[];
-  __shared__ __align__(8) uint64_t bars[kPvMaxStages];
+  __shared__ __align__(8) uint64_t full[kPvMaxStages], empty[kPvMaxStages];
   const int kvh = blockIdx.x;
   const int nseg = active_rows(nseg_dev, nseg_max);
   if ((int)blockIdx.y >= nseg) return;
   const int hpk = nh / nkv;
+  const int ncw = (int)(blockDim.x >> 5) - 1;  // compute warps
   if (threadIdx.x == 0) {
-    for (int s = 0; s < ns; ++s) mbar_init(&bars[s], 1);
+    for (int s = 0; s < ns; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], (uint32_t)ncw);
+    }
     fence_barrier_init();
   }
   __syncthreads();
+  if ((int)(threadIdx.x >> 5) == ncw) {
+    pv_produce<HD>(kv, layer, segs, nseg, nh, nkv, hpk, kvh, p, n_alloc, rb_alloc, ns, sm, full, empty, err);
+    return;
+  }
   int head = 0;
   uint32_t bits = 0;
   for (int si = blockIdx.y; si < nseg; si += gridDim.y) {
     const AttnSeg sg = segs[si];
-    const StreamKV sk_ = kv[sg.stream];
-    const float* vbase = sk_.v + ((size_t)layer * nkv + kvh) * sk_.max_ctx * HD;
     bool ok;
-#define RAI_PV(RB) pv_body<HD, RB, HPT>(vbase, p, nh, hpk, kvh, sg, n_alloc, rb_alloc, ns, out, sm, bars, err, head, bits)
+#define RAI_PV(RB) pv_consume<HD, RB, HPT>(nh, hpk, kvh, sg, rb_alloc, ns, out, sm, full, empty, err, head, bits)
     if (sg.nrows <= 1) ok = RAI_PV(1);
     else if (sg.nrows <= 2) ok = RAI_PV(2);
     else if (sg.nrows <= 4) ok = RAI_PV(4);
@@ -567,7 +591,6 @@ __global__ void __launch_bounds__(512) attn_pv_kernel(const StreamKV* __restrict
     }
 #undef RAI_PV
     if (!ok) return;
-    __syncthreads();  // the stages are refilled for the next segment
   }
 }
 
@@ -931,7 +954,9 @@ size_t pv_stage_bytes(int hd, int hpk, int rb_alloc) {
 int pv_heads_per_thread(int hpk, int seg_rows, int nseg_max, int nkv) {
   return seg_rows <= kPvStepRows && nseg_max * nkv >= 4 * device_sm_count() ? std::min(hpk, kPvStepHeads) : 1;
 }
-int pv_threads(int hd, int hpk, int hpt) { return ((hd / 2) * ((hpk + hpt - 1) / hpt) + 31) / 32 * 32; }
+// P.V block: the compute threads (dim pair x head group), whole warps, plus
+// the producer warp.
+int pv_threads(int hd, int hpk, int hpt) { return ((hd / 2) * ((hpk + hpt - 1) / hpt) + 31) / 32 * 32 + 32; }
 // Head-dimension slices of the split P.V: the most (up to kPvsMaxSlices, at
 // least 4 columns each) that keep the launch within two CTAs per SM, and at
 // least enough for a CTA of at most 256 threads (HDS x hpk), when the
@@ -999,7 +1024,7 @@ cudaError_t launch_attention(const float* q, float* out, const StreamKV* kv, int
   const int ds = pv_dim_slices(hd, hpk, nseg_max, nkv);
   const int t3s = ((hd / ds) * hpk + 31) / 32 * 32;
   const size_t sm3s = pvs_smem_bytes(hd, ds, hpk, seg_rows);
-  if (hb < 1 || sm1 > kAttnMaxSmem || sm3 > kAttnMaxSmem || t3 > 512 ||
+  if (hb < 1 || sm1 > kAttnMaxSmem || sm3 > kAttnMaxSmem || t3 > (hpt > 1 ? kPvMaxThreadsH2 : kPvMaxThreads) ||
       (ds > 1 && (sm3s > kAttnMaxSmem || t3s > 256)))
     return cudaErrorInvalidValue;
   const size_t sm2 = (size_t)hb * n_alloc * sizeof(float);
