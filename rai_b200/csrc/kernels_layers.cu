@@ -210,9 +210,21 @@ __global__ void __launch_bounds__(ScoreCfg<HD>::CHUNK) attn_scores_kernel(
   }
   asm volatile("cp.async.commit_group;" ::: "memory");
   const int per_row = hpk * HD;
-  for (int i = tid; i < sg.nrows * per_row; i += CH) {
-    const int r = i / per_row, o = i - r * per_row;
-    sq[i] = q[(size_t)(sg.row0 + r) * nh * HD + (size_t)kvh * per_row + o];
+  if ((reinterpret_cast<uintptr_t>(q) & 15u) == 0) {
+    // The segment's q rows as 16-byte asynchronous copies beside the K
+    // chunk's (row strides are multiples of 4 floats), rather than one
+    // dependent global load per element before the barrier.
+    const int pr4 = per_row / 4;
+    for (int i = tid; i < sg.nrows * pr4; i += CH) {
+      const int r = i / pr4, o4 = i - r * pr4;
+      cp_async16(sq + 4 * i, q + (size_t)(sg.row0 + r) * nh * HD + (size_t)kvh * per_row + 4 * o4);
+    }
+    cp_async_commit();
+  } else {
+    for (int i = tid; i < sg.nrows * per_row; i += CH) {
+      const int r = i / per_row, o = i - r * per_row;
+      sq[i] = q[(size_t)(sg.row0 + r) * nh * HD + (size_t)kvh * per_row + o];
+    }
   }
   asm volatile("cp.async.wait_group 0;" ::: "memory");
   __syncthreads();
