@@ -173,6 +173,15 @@ class ClockSampler:
                 "reasons": reasons, "samples": len(sm), "source": "nvml, 10 ms"}
 
 
+def streams_for_rank(n: int, world: int, rank: int, split: bool) -> list:
+    """Global ids of the streams rank `rank` of `world` runs: its own `n`
+    (weak scaling: n * world streams in all, distinct seeds), or with
+    `split` its round-robin share of one n-stream job."""
+    if split:
+        return [s for s in range(n) if s % world == rank]
+    return [rank * n + s for s in range(n)]
+
+
 def peaks():
     """HBM copy bandwidth measured on this pool's B200s: the per-pod file, or
     the copy build() keeps beside the library; else the earlier pool
@@ -401,13 +410,9 @@ def main():
         mine = list(range(CFG["streams"]))
         if not CFG.get("ep"):
             CFG["gemm"] = (CFG["gemm"][0] // world, CFG["gemm"][1])
-    elif args.split_streams:
-        model = rai_b200.RaiModel.load(path, device=local)
-        mine = [s for s in range(CFG["streams"]) if s % world == rank]
     else:
-        # Weak scaling: this rank's own streams (distinct seeds across ranks).
         model = rai_b200.RaiModel.load(path, device=local)
-        mine = [rank * CFG["streams"] + s for s in range(CFG["streams"])]
+        mine = streams_for_rank(CFG["streams"], world, rank, args.split_streams)
     vocab = model.config["vocab_size"]
     K_DRAFT = CFG["k"]
     max_ctx = CFG["prompt"] + (args.steps + args.warmup + 2) * (K_DRAFT + 1) + 16
