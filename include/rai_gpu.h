@@ -116,7 +116,12 @@ RAI_API int rai_gpu_model_info(const rai_model* model, rai_model_info* info);
  * tokens. Mixture-of-experts models are split by experts instead (expert
  * parallel: whole experts per rank, attention and head replicated). Not on
  * multi-GPU models: rai_gpu_prefill_many; not under tensor parallelism:
- * rai_gpu_forward_logits and sampled acceptance. */
+ * rai_gpu_forward_logits and sampled acceptance.
+ * Cross-GPU waits are bounded (about a second). When one times out (a rank
+ * that stopped making the same calls) the call returns RAI_ERR_TIMEOUT and
+ * the model is failed for good: every later call that would run it returns
+ * RAI_ERR_TIMEOUT, because the ranks no longer agree on which exchange is
+ * which. Recover by destroying and re-creating the model on every rank. */
 RAI_API int rai_gpu_model_create_tp(const uint8_t* blob, size_t len, int device, int tp_rank, int tp_size,
                                     rai_model** out);
 RAI_API int rai_gpu_tp_handle(rai_model* model, void* handle, size_t cap);
@@ -226,6 +231,13 @@ RAI_API int rai_gpu_w4a8_matmul(float* out, const void* packed, const float* inp
                         size_t cols, size_t tokens, size_t group_size, void* scratch,
                         size_t scratch_bytes, void* stream);
 
+/* Status of the kernel-level calls on the current device (the w4a8 GEMM
+ * entries), which return as soon as their kernels are queued: synchronizes
+ * `stream`, then returns RAI_ERR_TIMEOUT if one of their bounded device waits
+ * gave up since the last query (that call's output is incomplete), else
+ * RAI_OK. The status word is per device and cleared by the query. */
+RAI_API int rai_gpu_kernel_status(void* stream);
+
 /* rai_gpu_w4a8_matmul without a caller scratch buffer and without any
  * allocation: the quantized activations go to a 2 MiB file-scope device
  * array of the library (one per device). No reference counterpart: this
@@ -267,6 +279,13 @@ RAI_API int rai_gpu_attention(const float* q, const float* k, const float* v, co
 RAI_API int rai_gpu_sample_accept(const float* logits, const float* draft_logits, size_t vocab,
                                   const uint32_t* draft, size_t n_drafted, float temperature, uint64_t seed,
                                   uint64_t step, uint32_t* out, size_t* n_out, size_t* accepted);
+
+/* The library's reproduction of the host libm expf (the reference's
+ * f32::exp in its softmax tails and router, rai-infer/src/layers.rs:
+ * 1266-1380, 1808-1870) on the device: out[i] (device) = expf of the float
+ * whose bit pattern is first_bits + i, for i < n (first_bits + n <= 2^32).
+ * For checking it against the host libm over every input. */
+RAI_API int rai_gpu_expf_range(uint32_t first_bits, size_t n, float* out, void* stream);
 
 /* Number of kernels one rai_gpu_step replays (the captured CUDA graph's
  * kernel nodes for the decoder's current configuration; 0 before the first

@@ -78,6 +78,11 @@ def _declare(L):
     L.orc_last_error.argtypes = [C.c_char_p, SZ]
     L.orc_last_error.restype = SZ
     L.orc_num_threads.restype = C.c_int
+    L.orc_expf_range.argtypes = [C.c_uint32, SZ, P]
+    L.orc_rtn_quantize.argtypes = [P, SZ, SZ, C.c_int, SZ, P, P]
+    L.orc_rtn_quantize.restype = C.c_int
+    L.orc_synth_normal_f16.argtypes = [C.c_uint64, C.c_uint64, SZ, F, P]
+    L.orc_synth_normal_f16.restype = C.c_int
 
 
 def _p(a: np.ndarray):
@@ -210,6 +215,48 @@ def find_ngram_draft(tokens, min_ngram, max_ngram, max_draft):
 def argmax(v) -> int:
     v = np.ascontiguousarray(v, np.float32)
     return int(lib().orc_argmax(_p(v), v.size))
+
+
+def expf_range(first: int, n: int) -> np.ndarray:
+    """glibc expf of the floats with bit patterns first .. first + n - 1."""
+    out = np.empty(n, np.float32)
+    lib().orc_expf_range(first, n, _p(out))
+    return out
+
+
+# ---- synthetic model writing ----------------------------------------------
+
+def rtn_quantize(w: np.ndarray, bits: int, group_size: int):
+    """`rai convert`'s RTN quantizer (convert.rs:2551-2639); returns
+    (params, codes) bytes in the .raimodel layout."""
+    w = np.ascontiguousarray(w, np.float32)
+    rows, cols = w.shape
+    ng = -(-cols // group_size)
+    params = np.empty(rows * ng * 4, np.uint8)
+    codes = np.empty(rows * (cols // 2 if bits == 4 else cols), np.uint8)
+    if lib().orc_rtn_quantize(_p(w), rows, cols, bits, group_size, _p(params), _p(codes)) != 0:
+        raise ValueError("rtn_quantize: bad arguments or a non-finite weight")
+    return params.tobytes(), codes.tobytes()
+
+
+class WriterBackend:
+    """Weight source and quantizer for rai_b200.convert.write_synthetic
+    (fast=True layout and draws) that runs on oracle code only."""
+
+    def __init__(self, seed: int):
+        self.seed = seed
+        self.stream = 0
+
+    def normal(self, shape, std=0.02) -> np.ndarray:
+        n = int(np.prod(shape))
+        out = np.empty(n, np.float32)
+        lib().orc_synth_normal_f16(self.seed, self.stream, n, std, _p(out))
+        self.stream += 1
+        return out.reshape(shape)
+
+    @staticmethod
+    def quantize(w, bits, group_size):
+        return rtn_quantize(w, bits, group_size)
 
 
 # ---- model / decoder -------------------------------------------------------

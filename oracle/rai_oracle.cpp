@@ -669,6 +669,18 @@ size_t orc_argmax(const float* v, size_t n) {
 }
 
 int orc_num_threads(void) { return omp_get_max_threads(); }
+
+// f32::exp as the reference runs it (glibc expf) for the floats with bit
+// patterns first .. first + n - 1.
+void orc_expf_range(uint32_t first, size_t n, float* out) {
+#pragma omp parallel for schedule(static)
+  for (size_t i = 0; i < n; ++i) {
+    const uint32_t b = first + (uint32_t)i;
+    float x;
+    std::memcpy(&x, &b, 4);
+    out[i] = expf(x);
+  }
+}
 void orc_set_num_threads(int n) { if (n > 0) omp_set_num_threads(n); }
 
 size_t orc_last_error(char* buf, size_t len) {

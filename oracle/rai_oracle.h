@@ -70,7 +70,19 @@ void orc_kv_truncate(orc_decoder* d, size_t len);
 int orc_kv_read(const orc_decoder* d, size_t layer, size_t kv_head, size_t pos, float* k,
                 float* v);
 size_t orc_last_error(char* buf, size_t len);
+
+/* ---- synthetic model writing (oracle/model_writer.cpp) ---- */
+/* quantize_row (rai-infer/src/convert.rs:2551-2639) over a [rows][cols]
+   matrix; params rows*ceil(cols/gs)*4 bytes, codes rows*cols/2 (bits 4) or
+   rows*cols (bits 8). 0 ok, -1 on bad arguments or a non-finite weight. */
+int orc_rtn_quantize(const float* w, size_t rows, size_t cols, int bits, size_t gs, uint8_t* params,
+                     uint8_t* codes);
+/* The synthetic models' seeded N(0, stddev) source, f16-rounded. */
+int orc_synth_normal_f16(uint64_t seed, uint64_t stream, size_t n, float stddev, float* out);
 int orc_num_threads(void);
+/* glibc expf (the reference's f32::exp) of the floats with bit patterns
+   first .. first + n - 1. */
+void orc_expf_range(uint32_t first, size_t n, float* out);
 void orc_set_num_threads(int n);
 
 #ifdef __cplusplus

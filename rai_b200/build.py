@@ -44,10 +44,24 @@ def _digest() -> str:
 EXPF_TABLE = os.path.join(HERE, "expf_exceptions.bin")
 
 
+def _expf_table_current() -> bool:
+    """The table has the versioned layout and was made with this glibc."""
+    try:
+        with open(EXPF_TABLE, "rb") as f:
+            head = f.read(40)
+    except OSError:
+        return False
+    if len(head) < 40 or head[:4] != b"EXP2":
+        return False
+    made_with = head[8:40].split(b"\0", 1)[0].decode(errors="replace")
+    running = os.confstr("CS_GNU_LIBC_VERSION").split()[-1]
+    return made_with == running
+
+
 def build_expf_table(force: bool = False) -> str:
     """Tabulate where the host libm expf differs from correctly rounded exp
     (csrc/gen_expf_table.c); the library loads the table at model load."""
-    if os.path.exists(EXPF_TABLE) and not force:
+    if os.path.exists(EXPF_TABLE) and not force and _expf_table_current():
         return EXPF_TABLE
     bdir = os.path.join(HERE, "_build")
     os.makedirs(bdir, exist_ok=True)

@@ -260,11 +260,18 @@ def write_model(path: str, s: Shape, sections: Iterable[bytes]) -> int:
 
 
 def synthetic_sections(s: Shape, seed: int, progress: Callable[[str], None] | None = None,
-                       fast: bool = False):
+                       fast: bool = False, backend=None):
     """Yield the sections of a seeded random model of shape `s`. `fast` uses
-    the C++ weight source and quantizer (same format, different draws)."""
-    rng = _NativeRng(seed) if fast else _Rng(seed)
-    q = quantize_rtn_native if fast else quantize_rtn
+    the C++ weight source and quantizer (same format, different draws).
+    `backend(seed)` replaces that pair with another object offering
+    `normal(shape, std)` and `quantize(w, bits, group_size)` that draws the
+    same values (a writer that must not load this package's library)."""
+    if backend is not None:
+        rng = backend(seed)
+        q = rng.quantize
+    else:
+        rng = _NativeRng(seed) if fast else _Rng(seed)
+        q = quantize_rtn_native if fast else quantize_rtn
     emb = rng.normal((s.vocab, s.hidden))
     ep, ec = q(emb, 8, s.embed_group_size)
     yield ep + ec
@@ -295,11 +302,12 @@ def synthetic_sections(s: Shape, seed: int, progress: Callable[[str], None] | No
         yield linear_section(rng.normal((s.vocab, s.hidden)), s.group_size, q)
 
 
-def write_synthetic(path: str, s: Shape | str, seed: int = 0, progress=None, fast: bool = False) -> int:
+def write_synthetic(path: str, s: Shape | str, seed: int = 0, progress=None, fast: bool = False,
+                    backend=None) -> int:
     """Write a seeded synthetic .raimodel of the given shape (or preset name)."""
     if isinstance(s, str):
         s = PRESETS[s]
-    return write_model(path, s, synthetic_sections(s, seed, progress, fast))
+    return write_model(path, s, synthetic_sections(s, seed, progress, fast, backend))
 
 
 def weight_bytes_per_step(s: Shape) -> int:

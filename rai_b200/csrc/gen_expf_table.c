@@ -8,11 +8,14 @@
  * table on top of its correctly rounded exp to return exactly what the host
  * libm returns.
  *
- * Output (little-endian): u32 magic "EXPF", u32 count, count sorted u32 input
- * bit patterns, count u32 result bit patterns.
+ * Output (little-endian): u32 magic "EXP2", u32 count, the 32-byte
+ * NUL-padded glibc version string the table was made with, count sorted u32
+ * input bit patterns, count u32 result bit patterns. The library refuses a
+ * table made with another glibc than the one it runs with.
  *
  *   gcc -O2 -fopenmp gen_expf_table.c -o gen -lm && ./gen out.bin
  */
+#include <gnu/libc-version.h>
 #include <math.h>
 #include <omp.h>
 #include <stdint.h>
@@ -66,8 +69,11 @@ int main(int argc, char** argv) {
   for (int t = 0; t < nthreads; ++t) n += counts[t];
   FILE* f = fopen(argv[1], "wb");
   if (!f) return 1;
-  uint32_t hdr[2] = {0x46505845u, (uint32_t)n};
+  uint32_t hdr[2] = {0x32505845u, (uint32_t)n};
+  char ver[32] = {0};
+  strncpy(ver, gnu_get_libc_version(), sizeof(ver) - 1);
   fwrite(hdr, 4, 2, f);
+  fwrite(ver, 1, sizeof(ver), f);
   /* thread ranges are ascending, so concatenation is sorted */
   for (int t = 0; t < nthreads; ++t) fwrite(keys[t], 4, counts[t], f);
   for (int t = 0; t < nthreads; ++t) fwrite(vals[t], 4, counts[t], f);

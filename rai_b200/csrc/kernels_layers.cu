@@ -929,8 +929,20 @@ __global__ void accept_kernel(StreamStep* st_all, const unsigned long long* __re
   st->produced = produced;
 }
 
+__global__ void expf_range_kernel(uint32_t first, size_t n, float* __restrict__ out, ExpfTable et) {
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
+    out[i] = expf_host(__uint_as_float(first + (uint32_t)i), et);
+}
+
 // ---------------------------------------------------------------------------
 // Host launchers.
+cudaError_t launch_expf_range(uint32_t first, size_t n, float* out, const ExpfTable& et, cudaStream_t s) {
+  const size_t blocks = (n + 255) / 256;
+  expf_range_kernel<<<(unsigned)grid_cap((int)(blocks < (1u << 20) ? blocks : (1u << 20)), 8), 256, 0, s>>>(
+      first, n, out, et);
+  return cudaGetLastError();
+}
+
 cudaError_t launch_embed(const uint32_t* ids, const int* m_dev, int M, const uint8_t* codes,
                          const uint8_t* params, int vocab, int hidden, int gs, float embed_scale,
                          float* out, uint32_t* err, cudaStream_t s, uint32_t* epoch, bool with_logits) {

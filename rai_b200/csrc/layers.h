@@ -109,6 +109,9 @@ cudaError_t launch_plan(StreamStep* st, int n, RowInfo* rows, uint32_t* ids, int
 // row for speculative decoding; null = the point mass of prompt lookup.
 cudaError_t launch_sample_accept(StreamStep* st, int n, const float* logits, int vocab, float temperature,
                                  cudaStream_t s, const float* draft_logits = nullptr);
+// out[i] = expf_host of the float with bit pattern first + i (i < n): the
+// library's reproduction of the host libm expf, for an exhaustive check.
+cudaError_t launch_expf_range(uint32_t first, size_t n, float* out, const ExpfTable& et, cudaStream_t s);
 // With tp (world > 1) and slot >= 0, best[] is awaited as exchange `slot`.
 cudaError_t launch_accept(StreamStep* st, int n, const unsigned long long* best, cudaStream_t s,
                           const TpLink* tp = nullptr, int slot = -1, uint32_t* err = nullptr);

@@ -9,6 +9,7 @@
 // context in, replays one CUDA graph and reads one small struct back.
 #include <cuda_runtime.h>
 #include <dlfcn.h>
+#include <gnu/libc-version.h>
 
 #include <algorithm>
 #include <fstream>
@@ -141,6 +142,12 @@ struct rai_model {
   uint8_t* peer_arena[rai::kMaxTp] = {};
   bool tp_connected = false;
   std::vector<void*> ipc_opened;
+  // Set when a cross-GPU wait of this multi-GPU model timed out: the ranks'
+  // exchange counters no longer agree on how many forwards ran, so a later
+  // wait could pass on a peer's counts from another forward. The model
+  // refuses all further work; every rank must destroy and re-create its model
+  // together (fresh arenas, counters at zero).
+  bool failed = false;
 
   template <class T>
   int alloc(T** p, size_t bytes) {
@@ -279,8 +286,17 @@ int expf_table(rai::ExpfTable* out) {
   std::ifstream f(path, std::ios::binary);
   if (!f) return fail(RAI_ERR_INVALID, "missing " + path + " (run rai_b200.build)");
   uint32_t hdr[2] = {0, 0};
+  char ver[33] = {0};
   f.read(reinterpret_cast<char*>(hdr), 8);
-  if (!f || hdr[0] != 0x46505845u) return fail(RAI_ERR_INVALID, "bad expf table " + path);
+  f.read(ver, 32);
+  if (!f || hdr[0] != 0x32505845u) return fail(RAI_ERR_INVALID, "bad expf table " + path);
+  // The table lists where this glibc's expf is not correctly rounded; the
+  // reference calls the glibc of the machine it runs on, so a table made
+  // with another glibc would reproduce the wrong function.
+  if (std::strcmp(ver, gnu_get_libc_version()) != 0)
+    return fail(RAI_ERR_UNSUPPORTED, std::string("expf table ") + path + " was made with glibc " + ver +
+                                         ", this process runs glibc " + gnu_get_libc_version() +
+                                         " (rebuild it: python -m rai_b200.build)");
   std::vector<uint32_t> kv(2 * (size_t)hdr[1]);
   f.read(reinterpret_cast<char*>(kv.data()), kv.size() * 4);
   if (!f) return fail(RAI_ERR_INVALID, "truncated expf table " + path);
@@ -742,9 +758,22 @@ int check_err(rai_model* m, cudaStream_t s) {
   if (e) {
     cudaMemsetAsync(m->err_dev, 0, 4, s);
     cudaStreamSynchronize(s);
+    if ((e & rai::kErrWaitTimeout) && m->tp_world > 1) {
+      m->failed = true;
+      return fail(RAI_ERR_TIMEOUT, "a cross-GPU wait timed out; this multi-GPU model now refuses work until every "
+                                   "rank destroys and re-creates it");
+    }
     if (e & rai::kErrWaitTimeout) return fail(RAI_ERR_TIMEOUT, "a device-side wait timed out");
     return fail(RAI_ERR_INVALID, "device kernel rejected its input (token id out of range)");
   }
+  return RAI_OK;
+}
+
+// Entry points that launch work on a model call this first.
+int check_usable(const rai_model* m) {
+  if (m->failed)
+    return fail(RAI_ERR_TIMEOUT, "multi-GPU model failed after a cross-GPU wait timed out: destroy and re-create it "
+                                 "on every rank");
   return RAI_OK;
 }
 
@@ -841,6 +870,7 @@ int ensure_graph(Batch* B, const rai_lookup_cfg* cfg) {
 int step_batch(Batch* B, const size_t* pos, const uint32_t* const* ctx, const size_t* ctx_len,
                const rai_lookup_cfg* cfg, uint32_t* out_tokens, size_t out_cap, size_t* n_out,
                rai_lookup_metrics* metrics, bool lookup = true) {
+  if (int rc = check_usable(B->m)) return rc;
   if (lookup)
     if (int rc = validate_cfg(cfg)) return rc;
   if (out_cap < cfg->max_draft + 1) return fail(RAI_ERR_INVALID, "out_tokens capacity below max_draft + 1");
@@ -969,6 +999,30 @@ __device__ __align__(256) uint8_t g_w4a8_static_scratch[kStaticScratchBytes];
 constexpr int kMaxDevices = 64;
 std::mutex g_static_mu;
 void* g_static_scratch_ptr[kMaxDevices] = {};
+
+// Status word of the kernel-level entries (one per device): their bounded
+// device waits record a timeout here; rai_gpu_kernel_status reads and
+// clears it.
+__device__ uint32_t g_kernel_err_word;
+uint32_t* g_kernel_err_ptr[kMaxDevices] = {};
+
+int kernel_err_word(uint32_t** out) {
+  int dev = 0;
+  RAI_CUDA(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= kMaxDevices) return fail(RAI_ERR_UNSUPPORTED, "device ordinal beyond the status table");
+  std::lock_guard<std::mutex> lk(g_static_mu);
+  if (!g_kernel_err_ptr[dev]) {
+    void* p = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&p, g_kernel_err_word);
+    if (e != cudaSuccess) {
+      (void)cudaGetLastError();
+      return fail(RAI_ERR_DEVICE, std::string("cudaGetSymbolAddress: ") + cudaGetErrorString(e));
+    }
+    g_kernel_err_ptr[dev] = static_cast<uint32_t*>(p);
+  }
+  *out = g_kernel_err_ptr[dev];
+  return RAI_OK;
+}
 
 int static_scratch(void** out) {
   int dev = 0;
@@ -1237,6 +1291,7 @@ int rai_gpu_model_info(const rai_model* m, rai_model_info* info) {
 int rai_gpu_decoder_create(rai_model* m, size_t max_ctx, rai_dec** out) {
   if (!m || !out) return fail(RAI_ERR_INVALID, "null argument");
   *out = nullptr;
+  if (int rc = check_usable(m)) return rc;
   size_t ctx = std::min<size_t>(max_ctx, m->cfg.max_context);
   if (ctx == 0) return fail(RAI_ERR_INVALID, "prompt-lookup context must be non-zero");
   DeviceGuard guard(m->device);
@@ -1271,6 +1326,7 @@ int rai_gpu_prefill(rai_dec* d, const uint32_t* ids, size_t n, size_t* pos_out) 
   if (!d || !pos_out || (!ids && n)) return fail(RAI_ERR_INVALID, "null argument");
   if (n == 0) return fail(RAI_ERR_INVALID, "prompt must contain at least one token");
   if (n > (size_t)d->max_ctx) return fail(RAI_ERR_INVALID, "prompt exceeds the prompt-lookup context window");
+  if (int rc = check_usable(d->m)) return rc;
   const Config& c = d->m->cfg;
   for (size_t i = 0; i + 1 < n; ++i)
     if (ids[i] >= c.vocab_size) return fail(RAI_ERR_INVALID, "token id is out of model vocabulary");
@@ -1343,6 +1399,7 @@ int rai_gpu_prefill_many(rai_dec* const* decs, size_t n, const uint32_t* const* 
 
 int rai_gpu_forward_logits(rai_dec* d, const uint32_t* ids, size_t start_pos, size_t batch, float* logits) {
   if (!d || !ids || batch == 0) return fail(RAI_ERR_INVALID, "bad argument");
+  if (int rc = check_usable(d->m)) return rc;
   if (d->m->tp_world > 1 && !d->m->ep)
     return fail(RAI_ERR_UNSUPPORTED, "forward_logits on a tensor-parallel model (each rank holds a vocabulary slice)");
   const Config& c = d->m->cfg;
@@ -1645,6 +1702,23 @@ PackedLinear packed_view(const void* packed, size_t rows, size_t cols, size_t gs
 }
 }  // namespace
 
+namespace {
+// Sizes the kernel-level linear accepts: counts stay far inside the int
+// ranges the kernels index with (rows and columns below 2^30, tokens below
+// 2^24, the group count within the kernels' limit), checked before any
+// narrowing.
+constexpr size_t kMaxLinearDim = (size_t)1 << 30, kMaxLinearTokens = (size_t)1 << 24;
+int check_linear(size_t rows, size_t cols, size_t tokens, size_t gs) {
+  if (gs != 64 && gs != 128) return fail(RAI_ERR_UNSUPPORTED, "group_size must be 64 or 128");
+  if (tokens == 0 || rows == 0 || cols == 0 || cols % 2) return fail(RAI_ERR_INVALID, "bad dimensions");
+  if (rows > kMaxLinearDim || cols > kMaxLinearDim || tokens > kMaxLinearTokens)
+    return fail(RAI_ERR_INVALID, "rows / cols above 2^30 or tokens above 2^24");
+  if (rai::ceil_div(cols, gs) > raimodel::kMaxGroups)
+    return fail(RAI_ERR_INVALID, "quantization group count exceeds kernel capacity");
+  return RAI_OK;
+}
+}  // namespace
+
 size_t rai_gpu_w4a8_packed_bytes(size_t rows, size_t cols, size_t gs) {
   return tc_offset(rows, cols, gs) + rai::tc_image_bytes(rows, cols, gs);
 }
@@ -1652,9 +1726,7 @@ size_t rai_gpu_w4a8_packed_bytes(size_t rows, size_t cols, size_t gs) {
 int rai_gpu_w4a8_pack(const uint8_t* nibbles, const uint8_t* params, size_t rows, size_t cols, size_t gs,
                       void* packed, void* stream) {
   if (!nibbles || !params || !packed) return fail(RAI_ERR_INVALID, "null argument");
-  if (gs != 64 && gs != 128) return fail(RAI_ERR_UNSUPPORTED, "group_size must be 64 or 128");
-  if (cols % 2 || cols == 0 || rows == 0) return fail(RAI_ERR_INVALID, "rows must be non-zero, cols non-zero and even");
-  if (rai::ceil_div(cols, gs) > raimodel::kMaxGroups) return fail(RAI_ERR_INVALID, "quantization group count exceeds kernel capacity");
+  if (int rc = check_linear(rows, cols, 1, gs)) return rc;
   RAI_CUDA(rai::pack_linear4(nibbles, params, (int)rows, (int)cols, (int)gs, static_cast<uint8_t*>(packed),
                              static_cast<cudaStream_t>(stream)));
   RAI_CUDA(rai::pack_linear4_tc(nibbles, params, (int)rows, (int)cols, (int)gs,
@@ -1664,15 +1736,14 @@ int rai_gpu_w4a8_pack(const uint8_t* nibbles, const uint8_t* params, size_t rows
 }
 
 size_t rai_gpu_w4a8_scratch_bytes(size_t tokens, size_t cols, size_t gs) {
-  return ActBuf::bytes((int)rai::round_up(tokens, 8), (int)rai::ceil_div(cols, gs));
+  if (tokens > kMaxLinearTokens || gs == 0) return SIZE_MAX;  // rejected by every entry that takes a scratch
+  return rai::round_up(tokens, 8) * rai::kActTokBytes * rai::ceil_div(cols, gs);
 }
 
 int rai_gpu_w4a8_matmul(float* out, const void* packed, const float* input, size_t rows, size_t cols, size_t tokens,
                         size_t gs, void* scratch, size_t scratch_bytes, void* stream) {
   if (!out || !packed || !input || !scratch) return fail(RAI_ERR_INVALID, "null argument");
-  if (gs != 64 && gs != 128) return fail(RAI_ERR_UNSUPPORTED, "group_size must be 64 or 128");
-  if (tokens == 0 || rows == 0 || cols == 0 || cols % 2) return fail(RAI_ERR_INVALID, "bad dimensions");
-  if (rai::ceil_div(cols, gs) > raimodel::kMaxGroups) return fail(RAI_ERR_INVALID, "quantization group count exceeds kernel capacity");
+  if (int rc = check_linear(rows, cols, tokens, gs)) return rc;
   if (scratch_bytes < rai_gpu_w4a8_scratch_bytes(tokens, cols, gs)) return fail(RAI_ERR_INVALID, "scratch buffer is too small");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   RAI_CUDA(rai::init_gemm_attributes());
@@ -1680,9 +1751,11 @@ int rai_gpu_w4a8_matmul(float* out, const void* packed, const float* input, size
   a.data = static_cast<uint8_t*>(scratch);
   a.tok_alloc = (int)rai::round_up(tokens, 8);
   a.groups = (int)rai::ceil_div(cols, gs);
+  uint32_t* err = nullptr;
+  if (int rc = kernel_err_word(&err)) return rc;
   RAI_CUDA(rai::quantize_act(input, (int)cols, (int)tokens, nullptr, (int)cols, (int)gs, 4, a, s));
   const PackedLinear w = packed_view(packed, rows, cols, gs);
-  RAI_CUDA(rai::gemm_exact(w, a, (int)tokens, out, (int)rows, rai::GemmEpilogue{}, nullptr, s));
+  RAI_CUDA(rai::gemm_exact(w, a, (int)tokens, out, (int)rows, rai::GemmEpilogue{}, err, s));
   return RAI_OK;
 }
 
@@ -1731,11 +1804,34 @@ int rai_gpu_attention(const float* q, const float* k, const float* v, const int*
   return RAI_OK;
 }
 
+int rai_gpu_kernel_status(void* stream) {
+  uint32_t* err = nullptr;
+  if (int rc = kernel_err_word(&err)) return rc;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  uint32_t e = 0;
+  RAI_CUDA(cudaMemcpyAsync(&e, err, 4, cudaMemcpyDeviceToHost, s));
+  RAI_CUDA(cudaStreamSynchronize(s));
+  if (e) {
+    RAI_CUDA(cudaMemsetAsync(err, 0, 4, s));
+    RAI_CUDA(cudaStreamSynchronize(s));
+    return fail(RAI_ERR_TIMEOUT, "a device-side wait of a kernel-level call timed out (its output is incomplete)");
+  }
+  return RAI_OK;
+}
+
+int rai_gpu_expf_range(uint32_t first_bits, size_t n, float* out, void* stream) {
+  if (!out && n) return fail(RAI_ERR_INVALID, "null argument");
+  if (n > ((size_t)1 << 32) - first_bits) return fail(RAI_ERR_INVALID, "range passes 2^32");
+  rai::ExpfTable et;
+  if (int rc = expf_table(&et)) return rc;
+  if (n) RAI_CUDA(rai::launch_expf_range(first_bits, n, out, et, static_cast<cudaStream_t>(stream)));
+  return RAI_OK;
+}
+
 int rai_gpu_w4a8_quantize(const float* input, size_t cols, size_t tokens, size_t gs, void* scratch,
                           size_t scratch_bytes, void* stream) {
   if (!input || !scratch) return fail(RAI_ERR_INVALID, "null argument");
-  if (gs != 64 && gs != 128) return fail(RAI_ERR_UNSUPPORTED, "group_size must be 64 or 128");
-  if (tokens == 0 || cols == 0 || cols % 2) return fail(RAI_ERR_INVALID, "bad dimensions");
+  if (int rc = check_linear(1, cols, tokens, gs)) return rc;
   if (scratch_bytes < rai_gpu_w4a8_scratch_bytes(tokens, cols, gs)) return fail(RAI_ERR_INVALID, "scratch buffer is too small");
   ActBuf a;
   a.data = static_cast<uint8_t*>(scratch);
@@ -1749,15 +1845,16 @@ int rai_gpu_w4a8_quantize(const float* input, size_t cols, size_t tokens, size_t
 int rai_gpu_w4a8_matmul_prequant(float* out, const void* packed, const void* scratch, size_t rows, size_t cols,
                                  size_t tokens, size_t gs, void* stream) {
   if (!out || !packed || !scratch) return fail(RAI_ERR_INVALID, "null argument");
-  if (gs != 64 && gs != 128) return fail(RAI_ERR_UNSUPPORTED, "group_size must be 64 or 128");
-  if (tokens == 0 || rows == 0 || cols == 0 || cols % 2) return fail(RAI_ERR_INVALID, "bad dimensions");
+  if (int rc = check_linear(rows, cols, tokens, gs)) return rc;
   RAI_CUDA(rai::init_gemm_attributes());
   ActBuf a;
   a.data = static_cast<uint8_t*>(const_cast<void*>(scratch));
   a.tok_alloc = (int)rai::round_up(tokens, 8);
   a.groups = (int)rai::ceil_div(cols, gs);
   const PackedLinear w = packed_view(packed, rows, cols, gs);
-  RAI_CUDA(rai::gemm_exact(w, a, (int)tokens, out, (int)rows, rai::GemmEpilogue{}, nullptr,
+  uint32_t* err = nullptr;
+  if (int rc = kernel_err_word(&err)) return rc;
+  RAI_CUDA(rai::gemm_exact(w, a, (int)tokens, out, (int)rows, rai::GemmEpilogue{}, err,
                            static_cast<cudaStream_t>(stream)));
   return RAI_OK;
 }
@@ -1765,8 +1862,7 @@ int rai_gpu_w4a8_matmul_prequant(float* out, const void* packed, const void* scr
 int rai_gpu_w4a8_matmul_static(float* out, const void* packed, const float* input, size_t rows, size_t cols,
                                size_t tokens, size_t gs, void* stream) {
   if (!out || !packed || !input) return fail(RAI_ERR_INVALID, "null argument");
-  if (gs != 64 && gs != 128) return fail(RAI_ERR_UNSUPPORTED, "group_size must be 64 or 128");
-  if (tokens == 0 || rows == 0 || cols == 0 || cols % 2) return fail(RAI_ERR_INVALID, "bad dimensions");
+  if (int rc = check_linear(rows, cols, tokens, gs)) return rc;
   const size_t need = rai_gpu_w4a8_scratch_bytes(tokens, cols, gs);
   if (need > kStaticScratchBytes)
     return fail(RAI_ERR_INVALID, "tokens x groups exceed the 2 MiB static scratch (136 B per token per group, "

@@ -48,6 +48,9 @@ __device__ __forceinline__ void tp_signal(const TpLink& t, int slot) {
 }
 
 __device__ __forceinline__ bool tp_wait(const TpLink& t, int slot, int which, uint32_t* err) {
+  // A wait of this forward already gave up: the peers are not coming, so
+  // later exchanges fail at once instead of each waiting out its bound.
+  if (err && (*reinterpret_cast<volatile uint32_t*>(err) & kErrWaitTimeout)) return false;
   const unsigned long long target = (unsigned long long)t.epoch[which] * (unsigned long long)t.world;
   const unsigned long long* f = t.flags[t.rank] + slot;
   for (uint32_t i = 0; i < kTpMaxPolls; ++i) {

@@ -9,7 +9,7 @@
 The tests read only these copies, so they run where the reference tree is
 absent (the GPU box).
 
-    python tests/golden/make_golden.py [/path/to/reference]
+    python tests/golden/make_golden.py /path/to/reference
 """
 import json
 import os
@@ -43,6 +43,8 @@ def extract_llama3_table(ref: str) -> None:
 
 
 if __name__ == "__main__":
-    ref = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
+    if len(sys.argv) != 2:
+        sys.exit("usage: python tests/golden/make_golden.py /path/to/reference")
+    ref = sys.argv[1]
     copy_fixtures(ref)
     extract_llama3_table(ref)

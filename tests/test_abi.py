@@ -36,3 +36,18 @@ def test_errors_are_status_codes_not_aborts():
         raise AssertionError("expected an error")
     except rai_b200.RaiError as e:
         assert e.code == native.RAI_ERR_FORMAT
+
+
+def test_linear_entries_reject_sizes_before_narrowing():
+    """Token, row and column counts beyond the kernels' int ranges are
+    refused up front (no device needed: the checks run before any launch)."""
+    from rai_b200 import native
+    L = native.lib()
+    big = (1 << 32) + 8
+    assert L.rai_gpu_w4a8_scratch_bytes(big, 2048, 128) == (1 << 64) - 1
+    dummy = 16
+    for rows, cols, tokens in ((256, 2048, big), (1 << 31, 2048, 9), (256, (1 << 31) + 2, 9)):
+        assert L.rai_gpu_w4a8_matmul_static(dummy, dummy, dummy, rows, cols, tokens, 128, None) == \
+            native.RAI_ERR_INVALID
+        assert L.rai_gpu_w4a8_matmul(dummy, dummy, dummy, rows, cols, tokens, 128, dummy, 1 << 40, None) == \
+            native.RAI_ERR_INVALID

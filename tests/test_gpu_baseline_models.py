@@ -1,0 +1,284 @@
+"""The device decode path against the oracle at the BASELINE model shapes.
+
+Every other decode test runs two-layer models; these run the four BASELINE
+architectures at full size (seeded synthetic weights, the same files
+bench.py writes):
+  * Qwen2.5-0.5B   (24 layers, tied 8-bit head of 151,936 rows, QKV bias)
+  * TinyLlama-1.1B (22 layers, 32/4 heads of 64)
+  * Llama-3.1-8B   (32 layers, head_dim 128, llama3 RoPE, 128,256-row head)
+  * OLMoE-1B-7B    (16 layers, 64 experts, top-8, full-width QK-norm)
+
+Bar: logits within max|d| <= 1e-3 * max|logit|;
+greedy tokens and drafted / accepted / produced counts identical, a token
+difference only being allowed at a row whose oracle top-2 margin is below
+that tolerance; the KV watermark equals pos + produced after every step.
+Prompts are shorter than bench.py's so the oracle finishes in seconds.
+"""
+import numpy as np
+import pytest
+
+import bench
+
+pytestmark = pytest.mark.gpu
+torch = pytest.importorskip("torch")
+
+# (bench config, prompt length, prompt recipe) per preset. Copied spans make
+# the n-gram search fire; the 8B config's own prompt is uniform random,
+# which would rarely draft, so its parity test uses copied spans too.
+CASES = {
+    "qwen2.5-0.5b": ("qwen", 256, None),
+    "tinyllama-1.1b": ("tinyllama", 320, None),
+    "llama3.1-8b": ("llama8b", 160, ("copy", 0.40)),
+    "olmoe-1b-7b": ("olmoe", 256, None),
+}
+STEPS = 16
+
+
+def _tol(want):
+    return 1e-3 * max(float(np.max(np.abs(want))), 1e-30)
+
+
+def _prompt(preset, seed, vocab):
+    name, n, recipe = CASES[preset]
+    cfg = dict(bench.CONFIGS[name])
+    if recipe:
+        cfg["recipe"] = recipe
+    return bench.prompt_for(cfg, seed, n, vocab)
+
+
+_loaded = {}
+
+
+def _models(preset, oracle):
+    """(path, GPU model, oracle model) of a preset, one preset held at a
+    time (the 8B and MoE models take ~4 GB each on both sides)."""
+    import rai_b200
+    if preset not in _loaded:
+        for k in list(_loaded):
+            _loaded.pop(k)[1].close()
+        path = bench.model_path(0, 1, preset)
+        _loaded[preset] = (path, rai_b200.RaiModel.load(path), oracle.Model.load(path))
+    return _loaded[preset]
+
+
+def _explain_divergence(path, gm, oracle, ctx, pos, k, gt, ot, window):
+    """A token mismatch is allowed only where the oracle's top-2 logit margin
+    is below the logit tolerance: replay the step's verify rows on fresh
+    decoders and check exactly that."""
+    import rai_b200
+    n = oracle.find_ngram_draft(ctx, 1, 3, k)
+    draft = ctx[n[1]:n[1] + n[2]] if n else []
+    rows = [ctx[pos]] + draft
+    od = oracle.Decoder(oracle.Model.load(path), window)
+    od.prefill(ctx[:pos + 1])
+    want = od.forward_logits(rows, pos)
+    gd = rai_b200.LookupDecoder(gm, window)
+    gd.prefill(ctx[:pos + 1])
+    got = gd.forward_logits(rows, pos)
+    gd.close()
+    tol = _tol(want)
+    assert np.max(np.abs(got - want)) <= tol, "logits differ beyond tolerance"
+    i = 0
+    while i < min(len(gt), len(ot)) and gt[i] == ot[i]:
+        i += 1
+    top2 = np.sort(want[i])[-2:]
+    margin = float(top2[1] - top2[0])
+    assert margin <= tol, f"tokens differ at row {i} with a top-2 margin {margin} above the tolerance {tol}"
+
+
+@pytest.mark.parametrize("preset", list(CASES))
+def test_verify_logits_match_oracle(oracle, preset):
+    """forward_batch + hidden_to_logits_batch of a 9-row verify batch on top
+    of a prefilled cache: logits within tolerance (and counted bit for bit),
+    argmax rows equal."""
+    import rai_b200
+    path, gm, om = _models(preset, oracle)
+    vocab = gm.config["vocab_size"]
+    prompt = _prompt(preset, 7, vocab)
+    window = len(prompt) + 32
+    gd, od = rai_b200.LookupDecoder(gm, window), oracle.Decoder(om, window)
+    pos = gd.prefill(prompt)
+    assert od.prefill(prompt) == pos
+    rows = [prompt[-1]] + prompt[-40:-32]
+    want = od.forward_logits(rows, pos)
+    got = gd.forward_logits(rows, pos)
+    gd.close()
+    err = float(np.max(np.abs(got - want)))
+    exact = sum(np.array_equal(a, b) for a, b in zip(got, want))
+    print(f"{preset}: max|d| {err:.3g} (tol {_tol(want):.3g}), {exact}/{len(rows)} rows bit-identical")
+    assert err <= _tol(want)
+    assert np.array_equal(np.argmax(got, 1), np.argmax(want, 1))
+
+
+def _run_steps(oracle, preset, k, seed, steps=STEPS):
+    import rai_b200
+    path, gm, om = _models(preset, oracle)
+    vocab = gm.config["vocab_size"]
+    prompt = _prompt(preset, seed, vocab)
+    window = len(prompt) + (steps + 2) * (k + 1)
+    gd, od = rai_b200.LookupDecoder(gm, window), oracle.Decoder(om, window)
+    pos = gd.prefill(prompt)
+    assert od.prefill(prompt) == pos
+    ctx = list(prompt)
+    cfg = rai_b200.LookupConfig(max_draft=k, max_ngram=3, min_ngram=1)
+    totals = np.zeros(3, np.int64)
+    for _ in range(steps):
+        gt, gmet = gd.step(pos, ctx, cfg)
+        ot, omet = od.step(pos, ctx, k)
+        if gt != ot:
+            _explain_divergence(path, gm, oracle, ctx, pos, k, gt, ot, window)
+            break
+        assert (gmet.drafted, gmet.accepted, gmet.produced) == (omet["drafted"], omet["accepted"], omet["produced"])
+        assert gmet.matched_ngram == omet["matched_ngram"]
+        ctx += gt
+        pos += len(gt)
+        assert gd.kv_filled(0) == pos == od.kv_filled(0)
+        assert gd.kv_filled(gm.config["num_layers"] - 1) == pos
+        totals += (gmet.drafted, gmet.accepted, gmet.produced)
+    gd.close()
+    return totals
+
+
+@pytest.mark.parametrize("preset", list(CASES))
+def test_lookup_steps_match_oracle_k8(oracle, preset):
+    totals = _run_steps(oracle, preset, 8, seed=11)
+    print(f"{preset} k=8: drafted {totals[0]}, accepted {totals[1]}, produced {totals[2]}")
+    assert totals[0] > 0, "the prompt's copied spans should make the n-gram search draft"
+
+
+@pytest.mark.parametrize("k", [1, 4, 16])
+def test_tinyllama_lookup_steps_other_k(oracle, k):
+    totals = _run_steps(oracle, "tinyllama-1.1b", k, seed=12)
+    assert totals[0] > 0
+
+
+def test_tinyllama_step_batch_matches_independent_oracle_streams(oracle):
+    """The serving-loop batch (one verify forward over every stream's rows)
+    at the bench's model: each stream equals its own oracle decoder."""
+    import rai_b200
+    path, gm, om = _models("tinyllama-1.1b", oracle)
+    vocab = gm.config["vocab_size"]
+    n, k = 4, 8
+    prompts = [_prompt("tinyllama-1.1b", 1000 + i, vocab)[: 200 + 17 * i] for i in range(n)]
+    windows = [len(p) + (STEPS + 2) * (k + 1) for p in prompts]
+    gds = [rai_b200.LookupDecoder(gm, w) for w in windows]
+    ods = [oracle.Decoder(om, w) for w in windows]
+    batch = rai_b200.StepBatch(gds)
+    poss = batch.prefill(prompts)
+    assert poss == [od.prefill(p) for od, p in zip(ods, prompts)]
+    ctxs = [list(p) for p in prompts]
+    cfg = rai_b200.LookupConfig(max_draft=k, max_ngram=3, min_ngram=1)
+    drafted = 0
+    for _ in range(STEPS):
+        toks, counts, mets = batch.step(cfg)
+        for i in range(n):
+            ot, om_ = ods[i].step(poss[i], ctxs[i], k)
+            assert toks[i, : counts[i]].tolist() == ot, (i, poss[i])
+            assert (int(mets["drafted"][i]), int(mets["accepted"][i]), int(mets["produced"][i])) == \
+                (om_["drafted"], om_["accepted"], om_["produced"])
+            drafted += om_["drafted"]
+            ctxs[i] += ot
+            poss[i] += len(ot)
+            assert gds[i].kv_filled(0) == poss[i] == ods[i].kv_filled(0)
+    for d in gds:
+        d.close()
+    assert drafted > 0
+
+
+# ---------------------------------------------------------------------------
+# Forced acceptance: drafts that are the model's own greedy continuation.
+
+def _greedy(gm, prompt, n, window):
+    """The model's greedy continuation of `prompt` (n tokens, decode_one)."""
+    import rai_b200
+    d = rai_b200.LookupDecoder(gm, window)
+    pos = d.prefill(prompt)
+    last, out = prompt[-1], []
+    for _ in range(n):
+        last = d.decode_one(pos, last)
+        out.append(last)
+        pos += 1
+    d.close()
+    return out
+
+
+def _planted(prompt, at, cont):
+    """The prompt with its last 3 tokens followed by `cont` copied to
+    position `at`: the n-gram search at the prompt's end then drafts `cont`."""
+    g = prompt[-3:]
+    p = list(prompt)
+    p[at:at + 3 + len(cont)] = g + list(cont)
+    return p
+
+
+def _plant_at(prompt, k):
+    """Where the planted copy goes: close enough to the end that it is the
+    most recent earlier occurrence of the final 3-gram (the search scans
+    from the end), clear of the final tokens."""
+    return len(prompt) - 3 - (3 + k) - 8
+
+
+def _forced_case(gm, prompt, k, window, rounds=4):
+    """Plant the greedy continuation and re-plant until it is a fixed point
+    (one planted copy among many positions rarely moves the argmax)."""
+    at = _plant_at(prompt, k)
+    cont = _greedy(gm, prompt, k + 1, window)
+    p = _planted(prompt, at, cont[:k])
+    for _ in range(rounds):
+        c2 = _greedy(gm, p, k + 1, window)
+        if c2[:k] == cont[:k]:
+            return p, c2
+        cont = c2
+        p = _planted(prompt, at, cont[:k])
+    return p, _greedy(gm, p, k + 1, window)
+
+
+@pytest.mark.parametrize("preset", ["tinyllama-1.1b", "qwen2.5-0.5b"])
+def test_forced_acceptance_partial_full_and_rollback(oracle, preset):
+    """Drafts equal to the model's greedy continuation are all accepted and
+    the bonus token follows; with one drafted token changed the step accepts
+    the tokens before it, emits the target's token in its place and rolls
+    the cache back past the rejected rows (lookup.rs:359-411). The device
+    must equal the oracle on tokens, counts and the KV watermark in both."""
+    import rai_b200
+    path, gm, om = _models(preset, oracle)
+    vocab = gm.config["vocab_size"]
+    k = 8
+    seen_full = seen_partial = False
+    for seed in range(40, 46):
+        base = _prompt(preset, seed, vocab)[:160]
+        window = len(base) + 4 * (k + 1)
+        p, cont = _forced_case(gm, base, k, window)
+        for perturb in (None, 3):
+            ctx = list(p)
+            if perturb is not None:
+                # Change the planted draft's token `perturb` (the copy, not
+                # the prompt's tail), so the draft differs from the target
+                # there.
+                at = _plant_at(base, k) + 3 + perturb
+                ctx[at] = (ctx[at] + 1) % vocab
+            gd, od = rai_b200.LookupDecoder(gm, window), oracle.Decoder(om, window)
+            pos = gd.prefill(ctx)
+            assert od.prefill(ctx) == pos
+            cfg = rai_b200.LookupConfig(max_draft=k, max_ngram=3, min_ngram=1)
+            for _ in range(2):
+                gt, gmet = gd.step(pos, ctx, cfg)
+                ot, omet = od.step(pos, ctx, k)
+                if gt != ot:
+                    _explain_divergence(path, gm, oracle, ctx, pos, k, gt, ot, window)
+                    break
+                assert (gmet.drafted, gmet.accepted, gmet.produced) == \
+                    (omet["drafted"], omet["accepted"], omet["produced"])
+                assert gmet.produced == gmet.accepted + 1
+                if gmet.drafted == k and gmet.accepted == k:
+                    seen_full = True
+                if 0 < gmet.accepted < gmet.drafted:
+                    seen_partial = True
+                ctx += gt
+                pos += len(gt)
+                assert gd.kv_filled(0) == pos == od.kv_filled(0)
+            gd.close()
+        if seen_full and seen_partial:
+            break
+    assert seen_full, "no step accepted a whole draft (planted continuation not a fixed point for any seed)"
+    assert seen_partial, "no step accepted part of a draft"

@@ -40,6 +40,7 @@ def gpu_matmul(nib, params, x, rows, cols, gs):
     native.check(L.rai_gpu_w4a8_pack(n_d.data_ptr(), p_d.data_ptr(), rows, cols, gs, packed.data_ptr(), s))
     native.check(L.rai_gpu_w4a8_matmul(out.data_ptr(), packed.data_ptr(), x_d.data_ptr(), rows, cols, tokens, gs,
                                        scratch.data_ptr(), sb, s))
+    native.check(L.rai_gpu_kernel_status(s))  # no device wait of the call gave up
     torch.cuda.synchronize()
     return out.cpu().numpy()
 

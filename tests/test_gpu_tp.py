@@ -52,7 +52,7 @@ def tp_models(tmp_path_factory):
     return out
 
 
-def _launch(path, world, tmp, steps=6, k=8):
+def _launch(path, world, tmp, steps=6, k=8, mode="decode"):
     port = _free_port()
     procs, outs = [], []
     env = dict(os.environ, NCCL_NVLS_ENABLE="0")
@@ -60,7 +60,7 @@ def _launch(path, world, tmp, steps=6, k=8):
         o = str(tmp / f"w{world}_r{r}.json")
         outs.append(o)
         procs.append(subprocess.Popen([sys.executable, os.path.join(HERE, "tp_worker.py"), path, str(world), str(r),
-                                       str(port), o, str(steps), str(k)], env=env, stdout=subprocess.PIPE,
+                                       str(port), o, str(steps), str(k), mode], env=env, stdout=subprocess.PIPE,
                                       stderr=subprocess.STDOUT, text=True))
     logs = []
     for p in procs:
@@ -100,3 +100,21 @@ def test_tp_decode_matches_one_gpu(tp_models, tmp_path, name, world):
             assert val == ref["kv"][key], f"rank {r}: KV rows of layer/head {key} differ"
         if "logits" in ref:
             assert got["logits"] == ref["logits"], f"rank {r}: logits differ"
+
+
+def test_tp_wait_times_out_and_fails_the_model(tp_models, tmp_path):
+    """A rank that stops making the calls (between steps) turns its peer's
+    next step into RAI_ERR_TIMEOUT after the bounded cross-GPU waits (about a
+    second each, later waits of the same forward give up at once), and the
+    model then refuses work instead of reading exchanges of another forward.
+    No GPU faults or hangs: the waiting kernels return, and the dropped rank
+    stays alive (its memory mapped) until the other's calls have returned."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    r0, r1 = _launch(tp_models["tp-llama3"], 2, tmp_path, mode="timeout")
+    assert r0["first_step"] == r1["first_step"] >= 1
+    code = r0["timeout_code"]
+    (c1, t1), (c2, t2), (c3, _) = r0["codes"]
+    assert c1 == code and t1 < 30.0, r0["codes"]
+    assert c2 == code and t2 < 1.0, r0["codes"]  # failed state: refused without running
+    assert c3 == code  # no new decoder on a failed model either
