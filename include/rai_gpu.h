@@ -127,6 +127,19 @@ RAI_API int rai_gpu_model_create_tp(const uint8_t* blob, size_t len, int device,
 RAI_API int rai_gpu_tp_handle(rai_model* model, void* handle, size_t cap);
 RAI_API int rai_gpu_tp_connect(rai_model* model, const void* handles, size_t n);
 
+/* Which kernel the model's dense 4-bit linears run on (no reference
+ * counterpart: the reference has one CPU kernel). 0 (auto, the default or
+ * RAI_GEMM_MODE=auto): forward passes of fewer than 64 rows (a single
+ * stream's verify step) run the bit-exact kernel; passes of 64 rows or more
+ * (prefill chunks, many streams' verify rows) run the tcgen05 kernel, whose
+ * int32 group dots are exact but whose f32 scaling runs in another order than
+ * the reference's, so logits agree to the BASELINE tolerance (max|d| <=
+ * 1e-3 max|logit|) rather than bit for bit. 1: always bit-exact. 2: always
+ * the tcgen05 kernel. Multi-GPU models always run exact. Set it before the
+ * model's decoders run (a step graph records the mode it was built with). */
+RAI_API int rai_gpu_model_set_gemm_mode(rai_model* model, int mode);
+RAI_API int rai_gpu_model_gemm_mode(const rai_model* model, int* mode);
+
 /* LookupDecoder::new (rai-infer/src/lookup.rs:192-209): context window =
  * min(max_ctx, model max_context); allocates the KV cache on the device. */
 RAI_API int rai_gpu_decoder_create(rai_model* model, size_t max_ctx, rai_dec** out);
@@ -237,6 +250,20 @@ RAI_API int rai_gpu_w4a8_matmul(float* out, const void* packed, const float* inp
  * gave up since the last query (that call's output is incomplete), else
  * RAI_OK. The status word is per device and cleared by the query. */
 RAI_API int rai_gpu_kernel_status(void* stream);
+
+/* The same linear on the tcgen05 tensor cores (w4a8_matmul,
+ * rai-infer/src/gemm.rs:1774-1919, to the BASELINE tolerance: the int32
+ * group dots are exact; per group acc += dot * (w_scale * x_scale) +
+ * w_zero * x_sum in f32 fused multiply-adds, another rounding order than the
+ * reference's eight lane accumulators), on activations quantized by
+ * rai_gpu_w4a8_quantize. `workspace` (device, rai_gpu_w4a8_tol_workspace_bytes,
+ * zeroed once before its first use; calls leave it zeroed) lets launches with
+ * few row tiles split the groups over more SMs; NULL runs without the split.
+ * Calls sharing a workspace must not overlap on the GPU. */
+RAI_API size_t rai_gpu_w4a8_tol_workspace_bytes(void);
+RAI_API int rai_gpu_w4a8_matmul_tol_prequant(float* out, const void* packed, const void* scratch, size_t rows,
+                                             size_t cols, size_t tokens, size_t group_size, void* workspace,
+                                             size_t workspace_bytes, void* stream);
 
 /* rai_gpu_w4a8_matmul without a caller scratch buffer and without any
  * allocation: the quantized activations go to a 2 MiB file-scope device

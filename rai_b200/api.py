@@ -97,6 +97,19 @@ class RaiModel:
         blob = b"".join(handles)
         check(native.lib().rai_gpu_tp_connect(self._h, blob, len(handles)))
 
+    GEMM_MODES = {"auto": 0, "exact": 1, "tol": 2}
+
+    def set_gemm_mode(self, mode: str) -> None:
+        """Kernel of the dense linears: "auto" (bit-exact below 64 rows per
+        forward, the tcgen05 kernel to the BASELINE tolerance from there on),
+        "exact" or "tol". Set before the model's decoders run."""
+        check(native.lib().rai_gpu_model_set_gemm_mode(self._h, self.GEMM_MODES[mode]))
+
+    def gemm_mode(self) -> str:
+        m = C.c_int()
+        check(native.lib().rai_gpu_model_gemm_mode(self._h, C.byref(m)))
+        return {v: k for k, v in self.GEMM_MODES.items()}[m.value]
+
     def close(self) -> None:
         if getattr(self, "_h", None):
             native.lib().rai_gpu_model_destroy(self._h)

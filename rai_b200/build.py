@@ -17,7 +17,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(HERE)
 CSRC = os.path.join(HERE, "csrc")
 LIB = os.path.join(HERE, "librai_gpu.so")
-SOURCES = ["kernels_gemm.cu", "kernels_gemm_tc.cu", "kernels_layers.cu", "kernels_moe.cu", "kernels_sample.cu", "runtime.cu", "convert_host.cpp"]
+SOURCES = ["kernels_gemm.cu", "kernels_gemm_tc.cu", "kernels_gemm_tol.cu", "kernels_layers.cu", "kernels_moe.cu", "kernels_sample.cu", "runtime.cu", "convert_host.cpp"]
 HEADERS = ["common.cuh", "kernels.h", "layers.h", "moe.h", "quant.cuh", "raimodel_format.h", "tp.cuh"]
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 FLAGS = [

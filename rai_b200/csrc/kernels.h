@@ -124,9 +124,32 @@ struct GemmTp {
   int n_out = 1;
   float* outs[kMaxTp] = {};
 };
+// Which kernel a dense 4-bit linear runs on. kGemmAuto: the exact kernel
+// below kTolMinRows rows (the launch's static row budget), the tolerance-mode
+// tcgen05 kernel from there on (prefill, many-stream verify); kGemmExact:
+// always exact; kGemmTol: always the tcgen05 kernel. Linears with a
+// tensor-parallel exchange and the 8-bit tied head always run exact.
+enum GemmMode : int { kGemmAuto = 0, kGemmExact = 1, kGemmTol = 2 };
+constexpr int kTolMinRows = 64;
+struct GemmPolicy {
+  int mode = kGemmAuto;
+  void* ws = nullptr;  // split-K workspace of the tcgen05 kernel (gemm_tol_workspace_bytes), may be null
+  size_t ws_bytes = 0;
+};
 cudaError_t gemm_exact(const PackedLinear& w, const ActBuf& act, int M, float* out, int ld_out,
                        const GemmEpilogue& epi, uint32_t* err, cudaStream_t s, bool pdl = false,
-                       const int* m_dev = nullptr, const GemmTp* tp = nullptr);
+                       const int* m_dev = nullptr, const GemmTp* tp = nullptr, const GemmPolicy* pol = nullptr);
+
+// The W4A8 linear to the BASELINE tolerance on the tcgen05 tensor cores
+// (kernels_gemm_tol.cu): exact int32 group dots, f32 scaling in a different
+// order than the reference. `ws` (may be null: no split-K) is a per-stream
+// workspace of gemm_tol_workspace_bytes() whose counters start at zero
+// (cudaMemset once; the kernel leaves them at zero).
+size_t gemm_tol_workspace_bytes();
+cudaError_t init_gemm_tol_attributes();
+cudaError_t gemm_tol(const PackedLinear& w, const ActBuf& act, int M, float* out, int ld_out,
+                     const GemmEpilogue& epi, uint32_t* err, cudaStream_t s, const int* m_dev, void* ws,
+                     size_t ws_bytes);
 
 // The same linear (4-bit weights, one output buffer, no exchange) on the
 // tcgen05 tensor cores; gemm_exact takes this path when RAI_GEMM_TC=1 and the

@@ -880,6 +880,7 @@ cudaError_t init_gemm_attributes() {
   set(gemm_exact_kernel<8, Gemm8N1>); set(gemm_exact_kernel<8, Gemm8N2>);
   set(gemm_exact_kernel<8, Gemm8N3>); set(gemm_exact_kernel<8, Gemm8N4>);
   if (e == cudaSuccess) e = init_gemm_tc_attributes();
+  if (e == cudaSuccess) e = init_gemm_tol_attributes();
   return e;
 }
 
@@ -970,9 +971,12 @@ cudaError_t swiglu_quant(const float* gu, int ff, int M, const int* m_dev, int g
 
 cudaError_t gemm_exact(const PackedLinear& w, const ActBuf& act, int M, float* out, int ld_out,
                        const GemmEpilogue& epi, uint32_t* err, cudaStream_t s, bool pdl, const int* m_dev,
-                       const GemmTp* tp) {
+                       const GemmTp* tp, const GemmPolicy* pol) {
   if (M <= 0) return cudaSuccess;
   const bool exchange = tp && tp->link.world > 1;
+  if (w.wbits == 4 && !exchange && pol &&
+      (pol->mode == kGemmTol || (pol->mode == kGemmAuto && M >= kTolMinRows)))
+    return gemm_tol(w, act, M, out, ld_out, epi, err, s, m_dev, pol->ws, pol->ws_bytes);
   if (w.wbits == 4 && w.tc && !exchange && gemm_tc_enabled())
     return gemm_tc(w, act, M, out, ld_out, epi, err, s, m_dev);
   GemmParams gp = {};

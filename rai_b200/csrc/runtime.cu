@@ -148,6 +148,9 @@ struct rai_model {
   // refuses all further work; every rank must destroy and re-create its model
   // together (fresh arenas, counters at zero).
   bool failed = false;
+  // Kernel choice of the dense 4-bit linears (rai::GemmMode; RAI_GEMM_MODE
+  // = auto | exact | tol sets the default). Multi-GPU models run exact.
+  int gemm_mode = rai::kGemmAuto;
 
   template <class T>
   int alloc(T** p, size_t bytes) {
@@ -322,6 +325,15 @@ int expf_table(rai::ExpfTable* out) {
   return RAI_OK;
 }
 
+// RAI_GEMM_MODE = auto | exact | tol (default auto).
+int default_gemm_mode() {
+  const char* e = std::getenv("RAI_GEMM_MODE");
+  if (!e) return rai::kGemmAuto;
+  if (std::strcmp(e, "exact") == 0) return rai::kGemmExact;
+  if (std::strcmp(e, "tol") == 0) return rai::kGemmTol;
+  return rai::kGemmAuto;
+}
+
 int check_supported(const Config& c, const raimodel::Model& L) {
   if (c.group_size != 64 && c.group_size != 128)
     return fail(RAI_ERR_UNSUPPORTED, "group_size " + std::to_string(c.group_size) + " (this build runs 64 or 128)");
@@ -417,9 +429,13 @@ struct Batch {
   uint8_t* act_ff_peer[rai::kMaxTp] = {};
   unsigned long long* best_peer[rai::kMaxTp] = {};
   float* moe_eo_peer[rai::kMaxTp] = {};  // expert parallelism: rank t's expert-output rows
+  // Split-K workspace of the tcgen05 linear (allocated before the first
+  // forward that may use it; its counters start at zero).
+  void* tol_ws = nullptr;
+  size_t tol_ws_bytes = 0;
   cudaGraphExec_t graph = nullptr;
   size_t graph_kernels = 0;
-  uint32_t graph_key[4] = {0, 0, 0, 0};
+  uint32_t graph_key[5] = {0, 0, 0, 0, 0};
   cudaEvent_t ev0 = nullptr, ev1 = nullptr;
   float last_us = 0.f;
 
@@ -645,8 +661,31 @@ int create_batch(rai_model* m, const std::vector<rai_dec*>& decs, int R, int row
 // is set; rows[] gives each row's (position, stream), ids[] its token; the
 // rows' attention segments are segs[] (nseg of them, or *nseg_dev when set;
 // at most seg_rows rows each).
+// The kernel policy of a batch's dense linears.
+rai::GemmPolicy gemm_policy(const Batch* B) {
+  rai::GemmPolicy pol;
+  pol.mode = B->m->tp_world > 1 ? rai::kGemmExact : B->m->gemm_mode;
+  pol.ws = B->tol_ws;
+  pol.ws_bytes = B->tol_ws_bytes;
+  return pol;
+}
+
+// Allocate the batch's tcgen05 workspace before a forward of `rows` rows
+// that may run the tcgen05 linear (never during graph capture).
+int ensure_tol_ws(Batch* B, int rows) {
+  const rai::GemmPolicy pol = gemm_policy(B);
+  const bool may = pol.mode == rai::kGemmTol || (pol.mode == rai::kGemmAuto && rows >= rai::kTolMinRows);
+  if (!may || B->tol_ws) return RAI_OK;
+  const size_t bytes = rai::gemm_tol_workspace_bytes();
+  if (int rc = B->alloc(&B->tol_ws, bytes)) return rc;
+  RAI_CUDA(cudaMemset(B->tol_ws, 0, bytes));
+  B->tol_ws_bytes = bytes;
+  return RAI_OK;
+}
+
 int forward(Batch* B, int M, const int* m_dev, int nseg, const int* nseg_dev, int seg_rows, bool logits) {
   rai_model* Mo = B->m;
+  const rai::GemmPolicy pol = gemm_policy(B);
   const Config& c = Mo->cfg;
   cudaStream_t s = B->stream;
   const int h = c.hidden_size, hd = c.head_dim;
@@ -699,7 +738,7 @@ int forward(Batch* B, int M, const int* m_dev, int nseg, const int* nseg_dev, in
                              tp && li > 0 ? slot(li - 1, rai::kXchHiddenDown) : -1, err));
     rai::GemmEpilogue e_qkv;
     if (L.bias_qkv) { e_qkv.mode = rai::kEpiBias; e_qkv.bias = L.bias_qkv; }
-    RAI_CUDA(rai::gemm_exact(L.qkv, B->act_h, M, B->qkv, qd + 2 * kvd, e_qkv, err, s, false, m_dev));
+    RAI_CUDA(rai::gemm_exact(L.qkv, B->act_h, M, B->qkv, qd + 2 * kvd, e_qkv, err, s, false, m_dev, nullptr, &pol));
     RAI_CUDA(rai::launch_qkv_post(B->qkv, qd + 2 * kvd, B->q, nh, nkv, hd, L.q_norm, L.k_norm, Mo->qk_mode, eps,
                                   Mo->rope_cos, Mo->rope_sin, B->kv, (int)li, B->rows, m_dev, M, s));
     RAI_CUDA(rai::launch_attention(B->q, B->attn, B->kv, (int)li, B->rows, m_dev, M, B->segs, nseg_dev, nseg,
@@ -707,7 +746,7 @@ int forward(Batch* B, int M, const int* m_dev, int nseg, const int* nseg_dev, in
                                    Mo->expf, err, s));
     RAI_CUDA(rai::quantize_act(B->attn, qd, M, m_dev, qd, gs, 4, B->act_q, s, tp ? &dst_q : nullptr));
     if (tp) gtp.wait_slot = slot(li, rai::kXchActQ);
-    RAI_CUDA(rai::gemm_exact(L.o, B->act_q, M, hid_out, h, e_res, err, s, false, m_dev, tp ? &gtp : nullptr));
+    RAI_CUDA(rai::gemm_exact(L.o, B->act_q, M, hid_out, h, e_res, err, s, false, m_dev, tp ? &gtp : nullptr, &pol));
     if (L.moe) {
       // mlp_block (model.rs:208-261): route, expert SwiGLU MLPs grouped by
       // expert, weighted sum in pick order, residual add.
@@ -731,11 +770,13 @@ int forward(Batch* B, int M, const int* m_dev, int nseg, const int* nseg_dev, in
     }
     RAI_CUDA(rai::norm_quant(B->hidden, L.post_norm, h, eps, B->resid, M, m_dev, gs, 4, B->act_h, s, nullptr, link,
                              tp ? slot(li, rai::kXchHiddenO) : -1, err));
-    RAI_CUDA(rai::gemm_exact(L.gateup, B->act_h, M, B->gu, 2 * ffd, rai::GemmEpilogue{}, err, s, false, m_dev));
+    RAI_CUDA(rai::gemm_exact(L.gateup, B->act_h, M, B->gu, 2 * ffd, rai::GemmEpilogue{}, err, s, false, m_dev,
+                             nullptr, &pol));
     RAI_CUDA(rai::swiglu_quant(B->gu, ffd, M, m_dev, gs, Mo->expf, B->act_ff, s, tp ? &dst_ff : nullptr, r * ffd,
                                (int)c.intermediate_size));
     if (tp) gtp.wait_slot = slot(li, rai::kXchActFF);
-    RAI_CUDA(rai::gemm_exact(L.down, B->act_ff, M, hid_out, h, e_res, err, s, false, m_dev, tp ? &gtp : nullptr));
+    RAI_CUDA(rai::gemm_exact(L.down, B->act_ff, M, hid_out, h, e_res, err, s, false, m_dev, tp ? &gtp : nullptr,
+                             &pol));
   }
   if (logits || tp) {
     // Under tensor parallelism the last layer's hidden exchange is awaited
@@ -747,7 +788,7 @@ int forward(Batch* B, int M, const int* m_dev, int nseg, const int* nseg_dev, in
   }
   if (logits)
     RAI_CUDA(rai::gemm_exact(Mo->head, B->act_head, M, B->logits, Mo->v_l, rai::GemmEpilogue{}, err, s, false,
-                             m_dev));
+                             m_dev, nullptr, &pol));
   return RAI_OK;
 }
 
@@ -798,7 +839,7 @@ int validate_cfg(const rai_lookup_cfg* cfg) {
 int ensure_graph(Batch* B, const rai_lookup_cfg* cfg) {
   uint32_t tbits = 0;
   std::memcpy(&tbits, &cfg->temperature, 4);
-  uint32_t key[4] = {cfg->max_draft, cfg->max_ngram, cfg->min_ngram, tbits};
+  uint32_t key[5] = {cfg->max_draft, cfg->max_ngram, cfg->min_ngram, tbits, (uint32_t)B->m->gemm_mode};
   if (B->graph && std::memcmp(key, B->graph_key, sizeof(key)) == 0) return RAI_OK;
   if (B->graph) {
     cudaGraphExecDestroy(B->graph);
@@ -807,6 +848,7 @@ int ensure_graph(Batch* B, const rai_lookup_cfg* cfg) {
   const int R = (int)cfg->max_draft + 1;
   const int rows = B->n * R;
   if (rows > B->rows_cap) return fail(RAI_ERR_INVALID, "batch row budget exceeded");
+  if (int rc = ensure_tol_ws(B, rows)) return rc;
   cudaStream_t s = B->stream;
   cudaGraph_t g = nullptr;
   RAI_CUDA(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal));
@@ -946,6 +988,7 @@ int forward_host_rows(Batch* B, int M, bool logits) {
   for (int i = 0; i < nseg; ++i) seg_rows = std::max(seg_rows, B->segs_host[i].nrows);
   RAI_CUDA(cudaMemcpyAsync(B->rows, B->rows_host, M * sizeof(rai::RowInfo), cudaMemcpyHostToDevice, s));
   RAI_CUDA(cudaMemcpyAsync(B->segs, B->segs_host, nseg * sizeof(rai::AttnSeg), cudaMemcpyHostToDevice, s));
+  if (int rc = ensure_tol_ws(B, M)) return rc;
   return forward(B, M, nullptr, nseg, nullptr, seg_rows, logits);
 }
 
@@ -1074,6 +1117,7 @@ static int create_model(const uint8_t* blob, size_t len, int device, int tp_rank
   RAI_CUDA(rai::init_moe_attributes());
   auto M = std::make_unique<rai_model>();
   M->device = device;
+  M->gemm_mode = default_gemm_mode();
   M->layout = std::move(layout);
   M->cfg = M->layout.cfg;
   const Config& c = M->cfg;
@@ -1285,6 +1329,20 @@ int rai_gpu_model_info(const rai_model* m, rai_model_info* info) {
   info->tied_embeddings = m->layout.has_lm_head ? 0 : 1;
   info->version = c.version;
   info->device_bytes = m->device_bytes;
+  return RAI_OK;
+}
+
+int rai_gpu_model_set_gemm_mode(rai_model* m, int mode) {
+  if (!m) return fail(RAI_ERR_INVALID, "null argument");
+  if (mode != rai::kGemmAuto && mode != rai::kGemmExact && mode != rai::kGemmTol)
+    return fail(RAI_ERR_INVALID, "gemm mode must be 0 (auto), 1 (exact) or 2 (tolerance)");
+  m->gemm_mode = mode;
+  return RAI_OK;
+}
+
+int rai_gpu_model_gemm_mode(const rai_model* m, int* mode) {
+  if (!m || !mode) return fail(RAI_ERR_INVALID, "null argument");
+  *mode = m->tp_world > 1 ? rai::kGemmExact : m->gemm_mode;
   return RAI_OK;
 }
 
@@ -1856,6 +1914,28 @@ int rai_gpu_w4a8_matmul_prequant(float* out, const void* packed, const void* scr
   if (int rc = kernel_err_word(&err)) return rc;
   RAI_CUDA(rai::gemm_exact(w, a, (int)tokens, out, (int)rows, rai::GemmEpilogue{}, err,
                            static_cast<cudaStream_t>(stream)));
+  return RAI_OK;
+}
+
+size_t rai_gpu_w4a8_tol_workspace_bytes(void) { return rai::gemm_tol_workspace_bytes(); }
+
+int rai_gpu_w4a8_matmul_tol_prequant(float* out, const void* packed, const void* scratch, size_t rows, size_t cols,
+                                     size_t tokens, size_t gs, void* workspace, size_t workspace_bytes,
+                                     void* stream) {
+  if (!out || !packed || !scratch) return fail(RAI_ERR_INVALID, "null argument");
+  if (int rc = check_linear(rows, cols, tokens, gs)) return rc;
+  if (workspace && workspace_bytes < rai::gemm_tol_workspace_bytes())
+    return fail(RAI_ERR_INVALID, "workspace smaller than rai_gpu_w4a8_tol_workspace_bytes()");
+  RAI_CUDA(rai::init_gemm_attributes());
+  ActBuf a;
+  a.data = static_cast<uint8_t*>(const_cast<void*>(scratch));
+  a.tok_alloc = (int)rai::round_up(tokens, 8);
+  a.groups = (int)rai::ceil_div(cols, gs);
+  const PackedLinear w = packed_view(packed, rows, cols, gs);
+  uint32_t* err = nullptr;
+  if (int rc = kernel_err_word(&err)) return rc;
+  RAI_CUDA(rai::gemm_tol(w, a, (int)tokens, out, (int)rows, rai::GemmEpilogue{}, err, static_cast<cudaStream_t>(stream),
+                         nullptr, workspace, workspace_bytes));
   return RAI_OK;
 }
 

@@ -111,6 +111,11 @@ def lib() -> C.CDLL:
         L.rai_gpu_step_kernel_count.argtypes = [P, PSZ]
         L.rai_gpu_expf_range.argtypes = [C.c_uint32, SZ, P, P]
         L.rai_gpu_kernel_status.argtypes = [P]
+        L.rai_gpu_model_set_gemm_mode.argtypes = [P, C.c_int]
+        L.rai_gpu_model_gemm_mode.argtypes = [P, C.POINTER(C.c_int)]
+        L.rai_gpu_w4a8_tol_workspace_bytes.argtypes = []
+        L.rai_gpu_w4a8_tol_workspace_bytes.restype = SZ
+        L.rai_gpu_w4a8_matmul_tol_prequant.argtypes = [P, P, P, SZ, SZ, SZ, SZ, P, SZ, P]
         L.rai_gpu_attention.argtypes = [P, P, P, P, SZ, SZ, SZ, SZ, SZ, C.c_float, P, P]
         L.rai_rtn_quantize.argtypes = [P, SZ, SZ, C.c_int, SZ, P, P, C.c_int]
         L.rai_synth_normal_f16.argtypes = [C.c_uint64, C.c_uint64, SZ, C.c_float, P, C.c_int]

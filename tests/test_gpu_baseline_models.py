@@ -12,7 +12,10 @@ Bar (BASELINE north_star): logits within max|d| <= 1e-3 * max|logit|;
 greedy tokens and drafted / accepted / produced counts identical, a token
 difference only being allowed at a row whose oracle top-2 margin is below
 that tolerance; the KV watermark equals pos + produced after every step.
-Prompts are shorter than bench.py's so the oracle finishes in seconds.
+Prompts are shorter than bench.py's so the oracle finishes in seconds. The
+prompts' prefill (64 rows or more per forward) runs on the tcgen05 linear,
+so the cached K/V agree with the oracle to the tolerance, not bit for bit;
+the single-stream verify steps that follow run the exact kernel.
 """
 import numpy as np
 import pytest
@@ -39,11 +42,17 @@ def _tol(want):
 
 
 def _prompt(preset, seed, vocab):
+    """The config's prompt recipe at the test's length, ending with a copy
+    of an earlier 24-token span (the Qwen recipe's own last span), so the
+    n-gram search drafts from the first step whatever the vocabulary."""
     name, n, recipe = CASES[preset]
     cfg = dict(bench.CONFIGS[name])
     if recipe:
         cfg["recipe"] = recipe
-    return bench.prompt_for(cfg, seed, n, vocab)
+    p = bench.prompt_for(cfg, seed, n, vocab)
+    src = n // 3
+    p[n - 24:] = p[src:src + 24]
+    return p
 
 
 _loaded = {}
@@ -107,7 +116,13 @@ def test_verify_logits_match_oracle(oracle, preset):
     exact = sum(np.array_equal(a, b) for a, b in zip(got, want))
     print(f"{preset}: max|d| {err:.3g} (tol {_tol(want):.3g}), {exact}/{len(rows)} rows bit-identical")
     assert err <= _tol(want)
-    assert np.array_equal(np.argmax(got, 1), np.argmax(want, 1))
+    # The prompt's prefill ran on the tcgen05 linear (>= 64 rows), so a row's
+    # argmax may differ only where the oracle's top-2 margin is below the
+    # tolerance.
+    for g, w in zip(got, want):
+        if np.argmax(g) != np.argmax(w):
+            top2 = np.sort(w)[-2:]
+            assert top2[1] - top2[0] <= _tol(want)
 
 
 def _run_steps(oracle, preset, k, seed, steps=STEPS):
