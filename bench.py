@@ -232,12 +232,14 @@ def gemm_traffic_from_profile(m: int):
     return best[1] if best else None
 
 
-def measure_gemm(torch, N: int, K: int, M: int, iters: int = 50, gs: int = 128):
-    """Time the exact W4A8 GEMM kernel alone (activations quantized once, then
-    the GEMM launch on them) for N output rows, K columns and M tokens,
-    rotating through enough packed weight copies to exceed L2, CUDA events
-    on the launching stream. Weights in the reference format: codes uniform
-    0..15, scale f16 U(0.001, 0.02), zero = -8 scale."""
+def measure_gemm(torch, N: int, K: int, M: int, iters: int = 50, gs: int = 128, kernel: str = "exact"):
+    """Time one W4A8 GEMM kernel alone (activations quantized once, then the
+    GEMM launch on them) for N output rows, K columns and M tokens, rotating
+    through enough packed weight copies to exceed L2, CUDA events on the
+    launching stream. kernel: "exact" (the bit-exact kernel) or "tcgen05"
+    (the tolerance-mode tcgen05 kernel with its split-K workspace). Weights
+    in the reference format: codes uniform 0..15, scale f16 U(0.001, 0.02),
+    zero = -8 scale."""
     from rai_b200 import native
     L = native.lib()
     dev = torch.device("cuda")
@@ -259,22 +261,31 @@ def measure_gemm(torch, N: int, K: int, M: int, iters: int = 50, gs: int = 128):
     scratch = torch.empty(sb, dtype=torch.uint8, device=dev)
     out = torch.empty(M, N, device=dev)
     native.check(L.rai_gpu_w4a8_quantize(x.data_ptr(), K, M, gs, scratch.data_ptr(), sb, s))
+    if kernel == "tcgen05":
+        wsb = L.rai_gpu_w4a8_tol_workspace_bytes()
+        ws = torch.zeros(wsb, dtype=torch.uint8, device=dev)
+
+        def launch(i):
+            native.check(L.rai_gpu_w4a8_matmul_tol_prequant(out.data_ptr(), packs[i % copies].data_ptr(),
+                                                            scratch.data_ptr(), N, K, M, gs, ws.data_ptr(), wsb, s))
+    else:
+        def launch(i):
+            native.check(L.rai_gpu_w4a8_matmul_prequant(out.data_ptr(), packs[i % copies].data_ptr(),
+                                                        scratch.data_ptr(), N, K, M, gs, s))
     for i in range(5):
-        native.check(L.rai_gpu_w4a8_matmul_prequant(out.data_ptr(), packs[i % copies].data_ptr(),
-                                                    scratch.data_ptr(), N, K, M, gs, s))
+        launch(i)
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
     for i in range(iters):
-        native.check(L.rai_gpu_w4a8_matmul_prequant(out.data_ptr(), packs[i % copies].data_ptr(),
-                                                    scratch.data_ptr(), N, K, M, gs, s))
+        launch(i)
     e1.record()
     torch.cuda.synchronize()
     us = e0.elapsed_time(e1) * 1e3 / iters
     alg = N * K // 2 + N * (-(-K // gs)) * 4  # gemm_bench.rs:73-76 accounting
     del packs
     torch.cuda.empty_cache()
-    return {"N": N, "K": K, "M": M, "us_per_launch": us, "alg_bytes": alg, "gbs": alg / us / 1e3,
+    return {"N": N, "K": K, "M": M, "kernel": kernel, "us_per_launch": us, "alg_bytes": alg, "gbs": alg / us / 1e3,
             "int8_tops": 2.0 * M * N * K / us / 1e6}
 
 
@@ -289,10 +300,14 @@ def gemm_sweep(torch, iters: int):
     """the isolated W4A8 GEMM at the Llama-3.1-8B
     projection shapes (K x N), M in {1,2,4,8,9,16,64,512}."""
     out = []
+    peak, _ = int8_peak_tops()
     for K, N in [(4096, 4096), (4096, 1024), (4096, 14336), (14336, 4096)]:
         for M in [1, 2, 4, 8, 9, 16, 64, 512]:
-            r = measure_gemm(torch, N, K, M, iters)
-            out.append({k: (round(v, 3) if isinstance(v, float) else v) for k, v in r.items()})
+            for kernel in (("exact", "tcgen05") if M >= 64 else ("exact",)):
+                r = measure_gemm(torch, N, K, M, iters, kernel=kernel)
+                if M >= 64:
+                    r["int8_tensor_frac"] = r["int8_tops"] / peak
+                out.append({k: (round(v, 4) if isinstance(v, float) else v) for k, v in r.items()})
     return out
 
 
@@ -475,6 +490,11 @@ def main():
     ap.add_argument("--gemm-only", action="store_true",
                     help="time only the isolated verify GEMM (for a small ncu capture) and print it")
     ap.add_argument("--gemm-shape", default=None, help="N,K,M for --gemm-only (default: the config's verify GEMM)")
+    ap.add_argument("--gemm-kernel", default="exact", choices=["exact", "tcgen05"],
+                    help="kernel of --gemm-only (tcgen05: the tolerance-mode tensor-core linear)")
+    ap.add_argument("--gemm-mode", default="exact", choices=["exact", "auto", "tol"],
+                    help="kernel of the model's linears in the step (exact: bit-exact, the parity mode; auto / tol: "
+                         "the tcgen05 throughput modes)")
     args = ap.parse_args()
     global CFG
     CFG = dict(CONFIGS[args.config])
@@ -487,7 +507,7 @@ def main():
         torch.cuda.set_device(0)
         if args.gemm_shape:
             n_, k_, m_ = (int(v) for v in args.gemm_shape.split(","))
-            print(json.dumps(measure_gemm(torch, n_, k_, m_, iters=args.steps)), flush=True)
+            print(json.dumps(measure_gemm(torch, n_, k_, m_, iters=args.steps, kernel=args.gemm_kernel)), flush=True)
         else:
             print(json.dumps(measure_gemm_roofline(torch, CFG["k"] + 1, iters=args.steps)), flush=True)
         return
@@ -540,6 +560,8 @@ def main():
     else:
         model = rai_b200.RaiModel.load(path, device=local)
         mine = streams_for_rank(CFG["streams"], world, rank, js["split"])
+    if args.gemm_mode != "exact":
+        model.set_gemm_mode(args.gemm_mode)
     vocab = model.config["vocab_size"]
     K_DRAFT = CFG["k"]
     max_ctx = CFG["prompt"] + (args.steps + args.warmup + 2) * (K_DRAFT + 1) + 16
@@ -630,7 +652,7 @@ def main():
             "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": steps,
             "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
             "scaling": "weak" if js["weak"] else "strong", "vs_baseline": None, "dtype": "int8xu4->int32->f32",
-            "data": "synthetic", "config": config_object(args, world),
+            "data": "synthetic", "config": config_object(args, world), "gemm_mode": args.gemm_mode,
             "per_stream_tok_s": produced / dev_s / total_streams,
             "verify_step_us": dev_s * 1e6 / steps,
             "tokens_per_step": produced / (total_streams * steps),

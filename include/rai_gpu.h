@@ -98,6 +98,8 @@ typedef struct {
  * validates like RaiModelFile::open (format.rs:557-637), uploads the blob to
  * HBM once and repacks the weights into the device layout. */
 RAI_API int rai_gpu_model_create(const uint8_t* blob, size_t len, int device, rai_model** out);
+/* Refused (RAI_ERR_INVALID) while decoders created on the model are alive:
+ * destroy them first. */
 RAI_API int rai_gpu_model_destroy(rai_model* model);
 RAI_API int rai_gpu_model_info(const rai_model* model, rai_model_info* info);
 
@@ -128,15 +130,19 @@ RAI_API int rai_gpu_tp_handle(rai_model* model, void* handle, size_t cap);
 RAI_API int rai_gpu_tp_connect(rai_model* model, const void* handles, size_t n);
 
 /* Which kernel the model's dense 4-bit linears run on (no reference
- * counterpart: the reference has one CPU kernel). 0 (auto, the default or
- * RAI_GEMM_MODE=auto): forward passes of fewer than 64 rows (a single
- * stream's verify step) run the bit-exact kernel; passes of 64 rows or more
- * (prefill chunks, many streams' verify rows) run the tcgen05 kernel, whose
- * int32 group dots are exact but whose f32 scaling runs in another order than
- * the reference's, so logits agree to the BASELINE tolerance (max|d| <=
- * 1e-3 max|logit|) rather than bit for bit. 1: always bit-exact. 2: always
- * the tcgen05 kernel. Multi-GPU models always run exact. Set it before the
- * model's decoders run (a step graph records the mode it was built with). */
+ * counterpart: the reference has one CPU kernel). 1 (exact, the default):
+ * the bit-exact kernel everywhere. 0 (auto): forward passes of fewer than 64
+ * rows run the bit-exact kernel, passes of 64 rows or more (prefill chunks,
+ * many streams' verify rows) the tcgen05 kernel. 2 (tol): always the tcgen05
+ * kernel. The tcgen05 kernel's int32 group dots are exact and its outputs
+ * agree with the reference's to a few f32 ulps, but the reference
+ * re-quantizes every linear's input to int8, which turns ulp-level
+ * differences into code flips: on seeded random-weight models a 1-ulp change
+ * of one constant moves the reference's own logits by up to ~18% of their
+ * range, and modes 0 / 2 move them as much. They are throughput modes, not
+ * parity modes. RAI_GEMM_MODE=exact|auto|tol sets the default. Multi-GPU
+ * models always run exact. Set it before the model's decoders run (a step
+ * graph records the mode it was built with). */
 RAI_API int rai_gpu_model_set_gemm_mode(rai_model* model, int mode);
 RAI_API int rai_gpu_model_gemm_mode(const rai_model* model, int* mode);
 

@@ -100,9 +100,12 @@ class RaiModel:
     GEMM_MODES = {"auto": 0, "exact": 1, "tol": 2}
 
     def set_gemm_mode(self, mode: str) -> None:
-        """Kernel of the dense linears: "auto" (bit-exact below 64 rows per
-        forward, the tcgen05 kernel to the BASELINE tolerance from there on),
-        "exact" or "tol". Set before the model's decoders run."""
+        """Kernel of the dense linears: "exact" (the default: bit-exact),
+        "auto" (the tcgen05 kernel for forwards of 64 rows or more) or "tol"
+        (always the tcgen05 kernel). The tcgen05 kernel agrees with the
+        reference to a few f32 ulps per linear, which the reference's int8
+        re-quantization amplifies: "auto" and "tol" are throughput modes,
+        not parity modes. Set before the model's decoders run."""
         check(native.lib().rai_gpu_model_set_gemm_mode(self._h, self.GEMM_MODES[mode]))
 
     def gemm_mode(self) -> str:
@@ -111,12 +114,17 @@ class RaiModel:
         return {v: k for k, v in self.GEMM_MODES.items()}[m.value]
 
     def close(self) -> None:
+        """Release the device copy; refused (RaiError) while decoders
+        created on this model are still open."""
         if getattr(self, "_h", None):
-            native.lib().rai_gpu_model_destroy(self._h)
+            check(native.lib().rai_gpu_model_destroy(self._h))
             self._h = None
 
     def __del__(self):
-        self.close()
+        # Decoders keep a reference to their model, so none is alive here.
+        if getattr(self, "_h", None):
+            native.lib().rai_gpu_model_destroy(self._h)
+            self._h = None
 
 
 def _u32(a: Sequence[int]) -> np.ndarray:

@@ -124,11 +124,12 @@ struct GemmTp {
   int n_out = 1;
   float* outs[kMaxTp] = {};
 };
-// Which kernel a dense 4-bit linear runs on. kGemmAuto: the exact kernel
-// below kTolMinRows rows (the launch's static row budget), the tolerance-mode
-// tcgen05 kernel from there on (prefill, many-stream verify); kGemmExact:
-// always exact; kGemmTol: always the tcgen05 kernel. Linears with a
-// tensor-parallel exchange and the 8-bit tied head always run exact.
+// Which kernel a dense 4-bit linear runs on. kGemmExact (the default): the
+// bit-exact kernel. kGemmAuto: the exact kernel below kTolMinRows rows (the
+// launch's static row budget), the tolerance-mode tcgen05 kernel from there
+// on (prefill, many-stream verify); kGemmTol: always the tcgen05 kernel.
+// Linears with a tensor-parallel exchange and the 8-bit tied head always run
+// exact.
 enum GemmMode : int { kGemmAuto = 0, kGemmExact = 1, kGemmTol = 2 };
 constexpr int kTolMinRows = 64;
 struct GemmPolicy {

@@ -17,6 +17,7 @@
 #include <cstdio>
 #include <cstring>
 #include <memory>
+#include <atomic>
 #include <mutex>
 #include <string>
 #include <vector>
@@ -149,8 +150,12 @@ struct rai_model {
   // together (fresh arenas, counters at zero).
   bool failed = false;
   // Kernel choice of the dense 4-bit linears (rai::GemmMode; RAI_GEMM_MODE
-  // = auto | exact | tol sets the default). Multi-GPU models run exact.
-  int gemm_mode = rai::kGemmAuto;
+  // = exact | auto | tol sets the default, exact unless set). Multi-GPU
+  // models run exact.
+  int gemm_mode = rai::kGemmExact;
+  // Decoders created on this model and not yet destroyed: the model refuses
+  // to be destroyed under them (their teardown reads the model).
+  std::atomic<int> live_decoders{0};
 
   template <class T>
   int alloc(T** p, size_t bytes) {
@@ -325,13 +330,13 @@ int expf_table(rai::ExpfTable* out) {
   return RAI_OK;
 }
 
-// RAI_GEMM_MODE = auto | exact | tol (default auto).
+// RAI_GEMM_MODE = exact | auto | tol (default exact).
 int default_gemm_mode() {
   const char* e = std::getenv("RAI_GEMM_MODE");
-  if (!e) return rai::kGemmAuto;
-  if (std::strcmp(e, "exact") == 0) return rai::kGemmExact;
+  if (!e) return rai::kGemmExact;
+  if (std::strcmp(e, "auto") == 0) return rai::kGemmAuto;
   if (std::strcmp(e, "tol") == 0) return rai::kGemmTol;
-  return rai::kGemmAuto;
+  return rai::kGemmExact;
 }
 
 int check_supported(const Config& c, const raimodel::Model& L) {
@@ -1028,6 +1033,7 @@ rai_dec::~rai_dec() {
   if (kc) cudaFree(kc);
   if (vc) cudaFree(vc);
   cudaSetDevice(prev);
+  --m->live_decoders;
 }
 
 // ---------------------------------------------------------------------------
@@ -1306,6 +1312,8 @@ int rai_gpu_tp_connect(rai_model* m, const void* handles, size_t n) {
 
 int rai_gpu_model_destroy(rai_model* model) {
   if (!model) return RAI_OK;
+  if (const int n = model->live_decoders.load())
+    return fail(RAI_ERR_INVALID, "model still has " + std::to_string(n) + " live decoder(s): destroy them first");
   drop_batches_of_model(model);
   delete model;
   return RAI_OK;
@@ -1356,6 +1364,7 @@ int rai_gpu_decoder_create(rai_model* m, size_t max_ctx, rai_dec** out) {
   const Config& c = m->cfg;
   auto d = std::make_unique<rai_dec>();
   d->m = m;
+  ++m->live_decoders;  // ~rai_dec gives it back, on every path
   d->max_ctx = (int)ctx;
   // Under tensor parallelism a rank caches only its own KV heads.
   size_t kv = (size_t)c.num_layers * m->nkv_l * ctx * c.head_dim * sizeof(float);

@@ -13,9 +13,8 @@ greedy tokens and drafted / accepted / produced counts identical, a token
 difference only being allowed at a row whose oracle top-2 margin is below
 that tolerance; the KV watermark equals pos + produced after every step.
 Prompts are shorter than bench.py's so the oracle finishes in seconds. The
-prompts' prefill (64 rows or more per forward) runs on the tcgen05 linear,
-so the cached K/V agree with the oracle to the tolerance, not bit for bit;
-the single-stream verify steps that follow run the exact kernel.
+default (exact) kernels run, so tokens are expected to match exactly; the
+margin rule is the written allowance.
 """
 import numpy as np
 import pytest
@@ -61,10 +60,11 @@ _loaded = {}
 def _models(preset, oracle):
     """(path, GPU model, oracle model) of a preset, one preset held at a
     time (the 8B and MoE models take ~4 GB each on both sides)."""
+    import gc
     import rai_b200
     if preset not in _loaded:
-        for k in list(_loaded):
-            _loaded.pop(k)[1].close()
+        _loaded.clear()  # decoders of a failed test may still hold the old model; it goes with them
+        gc.collect()
         path = bench.model_path(0, 1, preset)
         _loaded[preset] = (path, rai_b200.RaiModel.load(path), oracle.Model.load(path))
     return _loaded[preset]
@@ -116,9 +116,8 @@ def test_verify_logits_match_oracle(oracle, preset):
     exact = sum(np.array_equal(a, b) for a, b in zip(got, want))
     print(f"{preset}: max|d| {err:.3g} (tol {_tol(want):.3g}), {exact}/{len(rows)} rows bit-identical")
     assert err <= _tol(want)
-    # The prompt's prefill ran on the tcgen05 linear (>= 64 rows), so a row's
-    # argmax may differ only where the oracle's top-2 margin is below the
-    # tolerance.
+    # A row's argmax may differ only where the oracle's top-2 margin is below
+    # the tolerance.
     for g, w in zip(got, want):
         if np.argmax(g) != np.argmax(w):
             top2 = np.sort(w)[-2:]
@@ -169,7 +168,9 @@ def test_tinyllama_lookup_steps_other_k(oracle, k):
 
 def test_tinyllama_step_batch_matches_independent_oracle_streams(oracle):
     """The serving-loop batch (one verify forward over every stream's rows)
-    at the bench's model: each stream equals its own oracle decoder."""
+    at the bench's model: each stream equals its own oracle decoder (a
+    divergence is only allowed at a row whose oracle top-2 margin is below
+    the tolerance, after which that stream is no longer compared)."""
     import rai_b200
     path, gm, om = _models("tinyllama-1.1b", oracle)
     vocab = gm.config["vocab_size"]
@@ -184,11 +185,18 @@ def test_tinyllama_step_batch_matches_independent_oracle_streams(oracle):
     ctxs = [list(p) for p in prompts]
     cfg = rai_b200.LookupConfig(max_draft=k, max_ngram=3, min_ngram=1)
     drafted = 0
+    live = [True] * n
     for _ in range(STEPS):
         toks, counts, mets = batch.step(cfg)
         for i in range(n):
+            if not live[i]:
+                continue
             ot, om_ = ods[i].step(poss[i], ctxs[i], k)
-            assert toks[i, : counts[i]].tolist() == ot, (i, poss[i])
+            got = toks[i, : counts[i]].tolist()
+            if got != ot:
+                _explain_divergence(path, gm, oracle, ctxs[i], poss[i], k, got, ot, windows[i])
+                live[i] = False
+                continue
             assert (int(mets["drafted"][i]), int(mets["accepted"][i]), int(mets["produced"][i])) == \
                 (om_["drafted"], om_["accepted"], om_["produced"])
             drafted += om_["drafted"]

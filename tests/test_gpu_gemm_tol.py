@@ -53,7 +53,7 @@ def tol_matmul(nib, params, x, rows, cols, gs, split=True, repeat=1):
 def _check(got, want):
     assert np.all(np.isfinite(got)), "unwritten or non-finite outputs"
     err = float(np.max(np.abs(got - want)))
-    scale = float(np.max(np.abs(want)))
+    scale = max(float(np.max(np.abs(want))), 1e-30)
     print(f"max|d| {err:.3g} = {err / scale:.3g} of max|out|")
     assert err <= REL * scale
 
