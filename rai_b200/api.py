@@ -121,9 +121,13 @@ class RaiModel:
             self._h = None
 
     def __del__(self):
-        # Decoders keep a reference to their model, so none is alive here.
+        # Decoders keep a reference to their model, so none is alive here. At
+        # interpreter exit the binding module may already be torn down.
         if getattr(self, "_h", None):
-            native.lib().rai_gpu_model_destroy(self._h)
+            try:
+                native.lib().rai_gpu_model_destroy(self._h)
+            except Exception:
+                pass
             self._h = None
 
 

@@ -210,6 +210,15 @@ def test_tinyllama_step_batch_matches_independent_oracle_streams(oracle):
 
 # ---------------------------------------------------------------------------
 # Forced acceptance: drafts that are the model's own greedy continuation.
+#
+# LookupDecoder::step drafts from the caller's `context` (find_ngram_draft,
+# lookup.rs:131-171) while the verify forward reads the decoder's KV cache
+# (lookup.rs:260-425). So a context equal to the prefilled prompt except for
+# an earlier copy of its final 3-gram followed by chosen tokens makes the
+# n-gram search draft exactly those tokens without changing what the model
+# predicts. Planting the model's greedy continuation makes every draft
+# accepted; changing one planted token makes the step accept the tokens
+# before it, emit the target's token in its place and roll back the rest.
 
 def _greedy(gm, prompt, n, window):
     """The model's greedy continuation of `prompt` (n tokens, decode_one)."""
@@ -225,83 +234,43 @@ def _greedy(gm, prompt, n, window):
     return out
 
 
-def _planted(prompt, at, cont):
-    """The prompt with its last 3 tokens followed by `cont` copied to
-    position `at`: the n-gram search at the prompt's end then drafts `cont`."""
-    g = prompt[-3:]
-    p = list(prompt)
-    p[at:at + 3 + len(cont)] = g + list(cont)
-    return p
-
-
-def _plant_at(prompt, k):
-    """Where the planted copy goes: close enough to the end that it is the
-    most recent earlier occurrence of the final 3-gram (the search scans
-    from the end), clear of the final tokens."""
-    return len(prompt) - 3 - (3 + k) - 8
-
-
-def _forced_case(gm, prompt, k, window, rounds=4):
-    """Plant the greedy continuation and re-plant until it is a fixed point
-    (one planted copy among many positions rarely moves the argmax)."""
-    at = _plant_at(prompt, k)
-    cont = _greedy(gm, prompt, k + 1, window)
-    p = _planted(prompt, at, cont[:k])
-    for _ in range(rounds):
-        c2 = _greedy(gm, p, k + 1, window)
-        if c2[:k] == cont[:k]:
-            return p, c2
-        cont = c2
-        p = _planted(prompt, at, cont[:k])
-    return p, _greedy(gm, p, k + 1, window)
-
-
 @pytest.mark.parametrize("preset", ["tinyllama-1.1b", "qwen2.5-0.5b"])
 def test_forced_acceptance_partial_full_and_rollback(oracle, preset):
-    """Drafts equal to the model's greedy continuation are all accepted and
-    the bonus token follows; with one drafted token changed the step accepts
-    the tokens before it, emits the target's token in its place and rolls
-    the cache back past the rejected rows (lookup.rs:359-411). The device
-    must equal the oracle on tokens, counts and the KV watermark in both."""
+    """Full acceptance plus bonus, partial acceptance with a correction, and
+    a rejected first draft, each compared with the oracle on tokens, counts
+    and the KV watermark, then one more ordinary step on the true history."""
     import rai_b200
     path, gm, om = _models(preset, oracle)
     vocab = gm.config["vocab_size"]
     k = 8
-    seen_full = seen_partial = False
-    for seed in range(40, 46):
-        base = _prompt(preset, seed, vocab)[:160]
-        window = len(base) + 4 * (k + 1)
-        p, cont = _forced_case(gm, base, k, window)
-        for perturb in (None, 3):
-            ctx = list(p)
-            if perturb is not None:
-                # Change the planted draft's token `perturb` (the copy, not
-                # the prompt's tail), so the draft differs from the target
-                # there.
-                at = _plant_at(base, k) + 3 + perturb
-                ctx[at] = (ctx[at] + 1) % vocab
-            gd, od = rai_b200.LookupDecoder(gm, window), oracle.Decoder(om, window)
-            pos = gd.prefill(ctx)
-            assert od.prefill(ctx) == pos
-            cfg = rai_b200.LookupConfig(max_draft=k, max_ngram=3, min_ngram=1)
-            for _ in range(2):
-                gt, gmet = gd.step(pos, ctx, cfg)
-                ot, omet = od.step(pos, ctx, k)
-                if gt != ot:
-                    _explain_divergence(path, gm, oracle, ctx, pos, k, gt, ot, window)
-                    break
-                assert (gmet.drafted, gmet.accepted, gmet.produced) == \
-                    (omet["drafted"], omet["accepted"], omet["produced"])
-                assert gmet.produced == gmet.accepted + 1
-                if gmet.drafted == k and gmet.accepted == k:
-                    seen_full = True
-                if 0 < gmet.accepted < gmet.drafted:
-                    seen_partial = True
-                ctx += gt
-                pos += len(gt)
-                assert gd.kv_filled(0) == pos == od.kv_filled(0)
-            gd.close()
-        if seen_full and seen_partial:
-            break
-    assert seen_full, "no step accepted a whole draft (planted continuation not a fixed point for any seed)"
-    assert seen_partial, "no step accepted part of a draft"
+    base = _prompt(preset, 40, vocab)[:160]
+    window = len(base) + 4 * (k + 1)
+    cont = _greedy(gm, base, k + 1, window)
+    at = len(base) - 3 - (3 + k) - 2  # the most recent earlier occurrence of the final 3-gram
+    for bad, want_acc in ((None, k), (3, 3), (0, 0)):
+        plant = list(cont[:k])
+        if bad is not None:
+            plant[bad] = (plant[bad] + 1) % vocab
+        ctx = list(base)
+        ctx[at:at + 3 + k] = base[-3:] + plant
+        gd, od = rai_b200.LookupDecoder(gm, window), oracle.Decoder(om, window)
+        pos = gd.prefill(base)
+        assert od.prefill(base) == pos
+        cfg = rai_b200.LookupConfig(max_draft=k, max_ngram=3, min_ngram=1)
+        gt, gmet = gd.step(pos, ctx, cfg)
+        ot, omet = od.step(pos, ctx, k)
+        assert gt == ot
+        assert (gmet.drafted, gmet.accepted, gmet.produced) == (omet["drafted"], omet["accepted"], omet["produced"])
+        assert gmet.drafted == k and gmet.matched_ngram == 3
+        assert gmet.accepted == want_acc and gmet.produced == want_acc + 1
+        assert gt == cont[:want_acc + 1]  # accepted drafts, then the correction or the bonus
+        pos += len(gt)
+        assert gd.kv_filled(0) == pos == od.kv_filled(0)
+        assert gd.kv_filled(gm.config["num_layers"] - 1) == pos
+        # The next step runs on the true history after the rollback.
+        hist = base + gt
+        gt2, gmet2 = gd.step(pos, hist, cfg)
+        ot2, omet2 = od.step(pos, hist, k)
+        assert gt2 == ot2 and gmet2.produced == omet2["produced"]
+        assert gd.kv_filled(0) == pos + len(gt2) == od.kv_filled(0)
+        gd.close()
