@@ -840,6 +840,11 @@ using Gemm4N1 = GemmCfg<1, 1, 1, 2, 4>;
 using Gemm4N2 = GemmCfg<2, 1, 1, 2, 1>;
 using Gemm4N3 = GemmCfg<3, 1, 1, 1, 1>;
 using Gemm4N4 = GemmCfg<4, 1, 2, 1, 1>;
+// Candidates with one 8-token N tile per consumer warp (more warps in flight,
+// each with a shorter chain): 32-token items over 16 consumer warps, 16-token
+// items over 8. RAI_GEMM_VARIANT=1 selects them (A/B measurement).
+using Gemm4N4W = GemmCfg<4, 1, 4, 1, 1>;
+using Gemm4N2W = GemmCfg<2, 1, 2, 1, 1>;
 // Launches with fewer tiles than SMs: each 64-row tile split over 2 or 4
 // CTAs.
 using Gemm4N1S2 = GemmCfg<1, 2, 1, 2, 4, true>;
@@ -875,6 +880,7 @@ cudaError_t init_gemm_attributes() {
   };
   set(gemm_exact_kernel<4, Gemm4N1>); set(gemm_exact_kernel<4, Gemm4N2>);
   set(gemm_exact_kernel<4, Gemm4N3>); set(gemm_exact_kernel<4, Gemm4N4>);
+  set(gemm_exact_kernel<4, Gemm4N4W>); set(gemm_exact_kernel<4, Gemm4N2W>);
   set(gemm_exact_kernel<4, Gemm4N1S2>); set(gemm_exact_kernel<4, Gemm4N1S4>);
   set(gemm_exact_kernel<4, Gemm4N2S2>); set(gemm_exact_kernel<4, Gemm4N2S4>);
   set(gemm_exact_kernel<8, Gemm8N1>); set(gemm_exact_kernel<8, Gemm8N2>);
@@ -1007,6 +1013,12 @@ cudaError_t gemm_exact(const PackedLinear& w, const ActBuf& act, int M, float* o
   (void)pdl;  // every GEMM launch uses programmatic dependent launch
   if (w.wbits == 4) {
     const int split = gemm_split(w.tiles * chunks);
+    static const int variant = [] {
+      const char* e = std::getenv("RAI_GEMM_VARIANT");
+      return e ? std::atoi(e) : 0;
+    }();
+    if (variant == 1 && ntiles == 4) return launch_gemm<4, Gemm4N4W>(gp, w.tiles, chunks, s);
+    if (variant == 1 && ntiles == 2 && split == 1) return launch_gemm<4, Gemm4N2W>(gp, w.tiles, chunks, s);
     switch (ntiles) {
       case 1:
         if (split == 4) return launch_gemm<4, Gemm4N1S4>(gp, w.tiles, chunks, s);

@@ -51,8 +51,8 @@ namespace {
 
 constexpr int kTolRows = 128;
 constexpr int kTolTok = 128;
-constexpr int kTolStages = 4;
-constexpr int kTolASlots = 2;
+constexpr int kTolStages = 5;
+constexpr int kTolASlots = 4;
 constexpr int kTolScal = 4;
 constexpr int kTolSlots = 4;  // TMEM accumulator slots of 128 columns
 constexpr int kTolCols = kTolSlots * 128;
