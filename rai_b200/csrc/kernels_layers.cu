@@ -18,6 +18,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <cstdlib>
 
 #include "common.cuh"
 #include "layers.h"
@@ -753,6 +754,226 @@ __global__ void __launch_bounds__(256) attn_pv_split_kernel(const StreamKV* __re
 }
 
 // ---------------------------------------------------------------------------
+// Fused attention for launches of many short segments (a many-stream verify
+// step, each stream's rows cut into segments of at most kFusedRows). CTA
+// (kv head, segment): the segment's scores and probabilities stay in shared
+// memory, and the stream's K and V rows are read once each per segment,
+// through a double-buffered ring of 16-byte asynchronous copies. Same
+// arithmetic, in the same order, as the three kernels above:
+//   scores: per (row, head, position) the 8-lane FMA dot, the horizontal-sum
+//     tree, times scale (then softcap);
+//   softmax: one warp per (row, head): max; Schraudolph's exp for the first
+//     (n/8)*8 positions, the host-libm expf for the tail; the 8-lane ordered
+//     sum, the tree, the tail in order; p = e * (1/sum);
+//   P.V: out = fma(p_t, v_t[d], out) over t in order.
+constexpr int kFusedRows = 2;
+constexpr int kFusedThreads = 256;
+
+template <int HD>
+struct FusedCfg {
+  static constexpr int CH = HD >= 128 ? 64 : 128;      // positions per K / V chunk
+  static constexpr int LD = HD + 4;                    // padded row stride (floats)
+  static constexpr int TPP = kFusedThreads / CH;       // score threads per position
+  static constexpr int NDP = HD / 2;                   // P.V dim pairs
+  static constexpr int HG = kFusedThreads / NDP;       // P.V head groups
+  static constexpr int HMAX = (8 + HG - 1) / HG;       // P.V heads per thread (hpk <= 8)
+};
+
+template <int HD>
+__global__ void __launch_bounds__(kFusedThreads) attn_fused_kernel(
+    const float* __restrict__ q, const StreamKV* __restrict__ kv, int layer, const AttnSeg* __restrict__ segs,
+    const int* nseg_dev, int nseg_max, int nh, int nkv, float scale, float softcap, int n_alloc, ExpfTable et,
+    float* __restrict__ out) {
+  pdl_wait_prior();
+  pdl_launch_dependents();
+  constexpr int CH = FusedCfg<HD>::CH, LD = FusedCfg<HD>::LD, TPP = FusedCfg<HD>::TPP;
+  constexpr int NDP = FusedCfg<HD>::NDP, HG = FusedCfg<HD>::HG, HMAX = FusedCfg<HD>::HMAX;
+  extern __shared__ __align__(16) float sm[];
+  const int hpk = nh / nkv;
+  float* kb = sm;                          // [2][CH][LD] K, then V, chunks
+  float* sq = kb + 2 * CH * LD;            // [kFusedRows][hpk][HD] the segment's q rows
+  float* ss = sq + kFusedRows * hpk * HD;  // [kFusedRows * hpk][n_alloc] scores, then p
+  const int kvh = blockIdx.x;
+  const int nseg = active_rows(nseg_dev, nseg_max);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  for (int si = blockIdx.y; si < nseg; si += gridDim.y) {
+    const AttnSeg sg = segs[si];
+    const int nrows = sg.nrows;  // <= kFusedRows (the launch guarantees it)
+    const int n_max = sg.pos0 + nrows;
+    const int nch = (n_max + CH - 1) / CH;
+    const int npairs = nrows * hpk;  // (row, head) pairs, index r * hpk + h
+    const StreamKV sk_ = kv[sg.stream];
+    const size_t hoff = ((size_t)layer * nkv + kvh) * sk_.max_ctx * HD;
+    // Chunk c of K or V into buffer c & 1 (an empty commit past the end keeps
+    // the wait counts uniform).
+    auto load = [&](const float* base, int c) {
+      if (c < nch) {
+        const int t0 = c * CH, cnt = min(CH, n_max - t0);
+        float* dst = kb + (c & 1) * CH * LD;
+        for (int i = tid; i < cnt * (HD / 4); i += kFusedThreads) {
+          const int row = i / (HD / 4), c4 = i - row * (HD / 4);
+          cp_async16(dst + row * LD + 4 * c4, base + (size_t)(t0 + row) * HD + 4 * c4);
+        }
+      }
+      cp_async_commit();
+    };
+    load(sk_.k + hoff, 0);
+    {
+      const int per_row = hpk * HD;
+      for (int i = tid; i < nrows * per_row; i += kFusedThreads) {
+        const int r = i / per_row, o = i - r * per_row;
+        sq[i] = q[(size_t)(sg.row0 + r) * nh * HD + (size_t)kvh * per_row + o];
+      }
+    }
+    // ---- scores: thread (position of the chunk, subset of the pairs) ----
+    const int pl = tid % CH, part = tid / CH;
+    for (int c = 0; c < nch; ++c) {
+      load(sk_.k + hoff, c + 1);
+      cp_async_wait<1>();  // chunk c has landed
+      __syncthreads();
+      const int t = c * CH + pl;
+      if (t < n_max) {
+        float kr[HD];
+        const float4* kp = reinterpret_cast<const float4*>(kb + (c & 1) * CH * LD + pl * LD);
+#pragma unroll
+        for (int i = 0; i < HD / 4; ++i) {
+          const float4 v = kp[i];
+          kr[4 * i] = v.x; kr[4 * i + 1] = v.y; kr[4 * i + 2] = v.z; kr[4 * i + 3] = v.w;
+        }
+        // Rows r with pos0 + r >= t see position t.
+        const int r_first = max(0, t - sg.pos0);
+        for (int pi = part; pi < npairs; pi += TPP) {
+          if (pi / hpk < r_first) continue;
+          const float4* qh = reinterpret_cast<const float4*>(sq + pi * HD);
+          float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+          for (int cc = 0; cc < HD / 8; ++cc) {
+            const float4 a0 = qh[2 * cc], a1 = qh[2 * cc + 1];
+            acc[0] = __fmaf_rn(a0.x, kr[8 * cc + 0], acc[0]);
+            acc[1] = __fmaf_rn(a0.y, kr[8 * cc + 1], acc[1]);
+            acc[2] = __fmaf_rn(a0.z, kr[8 * cc + 2], acc[2]);
+            acc[3] = __fmaf_rn(a0.w, kr[8 * cc + 3], acc[3]);
+            acc[4] = __fmaf_rn(a1.x, kr[8 * cc + 4], acc[4]);
+            acc[5] = __fmaf_rn(a1.y, kr[8 * cc + 5], acc[5]);
+            acc[6] = __fmaf_rn(a1.z, kr[8 * cc + 6], acc[6]);
+            acc[7] = __fmaf_rn(a1.w, kr[8 * cc + 7], acc[7]);
+          }
+          float sv = __fmul_rn(hsum8(acc), scale);
+          if (softcap > 0.f) sv = __fmul_rn(softcap, tanhf(__fdiv_rn(sv, softcap)));
+          ss[(size_t)pi * n_alloc + t] = sv;
+        }
+      }
+      __syncthreads();  // buffer c & 1 is refilled next
+    }
+    // V's first chunk streams in while the softmax runs.
+    load(sk_.v + hoff, 0);
+    // ---- softmax: one warp per (row, head) ----
+    for (int pi = warp; pi < npairs; pi += kFusedThreads / 32) {
+      const int n = sg.pos0 + pi / hpk + 1, n8 = (n / 8) * 8, cnt8 = n8 / 8;
+      float* se = ss + (size_t)pi * n_alloc;
+      float m = -INFINITY;
+      for (int t = lane; t < n; t += 32) m = fmaxf(m, se[t]);
+#pragma unroll
+      for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+      for (int t = lane; t < n; t += 32) {
+        const float x = __fsub_rn(se[t], m);
+        se[t] = t < n8 ? schraudolph(x) : expf_host(x, et);
+      }
+      __syncwarp();
+      float acc = 0.f;
+      if (lane < 8) {
+        int i = 0;
+        for (; i + 8 <= cnt8; i += 8) {
+          float v[8];
+#pragma unroll
+          for (int u = 0; u < 8; ++u) v[u] = se[8 * (i + u) + lane];
+#pragma unroll
+          for (int u = 0; u < 8; ++u) acc = __fadd_rn(acc, v[u]);
+        }
+        for (; i < cnt8; ++i) acc = __fadd_rn(acc, se[8 * i + lane]);
+      }
+      float a[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) a[u] = __shfl_sync(0xffffffffu, acc, u);
+      float sum = hsum8(a);
+      for (int t = n8; t < n; ++t) sum = __fadd_rn(sum, se[t]);
+      const float inv = __fdiv_rn(1.0f, sum);
+      __syncwarp();
+      for (int t = lane; t < n; t += 32) se[t] = __fmul_rn(se[t], inv);
+    }
+    // ---- P.V: thread (dim pair, head group), chains of its rows x heads ----
+    const int dp = tid % NDP, hg = tid / NDP;
+    float acc[kFusedRows][HMAX][2];
+#pragma unroll
+    for (int r = 0; r < kFusedRows; ++r)
+#pragma unroll
+      for (int j = 0; j < HMAX; ++j) acc[r][j][0] = acc[r][j][1] = 0.f;
+    for (int c = 0; c < nch; ++c) {
+      load(sk_.v + hoff, c + 1);
+      cp_async_wait<1>();
+      __syncthreads();  // chunk c of V and (first pass) every warp's p rows
+      const int t0 = c * CH, cnt = min(CH, n_max - t0);
+      const float* vb = kb + (c & 1) * CH * LD + 2 * dp;
+      int tl = 0;
+      if (t0 + cnt <= sg.pos0 + 1) {
+        // Every row sees the whole chunk: 4 positions per round, loads first.
+        for (; tl + 4 <= cnt; tl += 4) {
+          float2 v[4];
+#pragma unroll
+          for (int u = 0; u < 4; ++u) v[u] = *reinterpret_cast<const float2*>(vb + (tl + u) * LD);
+#pragma unroll
+          for (int r = 0; r < kFusedRows; ++r) {
+            if (r >= nrows) break;
+#pragma unroll
+            for (int j = 0; j < HMAX; ++j) {
+              const int h = hg + j * HG;
+              if (h >= hpk) break;
+              const float4 pq = *reinterpret_cast<const float4*>(ss + (size_t)(r * hpk + h) * n_alloc + t0 + tl);
+              const float p4[4] = {pq.x, pq.y, pq.z, pq.w};
+#pragma unroll
+              for (int u = 0; u < 4; ++u) {
+                acc[r][j][0] = __fmaf_rn(p4[u], v[u].x, acc[r][j][0]);
+                acc[r][j][1] = __fmaf_rn(p4[u], v[u].y, acc[r][j][1]);
+              }
+            }
+          }
+        }
+      }
+      for (; tl < cnt; ++tl) {
+        const int t = t0 + tl;
+        const float2 v = *reinterpret_cast<const float2*>(vb + tl * LD);
+#pragma unroll
+        for (int r = 0; r < kFusedRows; ++r) {
+          if (r >= nrows || t > sg.pos0 + r) continue;
+#pragma unroll
+          for (int j = 0; j < HMAX; ++j) {
+            const int h = hg + j * HG;
+            if (h >= hpk) break;
+            const float a = ss[(size_t)(r * hpk + h) * n_alloc + t];
+            acc[r][j][0] = __fmaf_rn(a, v.x, acc[r][j][0]);
+            acc[r][j][1] = __fmaf_rn(a, v.y, acc[r][j][1]);
+          }
+        }
+      }
+      __syncthreads();  // buffer c & 1 is refilled next
+    }
+#pragma unroll
+    for (int r = 0; r < kFusedRows; ++r) {
+      if (r >= nrows) break;
+#pragma unroll
+      for (int j = 0; j < HMAX; ++j) {
+        const int h = hg + j * HG;
+        if (h >= hpk) break;
+        *reinterpret_cast<float2*>(out + (size_t)(sg.row0 + r) * nh * HD + (size_t)(kvh * hpk + h) * HD + 2 * dp) =
+            make_float2(acc[r][j][0], acc[r][j][1]);
+      }
+    }
+    cp_async_wait<0>();
+    __syncthreads();  // shared memory is reused by the next segment
+  }
+}
+
+// ---------------------------------------------------------------------------
 // Argmax with the reference's total order (NaN -> -inf first) and ties to
 // the LAST index: max over (orderable key << 32 | index).
 __device__ __forceinline__ unsigned long long argmax_key(float v, uint32_t idx) {
@@ -992,6 +1213,24 @@ int pv_dim_slices(int hd, int hpk, int nseg_max, int nkv) {
   while (ds < kPvsMaxSlices && hd / (2 * ds) >= 4 && (base * 2 * ds <= 2 * sms || (hd / ds) * hpk > 256)) ds *= 2;
   return ds > 1 && (hd / ds) * hpk <= 256 ? ds : 1;
 }
+size_t fused_smem_bytes(int hd, int hpk, int n_alloc) {
+  const int ch = hd >= 128 ? 64 : 128;
+  return ((size_t)2 * ch * (hd + 4) + (size_t)kFusedRows * hpk * hd + (size_t)kFusedRows * hpk * n_alloc) *
+         sizeof(float);
+}
+// The fused kernel serves launches whose segments are all short and whose
+// (kv head, segment) pairs fill the SMs (a many-stream verify step), when the
+// segment's scores fit in shared memory. RAI_ATTN_FUSED=0 turns it off, 2
+// uses it for every launch of short segments (to test it on few streams).
+bool use_fused(int hd, int hpk, int seg_rows, int nseg_max, int nkv, int n_alloc) {
+  static const int mode = [] {
+    const char* e = std::getenv("RAI_ATTN_FUSED");
+    return e ? std::atoi(e) : 1;
+  }();
+  if (mode == 0 || seg_rows > kFusedRows || hpk > 8 || fused_smem_bytes(hd, hpk, n_alloc) > kAttnMaxSmem)
+    return false;
+  return mode == 2 || nseg_max * nkv >= device_sm_count();
+}
 size_t pvs_smem_bytes(int hd, int ds, int hpk, int rb_alloc) {
   return (size_t)kPvsStages * ((size_t)kPvsTile * (hd / ds) + (size_t)rb_alloc * hpk * kPvsTile) * sizeof(float);
 }
@@ -1057,8 +1296,14 @@ cudaError_t launch_attention(const float* q, float* out, const StreamKV* kv, int
   const int seg_grid = std::max(1, grid_cap(nseg_max * nkv * nch, 8) / (nkv * nch));
   dim3 g1(nkv, std::min(nseg_max, seg_grid), nch), g2(grid_cap(M, 1), nkv),
       g3(nkv, std::min(nseg_max, std::max(1, grid_cap(nseg_max * nkv, 3) / nkv)));
+  const bool fused = use_fused(hd, hpk, seg_rows, nseg_max, nkv, n_alloc);
+  const dim3 gf(nkv, std::min(nseg_max, std::max(1, grid_cap(nseg_max * nkv, 1) / nkv)));
+  const size_t smf = fused_smem_bytes(hd, hpk, n_alloc);
 #define RAI_ATTN(HDV)                                                                                        \
   case HDV:                                                                                                  \
+    if (fused)                                                                                               \
+      return launch_pdl(attn_fused_kernel<HDV>, gf, dim3(kFusedThreads), smf, s, q, kv, layer, segs,          \
+                        nseg_dev, nseg_max, nh, nkv, scale, softcap, n_alloc, et, out);                      \
     if (cudaError_t e = launch_pdl(attn_scores_kernel<HDV>, g1, dim3(ScoreCfg<HDV>::CHUNK), sm1, s, q, kv,   \
                                    layer, segs, nseg_dev, nseg_max, nh, nkv, scale, softcap, scores,        \
                                    n_alloc))                                                                \
@@ -1107,6 +1352,8 @@ cudaError_t init_layer_attributes() {
   const int bytes = (int)kAttnMaxSmem;
   cudaError_t e = cudaFuncSetAttribute(attn_softmax_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
 #define RAI_ATTR(HDV)                                                                                     \
+  if (e == cudaSuccess)                                                                                   \
+    e = cudaFuncSetAttribute(attn_fused_kernel<HDV>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes); \
   if (e == cudaSuccess)                                                                                   \
     e = cudaFuncSetAttribute(attn_pv_kernel<HDV, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes); \
   if (e == cudaSuccess) e = set_pv_split_attributes<HDV>(bytes);                                          \

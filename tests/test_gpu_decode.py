@@ -389,3 +389,52 @@ def test_model_refuses_destroy_under_live_decoders(tiny_model_paths):
         gm.close()
     gd.close()
     gm.close()
+
+
+@pytest.mark.parametrize("name", ["tiny-llama", "tiny-qwen", "tiny-llama3"])
+def test_many_streams_run_the_fused_attention_bit_exact(tiny_model_paths, oracle, name):
+    """32 streams at k = 8: the step's (kv head, segment) pairs fill the SMs,
+    so its attention runs the fused kernel (scores and probabilities in
+    shared memory). Every stream equals its own oracle decoder token for
+    token and count for count."""
+    import rai_b200
+    gm = rai_b200.RaiModel.load(tiny_model_paths[name])
+    om = oracle.Model.load(tiny_model_paths[name])
+    vocab = gm.config["vocab_size"]
+    n, k = 32, 8
+    gds = [rai_b200.LookupDecoder(gm, 160) for _ in range(n)]
+    ods = [oracle.Decoder(om, 160) for _ in range(n)]
+    prompts = [periodic_prompt(24 + (i % 7) * 5, vocab, seed=500 + i) for i in range(n)]
+    batch = rai_b200.StepBatch(gds)
+    poss = batch.prefill(prompts, batched=False)
+    assert poss == [od.prefill(p) for od, p in zip(ods, prompts)]
+    ctxs = [list(p) for p in prompts]
+    cfg = rai_b200.LookupConfig(max_draft=k, max_ngram=3, min_ngram=1)
+    drafted = 0
+    for _ in range(8):
+        toks, counts, mets = batch.step(cfg)
+        for i in range(n):
+            ot, om_ = ods[i].step(poss[i], ctxs[i], k)
+            assert toks[i, : counts[i]].tolist() == ot, (i, poss[i])
+            assert (int(mets["drafted"][i]), int(mets["accepted"][i]), int(mets["produced"][i])) == \
+                (om_["drafted"], om_["accepted"], om_["produced"])
+            drafted += om_["drafted"]
+            ctxs[i] += ot
+            poss[i] += len(ot)
+    assert drafted > 0
+
+
+def test_forced_fused_attention_on_few_streams(tiny_model_paths):
+    """RAI_ATTN_FUSED=2 (read once per process, so a child process) puts
+    every step's attention on the fused kernel: the single-stream and
+    few-stream lookup tests of this file pass unchanged with it."""
+    import os
+    import subprocess
+    import sys
+    here = os.path.dirname(os.path.abspath(__file__))
+    env = dict(os.environ, RAI_ATTN_FUSED="2")
+    r = subprocess.run([sys.executable, "-m", "pytest", os.path.join(here, "test_gpu_decode.py"), "-q", "-x",
+                        "-p", "no:cacheprovider", "-k",
+                        "lookup_steps_match_oracle or step_many or step_batch_matches or window_end or decode_one"],
+                       env=env, capture_output=True, text=True, timeout=900)
+    assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-2000:]
