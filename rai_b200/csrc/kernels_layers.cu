@@ -1218,14 +1218,18 @@ size_t fused_smem_bytes(int hd, int hpk, int n_alloc) {
   return ((size_t)2 * ch * (hd + 4) + (size_t)kFusedRows * hpk * hd + (size_t)kFusedRows * hpk * n_alloc) *
          sizeof(float);
 }
-// The fused kernel serves launches whose segments are all short and whose
-// (kv head, segment) pairs fill the SMs (a many-stream verify step), when the
-// segment's scores fit in shared memory. RAI_ATTN_FUSED=0 turns it off, 2
-// uses it for every launch of short segments (to test it on few streams).
+// The fused kernel can serve launches whose segments are all short and
+// whose (kv head, segment) pairs fill the SMs (a many-stream verify step),
+// when the segment's scores fit in shared memory. It is opt-in: measured on
+// the 64-stream TinyLlama step it is slower than the three kernels (6.73 vs
+// 4.67 ms per step): its ~160 KB of shared memory leave one CTA per SM with a
+// two-deep copy ring, too few bytes in flight against the three kernels' many
+// CTAs per SM. RAI_ATTN_FUSED=1 uses it where it applies, 2 for every launch
+// of short segments (to test it on few streams); unset or 0: never.
 bool use_fused(int hd, int hpk, int seg_rows, int nseg_max, int nkv, int n_alloc) {
   static const int mode = [] {
     const char* e = std::getenv("RAI_ATTN_FUSED");
-    return e ? std::atoi(e) : 1;
+    return e ? std::atoi(e) : 0;
   }();
   if (mode == 0 || seg_rows > kFusedRows || hpk > 8 || fused_smem_bytes(hd, hpk, n_alloc) > kAttnMaxSmem)
     return false;

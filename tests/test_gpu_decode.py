@@ -392,11 +392,11 @@ def test_model_refuses_destroy_under_live_decoders(tiny_model_paths):
 
 
 @pytest.mark.parametrize("name", ["tiny-llama", "tiny-qwen", "tiny-llama3"])
-def test_many_streams_run_the_fused_attention_bit_exact(tiny_model_paths, oracle, name):
-    """32 streams at k = 8: the step's (kv head, segment) pairs fill the SMs,
-    so its attention runs the fused kernel (scores and probabilities in
-    shared memory). Every stream equals its own oracle decoder token for
-    token and count for count."""
+def test_many_streams_bit_exact(tiny_model_paths, oracle, name):
+    """32 streams at k = 8 (the step's (kv head, segment) pairs fill the SMs,
+    where the opt-in fused attention would apply; test_fused_attention_
+    many_streams runs this test with it). Every stream equals its own oracle
+    decoder token for token and count for count."""
     import rai_b200
     gm = rai_b200.RaiModel.load(tiny_model_paths[name])
     om = oracle.Model.load(tiny_model_paths[name])
@@ -424,17 +424,21 @@ def test_many_streams_run_the_fused_attention_bit_exact(tiny_model_paths, oracle
     assert drafted > 0
 
 
-def test_forced_fused_attention_on_few_streams(tiny_model_paths):
-    """RAI_ATTN_FUSED=2 (read once per process, so a child process) puts
-    every step's attention on the fused kernel: the single-stream and
-    few-stream lookup tests of this file pass unchanged with it."""
+@pytest.mark.parametrize("mode,tests", [
+    ("2", "lookup_steps_match_oracle or step_many or step_batch_matches or window_end or decode_one"),
+    ("1", "many_streams_bit_exact")])
+def test_fused_attention(tiny_model_paths, mode, tests):
+    """The opt-in fused attention kernel (RAI_ATTN_FUSED, read once per
+    process, so a child process): with 2 it serves every step's attention,
+    and the single- and few-stream lookup tests of this file pass unchanged;
+    with 1 it serves launches whose segments fill the SMs, which the
+    32-stream test reaches."""
     import os
     import subprocess
     import sys
     here = os.path.dirname(os.path.abspath(__file__))
-    env = dict(os.environ, RAI_ATTN_FUSED="2")
+    env = dict(os.environ, RAI_ATTN_FUSED=mode)
     r = subprocess.run([sys.executable, "-m", "pytest", os.path.join(here, "test_gpu_decode.py"), "-q", "-x",
-                        "-p", "no:cacheprovider", "-k",
-                        "lookup_steps_match_oracle or step_many or step_batch_matches or window_end or decode_one"],
+                        "-p", "no:cacheprovider", "-k", tests],
                        env=env, capture_output=True, text=True, timeout=900)
     assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-2000:]
