@@ -570,6 +570,9 @@ def main():
     # The streams' histories live in the StepBatch (the serving-loop API):
     # a step is one C call on precomputed pointers plus a vectorized append.
     batch = rai_b200.StepBatch(decs)
+    # torch creates its CUDA context lazily, on its first synchronize: that
+    # second or so belongs before the timed prefill, not inside it.
+    torch.cuda.synchronize()
     barrier()
     t0 = time.perf_counter()
     batch.prefill(ctxs, batched=not tp_mode)
