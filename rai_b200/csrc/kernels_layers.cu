@@ -615,11 +615,16 @@ __global__ void __launch_bounds__(HPT > 1 ? kPvMaxThreadsH2 : kPvMaxThreads) att
 // carries out[r][h][d] = fma(p_t, v_t[d], out) over t in order for each of
 // the segment's rows (the chains of pv_body, so results are identical). The
 // rows' FMAs are interleaved per position (independent chains back to back).
-// V slices and p tiles stream through a kPvsStages-deep ring of 16-byte
-// cp.async copies issued by every thread (one barrier per tile).
-constexpr int kPvsStages = 4;
-constexpr int kPvsTile = 64;  // positions per tile
+// V slices and p tiles stream through an NS-deep ring of 16-byte cp.async
+// copies issued by every thread (one barrier per tile). In the tiles every
+// row sees whole, a thread with one or two rows runs its chain at the FMA
+// latency: the shared loads of the next 8 positions are issued before the
+// FMAs of the current 8, and the copy addresses need no divisions.
+constexpr int kPvsStages = 8;         // ring depth where it fits in shared memory
+constexpr int kPvsShallowStages = 4;  // otherwise
+constexpr int kPvsTile = 64;          // positions per tile
 constexpr int kPvsMaxSlices = 16;
+constexpr int kPvsMaxPairs = kSegRows * 8;  // (row, head) pairs of a segment
 
 // Rows r0 .. r0 + RG - 1 (those < nrows) over the 8 positions t .. t + 7 of
 // a full tile: p from shared memory, v[] already loaded.
@@ -643,12 +648,29 @@ __device__ __forceinline__ void pvs_rows8(float* acc, const float* ph, int pstri
       if (r0 + r < nrows) acc[r0 + r] = __fmaf_rn(p8[r][u], v[u], acc[r0 + r]);
 }
 
-template <int HD, int DS, int RB>
+// The 8 positions of chunk k of a tile (V column values and the rows' p).
+template <int HDS, int RB>
+__device__ __forceinline__ void pvs_chunk_load(const float* sv, const float* ph, int pstride, int nrows, int k,
+                                               float (&v)[8], float (&pq)[RB][8]) {
+#pragma unroll
+  for (int u = 0; u < 8; ++u) v[u] = sv[(8 * k + u) * HDS];
+#pragma unroll
+  for (int r = 0; r < RB; ++r) {
+    if (r < nrows) {
+      const float4 pa = *reinterpret_cast<const float4*>(ph + r * pstride + 8 * k);
+      const float4 pb = *reinterpret_cast<const float4*>(ph + r * pstride + 8 * k + 4);
+      pq[r][0] = pa.x; pq[r][1] = pa.y; pq[r][2] = pa.z; pq[r][3] = pa.w;
+      pq[r][4] = pb.x; pq[r][5] = pb.y; pq[r][6] = pb.z; pq[r][7] = pb.w;
+    }
+  }
+}
+
+template <int HD, int DS, int RB, int NS>
 __device__ __forceinline__ void pvs_body(const float* __restrict__ vbase, const float* __restrict__ p, int nh,
                                          int hpk, int kvh, const AttnSeg& sg, int n_alloc, int rb_alloc,
-                                         float* __restrict__ out, float* sm) {
-  constexpr int HDS = HD / DS, VT = kPvsTile, NS = kPvsStages, V4 = HDS / 4;
-  constexpr int RG = RB < 4 ? RB : 4;  // rows per interleaved group
+                                         float* __restrict__ out, float* sm, int* pofs) {
+  constexpr int HDS = HD / DS, VT = kPvsTile, V4 = HDS / 4, C4 = VT / 4;
+  constexpr bool kPipelined = RB <= 2;
   const int stage_floats = VT * HDS + rb_alloc * hpk * VT;
   const int tid = threadIdx.x, nthr = blockDim.x;
   const int d = tid % HDS, h = tid / HDS;
@@ -657,13 +679,20 @@ __device__ __forceinline__ void pvs_body(const float* __restrict__ vbase, const 
   const int n_max = sg.pos0 + nrows, n_all = sg.pos0 + 1;
   const int ntiles = (n_max + VT - 1) / VT;
   const int pstride = hpk * VT;  // p of (row r, head h) at ph + r * pstride
+  const int npairs = nrows * hpk;
   const float* prow0 = p + ((size_t)sg.row0 * nh + (size_t)kvh * hpk) * n_alloc;
   const float* vsl = vbase + (size_t)blockIdx.z * HDS;
+  // Offset of (row r, head hh)'s p row from prow0, pair rh = r * hpk + hh.
+  for (int rh = tid; rh < npairs; rh += nthr) {
+    const int r = rh / hpk, hh = rh - r * hpk;
+    pofs[rh] = (r * nh + hh) * n_alloc;
+  }
+  __syncthreads();
   // Every thread's share of tile `tile` (none past the end: the group is
   // still committed so the wait counts stay uniform).
   auto load = [&](int tile) {
     if (tile < ntiles) {
-      const int t0 = tile * VT, cnt = min(VT, n_max - t0), c4 = (cnt + 3) / 4;
+      const int t0 = tile * VT, cnt = min(VT, n_max - t0);
       float* sv = sm + (size_t)(tile % NS) * stage_floats;
       float* sp = sv + VT * HDS;
       const float* vt0 = vsl + (size_t)t0 * HD;
@@ -671,10 +700,17 @@ __device__ __forceinline__ void pvs_body(const float* __restrict__ vbase, const 
         const int r = i / V4, c = i - r * V4;
         cp_async16(sv + 4 * i, vt0 + r * HD + 4 * c);
       }
-      for (int i = tid; i < nrows * hpk * c4; i += nthr) {
-        const int rh = i / c4, c = i - rh * c4;
-        const int r = rh / hpk, hh = rh - r * hpk;
-        cp_async16(sp + rh * VT + 4 * c, prow0 + ((size_t)r * nh + hh) * n_alloc + t0 + 4 * c);
+      const int c4 = (cnt + 3) / 4;
+      if (c4 == C4) {
+        for (int j = tid; j < npairs * C4; j += nthr) {
+          const int rh = j / C4, c = j - rh * C4;
+          cp_async16(sp + rh * VT + 4 * c, prow0 + pofs[rh] + t0 + 4 * c);
+        }
+      } else {
+        for (int j = tid; j < npairs * c4; j += nthr) {
+          const int rh = j / c4, c = j - rh * c4;
+          cp_async16(sp + rh * VT + 4 * c, prow0 + pofs[rh] + t0 + 4 * c);
+        }
       }
     }
     cp_async_commit();
@@ -692,7 +728,22 @@ __device__ __forceinline__ void pvs_body(const float* __restrict__ vbase, const 
     const int t0 = tile * VT, cnt = min(VT, n_max - t0);
     const float* sv = sm + (size_t)(tile % NS) * stage_floats + d;
     const float* ph = sm + (size_t)(tile % NS) * stage_floats + VT * HDS + h * VT;
-    if (t0 + cnt <= n_all) {
+    if (kPipelined && t0 + VT <= n_all) {
+      // Whole tile, every row: 8 chunks of 8 positions, chunk k + 1's loads
+      // issued before chunk k's FMAs.
+      float v[2][8], pq[2][RB][8];
+      pvs_chunk_load<HDS, RB>(sv, ph, pstride, nrows, 0, v[0], pq[0]);
+#pragma unroll
+      for (int k = 0; k < VT / 8; ++k) {
+        if (k + 1 < VT / 8) pvs_chunk_load<HDS, RB>(sv, ph, pstride, nrows, k + 1, v[(k + 1) & 1], pq[(k + 1) & 1]);
+#pragma unroll
+        for (int u = 0; u < 8; ++u)
+#pragma unroll
+          for (int r = 0; r < RB; ++r)
+            if (r < nrows) acc[r] = __fmaf_rn(pq[k & 1][r][u], v[k & 1][u], acc[r]);
+      }
+    } else if (t0 + cnt <= n_all) {
+      constexpr int RG = RB < 4 ? RB : 4;  // rows per interleaved group
       int t = 0;
       for (; t + 8 <= cnt; t += 8) {
         float v[8];
@@ -725,7 +776,7 @@ __device__ __forceinline__ void pvs_body(const float* __restrict__ vbase, const 
   }
 }
 
-template <int HD, int DS>
+template <int HD, int DS, int NS>
 __global__ void __launch_bounds__(256) attn_pv_split_kernel(const StreamKV* __restrict__ kv, int layer,
                                                             const AttnSeg* __restrict__ segs, const int* nseg_dev,
                                                             int nseg_max, int nh, int nkv,
@@ -734,6 +785,7 @@ __global__ void __launch_bounds__(256) attn_pv_split_kernel(const StreamKV* __re
   pdl_wait_prior();
   pdl_launch_dependents();
   extern __shared__ __align__(16) float sm[];
+  __shared__ int pofs[kPvsMaxPairs];
   const int kvh = blockIdx.x;
   const int nseg = active_rows(nseg_dev, nseg_max);
   const int hpk = nh / nkv;
@@ -741,7 +793,7 @@ __global__ void __launch_bounds__(256) attn_pv_split_kernel(const StreamKV* __re
     const AttnSeg sg = segs[si];
     const StreamKV sk_ = kv[sg.stream];
     const float* vbase = sk_.v + ((size_t)layer * nkv + kvh) * sk_.max_ctx * HD;
-#define RAI_PVS(RB) pvs_body<HD, DS, RB>(vbase, p, nh, hpk, kvh, sg, n_alloc, rb_alloc, out, sm)
+#define RAI_PVS(RB) pvs_body<HD, DS, RB, NS>(vbase, p, nh, hpk, kvh, sg, n_alloc, rb_alloc, out, sm, pofs)
     if (sg.nrows <= 1) RAI_PVS(1);
     else if (sg.nrows <= 2) RAI_PVS(2);
     else if (sg.nrows <= 4) RAI_PVS(4);
@@ -1202,15 +1254,17 @@ int pv_heads_per_thread(int hpk, int seg_rows, int nseg_max, int nkv) {
 // P.V block: the compute threads (dim pair x head group), whole warps, plus
 // the producer warp.
 int pv_threads(int hd, int hpk, int hpt) { return ((hd / 2) * ((hpk + hpt - 1) / hpt) + 31) / 32 * 32 + 32; }
-// Head-dimension slices of the split P.V: the most (up to kPvsMaxSlices, at
-// least 4 columns each) that keep the launch within two CTAs per SM, and at
-// least enough for a CTA of at most 256 threads (HDS x hpk), when the
-// (kv head, segment) pairs alone do not fill the SMs; 1 = the pv_body path.
+// Head-dimension slices of the split P.V, when the (kv head, segment) pairs
+// alone do not fill the SMs (1 = the pv_body path): the thinnest slices (up
+// to kPvsMaxSlices, at least 4 columns each) that still give a CTA a warp of
+// threads (HDS x hpk >= 32), and at least enough for a CTA of at most 256
+// threads. Each thread's serial chain bounds the kernel, so the columns go
+// to as many CTAs, on as many SMs, as that allows.
 int pv_dim_slices(int hd, int hpk, int nseg_max, int nkv) {
   const int base = nseg_max * nkv, sms = device_sm_count();
   if (base >= sms) return 1;
   int ds = 1;
-  while (ds < kPvsMaxSlices && hd / (2 * ds) >= 4 && (base * 2 * ds <= 2 * sms || (hd / ds) * hpk > 256)) ds *= 2;
+  while (ds < kPvsMaxSlices && hd / (2 * ds) >= 4 && ((hd / (2 * ds)) * hpk >= 32 || (hd / ds) * hpk > 256)) ds *= 2;
   return ds > 1 && (hd / ds) * hpk <= 256 ? ds : 1;
 }
 size_t fused_smem_bytes(int hd, int hpk, int n_alloc) {
@@ -1235,8 +1289,12 @@ bool use_fused(int hd, int hpk, int seg_rows, int nseg_max, int nkv, int n_alloc
     return false;
   return mode == 2 || nseg_max * nkv >= device_sm_count();
 }
-size_t pvs_smem_bytes(int hd, int ds, int hpk, int rb_alloc) {
-  return (size_t)kPvsStages * ((size_t)kPvsTile * (hd / ds) + (size_t)rb_alloc * hpk * kPvsTile) * sizeof(float);
+size_t pvs_smem_bytes(int hd, int ds, int hpk, int rb_alloc, int ns) {
+  return (size_t)ns * ((size_t)kPvsTile * (hd / ds) + (size_t)rb_alloc * hpk * kPvsTile) * sizeof(float);
+}
+// Ring depth of the split P.V: kPvsStages where it fits in shared memory.
+int pvs_stages(int hd, int ds, int hpk, int rb_alloc) {
+  return pvs_smem_bytes(hd, ds, hpk, rb_alloc, kPvsStages) <= kAttnMaxSmem ? kPvsStages : kPvsShallowStages;
 }
 }  // namespace
 
@@ -1253,15 +1311,19 @@ int build_segments(const RowInfo* rows, int M, int seg_len, AttnSeg* segs) {
 
 namespace {
 template <int HD>
-cudaError_t launch_pv_split(int ds, dim3 g, int threads, size_t smem, cudaStream_t s, const StreamKV* kv, int layer,
-                            const AttnSeg* segs, const int* nseg_dev, int nseg_max, int nh, int nkv,
+cudaError_t launch_pv_split(int ds, int ns, dim3 g, int threads, size_t smem, cudaStream_t s, const StreamKV* kv,
+                            int layer, const AttnSeg* segs, const int* nseg_dev, int nseg_max, int nh, int nkv,
                             const float* p, int n_alloc, int rb_alloc, float* out) {
   switch (ds) {
-#define RAI_PVS_CASE(DSV)                                                                                    \
-  case DSV:                                                                                                  \
-    if constexpr (HD / DSV >= 4)                                                                             \
-      return launch_pdl(attn_pv_split_kernel<HD, DSV>, g, dim3(threads), smem, s, kv, layer, segs, nseg_dev, \
-                        nseg_max, nh, nkv, p, n_alloc, rb_alloc, out);                                       \
+#define RAI_PVS_CASE(DSV)                                                                                       \
+  case DSV:                                                                                                     \
+    if constexpr (HD / DSV >= 4) {                                                                              \
+      if (ns == kPvsStages)                                                                                     \
+        return launch_pdl(attn_pv_split_kernel<HD, DSV, kPvsStages>, g, dim3(threads), smem, s, kv, layer,      \
+                          segs, nseg_dev, nseg_max, nh, nkv, p, n_alloc, rb_alloc, out);                        \
+      return launch_pdl(attn_pv_split_kernel<HD, DSV, kPvsShallowStages>, g, dim3(threads), smem, s, kv, layer, \
+                        segs, nseg_dev, nseg_max, nh, nkv, p, n_alloc, rb_alloc, out);                          \
+    }                                                                                                           \
     break;
     RAI_PVS_CASE(2)
     RAI_PVS_CASE(4)
@@ -1290,7 +1352,8 @@ cudaError_t launch_attention(const float* q, float* out, const StreamKV* kv, int
   const int t3 = pv_threads(hd, hpk, hpt);
   const int ds = pv_dim_slices(hd, hpk, nseg_max, nkv);
   const int t3s = ((hd / ds) * hpk + 31) / 32 * 32;
-  const size_t sm3s = pvs_smem_bytes(hd, ds, hpk, seg_rows);
+  const int ns_split = pvs_stages(hd, ds, hpk, seg_rows);
+  const size_t sm3s = pvs_smem_bytes(hd, ds, hpk, seg_rows, ns_split);
   if (hb < 1 || sm1 > kAttnMaxSmem || sm3 > kAttnMaxSmem || t3 > (hpt > 1 ? kPvMaxThreadsH2 : kPvMaxThreads) ||
       (ds > 1 && (sm3s > kAttnMaxSmem || t3s > 256)))
     return cudaErrorInvalidValue;
@@ -1316,7 +1379,8 @@ cudaError_t launch_attention(const float* q, float* out, const StreamKV* kv, int
                                    scores, n_alloc, hb, et, err))                                           \
       return e;                                                                                             \
     if (ds > 1)                                                                                             \
-      return launch_pv_split<HDV>(ds, dim3(nkv, nseg_max, ds), t3s, sm3s, s, kv, layer, segs, nseg_dev,     \
+      return launch_pv_split<HDV>(ds, ns_split, dim3(nkv, nseg_max, ds), t3s, sm3s, s, kv, layer, segs,     \
+                                  nseg_dev,                                                                 \
                                   nseg_max, nh, nkv, (const float*)scores, n_alloc, seg_rows, out);         \
     return hpt > 1 ? launch_pdl(attn_pv_kernel<HDV, kPvStepHeads>, g3, dim3(t3), sm3, s, kv, layer, segs,   \
                                 nseg_dev, nseg_max, nh, nkv, (const float*)scores, n_alloc, seg_rows, ns, out, \
@@ -1339,10 +1403,15 @@ namespace {
 template <int HD>
 cudaError_t set_pv_split_attributes(int bytes) {
   cudaError_t e = cudaSuccess;
-#define RAI_PVS_ATTR(DSV)                                                                                    \
-  if constexpr (HD / DSV >= 4)                                                                               \
-    if (e == cudaSuccess)                                                                                    \
-      e = cudaFuncSetAttribute(attn_pv_split_kernel<HD, DSV>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+#define RAI_PVS_ATTR(DSV)                                                                                      \
+  if constexpr (HD / DSV >= 4) {                                                                               \
+    if (e == cudaSuccess)                                                                                      \
+      e = cudaFuncSetAttribute(attn_pv_split_kernel<HD, DSV, kPvsStages>,                                      \
+                               cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);                            \
+    if (e == cudaSuccess)                                                                                      \
+      e = cudaFuncSetAttribute(attn_pv_split_kernel<HD, DSV, kPvsShallowStages>,                               \
+                               cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);                            \
+  }
   RAI_PVS_ATTR(2)
   RAI_PVS_ATTR(4)
   RAI_PVS_ATTR(8)
