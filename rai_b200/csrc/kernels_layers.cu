@@ -689,29 +689,22 @@ __device__ __forceinline__ void pvs_body(const float* __restrict__ vbase, const 
   }
   __syncthreads();
   // Every thread's share of tile `tile` (none past the end: the group is
-  // still committed so the wait counts stay uniform).
+  // still committed so the wait counts stay uniform). The block is a whole
+  // number of warps, so a thread copies the same V column quad vc of rows
+  // vr0, vr0 + VRS, ... and the same p quad pc of pairs pr0, pr0 + PRS, ...
+  // in every tile.
+  const int vc = tid % V4, vr0 = tid / V4, VRS = nthr / V4;
+  const int pc = tid % C4, pr0 = tid / C4, PRS = nthr / C4;
   auto load = [&](int tile) {
     if (tile < ntiles) {
       const int t0 = tile * VT, cnt = min(VT, n_max - t0);
       float* sv = sm + (size_t)(tile % NS) * stage_floats;
       float* sp = sv + VT * HDS;
-      const float* vt0 = vsl + (size_t)t0 * HD;
-      for (int i = tid; i < cnt * V4; i += nthr) {
-        const int r = i / V4, c = i - r * V4;
-        cp_async16(sv + 4 * i, vt0 + r * HD + 4 * c);
-      }
-      const int c4 = (cnt + 3) / 4;
-      if (c4 == C4) {
-        for (int j = tid; j < npairs * C4; j += nthr) {
-          const int rh = j / C4, c = j - rh * C4;
-          cp_async16(sp + rh * VT + 4 * c, prow0 + pofs[rh] + t0 + 4 * c);
-        }
-      } else {
-        for (int j = tid; j < npairs * c4; j += nthr) {
-          const int rh = j / c4, c = j - rh * c4;
-          cp_async16(sp + rh * VT + 4 * c, prow0 + pofs[rh] + t0 + 4 * c);
-        }
-      }
+      const float* vsrc = vsl + (size_t)(t0 + vr0) * HD + 4 * vc;
+      float* vdst = sv + vr0 * HDS + 4 * vc;
+      for (int r = vr0; r < cnt; r += VRS, vsrc += (size_t)VRS * HD, vdst += VRS * HDS) cp_async16(vdst, vsrc);
+      if (4 * pc < cnt)
+        for (int rh = pr0; rh < npairs; rh += PRS) cp_async16(sp + rh * VT + 4 * pc, prow0 + pofs[rh] + t0 + 4 * pc);
     }
     cp_async_commit();
   };
