@@ -25,87 +25,163 @@ namespace {
 __device__ __forceinline__ int active(const int* m_dev, int M) { return m_dev ? *m_dev : M; }
 
 // Router logits: CTA = kRouterTok tokens x ne experts (one thread per expert);
-// the tokens' normalized rows sit in shared memory.
+// the tokens' normalized rows sit in shared memory. Each logit is one
+// sequential chain over the hidden dimension, so what bounds the kernel is
+// feeding it: the router rows stream in chunks of kRouterChunk columns
+// through an NS-deep ring of coalesced 16-byte cp.async copies (rows padded
+// to kRouterLd floats, so the per-thread 16-byte row reads are conflict
+// free), requested before the previous kernel finishes (they are model
+// constants).
 constexpr int kRouterTok = 4;
+constexpr int kRouterChunk = 32;
+constexpr int kRouterLd = kRouterChunk + 4;
+constexpr int kRouterDeep = 8;
+constexpr size_t kRouterSmemMax = 200 * 1024;
 
+template <int NS>
+size_t router_smem_bytes(int h, int ne) {
+  return ((size_t)kRouterTok * h + (size_t)NS * ne * kRouterLd) * sizeof(float);
+}
+
+template <int NS>
 __global__ void __launch_bounds__(kMaxMoeExperts) router_kernel(const float* __restrict__ x, const float* __restrict__ router,
                                                          int h, int ne, const int* m_dev, int M,
                                                          float* __restrict__ logits) {
-  extern __shared__ __align__(16) float sx[];  // [kRouterTok][h]
+  extern __shared__ __align__(16) float sm[];
+  float* sx = sm;                               // [kRouterTok][h]
+  float* sr = sm + (size_t)kRouterTok * h;      // [NS][ne][kRouterLd]
+  const int tid = threadIdx.x, nthr = blockDim.x;
+  const int nch = (h + kRouterChunk - 1) / kRouterChunk;
+  auto load = [&](int c) {
+    if (c < nch) {
+      const int c0 = c * kRouterChunk, g4 = min(kRouterChunk, h - c0) / 4;
+      float* dst = sr + (size_t)(c % NS) * ne * kRouterLd;
+      for (int i = tid; i < ne * g4; i += nthr) {
+        const int e = i / g4, q = i - e * g4;
+        cp_async16(dst + e * kRouterLd + 4 * q, router + (size_t)e * h + c0 + 4 * q);
+      }
+    }
+    cp_async_commit();
+  };
+  for (int c = 0; c < NS - 1; ++c) load(c);
   pdl_wait_prior();
   pdl_launch_dependents();
   const int b0 = blockIdx.x * kRouterTok;
   const int mact = active(m_dev, M);
-  if (b0 >= mact) return;
+  if (b0 >= mact) {
+    cp_async_wait<0>();  // no copy outlives the CTA
+    return;
+  }
   const int nt = min(kRouterTok, mact - b0);
-  stage_f32(sx, x + (size_t)b0 * h, nt * h, threadIdx.x, blockDim.x);
+  stage_f32(sx, x + (size_t)b0 * h, nt * h, tid, nthr);
+  cp_async_commit();
   cp_async_wait<0>();
   __syncthreads();
-  const int e = threadIdx.x;
-  if (e >= ne) return;
-  const float* r = router + (size_t)e * h;
+  const int e = tid;
   float acc[kRouterTok];
 #pragma unroll
   for (int t = 0; t < kRouterTok; ++t) acc[t] = -0.0f;
-  for (int i = 0; i < h; i += 4) {
-    const float4 rv = *reinterpret_cast<const float4*>(r + i);
-    const float r4[4] = {rv.x, rv.y, rv.z, rv.w};
+  for (int c = 0; c < nch; ++c) {
+    load(c + NS - 1);
+    cp_async_wait<NS - 1>();  // chunk c has landed (this thread's copies)
+    __syncthreads();          // ... and every thread's
+    if (e < ne) {
+      const int c0 = c * kRouterChunk, cw = min(kRouterChunk, h - c0);
+      const float* rr = sr + (size_t)(c % NS) * ne * kRouterLd + e * kRouterLd;
+      for (int i = 0; i < cw; i += 4) {
+        const float4 rv = *reinterpret_cast<const float4*>(rr + i);
+        const float r4[4] = {rv.x, rv.y, rv.z, rv.w};
 #pragma unroll
-    for (int t = 0; t < kRouterTok; ++t) {
-      if (t < nt) {
+        for (int t = 0; t < kRouterTok; ++t) {
+          if (t < nt) {
 #pragma unroll
-        for (int u = 0; u < 4; ++u) acc[t] = __fadd_rn(acc[t], __fmul_rn(r4[u], sx[t * h + i + u]));
+            for (int u = 0; u < 4; ++u) acc[t] = __fadd_rn(acc[t], __fmul_rn(r4[u], sx[t * h + c0 + i + u]));
+          }
+        }
       }
     }
+    __syncthreads();  // stage c % NS is refilled by the next iteration
   }
+  if (e < ne) {
 #pragma unroll
-  for (int t = 0; t < kRouterTok; ++t)
-    if (t < nt) logits[(size_t)(b0 + t) * ne + e] = acc[t];
+    for (int t = 0; t < kRouterTok; ++t)
+      if (t < nt) logits[(size_t)(b0 + t) * ne + e] = acc[t];
+  }
 }
 
-// Softmax, top-k and optional renormalization: one thread per token.
-__global__ void route_kernel(float* __restrict__ logits, int ne, int k, int norm_topk, const int* m_dev, int M,
-                             int* __restrict__ experts, float* __restrict__ weights, ExpfTable et) {
+// Softmax, top-k and optional renormalization: one warp per token. The max,
+// the exps and the divisions run across the lanes (each element's value does
+// not depend on the order); the sum runs in expert order on lane 0; each
+// top-k scan takes the largest not yet taken probability, the lowest expert
+// index among equals (a strict '>' scan in expert order).
+constexpr int kRouteWarps = 4;
+
+__global__ void __launch_bounds__(kRouteWarps * 32) route_kernel(float* __restrict__ logits, int ne, int k,
+                                                                 int norm_topk, const int* m_dev, int M,
+                                                                 int* __restrict__ experts,
+                                                                 float* __restrict__ weights, ExpfTable et) {
+  __shared__ float sv[kRouteWarps][kMaxMoeExperts];
   pdl_wait_prior();
   pdl_launch_dependents();
-  const int b = blockIdx.x * blockDim.x + threadIdx.x;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int b = blockIdx.x * kRouteWarps + warp;
   if (b >= active(m_dev, M)) return;
   float* p = logits + (size_t)b * ne;
+  float* v = sv[warp];
   float mx = -INFINITY;
-  for (int e = 0; e < ne; ++e) mx = fmaxf(mx, p[e]);
+  for (int e = lane; e < ne; e += 32) mx = fmaxf(mx, p[e]);
+#pragma unroll
+  for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  for (int e = lane; e < ne; e += 32) v[e] = expf_host(__fsub_rn(p[e], mx), et);
+  __syncwarp();
   float sum = 0.0f;
-  for (int e = 0; e < ne; ++e) {
-    const float v = expf_host(__fsub_rn(p[e], mx), et);
-    p[e] = v;
-    sum = __fadd_rn(sum, v);
+  if (lane == 0)
+    for (int e = 0; e < ne; ++e) sum = __fadd_rn(sum, v[e]);
+  sum = __shfl_sync(0xffffffffu, sum, 0);
+  for (int e = lane; e < ne; e += 32) {
+    const float q = __fdiv_rn(v[e], sum);
+    v[e] = q;
+    p[e] = q;
   }
-  for (int e = 0; e < ne; ++e) p[e] = __fdiv_rn(p[e], sum);
-  uint32_t taken[kMaxMoeExperts / 32];
-  for (int i = 0; i < kMaxMoeExperts / 32; ++i) taken[i] = 0u;
+  __syncwarp();
+  uint32_t taken = 0u;  // bit j: expert lane + 32 j (ne <= 256)
   int count = 0;
   for (int s = 0; s < k; ++s) {
-    int best = -1;
     float bv = -INFINITY;
-    for (int e = 0; e < ne; ++e)
-      if (!(taken[e >> 5] >> (e & 31) & 1u) && p[e] > bv) {
-        bv = p[e];
+    int best = -1;
+    for (int j = 0, e = lane; e < ne; ++j, e += 32)
+      if (!(taken >> j & 1u) && v[e] > bv) {
+        bv = v[e];
         best = e;
       }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, best, o);
+      if (oi >= 0 && (best < 0 || ov > bv || (ov == bv && oi < best))) {
+        bv = ov;
+        best = oi;
+      }
+    }
     if (best < 0) break;
-    taken[best >> 5] |= 1u << (best & 31);
-    experts[(size_t)b * k + count] = best;
-    weights[(size_t)b * k + count] = bv;
+    if ((best & 31) == lane) taken |= 1u << (best >> 5);
+    if (lane == 0) {
+      experts[(size_t)b * k + count] = best;
+      weights[(size_t)b * k + count] = bv;
+    }
     ++count;
   }
-  for (int s = count; s < k; ++s) {
-    experts[(size_t)b * k + s] = -1;
-    weights[(size_t)b * k + s] = 0.f;
-  }
-  if (norm_topk) {
-    float total = -0.0f;
-    for (int s = 0; s < count; ++s) total = __fadd_rn(total, weights[(size_t)b * k + s]);
-    if (total > 0.0f)
-      for (int s = 0; s < count; ++s) weights[(size_t)b * k + s] = __fdiv_rn(weights[(size_t)b * k + s], total);
+  if (lane == 0) {
+    for (int s = count; s < k; ++s) {
+      experts[(size_t)b * k + s] = -1;
+      weights[(size_t)b * k + s] = 0.f;
+    }
+    if (norm_topk) {
+      float total = -0.0f;
+      for (int s = 0; s < count; ++s) total = __fadd_rn(total, weights[(size_t)b * k + s]);
+      if (total > 0.0f)
+        for (int s = 0; s < count; ++s) weights[(size_t)b * k + s] = __fdiv_rn(weights[(size_t)b * k + s], total);
+    }
   }
 }
 
@@ -239,11 +315,21 @@ __global__ void moe_combine_kernel(const float* __restrict__ eo, const int* __re
 cudaError_t moe_route(const float* x, const float* router, int h, int ne, int k, bool norm_topk, const int* m_dev,
                       int M, const ExpfTable& et, const MoeBuffers& mb, cudaStream_t s) {
   if (ne < 2 || ne > kMaxMoeExperts || k < 1 || k > ne || h % 4) return cudaErrorInvalidValue;
-  if (cudaError_t e = launch_pdl(router_kernel, dim3((unsigned)ceil_div(M, kRouterTok)), dim3(kMaxMoeExperts),
-                                 (size_t)kRouterTok * h * sizeof(float), s, x, router, h, ne, m_dev, M, mb.logits))
-    return e;
-  if (cudaError_t e = launch_pdl(route_kernel, dim3((unsigned)ceil_div(M, 128)), dim3(128), 0, s, mb.logits, ne, k,
-                                 (int)norm_topk, m_dev, M, mb.experts, mb.weights, et))
+  // The deep ring for up to 64 experts, two stages beyond.
+  const dim3 rg((unsigned)ceil_div(M, kRouterTok)), rb((unsigned)ne);
+  cudaError_t re;
+  if (ne <= 64) {
+    if (router_smem_bytes<kRouterDeep>(h, ne) > kRouterSmemMax) return cudaErrorInvalidValue;
+    re = launch_pdl(router_kernel<kRouterDeep>, rg, rb, router_smem_bytes<kRouterDeep>(h, ne), s, x, router, h, ne,
+                    m_dev, M, mb.logits);
+  } else {
+    if (router_smem_bytes<2>(h, ne) > kRouterSmemMax) return cudaErrorInvalidValue;
+    re = launch_pdl(router_kernel<2>, rg, rb, router_smem_bytes<2>(h, ne), s, x, router, h, ne, m_dev, M,
+                    mb.logits);
+  }
+  if (re) return re;
+  if (cudaError_t e = launch_pdl(route_kernel, dim3((unsigned)ceil_div(M, kRouteWarps)), dim3(kRouteWarps * 32), 0, s,
+                                 mb.logits, ne, k, (int)norm_topk, m_dev, M, mb.experts, mb.weights, et))
     return e;
   return launch_pdl(moe_sort_kernel, dim3(1), dim3(1024), 0, s, (const int*)mb.experts, k, ne, m_dev, M, mb.cnt,
                     mb.off, mb.row_of_pair, mb.pair_of_row, mb.n_rows, mb.rows_cap);
@@ -266,7 +352,11 @@ cudaError_t moe_combine(const float* eo, int k, int h, const float* residual, fl
 }
 
 cudaError_t init_moe_attributes() {
-  return cudaFuncSetAttribute(router_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024);
+  cudaError_t e = cudaFuncSetAttribute(router_kernel<kRouterDeep>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)kRouterSmemMax);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(router_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kRouterSmemMax);
+  return e;
 }
 
 }  // namespace rai
