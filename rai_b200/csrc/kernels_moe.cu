@@ -43,6 +43,30 @@ size_t router_smem_bytes(int h, int ne) {
   return ((size_t)kRouterTok * h + (size_t)NS * ne * kRouterLd) * sizeof(float);
 }
 
+// One full chunk of one expert's logit chains for NT tokens: the chunk's
+// router values and the tokens' inputs are loaded first (16-byte shared
+// loads), then each token's chain adds its products in column order.
+template <int NT>
+__device__ __forceinline__ void router_chunk(const float* __restrict__ rr, const float* __restrict__ sxc, int h,
+                                             float (&acc)[kRouterTok]) {
+  float4 rv[kRouterChunk / 4], xv[NT][kRouterChunk / 4];
+#pragma unroll
+  for (int q = 0; q < kRouterChunk / 4; ++q) rv[q] = *reinterpret_cast<const float4*>(rr + 4 * q);
+#pragma unroll
+  for (int t = 0; t < NT; ++t)
+#pragma unroll
+    for (int q = 0; q < kRouterChunk / 4; ++q) xv[t][q] = *reinterpret_cast<const float4*>(sxc + (size_t)t * h + 4 * q);
+#pragma unroll
+  for (int q = 0; q < kRouterChunk / 4; ++q)
+#pragma unroll
+    for (int t = 0; t < NT; ++t) {
+      acc[t] = __fadd_rn(acc[t], __fmul_rn(rv[q].x, xv[t][q].x));
+      acc[t] = __fadd_rn(acc[t], __fmul_rn(rv[q].y, xv[t][q].y));
+      acc[t] = __fadd_rn(acc[t], __fmul_rn(rv[q].z, xv[t][q].z));
+      acc[t] = __fadd_rn(acc[t], __fmul_rn(rv[q].w, xv[t][q].w));
+    }
+}
+
 template <int NS>
 __global__ void __launch_bounds__(kMaxMoeExperts) router_kernel(const float* __restrict__ x, const float* __restrict__ router,
                                                          int h, int ne, const int* m_dev, int M,
@@ -85,9 +109,16 @@ __global__ void __launch_bounds__(kMaxMoeExperts) router_kernel(const float* __r
     load(c + NS - 1);
     cp_async_wait<NS - 1>();  // chunk c has landed (this thread's copies)
     __syncthreads();          // ... and every thread's
-    if (e < ne) {
-      const int c0 = c * kRouterChunk, cw = min(kRouterChunk, h - c0);
-      const float* rr = sr + (size_t)(c % NS) * ne * kRouterLd + e * kRouterLd;
+    const int c0 = c * kRouterChunk, cw = min(kRouterChunk, h - c0);
+    const float* rr = sr + (size_t)(c % NS) * ne * kRouterLd + e * kRouterLd;
+    if (e < ne && cw == kRouterChunk) {
+      switch (nt) {
+        case 1: router_chunk<1>(rr, sx + c0, h, acc); break;
+        case 2: router_chunk<2>(rr, sx + c0, h, acc); break;
+        case 3: router_chunk<3>(rr, sx + c0, h, acc); break;
+        default: router_chunk<4>(rr, sx + c0, h, acc); break;
+      }
+    } else if (e < ne) {
       for (int i = 0; i < cw; i += 4) {
         const float4 rv = *reinterpret_cast<const float4*>(rr + i);
         const float r4[4] = {rv.x, rv.y, rv.z, rv.w};
