@@ -68,9 +68,35 @@ __global__ void embed_kernel(const uint32_t* __restrict__ ids, const int* m_dev,
 
 // ---------------------------------------------------------------------------
 // rms_norm_heads: sequential scalar sum of squares over `len` values.
+// The sum of squares is one ordered chain over the row (the reference's
+// scalar loop), so its loads are issued 16 elements ahead of the adds.
 __device__ float rms_inv_seq(const float* x, int len, float eps) {
   float ss = 0.f;
-  for (int i = 0; i < len; ++i) ss = __fadd_rn(ss, __fmul_rn(x[i], x[i]));
+  int i = 0;
+  if ((reinterpret_cast<uintptr_t>(x) & 15u) == 0 && len >= 16) {
+    const float4* x4 = reinterpret_cast<const float4*>(x);
+    const int n16 = len / 16;
+    float4 a[4], b[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) a[u] = x4[u];
+    for (int j = 0; j < n16; ++j) {
+      if (j + 1 < n16) {
+#pragma unroll
+        for (int u = 0; u < 4; ++u) b[u] = x4[4 * (j + 1) + u];
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        ss = __fadd_rn(ss, __fmul_rn(a[u].x, a[u].x));
+        ss = __fadd_rn(ss, __fmul_rn(a[u].y, a[u].y));
+        ss = __fadd_rn(ss, __fmul_rn(a[u].z, a[u].z));
+        ss = __fadd_rn(ss, __fmul_rn(a[u].w, a[u].w));
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) a[u] = b[u];
+    }
+    i = n16 * 16;
+  }
+  for (; i < len; ++i) ss = __fadd_rn(ss, __fmul_rn(x[i], x[i]));
   return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)len), eps)));
 }
 

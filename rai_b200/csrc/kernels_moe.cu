@@ -332,11 +332,23 @@ __global__ void moe_combine_kernel(const float* __restrict__ eo, const int* __re
   if (b >= active(m_dev, M)) return;
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= h) return;
+  // The picks' expert outputs are loaded before the ordered adds.
+  constexpr int kBatch = 8;
   float acc = 0.0f;
-  for (int s = 0; s < k; ++s) {
-    const int r = row_of_pair[(size_t)b * k + s];
-    if (r < 0) continue;
-    acc = __fadd_rn(acc, __fmul_rn(weights[(size_t)b * k + s], eo[(size_t)r * h + i]));
+  for (int s0 = 0; s0 < k; s0 += kBatch) {
+    float wv[kBatch], ev[kBatch];
+    bool use[kBatch];
+#pragma unroll
+    for (int u = 0; u < kBatch; ++u) {
+      const int s = s0 + u;
+      const int r = s < k ? row_of_pair[(size_t)b * k + s] : -1;
+      use[u] = r >= 0;
+      wv[u] = use[u] ? weights[(size_t)b * k + s] : 0.f;
+      ev[u] = use[u] ? eo[(size_t)r * h + i] : 0.f;
+    }
+#pragma unroll
+    for (int u = 0; u < kBatch; ++u)
+      if (use[u]) acc = __fadd_rn(acc, __fmul_rn(wv[u], ev[u]));
   }
   out[(size_t)b * h + i] = __fadd_rn(residual[(size_t)b * h + i], acc);
 }
