@@ -80,9 +80,17 @@ __global__ void __launch_bounds__(kMaxMoeExperts) router_kernel(const float* __r
     if (c < nch) {
       const int c0 = c * kRouterChunk, g4 = min(kRouterChunk, h - c0) / 4;
       float* dst = sr + (size_t)(c % NS) * ne * kRouterLd;
-      for (int i = tid; i < ne * g4; i += nthr) {
-        const int e = i / g4, q = i - e * g4;
-        cp_async16(dst + e * kRouterLd + 4 * q, router + (size_t)e * h + c0 + 4 * q);
+      if (g4 == kRouterChunk / 4) {
+        constexpr int kG = kRouterChunk / 4;  // whole chunk: no division
+        for (int i = tid; i < ne * kG; i += nthr) {
+          const int e = i / kG, q = i % kG;
+          cp_async16(dst + e * kRouterLd + 4 * q, router + (size_t)e * h + c0 + 4 * q);
+        }
+      } else {
+        for (int i = tid; i < ne * g4; i += nthr) {
+          const int e = i / g4, q = i - e * g4;
+          cp_async16(dst + e * kRouterLd + 4 * q, router + (size_t)e * h + c0 + 4 * q);
+        }
       }
     }
     cp_async_commit();
