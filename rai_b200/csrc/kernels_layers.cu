@@ -155,32 +155,35 @@ __global__ void qkv_post_kernel(const float* __restrict__ qkv, int ld, float* __
   }
   const float* c = rope_cos + (size_t)pos * half;
   const float* s = rope_sin + (size_t)pos * half;
-  for (int idx = threadIdx.x; idx < (nh + nkv) * half; idx += blockDim.x) {
-    int h = idx / half, i = idx % half;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
+  // Warp per head, lane per pair: no index division.
+  for (int h = warp; h < nh + nkv; h += nwarps) {
     float* hp = h < nh ? sq + h * hd : sk + (h - nh) * hd;
-    rope_pair(hp, i, half, chunked, c, s);
+    for (int i = lane; i < half; i += 32) rope_pair(hp, i, half, chunked, c, s);
   }
   __syncthreads();
   for (int i = threadIdx.x; i < qd; i += blockDim.x) q_out[(size_t)b * qd + i] = sq[i];
   const float* vrow = row + qd + kvd;
   const size_t lbase = (size_t)layer * nkv * sk_.max_ctx * hd;
-  // v goes from the projection row to the cache: four loads per thread in
-  // flight before their stores.
-  for (int i0 = threadIdx.x; i0 < kvd; i0 += 4 * blockDim.x) {
-    float vv[4];
+  // k and v go to the cache, warp per KV head; v comes from the projection
+  // row, its loads issued before the stores.
+  for (int h = warp; h < nkv; h += nwarps) {
+    const size_t o = lbase + ((size_t)h * sk_.max_ctx + pos) * hd;
+    for (int d0 = 0; d0 < hd; d0 += 128) {
+      float vv[4];
 #pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      const int i = i0 + u * blockDim.x;
-      vv[u] = i < kvd ? vrow[i] : 0.f;
-    }
+      for (int u = 0; u < 4; ++u) {
+        const int d = d0 + lane + 32 * u;
+        vv[u] = d < hd ? vrow[h * hd + d] : 0.f;
+      }
 #pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      const int i = i0 + u * blockDim.x;
-      if (i >= kvd) continue;
-      const int h = i / hd, d = i % hd;
-      const size_t o = lbase + ((size_t)h * sk_.max_ctx + pos) * hd + d;
-      sk_.k[o] = sk[i];
-      sk_.v[o] = vv[u];
+      for (int u = 0; u < 4; ++u) {
+        const int d = d0 + lane + 32 * u;
+        if (d < hd) {
+          sk_.k[o + d] = sk[h * hd + d];
+          sk_.v[o + d] = vv[u];
+        }
+      }
     }
   }
   __syncthreads();  // shared rows are reused by the next row
