@@ -51,3 +51,21 @@ def test_linear_entries_reject_sizes_before_narrowing():
             native.RAI_ERR_INVALID
         assert L.rai_gpu_w4a8_matmul(dummy, dummy, dummy, rows, cols, tokens, 128, dummy, 1 << 40, None) == \
             native.RAI_ERR_INVALID
+
+
+def test_rust_binding_declares_every_entry_point():
+    """INTEGRATION.md's extern "C" block (the binding a maintainer adds to
+    rai-infer) names every rai_gpu_* entry the header declares."""
+    doc = open(os.path.join(ROOT, "INTEGRATION.md")).read()
+    bound = set(re.findall(r"pub fn (rai_gpu_\w+)\s*\(", doc))
+    missing = [n for n in _declared() if n not in bound]
+    assert not missing, missing
+
+
+def test_ctypes_binding_sets_argtypes_for_every_entry_point():
+    """rai_b200.native gives every declared entry its argument types, so no
+    call goes through ctypes' default int conversion of size_t or pointers."""
+    from rai_b200 import native
+    lib = native.lib()
+    untyped = [n for n in _declared() if getattr(lib, n).argtypes is None]
+    assert not untyped, untyped
