@@ -1,6 +1,7 @@
-"""The oracle's attention head against a scalar restatement of the reference's
-attention_head_avx2 (rai-infer/src/layers.rs:1266-1380), written here in
-plain Python over float32 values, one operation at a time:
+"""The oracle's attention head and RMSNorm against scalar restatements of the
+reference's attention_head_avx2 (rai-infer/src/layers.rs:1266-1380) and
+rms_norm_avx2 (layers.rs:325-376), written here in plain Python over float32
+values, one operation at a time. The attention head:
 
   score t = soft_cap(dot * scale) with dot = 8 lane accumulators of fused
             multiply-adds over head_dim / 8 chunks, then the tree
@@ -137,4 +138,39 @@ def test_attention_head_with_softcap(oracle):
     V = rng.standard_normal((pos + 1, hd)).astype(np.float32)
     want = _attention(q, K, V, pos, 0.25, 5.0)
     got = oracle.attention_head(q, K, V, pos, 0.25, 5.0)
+    assert np.array_equal(want.view(np.uint32), got.view(np.uint32))
+
+
+def _rms_norm(x, w, eps):
+    """rms_norm_avx2 (layers.rs:325-376): two 8-lane FMA accumulators over
+    16-element strides, one more 8-chunk into the first, lane-wise add, the
+    tree, a scalar tail (multiply, then add); 1 / sqrt(ss / n + eps); then
+    (x * inv) * w."""
+    n = x.size
+    sq0, sq1 = [f32(0.0)] * 8, [f32(0.0)] * 8
+    i = 0
+    for _ in range((n // 8) // 2):
+        for lane in range(8):
+            sq0[lane] = _fma32(x[i + lane], x[i + lane], sq0[lane])
+            sq1[lane] = _fma32(x[i + 8 + lane], x[i + 8 + lane], sq1[lane])
+        i += 16
+    if i + 8 <= n:
+        for lane in range(8):
+            sq0[lane] = _fma32(x[i + lane], x[i + lane], sq0[lane])
+        i += 8
+    ss = _hsum8([f32(sq0[lane] + sq1[lane]) for lane in range(8)])
+    while i < n:
+        ss = f32(ss + f32(x[i] * x[i]))
+        i += 1
+    inv = f32(f32(1.0) / np.sqrt(f32(f32(ss / f32(n)) + f32(eps)), dtype=np.float32))
+    return np.asarray([f32(f32(x[j] * inv) * w[j]) for j in range(n)], np.float32)
+
+
+@pytest.mark.parametrize("n", [13, 24, 37, 256, 2048])
+def test_rms_norm_matches_the_scalar_restatement(oracle, n):
+    rng = np.random.default_rng(n)
+    x = (rng.standard_normal(n) * 3).astype(np.float32)
+    w = (1 + 0.1 * rng.standard_normal(n)).astype(np.float32)
+    want = _rms_norm(x, w, 1e-5)
+    got = oracle.rms_norm(x, w, 1e-5)
     assert np.array_equal(want.view(np.uint32), got.view(np.uint32))
