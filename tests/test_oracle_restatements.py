@@ -1,7 +1,8 @@
-"""The oracle's attention head and RMSNorm against scalar restatements of the
-reference's attention_head_avx2 (rai-infer/src/layers.rs:1266-1380) and
-rms_norm_avx2 (layers.rs:325-376), written here in plain Python over float32
-values, one operation at a time. The attention head:
+"""The oracle's attention head, RMSNorm and RoPE against scalar restatements
+of the reference's attention_head_avx2 (rai-infer/src/layers.rs:1266-1380),
+rms_norm_avx2 (layers.rs:325-376) and RoPE application (layers.rs:690-727),
+written here in plain Python over float32 values, one operation at a time.
+The attention head:
 
   score t = soft_cap(dot * scale) with dot = 8 lane accumulators of fused
             multiply-adds over head_dim / 8 chunks, then the tree
@@ -173,4 +174,35 @@ def test_rms_norm_matches_the_scalar_restatement(oracle, n):
     w = (1 + 0.1 * rng.standard_normal(n)).astype(np.float32)
     want = _rms_norm(x, w, 1e-5)
     got = oracle.rms_norm(x, w, 1e-5)
+    assert np.array_equal(want.view(np.uint32), got.view(np.uint32))
+
+
+def _rope(heads, nh, hd, c, s):
+    """The reference's RoPE application (layers.rs:690-727): per head, pairs
+    (i, i + half); fmsub(x0, cos, x1 * sin) and fmadd(x1, cos, x0 * sin) for
+    the first (half/8)*8 pairs, the unfused scalar form for the tail."""
+    out = heads.copy()
+    half = hd // 2
+    n8 = (half // 8) * 8
+    for h in range(nh):
+        b = h * hd
+        for i in range(half):
+            x0, x1 = heads[b + i], heads[b + half + i]
+            if i < n8:
+                out[b + i] = _fma32(x0, c[i], f32(-f32(x1 * s[i])))
+                out[b + half + i] = _fma32(x1, c[i], f32(x0 * s[i]))
+            else:
+                out[b + i] = f32(f32(x0 * c[i]) - f32(x1 * s[i]))
+                out[b + half + i] = f32(f32(x1 * c[i]) + f32(x0 * s[i]))
+    return out
+
+
+@pytest.mark.parametrize("nh,hd", [(2, 16), (3, 40), (2, 64)])
+def test_rope_matches_the_scalar_restatement(oracle, nh, hd):
+    rng = np.random.default_rng(nh * 1000 + hd)
+    heads = rng.standard_normal(nh * hd).astype(np.float32)
+    ang = rng.uniform(-3, 3, hd // 2)
+    c, s = np.cos(ang).astype(np.float32), np.sin(ang).astype(np.float32)
+    want = _rope(heads, nh, hd, c, s)
+    got = oracle.rope_apply(heads, nh, hd, c, s)
     assert np.array_equal(want.view(np.uint32), got.view(np.uint32))
