@@ -1,6 +1,7 @@
-"""The oracle's attention head, RMSNorm and RoPE against scalar restatements
-of the reference's attention_head_avx2 (rai-infer/src/layers.rs:1266-1380),
-rms_norm_avx2 (layers.rs:325-376) and RoPE application (layers.rs:690-727),
+"""The oracle's attention head, RMSNorm, RoPE and SwiGLU against scalar
+restatements of the reference's attention_head_avx2
+(rai-infer/src/layers.rs:1266-1380), rms_norm_avx2 (layers.rs:325-376), RoPE
+application (layers.rs:690-727) and silu_mul_avx2 (layers.rs:850-883),
 written here in plain Python over float32 values, one operation at a time.
 The attention head:
 
@@ -205,4 +206,32 @@ def test_rope_matches_the_scalar_restatement(oracle, nh, hd):
     c, s = np.cos(ang).astype(np.float32), np.sin(ang).astype(np.float32)
     want = _rope(heads, nh, hd, c, s)
     got = oracle.rope_apply(heads, nh, hd, c, s)
+    assert np.array_equal(want.view(np.uint32), got.view(np.uint32))
+
+
+def _silu_mul(gate, up):
+    """silu_mul_avx2 (layers.rs:850-883): for the first (n/8)*8 elements
+    exp(-x) by Schraudolph's form on -x (x * -1), then x / (1 + e), times up;
+    the tail by the scalar silu (layers.rs:816-818) with the libm expf."""
+    n = gate.size
+    n8 = (n // 8) * 8
+    out = np.empty(n, np.float32)
+    for i in range(n):
+        x = gate[i]
+        if i < n8:
+            e = _schraudolph(f32(x * f32(-1.0)))
+        else:
+            e = f32(_libm.expf(float(-x)))
+        out[i] = f32(f32(x / f32(f32(1.0) + e)) * up[i])
+    return out
+
+
+@pytest.mark.parametrize("n", [8, 29, 256])
+def test_silu_mul_matches_the_scalar_restatement(oracle, n):
+    rng = np.random.default_rng(n)
+    gate = (rng.standard_normal(n) * 4).astype(np.float32)
+    gate[0] = np.float32(-90.0)  # exp(-x) clamps to the +inf bit pattern: silu = -0
+    up = rng.standard_normal(n).astype(np.float32)
+    want = _silu_mul(gate, up)
+    got = oracle.silu_mul(gate, up)
     assert np.array_equal(want.view(np.uint32), got.view(np.uint32))
