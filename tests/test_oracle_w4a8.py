@@ -1,5 +1,6 @@
-"""The oracle's W4A8 linear against a scalar restatement of the reference's
-AVX2 path, bit for bit (rai-infer/src/gemm.rs):
+"""The oracle's W4A8 linear and tied 8-bit LM head against scalar
+restatements of the reference's AVX2 paths, bit for bit
+(rai-infer/src/gemm.rs; the tied head is described at _tied_head):
 
   quantize_input_split_avx2 (gemm.rs:280-374): per (token, group) absmax,
       scale = absmax / 127 (1 when absmax <= 1e-10), inv = 1 / scale, codes
@@ -109,3 +110,64 @@ def test_quantization_matches_the_scalar_restatement(oracle):
     assert np.array_equal(ev.astype(np.int32), codes[0::2]) and np.array_equal(od.astype(np.int32), codes[1::2])
     assert np.array_equal(np.asarray(scales, np.float32).view(np.uint32), sc.view(np.uint32))
     assert np.array_equal(np.asarray(sums, np.float32).view(np.uint32), su.view(np.uint32))
+
+
+def _tied_head(hidden, data, params, vocab, hs, gs):
+    """tied_lm_head (gemm.rs:1981-2076) on its AVX2 path: the hidden state
+    quantized to +-63 per group (quantize_hidden_i8_avx2, gemm.rs:976-1047:
+    scale = absmax / 63, round half to even), the group sums of the raw
+    hidden (compute_input_sums_avx2); per vocabulary row (lm_head_chunk_i8,
+    gemm.rs:804-915) 8 f32 lanes, lane m's exact dot over bytes 4m .. 4m+3
+    of every 32-byte block of the group's 8-bit codes, acc_m += float(dot_m)
+    * (w_scale * h_scale) in group order, the tree, plus the zero
+    correction summed in group order from 0."""
+    ng = hs // gs
+    hq = np.zeros(hs, np.int64)
+    hsc, hsum = [], []
+    for g in range(ng):
+        seg = hidden[g * gs:(g + 1) * gs]
+        absmax = f32(np.max(np.abs(seg)))
+        scale = f32(absmax / f32(63.0)) if absmax > f32(1e-10) else f32(1.0)
+        inv = f32(f32(1.0) / scale)
+        for i in range(gs):
+            hq[g * gs + i] = int(min(max(np.rint(f32(seg[i] * inv)), -63.0), 63.0))
+        lanes = [f32(0.0)] * 8
+        for i in range(gs):
+            lanes[i % 8] = f32(lanes[i % 8] + seg[i])
+        s = [f32(lanes[i] + lanes[i + 4]) for i in range(4)]
+        hsum.append(f32(f32(s[0] + s[1]) + f32(s[2] + s[3])))
+        hsc.append(scale)
+    codes = data.reshape(vocab, hs).astype(np.int64)
+    par = params.view("<f2").reshape(vocab, ng, 2).astype(np.float32)
+    out = np.zeros(vocab, np.float32)
+    for v in range(vocab):
+        zc = f32(0.0)
+        for g in range(ng):
+            zc = f32(zc + f32(par[v, g, 1] * hsum[g]))
+        acc = [f32(0.0)] * 8
+        for g in range(ng):
+            dots = [0] * 8
+            for c in range(gs // 32):
+                for m in range(8):
+                    j = g * gs + 32 * c + 4 * m
+                    dots[m] += int(np.dot(codes[v, j:j + 4], hq[j:j + 4]))
+            cs = f32(par[v, g, 0] * hsc[g])
+            for m in range(8):
+                acc[m] = f32(acc[m] + f32(f32(dots[m]) * cs))
+        s = [f32(acc[i] + acc[i + 4]) for i in range(4)]
+        out[v] = f32(f32(f32(s[0] + s[1]) + f32(s[2] + s[3])) + zc)
+    return out
+
+
+@pytest.mark.parametrize("vocab,hs,gs", [(10, 128, 64), (7, 256, 64)])
+def test_tied_head_matches_the_scalar_restatement(oracle, vocab, hs, gs):
+    rng = np.random.default_rng(vocab * hs)
+    data = rng.integers(0, 256, size=vocab * hs, dtype=np.uint8)
+    ng = hs // gs
+    scale = rng.uniform(0.001, 0.01, size=(vocab, ng)).astype(np.float16)
+    zero = (-128.0 * scale.astype(np.float32)).astype(np.float16)
+    params = np.stack([scale, zero], axis=-1).astype("<f2").view(np.uint8).reshape(-1)
+    hidden = rng.standard_normal(hs).astype(np.float32)
+    want = _tied_head(hidden, data, params, vocab, hs, gs)
+    got = oracle.tied_lm_head(hidden, data, params, vocab, hs, gs)
+    assert np.array_equal(want.view(np.uint32), got.view(np.uint32))
