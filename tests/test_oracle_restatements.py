@@ -1,7 +1,8 @@
-"""The oracle's attention head, RMSNorm, RoPE and SwiGLU against scalar
-restatements of the reference's attention_head_avx2
-(rai-infer/src/layers.rs:1266-1380), rms_norm_avx2 (layers.rs:325-376), RoPE
-application (layers.rs:690-727) and silu_mul_avx2 (layers.rs:850-883),
+"""The oracle's attention head, RMSNorm, QK-norm, RoPE and SwiGLU against
+scalar restatements of the reference's attention_head_avx2
+(rai-infer/src/layers.rs:1266-1380), rms_norm_avx2 (layers.rs:325-376),
+rms_norm_heads (layers.rs:201-240), RoPE application (layers.rs:690-727) and
+silu_mul_avx2 (layers.rs:850-883),
 written here in plain Python over float32 values, one operation at a time.
 The attention head:
 
@@ -234,4 +235,31 @@ def test_silu_mul_matches_the_scalar_restatement(oracle, n):
     up = rng.standard_normal(n).astype(np.float32)
     want = _silu_mul(gate, up)
     got = oracle.silu_mul(gate, up)
+    assert np.array_equal(want.view(np.uint32), got.view(np.uint32))
+
+
+def _rms_norm_heads(x, nh, hd, w, eps):
+    """rms_norm_heads (layers.rs:201-240), the QK-norm: per head a scalar sum
+    of squares from 0 (multiply, then add), 1 / sqrt(ss / hd + eps), then
+    (x * inv) * w. The full-width form (OLMo2) is one head over the whole
+    projection (layers.rs:308-313)."""
+    out = x.copy()
+    for h in range(nh):
+        seg = x[h * hd:(h + 1) * hd]
+        ss = f32(0.0)
+        for v in seg:
+            ss = f32(ss + f32(v * v))
+        inv = f32(f32(1.0) / np.sqrt(f32(f32(ss / f32(hd)) + f32(eps)), dtype=np.float32))
+        for i in range(hd):
+            out[h * hd + i] = f32(f32(seg[i] * inv) * w[i])
+    return out
+
+
+@pytest.mark.parametrize("nh,hd", [(4, 64), (1, 512)])
+def test_qk_norm_matches_the_scalar_restatement(oracle, nh, hd):
+    rng = np.random.default_rng(nh * hd)
+    x = (rng.standard_normal(nh * hd) * 2).astype(np.float32)
+    w = (1 + 0.1 * rng.standard_normal(hd)).astype(np.float32)
+    want = _rms_norm_heads(x, nh, hd, w, 1e-6)
+    got = oracle.rms_norm_heads(x, nh, hd, w, 1e-6)
     assert np.array_equal(want.view(np.uint32), got.view(np.uint32))
